@@ -1,0 +1,262 @@
+/* thvm_sm100.h - the C ABI of the B200 (sm_100a) device for thvm's tensor track.
+ *
+ * Three layers, all plain C (no torch or CUDA types in any signature; a
+ * stream is passed as `void *` and is a cudaStream_t / CUstream):
+ *
+ *  1. The Backend vtable entries.  Each replaces the CUDA_BACKEND field of
+ *     `struct Backend` (src/thvm.h:751-829, filled at src/backend/cuda/_.c:29-53)
+ *     with the same meaning: u32 buffer ids (0 = none), refcounts, a best-fit
+ *     freelist that hands recycled storage to a FRESH slot id, zero-filled new
+ *     allocations, offset writes for the KV-cache append, stream-ordered
+ *     launches and a sync at the realize boundary.
+ *  2. sm100_dispatch_kernel: the replacement of
+ *     `int (*dispatch_kernel)(KernelEntry *, u32 *in_buf_ids, u32 out_buf_id)`.
+ *     The schedule-side router turns a recognised lifted DAG into an
+ *     Sm100Kernel descriptor (input slots index in_buf_ids) and calls this.
+ *  3. One launcher per kernel family over device pointers and a stream
+ *     (sm100_linear, sm100_attention, sm100_layernorm, ...), for hosts that
+ *     manage their own memory, and for the dispatcher itself.
+ *  4. TinyJit replay as CUDA graphs (replaces cuda_jit_graph_*,
+ *     src/backend/cuda/jit.c:444-604, and jit_replay's all-CUDA fast path,
+ *     src/jit/capture.c:2695-2738): runtime values that change per step
+ *     (a symbolic position, a token id) live in device buffers, so one
+ *     captured graph serves every step.
+ *
+ * Every entry point returns an int status (SM100_OK = 0, negative on error)
+ * unless it mirrors a void / u32 vtable field; sm100_last_error() gives the
+ * message of the last failure (as thvm_cuda_last_error, src/backend/cuda/init.c:96-101).
+ */
+#ifndef THVM_SM100_H
+#define THVM_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status, dtypes ------------------------------------------------------ */
+enum {
+  SM100_OK = 0,
+  SM100_ERR_ARG = -1,         /* bad id, size, shape or pointer */
+  SM100_ERR_CUDA = -2,        /* a CUDA runtime call failed */
+  SM100_ERR_UNSUPPORTED = -3, /* kernel kind / dtype / shape not handled */
+  SM100_ERR_OOM = -4,         /* device allocation failed */
+  SM100_ERR_STATE = -5,       /* not initialised, or wrong capture state */
+  SM100_ERR_TIMEOUT = -6      /* a bounded device wait gave up (status word set) */
+};
+
+/* dtype ids (the reference's DT_* storage types that reach this path) */
+enum {
+  SM100_DT_F32 = 0,
+  SM100_DT_BF16 = 1,
+  SM100_DT_FP8E4M3 = 2, /* weights only, with fp32 128x128 block scales */
+  SM100_DT_I32 = 3
+};
+
+/* ---- 1. Backend vtable (src/thvm.h:751-829) ------------------------------ */
+
+/* Backend.init / shutdown (cuda_init, src/backend/cuda/init.c:110-143).
+ * Selects device $THVM_SM100_DEVICE (default: the current device). */
+int sm100_init(void);
+void sm100_shutdown(void);
+const char *sm100_last_error(void);
+/* 1 after a successful sm100_init on an sm_100 device. */
+int sm100_ready(void);
+/* Host-memory mode for CPU-only tests of the buffer table: buffers are host
+ * allocations and no kernel runs.  Call before sm100_init. */
+void sm100_debug_host_memory(int on);
+
+/* Buffers: u32 ids into a 65536-slot table (CUDA_BUFS, src/backend/cuda/init.c:47-53).
+ * buf_alloc returns 0 on failure (OOM, slot table full, above the per-buffer
+ * ceiling $THVM_MAX_BUF_BYTES, 0 = unlimited, default unlimited here since
+ * 180 GB of HBM holds whole weight sets); new storage reads as zeros
+ * (cuda_buf_alloc's cuMemsetD8, src/backend/cuda/buf_alloc.c:122). */
+uint32_t sm100_buf_alloc(uint64_t nbytes);
+void sm100_buf_free(uint32_t buf_id);
+void sm100_buf_incref(uint32_t buf_id);
+void sm100_buf_decref(uint32_t buf_id); /* frees at refcount 0 unless jit-pinned */
+void sm100_buf_jit_pin(uint32_t buf_id);
+void sm100_buf_jit_unpin(uint32_t buf_id);
+int sm100_buf_read(uint32_t buf_id, void *dst, uint64_t nbytes);
+int sm100_buf_write(uint32_t buf_id, const void *src, uint64_t nbytes);
+int sm100_buf_copy(uint32_t dst_buf_id, uint32_t src_buf_id, uint64_t nbytes);
+/* KV-cache append: bounds-checked offset write / copy (src/thvm.h:783-795). */
+int sm100_buf_write_at(uint32_t buf_id, uint64_t byte_off, const void *src, uint64_t nbytes);
+int sm100_buf_copy_at(uint32_t dst_buf_id, uint64_t dst_byte_off, uint32_t src_buf_id,
+                      uint64_t nbytes);
+uint32_t sm100_buf_refcount(uint32_t buf_id);
+/* Freelist hand-off (src/backend/cuda/buf_freelist.c:10-110): push parks the
+ * storage; the next alloc that best-fits it gets a NEW id and the donor id
+ * goes dead; remove un-parks a buffer not yet re-issued. */
+void sm100_buf_freelist_push(uint32_t buf_id);
+void sm100_buf_freelist_remove(uint32_t buf_id);
+uint32_t sm100_buf_storage_root(uint32_t buf_id);
+uint64_t sm100_buf_nbytes(uint32_t buf_id); /* the requested size */
+void sm100_buf_zero(uint32_t buf_id);       /* stream-ordered, no host sync */
+/* An arena view: bytes [off, off+nbytes) of parent, sharing its storage
+ * (parent_buf_id, src/backend/cuda/buf_alloc.c:196-204). 0 on failure. */
+uint32_t sm100_buf_view(uint32_t parent_buf_id, uint64_t off, uint64_t nbytes);
+/* Device address of a live buffer (NULL if dead), for launcher callers. */
+void *sm100_buf_dptr(uint32_t buf_id);
+uint64_t sm100_mem_live_bytes(void);
+uint64_t sm100_mem_peak_bytes(void);
+uint32_t sm100_buf_live_count(void);
+
+/* Launch stream: the backend's own non-blocking stream unless set. */
+void *sm100_stream(void);
+int sm100_set_stream(void *stream);
+
+/* dispatch_begin / flush / end (src/backend/dispatch/*.c): end synchronises
+ * the stream at the realize boundary unless a capture is open
+ * (cuda_dispatch_end, src/backend/cuda/_.c:23-27). */
+void sm100_dispatch_begin(void);
+void sm100_dispatch_flush(void);
+void sm100_dispatch_end(void);
+
+/* ---- 2. dispatch_kernel -------------------------------------------------- */
+
+enum {
+  SM100_K_LINEAR = 1,   /* y = x W^T (+b) [+GELU] [+residual]; optional LN prologue */
+  SM100_K_LAYERNORM,    /* y = LN(x) (*g + b) over the last axis */
+  SM100_K_RMSNORM,      /* y = x rsqrt(mean(x^2) + eps) (*g) */
+  SM100_K_SOFTMAX,      /* softmax over the last axis */
+  SM100_K_GELU,         /* tanh-form GELU, elementwise */
+  SM100_K_ADD,          /* y = a + b, elementwise */
+  SM100_K_ATTENTION,    /* softmax(q k^T scale [+causal]) v over a KV cache */
+  SM100_K_EMBEDDING,    /* y[i] = table[idx[i]] (zero row outside [0, V)) [+ pos rows] */
+  SM100_K_ARGMAX,       /* first index of each row's max (int32) */
+  SM100_K_SCATTER,      /* dst[idx[i]] = src[i] rows, idx outside [0, V) skipped */
+  SM100_K_KV_APPEND,    /* cache[:, pos:pos+T] = stack(k, v) at a device position */
+  SM100_K_POS_ADD       /* device int32 counter += value (the kvar bump) */
+};
+
+/* Linear flags */
+enum {
+  SM100_LIN_LN = 1u << 0,        /* x -> layernorm(x) * ln_g + ln_b before the product */
+  SM100_LIN_GELU = 1u << 1,      /* tanh GELU after the bias */
+  SM100_LIN_RESIDUAL = 1u << 2,  /* y = residual + (xW^T + b) */
+  SM100_LIN_KV_APPEND = 1u << 3  /* also store output columns [d, 3d) into the KV cache */
+};
+
+/* Input slots of a descriptor index the in_buf_ids array; -1 = absent.
+ * Unused fields are 0 / -1. */
+typedef struct {
+  uint32_t kind;
+  uint32_t dtype;   /* weight / table dtype (SM100_DT_*); activations are f32 */
+  uint32_t flags;
+  int32_t in[10];   /* slot meaning per kind, below */
+  int64_t m, n, k;  /* rows, cols / outputs, contraction (per kind, below) */
+  int64_t ld_in, ld_out; /* row strides (elements) of the first input / the output; 0 = dense */
+  int64_t row_off;  /* first input row to read (e.g. the last prompt row) */
+  int32_t heads, head_dim, max_ctx, causal;
+  int32_t pos;      /* host value of the runtime position when in[7] < 0 */
+  float eps, scale;
+} Sm100Kernel;
+/* Slot meaning:
+ *  LINEAR     in[0]=x [m,k]  in[1]=W [n,k]  in[2]=bias  in[3]=ln_g  in[4]=ln_b
+ *             in[5]=residual [m,n] (may be the output)  in[6]=block scales (fp8)
+ *             in[7]=position (i32)  in[8]=KV cache [2, max_ctx, n/3] (KV_APPEND:
+ *             output columns [n/3, n) also go to cache rows pos+row)
+ *  LAYERNORM  in[0]=x [m,k] in[1]=g in[2]=b
+ *  RMSNORM    in[0]=x [m,k] in[1]=g
+ *  SOFTMAX    in[0]=x [m,k]
+ *  GELU       in[0]=x (m*k elements)
+ *  ADD        in[0]=a in[1]=b (m*k elements)
+ *  ATTENTION  in[0]=q rows [m=T, heads*head_dim] (stride ld_in) in[1]=KV cache
+ *             [2, max_ctx, heads*head_dim] in[7]=position; keys 0..pos+t for
+ *             query row t (causal within the new rows), scale = 1/sqrt(hd)
+ *  EMBEDDING  in[0]=table [n=V, k=D] in[1]=idx i32 [m] in[2]=pos table [*, D]
+ *             (optional, adds row pos+i) in[7]=position
+ *  ARGMAX     in[0]=x [m, n] (stride ld_in, from row_off); out = i32 [m];
+ *             in[7]=position to bump by 1 after the write (optional)
+ *  SCATTER    in[0]=src [m, k] in[1]=idx i32 [m]; out = dst [n, k]
+ *  KV_APPEND  in[0]=k rows in[1]=v rows [m, k] (stride ld_in) in[7]=position;
+ *             out = cache [2, max_ctx, k]
+ *  POS_ADD    out = i32 counter; pos = value to add
+ */
+int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *in_buf_ids, uint32_t n_in,
+                          uint32_t out_buf_id);
+
+/* gather_strided (src/thvm.h:822-828): dst[i] = src[offset + sum_d idx_d * strides[d]]
+ * over a row-major walk of dims, elements of elem_bytes (1, 2, 4 or 8). */
+typedef struct {
+  uint32_t ndim;
+  uint32_t elem_bytes;
+  int64_t offset;
+  int64_t dims[8];
+  int64_t strides[8];
+} Sm100View;
+int sm100_gather_strided(uint32_t dst_buf_id, uint32_t src_buf_id, const Sm100View *view);
+
+/* ---- 3. launchers over device pointers ----------------------------------- */
+
+typedef struct {
+  const float *x;        /* [M, K] f32, row stride ldx (>= K) */
+  const void *w;         /* [N, K], row-major, wdtype */
+  const float *w_scale;  /* fp8: [ceil(N/128), ceil(K/128)] fp32 block scales */
+  const float *bias;     /* [N] or NULL */
+  const float *ln_g;     /* LN prologue gamma / beta (NULL: no affine) */
+  const float *ln_b;
+  const float *residual; /* [M, N] stride ldy, may equal y */
+  float *y;              /* [M, N] f32, row stride ldy (>= N) */
+  float *kv_cache;       /* KV_APPEND: [2, max_ctx, N/3] */
+  const int32_t *pos;    /* KV_APPEND: device start position (NULL: host_pos) */
+  int64_t M, N, K, ldx, ldy;
+  int32_t wdtype, flags, max_ctx, host_pos;
+  float eps;
+} Sm100LinearArgs;
+int sm100_linear(const Sm100LinearArgs *a, void *stream);
+
+typedef struct {
+  const float *q;        /* [T, H*hd] rows, stride ldq (a qkv buffer: 3*H*hd) */
+  const float *k_cache;  /* [max_ctx, H*hd] */
+  const float *v_cache;  /* [max_ctx, H*hd] */
+  float *out;            /* [T, H*hd] */
+  const int32_t *pos;    /* device start position (NULL: host_pos) */
+  int64_t ldq;
+  int32_t T, H, hd, max_ctx, host_pos;
+  float scale;
+} Sm100AttnArgs;
+int sm100_attention(const Sm100AttnArgs *a, void *stream);
+
+int sm100_layernorm(const float *x, const float *g, const float *b, float *y, int64_t M,
+                    int64_t D, float eps, void *stream);
+int sm100_rmsnorm(const float *x, const float *g, float *y, int64_t M, int64_t D, float eps,
+                  void *stream);
+int sm100_softmax(const float *x, float *y, int64_t M, int64_t N, void *stream);
+int sm100_gelu(const float *x, float *y, int64_t n, void *stream);
+int sm100_add(const float *a, const float *b, float *y, int64_t n, void *stream);
+/* y[i] = table[idx[i]] (+ pos_table[pos + i]); rows of D floats. */
+int sm100_embedding(const float *table, const int32_t *idx, const float *pos_table,
+                    const int32_t *pos, float *y, int64_t n_idx, int64_t V, int64_t D,
+                    void *stream);
+/* out[m] = first index of the max of row m (rows of N floats, stride ld);
+ * bump (optional) is incremented by 1 after the write. */
+int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
+                 int32_t *bump, void *stream);
+/* dst[idx[i]] = src[i], rows of D elements of elem_bytes; idx outside [0, V) skipped. */
+int sm100_scatter_rows(void *dst, const int32_t *idx, const void *src, int64_t n_idx,
+                       int64_t V, int64_t D, int32_t elem_bytes, void *stream);
+/* cache[0][pos+t] = k[t], cache[1][pos+t] = v[t] for t < T (rows of D floats). */
+int sm100_kv_append(float *cache, const float *k, const float *v, int64_t ld, const int32_t *pos,
+                    int32_t host_pos, int32_t T, int32_t D, int32_t max_ctx, void *stream);
+int sm100_pos_add(int32_t *counter, int32_t value, void *stream);
+
+/* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
+/* Capture every launch on the backend stream between begin and end into
+ * graph slot `slot` (0..63); replay launches it. */
+int sm100_graph_capture_begin(uint32_t slot);
+int sm100_graph_capture_end(uint32_t slot);
+int sm100_graph_replay(uint32_t slot);
+void sm100_graph_drop(uint32_t slot);
+int sm100_graph_capturing(void);
+
+/* launches issued by this library since load (for reporting) */
+uint64_t sm100_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

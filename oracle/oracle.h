@@ -1,0 +1,101 @@
+/* CPU oracle: a plain-C restatement of the reference's CPU arithmetic for the
+ * tensor track's decode path.  TEST INFRASTRUCTURE ONLY: it is linked by
+ * tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference arm
+ * as the checker, never by the product path (thvm_b200/).
+ *
+ * Every function states the reference op it restates (file:line inside the
+ * reference project).  Each reduction is one float accumulator walked in index
+ * order, as the reference's rendered C loops are (src/codegen/render_uop.c
+ * emits a serial in-thread loop per REDUCE; the CPU JIT compiles it with
+ * -ffp-contract=off, src/backend/cpu/jit.c).  Elementwise constants are the
+ * reference's doubles rounded to float, as a CONST of a float32 graph is.
+ *
+ * Pinned against the fixtures in tests/golden/, which were produced by running the
+ * reference itself (tests/golden/make_golden.py).
+ */
+#ifndef THVM_ORACLE_H
+#define THVM_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* y[m,n] = sum_k x[m,k] * w[n,k] (+ b[n]); w stored (out, in) as nn.Linear
+ * keeps it and read through .T (py/thvm/nn.py:12-25, src/nn/linear.c:1-6,
+ * src/nn/dot.c:1-20).  b may be NULL. */
+void orc_linear_f32(const float *x, const float *w, const float *b, float *y,
+                    int64_t M, int64_t K, int64_t N);
+
+/* (x - mean) * recip(sqrt(mean((x-mean)^2) + eps)) * g + b over the last axis
+ * (src/nn/layernorm.c:1-7, src/nn/reduce.c:28-35, py/thvm/nn.py:160-164).
+ * g, b may be NULL (no affine). */
+void orc_layernorm_f32(const float *x, const float *g, const float *b, float *y,
+                       int64_t M, int64_t D, float eps);
+
+/* x * recip(sqrt(mean(x^2) + eps)) * g (py/thvm/nn.py RMSNorm._norm). */
+void orc_rmsnorm_f32(const float *x, const float *g, float *y, int64_t M, int64_t D,
+                     float eps);
+
+/* softmax over the last axis: max, x - max, exp2(.*log2e), sum, * recip(sum)
+ * (src/nn/softmax.c:1-16, src/nn/elementwise.c:7-9). */
+void orc_softmax_f32(const float *x, float *y, int64_t M, int64_t N);
+
+/* tanh-form GELU, tanh as 2*sigmoid(2x)-1, sigmoid as recip(exp(-x)+1)
+ * (src/nn/elementwise.c:13-34). */
+void orc_gelu_f32(const float *x, float *y, int64_t n);
+
+/* softmax(q k^T * (1/sqrt(D)) + mask) v per (b, h) (src/nn/scaled_dot_product_attention.c:1-34).
+ * q [BH, Lq, D], k and v [BH, Lk, D], y [BH, Lq, D].  mask: NULL, or an additive
+ * [Lq, Lk] float mask broadcast over BH.  causal: 0, or 1 for the is_causal
+ * mask, key j allowed for query i iff j <= i (tril with diagonal 0 on the
+ * [Lq, Lk] grid, src/nn/tri.c:1-17). */
+void orc_sdpa_f32(const float *q, const float *k, const float *v, const float *mask,
+                  float *y, int64_t BH, int64_t Lq, int64_t Lk, int64_t D, int causal);
+
+/* first index of the row max (py/thvm/tensor.py:998-1011): max, compare,
+ * times the descending ramp n..1, max, n - that. */
+void orc_argmax_f32(const float *x, int32_t *out, int64_t M, int64_t N);
+
+/* rows of w [V, D] at idx; an id outside [0, V) reads a zero row
+ * (py/thvm/tensor.py:1706-1714, py/thvm/nn.py Embedding). */
+void orc_embedding_f32(const float *w, const int32_t *idx, float *y, int64_t n_idx,
+                       int64_t V, int64_t D);
+
+/* ---- GPT-2 decoder (bench/gpt2/thvm_gpt2.py:27-128) ------------------------
+ * Weights are pointers into caller memory, Linear weights (out, in). */
+typedef struct {
+  int32_t n_layers, n_heads, dim, vocab, max_ctx;
+  float norm_eps;
+  const float *wte, *wpe, *ln_f_w, *ln_f_b, *lm_head;
+  const float **c_attn_w, **c_attn_b, **c_proj_w, **c_proj_b;
+  const float **c_fc_w, **c_fc_b, **mlp_proj_w, **mlp_proj_b;
+  const float **ln_1_w, **ln_1_b, **ln_2_w, **ln_2_b;
+} OrcGPT2;
+
+/* Opaque decode state: the per-layer KV cache [2, max_ctx, H, hd] and scratch. */
+typedef struct OrcGPT2State OrcGPT2State;
+
+OrcGPT2State *orc_gpt2_state_new(const OrcGPT2 *m);
+void orc_gpt2_state_free(OrcGPT2State *s);
+
+/* One forward over `n_tok` ids at positions start_pos.., updating the cache,
+ * as Transformer.forward (thvm_gpt2.py:91-124): embeddings, the blocks (causal
+ * -inf mask when n_tok > 1), ln_f, lm_head of the last row.  Writes that row's
+ * logits [vocab] when `logits` is non-NULL and returns its argmax. */
+int32_t orc_gpt2_forward(OrcGPT2State *s, const int32_t *tokens, int32_t n_tok,
+                         int32_t start_pos, float *logits);
+
+/* The greedy loop of GPT2.generate (thvm_gpt2.py:195-220) at temperature 0:
+ * the prompt in one forward, then one id per step.  out gets n_new ids. */
+int orc_gpt2_generate(const OrcGPT2 *m, const int32_t *prompt, int32_t n_prompt,
+                      int32_t n_new, int32_t *out);
+
+/* threads the oracle's row-parallel loops use (pthreads), for reporting. */
+int orc_num_threads(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,61 @@
+"""GPT-2 small (fp32, 12 layers, seeded weights) on the sm_100a device against
+the reference's own CPU run (tests/golden/gpt2.npz): the 64 greedy ids must be
+identical, and the logits within 1e-4 of the reference relative to their
+scale (max |dev - ref| <= 1e-4 * max |ref|)."""
+import numpy as np
+import pytest
+
+from thvm_b200.gpt2 import Transformer
+from thvm_b200.synthetic import GPT2_SMALL
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model(device, gpt2_small_weights):
+    return Transformer(GPT2_SMALL, gpt2_small_weights, device)
+
+
+def rel(dev, ref):
+    return float(np.abs(dev - ref).max() / np.abs(ref).max())
+
+
+def test_prompt_and_first_decode_logits(model, golden_gpt2):
+    g = golden_gpt2
+    tok = model.forward(g["prompt"], 0)
+    assert tok == g["tokens"][0]
+    assert rel(model.logits(), g["logits_step0"]) <= 1e-4
+    tok1 = model.forward([tok], len(g["prompt"]))
+    assert tok1 == g["tokens"][1]
+    assert rel(model.logits(), g["logits_step1"]) <= 1e-4
+
+
+def test_greedy_64_tokens_graph_replay(model, golden_gpt2):
+    """Prompt eagerly, then 63 replays of ONE captured decode-step graph with
+    the position and token in device memory."""
+    g = golden_gpt2
+    out = model.generate(g["prompt"], 64)
+    assert out == g["tokens"].tolist()
+    assert rel(model.logits(), g["logits_step63"]) <= 1e-4
+
+
+def test_whole_run_graph_replays_identically(model, golden_gpt2):
+    """63 decode steps captured as one graph that restores (token, position)
+    first: every replay regenerates the same stream."""
+    g = golden_gpt2
+    first = model.forward(g["prompt"], 0)
+    model.capture_run(63, first, len(g["prompt"]))
+    for _ in range(3):
+        model.replay_run()
+        assert model.current_token() == g["tokens"][63]
+
+
+def test_host_inputs_per_step(model, golden_gpt2):
+    """The end-to-end call pattern: host token and position in, host id out."""
+    g = golden_gpt2
+    toks = list(g["prompt"]) + [model.forward(g["prompt"], 0)]
+    model.capture_step()
+    for i in range(8):
+        model.step(token=toks[-1], start_pos=len(toks) - 1)
+        toks.append(model.current_token())
+    assert toks[16:] == g["tokens"][:9].tolist()

@@ -1,0 +1,153 @@
+"""ctypes bindings over libthvm_sm100.so (include/thvm_sm100.h).
+
+The library is the product: there is no CPU fallback.  Loading fails with an
+ImportError when the in-tree build is missing (build it with
+`python -m thvm_b200.build`).
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_uint32, c_uint64, c_void_p
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libthvm_sm100.so"
+
+OK = 0
+ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_OOM, ERR_STATE, ERR_TIMEOUT = -1, -2, -3, -4, -5, -6
+DT_F32, DT_BF16, DT_FP8E4M3, DT_I32 = 0, 1, 2, 3
+
+(K_LINEAR, K_LAYERNORM, K_RMSNORM, K_SOFTMAX, K_GELU, K_ADD, K_ATTENTION, K_EMBEDDING, K_ARGMAX,
+ K_SCATTER, K_KV_APPEND, K_POS_ADD) = range(1, 13)
+
+LIN_LN, LIN_GELU, LIN_RESIDUAL, LIN_KV_APPEND = 1, 2, 4, 8
+
+
+class Sm100Kernel(ctypes.Structure):
+    _fields_ = [
+        ("kind", c_uint32), ("dtype", c_uint32), ("flags", c_uint32),
+        ("inp", c_int32 * 10),
+        ("m", c_int64), ("n", c_int64), ("k", c_int64),
+        ("ld_in", c_int64), ("ld_out", c_int64), ("row_off", c_int64),
+        ("heads", c_int32), ("head_dim", c_int32), ("max_ctx", c_int32), ("causal", c_int32),
+        ("pos", c_int32), ("eps", c_float), ("scale", c_float),
+    ]
+
+    @classmethod
+    def make(cls, kind, slots=None, **kw):
+        k = cls()
+        k.kind = kind
+        for i in range(10):
+            k.inp[i] = -1
+        for s, v in (slots or {}).items():
+            k.inp[s] = v
+        for name, v in kw.items():
+            setattr(k, name, v)
+        return k
+
+
+class Sm100View(ctypes.Structure):
+    _fields_ = [("ndim", c_uint32), ("elem_bytes", c_uint32), ("offset", c_int64),
+                ("dims", c_int64 * 8), ("strides", c_int64 * 8)]
+
+
+class Sm100LinearArgs(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("x", "w", "w_scale", "bias", "ln_g", "ln_b", "residual", "y",
+                                        "kv_cache", "pos")] + [
+        (n, c_int64) for n in ("M", "N", "K", "ldx", "ldy")] + [
+        (n, c_int32) for n in ("wdtype", "flags", "max_ctx", "host_pos")] + [("eps", c_float)]
+
+
+class Sm100AttnArgs(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("q", "k_cache", "v_cache", "out", "pos")] + [
+        ("ldq", c_int64)] + [(n, c_int32) for n in ("T", "H", "hd", "max_ctx", "host_pos")] + [
+        ("scale", c_float)]
+
+
+# name -> (restype, argtypes): every symbol include/thvm_sm100.h declares.
+SIGNATURES = {
+    "sm100_init": (c_int, []),
+    "sm100_shutdown": (None, []),
+    "sm100_last_error": (ctypes.c_char_p, []),
+    "sm100_ready": (c_int, []),
+    "sm100_debug_host_memory": (None, [c_int]),
+    "sm100_buf_alloc": (c_uint32, [c_uint64]),
+    "sm100_buf_free": (None, [c_uint32]),
+    "sm100_buf_incref": (None, [c_uint32]),
+    "sm100_buf_decref": (None, [c_uint32]),
+    "sm100_buf_jit_pin": (None, [c_uint32]),
+    "sm100_buf_jit_unpin": (None, [c_uint32]),
+    "sm100_buf_read": (c_int, [c_uint32, c_void_p, c_uint64]),
+    "sm100_buf_write": (c_int, [c_uint32, c_void_p, c_uint64]),
+    "sm100_buf_copy": (c_int, [c_uint32, c_uint32, c_uint64]),
+    "sm100_buf_write_at": (c_int, [c_uint32, c_uint64, c_void_p, c_uint64]),
+    "sm100_buf_copy_at": (c_int, [c_uint32, c_uint64, c_uint32, c_uint64]),
+    "sm100_buf_refcount": (c_uint32, [c_uint32]),
+    "sm100_buf_freelist_push": (None, [c_uint32]),
+    "sm100_buf_freelist_remove": (None, [c_uint32]),
+    "sm100_buf_storage_root": (c_uint32, [c_uint32]),
+    "sm100_buf_nbytes": (c_uint64, [c_uint32]),
+    "sm100_buf_zero": (None, [c_uint32]),
+    "sm100_buf_view": (c_uint32, [c_uint32, c_uint64, c_uint64]),
+    "sm100_buf_dptr": (c_void_p, [c_uint32]),
+    "sm100_mem_live_bytes": (c_uint64, []),
+    "sm100_mem_peak_bytes": (c_uint64, []),
+    "sm100_buf_live_count": (c_uint32, []),
+    "sm100_stream": (c_void_p, []),
+    "sm100_set_stream": (c_int, [c_void_p]),
+    "sm100_dispatch_begin": (None, []),
+    "sm100_dispatch_flush": (None, []),
+    "sm100_dispatch_end": (None, []),
+    "sm100_dispatch_kernel": (c_int, [POINTER(Sm100Kernel), POINTER(c_uint32), c_uint32, c_uint32]),
+    "sm100_gather_strided": (c_int, [c_uint32, c_uint32, POINTER(Sm100View)]),
+    "sm100_linear": (c_int, [POINTER(Sm100LinearArgs), c_void_p]),
+    "sm100_attention": (c_int, [POINTER(Sm100AttnArgs), c_void_p]),
+    "sm100_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
+    "sm100_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_float, c_void_p]),
+    "sm100_softmax": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
+    "sm100_gelu": (c_int, [c_void_p, c_void_p, c_int64, c_void_p]),
+    "sm100_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "sm100_embedding": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                c_void_p]),
+    "sm100_argmax": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p]),
+    "sm100_scatter_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32, c_void_p]),
+    "sm100_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int32,
+                                c_int32, c_void_p]),
+    "sm100_pos_add": (c_int, [c_void_p, c_int32, c_void_p]),
+    "sm100_graph_capture_begin": (c_int, [c_uint32]),
+    "sm100_graph_capture_end": (c_int, [c_uint32]),
+    "sm100_graph_replay": (c_int, [c_uint32]),
+    "sm100_graph_drop": (None, [c_uint32]),
+    "sm100_graph_capturing": (c_int, []),
+    "sm100_launch_count": (c_uint64, []),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library with every declared signature bound."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m thvm_b200.build` "
+                              "(the sm_100a device has no CPU fallback)")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = L
+    return _lib
+
+
+class Sm100Error(RuntimeError):
+    def __init__(self, code: int, what: str):
+        msg = lib().sm100_last_error()
+        super().__init__(f"{what} failed ({code}): {msg.decode() if msg else ''}")
+        self.code = code
+
+
+def check(code: int, what: str) -> int:
+    if code != OK:
+        raise Sm100Error(code, what)
+    return code
