@@ -118,7 +118,7 @@ extern "C" int sm100_attention(const Sm100AttnArgs *a, void *stream) {
   p.scale = a->scale != 0.0f ? a->scale : (float)(1.0 / sqrt((double)a->hd));
   const size_t smem = sizeof(float) * ((size_t)a->max_ctx + (size_t)a->hd + 256);
   if (smem > 227 * 1024) return sm100_set_error(SM100_ERR_UNSUPPORTED, "attention: max_ctx too large");
-  if (smem > 48 * 1024)
+  if (smem > 40 * 1024)
     cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   dim3 grid((unsigned)a->H, (unsigned)a->T);
   attn_kernel<<<grid, 256, smem, (cudaStream_t)stream>>>(p);

@@ -251,8 +251,9 @@ static int launch_tpr(const LinParams &p, bool vec, cudaStream_t st) {
   const int64_t grid = (p.N + RPC - 1) / RPC;
   const size_t smem = sizeof(float) * (size_t)MB * (size_t)p.K;
   auto kern = vec ? linear_kernel<WT, TPR, MB, true> : linear_kernel<WT, TPR, MB, false>;
-  if (smem > 48 * 1024) {
-    if (smem > 227 * 1024) return sm100_set_error(SM100_ERR_UNSUPPORTED, "linear: K=%lld too large", (long long)p.K);
+  // dynamic + static shared memory above the default 48 KB needs the opt-in
+  if (smem > 40 * 1024) {
+    if (smem > 220 * 1024) return sm100_set_error(SM100_ERR_UNSUPPORTED, "linear: K=%lld too large", (long long)p.K);
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }
   kern<<<(unsigned)grid, 256, smem, st>>>(p);

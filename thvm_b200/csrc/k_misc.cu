@@ -259,12 +259,16 @@ extern "C" int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, in
   if (!x || !out || M < 0 || N <= 0 || N > 0x7ffffffe || M > 65535)
     return sm100_set_error(SM100_ERR_ARG, "argmax: bad arguments");
   if (M == 0) return SM100_OK;
-  const uint64_t need = (uint64_t)M * kArgmaxMaxBlocks * 8 + (uint64_t)M * 4;
+  // Workspace: per-row completion counters at a fixed offset (each reset to
+  // 0 by the CTA that consumes it, so they start at 0 for every launch
+  // whatever the previous launch's row count), then the per-CTA partials.
+  const uint64_t counters = 65536 * 4;
+  const uint64_t need = counters + (uint64_t)M * kArgmaxMaxBlocks * 8;
   char *ws = (char *)sm100_workspace(need);
   if (!ws) return sm100_set_error(SM100_ERR_OOM, "argmax: no workspace");
-  float *pv = (float *)ws;
-  int32_t *pi = (int32_t *)(ws + (uint64_t)M * kArgmaxMaxBlocks * 4);
-  uint32_t *counter = (uint32_t *)(ws + (uint64_t)M * kArgmaxMaxBlocks * 8);
+  uint32_t *counter = (uint32_t *)ws;
+  float *pv = (float *)(ws + counters);
+  int32_t *pi = (int32_t *)(ws + counters + (uint64_t)M * kArgmaxMaxBlocks * 4);
   int64_t nb = (N + 256 * 8 - 1) / (256 * 8);
   if (nb > kArgmaxMaxBlocks) nb = kArgmaxMaxBlocks;
   dim3 grid((unsigned)nb, (unsigned)M);
