@@ -236,6 +236,24 @@ int sm100_embedding(const float *table, const int32_t *idx, const float *pos_tab
  * bump (optional) is incremented by 1 after the write. */
 int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
                  int32_t *bump, void *stream);
+/* sm100_argmax without any device allocation.  This entry point has no
+ * counterpart in the reference: it is for callers that cannot allocate device
+ * memory (a plugin whose device memory all belongs to a host framework's
+ * allocator, code recording a CUDA graph that must add no allocation nodes,
+ * a process whose device budget is spent).  Its scratch is a fixed array
+ * compiled into this library (about 33 KB per GPU that loads the library,
+ * held until the process exits): at most SM100_ARGMAX_NOALLOC_MAX_ROWS rows
+ * per call, more is rejected with SM100_ERR_ARG.  Same results as
+ * sm100_argmax.  It calls no cudaMalloc / cudaFree; it clears the array's
+ * counters with cudaMemsetAsync on `stream` before each launch.  The first
+ * call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * which may load the module), so make that first call before any stream
+ * capture.  Every call shares the one array: calls that can overlap on the
+ * GPU (other streams, other host threads) race and must be serialised by the
+ * caller. */
+#define SM100_ARGMAX_NOALLOC_MAX_ROWS 64
+int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
+                         int32_t *bump, void *stream);
 /* dst[idx[i]] = src[i], rows of D elements of elem_bytes; idx outside [0, V) skipped. */
 int sm100_scatter_rows(void *dst, const int32_t *idx, const void *src, int64_t n_idx,
                        int64_t V, int64_t D, int32_t elem_bytes, void *stream);

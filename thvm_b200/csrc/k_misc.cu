@@ -318,3 +318,55 @@ extern "C" int sm100_gather_strided_dev(void *dst, const void *src, const Sm100V
   gather_strided_kernel<<<ew_grid(v.total), 256, 0, (cudaStream_t)stream>>>((char *)dst, (const char *)src, v);
   return launch_status("gather_strided");
 }
+
+// ---- argmax without device allocation ------------------------------------
+// For callers that cannot allocate device memory: a plugin whose device
+// memory all belongs to a host framework's allocator, code that runs while a
+// CUDA graph is being captured and must add no allocation nodes, or a process
+// whose device-memory budget is already spent.  The scratch that argmax needs
+// (per-row completion counters and per-CTA partials) lives in this fixed
+// array instead, which every GPU that loads this library holds until the
+// process exits.
+#define ARGMAX_NOALLOC_COUNTER_BYTES 256
+#define ARGMAX_NOALLOC_BYTES \
+  (ARGMAX_NOALLOC_COUNTER_BYTES + 2 * SM100_ARGMAX_NOALLOC_MAX_ROWS * 64 * 4)
+
+static __device__ __align__(256) unsigned char g_argmax_noalloc_scratch[ARGMAX_NOALLOC_BYTES];
+
+// Device address of the array per device ordinal (host code may not use the
+// array's name as an address: that is only a host-side stand-in).
+static void *g_argmax_noalloc_dev[64];
+
+extern "C" int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
+                                    int32_t *bump, void *stream) {
+  if (!x || !out || M < 0 || N <= 0 || N > 0x7ffffffe)
+    return sm100_set_error(SM100_ERR_ARG, "argmax_noalloc: bad arguments");
+  if (M > SM100_ARGMAX_NOALLOC_MAX_ROWS)
+    return sm100_set_error(SM100_ERR_ARG, "argmax_noalloc: %lld rows exceed the static scratch limit of %d rows",
+                           (long long)M, SM100_ARGMAX_NOALLOC_MAX_ROWS);
+  if (M == 0) return SM100_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "argmax_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_UNSUPPORTED, "argmax_noalloc: device %d", dev);
+  if (!g_argmax_noalloc_dev[dev]) {
+    // once per device, with that device current
+    void *p = NULL;
+    e = cudaGetSymbolAddress(&p, g_argmax_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return sm100_set_error(SM100_ERR_CUDA, "argmax_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_argmax_noalloc_dev[dev] = p;
+  }
+  char *ws = (char *)g_argmax_noalloc_dev[dev];
+  uint32_t *counter = (uint32_t *)ws;
+  float *pv = (float *)(ws + ARGMAX_NOALLOC_COUNTER_BYTES);
+  int32_t *pi = (int32_t *)(ws + ARGMAX_NOALLOC_COUNTER_BYTES + (size_t)M * kArgmaxMaxBlocks * 4);
+  // the array keeps the previous call's contents: the counters must start at 0
+  e = cudaMemsetAsync(counter, 0, ARGMAX_NOALLOC_COUNTER_BYTES, (cudaStream_t)stream);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "argmax_noalloc: cudaMemsetAsync: %s", cudaGetErrorString(e));
+  int64_t nb = (N + 256 * 8 - 1) / (256 * 8);
+  if (nb > kArgmaxMaxBlocks) nb = kArgmaxMaxBlocks;
+  dim3 grid((unsigned)nb, (unsigned)M);
+  argmax_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(x, N, ld ? ld : N, out, bump, pv, pi, counter);
+  return launch_status("argmax_noalloc");
+}
