@@ -129,7 +129,8 @@ enum {
   SM100_K_ARGMAX,       /* first index of each row's max (int32) */
   SM100_K_SCATTER,      /* dst[idx[i]] = src[i] rows, idx outside [0, V) skipped */
   SM100_K_KV_APPEND,    /* cache[:, pos:pos+T] = stack(k, v) at a device position */
-  SM100_K_POS_ADD       /* device int32 counter += value (the kvar bump) */
+  SM100_K_POS_ADD,      /* device int32 counter += value (the kvar bump) */
+  SM100_K_DECODE_STEP   /* the fused GPT-2 decode step (sm100_decode_step) */
 };
 
 /* Linear flags */
@@ -175,6 +176,8 @@ typedef struct {
  *  KV_APPEND  in[0]=k rows in[1]=v rows [m, k] (stride ld_in) in[7]=position;
  *             out = cache [2, max_ctx, k]
  *  POS_ADD    out = i32 counter; pos = value to add
+ *  DECODE_STEP in[0]=an Sm100DecodeModel in device memory; m = n_layers,
+ *             k = dim, max_ctx, n = tokens (0 means 1); out = the model's io buffer
  */
 int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *in_buf_ids, uint32_t n_in,
                           uint32_t out_buf_id);
@@ -261,6 +264,62 @@ int sm100_scatter_rows(void *dst, const int32_t *idx, const void *src, int64_t n
 int sm100_kv_append(float *cache, const float *k, const float *v, int64_t ld, const int32_t *pos,
                     int32_t host_pos, int32_t T, int32_t D, int32_t max_ctx, void *stream);
 int sm100_pos_add(int32_t *counter, int32_t value, void *stream);
+
+/* ---- fused decode step ---------------------------------------------------- */
+/* One GPT-2 decode step (batch 1, fp32 weights and activations) as one
+ * persistent kernel: the whole schedule of bench/gpt2/thvm_gpt2.py's
+ * Transformer.forward for a single token at the device position
+ * (embedding, n_layers x {ln_1 + c_attn + KV append, attention, c_proj +
+ * residual, ln_2 + c_fc + GELU, mlp.c_proj + residual}, ln_f + lm_head,
+ * argmax), i.e. what jit_replay runs per token (src/jit/capture.c:2687).
+ * The model descriptor lives in DEVICE memory (the caller uploads it);
+ * io = [position, token] int32 is read at the start and, unless an error
+ * was flagged, the next token written to io[1] (and io[0] += 1 when bump). */
+#define SM100_DECODE_MAX_LAYERS 48
+enum {
+  SM100_DECODE_ERR_STALL = 1u << 0,   /* a ring (mbarrier) wait timed out */
+  SM100_DECODE_ERR_BARRIER = 1u << 1, /* a wait for another CTA's output timed out */
+  SM100_DECODE_ERR_ARG = 1u << 2      /* position outside [0, max_ctx) */
+};
+typedef struct {
+  int32_t n_layers, dim, hidden, vocab, max_ctx, heads, head_dim, bump;
+  float eps, attn_scale;
+  const float *wte, *wpe, *ln_f_g, *ln_f_b, *lm_head;
+  const float *ln1_g[SM100_DECODE_MAX_LAYERS], *ln1_b[SM100_DECODE_MAX_LAYERS];
+  const float *w_qkv[SM100_DECODE_MAX_LAYERS], *b_qkv[SM100_DECODE_MAX_LAYERS];
+  const float *w_o[SM100_DECODE_MAX_LAYERS], *b_o[SM100_DECODE_MAX_LAYERS];
+  const float *ln2_g[SM100_DECODE_MAX_LAYERS], *ln2_b[SM100_DECODE_MAX_LAYERS];
+  const float *w_fc[SM100_DECODE_MAX_LAYERS], *b_fc[SM100_DECODE_MAX_LAYERS];
+  const float *w_p2[SM100_DECODE_MAX_LAYERS], *b_p2[SM100_DECODE_MAX_LAYERS];
+  float *kv_cache[SM100_DECODE_MAX_LAYERS]; /* [2, max_ctx, dim] each */
+  int32_t *io;                              /* [position, token] */
+  /* step outputs as tagged words (float bits | tag << 32), zero-initialised:
+   * x [dim], qkv [3 dim], att [dim], fc [hidden] */
+  uint64_t *x_w, *qkv_w, *att_w, *fc_w;
+  uint64_t *part_w;                         /* per-CTA argmax partials, sm100_decode_part_bytes() */
+  float *logits;                            /* [vocab], or NULL: not stored */
+  /* optional phase timeline, or NULL: [grid][5 n_layers + 1][4] u64 global
+   * timer ns per CTA and phase: barrier arrive, barrier passed, input
+   * staged, phase done (sm100_decode_trace_bytes) */
+  uint64_t *trace;
+  /* zero-initialised scratch of sm100_decode_sync_bytes(): sync[1] completion
+   * counter (reset by the kernel), sync[2] the sticky status word
+   * (SM100_DECODE_ERR_* bits; cleared by the caller), sync[3] the launch
+   * epoch the tags derive from, then per-CTA argmax partials */
+  uint32_t *sync;
+} Sm100DecodeModel;
+uint64_t sm100_decode_sync_bytes(void);
+uint64_t sm100_decode_part_bytes(void);
+uint64_t sm100_decode_trace_bytes(int32_t n_layers);
+/* n_tokens greedy tokens in one launch (positions io[0] .. io[0]+n-1, each
+ * token's argmax feeding the next); head_dim 32 or 64, dim % 32 == 0,
+ * 4*dim <= 4096, max_ctx <= 3392, n_tokens * (5 n_layers + 2) < 65536, and one
+ * CTA's row slice of every projection within 80 KB (GPT-2 small on 148 SMs) */
+int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_tokens, int32_t n_layers,
+                       int32_t dim, int32_t max_ctx, void *stream);
+/* one token: sm100_decode_steps with n_tokens = 1 */
+int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim,
+                      int32_t max_ctx, void *stream);
 
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into

@@ -50,6 +50,40 @@ def test_whole_run_graph_replays_identically(model, golden_gpt2):
         assert model.current_token() == g["tokens"][63]
 
 
+def test_fused_and_per_op_steps_agree(device, gpt2_small_weights, golden_gpt2):
+    """The fused decode-step kernel and the per-op schedule (both as graph
+    replays) give the golden ids, with logits within 1e-4 of each other."""
+    g = golden_gpt2
+    per_op = Transformer(GPT2_SMALL, gpt2_small_weights, device, fused=False)
+    fused = Transformer(GPT2_SMALL, gpt2_small_weights, device, fused=True)
+    assert fused.fused and not per_op.fused
+    for m in (per_op, fused):
+        m.forward(g["prompt"], 0)
+        m.capture_step()
+    for i in range(12):
+        per_op.step()
+        fused.step()
+        a, b = per_op.current_token(), fused.current_token()
+        assert a == b == g["tokens"][i + 1], (i, a, b)
+        assert rel(fused.logits(), per_op.logits()) <= 1e-4
+    assert fused.decode_status() == 0
+
+
+def test_fused_step_rejects_out_of_range_position(model, golden_gpt2):
+    """A position outside the cache is caught by the kernel's own bounds
+    check: the status word says so and no token is published."""
+    from thvm_b200 import _lib as L
+    g = golden_gpt2
+    model.forward(g["prompt"], 0)
+    model.capture_step()
+    model.step(token=1234, start_pos=GPT2_SMALL.max_ctx)
+    assert model.current_token() == 1234
+    assert model.decode_status() & L.DECODE_ERR_ARG
+    assert model.decode_status() == 0            # cleared by the read above
+    model.step(token=int(g["tokens"][0]), start_pos=len(g["prompt"]))
+    assert model.current_token() == g["tokens"][1]
+
+
 def test_host_inputs_per_step(model, golden_gpt2):
     """The end-to-end call pattern: host token and position in, host id out."""
     g = golden_gpt2

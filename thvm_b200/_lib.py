@@ -7,17 +7,21 @@ ImportError when the in-tree build is missing (build it with
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_uint32, c_uint64, c_void_p
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / "libthvm_sm100.so"
+LIB_PATH = Path(os.environ.get("THVM_SM100_LIB") or Path(__file__).resolve().parent / "libthvm_sm100.so")
 
 OK = 0
 ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_OOM, ERR_STATE, ERR_TIMEOUT = -1, -2, -3, -4, -5, -6
 DT_F32, DT_BF16, DT_FP8E4M3, DT_I32 = 0, 1, 2, 3
 
 (K_LINEAR, K_LAYERNORM, K_RMSNORM, K_SOFTMAX, K_GELU, K_ADD, K_ATTENTION, K_EMBEDDING, K_ARGMAX,
- K_SCATTER, K_KV_APPEND, K_POS_ADD) = range(1, 13)
+ K_SCATTER, K_KV_APPEND, K_POS_ADD, K_DECODE_STEP) = range(1, 14)
+
+DECODE_MAX_LAYERS = 48
+DECODE_ERR_STALL, DECODE_ERR_BARRIER, DECODE_ERR_ARG = 1, 2, 4
 
 LIN_LN, LIN_GELU, LIN_RESIDUAL, LIN_KV_APPEND = 1, 2, 4, 8
 
@@ -61,6 +65,19 @@ class Sm100AttnArgs(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("q", "k_cache", "v_cache", "out", "pos")] + [
         ("ldq", c_int64)] + [(n, c_int32) for n in ("T", "H", "hd", "max_ctx", "host_pos")] + [
         ("scale", c_float)]
+
+
+_PL = ctypes.c_void_p * DECODE_MAX_LAYERS
+
+
+class Sm100DecodeModel(ctypes.Structure):
+    _fields_ = [(n, c_int32) for n in ("n_layers", "dim", "hidden", "vocab", "max_ctx", "heads", "head_dim",
+                                       "bump")] + [
+        ("eps", c_float), ("attn_scale", c_float)] + [
+        (n, c_void_p) for n in ("wte", "wpe", "ln_f_g", "ln_f_b", "lm_head")] + [
+        (n, _PL) for n in ("ln1_g", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_g", "ln2_b", "w_fc", "b_fc",
+                           "w_p2", "b_p2", "kv_cache")] + [
+        (n, c_void_p) for n in ("io", "x_w", "qkv_w", "att_w", "fc_w", "part_w", "logits", "trace", "sync")]
 
 
 # name -> (restype, argtypes): every symbol include/thvm_sm100.h declares.
@@ -114,6 +131,11 @@ SIGNATURES = {
     "sm100_kv_append": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_int32, c_int32, c_int32,
                                 c_int32, c_void_p]),
     "sm100_pos_add": (c_int, [c_void_p, c_int32, c_void_p]),
+    "sm100_decode_sync_bytes": (c_uint64, []),
+    "sm100_decode_trace_bytes": (c_uint64, [c_int32]),
+    "sm100_decode_part_bytes": (c_uint64, []),
+    "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p]),
+    "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),

@@ -537,6 +537,10 @@ int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *ids, uint32_t n_
     case SM100_K_POS_ADD:
       if (!out) return sm100_set_error(SM100_ERR_ARG, "pos_add: dead counter buffer");
       return sm100_pos_add((int32_t *)out, k->pos, st);
+    case SM100_K_DECODE_STEP:
+      if (!p[0]) return sm100_set_error(SM100_ERR_ARG, "decode_step: no model descriptor");
+      return sm100_decode_steps((const Sm100DecodeModel *)p[0], k->n > 0 ? (int32_t)k->n : 1, (int32_t)k->m,
+                                (int32_t)k->k, k->max_ctx, st);
     default:
       return sm100_set_error(SM100_ERR_UNSUPPORTED, "dispatch_kernel: kind %u", k->kind);
   }

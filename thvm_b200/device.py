@@ -88,6 +88,15 @@ class Device:
             raise L.Sm100Error(L.ERR_CUDA, "dispatch_end")
 
     # ---- graphs (TinyJit replay) -----------------------------------------
+    _next_slot = 0
+
+    def new_graph_slot(self) -> int:
+        """A graph slot no other user of this Device holds (64 per process)."""
+        if Device._next_slot >= 64:
+            raise L.Sm100Error(L.ERR_STATE, "graph slots exhausted")
+        Device._next_slot += 1
+        return Device._next_slot - 1
+
     def capture_begin(self, slot: int) -> None:
         check(self.lib.sm100_graph_capture_begin(slot), "graph_capture_begin")
 

@@ -23,6 +23,8 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
+import ctypes
+
 import numpy as np
 
 from . import _lib as L
@@ -143,10 +145,9 @@ class _State:
 class Transformer:
     """GPT-2 decoder (thvm_gpt2.py:81-128) on the sm_100a device."""
 
-    GRAPH_STEP = 0
-    GRAPH_RUN = 1
 
-    def __init__(self, cfg: GPT2Config, weights: dict, device: Device | None = None, max_prompt: int = 128):
+    def __init__(self, cfg: GPT2Config, weights: dict, device: Device | None = None, max_prompt: int = 128,
+                 fused: bool = True):
         self.cfg = cfg
         dev = self.dev = device or Device.get()
         self.wte = dev.upload(weights["wte.weight"])
@@ -156,6 +157,90 @@ class Transformer:
         self.lm_head = Linear(dev, weights["lm_head.weight"], None)
         self.s = _State(dev, cfg, max_prompt)
         self._run_tokens = 0
+        # graph slots of this model: one decode step; one whole generation
+        self.GRAPH_STEP = dev.new_graph_slot()
+        self.GRAPH_RUN = dev.new_graph_slot()
+        self.fused = fused and self.fused_fits(cfg)
+        if self.fused:
+            self._build_fused()
+
+    @staticmethod
+    def fused_fits(cfg: GPT2Config) -> bool:
+        """Shapes the fused decode-step kernel takes (include/thvm_sm100.h)."""
+        return (cfg.n_layers <= L.DECODE_MAX_LAYERS and cfg.dim % 32 == 0 and 4 * cfg.dim <= 4096
+                and cfg.max_ctx <= 3392 and cfg.head_dim in (32, 64))
+
+    def _build_fused(self) -> None:
+        """The device-resident Sm100DecodeModel over this model's buffers."""
+        cfg, dev, s = self.cfg, self.dev, self.s
+        p = dev.dptr
+        m = L.Sm100DecodeModel()
+        m.n_layers, m.dim, m.hidden, m.vocab = cfg.n_layers, cfg.dim, cfg.hidden, cfg.vocab
+        m.max_ctx, m.heads, m.head_dim, m.bump = cfg.max_ctx, cfg.n_heads, cfg.head_dim, 1
+        m.eps, m.attn_scale = cfg.norm_eps, float(1.0 / np.sqrt(cfg.head_dim))
+        m.wte, m.wpe = p(self.wte), p(self.wpe)
+        m.ln_f_g, m.ln_f_b, m.lm_head = p(self.ln_f.g), p(self.ln_f.b), p(self.lm_head.w)
+        for i, blk in enumerate(self.h):
+            m.ln1_g[i], m.ln1_b[i] = p(blk.ln_1.g), p(blk.ln_1.b)
+            m.w_qkv[i], m.b_qkv[i] = p(blk.attn.c_attn.w), p(blk.attn.c_attn.b)
+            m.w_o[i], m.b_o[i] = p(blk.attn.c_proj.w), p(blk.attn.c_proj.b)
+            m.ln2_g[i], m.ln2_b[i] = p(blk.ln_2.g), p(blk.ln_2.b)
+            m.w_fc[i], m.b_fc[i] = p(blk.mlp.c_fc.w), p(blk.mlp.c_fc.b)
+            m.w_p2[i], m.b_p2[i] = p(blk.mlp.c_proj.w), p(blk.mlp.c_proj.b)
+            m.kv_cache[i] = p(blk.attn.cache_kv)
+        # the kernel's step outputs: tagged 8-byte words, zero-initialised
+        self.words = [dev.alloc(8 * n) for n in (cfg.dim, 3 * cfg.dim, cfg.dim, cfg.hidden)]
+        m.io = p(s.io)
+        m.x_w, m.qkv_w, m.att_w, m.fc_w = (p(b) for b in self.words)
+        self.part = dev.alloc(dev.lib.sm100_decode_part_bytes())
+        m.part_w = p(self.part)
+        m.logits = p(s.logits)
+        self.sync = dev.alloc(dev.lib.sm100_decode_sync_bytes())
+        m.sync = p(self.sync)
+        self.desc = dev.alloc(ctypes.sizeof(m))
+        L.check(dev.lib.sm100_buf_write(self.desc, ctypes.addressof(m), ctypes.sizeof(m)), "buf_write(desc)")
+        self._desc_host = m
+        self.fused_op = self.fused_tokens_op(1)
+
+    def fused_tokens_op(self, n_tokens: int) -> Op:
+        """The fused kernel over n greedy tokens (one launch)."""
+        cfg = self.cfg
+        return make_op(L.K_DECODE_STEP, self.s.io, {0: self.desc}, m=cfg.n_layers, k=cfg.dim,
+                       max_ctx=cfg.max_ctx, n=n_tokens)
+
+    def set_trace(self, on: bool = True) -> None:
+        """Record the fused kernel's per-CTA phase timeline (read_trace); the
+        step graphs must be captured again after a change."""
+        if not self.fused:
+            raise ValueError("tracing is a feature of the fused decode step")
+        m = self._desc_host
+        if on:
+            if not getattr(self, "trace", None):
+                self.trace = self.dev.alloc(self.dev.lib.sm100_decode_trace_bytes(self.cfg.n_layers))
+            m.trace = self.dev.dptr(self.trace)
+        else:
+            m.trace = None
+        L.check(self.dev.lib.sm100_buf_write(self.desc, ctypes.addressof(m), ctypes.sizeof(m)), "buf_write(desc)")
+
+    def read_trace(self, grid: int) -> np.ndarray:
+        """[grid, 5 n_layers + 1, 4] ns: barrier arrive, barrier passed,
+        input staged, phase done (kernel-relative after subtracting the min)."""
+        n = grid * (5 * self.cfg.n_layers + 1) * 4
+        return self.dev.read(self.trace, np.uint64, (n,)).reshape(grid, -1, 4)
+
+    def step_ops(self) -> list:
+        """The kernels of one decode step (T = 1, bump): the fused kernel, or
+        the per-op schedule."""
+        return [self.fused_op] if self.fused else self.forward_ops(1, bump=True)
+
+    def decode_status(self, clear: bool = True) -> int:
+        """The fused kernel's sticky status word (0 = no error)."""
+        if not self.fused:
+            return 0
+        st = int(self.dev.read(self.sync, np.uint32, (4,))[2])
+        if clear and st:
+            self.dev.write(self.sync, np.zeros(4, np.uint32))
+        return st
 
     # ---- the schedule ---------------------------------------------------
     def forward_ops(self, T: int, bump: bool) -> list:
@@ -200,7 +285,7 @@ class Transformer:
         writes the next id to tok[0] and advances pos."""
         self.dev.capture_begin(self.GRAPH_STEP)
         try:
-            self._run(self.forward_ops(1, bump=True))
+            self._run(self.step_ops())
         finally:
             self.dev.capture_end(self.GRAPH_STEP)
 
@@ -218,15 +303,19 @@ class Transformer:
     def capture_run(self, n_tokens: int, token: int, start_pos: int) -> None:
         """n_tokens greedy decode steps as ONE graph that first restores
         (tok, pos) = (token, start_pos), so every replay regenerates the same
-        stream: the decode loop of GPT2.generate (thvm_gpt2.py:195-220)."""
+        stream: the decode loop of GPT2.generate (thvm_gpt2.py:195-220).
+        Fused: the n tokens are one launch of the persistent kernel."""
         self.dev.write(self.s.start, np.array([token, start_pos], np.int32))
-        ops = self.forward_ops(1, bump=True)
         self.dev.capture_begin(self.GRAPH_RUN)
         try:
             self.dev.copy_at(self.s.tok, 0, self.s.start, 4)
             self._copy_pos_from_start()
-            for _ in range(n_tokens):
-                self._run(ops)
+            if self.fused:
+                self._run([self.fused_tokens_op(n_tokens)])
+            else:
+                ops = self.step_ops()
+                for _ in range(n_tokens):
+                    self._run(ops)
         finally:
             self.dev.capture_end(self.GRAPH_RUN)
         self._run_tokens = n_tokens
