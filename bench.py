@@ -11,8 +11,10 @@ data-path collective), so scaling is weak.
 
 Also reported: `e2e` (the same 64 tokens per step through the C-ABI with the
 token and position written from pinned host memory and the next id read back
-every token), `roofline` (the linear kernel that streams the weights, timed on
-the library's stream with CUDA events), `cpu_baseline` (the CPU oracle port on
+every token), `roofline` (the fused decode kernel: algorithmic bytes of its
+64-token launch over the event-timed launch, against the measured HBM copy
+bandwidth; `traffic` from the committed ncu summary), `cpu_baseline` (the CPU
+oracle port on
 the host cores), the SM clocks sampled during the timed region, and the
 kernel launch count.  `--impl reference` times the CPU path instead.
 """
@@ -102,6 +104,20 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def _ncu_traffic(kernel):
+    """DRAM bytes (read + write) of one launch of `kernel` from its committed
+    ncu summary (a `traffic_bytes_per_launch:` line in profiles/<kernel>_*.md),
+    or None when no capture of the current kernel is committed."""
+    for p in sorted((ROOT / "profiles").glob(f"{kernel}_*.md")):
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                try:
+                    return int(line.split(":", 1)[1].strip())
+                except ValueError:
+                    return None
+    return None
+
+
 def linear_bytes(cfg, T=1):
     """Algorithmic bytes of the decode step's linear launches: every weight,
     bias and LayerNorm parameter once, the x rows read, the outputs written
@@ -114,13 +130,23 @@ def linear_bytes(cfg, T=1):
     return cfg.n_layers * per_layer + head, cfg.n_layers * 4 + 1
 
 
-def token_bytes(cfg, mean_len):
-    """Algorithmic HBM bytes of one decode token at KV length mean_len:
-    all weights once + the two embedding rows + KV reads and the new KV row."""
+def weight_params(cfg):
+    """Parameters one decode token reads: every block (c_attn 3d x d, c_proj
+    d x d, c_fc h x d, mlp.c_proj d x h, their biases, two LayerNorms), ln_f
+    and lm_head; the embeddings contribute one row each (counted per token)."""
+    d, h = cfg.dim, cfg.hidden
+    block = 3 * d * d + d * d + h * d + d * h + (3 * d + d + h + d) + 4 * d
+    return cfg.n_layers * block + 2 * d + cfg.vocab * d
+
+
+def tokens_bytes(cfg, pos0, n):
+    """Algorithmic HBM bytes of n decode tokens at positions pos0..pos0+n-1:
+    per token all weights once, the wte and wpe rows, the keys and values of
+    the earlier positions (pos rows per layer) and the new row written."""
     d = cfg.dim
-    params = (cfg.n_layers * (4 * d * d + 4 * d * 4 * d + 4 * d + 4 * d + 4 * d)
-              + 2 * d + cfg.vocab * d)
-    return 4 * params + 2 * 4 * d + cfg.n_layers * 2 * 4 * d * mean_len + cfg.n_layers * 2 * 4 * d
+    per_tok = 4 * weight_params(cfg) + 2 * 4 * d + cfg.n_layers * 2 * 4 * d
+    kv_rows = sum(range(pos0, pos0 + n))
+    return n * per_tok + cfg.n_layers * 2 * 4 * d * kv_rows
 
 
 def cpu_baseline(cfg, weights, prompt, seconds=15.0):
@@ -245,16 +271,19 @@ def main():
 
     # ---- roofline of the dominant kernel --------------------------------
     hbm, peak_kind = _peaks()
-    tb = token_bytes(cfg, mean_len=N_PROMPT + N_NEW // 2)
-    step_gbs = tb * N_NEW * args.steps / (ms / 1e3) / 1e9
+    run_bytes = tokens_bytes(cfg, N_PROMPT, N_NEW)
+    step_gbs = run_bytes * args.steps / (ms / 1e3) / 1e9
     if model.fused:
-        # one decode_step_kernel launch per token: its average duration is the
-        # timed region's per-token time (the run graph holds 64 of them)
-        kern_us = ms * 1e3 / (args.steps * N_NEW)
-        roof = {"bound": "hbm", "kernel": "decode_step_kernel (fused GPT-2 decode step, 1 launch per token)",
-                "achieved": round(tb / (kern_us / 1e6) / 1e9, 1), "peak": hbm, "unit": "GB/s",
-                "frac": round(tb / (kern_us / 1e6) / 1e9 / hbm, 4), "peak_source": peak_kind,
-                "bytes_per_launch": tb, "avg_launch_us": round(kern_us, 3), "traffic": None}
+        # the run graph is one decode_kernel launch over the 64 tokens plus
+        # two 4-byte copy nodes that reset (token, position): the replay's
+        # event-timed duration is the launch's duration (copies included)
+        kern_us = ms * 1e3 / args.steps
+        ach = run_bytes / (kern_us / 1e6) / 1e9
+        roof = {"bound": "hbm", "kernel": "decode_kernel (fused GPT-2 decode, 64 tokens per launch)",
+                "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(ach / hbm, 4), "peak_source": peak_kind,
+                "bytes_per_launch": run_bytes, "avg_launch_us": round(kern_us, 3),
+                "traffic": _ncu_traffic("decode_kernel")}
     else:
         lin_ops = [op for op in model.forward_ops(1, bump=False) if op.kernel.kind == 1]
         dev.write(model.s.io, np.array([N_PROMPT + 32, first], np.int32))
@@ -280,7 +309,7 @@ def main():
                 "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                 "peak_source": peak_kind, "bytes_per_launch": round(lb / nl), "launches": nl,
                 "avg_launch_us": round(lin_ms * 1e3 / nl, 3), "traffic": None}
-    roof["step"] = {"algorithmic_bytes_per_token": tb, "achieved_gbs": round(step_gbs, 1),
+    roof["step"] = {"algorithmic_bytes_per_token": round(run_bytes / N_NEW), "achieved_gbs": round(step_gbs, 1),
                     "frac": round(step_gbs / hbm, 4)}
     status = model.decode_status()
     if status:
