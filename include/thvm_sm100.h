@@ -177,7 +177,8 @@ typedef struct {
  *             out = cache [2, max_ctx, k]
  *  POS_ADD    out = i32 counter; pos = value to add
  *  DECODE_STEP in[0]=an Sm100DecodeModel in device memory; m = n_layers,
- *             k = dim, max_ctx, n = tokens (0 means 1); out = the model's io buffer
+ *             k = dim, heads, ld_out = vocab (lm_head rows), max_ctx,
+ *             n = tokens (0 means 1); out = the model's io buffer
  */
 int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *in_buf_ids, uint32_t n_in,
                           uint32_t out_buf_id);
@@ -276,6 +277,7 @@ int sm100_pos_add(int32_t *counter, int32_t value, void *stream);
  * io = [position, token] int32 is read at the start and, unless an error
  * was flagged, the next token written to io[1] (and io[0] += 1 when bump). */
 #define SM100_DECODE_MAX_LAYERS 48
+#define SM100_DECODE_REPLICAS 8   /* copies of every step output a launch writes */
 enum {
   SM100_DECODE_ERR_STALL = 1u << 0,   /* a ring (mbarrier) wait timed out */
   SM100_DECODE_ERR_BARRIER = 1u << 1, /* a wait for another CTA's output timed out */
@@ -293,14 +295,18 @@ typedef struct {
   const float *w_p2[SM100_DECODE_MAX_LAYERS], *b_p2[SM100_DECODE_MAX_LAYERS];
   float *kv_cache[SM100_DECODE_MAX_LAYERS]; /* [2, max_ctx, dim] each */
   int32_t *io;                              /* [position, token] */
-  /* step outputs as tagged words (float bits | tag << 32), zero-initialised:
-   * x [dim], qkv [3 dim], att [dim], fc [hidden] */
+  /* step outputs as tagged words (float bits | tag << 32), zero-initialised,
+   * SM100_DECODE_REPLICAS copies of each: x [R][dim], qkv [R][3 dim],
+   * att [R][dim], fc [R][hidden] */
   uint64_t *x_w, *qkv_w, *att_w, *fc_w;
   uint64_t *part_w;                         /* per-CTA argmax partials, sm100_decode_part_bytes() */
   float *logits;                            /* [vocab], or NULL: not stored */
-  /* optional phase timeline, or NULL: [grid][5 n_layers + 1][4] u64 global
-   * timer ns per CTA and phase: barrier arrive, barrier passed, input
-   * staged, phase done (sm100_decode_trace_bytes) */
+  /* optional timeline of the last token of a launch, or NULL: [grid][5
+   * n_layers + 1][8] u64 global-timer ns per CTA and step: 0 step start, 1
+   * input landed, 2 weights landed (attention: scores done), 3 input in
+   * registers (attention: softmax done), 4 step done, 5 the step's weight
+   * transfer issued, 6 its issue began waiting for a free stage, 7 unused
+   * (sm100_decode_trace_bytes) */
   uint64_t *trace;
   /* zero-initialised scratch of sm100_decode_sync_bytes(): sync[1] completion
    * counter (reset by the kernel), sync[2] the sticky status word
@@ -312,14 +318,17 @@ uint64_t sm100_decode_sync_bytes(void);
 uint64_t sm100_decode_part_bytes(void);
 uint64_t sm100_decode_trace_bytes(int32_t n_layers);
 /* n_tokens greedy tokens in one launch (positions io[0] .. io[0]+n-1, each
- * token's argmax feeding the next); head_dim 32 or 64, dim % 32 == 0,
- * 4*dim <= 4096, max_ctx <= 3392, n_tokens * (5 n_layers + 2) < 65536, and one
- * CTA's row slice of every projection within 80 KB (GPT-2 small on 148 SMs) */
+ * token's argmax feeding the next).  The scalars repeat the descriptor's
+ * (the host checks the shape with them): dim % 128 == 0 and dim in {512, 768,
+ * 1024}, heads * 64 == dim or heads * 32 == dim, hidden = 4 dim,
+ * 2 max_ctx + 3 head_dim + 512 <= 8192, n_tokens * (5 n_layers + 2) < 65536,
+ * and one projection CTA's row slice of every projection within 88 KB
+ * (GPT-2 small on 148 SMs: 12 attention CTAs + 136 projection CTAs). */
 int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_tokens, int32_t n_layers,
-                       int32_t dim, int32_t max_ctx, void *stream);
+                       int32_t dim, int32_t heads, int32_t vocab, int32_t max_ctx, void *stream);
 /* one token: sm100_decode_steps with n_tokens = 1 */
 int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim,
-                      int32_t max_ctx, void *stream);
+                      int32_t heads, int32_t vocab, int32_t max_ctx, void *stream);
 
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into

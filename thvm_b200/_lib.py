@@ -21,6 +21,7 @@ DT_F32, DT_BF16, DT_FP8E4M3, DT_I32 = 0, 1, 2, 3
  K_SCATTER, K_KV_APPEND, K_POS_ADD, K_DECODE_STEP) = range(1, 14)
 
 DECODE_MAX_LAYERS = 48
+DECODE_REPLICAS = 8
 DECODE_ERR_STALL, DECODE_ERR_BARRIER, DECODE_ERR_ARG = 1, 2, 4
 
 LIN_LN, LIN_GELU, LIN_RESIDUAL, LIN_KV_APPEND = 1, 2, 4, 8
@@ -134,8 +135,8 @@ SIGNATURES = {
     "sm100_decode_sync_bytes": (c_uint64, []),
     "sm100_decode_trace_bytes": (c_uint64, [c_int32]),
     "sm100_decode_part_bytes": (c_uint64, []),
-    "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p]),
-    "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
+    "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),

@@ -540,7 +540,7 @@ int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *ids, uint32_t n_
     case SM100_K_DECODE_STEP:
       if (!p[0]) return sm100_set_error(SM100_ERR_ARG, "decode_step: no model descriptor");
       return sm100_decode_steps((const Sm100DecodeModel *)p[0], k->n > 0 ? (int32_t)k->n : 1, (int32_t)k->m,
-                                (int32_t)k->k, k->max_ctx, st);
+                                (int32_t)k->k, k->heads, (int32_t)k->ld_out, k->max_ctx, st);
     default:
       return sm100_set_error(SM100_ERR_UNSUPPORTED, "dispatch_kernel: kind %u", k->kind);
   }

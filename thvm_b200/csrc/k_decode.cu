@@ -1,32 +1,36 @@
-// GPT-2 decoding (batch 1, fp32) as ONE persistent kernel that runs n
-// greedy tokens: per token the whole schedule of thvm_gpt2.py's
-// Transformer.forward (embedding, n_layers x {ln_1 + c_attn, attention + KV
-// append, c_proj + residual, ln_2 + c_fc + GELU, mlp.c_proj + residual},
-// ln_f + lm_head, argmax), the position and token carried on the device, so
-// one launch replaces n TinyJit replays.
+// GPT-2 decoding (batch 1, fp32) as ONE persistent kernel that runs n greedy
+// tokens: per token the whole schedule of thvm_gpt2.py's Transformer.forward
+// (embedding, n_layers x {ln_1 + c_attn, attention + KV append, c_proj +
+// residual, ln_2 + c_fc + GELU, mlp.c_proj + residual}, ln_f + lm_head,
+// argmax), the position and token carried on the device, so one launch
+// replaces n TinyJit replays.
 //
 // A token reads 495 MB of weights once (77 us at the HBM roofline) but is a
 // chain of ~60 dependent steps, each too small to fill the GPU, so the design
-// attacks latency between steps:
+// attacks the latency between steps:
 //
+//  * Two CTA roles.  CTAs 0..heads-1 are attention CTAs (one per head); the
+//    other CTAs own fixed row slices of every projection.  An attention CTA
+//    keeps its head's cached keys / values of the earlier positions in shared
+//    memory, loaded by TMA bulk copies one layer ahead, so the attention step
+//    only waits for q, k, v of the new row.
 //  * No grid barriers.  Each step's output vector is written as 8-byte words
 //    (float bits | 32-bit tag << 32); a 64-bit store is single-copy atomic, so
-//    a reader that sees the step's tag also sees the value.  Each consumer
-//    thread spins (bounded) on exactly the words it needs: one cross-SM hop
-//    (~0.5 us on B200) per step.  A step's consumers depend on every CTA's
-//    previous step, so no word is overwritten while a slower CTA still needs
-//    its older value.  The argmax is folded by every CTA from the per-CTA
-//    partial words, so the next token starts without another hop.
-//  * Weights never wait for activations.  Each CTA owns a fixed slice of rows
-//    of every projection (contiguous: W is [out, in]); one thread keeps two
-//    TMA bulk copies (cp.async.bulk + mbarrier) of the coming slices in flight
-//    in a 2 x 80 KB shared-memory double buffer, plus L2 bulk prefetches a few
-//    slices further on, so HBM streams ahead of the dependent chain; lm_head
-//    (154 MB) streams through the same buffers in 24-row chunks.
-//  * Short steps: 16 warps; reductions with one CTA barrier; attention (one
-//    CTA per head) loads the cached keys / values of earlier positions into
-//    registers before it waits for the new row, and appends that row to the
-//    cache itself (so a later token reads its own CTA's writes).
+//    a reader that sees the step's tag also sees the value.  Consumers poll
+//    (bounded) exactly the words they need: one cross-SM hop per step.  A
+//    step's consumers depend on every producer of the previous step, so no
+//    word is overwritten while a slower CTA still needs its older value.
+//  * Weights never wait for activations.  One producer warp per projection
+//    CTA keeps TMA bulk copies (cp.async.bulk + mbarrier) of the coming slices
+//    in a 2 x 88 KB shared-memory ring plus L2 prefetches a few slices ahead;
+//    lm_head (154 MB) streams through the same ring in 27-row chunks.
+//  * One CTA barrier per step.  After the input vector lands in shared
+//    memory every warp works alone: it computes the LayerNorm statistics with
+//    warp shuffles (redundantly, 768 floats), keeps its lanes' normalised
+//    inputs in registers, and finishes whole rows (dot product, bias, GELU or
+//    residual, publish) without waiting for other warps.  mlp.c_proj (K =
+//    4 dim) splits each row in four quarters and adds them after one more
+//    barrier, in a fixed order.
 //
 // Math is the reference's op order (LayerNorm two-pass with recip(sqrt), bias
 // then GELU / residual, scale -> max -> xexp2 -> sum -> recip, first index of
@@ -40,17 +44,21 @@
 
 namespace sm100 {
 
-constexpr int kWarps = 15;                   // consumer warps
+constexpr int kWarps = 15;                   // consumer warps (16 warps in all: 128 registers)
 constexpr int kThreads = kWarps * 32;        // consumer threads
 constexpr int kBlockThreads = kThreads + 32; // + one producer warp (TMA issue)
-constexpr int kBufBytes = 81920;   // one half of the weight double buffer
-constexpr int kXsFloats = 4096;    // staged input vector / attention scratch
-constexpr int kMaxRows = 64;       // rows of one transfer
-constexpr int kPrefetchAhead = 4;  // L2 prefetch distance in transfers
-constexpr int kKeyRegs = 3;        // cached keys per 8-lane group held in registers
-constexpr int kValRegs = 24;       // cached values per thread held in registers
+constexpr int kStages = 2;                   // weight ring stages
+constexpr int kStageBytes = 88 * 1024;       // one stage
+constexpr int kXsFloats = 4096;              // one staged input vector (hidden <= 4096)
+constexpr int kMaxRows = 64;                 // rows of one CTA's slice (non-lm_head steps)
+constexpr int kRowsPerWarp = 6;              // >= ceil(kMaxRows / kWarps), even (rows go in pairs)
+constexpr int kPrefetchAhead = 4;            // L2 prefetch distance in transfers
 constexpr int kMaxLayers = SM100_DECODE_MAX_LAYERS;
-constexpr int kMaxLmChunks = 64;   // lm_head chunks per CTA (vocab <= G * 64 * rows per chunk)
+constexpr int kMaxLmChunks = 64;             // lm_head chunks per CTA
+constexpr int kBiasFloats = 72;              // stage region of a transfer's biases (kMaxRows + 3, 16-byte multiple)
+constexpr int kSmemLimit = 227 * 1024;
+constexpr int kTraceSlots = 8;
+constexpr size_t kPartWords = 2 * 1024;       // argmax partials of one copy: (value, index) per CTA             // u64 timestamps per (CTA, step) in the optional trace
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -62,6 +70,10 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
                "r"(bytes)
                : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
@@ -76,9 +88,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait on an mbarrier phase.  With abort_on_status a status already
 // set by any CTA ends it at once; without it (draining copies before exit)
-// only the iteration limit does.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *status,
-                                          bool abort_on_status = true) {
+// only the iteration limit does.  The spin is out of line: the hot path is
+// one try_wait, and the kernel's code stays small enough for the
+// instruction caches.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t *bar, uint32_t parity, uint32_t *status, bool abort_on_status) {
   for (uint32_t i = 0; i < (1u << 20); i++) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 63u) {
@@ -90,6 +103,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
   return false;
 }
 
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t *status,
+                                          bool abort_on_status = true) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, status, abort_on_status);
+}
+
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
@@ -97,8 +115,37 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// L2 policies: weights are streamed once per token and must not push the
+// small, re-read data out of L2 (biases, LayerNorm parameters, the KV cache,
+// the step words and the kernel's own code), so their copies are evict_first.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, uint32_t bytes, uint64_t *bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Generic-proxy writes made visible to later bulk copies (async proxy).
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint64_t ld_word(const uint64_t *p) {
@@ -112,8 +159,20 @@ __device__ __forceinline__ void st_word(uint64_t *p, uint32_t bits, uint32_t tag
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 
-// The payload of a tagged word once its tag is `tag` (bounded spin).
-__device__ __forceinline__ uint32_t wait_word(const uint64_t *p, uint32_t tag, uint32_t *status) {
+// A step's output word goes to kReplicas copies (stride n words); consumer
+// CTA c polls copy c % kReplicas.  Every consumer reads every word; with one
+// copy the ~136 CTAs re-polling the same L2 lines slowed each hop (GPT-2
+// small on B200: 287 us per token with one copy, 261 with eight).
+constexpr int kReplicas = SM100_DECODE_REPLICAS;
+
+__device__ __forceinline__ void st_word_rep(uint64_t *p, size_t n, uint32_t bits, uint32_t tag) {
+#pragma unroll
+  for (int r = 0; r < kReplicas; r++) st_word(p + (size_t)r * n, bits, tag);
+}
+
+// The payload of a tagged word once its tag is `tag` (bounded spin, out of
+// line like mbar_wait_slow).
+__device__ __noinline__ uint32_t wait_word(const uint64_t *p, uint32_t tag, uint32_t *status) {
   uint64_t w = ld_word(p);
   if ((uint32_t)(w >> 32) == tag) return (uint32_t)w;
   for (uint32_t i = 0; i < (1u << 22); i++) {
@@ -129,19 +188,33 @@ __device__ __forceinline__ uint32_t wait_word(const uint64_t *p, uint32_t tag, u
 }
 
 // N tagged words at p[0], p[stride], ...: every load is issued before any tag
-// is checked (one L2 round trip when the words are ready), then only the
-// words not yet tagged are polled (bounded).  n <= N of them are live.
+// is checked (one L2 round trip when the words are ready); the words not yet
+// tagged are then re-polled together, one round trip per round (bounded).
+// n <= N of them are live.
 template <int N>
 __device__ __forceinline__ void wait_words(const uint64_t *p, int stride, int n, uint32_t tag, uint32_t *status,
                                            float (&out)[N]) {
   uint64_t w[N];
+  uint32_t pending = 0;
 #pragma unroll
   for (int i = 0; i < N; i++) w[i] = i < n ? ld_word(p + (size_t)i * stride) : ((uint64_t)tag << 32);
 #pragma unroll
-  for (int i = 0; i < N; i++) {
-    if ((uint32_t)(w[i] >> 32) != tag) w[i] = ((uint64_t)tag << 32) | wait_word(p + (size_t)i * stride, tag, status);
-    out[i] = i < n ? __uint_as_float((uint32_t)w[i]) : 0.0f;
+  for (int i = 0; i < N; i++)
+    if ((uint32_t)(w[i] >> 32) != tag) pending |= 1u << i;
+  for (uint32_t it = 0; pending; it++) {
+    if (it >= (1u << 22) || ((it & 15u) == 15u && *(volatile uint32_t *)status)) {
+      if (it >= (1u << 22)) atomicOr(status, SM100_DECODE_ERR_BARRIER);
+      break;
+    }
+#pragma unroll
+    for (int i = 0; i < N; i++)
+      if ((pending >> i) & 1u) w[i] = ld_word(p + (size_t)i * stride);
+#pragma unroll
+    for (int i = 0; i < N; i++)
+      if (((pending >> i) & 1u) && (uint32_t)(w[i] >> 32) == tag) pending &= ~(1u << i);
   }
+#pragma unroll
+  for (int i = 0; i < N; i++) out[i] = (i < n && !((pending >> i) & 1u)) ? __uint_as_float((uint32_t)w[i]) : 0.0f;
 }
 
 __device__ __forceinline__ uint64_t gtimer() {
@@ -153,8 +226,18 @@ __device__ __forceinline__ uint64_t gtimer() {
 // barrier of the consumer warps only (the producer warp never joins it)
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar)) : "memory");
+// (value, index): larger value wins, then the lower index (first max).
+__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
+  return v1 > v2 || (v1 == v2 && i1 < i2);
+}
+
+__device__ __forceinline__ void warp_best(float &v, int &i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(v2, i2, v, i)) { v = v2; i = i2; }
+  }
 }
 
 enum { PH_QKV = 0, PH_ATT, PH_O, PH_FC, PH_P2, PH_LM };
@@ -166,7 +249,7 @@ struct Phase {
   const float *ln_g, *ln_b;   // LayerNorm of the input (QKV, FC, LM), else null
 };
 
-__device__ __forceinline__ Phase phase_of(const Sm100DecodeModel &m, int p) {
+__device__ __noinline__ Phase phase_of(const Sm100DecodeModel &m, int p) {
   Phase ph;
   ph.ln_g = ph.ln_b = ph.bias = nullptr;
   const int nl = m.n_layers;
@@ -193,59 +276,67 @@ __device__ __forceinline__ Phase phase_of(const Sm100DecodeModel &m, int p) {
   return ph;
 }
 
-__device__ __forceinline__ void rows_of(int64_t N, int c, int G, int64_t &r0, int64_t &r1) {
-  r0 = (N * c) / G;
-  r1 = (N * (c + 1)) / G;
+// rows [r0, r1) of an N-row projection owned by projection CTA c of P
+__device__ __forceinline__ void rows_of(int64_t N, int c, int P, int64_t &r0, int64_t &r1) {
+  r0 = (N * c) / P;
+  r1 = (N * (c + 1)) / P;
 }
 
 // ---- the per-CTA schedule, built once per launch in shared memory --------
 // Step records (one per step of a token) and transfer records (the weight
-// slices of one token, in order: one per non-lm_head weight step, then
-// lm_head's rows in chunks; the first transfer of a LayerNorm step also
-// carries its LayerNorm parameters at the buffer front), so the token loop
-// does no index arithmetic and no dependent loads of model pointers.
+// slices of one token, in order: one per projection step, then lm_head's rows
+// in chunks; the first transfer of a LayerNorm step also carries its
+// LayerNorm parameters at the stage front), so the token loop does no index
+// arithmetic and no dependent loads of model pointers.
 struct StepRec {
   const float *bias;      // bias of this CTA's first row, or null
-  const uint64_t *src;    // input words (null: the embedding)
-  uint64_t *dst;          // output words of this CTA's first row (null: lm_head)
+  const uint64_t *src;    // input words, this CTA's copy (null: the embedding)
+  uint64_t *dst;          // output words of this CTA's first row, copy 0 (null: lm_head)
+  int64_t dst_n;          // words between the output copies
   int kind, layer, K, r0, nrows;
 };
 
+// Stage layout of a transfer: [ln_g | ln_b] (lnbytes), then the bias rows
+// from the 16-byte boundary at or below row r (bbytes, in a kBiasFloats
+// region), then the weight rows at float offset wofs.
 struct XferRec {
-  const float *w, *ln_g, *ln_b;
-  uint32_t wbytes, lnbytes;
+  const float *w, *ln_g, *ln_b, *b;
+  uint32_t wbytes, lnbytes, bbytes;
   int r, nr;              // rows [r, r + nr)
+  int bofs, wofs;         // float offsets in the stage: row r's bias, the first weight row
 };
 
-__device__ __forceinline__ int lm_rows_per_chunk(int64_t K) {
-  const int r = (int)((kBufBytes - 2 * K * 4) / (K * 4));
-  return r < kMaxRows ? r : kMaxRows;
+__host__ __device__ __forceinline__ int lm_rows_per_chunk(int64_t K) {
+  return (int)((kStageBytes - 2 * K * 4 - kBiasFloats * 4) / (K * 4));
 }
 
-__device__ __forceinline__ int xfers_per_token(const Sm100DecodeModel &m, int c, int G) {
+__device__ __forceinline__ int xfers_per_token(const Sm100DecodeModel &m, int c, int P) {
   int64_t r0, r1;
-  rows_of(m.vocab, c, G, r0, r1);
+  rows_of(m.vocab, c, P, r0, r1);
   const int64_t R = lm_rows_per_chunk(m.dim);
   const int64_t chunks = (r1 - r0 + R - 1) / R;
   return 4 * m.n_layers + (int)(chunks > 0 ? chunks : 1);
 }
 
-__device__ void build_step(const Sm100DecodeModel &m, int p, int c, int G, StepRec &s) {
+__device__ __noinline__ void build_step(const Sm100DecodeModel &m, int p, int c, int P, StepRec &s) {
   const Phase ph = phase_of(m, p);
   s.kind = ph.kind;
   s.layer = ph.layer;
   s.K = (int)ph.K;
   int64_t r0 = 0, r1 = 0;
-  if (ph.N) rows_of(ph.N, c, G, r0, r1);
+  if (ph.N) rows_of(ph.N, c, P, r0, r1);
   s.r0 = (int)r0;
   s.nrows = (int)(r1 - r0);
   s.bias = ph.bias ? ph.bias + r0 : nullptr;
-  s.src = ph.kind == PH_O ? m.att_w : ph.kind == PH_P2 ? m.fc_w : (ph.kind == PH_QKV && ph.layer == 0) ? nullptr : m.x_w;
+  const int rc = c % kReplicas;
+  s.src = ph.kind == PH_O ? m.att_w + (size_t)rc * m.dim : ph.kind == PH_P2 ? m.fc_w + (size_t)rc * m.hidden
+        : (ph.kind == PH_QKV && ph.layer == 0) ? nullptr : m.x_w + (size_t)rc * m.dim;
   s.dst = ph.kind == PH_QKV ? m.qkv_w + r0 : ph.kind == PH_FC ? m.fc_w + r0
         : (ph.kind == PH_O || ph.kind == PH_P2) ? m.x_w + r0 : nullptr;
+  s.dst_n = ph.N;
 }
 
-__device__ void build_xfer(const Sm100DecodeModel &m, int i, int c, int G, XferRec &x) {
+__device__ __noinline__ void build_xfer(const Sm100DecodeModel &m, int i, int c, int P, XferRec &x) {
   const int nl = m.n_layers;
   int p;
   int64_t r, nr;
@@ -255,14 +346,14 @@ __device__ void build_xfer(const Sm100DecodeModel &m, int i, int c, int G, XferR
     p = 5 * l + (k == 0 ? PH_QKV : k == 1 ? PH_O : k == 2 ? PH_FC : PH_P2);
     const Phase ph = phase_of(m, p);
     int64_t r0, r1;
-    rows_of(ph.N, c, G, r0, r1);
+    rows_of(ph.N, c, P, r0, r1);
     r = r0;
     nr = r1 - r0;
     with_ln = ph.ln_g != nullptr;
   } else {
     const int j = i - 4 * nl;
     int64_t r0, r1;
-    rows_of(m.vocab, c, G, r0, r1);
+    rows_of(m.vocab, c, P, r0, r1);
     const int64_t R = lm_rows_per_chunk(m.dim);
     p = 5 * nl;
     r = r0 + (int64_t)j * R;
@@ -275,440 +366,593 @@ __device__ void build_xfer(const Sm100DecodeModel &m, int i, int c, int G, XferR
   x.ln_b = with_ln ? ph.ln_b : nullptr;
   x.wbytes = (uint32_t)(nr * ph.K * 4);
   x.lnbytes = with_ln ? (uint32_t)(2 * ph.K * 4) : 0u;
+  // the bias rows ride in the same transfer (a global load of them at the
+  // step would wait behind the weight streams): from row r rounded down to a
+  // 16-byte boundary, a whole number of 16-byte groups
+  const int64_t b0 = r & ~(int64_t)3, b1 = (r + nr + 3) & ~(int64_t)3;
+  x.b = (ph.bias && nr > 0) ? ph.bias + b0 : nullptr;
+  x.bbytes = x.b ? (uint32_t)((b1 - b0) * 4) : 0u;
+  x.bofs = (int)(x.lnbytes / 4) + (int)(r - b0);
+  x.wofs = (int)(x.lnbytes / 4) + (ph.bias ? kBiasFloats : 0);
   x.r = (int)r;
   x.nr = (int)nr;
 }
 
-__device__ __forceinline__ void issue(const XferRec &x, int half, float *buf0, uint64_t *full) {
-  float *dst = buf0 + (size_t)half * (kBufBytes / 4);
-  mbar_expect_tx(&full[half], x.wbytes + x.lnbytes);
+__device__ __forceinline__ void issue(const XferRec &x, int stage, float *ring, uint64_t *full, uint64_t pol_stream,
+                                      uint64_t pol_keep) {
+  float *dst = ring + (size_t)stage * (kStageBytes / 4);
+  mbar_expect_tx(&full[stage], x.wbytes + x.lnbytes + x.bbytes);
   if (x.lnbytes) {
-    bulk_g2s(dst, x.ln_g, x.lnbytes / 2, &full[half]);
-    bulk_g2s(dst + x.lnbytes / 8, x.ln_b, x.lnbytes / 2, &full[half]);
+    bulk_g2s_hint(dst, x.ln_g, x.lnbytes / 2, &full[stage], pol_keep);
+    bulk_g2s_hint(dst + x.lnbytes / 8, x.ln_b, x.lnbytes / 2, &full[stage], pol_keep);
   }
-  if (x.wbytes) bulk_g2s(dst + x.lnbytes / 4, x.w, x.wbytes, &full[half]);
+  if (x.bbytes) bulk_g2s_hint(dst + x.lnbytes / 4, x.b, x.bbytes, &full[stage], pol_keep);
+  if (x.wbytes) bulk_g2s_hint(dst + x.wofs, x.w, x.wbytes, &full[stage], pol_stream);
 }
 
-// CTA-wide sum / max with one barrier; `red` alternates between two 16-float
-// halves (sel) so back-to-back reductions need no second barrier.
-__device__ __forceinline__ float bsum(float v, float *red, int &sel) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float *r = red + 16 * sel;
-  sel ^= 1;
-  v = warp_sum(v);
-  if (lane == 0) r[w] = v;
-  csync();
+// Shared-memory layout (bytes), the same for both roles.
+struct Smem {
+  static constexpr size_t ring = 0;
+  static constexpr size_t xs = ring + (size_t)kStages * kStageBytes;   // [2][kXsFloats] f32
+  static constexpr size_t xown = xs + 2 * kXsFloats * 4;                // [kMaxRows] f32
+  static constexpr size_t part = xown + kMaxRows * 4;                   // [4][kMaxRows] f32
+  static constexpr size_t rbv = part + 4 * kMaxRows * 4;                // [kWarps] f32
+  static constexpr size_t rbi = rbv + kWarps * 4;                       // [kWarps] i32
+  static constexpr size_t tok = rbi + kWarps * 4;                       // [4] i32
+  static constexpr size_t bars = tok + 16;                              // full[2], empty[2], pfx
+  static constexpr size_t steps = bars + 8 * 8;                         // StepRec[5 L + 1]
+  static size_t __host__ __device__ xfers(int n_layers) {
+    return steps + (size_t)(5 * n_layers + 1) * sizeof(StepRec);
+  }
+  static size_t __host__ __device__ total(int n_layers) {
+    return xfers(n_layers) + (size_t)(4 * n_layers + kMaxLmChunks) * sizeof(XferRec);
+  }
+};
+
+struct Launch {
+  int n_tokens, pos0;
+  bool pos_ok;
+  uint32_t tag_base, stride;   // tag of (token tk, step p): tag_base + tk * stride + p
+  uint32_t *status;
+};
+
+// ---------------------------------------------------------------------------
+// Attention CTA: head h of every layer (thvm_gpt2.py:49-61), including the
+// KV-cache assign of the new row.  The keys / values of the earlier
+// positions (up to smax of them) sit in shared memory, brought in by bulk
+// copies issued at the end of the previous layer's attention.
+template <int NK>
+__device__ __noinline__ void attention_role(const Sm100DecodeModel &m, const Launch &ln, unsigned char *smem) {
+  const int h = blockIdx.x, t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int D = m.dim, hd = m.head_dim, nl = m.n_layers, max_ctx = m.max_ctx;
+  const int smax = (kStages * kStageBytes) / (8 * hd);   // staged positions
+  float *Ks = reinterpret_cast<float *>(smem + Smem::ring);
+  float *Vs = Ks + (size_t)smax * hd;
+  float *sc = reinterpret_cast<float *>(smem + Smem::xs);   // [max_ctx] scores
+  float *pr = sc + max_ctx;                                 // [max_ctx] probabilities
+  float *qs = pr + max_ctx, *kn = qs + hd, *vn = kn + hd;   // [hd] each
+  float *acc = vn + hd;                                     // [kThreads / hd][hd]
+  uint64_t *pfx = reinterpret_cast<uint64_t *>(smem + Smem::bars) + 4;
+  uint32_t *status = ln.status;
+  const int n_phases = 5 * nl + 1;
+  uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * n_phases * kTraceSlots : nullptr;
+
+  // prefix copies of (layer l, rows [0, n)); thread 0 armed the barrier
+  auto issue_prefix = [&](int l, int n) {
+    const float *kc = m.kv_cache[l], *vc = kc + (size_t)max_ctx * D;
+    for (int j = t; j < n; j += kThreads) {
+      bulk_g2s(Ks + (size_t)j * hd, kc + (size_t)j * D + (size_t)h * hd, (uint32_t)hd * 4, pfx);
+      bulk_g2s(Vs + (size_t)j * hd, vc + (size_t)j * D + (size_t)h * hd, (uint32_t)hd * 4, pfx);
+    }
+  };
+  auto staged = [&](int n) { return n < smax ? n : smax; };
+
+  int pf = 0;          // prefix phases consumed
+  bool pending = true; // a prefix phase is armed and not yet waited for
+  {
+    const int n = staged(ln.pos_ok ? ln.pos0 : 0);
+    if (t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * n * hd * 4));
+    csync();
+    issue_prefix(0, n);
+  }
+  for (int tk = 0; tk < ln.n_tokens; tk++) {
+    const int pos = ln.pos_ok ? ln.pos0 + tk : 0, L = pos + 1;
+    const uint32_t tag_tok = ln.tag_base + (uint32_t)tk * ln.stride;
+    const bool trace = tr && t == 0 && tk == ln.n_tokens - 1;
+    for (int l = 0; l < nl; l++) {
+      const int p = 5 * l + PH_ATT;
+      const uint32_t tag = tag_tok + (uint32_t)p;
+      float *kc = m.kv_cache[l], *vc = kc + (size_t)max_ctx * D;
+      if (trace) tr[p * kTraceSlots + 0] = gtimer();
+      // the prefix copies are ours and always complete: wait for them even
+      // after an error, so the staging area is never written by two phases
+      mbar_wait(pfx, (uint32_t)(pf & 1), status, false);
+      pf++;
+      pending = false;
+      // q, k, v of the new row; k, v appended to the cache (global and staged)
+      for (int i = t; i < 3 * hd; i += kThreads) {
+        const int which = i / hd, dd = i % hd;
+        const float v = __uint_as_float(wait_word(m.qkv_w + (size_t)(h % kReplicas) * 3 * D + (size_t)which * D +
+                                                  (size_t)h * hd + dd,
+                                                  tag - 1, status));
+        if (which == 0) {
+          qs[dd] = v;
+        } else {
+          (which == 1 ? kn : vn)[dd] = v;
+          if (pos < smax) (which == 1 ? Ks : Vs)[(size_t)pos * hd + dd] = v;
+          if (ln.pos_ok) (which == 1 ? kc : vc)[(size_t)pos * D + (size_t)h * hd + dd] = v;
+          fence_proxy_async();
+        }
+      }
+      csync();
+      if (trace) tr[p * kTraceSlots + 1] = gtimer();
+      // scores: 8 lanes per key, hd / 8 floats per lane
+      {
+        const int grp = t >> 3, gl = t & 7, per4 = hd / 32;
+        constexpr int NG = kThreads / 8;
+        float4 q4[2];
+#pragma unroll
+        for (int v = 0; v < 2; v++)
+          if (v < per4) q4[v] = reinterpret_cast<const float4 *>(qs)[gl * per4 + v];
+        for (int j0 = 0; j0 < L; j0 += NG) {
+          const int j = j0 + grp;
+          float s = 0.0f;
+          if (j < L) {
+            float4 k4[2];
+            if (j < smax) {
+#pragma unroll
+              for (int v = 0; v < 2; v++)
+                if (v < per4) k4[v] = reinterpret_cast<const float4 *>(Ks + (size_t)j * hd)[gl * per4 + v];
+            } else if (j == pos) {
+#pragma unroll
+              for (int v = 0; v < 2; v++)
+                if (v < per4) k4[v] = reinterpret_cast<const float4 *>(kn)[gl * per4 + v];
+            } else {
+#pragma unroll
+              for (int v = 0; v < 2; v++)
+                if (v < per4)
+                  k4[v] = __ldcg(reinterpret_cast<const float4 *>(kc + (size_t)j * D + (size_t)h * hd) + gl * per4 + v);
+            }
+#pragma unroll
+            for (int v = 0; v < 2; v++) {
+              if (v < per4) {
+                s = fmaf(q4[v].x, k4[v].x, s);
+                s = fmaf(q4[v].y, k4[v].y, s);
+                s = fmaf(q4[v].z, k4[v].z, s);
+                s = fmaf(q4[v].w, k4[v].w, s);
+              }
+            }
+          }
+          s += __shfl_xor_sync(0xffffffffu, s, 4);
+          s += __shfl_xor_sync(0xffffffffu, s, 2);
+          s += __shfl_xor_sync(0xffffffffu, s, 1);
+          if (j < L && gl == 0) sc[j] = __fmul_rn(s, m.attn_scale);
+        }
+      }
+      csync();
+      // softmax: every warp folds max and sum itself (no block reduction),
+      // then writes p_j = exp(s_j - max) * recip(sum) for its share of j
+      {
+        float mx = -INFINITY;
+        for (int j = lane; j < L; j += 32) mx = fmaxf(mx, sc[j]);
+        mx = warp_max(mx);
+        float sum = 0.0f;
+        for (int j = lane; j < L; j += 32) sum += xexp(__fsub_rn(sc[j], mx));
+        sum = warp_sum(sum);
+        const float r = __frcp_rn(sum);
+        for (int j = t; j < L; j += kThreads) pr[j] = __fmul_rn(xexp(__fsub_rn(sc[j], mx)), r);
+      }
+      csync();
+      if (trace) tr[p * kTraceSlots + 2] = tr[p * kTraceSlots + 3] = gtimer();
+      // p @ v: key slices x dims, then the slices in order
+      const int nslice = kThreads / hd, slice = t / hd, d = t % hd;
+      if (slice < nslice) {
+        float a = 0.0f;
+        for (int j = slice; j < L; j += nslice) {
+          const float v = j < smax ? Vs[(size_t)j * hd + d] : j == pos ? vn[d] : __ldcg(vc + (size_t)j * D + (size_t)h * hd + d);
+          a = fmaf(pr[j], v, a);
+        }
+        acc[slice * hd + d] = a;
+      }
+      // the next attention's prefix: this token's next layer (rows < pos), or
+      // layer 0 of the next token (rows <= pos)
+      const bool more = l + 1 < nl || tk + 1 < ln.n_tokens;
+      const int nl2 = l + 1 < nl ? l + 1 : 0;
+      const int nrows = more ? staged(l + 1 < nl ? pos : (ln.pos_ok ? pos + 1 : 0)) : 0;
+      if (more && t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nrows * hd * 4));
+      csync();
+      if (t < hd) {
+        float a = 0.0f;
+        for (int s2 = 0; s2 < nslice; s2++) a += acc[s2 * hd + t];
+        st_word_rep(m.att_w + (size_t)h * hd + t, (size_t)D, __float_as_uint(a), tag);
+      }
+      if (more) {
+        issue_prefix(nl2, nrows);
+        pending = true;
+      }
+      if (trace) tr[p * kTraceSlots + 4] = gtimer();
+    }
+  }
+  // every issued copy has landed before the CTA exits
+  if (pending) mbar_wait(pfx, (uint32_t)(pf & 1), status, false);
+}
+
+// ---------------------------------------------------------------------------
+// Projection CTA (consumer warps): every step's row slice, lm_head chunks and
+// the argmax.  NK = dim / 128: float4s per lane of a dim-long row.
+template <int NK>
+__device__ __forceinline__ void load_x(const float *xb, int lane, float (&xr)[4 * NK]) {
+#pragma unroll
+  for (int j = 0; j < NK; j++) {
+    const float4 v = reinterpret_cast<const float4 *>(xb)[lane + 32 * j];
+    xr[4 * j] = v.x; xr[4 * j + 1] = v.y; xr[4 * j + 2] = v.z; xr[4 * j + 3] = v.w;
+  }
+}
+
+// LayerNorm of the staged vector in the lanes' registers (statistics by warp
+// shuffles), with gamma / beta from the stage front.
+template <int NK>
+__device__ __forceinline__ void layernorm_regs(float (&xr)[4 * NK], const float *g, const float *b, int lane, int K,
+                                               float eps) {
+  const float inv_n = (float)(1.0 / (double)K);
   float s = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kWarps; i++) s += r[i];
-  return s;
-}
-
-__device__ __forceinline__ float bmax(float v, float *red, int &sel) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float *r = red + 16 * sel;
-  sel ^= 1;
-  v = warp_max(v);
-  if (lane == 0) r[w] = v;
-  csync();
-  float s = -INFINITY;
+  for (int i = 0; i < 4 * NK; i++) s += xr[i];
+  const float mean = __fmul_rn(warp_sum(s), inv_n);
+  float v2 = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kWarps; i++) s = fmaxf(s, r[i]);
-  return s;
+  for (int i = 0; i < 4 * NK; i++) {
+    const float dd = __fsub_rn(xr[i], mean);
+    v2 = fmaf(dd, dd, v2);
+  }
+  const float var = __fmul_rn(warp_sum(v2), inv_n);
+  const float rr = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+  for (int j = 0; j < NK; j++) {
+    const float4 gv = reinterpret_cast<const float4 *>(g)[lane + 32 * j];
+    const float4 bv = reinterpret_cast<const float4 *>(b)[lane + 32 * j];
+    const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, bb[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+    for (int c = 0; c < 4; c++)
+      xr[4 * j + c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[4 * j + c], mean), rr), gg[c]), bb[c]);
+  }
 }
 
-// (value, index): larger value wins, then the lower index (first max).
-__device__ __forceinline__ bool better(float v1, int i1, float v2, int i2) {
-  return v1 > v2 || (v1 == v2 && i1 < i2);
-}
-
-__device__ __forceinline__ void warp_best(float &v, int &i) {
+// Dot products of two rows (w0, w1: float4 rows in shared memory) with the
+// lanes' registers; every lane gets both sums.
+template <int NK>
+__device__ __forceinline__ void dot2(const float4 *w0, const float4 *w1, bool two, const float (&xr)[4 * NK], int lane,
+                                     float &a, float &b) {
+  float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < NK; j++) {
+    const float4 u = w0[lane + 32 * j];
+    float &aa = (j & 1) ? a1 : a0;
+    aa = fmaf(u.x, xr[4 * j], aa);
+    aa = fmaf(u.y, xr[4 * j + 1], aa);
+    aa = fmaf(u.z, xr[4 * j + 2], aa);
+    aa = fmaf(u.w, xr[4 * j + 3], aa);
+    if (two) {
+      const float4 v = w1[lane + 32 * j];
+      float &bb = (j & 1) ? b1 : b0;
+      bb = fmaf(v.x, xr[4 * j], bb);
+      bb = fmaf(v.y, xr[4 * j + 1], bb);
+      bb = fmaf(v.z, xr[4 * j + 2], bb);
+      bb = fmaf(v.w, xr[4 * j + 3], bb);
+    }
+  }
+  a = a0 + a1;
+  b = b0 + b1;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
-    const int i2 = __shfl_xor_sync(0xffffffffu, i, o);
-    if (better(v2, i2, v, i)) { v = v2; i = i2; }
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
   }
 }
 
-// CTA-wide (value, index) best; every thread gets it (two barriers).
-__device__ __forceinline__ void block_best(float &v, int &i, float *rv, int *ri) {
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  warp_best(v, i);
-  if (lane == 0) { rv[w] = v; ri[w] = i; }
-  csync();
-  v = lane < kWarps ? rv[lane] : -INFINITY;
-  i = lane < kWarps ? ri[lane] : 0x7fffffff;
-  warp_best(v, i);
-  csync();
-}
-
-// Attention of head h for the new row at `pos` (thvm_gpt2.py:49-61), which
-// also appends that row's key / value to the cache (the KV-cache assign).
-// Keys / values of earlier positions are requested before the wait for the
-// new row (they do not depend on it).
-__device__ void attention_head(const Sm100DecodeModel &m, float *kc, int h, int pos, bool pos_ok, uint32_t tag_qkv,
-                               uint32_t tag_att, float *xs, float *red, int &sel, uint32_t *status) {
-  const int D = m.dim, hd = m.head_dim, L = pos + 1;
-  float *sc = xs;                  // [max_ctx] scores
-  float *qs = xs + m.max_ctx;      // [hd]
-  float *kn = qs + hd;             // [hd] new key
-  float *vn = kn + hd;             // [hd] new value
-  float *acc = vn + hd;            // [kThreads / hd][hd]
-  float *vc = kc + (int64_t)m.max_ctx * D;
-  const int t = threadIdx.x;
-  const int grp = t >> 3, gl = t & 7, per4 = hd / 32;   // float4s of a key row per lane
-  constexpr int NG = kThreads / 8;                       // key groups
-  const int nslice = kThreads / hd, slice = t / hd, d = t % hd;
-  float4 kr[kKeyRegs][2];
-  float vr[kValRegs];
-#pragma unroll
-  for (int i = 0; i < kKeyRegs; i++) {
-    const int j = grp + NG * i;
-#pragma unroll
-    for (int v = 0; v < 2; v++)
-      if (v < per4 && j < pos)
-        kr[i][v] = __ldcg(reinterpret_cast<const float4 *>(kc + (int64_t)j * D + (int64_t)h * hd + gl * per4 * 4) + v);
-  }
-#pragma unroll
-  for (int u = 0; u < kValRegs; u++) {
-    const int j = slice + nslice * u;
-    vr[u] = (j < pos) ? __ldcg(vc + (int64_t)j * D + (int64_t)h * hd + d) : 0.0f;
-  }
-  for (int i = t; i < 3 * hd; i += kThreads) {
-    const int which = i / hd, dd = i % hd;
-    const float v = __uint_as_float(wait_word(m.qkv_w + (int64_t)which * D + (int64_t)h * hd + dd, tag_qkv, status));
-    (which == 0 ? qs : which == 1 ? kn : vn)[dd] = v;
-    if (which > 0 && pos_ok) (which == 1 ? kc : vc)[(int64_t)pos * D + (int64_t)h * hd + dd] = v;
-  }
-  csync();
-  float4 q4[2];
-#pragma unroll
-  for (int v = 0; v < 2; v++)
-    if (v < per4) q4[v] = reinterpret_cast<const float4 *>(qs + gl * per4 * 4)[v];
-  for (int j0 = 0; j0 < L; j0 += NG) {
-    const int i = j0 / NG;
-    const int j = j0 + grp;
-    float s = 0.0f;
-    if (j < L) {
-      float4 k4[2];
-      if (j == pos) {
-#pragma unroll
-        for (int v = 0; v < 2; v++)
-          if (v < per4) k4[v] = reinterpret_cast<const float4 *>(kn + gl * per4 * 4)[v];
-      } else if (i < kKeyRegs) {
-#pragma unroll
-        for (int ii = 0; ii < kKeyRegs; ii++)
-          if (ii == i) {
-            k4[0] = kr[ii][0];
-            k4[1] = kr[ii][1];
-          }
-      } else {
-#pragma unroll
-        for (int v = 0; v < 2; v++)
-          if (v < per4)
-            k4[v] = __ldcg(reinterpret_cast<const float4 *>(kc + (int64_t)j * D + (int64_t)h * hd + gl * per4 * 4) + v);
-      }
-#pragma unroll
-      for (int v = 0; v < 2; v++) {
-        if (v < per4) {
-          s = fmaf(q4[v].x, k4[v].x, s);
-          s = fmaf(q4[v].y, k4[v].y, s);
-          s = fmaf(q4[v].z, k4[v].z, s);
-          s = fmaf(q4[v].w, k4[v].w, s);
-        }
-      }
-    }
-    s += __shfl_xor_sync(0xffffffffu, s, 4);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    if (j < L && gl == 0) sc[j] = __fmul_rn(s, m.attn_scale);
-  }
-  csync();
-  float mx = -INFINITY;
-  for (int j = t; j < L; j += kThreads) mx = fmaxf(mx, sc[j]);
-  mx = bmax(mx, red, sel);
-  float sum = 0.0f;
-  for (int j = t; j < L; j += kThreads) sum += xexp(__fsub_rn(sc[j], mx));
-  sum = bsum(sum, red, sel);
-  const float r = __frcp_rn(sum);
-  // mix: p_j = exp(s_j - max) * recip(sum), as the reference orders it
-  if (slice < nslice) {
-    float a = 0.0f;
-#pragma unroll
-    for (int u = 0; u < kValRegs; u++) {
-      const int j = slice + nslice * u;
-      if (j < L) a = fmaf(__fmul_rn(xexp(__fsub_rn(sc[j], mx)), r), j == pos ? vn[d] : vr[u], a);
-    }
-    for (int j = slice + nslice * kValRegs; j < L; j += nslice)
-      a = fmaf(__fmul_rn(xexp(__fsub_rn(sc[j], mx)), r),
-               j == pos ? vn[d] : __ldcg(vc + (int64_t)j * D + (int64_t)h * hd + d), a);
-    acc[slice * hd + d] = a;
-  }
-  csync();
-  for (int dd = t; dd < hd; dd += kThreads) {
-    float a = 0.0f;
-    for (int s2 = 0; s2 < nslice; s2++) a += acc[s2 * hd + dd];
-    st_word(m.att_w + (int64_t)h * hd + dd, __float_as_uint(a), tag_att);
-  }
-}
-
-__global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100DecodeModel *__restrict__ mp, int n_tokens) {
-  extern __shared__ __align__(1024) unsigned char smem[];
-  float *buf0 = reinterpret_cast<float *>(smem);                         // [2][kBufBytes / 4]
-  float *xs = reinterpret_cast<float *>(smem + 2 * kBufBytes);          // [kXsFloats]
-  float *xown = xs + kXsFloats;                                          // [kMaxRows] own residual rows
-  float *part = xown + kMaxRows;                                         // [kWarps][kMaxRows] partials
-  float *red = part + kWarps * kMaxRows;                                 // [2][16]
-  uint64_t *full = reinterpret_cast<uint64_t *>(red + 32);               // [2] transfer landed
-  uint64_t *empty = full + 2;                                            // [2] half released
-  StepRec *steps = reinterpret_cast<StepRec *>(empty + 2);               // [n_phases]
-  const Sm100DecodeModel &m = *mp;
+template <int NK>
+__device__ __forceinline__ void projection_role(const Sm100DecodeModel &m, const Launch &ln, unsigned char *smem, int nx) {
+  const int A = m.heads, P = gridDim.x - A, pc = blockIdx.x - A;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  float *ring = reinterpret_cast<float *>(smem + Smem::ring);
+  float *xs = reinterpret_cast<float *>(smem + Smem::xs);
+  float *xown = reinterpret_cast<float *>(smem + Smem::xown);
+  float *part = reinterpret_cast<float *>(smem + Smem::part);
+  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
+  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
+  int *tok_s = reinterpret_cast<int *>(smem + Smem::tok);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars), *empty = full + 2;
+  const StepRec *steps = reinterpret_cast<const StepRec *>(smem + Smem::steps);
+  const XferRec *xfers = reinterpret_cast<const XferRec *>(smem + Smem::xfers(m.n_layers));
+  uint32_t *status = ln.status;
   const int n_phases = 5 * m.n_layers + 1;
-  XferRec *xfers = reinterpret_cast<XferRec *>(steps + n_phases);        // [nx]
-  __shared__ float rbv[kWarps];
-  __shared__ int rbi[kWarps];
-
-  const int c = blockIdx.x, G = gridDim.x, t = threadIdx.x;
-  const int warp = t >> 5, lane = t & 31;
-  uint32_t *status = m.sync + 2;
-  int nx = xfers_per_token(m, c, G);
-  if (nx > 4 * m.n_layers + kMaxLmChunks) {   // vocab too large for the schedule table
-    if (threadIdx.x == 0) atomicOr(m.sync + 2, SM100_DECODE_ERR_ARG);
-    nx = 4 * m.n_layers + kMaxLmChunks;
-  }
-  const int total_x = nx * n_tokens;
-  // tags: (launch epoch mod 65535 + 1) << 16 | token * stride + step: never
-  // 0 (the zero-initialised words), distinct from the previous launch's and
-  // within a launch one per (token, step)
-  const uint32_t tag_base = ((m.sync[3] % 65535u) + 1u) << 16;
-  const uint32_t stride = (uint32_t)n_phases + 1u;
-  const int pos0 = m.io[0];
-  // a position range outside the cache is an argument error: flag it and keep
-  // every access in bounds (positions from 0, no cache write, nothing published)
-  const bool pos_ok = pos0 >= 0 && pos0 + n_tokens <= m.max_ctx;
+  const int dim = m.dim, vocab = m.vocab;
+  const float eps = m.eps;
   const float *wte = m.wte, *wpe = m.wpe;
   float *logits = m.logits;
-  const int vocab = m.vocab, dim = m.dim;
-  const float eps = m.eps;
-  int sel = 0;
+  uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * n_phases * kTraceSlots : nullptr;
+  constexpr int KPT = (kXsFloats + kThreads - 1) / kThreads;
 
-  for (int p = t; p < n_phases; p += kThreads) build_step(m, p, c, G, steps[p]);
-  for (int i = t; i < nx; i += kThreads) build_xfer(m, i, c, G, xfers[i]);
-  if (t == 0) {
-    if (!pos_ok && c == 0) atomicOr(status, SM100_DECODE_ERR_ARG);
-    mbar_init(&full[0], 1);
-    mbar_init(&full[1], 1);
-    mbar_init(&empty[0], 1);
-    mbar_init(&empty[1], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  if (warp == kWarps) {
-    // ---- producer: every weight transfer of the launch, in order, into the
-    // half its consumer released (two in flight), plus L2 prefetches ahead
-    if (lane == 0) {
-      int issued = 0, ia = 0;
-      for (int qq = 0; qq < total_x; qq++) {
-        const int h = qq & 1;
-        if (qq >= 2 && !mbar_wait(&empty[h], ((qq >> 1) - 1) & 1, status)) break;
-        issue(xfers[qq % nx], h, buf0, full);
-        issued = qq + 1;
-        for (; ia < qq + 2 + kPrefetchAhead && ia < total_x; ia++) {
-          if (ia < 2) continue;
-          const XferRec &x = xfers[ia % nx];
-          if (x.wbytes) bulk_prefetch_l2(x.w, x.wbytes);
-        }
-      }
-      // every issued transfer has landed before the CTA exits (the halves
-      // complete their uses in order; bounded, not cut short by the status)
-      for (int qq = issued - 2; qq < issued; qq++)
-        if (qq >= 0) mbar_wait(&full[qq & 1], (qq >> 1) & 1, status, false);
-    }
-    return;
-  }
-  uint64_t *tr = m.trace ? m.trace + (size_t)c * n_phases * 4 : nullptr;
-
-  int q = 0, qi = 0;   // next transfer: global index, index within the token
+  int q = 0, qi = 0, sidx = 0;   // next transfer (global, within the token), staged-input parity
   int tok = m.io[1];
-  for (int tk = 0; tk < n_tokens; tk++) {
-    const int pos = pos_ok ? pos0 + tk : 0;
-    const uint32_t tag_tok = tag_base + (uint32_t)tk * stride;
-    const bool trace = tr && t == 0 && tk == n_tokens - 1;
-    float my_best = -INFINITY;
-    int my_idx = 0x7fffffff;
+  for (int tk = 0; tk < ln.n_tokens; tk++) {
+    const int pos = ln.pos_ok ? ln.pos0 + tk : 0;
+    const uint32_t tag_tok = ln.tag_base + (uint32_t)tk * ln.stride;
+    const bool trace = tr && t == 0 && tk == ln.n_tokens - 1;
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
     for (int p = 0; p < n_phases; p++) {
       const StepRec st = steps[p];
+      if (st.kind == PH_ATT) continue;
       const uint32_t tag = tag_tok + (uint32_t)p;
-      if (trace) tr[p * 4 + 0] = gtimer();
-      if (st.kind == PH_ATT) {
-        if (c < m.heads) attention_head(m, m.kv_cache[st.layer], c, pos, pos_ok, tag - 1, tag, xs, red, sel, status);
-        csync();   // xs (attention scratch) is free again
-        if (trace) tr[p * 4 + 1] = tr[p * 4 + 2] = tr[p * 4 + 3] = gtimer();
-        continue;
-      }
-      const int K = st.K, K4 = K / 4;
-      const bool ln = st.kind == PH_QKV || st.kind == PH_FC || st.kind == PH_LM;
-      const float bpre = (st.bias && t < st.nrows) ? st.bias[t] : 0.0f;
+      if (trace) tr[p * kTraceSlots + 0] = gtimer();
+      const int K = st.K, nr = st.nrows;
+      float *xb = xs + (size_t)(sidx & 1) * kXsFloats;
+      sidx++;
 
       // ---- the input vector: embedding, or the previous step's words ------
-      constexpr int KPT = (kXsFloats + kThreads - 1) / kThreads;
-      float xv[KPT];
       if (st.src == nullptr) {
         // x = wte[tok] + wpe[pos] (thvm_gpt2.py:93-103); own rows kept for the residual
         const bool tok_ok = tok >= 0 && tok < vocab;
-#pragma unroll
-        for (int i = 0; i < KPT; i++) {
-          const int k = t + i * kThreads;
-          xv[i] = k < K ? __fadd_rn(tok_ok ? wte[(int64_t)tok * K + k] : 0.0f, wpe[(int64_t)pos * K + k]) : 0.0f;
-        }
+        for (int k = t; k < K; k += kThreads)
+          xb[k] = __fadd_rn(tok_ok ? wte[(size_t)tok * K + k] : 0.0f, wpe[(size_t)pos * K + k]);
         int64_t s0, s1;
-        rows_of(dim, c, G, s0, s1);
+        rows_of(dim, pc, P, s0, s1);
         if (t < s1 - s0)
-          xown[t] = __fadd_rn(tok_ok ? wte[(int64_t)tok * K + s0 + t] : 0.0f, wpe[(int64_t)pos * K + s0 + t]);
+          xown[t] = __fadd_rn(tok_ok ? wte[(size_t)tok * K + s0 + t] : 0.0f, wpe[(size_t)pos * K + s0 + t]);
       } else {
+        float xv[KPT];
         const int live = t < K ? (K - 1 - t) / kThreads + 1 : 0;
         wait_words<KPT>(st.src + t, kThreads, live, tag - 1, status, xv);
-      }
-      if (trace) tr[p * 4 + 1] = gtimer();
-
-      // ---- weights of this step; LayerNorm into xs -------------------------
-      XferRec xf = xfers[qi];
-      bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-      const float *wb = buf0 + (size_t)(q & 1) * (kBufBytes / 4);
-      if (ln) {
-        const float inv_n = (float)(1.0 / (double)K);
-        float s = 0.0f;
-#pragma unroll
-        for (int i = 0; i < KPT; i++) s += xv[i];
-        const float mean = __fmul_rn(bsum(s, red, sel), inv_n);
-        float v2 = 0.0f;
 #pragma unroll
         for (int i = 0; i < KPT; i++)
-          if (t + i * kThreads < K) {
-            const float dd = __fsub_rn(xv[i], mean);
-            v2 = fmaf(dd, dd, v2);
-          }
-        const float var = __fmul_rn(bsum(v2, red, sel), inv_n);
-        const float rr = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
-#pragma unroll
-        for (int i = 0; i < KPT; i++) {
-          const int k = t + i * kThreads;
-          if (k < K) xs[k] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xv[i], mean), rr), wb[k]), wb[K + k]);
-        }
-      } else {
-#pragma unroll
-        for (int i = 0; i < KPT; i++) {
-          const int k = t + i * kThreads;
-          if (k < K) xs[k] = xv[i];
-        }
+          if (i < live) xb[t + i * kThreads] = xv[i];
       }
       csync();
-      if (trace) tr[p * 4 + 2] = gtimer();
+      if (trace) tr[p * kTraceSlots + 1] = gtimer();
 
-      // ---- rows: this transfer (and for lm_head the following chunks) ------
-      const float4 *x4 = reinterpret_cast<const float4 *>(xs);
-      const float *w = wb + xf.lnbytes / 4;
-      for (;;) {
-        const int nr = xf.nr;
-        const int wpr = nr >= kWarps ? 1 : (nr > 0 ? kWarps / nr : 1);
-        if (have && nr > 0) {
-          // (row, k-slice) per warp: wpr warps per row when rows are few
-          const int per_pass = kWarps / wpr;
-          for (int i0 = 0; i0 < nr; i0 += per_pass) {
-            const int i = i0 + warp / wpr, j = warp % wpr;
-            if (i < nr) {
-              const int k0 = (K4 * j) / wpr, k1 = (K4 * (j + 1)) / wpr;
-              const float4 *wr = reinterpret_cast<const float4 *>(w + (size_t)i * K);
-              float a0 = 0.0f, a1 = 0.0f;
-              int k = k0 + lane;
-              for (; k + 32 < k1; k += 64) {
-                const float4 w0 = wr[k], w1 = wr[k + 32];
-                const float4 x0 = x4[k], x1 = x4[k + 32];
-                a0 = fmaf(w0.x, x0.x, a0); a1 = fmaf(w1.x, x1.x, a1);
-                a0 = fmaf(w0.y, x0.y, a0); a1 = fmaf(w1.y, x1.y, a1);
-                a0 = fmaf(w0.z, x0.z, a0); a1 = fmaf(w1.z, x1.z, a1);
-                a0 = fmaf(w0.w, x0.w, a0); a1 = fmaf(w1.w, x1.w, a1);
-              }
-              if (k < k1) {
-                const float4 w0 = wr[k], x0 = x4[k];
-                a0 = fmaf(w0.x, x0.x, a0);
-                a0 = fmaf(w0.y, x0.y, a0);
-                a0 = fmaf(w0.z, x0.z, a0);
-                a0 = fmaf(w0.w, x0.w, a0);
-              }
-              const float a = warp_sum(a0 + a1);
-              if (lane == 0) part[j * kMaxRows + i] = a;
+      // ---- weights of this step; the input in registers --------------------
+      XferRec xf = xfers[qi];
+      bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
+      const float *sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
+      if (trace) tr[p * kTraceSlots + 2] = gtimer();
+      float xr[4 * NK];
+      if (st.kind == PH_P2) {
+        load_x<NK>(xb + (warp & 3) * dim, lane, xr);   // this warp's quarter of K
+      } else {
+        load_x<NK>(xb, lane, xr);
+        if (st.kind != PH_O) layernorm_regs<NK>(xr, sb, sb + K, lane, K, eps);
+      }
+      if (trace) tr[p * kTraceSlots + 3] = gtimer();
+
+      // ---- rows ------------------------------------------------------------
+      if (st.kind == PH_P2) {
+        // (row, quarter) per warp: warps w = qq (mod 4) take quarter qq of rows
+        // w / 4, w / 4 + nq, ...; the quarters are added in order afterwards
+        const int qq = warp & 3, nq = (kWarps - qq + 3) >> 2;
+        if (have) {
+          for (int i = warp >> 2; i < nr; i += 2 * nq) {
+            const int i2 = i + nq;
+            const bool two = i2 < nr;
+            float a, b;
+            dot2<NK>(reinterpret_cast<const float4 *>(sb + xf.wofs + (size_t)i * K + qq * dim),
+                     reinterpret_cast<const float4 *>(sb + xf.wofs + (size_t)(two ? i2 : i) * K + qq * dim), two, xr,
+                     lane, a, b);
+            if (lane == 0) {
+              part[qq * kMaxRows + i] = a;
+              if (two) part[qq * kMaxRows + i2] = b;
             }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[q & 1]);
         csync();
-        if (trace && st.kind != PH_LM) tr[p * 4 + 3] = gtimer();
-        // this half is free again: the producer refills it
-        if (t == 0) mbar_arrive(&empty[q & 1]);
-        // epilogue: one thread per row
         if (have && t < nr) {
-          float a = 0.0f;
-          for (int j = 0; j < wpr; j++) a += part[j * kMaxRows + t];
-          switch (st.kind) {
-            case PH_QKV: st_word(st.dst + t, __float_as_uint(__fadd_rn(a, bpre)), tag); break;
-            case PH_O:
-            case PH_P2: {
-              const float v = __fadd_rn(xown[t], __fadd_rn(a, bpre));   // x + (xW^T + b)
-              xown[t] = v;
-              st_word(st.dst + t, __float_as_uint(v), tag);
-              break;
-            }
-            case PH_FC: st_word(st.dst + t, __float_as_uint(gelu_tanh(__fadd_rn(a, bpre))), tag); break;
-            default: {
-              const int n = xf.r + t;
-              if (logits) logits[n] = a;
-              if (better(a, n, my_best, my_idx)) { my_best = a; my_idx = n; }
-              break;
-            }
-          }
+          const float a = __fadd_rn(__fadd_rn(__fadd_rn(part[t], part[kMaxRows + t]), part[2 * kMaxRows + t]),
+                                    part[3 * kMaxRows + t]);
+          const float v = __fadd_rn(xown[t], __fadd_rn(a, sb[xf.bofs + t]));   // x + (h W^T + b)
+          xown[t] = v;
+          st_word_rep(st.dst + t, (size_t)st.dst_n, __float_as_uint(v), tag);
         }
         q++;
-        if (++qi == nx) qi = 0;
-        if (st.kind != PH_LM || qi == 0) break;
-        // next lm_head chunk
-        xf = xfers[qi];
-        have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-        w = buf0 + (size_t)(q & 1) * (kBufBytes / 4) + xf.lnbytes / 4;
-        csync();   // the epilogue above has read `part`
+        qi++;
+      } else if (st.kind != PH_LM) {
+        const float *w = sb + xf.wofs;
+        if (have) {
+#pragma unroll 1
+          for (int k = 0; k < kRowsPerWarp; k += 2) {
+            const int i = warp + kWarps * k, i2 = i + kWarps;
+            if (i < nr) {
+              const bool two = i2 < nr;
+              float a, b;
+              dot2<NK>(reinterpret_cast<const float4 *>(w + (size_t)i * K),
+                       reinterpret_cast<const float4 *>(w + (size_t)(two ? i2 : i) * K), two, xr, lane, a, b);
+              if (lane == 0) {
+#pragma unroll 1
+                for (int u = 0; u < 2; u++) {
+                  if (u == 1 && !two) break;
+                  const int row = u ? i2 : i;
+                  const float y = __fadd_rn(u ? b : a, sb[xf.bofs + row]);
+                  switch (st.kind) {
+                    case PH_QKV: st_word_rep(st.dst + row, (size_t)st.dst_n, __float_as_uint(y), tag); break;
+                    case PH_FC: st_word_rep(st.dst + row, (size_t)st.dst_n, __float_as_uint(gelu_tanh(y)), tag); break;
+                    default: {   // PH_O: x + (att W^T + b)
+                      const float v = __fadd_rn(xown[row], y);
+                      xown[row] = v;
+                      st_word_rep(st.dst + row, (size_t)st.dst_n, __float_as_uint(v), tag);
+                      break;
+                    }
+                  }
+                }
+              }
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[q & 1]);
+        q++;
+        qi++;
+      } else {
+        // lm_head: the chunks of this CTA's vocab rows, each warp on its own
+        const float *w = sb + xf.wofs;
+        for (;;) {
+          const int cn = xf.nr;
+          if (have) {
+            for (int i = warp; i < cn; i += 2 * kWarps) {
+              const int i2 = i + kWarps;
+              const bool two = i2 < cn;
+              float a, b;
+              dot2<NK>(reinterpret_cast<const float4 *>(w + (size_t)i * K),
+                       reinterpret_cast<const float4 *>(w + (size_t)(two ? i2 : i) * K), two, xr, lane, a, b);
+              if (lane == 0) {
+                const int n = xf.r + i;
+                if (logits) logits[n] = a;
+                if (better(a, n, best, bidx)) { best = a; bidx = n; }
+                if (two) {
+                  if (logits) logits[n + kWarps] = b;
+                  if (better(b, n + kWarps, best, bidx)) { best = b; bidx = n + kWarps; }
+                }
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[q & 1]);
+          q++;
+          if (++qi == nx) qi = 0;
+          if (qi == 0) break;
+          xf = xfers[qi];
+          have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
+          w = ring + (size_t)(q & 1) * (kStageBytes / 4) + xf.wofs;
+        }
       }
-      csync();
-      if (trace && st.kind == PH_LM) tr[p * 4 + 3] = gtimer();
+      if (trace) tr[p * kTraceSlots + 4] = gtimer();
     }
 
     // ---- argmax: publish this CTA's best, fold every CTA's -----------------
-    float bv = my_best;
-    int bi = my_idx;
-    block_best(bv, bi, rbv, rbi);
-    const uint32_t tag_am = tag_tok + (uint32_t)n_phases;
-    if (t == 0) {
-      st_word(m.part_w + 2 * c, __float_as_uint(bv), tag_am);
-      st_word(m.part_w + 2 * c + 1, (uint32_t)bi, tag_am);
+    if (lane == 0) {
+      rbv[warp] = best;
+      rbi[warp] = bidx;
     }
-    bv = -INFINITY;
-    bi = 0x7fffffff;
-    for (int b = t; b < G; b += kThreads) {
-      float pw[2];
-      wait_words<2>(m.part_w + 2 * b, 1, 2, tag_am, status, pw);
-      const int ib = (int)__float_as_uint(pw[1]);
-      if (better(pw[0], ib, bv, bi)) { bv = pw[0]; bi = ib; }
+    csync();
+    if (warp == 0) {
+      const uint32_t tag_am = tag_tok + (uint32_t)n_phases;
+      float bv = lane < kWarps ? rbv[lane] : -INFINITY;
+      int bi = lane < kWarps ? rbi[lane] : 0x7fffffff;
+      warp_best(bv, bi);
+      if (lane == 0) {
+        st_word_rep(m.part_w + 2 * pc, kPartWords, __float_as_uint(bv), tag_am);
+        st_word_rep(m.part_w + 2 * pc + 1, kPartWords, (uint32_t)bi, tag_am);
+      }
+      bv = -INFINITY;
+      bi = 0x7fffffff;
+      for (int b = lane; b < P; b += 32) {
+        float pw[2];
+        wait_words<2>(m.part_w + (size_t)(pc % kReplicas) * kPartWords + 2 * b, 1, 2, tag_am, status, pw);
+        const int ib = (int)__float_as_uint(pw[1]);
+        if (better(pw[0], ib, bv, bi)) { bv = pw[0]; bi = ib; }
+      }
+      warp_best(bv, bi);
+      if (lane == 0) tok_s[0] = bi == 0x7fffffff ? 0 : bi;
     }
-    block_best(bv, bi, rbv, rbi);
-    tok = bi == 0x7fffffff ? 0 : bi;
+    csync();
+    tok = tok_s[0];
   }
 
-  if (c == 0 && t == 0) {
+  if (pc == 0 && t == 0) {
     if (*(volatile uint32_t *)status == 0) {
       m.io[1] = tok;
-      if (m.bump) m.io[0] = pos0 + n_tokens;
+      if (m.bump) m.io[0] = ln.pos0 + ln.n_tokens;
     }
     m.sync[3] += 1u;   // next launch: new tags
   }
+}
+
+// Producer warp of a projection CTA: every weight transfer of the launch, in
+// order, into the stage its consumers released, plus L2 prefetches ahead.
+__device__ __noinline__ void producer_role(const Sm100DecodeModel &m, const Launch &ln, unsigned char *smem, int nx) {
+  if ((threadIdx.x & 31) != 0) return;
+  float *ring = reinterpret_cast<float *>(smem + Smem::ring);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars), *empty = full + 2;
+  const XferRec *xfers = reinterpret_cast<const XferRec *>(smem + Smem::xfers(m.n_layers));
+  const int total = nx * ln.n_tokens;
+  const int n_phases = 5 * m.n_layers + 1;
+  uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * n_phases * kTraceSlots : nullptr;
+  const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
+  int issued = 0, ia = 0;
+  for (int qq = 0; qq < total; qq++) {
+    const int s = qq & 1, qi = qq % nx;
+    // the step a transfer feeds (lm_head: its first chunk), traced on the last token
+    const int tp = qi < 4 * m.n_layers ? 5 * (qi / 4) + (qi % 4 == 0 ? 0 : qi % 4 + 1) : (qi == 4 * m.n_layers ? 5 * m.n_layers : -1);
+    const bool trace = tr && qq >= total - nx && tp >= 0;
+    if (trace) tr[tp * kTraceSlots + 6] = gtimer();
+    if (qq >= 2 && !mbar_wait(&empty[s], ((qq >> 1) - 1) & 1, ln.status)) break;
+    issue(xfers[qi], s, ring, full, pol_stream, pol_keep);
+    if (trace) tr[tp * kTraceSlots + 5] = gtimer();
+    issued = qq + 1;
+    for (; ia < qq + 2 + kPrefetchAhead && ia < total; ia++) {
+      if (ia < 2) continue;
+      const XferRec &x = xfers[ia % nx];
+      if (x.wbytes) bulk_prefetch_l2(x.w, x.wbytes);
+    }
+  }
+  // every issued transfer has landed before the CTA exits (bounded, not cut
+  // short by the status)
+  for (int qq = issued - 2; qq < issued; qq++)
+    if (qq >= 0) mbar_wait(&full[qq & 1], (qq >> 1) & 1, ln.status, false);
+}
+
+template <int NK>
+__global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100DecodeModel *__restrict__ mp, int n_tokens) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  const Sm100DecodeModel &m = *mp;
+  const int c = blockIdx.x, t = threadIdx.x;
+  const int A = m.heads, P = gridDim.x - A;
+  const bool att = c < A;
+  Launch ln;
+  ln.n_tokens = n_tokens;
+  ln.status = m.sync + 2;
+  // tags: (launch epoch mod 65535 + 1) << 16 | token * stride + step: never
+  // 0 (the zero-initialised words), distinct from the previous launch's and
+  // within a launch one per (token, step)
+  ln.tag_base = ((m.sync[3] % 65535u) + 1u) << 16;
+  ln.stride = (uint32_t)(5 * m.n_layers + 2);
+  ln.pos0 = m.io[0];
+  // a position range outside the cache is an argument error: flag it and keep
+  // every access in bounds (positions from 0, no cache write, nothing published)
+  ln.pos_ok = ln.pos0 >= 0 && ln.pos0 + n_tokens <= m.max_ctx;
+
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
+  int nx = 0;
+  if (!att) {
+    StepRec *steps = reinterpret_cast<StepRec *>(smem + Smem::steps);
+    XferRec *xfers = reinterpret_cast<XferRec *>(smem + Smem::xfers(m.n_layers));
+    const int n_phases = 5 * m.n_layers + 1;
+    nx = xfers_per_token(m, c - A, P);
+    if (nx > 4 * m.n_layers + kMaxLmChunks) {   // vocab too large for the schedule table
+      if (t == 0) atomicOr(ln.status, SM100_DECODE_ERR_ARG);
+      nx = 4 * m.n_layers + kMaxLmChunks;
+    }
+    for (int p = t; p < n_phases; p += kBlockThreads) build_step(m, p, c - A, P, steps[p]);
+    for (int i = t; i < nx; i += kBlockThreads) build_xfer(m, i, c - A, P, xfers[i]);
+  }
+  if (t == 0) {
+    if (!ln.pos_ok && c == A) atomicOr(ln.status, SM100_DECODE_ERR_ARG);
+    mbar_init(&bars[0], 1);        // full[0], full[1]: armed by the producer
+    mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], kWarps);   // empty[0], empty[1]: one arrival per consumer warp
+    mbar_init(&bars[3], kWarps);
+    mbar_init(&bars[4], 1);        // attention prefix
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (t >= kThreads) {
+    if (!att) producer_role(m, ln, smem, nx);
+    return;
+  }
+  if (att)
+    attention_role<NK>(m, ln, smem);
+  else
+    projection_role<NK>(m, ln, smem, nx);
 }
 
 }  // namespace sm100
@@ -719,14 +963,35 @@ static int g_num_sms[64];
 
 extern "C" uint64_t sm100_decode_sync_bytes(void) { return (uint64_t)(4 + 2 * 1024) * 4; }
 
-extern "C" uint64_t sm100_decode_part_bytes(void) { return (uint64_t)2 * 1024 * 8; }
+extern "C" uint64_t sm100_decode_part_bytes(void) { return (uint64_t)kPartWords * 8 * kReplicas; }
 
 extern "C" uint64_t sm100_decode_trace_bytes(int32_t n_layers) {
-  return (uint64_t)1024 * (5 * (uint64_t)(n_layers > 0 ? n_layers : 0) + 1) * 4 * 8;
+  return (uint64_t)1024 * (5 * (uint64_t)(n_layers > 0 ? n_layers : 0) + 1) * kTraceSlots * 8;
 }
 
+template <int NK>
+static int launch_decode(const Sm100DecodeModel *dev_model, int n_tokens, int G, size_t smem, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: smem attribute: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)G);
+  cfg.blockDim = dim3(kBlockThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, decode_kernel<NK>, dev_model, n_tokens);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: launch: %s", cudaGetErrorString(e));
+  return launch_status("decode");
+}
+
+// The host checks the shape from the scalars it is given (the descriptor
+// itself lives in device memory and must carry the same values).
 extern "C" int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_tokens, int32_t n_layers, int32_t dim,
-                                  int32_t max_ctx, void *stream) {
+                                  int32_t heads, int32_t vocab, int32_t max_ctx, void *stream) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "decode: device %d", dev);
@@ -737,39 +1002,35 @@ extern "C" int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_t
     g_num_sms[dev] = n;
   }
   const int G = g_num_sms[dev];
-  // every step's row slice (+ LayerNorm parameters) fits a buffer half, at
-  // most kMaxRows rows; c_fc (N = 4 dim) and mlp.c_proj (K = 4 dim) dominate
-  const int64_t rows_n = (4LL * dim + G - 1) / G, rows_d = ((int64_t)dim + G - 1) / G;
-  const int64_t fc_bytes = rows_n * dim * 4 + 2LL * dim * 4, p2_bytes = rows_d * 4LL * dim * 4;
-  if (!dev_model || n_tokens <= 0 || (int64_t)n_tokens * (5 * n_layers + 2) >= 65536 || n_layers <= 0 ||
-      n_layers > kMaxLayers || dim <= 0 ||
-      dim % 32 || 4 * dim > kXsFloats || max_ctx + 3 * 64 + kThreads > kXsFloats || fc_bytes > kBufBytes ||
-      p2_bytes > kBufBytes || rows_n > kMaxRows || 3LL * dim * 4 > kBufBytes)
-    return sm100_set_error(SM100_ERR_ARG, "decode: unsupported shape (tokens %d, layers %d, dim %d, ctx %d, %d SMs)",
-                           n_tokens, n_layers, dim, max_ctx, G);
-  // + the per-CTA schedule: step records, transfer records (lm_head chunks: at
-  // most ceil(vocab / G / rows per chunk))
-  const int64_t n_x = 4LL * n_layers + kMaxLmChunks;
-  const size_t smem = 2 * (size_t)kBufBytes + (kXsFloats + kMaxRows + kWarps * kMaxRows + 32) * 4 + 4 * 8 +
-                      (size_t)(5 * n_layers + 1) * sizeof(StepRec) + (size_t)n_x * sizeof(XferRec);
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: smem attribute: %s", cudaGetErrorString(e));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)G);
-  cfg.blockDim = dim3(kBlockThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = (cudaStream_t)stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, decode_kernel, dev_model, (int)n_tokens);
-  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: launch: %s", cudaGetErrorString(e));
-  return launch_status("decode");
+  const int hd = heads > 0 ? dim / heads : 0, P = G - heads;
+  const int64_t K = dim;
+  bool ok = dev_model && G <= 1024 && n_tokens > 0 && (int64_t)n_tokens * (5 * n_layers + 2) < 65536 && n_layers > 0 &&
+            n_layers <= kMaxLayers && dim > 0 && dim % 128 == 0 && heads > 0 && hd * heads == dim &&
+            (hd == 32 || hd == 64) && P >= 1 && vocab > 0 && max_ctx > 0 &&
+            2LL * max_ctx + 3LL * hd + kThreads <= 2LL * kXsFloats && 4 * K <= kXsFloats;
+  if (ok) {
+    const int64_t rq = (3 * K + P - 1) / P, rf = (4 * K + P - 1) / P, rd = (K + P - 1) / P;
+    const int64_t R = lm_rows_per_chunk(K), rv = ((int64_t)vocab + P - 1) / P;
+    const int64_t extra = 2 * K * 4 + kBiasFloats * 4;   // LayerNorm parameters + biases
+    ok = rq <= kMaxRows && rf <= kMaxRows && rd <= kMaxRows && rq * K * 4 + extra <= kStageBytes &&
+         rf * K * 4 + extra <= kStageBytes && rd * 4 * K * 4 + kBiasFloats * 4 <= kStageBytes && R >= 1 &&
+         (rv + R - 1) / R <= kMaxLmChunks && Smem::total(n_layers) <= (size_t)kSmemLimit;
+  }
+  if (!ok)
+    return sm100_set_error(SM100_ERR_ARG,
+                           "decode: unsupported shape (tokens %d, layers %d, dim %d, heads %d, vocab %d, ctx %d, %d SMs)",
+                           n_tokens, n_layers, dim, heads, vocab, max_ctx, G);
+  const size_t smem = Smem::total(n_layers);
+  switch (dim / 128) {
+    case 4: return launch_decode<4>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
+    case 6: return launch_decode<6>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
+    case 8: return launch_decode<8>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
+    default:
+      return sm100_set_error(SM100_ERR_ARG, "decode: dim %d not built (512, 768 or 1024)", dim);
+  }
 }
 
-extern "C" int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim, int32_t max_ctx,
-                                 void *stream) {
-  return sm100_decode_steps(dev_model, 1, n_layers, dim, max_ctx, stream);
+extern "C" int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim, int32_t heads,
+                                 int32_t vocab, int32_t max_ctx, void *stream) {
+  return sm100_decode_steps(dev_model, 1, n_layers, dim, heads, vocab, max_ctx, stream);
 }

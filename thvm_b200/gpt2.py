@@ -167,8 +167,8 @@ class Transformer:
     @staticmethod
     def fused_fits(cfg: GPT2Config) -> bool:
         """Shapes the fused decode-step kernel takes (include/thvm_sm100.h)."""
-        return (cfg.n_layers <= L.DECODE_MAX_LAYERS and cfg.dim % 32 == 0 and 4 * cfg.dim <= 4096
-                and cfg.max_ctx <= 3392 and cfg.head_dim in (32, 64))
+        return (cfg.n_layers <= L.DECODE_MAX_LAYERS and cfg.dim in (512, 768, 1024)
+                and cfg.head_dim in (32, 64) and 2 * cfg.max_ctx + 3 * cfg.head_dim + 512 <= 8192)
 
     def _build_fused(self) -> None:
         """The device-resident Sm100DecodeModel over this model's buffers."""
@@ -189,7 +189,7 @@ class Transformer:
             m.w_p2[i], m.b_p2[i] = p(blk.mlp.c_proj.w), p(blk.mlp.c_proj.b)
             m.kv_cache[i] = p(blk.attn.cache_kv)
         # the kernel's step outputs: tagged 8-byte words, zero-initialised
-        self.words = [dev.alloc(8 * n) for n in (cfg.dim, 3 * cfg.dim, cfg.dim, cfg.hidden)]
+        self.words = [dev.alloc(8 * L.DECODE_REPLICAS * n) for n in (cfg.dim, 3 * cfg.dim, cfg.dim, cfg.hidden)]
         m.io = p(s.io)
         m.x_w, m.qkv_w, m.att_w, m.fc_w = (p(b) for b in self.words)
         self.part = dev.alloc(dev.lib.sm100_decode_part_bytes())
@@ -206,7 +206,7 @@ class Transformer:
         """The fused kernel over n greedy tokens (one launch)."""
         cfg = self.cfg
         return make_op(L.K_DECODE_STEP, self.s.io, {0: self.desc}, m=cfg.n_layers, k=cfg.dim,
-                       max_ctx=cfg.max_ctx, n=n_tokens)
+                       heads=cfg.n_heads, ld_out=cfg.vocab, max_ctx=cfg.max_ctx, n=n_tokens)
 
     def set_trace(self, on: bool = True) -> None:
         """Record the fused kernel's per-CTA phase timeline (read_trace); the
@@ -223,10 +223,10 @@ class Transformer:
         L.check(self.dev.lib.sm100_buf_write(self.desc, ctypes.addressof(m), ctypes.sizeof(m)), "buf_write(desc)")
 
     def read_trace(self, grid: int) -> np.ndarray:
-        """[grid, 5 n_layers + 1, 4] ns: barrier arrive, barrier passed,
-        input staged, phase done (kernel-relative after subtracting the min)."""
-        n = grid * (5 * self.cfg.n_layers + 1) * 4
-        return self.dev.read(self.trace, np.uint64, (n,)).reshape(grid, -1, 4)
+        """[grid, 5 n_layers + 1, 8] global-timer ns per CTA and step (the
+        slots include/thvm_sm100.h lists for Sm100DecodeModel.trace)."""
+        n = grid * (5 * self.cfg.n_layers + 1) * 8
+        return self.dev.read(self.trace, np.uint64, (n,)).reshape(grid, -1, 8)
 
     def step_ops(self) -> list:
         """The kernels of one decode step (T = 1, bump): the fused kernel, or
