@@ -330,6 +330,17 @@ int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_tokens, int3
 int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim,
                       int32_t heads, int32_t vocab, int32_t max_ctx, void *stream);
 
+/* ---- dense bf16 GEMM on the tensor cores ------------------------------------- */
+/* C[M, N] (f32) = A[M, K] (bf16) . B[N, K]^T (bf16), f32 accumulate: the matmul
+ * shape the reference renders as rmu_emit_matmul_tc (src/codegen/render_uop.c:
+ * 1784-1986, WMMA) for nn_dot / nn_linear with a K-major weight.  tcgen05 MMA
+ * from TMA-loaded 128-byte-swizzled tiles into TMEM; M % 128 == 0,
+ * N % 256 == 0, K % 64 == 0, 16-byte aligned.  Device pointers. */
+int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K, void *stream);
+/* non-zero when a GEMM launch since the last call gave up a bounded wait;
+ * synchronises the device and clears the word */
+uint32_t sm100_gemm_status(void);
+
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into
  * graph slot `slot` (0..63); replay launches it. */

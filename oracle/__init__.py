@@ -53,6 +53,15 @@ def lib():
         L.orc_gpt2_generate.argtypes = [ctypes.c_void_p, _i32p, ctypes.c_int32, ctypes.c_int32,
                                         _i32p]
         L.orc_num_threads.restype = ctypes.c_int
+        _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+        _u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+        L.orc_f32_to_bf16_n.argtypes = [_f32p, _u16p, _i64]
+        L.orc_f32_to_fp8e4m3_n.argtypes = [_f32p, _u8p, _i64]
+        L.orc_fp8e4m3_to_f32.restype = ctypes.c_float
+        L.orc_fp8e4m3_to_f32.argtypes = [ctypes.c_uint8]
+        L.orc_linear_bf16.argtypes = [_f32p, _u16p, _f32p, _i64, _i64, _i64]
+        L.orc_linear_fp8bs.argtypes = [_f32p, _u8p, _f32p, _f32p, _i64, _i64, _i64]
+        L.orc_gemm_bf16.argtypes = [_u16p, _u16p, _f32p, _i64, _i64, _i64]
         _lib = L
     return _lib
 
@@ -133,6 +142,64 @@ def embedding(w, idx):
     y = np.empty(idx.shape + (w.shape[1],), np.float32)
     lib().orc_embedding_f32(w, idx, y, idx.size, w.shape[0], w.shape[1])
     return y
+
+
+def to_bf16(x):
+    """f32 -> bf16 bits (uint16), the reference's f32_to_bf16."""
+    x = _c(x)
+    y = np.empty(x.shape, np.uint16)
+    lib().orc_f32_to_bf16_n(x.reshape(-1), y.reshape(-1), x.size)
+    return y
+
+
+def bf16_to_f32(b):
+    return (np.asarray(b, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def to_fp8e4m3(x):
+    """f32 -> e4m3 codes (uint8), the reference's saturating kernel store."""
+    x = _c(x)
+    y = np.empty(x.shape, np.uint8)
+    lib().orc_f32_to_fp8e4m3_n(x.reshape(-1), y.reshape(-1), x.size)
+    return y
+
+
+FP8E4M3_TABLE = None
+
+
+def fp8e4m3_to_f32(b):
+    global FP8E4M3_TABLE
+    if FP8E4M3_TABLE is None:
+        FP8E4M3_TABLE = np.array([lib().orc_fp8e4m3_to_f32(i) for i in range(256)], np.float32)
+    return FP8E4M3_TABLE[np.asarray(b, np.uint8)]
+
+
+def linear_bf16(x, w_bits):
+    """y = x @ bf16(W)^T, W bits [N, K]."""
+    x, w = _c(x), _c(w_bits, np.uint16)
+    K, N = x.shape[-1], w.shape[0]
+    y = np.empty(x.shape[:-1] + (N,), np.float32)
+    lib().orc_linear_bf16(x, w, y, x.size // K, K, N)
+    return y
+
+
+def linear_fp8bs(x, w_codes, scale):
+    """y = x @ (e4m3(W) * scale.repeat(128, 128))^T, W codes [N, K], scale [ceil(N/128), ceil(K/128)]."""
+    x, w, s = _c(x), _c(w_codes, np.uint8), _c(scale)
+    K, N = x.shape[-1], w.shape[0]
+    y = np.empty(x.shape[:-1] + (N,), np.float32)
+    lib().orc_linear_fp8bs(x, w, s, y, x.size // K, K, N)
+    return y
+
+
+def gemm_bf16(a_bits, b_bits):
+    """C[M, N] = bf16(A)[M, K] @ bf16(B)[N, K]^T with f32 accumulate."""
+    a, b = _c(a_bits, np.uint16), _c(b_bits, np.uint16)
+    M, K = a.shape
+    N = b.shape[0]
+    c = np.empty((M, N), np.float32)
+    lib().orc_gemm_bf16(a, b, c, M, N, K)
+    return c
 
 
 class _OrcGPT2(ctypes.Structure):

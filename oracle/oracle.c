@@ -369,3 +369,141 @@ int orc_gpt2_generate(const OrcGPT2 *m, const int32_t *prompt, int32_t n_prompt,
   orc_gpt2_state_free(s);
   return tok < 0 ? -1 : 0;
 }
+
+/* ---- low-precision storage formats ---------------------------------------- */
+
+uint16_t orc_f32_to_bf16(float v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u && (u & 0x007fffffu))   /* NaN: quiet, sign kept */
+    return (uint16_t)(((u & 0x80000000u) | 0x7fc00000u) >> 16);
+  const uint32_t lsb = (u >> 16) & 1u;                           /* ties to even */
+  return (uint16_t)((u + 0x7fffu + lsb) >> 16);
+}
+
+float orc_bf16_to_f32(uint16_t b) {
+  const uint32_t u = (uint32_t)b << 16;
+  float v;
+  memcpy(&v, &u, 4);
+  return v;
+}
+
+/* e4m3: bias 7, 3 mantissa bits, no infinities, 0x7f the NaN, max 448.
+ * Finite inputs round to nearest even on the exact value (f64 holds every
+ * f32 exactly, so the arithmetic below is exact up to the final rounding). */
+uint8_t orc_f32_to_fp8e4m3(float v) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  const uint8_t sign = (uint8_t)((u >> 24) & 0x80u);
+  if ((u & 0x7f800000u) == 0x7f800000u) return (u & 0x007fffffu) ? (uint8_t)(sign | 0x7f) : (uint8_t)(sign | 0x7e);
+  double a = fabs((double)v);
+  if (a == 0.0) return sign;
+  /* the e4m3 quantum at a: 2^(e - 3) for a in [2^e, 2^(e+1)), e >= -6; 2^-9 below */
+  int e;
+  frexp(a, &e);          /* a = f * 2^e, f in [0.5, 1) -> a in [2^(e-1), 2^e) */
+  e -= 1;
+  if (e < -6) e = -6;
+  const double q = ldexp(1.0, e - 3);
+  double n = a / q;       /* exact: q is a power of two */
+  double r = floor(n);
+  const double frac = n - r;
+  if (frac > 0.5 || (frac == 0.5 && fmod(r, 2.0) != 0.0)) r += 1.0;
+  double out = r * q;
+  if (out > 448.0) out = 448.0;  /* finite overflow saturates */
+  /* encode out (a multiple of its quantum, <= 448) */
+  if (out == 0.0) return sign;
+  int oe;
+  frexp(out, &oe);
+  oe -= 1;
+  uint32_t code;
+  if (oe < -6) {                         /* subnormal: out = m * 2^-9, m in 1..7 */
+    code = (uint32_t)(out / ldexp(1.0, -9));
+  } else {
+    const uint32_t mant = (uint32_t)(out / ldexp(1.0, oe - 3)) - 8u;   /* 0..7 */
+    code = ((uint32_t)(oe + 7) << 3) | mant;
+  }
+  return (uint8_t)(sign | code);
+}
+
+float orc_fp8e4m3_to_f32(uint8_t b) {
+  const uint32_t e = (b >> 3) & 0xfu, m = b & 0x7u;
+  const float s = (b & 0x80u) ? -1.0f : 1.0f;
+  if (e == 0xfu && m == 0x7u) return s * NAN;
+  if (e == 0) return s * (float)ldexp((double)m, -9);
+  return s * (float)ldexp((double)(8u + m), (int)e - 10);
+}
+
+void orc_f32_to_bf16_n(const float *x, uint16_t *y, int64_t n) {
+  for (int64_t i = 0; i < n; i++) y[i] = orc_f32_to_bf16(x[i]);
+}
+
+void orc_f32_to_fp8e4m3_n(const float *x, uint8_t *y, int64_t n) {
+  for (int64_t i = 0; i < n; i++) y[i] = orc_f32_to_fp8e4m3(x[i]);
+}
+
+typedef struct {
+  const float *x;
+  const void *w;
+  const float *scale;
+  float *y;
+  int64_t M, K, N;
+  int kind;   /* 0 bf16, 1 fp8 + block scales */
+} LowCtx;
+
+static void low_rows(void *p, int64_t lo, int64_t hi) {
+  const LowCtx *c = (const LowCtx *)p;
+  const int64_t sc = (c->K + 127) / 128;
+  for (int64_t m = 0; m < c->M; m++) {
+    const float *xr = c->x + m * c->K;
+    for (int64_t n = lo; n < hi; n++) {
+      float acc = 0.0f;
+      if (c->kind == 0) {
+        const uint16_t *wr = (const uint16_t *)c->w + n * c->K;
+        for (int64_t k = 0; k < c->K; k++) acc += xr[k] * orc_bf16_to_f32(wr[k]);
+      } else {
+        const uint8_t *wr = (const uint8_t *)c->w + n * c->K;
+        const float *srow = c->scale + (n / 128) * sc;
+        for (int64_t k = 0; k < c->K; k++) acc += xr[k] * (orc_fp8e4m3_to_f32(wr[k]) * srow[k / 128]);
+      }
+      c->y[m * c->N + n] = acc;
+    }
+  }
+}
+
+void orc_linear_bf16(const float *x, const uint16_t *w, float *y, int64_t M, int64_t K, int64_t N) {
+  LowCtx c = {x, w, NULL, y, M, K, N, 0};
+  par_for(N, 64, low_rows, &c);
+}
+
+void orc_linear_fp8bs(const float *x, const uint8_t *w, const float *scale, float *y, int64_t M,
+                      int64_t K, int64_t N) {
+  LowCtx c = {x, w, scale, y, M, K, N, 1};
+  par_for(N, 64, low_rows, &c);
+}
+
+typedef struct {
+  const uint16_t *a, *b;
+  float *c;
+  int64_t M, N, K;
+} GemmCtx;
+
+static void gemm_rows(void *p, int64_t lo, int64_t hi) {
+  const GemmCtx *g = (const GemmCtx *)p;
+  float *arow = (float *)malloc(sizeof(float) * (size_t)g->K);
+  if (!arow) return;
+  for (int64_t m = lo; m < hi; m++) {
+    for (int64_t k = 0; k < g->K; k++) arow[k] = orc_bf16_to_f32(g->a[m * g->K + k]);
+    for (int64_t n = 0; n < g->N; n++) {
+      const uint16_t *br = g->b + n * g->K;
+      float acc = 0.0f;
+      for (int64_t k = 0; k < g->K; k++) acc += arow[k] * orc_bf16_to_f32(br[k]);
+      g->c[m * g->N + n] = acc;
+    }
+  }
+  free(arow);
+}
+
+void orc_gemm_bf16(const uint16_t *a, const uint16_t *b, float *c, int64_t M, int64_t N, int64_t K) {
+  GemmCtx g = {a, b, c, M, N, K};
+  par_for(M, 1, gemm_rows, &g);
+}

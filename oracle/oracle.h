@@ -63,6 +63,38 @@ void orc_argmax_f32(const float *x, int32_t *out, int64_t M, int64_t N);
 void orc_embedding_f32(const float *w, const int32_t *idx, float *y, int64_t n_idx,
                        int64_t V, int64_t D);
 
+/* ---- low-precision storage formats (src/dtype/fp_convert.c, src/dtype/fp8.c)
+ * f32 -> bf16: round to nearest even on the dropped 16 bits; a NaN becomes the
+ * quiet NaN with the input's sign (fp_convert.c f32_to_bf16).  bf16 -> f32:
+ * the 16 bits on top (bf16_to_f32). */
+uint16_t orc_f32_to_bf16(float v);
+float orc_bf16_to_f32(uint16_t b);
+/* f32 -> fp8 e4m3 as the kernel store narrows (fp8.c f32_to_fp8e4m3_sat):
+ * round to nearest even, finite overflow and +-inf saturate to +-448 (0x7e),
+ * a NaN keeps its sign with the e4m3 NaN code 0x7f.  e4m3 -> f32 exact; 0x7f /
+ * 0xff decode to NaN (fp8e4m3_to_f32). */
+uint8_t orc_f32_to_fp8e4m3(float v);
+float orc_fp8e4m3_to_f32(uint8_t b);
+void orc_f32_to_bf16_n(const float *x, uint16_t *y, int64_t n);
+void orc_f32_to_fp8e4m3_n(const float *x, uint8_t *y, int64_t n);
+
+/* y[m,n] = sum_k x[m,k] * bf16(w[n,k]): a bf16 weight widened to f32, f32
+ * products and one f32 accumulator in k order (the reference's CAST to f32
+ * then the Linear loop, src/nn/linear.c:1-6). */
+void orc_linear_bf16(const float *x, const uint16_t *w, float *y, int64_t M, int64_t K, int64_t N);
+
+/* fp8 e4m3 weights with one f32 scale per 128 x 128 block: the composition
+ * W_f32 = W.cast(f32) * scale.repeat(128, 128) followed by the Linear loop
+ * (no fp8 block scaling exists in the reference; this is the composition of
+ * its own ops, py/thvm/dtypes.py fp8e4m3 + src/dtype/fp8.c).  scale is
+ * [ceil(N/128), ceil(K/128)] row-major. */
+void orc_linear_fp8bs(const float *x, const uint8_t *w, const float *scale, float *y, int64_t M,
+                      int64_t K, int64_t N);
+
+/* C[m,n] = sum_k bf16(A[m,k]) * bf16(B[n,k]) in f32, k order (a bf16 matmul
+ * with f32 accumulate, src/nn/dot.c:1-20 on bf16 inputs cast to f32). */
+void orc_gemm_bf16(const uint16_t *a, const uint16_t *b, float *c, int64_t M, int64_t N, int64_t K);
+
 /* ---- GPT-2 decoder (bench/gpt2/thvm_gpt2.py:27-128) ------------------------
  * Weights are pointers into caller memory, Linear weights (out, in). */
 typedef struct {

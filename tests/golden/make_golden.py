@@ -14,6 +14,12 @@ package finds its library beside itself) and the reference's GPT-2 model code
   ops.npz      per-op inputs and outputs (linear, layernorm, softmax, gelu,
                scaled_dot_product_attention decode / causal / masked, argmax
                with ties, embedding incl. out-of-range ids).
+  dtypes.npz   the reference's own storage conversions (src/dtype/fp_convert.c
+               f32_to_bf16, src/dtype/fp8.c f32_to_fp8e4m3_sat and
+               fp8e4m3_to_f32, called in its library) on f32 bit patterns:
+               seeded normals, random bit patterns (NaN payloads, subnormals,
+               infinities) and the e4m3 rounding / saturation edges; every e4m3
+               code decoded.
   gpt2.npz     GPT-2 small (12 layers, fp32, MAX_CONTEXT=1024) greedy decode:
                the 16 prompt ids, the 64 generated ids, per-step top-1 / top-2
                logits, and the full logits of the prompt step and the first
@@ -188,9 +194,37 @@ def make_gpt2(n_new: int = 64) -> None:
     print("wrote", OUT / "gpt2.npz")
 
 
+def make_dtypes() -> None:
+    """bf16 / fp8 e4m3 conversions of the reference library, bit for bit."""
+    import ctypes
+    lib = ctypes.CDLL(str(REPO / "oracle" / "_ref" / "libthvm_py.so"))
+    lib.f32_to_bf16.restype = ctypes.c_uint16
+    lib.f32_to_fp8e4m3_sat.restype = ctypes.c_uint8
+    lib.fp8e4m3_to_f32.restype = ctypes.c_float
+    lib.f32_to_bf16.argtypes = lib.f32_to_fp8e4m3_sat.argtypes = [ctypes.c_float]
+    lib.fp8e4m3_to_f32.argtypes = [ctypes.c_uint8]
+    rng = np.random.default_rng(7)
+    edges = np.array([0.0, -0.0, np.inf, -np.inf, 448, 456, 464, 464.0001, 472, 480, -1000, 2 ** -10,
+                      2 ** -9, 1.5 * 2 ** -10, 2.5 * 2 ** -9, 2 ** -6, 1.0625, 1.1875, 3e-38, 1e-45,
+                      1.00390625, 1.0078125, 1.01171875], np.float32)
+    x = np.concatenate([edges, -edges, rng.standard_normal(4096).astype(np.float32),
+                        (rng.standard_normal(2048) * 64).astype(np.float32),
+                        rng.integers(0, 2 ** 32, 4096, dtype=np.uint64).astype(np.uint32).view(np.float32)])
+    # pass the exact f32 bits (a NaN payload survives: no Python float round trip)
+    cf = [ctypes.c_float.from_buffer_copy(v.tobytes()) for v in x]
+    bf16 = np.array([lib.f32_to_bf16(v) for v in cf], np.uint16)
+    fp8 = np.array([lib.f32_to_fp8e4m3_sat(v) for v in cf], np.uint8)
+    dec = np.array([lib.fp8e4m3_to_f32(i) for i in range(256)], np.float32)
+    np.savez_compressed(OUT / "dtypes.npz", x_bits=x.view(np.uint32), bf16=bf16, fp8e4m3=fp8, fp8e4m3_decoded=dec)
+    print("wrote", OUT / "dtypes.npz")
+
+
 if __name__ == "__main__":
-    _setup()
-    which = sys.argv[1:] or ["ops", "gpt2"]
+    which = sys.argv[1:] or ["ops", "gpt2", "dtypes"]
+    if "dtypes" in which:
+        make_dtypes()
+    if "ops" in which or "gpt2" in which:
+        _setup()
     if "ops" in which:
         make_ops()
     if "gpt2" in which:

@@ -79,3 +79,49 @@ def test_planted_mistake_is_caught(golden_ops):
     y[0, 0, 3] += 1e-6
     assert not np.array_equal(y, g["lin_b_y"])
     assert not np.array_equal(O.argmax(g["am_x"][:, ::-1].copy()), g["am_y"])
+
+
+# ---- bf16 / fp8 e4m3 storage formats (tests/golden/dtypes.npz: the
+# reference library's own conversions, bit for bit) ---------------------------
+
+@pytest.fixture(scope="module")
+def golden_dtypes():
+    from conftest import GOLDEN
+    return dict(np.load(GOLDEN / "dtypes.npz"))
+
+
+def test_bf16_conversion_matches_reference(golden_dtypes):
+    g = golden_dtypes
+    x = g["x_bits"].view(np.float32)
+    assert np.array_equal(O.to_bf16(x), g["bf16"])
+
+
+def test_fp8e4m3_encode_matches_reference(golden_dtypes):
+    g = golden_dtypes
+    x = g["x_bits"].view(np.float32)
+    assert np.array_equal(O.to_fp8e4m3(x), g["fp8e4m3"])
+
+
+def test_fp8e4m3_decode_matches_reference(golden_dtypes):
+    ref = golden_dtypes["fp8e4m3_decoded"]
+    mine = O.fp8e4m3_to_f32(np.arange(256))
+    assert np.array_equal(np.isnan(mine), np.isnan(ref))
+    ok = ~np.isnan(ref)
+    assert np.array_equal(mine[ok].view(np.uint32), ref[ok].view(np.uint32))
+
+
+def test_lowp_linears_are_the_f32_loop_on_widened_weights():
+    """The bf16 and block-scaled fp8 oracles are the reference's f32 Linear
+    loop over the widened weights (for fp8: decoded * its block scale), bit
+    for bit."""
+    rng = np.random.default_rng(5)
+    M, K, N = 2, 300, 260
+    x = O.bf16_to_f32(O.to_bf16(rng.standard_normal((M, K)).astype(np.float32)))
+    wb = O.to_bf16(rng.standard_normal((N, K)).astype(np.float32))
+    assert np.array_equal(O.linear_bf16(x, wb), O.linear(x, O.bf16_to_f32(wb)))
+    w8 = O.to_fp8e4m3(rng.standard_normal((N, K)).astype(np.float32))
+    sc = rng.uniform(0.5, 2.0, ((N + 127) // 128, (K + 127) // 128)).astype(np.float32)
+    wide = O.fp8e4m3_to_f32(w8) * np.repeat(np.repeat(sc, 128, 0), 128, 1)[:N, :K]
+    assert np.array_equal(O.linear_fp8bs(x, w8, sc), O.linear(x, wide))
+    a = O.to_bf16(rng.standard_normal((7, K)).astype(np.float32))
+    assert np.array_equal(O.gemm_bf16(a, wb), O.linear(O.bf16_to_f32(a), O.bf16_to_f32(wb)))

@@ -1,0 +1,289 @@
+// Dense bf16 GEMM on the 5th-generation tensor cores: C[M, N] (f32) =
+// A[M, K] (bf16) . B[N, K]^T (bf16), f32 accumulate.  Both operands K-major,
+// as nn.Linear keeps its weight (out, in) and nn_dot contracts the last axis
+// (src/nn/dot.c:1-20, src/nn/linear.c:1-6); the reference renders this shape
+// as a WMMA 16x16x16 kernel (src/codegen/render_uop.c:1784-1986).
+//
+// One persistent CTA per SM, warp-specialised:
+//   warp 0  TMA producer: 2-D tensor copies (cp.async.bulk.tensor, 128-byte
+//           swizzle, no multicast) of A [128 x 64] and B [256 x 64] k-blocks
+//           into a 4-stage shared-memory ring (48 KB per stage);
+//   warp 1  MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16,
+//           kind::f16, bf16 in / f32 accumulate) four times per k-block from
+//           shared-memory descriptors into a TMEM accumulator, then
+//           tcgen05.commit frees the stage; the tile's last commit signals the
+//           epilogue;
+//   warps 2-5 epilogue: tcgen05.ld the accumulator (each warp its 32-lane
+//           quarter = 32 rows), store f32 rows to global memory.
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
+// the MMAs of tile i+1.  Tiles are walked round-robin over the CTAs.
+//
+// Every wait is bounded: a timeout sets a status word (sm100_gemm_status)
+// and the kernel runs to its end.  Shapes: M % 128 == 0, N % 256 == 0,
+// K % 64 == 0, 16-byte aligned rows.
+#include <cuda.h>
+
+#include "common.cuh"
+#include "tma.cuh"
+
+namespace sm100 {
+
+constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64;   // tile; BK = one 128-byte swizzle row of bf16
+constexpr int kGmStages = 4;
+constexpr int kGmABytes = kGmBM * kGmBK * 2;          // 16 KB
+constexpr int kGmBBytes = kGmBN * kGmBK * 2;          // 32 KB
+constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
+constexpr int kGmThreads = 6 * 32;
+constexpr int kGmEpiWarps = 4;
+constexpr int kGmTmemCols = 2 * kGmBN;                 // two accumulators
+constexpr int kGmSmem = kGmStages * kGmStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+
+__device__ uint32_t g_gemm_status;   // set when a bounded wait gave up
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// UMMA shared-memory descriptor of a K-major tile with the 128-byte swizzle:
+// rows of 128 bytes, 8-row atoms of 1024 bytes stacked contiguously (stride
+// byte offset 1024), version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void *p) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;          // start address (16-byte units)
+  d |= (uint64_t)1 << 16;                // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;      // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;                // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 A and B, f32 D, K-major both, M = 128, N = 256.
+constexpr uint32_t kGmIdesc = (1u << 4)              // D format f32
+                              | (1u << 7)            // A bf16
+                              | (1u << 10)           // B bf16
+                              | ((uint32_t)(kGmBN >> 3) << 17) | ((uint32_t)(kGmBM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kGmIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__global__ void __launch_bounds__(kGmThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, float *c,
+                     int M, int N, int K) {
+  extern __shared__ unsigned char smem_raw[];
+  // the 128-byte swizzle atoms want 1024-byte aligned tiles
+  unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGmStages * kGmStageBytes);   // [stages]
+  uint64_t *empty = full + kGmStages;                                                 // [stages]
+  uint64_t *acc_full = empty + kGmStages;                                             // [2]
+  uint64_t *acc_empty = acc_full + 2;                                                 // [2]
+  uint64_t *mma_done = acc_empty + 2;                                                 // all MMAs retired
+  uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(mma_done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles_m = M / kGmBM, tiles_n = N / kGmBN, n_tiles = tiles_m * tiles_n, kb_n = K / kGmBK;
+  uint32_t *status = &g_gemm_status;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGmStages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; a++) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], kGmEpiWarps);
+    }
+    mbar_init(mma_done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {   // TMEM: 512 columns (both accumulators), address into shared memory
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_base_s)),
+                 "r"(kGmTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem_base = *tmem_base_s;
+
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        const int tm = tile / tiles_n, tn = tile % tiles_n;
+        for (int kb = 0; kb < kb_n; kb++, it++) {
+          const int s = it % kGmStages;
+          if (it >= kGmStages && !mbar_wait(&empty[s], (uint32_t)(((it / kGmStages) - 1) & 1), status)) {
+            ok = false;
+            break;
+          }
+          unsigned char *st = smem + (size_t)s * kGmStageBytes;
+          mbar_expect_tx(&full[s], kGmStageBytes);
+          tma_load_2d(st, &map_a, kb * kGmBK, tm * kGmBM, &full[s]);
+          tma_load_2d(st + kGmABytes, &map_b, kb * kGmBK, tn * kGmBN, &full[s]);
+        }
+      }
+      // the last copies have landed before the CTA may exit
+      for (int j = it - kGmStages > 0 ? it - kGmStages : 0; j < it; j++)
+        mbar_wait(&full[j % kGmStages], (uint32_t)((j / kGmStages) & 1), status, false);
+    }
+  } else if (warp == 1) {
+    // ---- MMA issuer -----------------------------------------------------------
+    if (lane == 0) {
+      int it = 0, t_local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, t_local++) {
+        const int a = t_local & 1;
+        // the epilogue has drained this accumulator (its use two tiles ago)
+        if (t_local >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((t_local >> 1) - 1) & 1), status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t tmem_d = tmem_base + (uint32_t)(a * kGmBN);   // column offset
+        for (int kb = 0; kb < kb_n; kb++, it++) {
+          const int s = it % kGmStages;
+          if (!mbar_wait(&full[s], (uint32_t)((it / kGmStages) & 1), status)) {
+            ok = false;
+            break;
+          }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          unsigned char *st = smem + (size_t)s * kGmStageBytes;
+          const uint64_t da = smem_desc_sw128(st), db = smem_desc_sw128(st + kGmABytes);
+#pragma unroll
+          for (int k = 0; k < kGmBK / 16; k++)   // K = 16 per MMA: 32 bytes along the swizzled row
+            umma_bf16(tmem_d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);   // the stage is free once these MMAs have read it
+        }
+        umma_commit(&acc_full[a]);  // the accumulator is complete
+      }
+      // every MMA issued has retired before TMEM is released (also after a timeout)
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0, status, false);
+    }
+  } else {
+    // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 -----------------
+    const int q = warp & 3;
+    int t_local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, t_local++) {
+      const int a = t_local & 1;
+      const int tm = tile / tiles_n, tn = tile % tiles_n;
+      if (!mbar_wait(&acc_full[a], (uint32_t)((t_local >> 1) & 1), status)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const int row = tm * kGmBM + q * 32 + lane;
+      float *crow = c + (size_t)row * N + (size_t)tn * kGmBN;
+      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kGmBN);
+#pragma unroll 1
+      for (int cc = 0; cc < kGmBN; cc += 32) {
+        uint32_t r[32];
+        tmem_ld32(taddr + (uint32_t)cc, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float4 *dst = reinterpret_cast<float4 *>(crow + cc);
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+          dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
+                               __uint_as_float(r[4 * j + 3]));
+      }
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kGmTmemCols) : "memory");
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D map of a row-major bf16 [rows, cols] matrix, box [box_rows, 64 cols], 128-byte swizzle.
+static bool make_map(CUtensorMap *m, const void *base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGmBK, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace sm100
+
+using namespace sm100;
+
+extern "C" int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
+                               void *stream) {
+  if (!a || !b || !c || M <= 0 || N <= 0 || K <= 0 || M % kGmBM || N % kGmBN || K % kGmBK || M > (1 << 30) ||
+      N > (1 << 30) || K > (1 << 30) || ((uintptr_t)a & 15) || ((uintptr_t)b & 15) || ((uintptr_t)c & 15))
+    return sm100_set_error(SM100_ERR_ARG,
+                           "gemm_bf16: shape %lld x %lld x %lld (M %% 128, N %% 256, K %% 64 must be 0; 16-byte aligned)",
+                           (long long)M, (long long)N, (long long)K);
+  CUtensorMap ma, mb;
+  if (!make_map(&ma, a, M, K, kGmBM) || !make_map(&mb, b, N, K, kGmBN))
+    return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: tensor map encoding failed");
+  static int num_sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "gemm_bf16: device %d", dev);
+  if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = (M / kGmBM) * (N / kGmBN);
+  const int grid = (int)(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: smem attribute: %s", cudaGetErrorString(e));
+  gemm_bf16_kernel<<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mb, c, (int)M, (int)N, (int)K);
+  return launch_status("gemm_bf16");
+}
+
+// Status of the GEMM launches since the last call (non-zero: a bounded wait
+// gave up); reading clears it.  Synchronises the device.
+extern "C" uint32_t sm100_gemm_status(void) {
+  uint32_t v = 0, z = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(&v, g_gemm_status, sizeof(v));
+  cudaMemcpyToSymbol(g_gemm_status, &z, sizeof(z));
+  return v;
+}

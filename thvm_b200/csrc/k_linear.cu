@@ -18,6 +18,7 @@
 #include <cuda_fp8.h>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace sm100 {
 
@@ -245,6 +246,195 @@ __global__ void __launch_bounds__(256) linear_kernel(LinParams p) {
   }
 }
 
+// Decode matvec (M = 1, no LayerNorm prologue): one warp per output row.
+// Every lane issues all of its weight loads for the row (NV 16-byte vectors,
+// streaming, not L1-allocated) at CTA start, before x is staged into shared
+// memory, so the HBM latency overlaps the staging; then the dot product, a
+// warp reduction and the epilogue (bias / GELU / residual / KV append).
+// Bound: HBM, every weight byte read once.  128 threads (4 rows) per CTA
+// keeps the last wave short.
+template <typename WT, int NV>
+__global__ void __launch_bounds__(128) gemv_kernel(LinParams p) {
+  extern __shared__ float4 smem4[];
+  float *xs = reinterpret_cast<float *>(smem4);
+  constexpr int V = WVec<WT>::n;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t n = (int64_t)blockIdx.x * 4 + warp, K = p.K;
+  const bool live = n < p.N;
+  const WT *wr = static_cast<const WT *>(p.w) + (live ? n : 0) * K;
+  uint4 wv[NV];
+#pragma unroll
+  for (int v = 0; v < NV; v++) wv[v] = __ldcs(reinterpret_cast<const uint4 *>(wr + (int64_t)(lane + 32 * v) * V));
+  const float4 *x4 = reinterpret_cast<const float4 *>(p.x);
+  for (int64_t i = threadIdx.x; i < K / 4; i += blockDim.x) reinterpret_cast<float4 *>(xs)[i] = __ldg(x4 + i);
+  __syncthreads();
+  float acc[1] = {0.0f};
+#pragma unroll
+  for (int v = 0; v < NV; v++) {
+    const int64_t k0 = (int64_t)(lane + 32 * v) * V;
+    const float sc = (sizeof(WT) == 1) ? p.w_scale[(n >> 7) * p.scale_cols + (k0 >> 7)] : 1.0f;
+    dot_vec<WT, 1>(wv[v], xs + k0, K, acc, sc);
+  }
+  const float a = warp_sum(acc[0]);
+  if (live && lane == 0) epilogue_store(p, 0, n, a);
+}
+
+// Decode matvec streamed through shared memory (M = 1): one CTA per SM owns a
+// contiguous slice of rows; one producer thread keeps every stage of a ring
+// of 8-row stages in flight with TMA bulk copies (L2 evict_first: the
+// weights are read once); 16 consumer warps take (row, half of K) each per
+// stage, dot it with x (staged once per CTA in shared memory), reduce across
+// the warp, and after one barrier eight threads add the halves and run the
+// epilogue.  Streaming with up to ~190 KB in flight per SM is what reaches
+// HBM read bandwidth (loads issued per thread stall between short CTAs), and
+// 16 warps hide the fp8 widening and shared-memory latency.
+constexpr int kGvRows = 8;                        // rows per stage
+constexpr int kGvWarps = 2 * kGvRows;             // consumer warps: (row, K half)
+constexpr int kGvThreads = (kGvWarps + 1) * 32;   // + producer warp
+constexpr int kGvSmem = 200 * 1024;               // ring + x + scales + partials + barriers
+constexpr int kGvMaxStages = 8;
+
+template <typename WT>
+__global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, int stages, int stage_floats) {
+  extern __shared__ __align__(1024) unsigned char smem[];
+  constexpr int V = WVec<WT>::n;
+  const int64_t K = p.K;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r0 = (p.N * blockIdx.x) / gridDim.x, r1 = (p.N * (blockIdx.x + 1)) / gridDim.x;
+  const int nchunks = (int)((r1 - r0 + kGvRows - 1) / kGvRows);
+  float *ring = reinterpret_cast<float *>(smem);
+  float *xs = ring + (size_t)stages * stage_floats;                          // [K]
+  float *ss = xs + K;                                                         // [2][scale_cols]: this CTA's scale rows
+  float *part = ss + 2 * (size_t)p.scale_cols;                                // [2][kGvRows]
+  uint64_t *full = reinterpret_cast<uint64_t *>(part + 2 * kGvRows);          // [stages]
+  uint64_t *empty = full + kGvMaxStages;                                      // [stages]
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const size_t row_bytes = (size_t)K * sizeof(WT);
+  if (warp == kGvWarps) {
+    // producer: chunk c -> stage c % stages, rows [r0 + 8c, ...)
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_first();
+      const unsigned char *w = static_cast<const unsigned char *>(p.w);
+      for (int c = 0; c < nchunks; c++) {
+        const int s = c % stages;
+        if (c >= stages && !mbar_wait(&empty[s], (uint32_t)(((c / stages) - 1) & 1), nullptr)) break;
+        const int64_t rr = r0 + (int64_t)c * kGvRows, nr = (r1 - rr) < kGvRows ? (r1 - rr) : kGvRows;
+        const uint32_t bytes = (uint32_t)(nr * row_bytes);
+        mbar_expect_tx(&full[s], bytes);
+        bulk_g2s_hint(ring + (size_t)s * stage_floats, w + rr * row_bytes, bytes, &full[s], pol);
+      }
+      // every issued copy has landed before the CTA exits (bounded)
+      for (int c = nchunks - stages > 0 ? nchunks - stages : 0; c < nchunks; c++)
+        mbar_wait(&full[c % stages], (uint32_t)((c / stages) & 1), nullptr, false);
+    }
+    return;
+  }
+  // consumers: x (and the fp8 block scales of this CTA's rows) into shared memory
+  const int ct = threadIdx.x, nct = kGvWarps * 32;
+  for (int64_t i = ct; i < K / 4; i += nct)
+    reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
+  if constexpr (sizeof(WT) == 1) {
+    const int64_t sr0 = r0 >> 7;
+    for (int i = ct; i < 2 * p.scale_cols; i += nct) {
+      const int64_t sr = sr0 + i / p.scale_cols;
+      ss[i] = (sr * 128 < p.N) ? p.w_scale[sr * p.scale_cols + i % p.scale_cols] : 0.0f;
+    }
+  }
+  asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
+  const int nvec = (int)(K / V), half = warp / kGvRows, rw = warp % kGvRows;
+  const int v0 = half ? nvec / 2 : 0, v1 = half ? nvec : nvec / 2;
+  for (int c = 0; c < nchunks; c++) {
+    const int s = c % stages;
+    mbar_wait(&full[s], (uint32_t)((c / stages) & 1), nullptr);
+    const int64_t n = r0 + (int64_t)c * kGvRows + rw;
+    if (n < r1) {
+      const unsigned char *wrow = reinterpret_cast<const unsigned char *>(ring + (size_t)s * stage_floats) +
+                                  (size_t)rw * row_bytes;
+      const float *srow = ss + ((n >> 7) - (r0 >> 7)) * p.scale_cols;
+      float acc[1] = {0.0f};
+      for (int v = v0 + lane; v < v1; v += 32) {
+        const uint4 wv = *reinterpret_cast<const uint4 *>(wrow + (size_t)v * 16);
+        const int64_t k0 = (int64_t)v * V;
+        dot_vec<WT, 1>(wv, xs + k0, K, acc, (sizeof(WT) == 1) ? srow[k0 >> 7] : 1.0f);
+      }
+      const float a = warp_sum(acc[0]);
+      if (lane == 0) part[half * kGvRows + rw] = a;
+    }
+    // the stage is read: the producer may refill it
+    asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
+    if (ct == 0) mbar_arrive(&empty[s]);
+    if (ct < kGvRows) {
+      const int64_t n2 = r0 + (int64_t)c * kGvRows + ct;
+      if (n2 < r1) epilogue_store(p, 0, n2, part[ct] + part[kGvRows + ct]);
+    }
+    // part[] is rewritten next chunk only after every warp passed this point
+    asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
+  }
+}
+
+// Stages of the streamed matvec for this shape, or 0 when it does not fit.
+template <typename WT>
+static int gemv_tma_stages(const LinParams &p, int &stage_floats) {
+  const size_t stage = (size_t)kGvRows * (size_t)p.K * sizeof(WT);
+  const size_t fixed = (size_t)p.K * 4 + 2 * (size_t)p.scale_cols * 4 + 2 * kGvRows * 4 + 2 * kGvMaxStages * 8 + 64;
+  if (p.K % WVec<WT>::n || stage % 16 || fixed + 2 * stage > (size_t)kGvSmem) return 0;
+  stage_floats = (int)(stage / 4);
+  const size_t s = (kGvSmem - fixed) / stage;
+  return (int)(s < (size_t)kGvMaxStages ? s : (size_t)kGvMaxStages);
+}
+
+template <typename WT>
+static int launch_gemv_tma(const LinParams &p, int stages, int stage_floats, cudaStream_t st) {
+  static int num_sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "gemv: device %d", dev);
+  if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int64_t rows_per = (p.N + num_sms[dev] - 1) / num_sms[dev];
+  const int grid = rows_per < kGvRows ? (int)((p.N + kGvRows - 1) / kGvRows) : num_sms[dev];
+  cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
+  gemv_tma_kernel<WT><<<grid, kGvThreads, kGvSmem, st>>>(p, stages, stage_floats);
+  return launch_status("gemv_tma");
+}
+
+// NV = K / (V * 32) vectors per lane when it is one of the instantiated
+// counts, else 0 (the general kernel takes the shape).
+template <typename WT>
+static int gemv_nv(const LinParams &p) {
+  constexpr int V = WVec<WT>::n;
+  if (p.K % (V * 32)) return 0;
+  const int64_t nv = p.K / (V * 32);
+  return (nv == 2 || nv == 4 || nv == 6 || nv == 8 || nv == 12 || nv == 16) ? (int)nv : 0;
+}
+
+template <typename WT, int NV>
+static int launch_gemv_nv(const LinParams &p, cudaStream_t st) {
+  const size_t smem = sizeof(float) * (size_t)p.K;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(gemv_kernel<WT, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  gemv_kernel<WT, NV><<<(unsigned)((p.N + 3) / 4), 128, smem, st>>>(p);
+  return launch_status("gemv");
+}
+
+template <typename WT>
+static int launch_gemv(const LinParams &p, int nv, cudaStream_t st) {
+  switch (nv) {
+    case 2: return launch_gemv_nv<WT, 2>(p, st);
+    case 4: return launch_gemv_nv<WT, 4>(p, st);
+    case 6: return launch_gemv_nv<WT, 6>(p, st);
+    case 8: return launch_gemv_nv<WT, 8>(p, st);
+    case 12: return launch_gemv_nv<WT, 12>(p, st);
+    default: return launch_gemv_nv<WT, 16>(p, st);
+  }
+}
+
 template <typename WT, int TPR, int MB>
 static int launch_tpr(const LinParams &p, bool vec, cudaStream_t st) {
   constexpr int RPC = 256 / TPR;
@@ -277,6 +467,15 @@ static int launch_w(const LinParams &p, cudaStream_t st) {
                    ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0 || true);
   // Threads per row: the most that still give every thread >= 3 vectors, so
   // that small-N projections spread over many CTAs; at least a warp.
+  // decode matvec fast path: one row, no LayerNorm, aligned x / W, K a
+  // multiple of 32 vectors with an instantiated count
+  if (p.M == 1 && vec && !(p.flags & SM100_LIN_LN) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0)) {
+    int stage_floats = 0;
+    const int stages = gemv_tma_stages<WT>(p, stage_floats);
+    if (stages >= 2 && p.N >= 1024) return launch_gemv_tma<WT>(p, stages, stage_floats, st);
+    const int nv = p.K * sizeof(float) <= 200 * 1024 ? gemv_nv<WT>(p) : 0;
+    if (nv) return launch_gemv<WT>(p, nv, st);
+  }
   const int64_t nvec = (p.K + V - 1) / V;
   int tpr = 32;
   while (tpr < 256 && nvec / (tpr * 2) >= 3 && p.N * tpr < 148LL * 8 * 256) tpr *= 2;

@@ -89,9 +89,13 @@ class Device:
 
     # ---- graphs (TinyJit replay) -----------------------------------------
     _next_slot = 0
+    _free_slots: list = []
 
     def new_graph_slot(self) -> int:
-        """A graph slot no other user of this Device holds (64 per process)."""
+        """A graph slot no other user of this Device holds (64 per process;
+        drop() returns it)."""
+        if Device._free_slots:
+            return Device._free_slots.pop()
         if Device._next_slot >= 64:
             raise L.Sm100Error(L.ERR_STATE, "graph slots exhausted")
         Device._next_slot += 1
@@ -108,6 +112,8 @@ class Device:
 
     def drop(self, slot: int) -> None:
         self.lib.sm100_graph_drop(slot)
+        if slot not in Device._free_slots:
+            Device._free_slots.append(slot)
 
     @property
     def stream(self) -> int:

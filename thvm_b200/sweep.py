@@ -1,0 +1,172 @@
+"""The standalone contraction sweep on the sm_100a device.
+
+    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm]
+
+Seeded N(0,1) inputs, fp32 accumulate:
+  * decode matvec x[1, 4096] against W (11008 x 4096) in bf16, and in fp8 e4m3
+    with one f32 scale per 128 x 128 block (scales uniform in [0.5, 2]);
+  * bf16 GEMM C[M, N] = A[M, K] B[N, K]^T at M=N=K=4096 and M=8192, N=K=4096
+    (when the tcgen05 GEMM is built into the library).
+The launches of a case are captured into one CUDA graph and replayed between
+one pair of CUDA events on the library's stream, rotating over operand copies
+that together exceed twice L2 (every launch reads cold operands); one JSON
+line per case with the roofline fraction against MEASURED_PEAKS.json.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import numpy as np
+
+from . import _lib as L
+from .device import Device
+from .gpt2 import make_op
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def bf16_bits(a: np.ndarray) -> np.ndarray:
+    """f32 -> bf16 bits, round to nearest even (the storage format)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def fp8_codes(a: np.ndarray) -> np.ndarray:
+    """f32 -> e4m3 codes for |a| < 448 (finite draws of N(0,1)): round to nearest even."""
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+class Timer:
+    """The launches captured once into a CUDA graph (the library's TinyJit
+    graph slots) and replayed between one pair of CUDA events on the
+    library's stream, so host dispatch cost is outside the measurement.
+    Callers rotate over operand copies whose total is larger than L2, so
+    every launch reads operands the previous launches evicted."""
+
+    def __init__(self, dev: Device):
+        import torch
+        self.torch = torch
+        self.dev = dev
+        self.stream = torch.cuda.ExternalStream(dev.stream)
+
+    def time(self, launches, iters: int) -> float:
+        """Mean ms per launch over iters launches (launches[i % len] each)."""
+        torch, dev = self.torch, self.dev
+        slot = dev.new_graph_slot()
+        dev.capture_begin(slot)
+        try:
+            for i in range(iters):
+                launches[i % len(launches)]()
+        finally:
+            dev.capture_end(slot)
+        for _ in range(2):
+            dev.replay(slot)
+        dev.sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(self.stream)
+        dev.replay(slot)
+        e1.record(self.stream)
+        e1.synchronize()
+        dev.drop(slot)
+        return e0.elapsed_time(e1) / iters
+
+
+def copies_for(nbytes: int, l2: int = 126 << 20) -> int:
+    """Operand copies so that the rotation covers more than twice L2."""
+    return max(2, -(-2 * l2 // max(nbytes, 1)))
+
+
+def matvec_cases(dev: Device, timer: Timer, iters: int):
+    hbm, _, kind = peaks()
+    rng = np.random.default_rng(0)
+    M, K, N = 1, 4096, 11008
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    x = (bf16_bits(x).astype(np.uint32) << 16).view(np.float32)
+    y = dev.alloc(M * N * 4)
+    xb = dev.upload(x)
+    out = []
+    for name in ("bf16", "fp8e4m3_bs128"):
+        w = rng.standard_normal((N, K)).astype(np.float32)
+        if name == "bf16":
+            host, dt, wbytes, sc = bf16_bits(w), L.DT_BF16, N * K * 2, None
+        else:
+            sc = rng.uniform(0.5, 2.0, ((N + 127) // 128, (K + 127) // 128)).astype(np.float32)
+            host, dt, wbytes = fp8_codes(w), L.DT_FP8E4M3, N * K + sc.nbytes
+        ops, bufs = [], []
+        for _ in range(copies_for(wbytes)):
+            wb = dev.upload(host)
+            slots = {} if sc is None else {6: dev.upload(sc)}
+            bufs += [wb] + list(slots.values())
+            op = make_op(L.K_LINEAR, y, {0: xb, 1: wb, **slots}, m=M, n=N, k=K)
+            op.kernel.dtype = dt
+            ops.append(op)
+        ms = timer.time([lambda o=o: dev.dispatch(o.kernel, o.in_ids, o.out_id) for o in ops], iters)
+        byts = wbytes + x.nbytes + M * N * 4
+        gbs = byts / (ms / 1e3) / 1e9
+        out.append({"case": f"matvec_{name}", "M": M, "N": N, "K": K, "kernel": "gemv_kernel",
+                    "us": round(ms * 1e3, 2), "bytes": byts, "achieved": round(gbs, 1), "unit": "GB/s",
+                    "peak": hbm, "frac": round(gbs / hbm, 4), "peak_source": kind,
+                    "l2": f"{len(ops)} weight copies rotated (> 2x L2)"})
+        for bid in bufs:
+            dev.free(bid)
+    return out
+
+
+def gemm_cases(dev: Device, timer: Timer, iters: int):
+    lib = dev.lib
+    if not hasattr(lib, "sm100_gemm_bf16"):
+        return []
+    _, tflops, kind = peaks()
+    rng = np.random.default_rng(1)
+    out = []
+    for (M, N, K) in ((4096, 4096, 4096), (8192, 4096, 4096)):
+        ha = bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+        hb = bf16_bits(rng.standard_normal((N, K)).astype(np.float32))
+        c = dev.alloc(M * N * 4)
+        sets = [(dev.upload(ha), dev.upload(hb)) for _ in range(copies_for(ha.nbytes + hb.nbytes))]
+        pc = dev.dptr(c)
+
+        def mk(a, b):
+            pa, pb = dev.dptr(a), dev.dptr(b)
+            return lambda: L.check(lib.sm100_gemm_bf16(pa, pb, pc, M, N, K, dev.stream), "gemm_bf16")
+        ms = timer.time([mk(a, b) for a, b in sets], iters)
+        tf = 2.0 * M * N * K / (ms / 1e3) / 1e12
+        out.append({"case": "gemm_bf16", "M": M, "N": N, "K": K, "kernel": "gemm_bf16_kernel",
+                    "us": round(ms * 1e3, 2), "flops": 2 * M * N * K, "achieved": round(tf, 1),
+                    "unit": "TFLOP/s", "peak": tflops, "frac": round(tf / tflops, 4), "peak_source": kind})
+        for a, b in sets:
+            dev.free(a)
+            dev.free(b)
+        dev.free(c)
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--only", choices=["matvec", "gemm"], default=None)
+    args = ap.parse_args()
+    dev = Device.get()
+    timer = Timer(dev)
+    rows = []
+    if args.only in (None, "matvec"):
+        rows += matvec_cases(dev, timer, args.iters)
+    if args.only in (None, "gemm"):
+        rows += gemm_cases(dev, timer, args.iters)
+    for r in rows:
+        print(json.dumps(r), flush=True)
+
+
+if __name__ == "__main__":
+    main()
