@@ -281,51 +281,58 @@ __global__ void __launch_bounds__(128) gemv_kernel(LinParams p) {
 
 // Decode matvec streamed through shared memory (M = 1): one CTA per SM owns a
 // contiguous slice of rows; one producer thread keeps every stage of a ring
-// of 8-row stages in flight with TMA bulk copies (L2 evict_first: the
-// weights are read once); 16 consumer warps take (row, half of K) each per
-// stage, dot it with x (staged once per CTA in shared memory), reduce across
-// the warp, and after one barrier eight threads add the halves and run the
-// epilogue.  Streaming with up to ~190 KB in flight per SM is what reaches
-// HBM read bandwidth (loads issued per thread stall between short CTAs), and
-// 16 warps hide the fp8 widening and shared-memory latency.
-constexpr int kGvRows = 8;                        // rows per stage
-constexpr int kGvWarps = 2 * kGvRows;             // consumer warps: (row, K half)
+// of (16 / KS)-row stages in flight with TMA bulk copies (L2 evict_first:
+// the weights are read once); 16 consumer warps take (row, K slice) each per
+// stage, KS slices per row.  A lane always reads the same 16-byte columns of
+// its slice (vectors lane, lane + 32, ...), so its NJ slices of x are loaded
+// into registers once per launch: shared memory only carries the weights
+// (lane-contiguous reads, no bank conflicts).  No CTA barrier per stage:
+// each warp leaves its slice's partial in shared memory and the last of a
+// row's KS warps (a shared-memory counter) adds the slices in order and runs
+// the epilogue; every warp releases the stage itself (an mbarrier of 16
+// arrivals).
+// Streaming with ~190 KB in flight per SM is what reaches HBM read bandwidth
+// (loads issued per thread stall between short-lived CTAs).
+constexpr int kGvWarps = 16;                      // consumer warps
+constexpr int kGvRows = 32;                       // most rows per stage (KS = 1, 2 rows per warp)
 constexpr int kGvThreads = (kGvWarps + 1) * 32;   // + producer warp
-constexpr int kGvSmem = 200 * 1024;               // ring + x + scales + partials + barriers
+constexpr int kGvSmem = 200 * 1024;               // ring + scales + partials + barriers
 constexpr int kGvMaxStages = 8;
 
-template <typename WT>
+template <typename WT, int NJ, int KS, int RW>
 __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, int stages, int stage_floats) {
+  constexpr int R = kGvWarps / KS * RW;   // rows per stage (RW rows per warp)
   extern __shared__ __align__(1024) unsigned char smem[];
   constexpr int V = WVec<WT>::n;
   const int64_t K = p.K;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r0 = (p.N * blockIdx.x) / gridDim.x, r1 = (p.N * (blockIdx.x + 1)) / gridDim.x;
-  const int nchunks = (int)((r1 - r0 + kGvRows - 1) / kGvRows);
+  const int nchunks = (int)((r1 - r0 + R - 1) / R);
   float *ring = reinterpret_cast<float *>(smem);
-  float *xs = ring + (size_t)stages * stage_floats;                          // [K]
-  float *ss = xs + K;                                                         // [2][scale_cols]: this CTA's scale rows
-  float *part = ss + 2 * (size_t)p.scale_cols;                                // [2][kGvRows]
-  uint64_t *full = reinterpret_cast<uint64_t *>(part + 2 * kGvRows);          // [stages]
+  float *ss = ring + (size_t)stages * stage_floats;                          // [2][scale_cols]: this CTA's scale rows
+  float *part = ss + 2 * (size_t)p.scale_cols;                                // [stages][KS][R] partials
+  int *cnt = reinterpret_cast<int *>(part + (size_t)kGvMaxStages * 2 * kGvWarps);  // [stages][R] slices done
+  uint64_t *full = reinterpret_cast<uint64_t *>(cnt + (size_t)kGvMaxStages * kGvRows);   // [stages]
   uint64_t *empty = full + kGvMaxStages;                                      // [stages]
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kGvWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  for (int i = threadIdx.x; i < kGvMaxStages * kGvRows; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
   const size_t row_bytes = (size_t)K * sizeof(WT);
   if (warp == kGvWarps) {
-    // producer: chunk c -> stage c % stages, rows [r0 + 8c, ...)
+    // producer: chunk c -> stage c % stages, rows [r0 + R c, ...)
     if (lane == 0) {
       const uint64_t pol = policy_evict_first();
       const unsigned char *w = static_cast<const unsigned char *>(p.w);
       for (int c = 0; c < nchunks; c++) {
         const int s = c % stages;
         if (c >= stages && !mbar_wait(&empty[s], (uint32_t)(((c / stages) - 1) & 1), nullptr)) break;
-        const int64_t rr = r0 + (int64_t)c * kGvRows, nr = (r1 - rr) < kGvRows ? (r1 - rr) : kGvRows;
+        const int64_t rr = r0 + (int64_t)c * R, nr = (r1 - rr) < R ? (r1 - rr) : R;
         const uint32_t bytes = (uint32_t)(nr * row_bytes);
         mbar_expect_tx(&full[s], bytes);
         bulk_g2s_hint(ring + (size_t)s * stage_floats, w + rr * row_bytes, bytes, &full[s], pol);
@@ -336,73 +343,150 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
     }
     return;
   }
-  // consumers: x (and the fp8 block scales of this CTA's rows) into shared memory
+  // consumers: this lane's x columns into registers, the fp8 block scales of
+  // this CTA's rows into shared memory
   const int ct = threadIdx.x, nct = kGvWarps * 32;
-  for (int64_t i = ct; i < K / 4; i += nct)
-    reinterpret_cast<float4 *>(xs)[i] = __ldg(reinterpret_cast<const float4 *>(p.x) + i);
+  constexpr int WPS = kGvWarps / KS;          // warps per K slice; warp (ks, rw) has rows rw * RW + i
+  const int ks = warp / WPS, rw = warp % WPS;
+  const int vbase = ks * NJ * 32 + lane;   // vector j of this lane: vbase + 32 j
+  float xr[NJ * V];
+#pragma unroll
+  for (int j = 0; j < NJ; j++) {
+    const float4 *src = reinterpret_cast<const float4 *>(p.x + (int64_t)(vbase + 32 * j) * V);
+#pragma unroll
+    for (int q = 0; q < V / 4; q++) {
+      const float4 f = __ldg(src + q);
+      xr[j * V + 4 * q] = f.x;
+      xr[j * V + 4 * q + 1] = f.y;
+      xr[j * V + 4 * q + 2] = f.z;
+      xr[j * V + 4 * q + 3] = f.w;
+    }
+  }
   if constexpr (sizeof(WT) == 1) {
     const int64_t sr0 = r0 >> 7;
     for (int i = ct; i < 2 * p.scale_cols; i += nct) {
       const int64_t sr = sr0 + i / p.scale_cols;
       ss[i] = (sr * 128 < p.N) ? p.w_scale[sr * p.scale_cols + i % p.scale_cols] : 0.0f;
     }
+    asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
   }
-  asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
-  const int nvec = (int)(K / V), half = warp / kGvRows, rw = warp % kGvRows;
-  const int v0 = half ? nvec / 2 : 0, v1 = half ? nvec : nvec / 2;
   for (int c = 0; c < nchunks; c++) {
     const int s = c % stages;
     mbar_wait(&full[s], (uint32_t)((c / stages) & 1), nullptr);
-    const int64_t n = r0 + (int64_t)c * kGvRows + rw;
-    if (n < r1) {
-      const unsigned char *wrow = reinterpret_cast<const unsigned char *>(ring + (size_t)s * stage_floats) +
-                                  (size_t)rw * row_bytes;
-      const float *srow = ss + ((n >> 7) - (r0 >> 7)) * p.scale_cols;
-      float acc[1] = {0.0f};
-      for (int v = v0 + lane; v < v1; v += 32) {
-        const uint4 wv = *reinterpret_cast<const uint4 *>(wrow + (size_t)v * 16);
-        const int64_t k0 = (int64_t)v * V;
-        dot_vec<WT, 1>(wv, xs + k0, K, acc, (sizeof(WT) == 1) ? srow[k0 >> 7] : 1.0f);
+    const int64_t nb = r0 + (int64_t)c * R + (int64_t)rw * RW;   // this warp's first row
+    if (nb < r1) {
+      const uint4 *wrow = reinterpret_cast<const uint4 *>(reinterpret_cast<const unsigned char *>(
+                              ring + (size_t)s * stage_floats) + (size_t)rw * RW * row_bytes);
+      float acc[RW];
+#pragma unroll
+      for (int i = 0; i < RW; i++) acc[i] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < NJ; j++) {
+        const int v = vbase + 32 * j;
+#pragma unroll
+        for (int i = 0; i < RW; i++) {
+          if (nb + i < r1) {
+            const float sc = (sizeof(WT) == 1) ? ss[(((nb + i) >> 7) - (r0 >> 7)) * p.scale_cols + ((v * V) >> 7)] : 1.0f;
+            float a1[1] = {acc[i]};
+            dot_vec<WT, 1>(wrow[(size_t)i * (row_bytes / 16) + v], xr + j * V, K, a1, sc);
+            acc[i] = a1[0];
+          }
+        }
       }
-      const float a = warp_sum(acc[0]);
-      if (lane == 0) part[half * kGvRows + rw] = a;
+#pragma unroll
+      for (int i = 0; i < RW; i++) acc[i] = warp_sum(acc[i]);
+      if (lane == 0) {
+        float *ps = part + (size_t)s * 2 * kGvWarps;
+#pragma unroll
+        for (int i = 0; i < RW; i++) {
+          const int64_t n = nb + i;
+          const int slot = rw * RW + i;
+          if (n >= r1) break;
+          if (KS == 1) {
+            epilogue_store(p, 0, n, acc[i]);
+          } else {
+            ps[ks * R + slot] = acc[i];
+            __threadfence_block();
+            if (atomicAdd(&cnt[s * kGvRows + slot], 1) == KS - 1) {   // the row's last slice: add them in order
+              __threadfence_block();
+              float t2 = 0.0f;
+#pragma unroll
+              for (int k2 = 0; k2 < KS; k2++) t2 += *(volatile float *)&ps[k2 * R + slot];
+              cnt[s * kGvRows + slot] = 0;
+              epilogue_store(p, 0, n, t2);
+            }
+          }
+        }
+      }
     }
-    // the stage is read: the producer may refill it
-    asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
-    if (ct == 0) mbar_arrive(&empty[s]);
-    if (ct < kGvRows) {
-      const int64_t n2 = r0 + (int64_t)c * kGvRows + ct;
-      if (n2 < r1) epilogue_store(p, 0, n2, part[ct] + part[kGvRows + ct]);
-    }
-    // part[] is rewritten next chunk only after every warp passed this point
-    asm volatile("bar.sync 1, %0;" ::"n"(kGvWarps * 32) : "memory");
+    // this warp is done with the stage: the producer may refill it after all 16
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
 }
 
-// Stages of the streamed matvec for this shape, or 0 when it does not fit.
+// Stages of the streamed matvec for this shape (0: it does not fit), KS
+// (K slices per row: the fewest that keep x within 32 registers a lane) and
+// NJ, the 16-byte vectors per lane of a slice (K = KS * 32 * NJ * V).
 template <typename WT>
-static int gemv_tma_stages(const LinParams &p, int &stage_floats) {
-  const size_t stage = (size_t)kGvRows * (size_t)p.K * sizeof(WT);
-  const size_t fixed = (size_t)p.K * 4 + 2 * (size_t)p.scale_cols * 4 + 2 * kGvRows * 4 + 2 * kGvMaxStages * 8 + 64;
-  if (p.K % WVec<WT>::n || stage % 16 || fixed + 2 * stage > (size_t)kGvSmem) return 0;
+static int gemv_tma_stages(const LinParams &p, int &stage_floats, int &nj, int &ks, int rw) {
+  constexpr int V = WVec<WT>::n;
+  nj = 0;
+  for (ks = 1; ks <= 4; ks *= 2) {
+    if (p.K % ((int64_t)ks * 32 * V)) continue;
+    const int64_t n = p.K / ((int64_t)ks * 32 * V);
+    if (n * V <= 32 && (n == 1 || n == 2 || n == 3 || n == 4 || n == 6 || n == 8)) {
+      nj = (int)n;
+      break;
+    }
+  }
+  if (!nj) return 0;
+  const size_t stage = (size_t)(kGvWarps / ks * rw) * (size_t)p.K * sizeof(WT);
+  const size_t fixed = 2 * (size_t)p.scale_cols * 4 + (size_t)kGvMaxStages * (2 * kGvWarps + kGvRows) * 4 +
+                       2 * kGvMaxStages * 8 + 64;
+  if (stage % 16 || fixed + 2 * stage > (size_t)kGvSmem) return 0;
   stage_floats = (int)(stage / 4);
   const size_t s = (kGvSmem - fixed) / stage;
   return (int)(s < (size_t)kGvMaxStages ? s : (size_t)kGvMaxStages);
 }
 
-template <typename WT>
-static int launch_gemv_tma(const LinParams &p, int stages, int stage_floats, cudaStream_t st) {
+template <typename WT, int NJ, int KS>
+static int launch_gemv_tma_nj(const LinParams &p, int stages, int stage_floats, cudaStream_t st) {
+  constexpr int RW = sizeof(WT) == 1 ? 2 : 1;   // fp8 rows are short: two per warp per stage
+  constexpr int R = kGvWarps / KS * RW;
   static int num_sms[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "gemv: device %d", dev);
   if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int64_t rows_per = (p.N + num_sms[dev] - 1) / num_sms[dev];
-  const int grid = rows_per < kGvRows ? (int)((p.N + kGvRows - 1) / kGvRows) : num_sms[dev];
-  cudaError_t e = cudaFuncSetAttribute(gemv_tma_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem);
+  const int grid = rows_per < R ? (int)((p.N + R - 1) / R) : num_sms[dev];
+  cudaError_t e =
+      cudaFuncSetAttribute(gemv_tma_kernel<WT, NJ, KS, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-  gemv_tma_kernel<WT><<<grid, kGvThreads, kGvSmem, st>>>(p, stages, stage_floats);
+  gemv_tma_kernel<WT, NJ, KS, RW><<<grid, kGvThreads, kGvSmem, st>>>(p, stages, stage_floats);
   return launch_status("gemv_tma");
+}
+
+template <typename WT, int KS>
+static int launch_gemv_tma_ks(const LinParams &p, int stages, int stage_floats, int nj, cudaStream_t st) {
+  switch (nj) {
+    case 1: return launch_gemv_tma_nj<WT, 1, KS>(p, stages, stage_floats, st);
+    case 2: return launch_gemv_tma_nj<WT, 2, KS>(p, stages, stage_floats, st);
+    case 3: return launch_gemv_tma_nj<WT, 3, KS>(p, stages, stage_floats, st);
+    case 4: return launch_gemv_tma_nj<WT, 4, KS>(p, stages, stage_floats, st);
+    case 6: return launch_gemv_tma_nj<WT, 6, KS>(p, stages, stage_floats, st);
+    default: return launch_gemv_tma_nj<WT, 8, KS>(p, stages, stage_floats, st);
+  }
+}
+
+template <typename WT>
+static int launch_gemv_tma(const LinParams &p, int stages, int stage_floats, int nj, int ks, cudaStream_t st) {
+  switch (ks) {
+    case 1: return launch_gemv_tma_ks<WT, 1>(p, stages, stage_floats, nj, st);
+    case 2: return launch_gemv_tma_ks<WT, 2>(p, stages, stage_floats, nj, st);
+    default: return launch_gemv_tma_ks<WT, 4>(p, stages, stage_floats, nj, st);
+  }
 }
 
 // NV = K / (V * 32) vectors per lane when it is one of the instantiated
@@ -470,9 +554,9 @@ static int launch_w(const LinParams &p, cudaStream_t st) {
   // decode matvec fast path: one row, no LayerNorm, aligned x / W, K a
   // multiple of 32 vectors with an instantiated count
   if (p.M == 1 && vec && !(p.flags & SM100_LIN_LN) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0)) {
-    int stage_floats = 0;
-    const int stages = gemv_tma_stages<WT>(p, stage_floats);
-    if (stages >= 2 && p.N >= 1024) return launch_gemv_tma<WT>(p, stages, stage_floats, st);
+    int stage_floats = 0, nj = 0, ks = 1;
+    const int stages = gemv_tma_stages<WT>(p, stage_floats, nj, ks, sizeof(WT) == 1 ? 2 : 1);
+    if (stages >= 2 && p.N >= 1024) return launch_gemv_tma<WT>(p, stages, stage_floats, nj, ks, st);
     const int nv = p.K * sizeof(float) <= 200 * 1024 ? gemv_nv<WT>(p) : 0;
     if (nv) return launch_gemv<WT>(p, nv, st);
   }
