@@ -130,6 +130,46 @@ __device__ __forceinline__ void wait_words(const uint64_t *p, int stride, int n,
   for (int i = 0; i < N; i++) out[i] = (i < n && !((pending >> i) & 1u)) ? __uint_as_float((uint32_t)w[i]) : 0.0f;
 }
 
+// Pairs of tagged words (2 i, 2 i + 1) at p[0], p[stride], ... with one
+// 16-byte load each (half the polling requests of single words); a pair is
+// in when both tags are.  Bounded like wait_words.
+__device__ __forceinline__ void ld_pair(const uint64_t *p, uint64_t &a, uint64_t &b) {
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void wait_pairs(const uint64_t *p, int stride, int n, uint32_t tag, uint32_t *status,
+                                           float2 (&out)[N]) {
+  uint64_t w0[N], w1[N];
+  uint32_t pending = 0;
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    if (i < n) ld_pair(p + (size_t)i * stride, w0[i], w1[i]);
+    else w0[i] = w1[i] = (uint64_t)tag << 32;
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++)
+    if ((uint32_t)(w0[i] >> 32) != tag || (uint32_t)(w1[i] >> 32) != tag) pending |= 1u << i;
+  for (uint32_t it = 0; pending; it++) {
+    if (it >= (1u << 22) || ((it & 15u) == 15u && *(volatile uint32_t *)status)) {
+      if (it >= (1u << 22)) atomicOr(status, SM100_DECODE_ERR_BARRIER);
+      break;
+    }
+#pragma unroll
+    for (int i = 0; i < N; i++)
+      if ((pending >> i) & 1u) ld_pair(p + (size_t)i * stride, w0[i], w1[i]);
+#pragma unroll
+    for (int i = 0; i < N; i++)
+      if (((pending >> i) & 1u) && (uint32_t)(w0[i] >> 32) == tag && (uint32_t)(w1[i] >> 32) == tag)
+        pending &= ~(1u << i);
+  }
+#pragma unroll
+  for (int i = 0; i < N; i++) {
+    const bool ok = i < n && !((pending >> i) & 1u);
+    out[i] = make_float2(ok ? __uint_as_float((uint32_t)w0[i]) : 0.0f, ok ? __uint_as_float((uint32_t)w1[i]) : 0.0f);
+  }
+}
+
 __device__ __forceinline__ uint64_t gtimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -584,7 +624,7 @@ __device__ __forceinline__ void projection_role(const Sm100DecodeModel &m, const
   const float *wte = m.wte, *wpe = m.wpe;
   float *logits = m.logits;
   uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * n_phases * kTraceSlots : nullptr;
-  constexpr int KPT = (kXsFloats + kThreads - 1) / kThreads;
+  constexpr int PPT = (kXsFloats / 2 + kThreads - 1) / kThreads;   // input word pairs per thread
 
   int q = 0, qi = 0, sidx = 0;   // next transfer (global, within the token), staged-input parity
   int tok = m.io[1];
@@ -614,12 +654,14 @@ __device__ __forceinline__ void projection_role(const Sm100DecodeModel &m, const
         if (t < s1 - s0)
           xown[t] = __fadd_rn(tok_ok ? wte[(size_t)tok * K + s0 + t] : 0.0f, wpe[(size_t)pos * K + s0 + t]);
       } else {
-        float xv[KPT];
-        const int live = t < K ? (K - 1 - t) / kThreads + 1 : 0;
-        wait_words<KPT>(st.src + t, kThreads, live, tag - 1, status, xv);
+        // word pairs (2 j, 2 j + 1), j = t, t + kThreads, ...: one 16-byte poll each
+        float2 xv[PPT];
+        const int KP = K / 2;
+        const int live = t < KP ? (KP - 1 - t) / kThreads + 1 : 0;
+        wait_pairs<PPT>(st.src + 2 * t, 2 * kThreads, live, tag - 1, status, xv);
 #pragma unroll
-        for (int i = 0; i < KPT; i++)
-          if (i < live) xb[t + i * kThreads] = xv[i];
+        for (int i = 0; i < PPT; i++)
+          if (i < live) reinterpret_cast<float2 *>(xb)[t + i * kThreads] = xv[i];
       }
       csync();
       if (trace) tr[p * kTraceSlots + 1] = gtimer();
