@@ -130,7 +130,8 @@ enum {
   SM100_K_SCATTER,      /* dst[idx[i]] = src[i] rows, idx outside [0, V) skipped */
   SM100_K_KV_APPEND,    /* cache[:, pos:pos+T] = stack(k, v) at a device position */
   SM100_K_POS_ADD,      /* device int32 counter += value (the kvar bump) */
-  SM100_K_DECODE_STEP   /* the fused GPT-2 decode step (sm100_decode_step) */
+  SM100_K_DECODE_STEP,  /* the fused GPT-2 decode step (sm100_decode_step) */
+  SM100_K_ATTN_PREFILL  /* causal softmax(q k^T scale) v, bf16 q/k/v (sm100_attn_prefill_bf16) */
 };
 
 /* Linear flags */
@@ -179,6 +180,9 @@ typedef struct {
  *  DECODE_STEP in[0]=an Sm100DecodeModel in device memory; m = n_layers,
  *             k = dim, heads, ld_out = vocab (lm_head rows), max_ctx,
  *             n = tokens (0 means 1); out = the model's io buffer
+ *  ATTN_PREFILL in[0]=q in[1]=k in[2]=v, bf16 [m=B, heads, n=S, k=head_dim];
+ *             out = f32 [B, heads, S, head_dim]; causal must be 1; scale;
+ *             flags bit 0 = single bf16 P (fast; default is the hi+lo split)
  */
 int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *in_buf_ids, uint32_t n_in,
                           uint32_t out_buf_id);
@@ -340,6 +344,22 @@ int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N
 /* non-zero when a GEMM launch since the last call gave up a bounded wait;
  * synchronises the device and clears the word */
 uint32_t sm100_gemm_status(void);
+
+/* ---- causal attention prefill on the tensor cores ------------------------ */
+/* O[B, H, S, D] (f32) = softmax(Q K^T * scale + causal mask) V for bf16 Q, K, V
+ * [B, H, S, D] contiguous, D = 128, any S >= 0: the reference's
+ * nn_scaled_dot_product_attention with causal = 1 (src/nn/
+ * scaled_dot_product_attention.c:1-34, reached from Tensor.
+ * scaled_dot_product_attention(is_causal=True), py/thvm/tensor.py:1726-1749),
+ * fused flash style (QK^T and PV on tcgen05 into TMEM, online softmax between).
+ * precise_p = 1 feeds P to the PV product as bf16 hi + bf16 lo (two MMAs,
+ * ~16-bit P: ~2e-6 relative to an f32 softmax, row argmax stable); 0 feeds a
+ * single bf16 P (~2e-3 relative).  Device pointers, 16-byte aligned. */
+int sm100_attn_prefill_bf16(const void *q, const void *k, const void *v, float *o, int32_t B, int32_t H,
+                            int32_t S, int32_t D, float scale, int32_t precise_p, void *stream);
+/* non-zero when a prefill launch since the last call gave up a bounded wait;
+ * synchronises the device and clears the word */
+uint32_t sm100_attn_prefill_status(void);
 
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into

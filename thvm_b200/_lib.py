@@ -18,7 +18,7 @@ ERR_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_OOM, ERR_STATE, ERR_TIMEOUT = -1, -2, -3
 DT_F32, DT_BF16, DT_FP8E4M3, DT_I32 = 0, 1, 2, 3
 
 (K_LINEAR, K_LAYERNORM, K_RMSNORM, K_SOFTMAX, K_GELU, K_ADD, K_ATTENTION, K_EMBEDDING, K_ARGMAX,
- K_SCATTER, K_KV_APPEND, K_POS_ADD, K_DECODE_STEP) = range(1, 14)
+ K_SCATTER, K_KV_APPEND, K_POS_ADD, K_DECODE_STEP, K_ATTN_PREFILL) = range(1, 15)
 
 DECODE_MAX_LAYERS = 48
 DECODE_REPLICAS = 8
@@ -139,6 +139,9 @@ SIGNATURES = {
     "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     "sm100_gemm_status": (c_uint32, []),
+    "sm100_attn_prefill_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                        c_float, c_int32, c_void_p]),
+    "sm100_attn_prefill_status": (c_uint32, []),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),

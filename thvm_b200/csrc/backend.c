@@ -541,6 +541,13 @@ int sm100_dispatch_kernel(const Sm100Kernel *k, const uint32_t *ids, uint32_t n_
       if (!p[0]) return sm100_set_error(SM100_ERR_ARG, "decode_step: no model descriptor");
       return sm100_decode_steps((const Sm100DecodeModel *)p[0], k->n > 0 ? (int32_t)k->n : 1, (int32_t)k->m,
                                 (int32_t)k->k, k->heads, (int32_t)k->ld_out, k->max_ctx, st);
+    case SM100_K_ATTN_PREFILL:
+      if (k->causal != 1) return sm100_set_error(SM100_ERR_UNSUPPORTED, "attn_prefill: causal only");
+      if (k->dtype != SM100_DT_BF16) return sm100_set_error(SM100_ERR_UNSUPPORTED, "attn_prefill: bf16 q/k/v only");
+      if (k->m > INT32_MAX || k->n > INT32_MAX || k->k > INT32_MAX)
+        return sm100_set_error(SM100_ERR_ARG, "attn_prefill: shape out of range");
+      return sm100_attn_prefill_bf16(p[0], p[1], p[2], (float *)out, (int32_t)k->m, k->heads, (int32_t)k->n,
+                                     (int32_t)k->k, k->scale, (k->flags & 1u) ? 0 : 1, st);
     default:
       return sm100_set_error(SM100_ERR_UNSUPPORTED, "dispatch_kernel: kind %u", k->kind);
   }

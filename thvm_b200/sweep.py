@@ -1,12 +1,16 @@
 """The standalone contraction sweep on the sm_100a device.
 
-    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm]
+    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm|prefill]
 
 Seeded N(0,1) inputs, fp32 accumulate:
   * decode matvec x[1, 4096] against W (11008 x 4096) in bf16, and in fp8 e4m3
     with one f32 scale per 128 x 128 block (scales uniform in [0.5, 2]);
   * bf16 GEMM C[M, N] = A[M, K] B[N, K]^T at M=N=K=4096 and M=8192, N=K=4096
-    (when the tcgen05 GEMM is built into the library).
+    (when the tcgen05 GEMM is built into the library);
+  * causal attention prefill: bf16 Q, K, V [4, 16, 2048,
+    128] N(0,1), f32 O, with P split into bf16 hi + lo (the parity setting)
+    and as a single bf16 P; FLOPs counted as 2 B H S^2 D (the causal half of
+    the two S x S x D products).
 The launches of a case are captured into one CUDA graph and replayed between
 one pair of CUDA events on the library's stream, rotating over operand copies
 that together exceed twice L2 (every launch reads cold operands); one JSON
@@ -152,10 +156,41 @@ def gemm_cases(dev: Device, timer: Timer, iters: int):
     return out
 
 
+def prefill_cases(dev: Device, timer: Timer, iters: int):
+    lib = dev.lib
+    _, tflops, kind = peaks()
+    rng = np.random.default_rng(4)
+    B, H, S, D = 4, 16, 2048, 128
+    host = [bf16_bits(rng.standard_normal((B, H, S, D)).astype(np.float32)) for _ in range(3)]
+    o = dev.alloc(B * H * S * D * 4)
+    po = dev.dptr(o)
+    sets = [[dev.upload(h) for h in host] for _ in range(copies_for(sum(h.nbytes for h in host)))]
+    out = []
+    for precise in (1, 0):
+        def mk(ids):
+            pq, pk, pv = (dev.dptr(i) for i in ids)
+            return lambda: L.check(lib.sm100_attn_prefill_bf16(pq, pk, pv, po, B, H, S, D, 1.0 / np.sqrt(D),
+                                                               precise, dev.stream), "attn_prefill")
+        ms = timer.time([mk(ids) for ids in sets], iters)
+        assert lib.sm100_attn_prefill_status() == 0
+        flops = 2 * B * H * S * S * D
+        tf = flops / (ms / 1e3) / 1e12
+        out.append({"case": "attn_prefill_causal", "B": B, "H": H, "S": S, "D": D,
+                    "p": "bf16 hi+lo" if precise else "bf16", "kernel": "attn_prefill_kernel",
+                    "us": round(ms * 1e3, 2), "flops": flops, "achieved": round(tf, 1), "unit": "TFLOP/s",
+                    "peak": tflops, "frac": round(tf / tflops, 4), "peak_source": kind,
+                    "l2": f"{len(sets)} q/k/v copies rotated"})
+    for ids in sets:
+        for i in ids:
+            dev.free(i)
+    dev.free(o)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", choices=["matvec", "gemm"], default=None)
+    ap.add_argument("--only", choices=["matvec", "gemm", "prefill"], default=None)
     args = ap.parse_args()
     dev = Device.get()
     timer = Timer(dev)
@@ -164,6 +199,8 @@ def main():
         rows += matvec_cases(dev, timer, args.iters)
     if args.only in (None, "gemm"):
         rows += gemm_cases(dev, timer, args.iters)
+    if args.only in (None, "prefill"):
+        rows += prefill_cases(dev, timer, args.iters)
     for r in rows:
         print(json.dumps(r), flush=True)
 
