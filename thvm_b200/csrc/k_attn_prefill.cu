@@ -6,20 +6,25 @@
 // 1-16: max, x - max, exp, sum, times the reciprocal), then p v.  Here they are
 // fused flash style, so the S x S scores never leave the SM.
 //
-// One CTA per (b*h, 128-query block), heaviest query blocks first:
-//   warp 0    TMA: Q once, then K_j and V_j (128 keys each) into a 2-stage
-//             ring (3-D tensor maps [BH, S, D]: rows past S read as zeros);
-//   warp 1    MMA: S_j = Q K_j^T (tcgen05.mma kind::f16, M = N = 128, both
-//             operands K-major, 128-byte swizzle) into one of two TMEM score
-//             buffers, and O += P_j V_j (P K-major from shared memory, V
-//             MN-major) into a TMEM accumulator; QK of block j+1 is issued
-//             before PV of block j, so the scores of the next block are ready
-//             when the softmax of this one ends;
-//   warps 2-5 softmax, one query row per thread (TMEM lane): the score row by
-//             tcgen05.ld, causal mask on the diagonal block, online max and
-//             sum, P = exp2((s - max) * log2(e) / sqrt(D)), the O rescale in
-//             TMEM when a row maximum grew, P into shared memory in the MMA's
-//             swizzled layout; at the end O / sum.
+// One CTA per (b*h, pair of 128-query blocks 2t and 2t+1), heaviest pairs
+// first.  The two query tiles A and B share one stream of K / V blocks and
+// take turns on the tensor cores, so the softmax of one tile runs while the
+// products of the other do:
+//   warp 0    TMA: Q_A and Q_B once, then K_j and V_j (128 keys each) into
+//             2-stage K and V rings (3-D tensor maps [BH, S, D]: rows past S
+//             read as zeros); a K slot is refilled once its scores are done;
+//   warp 1    MMA: S_X = Q_X K_j^T (tcgen05.mma kind::f16, M = N = 128, both
+//             operands K-major in 128-byte-swizzled shared memory) into TMEM,
+//             and O_X += P_X V_j with P_X read from TMEM where the softmax
+//             wrote it over S_X, V MN-major from shared memory; per block:
+//             P_A V, Q_A K_next, P_B V, Q_B K_next;
+//   warps 2-5 / 6-9  softmax of tile A / B, one query row per thread (TMEM
+//             lane): the score row by tcgen05.ld, causal mask on the diagonal
+//             block, row max, P = exp2((s - m) * log2(e) * scale) written back
+//             as bf16 pairs by tcgen05.st, the row sum; the running max m is
+//             only raised (and O, sum rescaled) when a score exceeds it by
+//             8 / (log2(e) * scale), so P <= 2^8 and rescales are rare; at the
+//             end O / sum.
 // kSplit: P is passed to the tensor cores as bf16 hi + bf16 lo (lo = P -
 // hi), two MMAs per key step, so P carries ~16 bits instead of 8: the output
 // then agrees with an f32 softmax to ~2e-6 relative and its row-wise argmax
@@ -35,12 +40,8 @@ namespace sm100 {
 constexpr int kApD = 128, kApBM = 128, kApBN = 128;
 constexpr int kApTile = kApBM * kApD * 2;   // 32 KB: one [128 x 128] bf16 tile as two 64-column swizzle halves
 constexpr int kApHalf = kApTile / 2;        // 16 KB
-constexpr int kApThreads = 6 * 32;
-
-template <bool kSplit>
-constexpr int ap_smem() {
-  return (kSplit ? 7 : 6) * kApTile + 1024 + 256;
-}
+constexpr int kApThreads = 10 * 32;
+constexpr int kApSmem = 6 * kApTile + 1024 + 256;   // Q_A, Q_B, K ring, V ring; alignment slack; barriers
 
 __device__ uint32_t g_attn_status;
 
@@ -80,6 +81,15 @@ __device__ __forceinline__ void ap_mma(uint32_t tmem_d, uint64_t da, uint64_t db
       : "memory");
 }
 
+// The same with A read from TMEM (lane = row of A, bf16 pairs along columns).
+__device__ __forceinline__ void ap_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
 __device__ __forceinline__ void ap_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -110,6 +120,41 @@ __device__ __forceinline__ void ap_st32(uint32_t taddr, const uint32_t (&r)[32])
       : "memory");
 }
 
+__device__ __forceinline__ void ap_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void ap_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+__device__ __forceinline__ void ap_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+               : "memory");
+}
+
+// Maximum of a 128-score row held as f32 bits, as a tree (short dependency chains).
+__device__ __forceinline__ float ap_max128(const uint32_t (&v)[4][32]) {
+  float a[32];
+#pragma unroll
+  for (int i = 0; i < 32; i++)
+    a[i] = fmaxf(fmaxf(__uint_as_float(v[0][i]), __uint_as_float(v[1][i])),
+                 fmaxf(__uint_as_float(v[2][i]), __uint_as_float(v[3][i])));
+#pragma unroll
+  for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; i++) a[i] = fmaxf(a[i], a[i + w]);
+  return a[0];
+}
+
 __device__ __forceinline__ void ap_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void ap_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void ap_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -134,37 +179,38 @@ __device__ __forceinline__ bool ap_wait_warp(uint64_t *bar, uint32_t parity, uin
 template <bool kSplit>
 __global__ void __launch_bounds__(kApThreads, 1)
     attn_prefill_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                        const __grid_constant__ CUtensorMap map_v, float *o, int BH, int S, float c_log2) {
+                        const __grid_constant__ CUtensorMap map_v, float *o, int BH, int S, float c_log2, float tau) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  constexpr int kTiles = kSplit ? 7 : 6;
-  unsigned char *sq = smem;                 // Q
-  unsigned char *skv = smem + kApTile;      // K0, V0, K1, V1
-  unsigned char *sp = smem + 5 * kApTile;   // P (hi), then P lo when split
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kTiles * kApTile);
-  uint64_t *q_full = bars, *kv_full = bars + 1, *kv_empty = bars + 3, *s_full = bars + 5, *s_empty = bars + 7;
-  uint64_t *p_full = bars + 9, *pv_done = bars + 10, *mma_done = bars + 11;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+  unsigned char *sq = smem;                 // Q_A, Q_B
+  unsigned char *sk = smem + 2 * kApTile;   // K ring (2)
+  unsigned char *sv = smem + 4 * kApTile;   // V ring (2)
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 6 * kApTile);
+  uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
+  uint64_t *s_full = bars + 9, *p_full = bars + 11, *mma_done = bars + 13;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nqb = (S + kApBM - 1) / kApBM;
-  const int qb = nqb - 1 - (int)(blockIdx.x / BH), bh = (int)(blockIdx.x % BH);   // heaviest first
-  const int nb = qb + 1;                                                           // causal key blocks
+  const int nqb = (S + kApBM - 1) / kApBM, npairs = (nqb + 1) >> 1;
+  const int t = npairs - 1 - (int)(blockIdx.x / BH), bh = (int)(blockIdx.x % BH);   // heaviest pairs first
+  const int qbA = 2 * t, qbB = 2 * t + 1;
+  const int nA = qbA + 1, nB = qbB < nqb ? qbB + 1 : 0;   // causal key blocks of each tile (B may lie past S)
+  const int nK = nB > nA ? nB : nA;
   uint32_t *status = &g_attn_status;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; i++) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 4);
+      mbar_init(&p_full[i], 4);
     }
-    mbar_init(p_full, 4);
-    mbar_init(pv_done, 1);
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {   // TMEM: S0 columns [0, 128), S1 [128, 256), O [256, 384)
+  if (warp == 1) {   // TMEM columns: S_A / P_A [0, 128), S_B / P_B [128, 256), O_A [256, 384), O_B [384, 512)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(512)
                  : "memory");
@@ -177,160 +223,178 @@ __global__ void __launch_bounds__(kApThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_expect_tx(q_full, kApTile);
-      ap_tma_3d(sq, &map_q, 0, qb * kApBM, bh, q_full);
-      ap_tma_3d(sq + kApHalf, &map_q, 64, qb * kApBM, bh, q_full);
-      int j = 0;
-      for (; j < nb; j++) {
+      mbar_expect_tx(q_full, (nB > 0 ? 2 : 1) * kApTile);
+      ap_tma_3d(sq, &map_q, 0, qbA * kApBM, bh, q_full);
+      ap_tma_3d(sq + kApHalf, &map_q, 64, qbA * kApBM, bh, q_full);
+      if (nB > 0) {
+        ap_tma_3d(sq + kApTile, &map_q, 0, qbB * kApBM, bh, q_full);
+        ap_tma_3d(sq + kApTile + kApHalf, &map_q, 64, qbB * kApBM, bh, q_full);
+      }
+      // K_j returns to its ring slot when both tiles' scores against it are
+      // done, V_j when both P V products are: K runs up to two blocks ahead of
+      // the scores, V two blocks ahead of P V
+      int nk = 0, nv = 0;
+      for (int j = 0; j < nK; j++) {
         const int s = j & 1;
-        if (j >= 2 && !mbar_wait(&kv_empty[s], (uint32_t)(((j >> 1) - 1) & 1), status)) break;
-        unsigned char *sk = skv + (size_t)s * 2 * kApTile, *sv = sk + kApTile;
-        mbar_expect_tx(&kv_full[s], 2 * kApTile);
+        const uint32_t ph = (uint32_t)(((j >> 1) - 1) & 1);
         const int y = j * kApBN;
-        ap_tma_3d(sk, &map_k, 0, y, bh, &kv_full[s]);
-        ap_tma_3d(sk + kApHalf, &map_k, 64, y, bh, &kv_full[s]);
-        ap_tma_3d(sv, &map_v, 0, y, bh, &kv_full[s]);
-        ap_tma_3d(sv + kApHalf, &map_v, 64, y, bh, &kv_full[s]);
+        if (j >= 2 && !mbar_wait(&k_empty[s], ph, status)) break;
+        mbar_expect_tx(&k_full[s], kApTile);
+        ap_tma_3d(sk + s * kApTile, &map_k, 0, y, bh, &k_full[s]);
+        ap_tma_3d(sk + s * kApTile + kApHalf, &map_k, 64, y, bh, &k_full[s]);
+        nk++;
+        if (j >= 2 && !mbar_wait(&v_empty[s], ph, status)) break;
+        mbar_expect_tx(&v_full[s], kApTile);
+        ap_tma_3d(sv + s * kApTile, &map_v, 0, y, bh, &v_full[s]);
+        ap_tma_3d(sv + s * kApTile + kApHalf, &map_v, 64, y, bh, &v_full[s]);
+        nv++;
       }
       // every issued copy has landed before the CTA may exit
       mbar_wait(q_full, 0, status, false);
-      for (int i = j - 2 > 0 ? j - 2 : 0; i < j; i++)
-        mbar_wait(&kv_full[i & 1], (uint32_t)((i >> 1) & 1), status, false);
+      for (int i = nk - 2 > 0 ? nk - 2 : 0; i < nk; i++)
+        mbar_wait(&k_full[i & 1], (uint32_t)((i >> 1) & 1), status, false);
+      for (int i = nv - 2 > 0 ? nv - 2 : 0; i < nv; i++)
+        mbar_wait(&v_full[i & 1], (uint32_t)((i >> 1) & 1), status, false);
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      bool ok = mbar_wait(q_full, 0, status);
-      ap_fence_after();
-      auto issue_qk = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (uint32_t)((j >> 1) & 1), status)) return false;
-        if (j >= 2 && !mbar_wait(&s_empty[s], (uint32_t)(((j >> 1) - 1) & 1), status)) return false;
-        ap_fence_after();
-        const unsigned char *sk = skv + (size_t)s * 2 * kApTile;
+      // S_X(j) = Q_X K_j^T into TMEM columns 128X; s_full[X] marks it (and,
+      // after a tile's last block, marks its final O)
+      auto qk = [&](int X, int j) {
+        const unsigned char *kt = sk + (j & 1) * kApTile, *qt = sq + X * kApTile;
 #pragma unroll
         for (int kk = 0; kk < kApD / 16; kk++) {
           const int h = kk >> 2, o16 = 2 * (kk & 3);   // 16 elements = 32 bytes = 2 descriptor units
-          ap_mma(tmem + (uint32_t)(s * kApBN), ap_desc_k(sq + h * kApHalf) + o16, ap_desc_k(sk + h * kApHalf) + o16,
+          ap_mma(tmem + (uint32_t)(X * 128), ap_desc_k(qt + h * kApHalf) + o16, ap_desc_k(kt + h * kApHalf) + o16,
                  kApIdescQK, kk > 0 ? 1u : 0u);
         }
-        ap_commit(&s_full[s]);
-        return true;
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; j < nb && ok; j++) {
-        if (j + 1 < nb && !issue_qk(j + 1)) break;
-        if (!mbar_wait(p_full, (uint32_t)(j & 1), status)) break;   // P_j written, O rescaled
+      bool ok = mbar_wait(q_full, 0, status) && mbar_wait(&k_full[0], 0, status);
+      if (ok) {
         ap_fence_after();
-        const unsigned char *sv = skv + (size_t)(j & 1) * 2 * kApTile + kApTile;
-#pragma unroll
-        for (int kk = 0; kk < kApBN / 16; kk++) {
-          const int h = kk >> 2, o16 = 2 * (kk & 3);
-          const uint64_t dv = ap_desc_mn(sv) + (uint64_t)(kk * (16 * 128) / 16);   // 16 key rows of 128 bytes
-          ap_mma(tmem + 256u, ap_desc_k(sp + h * kApHalf) + o16, dv, kApIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
-          if (kSplit) ap_mma(tmem + 256u, ap_desc_k(sp + kApTile + h * kApHalf) + o16, dv, kApIdescPV, 1u);
+        qk(0, 0);
+        ap_commit(&s_full[0]);
+        if (nB > 0) {
+          qk(1, 0);
+          ap_commit(&s_full[1]);
         }
-        ap_commit(pv_done);
-        ap_commit(&kv_empty[j & 1]);
+        ap_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nK && ok; j++) {
+        bool v_ready = false, k_ready = false;
+        for (int X = 0; X < 2; X++) {
+          const int nX = X ? nB : nA;
+          if (j >= nX) continue;
+          if (!mbar_wait(&p_full[X], (uint32_t)(j & 1), status)) { ok = false; break; }
+          if (!v_ready && !(v_ready = mbar_wait(&v_full[j & 1], (uint32_t)((j >> 1) & 1), status))) { ok = false; break; }
+          ap_fence_after();
+          // O_X += P_X V_j: P from TMEM (bf16 pairs over the S_X columns: hi in
+          // [0, 64), lo in [64, 128)), V MN-major from shared memory
+          const unsigned char *vt = sv + (j & 1) * kApTile;
+          const uint32_t tp = tmem + (uint32_t)(X * 128), to = tmem + 256u + (uint32_t)(X * 128);
+#pragma unroll
+          for (int kk = 0; kk < kApBN / 16; kk++) {
+            const uint64_t dv = ap_desc_mn(vt) + (uint64_t)(kk * (16 * 128) / 16);   // 16 key rows of 128 bytes
+            ap_mma_ts(to, tp + (uint32_t)(8 * kk), dv, kApIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+            if constexpr (kSplit) ap_mma_ts(to, tp + 64u + (uint32_t)(8 * kk), dv, kApIdescPV, 1u);
+          }
+          if (j + 1 < nX) {
+            if (!k_ready && !(k_ready = mbar_wait(&k_full[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), status))) {
+              ok = false;
+              break;
+            }
+            ap_fence_after();
+            qk(X, j + 1);   // after P_X V_j in the pipe: overwrites P_X only once it is read
+          }
+          ap_commit(&s_full[X]);
+        }
+        if (!ok) break;
+        ap_commit(&v_empty[j & 1]);
+        if (k_ready) ap_commit(&k_empty[(j + 1) & 1]);
       }
       ap_commit(mma_done);
       mbar_wait(mma_done, 0, status, false);
     }
   } else {
-    // softmax: thread = query row r = TMEM lane r; a warp may only touch its
-    // own 32-lane quarter of TMEM (warp % 4)
-    const int qd = warp & 3, r = qd * 32 + lane;
+    // softmax: warps 2-5 own tile A, 6-9 tile B; thread = query row r = TMEM
+    // lane r (a warp may only touch its own 32-lane quarter, warp % 4)
+    const int X = (warp - 2) >> 2, qd = warp & 3, r = qd * 32 + lane;
+    const int nX = X ? nB : nA, qbX = X ? qbB : qbA;
     const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
+    const uint32_t tS = trow + (uint32_t)(X * 128), tO = trow + 256u + (uint32_t)(X * 128);
     float m = -INFINITY, l = 0.0f;
-    bool ok = true;
-    for (int j = 0; j < nb; j++) {
-      const int s = j & 1;
-      if (!ap_wait_warp(&s_full[s], (uint32_t)((j >> 1) & 1), status)) { ok = false; break; }
+    bool ok = nX > 0;
+    for (int j = 0; j < nX && ok; j++) {
+      if (!ap_wait_warp(&s_full[X], (uint32_t)(j & 1), status)) { ok = false; break; }
       ap_fence_after();
       uint32_t raw[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; c++) ap_ld32(trow + (uint32_t)(s * kApBN + 32 * c), raw[c]);
+      for (int c = 0; c < 4; c++) ap_ld32(tS + (uint32_t)(32 * c), raw[c]);
       ap_wait_ld();
-      ap_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&s_empty[s]);
-      float sv[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; c++)
-#pragma unroll
-        for (int i = 0; i < 32; i++) sv[c][i] = __uint_as_float(raw[c][i]);
-      if (j == qb) {   // diagonal block: key 32c + i of this block is masked above query r
+      if (j == qbX) {   // diagonal block: key 32c + i of the block is masked above query r
 #pragma unroll
         for (int c = 0; c < 4; c++)
 #pragma unroll
           for (int i = 0; i < 32; i++)
-            if (32 * c + i > r) sv[c][i] = -INFINITY;
+            if (32 * c + i > r) raw[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = m;
-#pragma unroll
-      for (int c = 0; c < 4; c++)
-#pragma unroll
-        for (int i = 0; i < 32; i++) mx = fmaxf(mx, sv[c][i]);
-      const float nmc = -mx * c_log2;
-      const float alpha = ap_exp2(fmaf(m, c_log2, nmc));   // 0 on the first block (m = -inf)
-      float sum = 0.0f;
-      uint32_t phi[64], plo[kSplit ? 64 : 1];
-#pragma unroll
-      for (int c = 0; c < 4; c++)
-#pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ap_exp2(fmaf(sv[c][i], c_log2, nmc)), p1 = ap_exp2(fmaf(sv[c][i + 1], c_log2, nmc));
-          sum += p0 + p1;
-          const uint32_t h = pack_bf16(p0, p1);
-          phi[(32 * c + i) >> 1] = h;
-          if (kSplit)
-            plo[(32 * c + i) >> 1] = pack_bf16(p0 - __uint_as_float(h << 16), p1 - __uint_as_float(h & 0xFFFF0000u));
+      float mx = ap_max128(raw);
+      if (j == 0) {
+        m = mx;   // key 0 is never masked: finite
+      } else if (__any_sync(0xffffffffu, mx > m + tau)) {
+        // the running maximum is kept until a score exceeds it by tau (P <= 2^8
+        // meanwhile); then O and the sum are rescaled (O is stable: the P V of
+        // the previous block completed before these scores)
+        float alpha = 1.0f;
+        if (mx > m + tau) {
+          alpha = ap_exp2((m - mx) * c_log2);
+          m = mx;
         }
-      l = fmaf(l, alpha, sum);
-      // PV of the previous block done: O is stable and the P buffer free
-      if (j > 0) {
-        if (!ap_wait_warp(pv_done, (uint32_t)((j - 1) & 1), status)) { ok = false; break; }
-        ap_fence_after();
-        if (__any_sync(0xffffffffu, mx > m)) {   // rescale the O row by alpha (1 where the max held)
+        l *= alpha;
 #pragma unroll 1
-          for (int c = 0; c < 4; c++) {
-            uint32_t ov[32];
-            ap_ld32(trow + 256u + (uint32_t)(32 * c), ov);
-            ap_wait_ld();
+        for (int c = 0; c < 16; c++) {   // 8 columns at a time: the scores stay live in registers
+          uint32_t ov[8];
+          ap_ld8(tO + (uint32_t)(8 * c), ov);
+          ap_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-            ap_st32(trow + 256u + (uint32_t)(32 * c), ov);
-          }
-          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+          for (int i = 0; i < 8; i++) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          ap_st8(tO + (uint32_t)(8 * c), ov);
         }
       }
-      m = mx;
-      // P row r in the K-major 128-byte swizzle: 16-byte chunk c of half h at
-      // r * 128 + ((c ^ (r & 7)) * 16)
+      const float nmc = -m * c_log2;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int h = 0; h < 2; h++)
+      for (int g = 0; g < 8; g++) {   // keys 16g .. 16g + 15: bf16 pairs in columns 8g .. 8g + 7 (hi), 64 + those (lo)
+        uint32_t hi[8], lo[8];
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-          const int w = h * 32 + c * 4;   // packed pairs of keys 64h + 8c ...
-          const int off = h * kApHalf + r * 128 + ((c ^ (r & 7)) * 16);
-          *reinterpret_cast<uint4 *>(sp + off) = make_uint4(phi[w], phi[w + 1], phi[w + 2], phi[w + 3]);
-          if (kSplit)
-            *reinterpret_cast<uint4 *>(sp + kApTile + off) = make_uint4(plo[w], plo[w + 1], plo[w + 2], plo[w + 3]);
+        for (int i = 0; i < 8; i++) {
+          const int k0 = 16 * g + 2 * i;
+          const float p0 = ap_exp2(fmaf(__uint_as_float(raw[k0 >> 5][k0 & 31]), c_log2, nmc));
+          const float p1 = ap_exp2(fmaf(__uint_as_float(raw[k0 >> 5][(k0 & 31) + 1]), c_log2, nmc));
+          acc[i & 3] += p0 + p1;
+          const uint32_t h = pack_bf16(p0, p1);
+          hi[i] = h;
+          if constexpr (kSplit) lo[i] = pack_bf16(p0 - __uint_as_float(h << 16), p1 - __uint_as_float(h & 0xFFFF0000u));
         }
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        ap_st8(tS + (uint32_t)(8 * g), hi);
+        if constexpr (kSplit) ap_st8(tS + 64u + (uint32_t)(8 * g), lo);
+      }
+      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       ap_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[X]);
     }
-    // O / l once the last PV is done; rows past S are not stored
-    if (ok && ap_wait_warp(pv_done, (uint32_t)((nb - 1) & 1), status)) {
+    // O / l after the tile's last P V; rows past S are not stored
+    if (ok && ap_wait_warp(&s_full[X], (uint32_t)(nX & 1), status)) {
       ap_fence_after();
       const float inv = 1.0f / l;
-      const int qrow = qb * kApBM + r;
+      const int qrow = qbX * kApBM + r;
       float *orow = o + ((size_t)bh * S + qrow) * kApD;
 #pragma unroll 1
       for (int c = 0; c < 4; c++) {
         uint32_t ov[32];
-        ap_ld32(trow + 256u + (uint32_t)(32 * c), ov);
+        ap_ld32(tO + (uint32_t)(32 * c), ov);
         ap_wait_ld();
         if (qrow < S) {
           float4 *dst = reinterpret_cast<float4 *>(orow + 32 * c);
@@ -378,12 +442,13 @@ static bool ap_map(CUtensorMap *m, const void *base, int64_t BH, int64_t S) {
 template <bool kSplit>
 static int ap_launch(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv, float *o, int BH, int S,
                      float c_log2, cudaStream_t st) {
-  constexpr int smem = ap_smem<kSplit>();
-  cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel<kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e =
+      cudaFuncSetAttribute(attn_prefill_kernel<kSplit>, cudaFuncAttributeMaxDynamicSharedMemorySize, kApSmem);
   if (e != cudaSuccess)
     return sm100_set_error(SM100_ERR_CUDA, "attn_prefill: shared memory attribute: %s", cudaGetErrorString(e));
-  const unsigned grid = (unsigned)BH * (unsigned)((S + kApBM - 1) / kApBM);
-  attn_prefill_kernel<kSplit><<<grid, kApThreads, smem, st>>>(mq, mk, mv, o, BH, S, c_log2);
+  const int nqb = (S + kApBM - 1) / kApBM;
+  const unsigned grid = (unsigned)BH * (unsigned)((nqb + 1) / 2);
+  attn_prefill_kernel<kSplit><<<grid, kApThreads, kApSmem, st>>>(mq, mk, mv, o, BH, S, c_log2, 8.0f / c_log2);
   return launch_status("attn_prefill");
 }
 
@@ -396,9 +461,10 @@ extern "C" int sm100_attn_prefill_bf16(const void *q, const void *k, const void 
   if (B == 0 || H == 0 || S == 0) return SM100_OK;   // empty batch: nothing to write
   if (!q || !k || !v || !o || B < 0 || H < 0 || S < 0 || D != kApD || (int64_t)B * H > (1 << 24) ||
       (int64_t)S > (1 << 24) || ((uintptr_t)q & 15) || ((uintptr_t)k & 15) || ((uintptr_t)v & 15) ||
-      ((uintptr_t)o & 15))
-    return sm100_set_error(SM100_ERR_ARG, "attn_prefill: B %d H %d S %d D %d (D must be 128; 16-byte aligned)", B, H,
-                           S, D);
+      ((uintptr_t)o & 15) || !(scale > 0.0f && scale < 1e30f))
+    return sm100_set_error(SM100_ERR_ARG,
+                           "attn_prefill: B %d H %d S %d D %d scale %g (D must be 128, scale > 0; 16-byte aligned)", B,
+                           H, S, D, (double)scale);
   const int BH = B * H;
   if ((int64_t)BH * ((S + kApBM - 1) / kApBM) > 0x7FFFFFFF)
     return sm100_set_error(SM100_ERR_ARG, "attn_prefill: grid too large");
