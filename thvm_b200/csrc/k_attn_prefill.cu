@@ -27,8 +27,10 @@
 //             end O / sum.
 // kSplit: P is passed to the tensor cores as bf16 hi + bf16 lo (lo = P -
 // hi), two MMAs per key step, so P carries ~16 bits instead of 8: the output
-// then agrees with an f32 softmax to ~2e-6 relative and its row-wise argmax
+// then agrees with an f32 softmax to ~1e-5 relative and its row-wise argmax
 // does not flip on near-ties (a single bf16 P flips ~0.2 % of rows at S=2048).
+// The bf16 packing is integer byte permutes, not conversions: the exp2 alone
+// fills the SFU pipe.
 // Every wait is bounded; a timeout sets g_attn_status.
 #include <cuda.h>
 
@@ -40,8 +42,10 @@ namespace sm100 {
 constexpr int kApD = 128, kApBM = 128, kApBN = 128;
 constexpr int kApTile = kApBM * kApD * 2;   // 32 KB: one [128 x 128] bf16 tile as two 64-column swizzle halves
 constexpr int kApHalf = kApTile / 2;        // 16 KB
-constexpr int kApThreads = 10 * 32;
-constexpr int kApSmem = 6 * kApTile + 1024 + 256;   // Q_A, Q_B, K ring, V ring; alignment slack; barriers
+constexpr int kApThreads = 18 * 32;
+// Q_A, Q_B, K ring, V ring; alignment slack; barriers; the row-half maxima
+// (2 parities x 2 tiles x 2 halves x 128 rows) and sums (2 tiles x 2 x 128)
+constexpr int kApSmem = 6 * kApTile + 1024 + 256 + (1024 + 512) * 4;
 
 __device__ uint32_t g_attn_status;
 
@@ -141,18 +145,56 @@ __device__ __forceinline__ void ap_st8(uint32_t taddr, const uint32_t (&r)[8]) {
                : "memory");
 }
 
-// Maximum of a 128-score row held as f32 bits, as a tree (short dependency chains).
+// Maximum of a 128-score row held as f32 bits: eight independent chains (few
+// extra registers while the scores stay live, short dependencies).
 __device__ __forceinline__ float ap_max128(const uint32_t (&v)[4][32]) {
-  float a[32];
+  float a[8];
 #pragma unroll
-  for (int i = 0; i < 32; i++)
-    a[i] = fmaxf(fmaxf(__uint_as_float(v[0][i]), __uint_as_float(v[1][i])),
-                 fmaxf(__uint_as_float(v[2][i]), __uint_as_float(v[3][i])));
+  for (int k = 0; k < 8; k++) a[k] = __uint_as_float(v[0][k]);
 #pragma unroll
-  for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-    for (int i = 0; i < w; i++) a[i] = fmaxf(a[i], a[i + w]);
-  return a[0];
+  for (int i = 8; i < 128; i++) a[i & 7] = fmaxf(a[i & 7], __uint_as_float(v[i >> 5][i & 31]));
+  return fmaxf(fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3])), fmaxf(fmaxf(a[4], a[5]), fmaxf(a[6], a[7])));
+}
+
+// Named barrier over `count` threads (whole warps).
+__device__ __forceinline__ void ap_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// The same, returning the AND of v over the participating threads.
+__device__ __forceinline__ bool ap_bar_and(uint32_t id, uint32_t count, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %3, 0;\n\tbar.red.and.pred q, %1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(id), "r"(count), "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+// Two f32 in one 64-bit register pair, and the sm_100 packed f32x2 arithmetic on them.
+__device__ __forceinline__ uint64_t ap_pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void ap_unpack2(uint64_t r, float &a, float &b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ap_fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t ap_add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ap_max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ void ap_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -163,11 +205,6 @@ __device__ __forceinline__ float ap_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<const uint32_t *>(&h);
 }
 
 // A bounded wait whose outcome is the same in every lane of the warp (the
@@ -189,6 +226,7 @@ __global__ void __launch_bounds__(kApThreads, 1)
   uint64_t *q_full = bars, *k_full = bars + 1, *k_empty = bars + 3, *v_full = bars + 5, *v_empty = bars + 7;
   uint64_t *s_full = bars + 9, *p_full = bars + 11, *mma_done = bars + 13;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 14);
+  float *xmax = reinterpret_cast<float *>(smem + 6 * kApTile + 256), *xsum = xmax + 1024;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nqb = (S + kApBM - 1) / kApBM, npairs = (nqb + 1) >> 1;
   const int t = npairs - 1 - (int)(blockIdx.x / BH), bh = (int)(blockIdx.x % BH);   // heaviest pairs first
@@ -205,7 +243,7 @@ __global__ void __launch_bounds__(kApThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
     }
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -316,35 +354,56 @@ __global__ void __launch_bounds__(kApThreads, 1)
       mbar_wait(mma_done, 0, status, false);
     }
   } else {
-    // softmax: warps 2-5 own tile A, 6-9 tile B; thread = query row r = TMEM
-    // lane r (a warp may only touch its own 32-lane quarter, warp % 4)
-    const int X = (warp - 2) >> 2, qd = warp & 3, r = qd * 32 + lane;
+    // softmax: warps 2-9 own tile A, 10-17 tile B.  Two threads per query row
+    // r = TMEM lane r (a warp may only touch its own 32-lane quarter, warp %
+    // 4): half hf of the row's keys (and of its O columns) each.  The halves
+    // trade their maxima through shared memory behind a 64-thread named barrier.
+    const int X = (warp - 2) >> 3, hf = ((warp - 2) >> 2) & 1, qd = warp & 3, r = qd * 32 + lane;
     const int nX = X ? nB : nA, qbX = X ? qbB : qbA;
     const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
-    const uint32_t tS = trow + (uint32_t)(X * 128), tO = trow + 256u + (uint32_t)(X * 128);
+    const uint32_t tS = trow + (uint32_t)(X * 128), tO = trow + 256u + (uint32_t)(X * 128 + 64 * hf);
+    const uint32_t bar_id = 1u + (uint32_t)(X * 4 + qd);
     float m = -INFINITY, l = 0.0f;
     bool ok = nX > 0;
     for (int j = 0; j < nX && ok; j++) {
-      if (!ap_wait_warp(&s_full[X], (uint32_t)(j & 1), status)) { ok = false; break; }
+      // both halves of a row leave together: the wait's outcome is combined in
+      // the named barrier below (a half that left alone would strand the other)
+      const bool got = ap_wait_warp(&s_full[X], (uint32_t)(j & 1), status);
       ap_fence_after();
-      uint32_t raw[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; c++) ap_ld32(tS + (uint32_t)(32 * c), raw[c]);
+      uint32_t raw[2][32];
+      ap_ld32(tS + (uint32_t)(64 * hf), raw[0]);
+      ap_ld32(tS + (uint32_t)(64 * hf + 32), raw[1]);
       ap_wait_ld();
-      if (j == qbX) {   // diagonal block: key 32c + i of the block is masked above query r
+      if (j == qbX) {   // diagonal block: key 64hf + 32c + i of the block is masked above query r
 #pragma unroll
-        for (int c = 0; c < 4; c++)
+        for (int c = 0; c < 2; c++)
 #pragma unroll
           for (int i = 0; i < 32; i++)
-            if (32 * c + i > r) raw[c][i] = __float_as_uint(-INFINITY);
+            if (64 * hf + 32 * c + i > r) raw[c][i] = __float_as_uint(-INFINITY);
       }
-      float mx = ap_max128(raw);
+      float mx;
+      {   // eight chains of three-input maxima
+        float a[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) a[k] = __uint_as_float(raw[0][k]);
+#pragma unroll
+        for (int i = 8; i < 64; i += 16)
+#pragma unroll
+          for (int k = 0; k < 8; k++)
+            a[k] = ap_max3(a[k], __uint_as_float(raw[(i + k) >> 5][(i + k) & 31]),
+                           __uint_as_float(raw[(i + 8 + k) >> 5][(i + 8 + k) & 31]));
+        mx = ap_max3(ap_max3(a[0], a[1], a[2]), ap_max3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
+      }
+      xmax[((j & 1) * 2 + X) * 256 + hf * 128 + r] = mx;
+      if (!ap_bar_and(bar_id, 64, got)) { ok = false; break; }
+      mx = fmaxf(mx, xmax[((j & 1) * 2 + X) * 256 + (hf ^ 1) * 128 + r]);
       if (j == 0) {
         m = mx;   // key 0 is never masked: finite
       } else if (__any_sync(0xffffffffu, mx > m + tau)) {
         // the running maximum is kept until a score exceeds it by tau (P <= 2^8
         // meanwhile); then O and the sum are rescaled (O is stable: the P V of
-        // the previous block completed before these scores)
+        // the previous block completed before these scores).  Both halves of a
+        // row see the same maximum and decide alike.
         float alpha = 1.0f;
         if (mx > m + tau) {
           alpha = ap_exp2((m - mx) * c_log2);
@@ -352,7 +411,7 @@ __global__ void __launch_bounds__(kApThreads, 1)
         }
         l *= alpha;
 #pragma unroll 1
-        for (int c = 0; c < 16; c++) {   // 8 columns at a time: the scores stay live in registers
+        for (int c = 0; c < 8; c++) {   // this half's 64 O columns, 8 at a time
           uint32_t ov[8];
           ap_ld8(tO + (uint32_t)(8 * c), ov);
           ap_wait_ld();
@@ -361,48 +420,86 @@ __global__ void __launch_bounds__(kApThreads, 1)
           ap_st8(tO + (uint32_t)(8 * c), ov);
         }
       }
+      // P = exp2(s * c - m * c): the scale and the sums on packed f32x2 lanes
+      // (one instruction per two keys), the exponent on the SFU
       const float nmc = -m * c_log2;
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const uint64_t c2 = ap_pack2(c_log2, c_log2), nm2 = ap_pack2(nmc, nmc), neg2 = ap_pack2(-1.0f, -1.0f);
+      uint64_t acc2[2] = {0ull, 0ull};
 #pragma unroll
-      for (int g = 0; g < 8; g++) {   // keys 16g .. 16g + 15: bf16 pairs in columns 8g .. 8g + 7 (hi), 64 + those (lo)
+      for (int g = 0; g < 4; g++) {   // keys 64hf + 16g ...: bf16 pairs in columns 32hf + 8g .. (hi), 64 + those (lo)
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int i = 0; i < 8; i++) {
           const int k0 = 16 * g + 2 * i;
-          const float p0 = ap_exp2(fmaf(__uint_as_float(raw[k0 >> 5][k0 & 31]), c_log2, nmc));
-          const float p1 = ap_exp2(fmaf(__uint_as_float(raw[k0 >> 5][(k0 & 31) + 1]), c_log2, nmc));
-          acc[i & 3] += p0 + p1;
-          const uint32_t h = pack_bf16(p0, p1);
-          hi[i] = h;
-          if constexpr (kSplit) lo[i] = pack_bf16(p0 - __uint_as_float(h << 16), p1 - __uint_as_float(h & 0xFFFF0000u));
+          float x0, x1;
+          ap_unpack2(ap_fma2(ap_pack2(__uint_as_float(raw[k0 >> 5][k0 & 31]), __uint_as_float(raw[k0 >> 5][(k0 & 31) + 1])),
+                             c2, nm2),
+                     x0, x1);
+          const float p0 = ap_exp2(x0), p1 = ap_exp2(x1);
+          const uint64_t pp = ap_pack2(p0, p1);
+          acc2[i & 1] = ap_add2(acc2[i & 1], pp);
+          const uint32_t b0 = __float_as_uint(p0), b1 = __float_as_uint(p1);
+          if constexpr (kSplit) {
+            // hi = P truncated to bf16 (its upper halves), lo = P - hi (exact in
+            // f32, >= 0) truncated to bf16: P to ~2^-15 relative
+            hi[i] = __byte_perm(b0, b1, 0x7632);
+            float l0, l1;
+            ap_unpack2(ap_fma2(ap_pack2(__uint_as_float(b0 & 0xFFFF0000u), __uint_as_float(b1 & 0xFFFF0000u)), neg2, pp),
+                       l0, l1);
+            lo[i] = __byte_perm(__float_as_uint(l0), __float_as_uint(l1), 0x7632);
+          } else {
+            hi[i] = __byte_perm(b0 + 0x8000u, b1 + 0x8000u, 0x7632);   // P rounded half-up to bf16
+          }
         }
-        ap_st8(tS + (uint32_t)(8 * g), hi);
-        if constexpr (kSplit) ap_st8(tS + 64u + (uint32_t)(8 * g), lo);
+        ap_st8(tS + (uint32_t)(32 * hf + 8 * g), hi);
+        if constexpr (kSplit) ap_st8(tS + 64u + (uint32_t)(32 * hf + 8 * g), lo);
       }
-      l += (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      {
+        float a0, a1, b0, b1;
+        ap_unpack2(acc2[0], a0, a1);
+        ap_unpack2(acc2[1], b0, b1);
+        l += (a0 + a1) + (b0 + b1);
+      }
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       ap_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[X]);
     }
-    // O / l after the tile's last P V; rows past S are not stored
+    // the row's sum from both halves, then O / l after the tile's last P V;
+    // rows past S are not stored
+    if (nX > 0) {
+      xsum[X * 256 + hf * 128 + r] = l;
+      ap_bar_sync(bar_id, 64);
+      l += xsum[X * 256 + (hf ^ 1) * 128 + r];
+    }
     if (ok && ap_wait_warp(&s_full[X], (uint32_t)(nX & 1), status)) {
       ap_fence_after();
+      // O / l, staged through this tile's Q buffer (its products are all done):
+      // 4 KB per warp, 16-byte chunks swizzled by row so that both the row-wise
+      // writes and the column-wise reads are free of bank conflicts; each
+      // global store instruction then writes four full 128-byte row segments
       const float inv = 1.0f / l;
-      const int qrow = qbX * kApBM + r;
-      float *orow = o + ((size_t)bh * S + qrow) * kApD;
+      float *stage = reinterpret_cast<float *>(sq + X * kApTile) + (hf * 4 + qd) * 1024;
+      const int row0 = qbX * kApBM + qd * 32;
 #pragma unroll 1
-      for (int c = 0; c < 4; c++) {
+      for (int c = 0; c < 2; c++) {
         uint32_t ov[32];
         ap_ld32(tO + (uint32_t)(32 * c), ov);
         ap_wait_ld();
-        if (qrow < S) {
-          float4 *dst = reinterpret_cast<float4 *>(orow + 32 * c);
 #pragma unroll
-          for (int i = 0; i < 8; i++)
-            dst[i] = make_float4(__uint_as_float(ov[4 * i]) * inv, __uint_as_float(ov[4 * i + 1]) * inv,
-                                 __uint_as_float(ov[4 * i + 2]) * inv, __uint_as_float(ov[4 * i + 3]) * inv);
+        for (int q = 0; q < 8; q++)
+          *reinterpret_cast<float4 *>(stage + lane * 32 + ((q ^ (lane & 7)) * 4)) =
+              make_float4(__uint_as_float(ov[4 * q]) * inv, __uint_as_float(ov[4 * q + 1]) * inv,
+                          __uint_as_float(ov[4 * q + 2]) * inv, __uint_as_float(ov[4 * q + 3]) * inv);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+          const int rr = (lane >> 3) + 4 * i, ch = lane & 7;
+          const float4 v = *reinterpret_cast<const float4 *>(stage + rr * 32 + ((ch ^ (rr & 7)) * 4));
+          if (row0 + rr < S)
+            *reinterpret_cast<float4 *>(o + ((size_t)bh * S + row0 + rr) * kApD + 64 * hf + 32 * c + 4 * ch) = v;
         }
+        __syncwarp();
       }
     }
   }
