@@ -345,6 +345,40 @@ int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N
  * synchronises the device and clears the word */
 uint32_t sm100_gemm_status(void);
 
+/* ---- skinny bf16 GEMM for batched decode (M <= 32) ------------------------ */
+/* Y[M, N] = epilogue(X[M, K] . W[N, K]^T), bf16 X and W, f32 accumulate: nn_linear
+ * on a [B, 1, K] activation (src/nn/linear.c:1-6, py/thvm/nn.py:12-25) at the
+ * decode batch of BASELINE config 3.  tcgen05 with the weight rows as the MMA's
+ * M and the batch as its N; weight units of 128 x 64 spread evenly over up to
+ * 148 CTAs, split row tiles finished deterministically by their last part.
+ * Epilogue flags: + bias (when non-NULL), tanh GELU, + residual, bf16 output,
+ * and the KV-cache append of the k / v thirds of a fused qkv projection. */
+enum {
+  SM100_SK_GELU = 1u << 0,
+  SM100_SK_RESIDUAL = 1u << 1,
+  SM100_SK_OUT_BF16 = 1u << 2,
+  SM100_SK_KV = 1u << 3
+};
+typedef struct {
+  const void *x;          /* [M, K] bf16, row stride ld_x (0: K) */
+  const void *w;          /* [N, K] bf16, row stride ld_w (0: K) */
+  const float *bias;      /* [N] or NULL */
+  const float *residual;  /* [M, N] f32, row stride ld_res (0: N); may equal y */
+  void *y;                /* [M, N] f32, or bf16 with SM100_SK_OUT_BF16; row stride ld_y (0: N) */
+  float *ws;              /* sm100_skinny_ws_bytes(M) bytes of scratch */
+  uint32_t *counters;     /* ceil(N / 128) words, zero before the first call; left zero */
+  void *kv_cache;         /* SM100_SK_KV: [2, M, kv_ctx, N / 3] bf16; columns [N/3, 2N/3) -> k, rest -> v */
+  const int32_t *pos;     /* SM100_SK_KV: device row of the cache to write */
+  int64_t M, N, K, ld_x, ld_w, ld_res, ld_y;
+  int32_t flags, kv_ctx;
+} Sm100SkinnyArgs;
+/* M in [1, 32]; K % 8 == 0; x and w 16-byte aligned.  Launches on stream. */
+int sm100_skinny_bf16(const Sm100SkinnyArgs *a, void *stream);
+uint64_t sm100_skinny_ws_bytes(int32_t M);
+/* non-zero when a skinny launch since the last call gave up a bounded wait;
+ * synchronises the device and clears the word */
+uint32_t sm100_skinny_status(void);
+
 /* ---- causal attention prefill on the tensor cores ------------------------ */
 /* O[B, H, S, D] (f32) = softmax(Q K^T * scale + causal mask) V for bf16 Q, K, V
  * [B, H, S, D] contiguous, D = 128, any S >= 0: the reference's

@@ -68,6 +68,15 @@ class Sm100AttnArgs(ctypes.Structure):
         ("scale", c_float)]
 
 
+SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV = 1, 2, 4, 8
+
+
+class Sm100SkinnyArgs(ctypes.Structure):
+    _fields_ = [(n, c_void_p) for n in ("x", "w", "bias", "residual", "y", "ws", "counters", "kv_cache", "pos")] + [
+        (n, c_int64) for n in ("M", "N", "K", "ld_x", "ld_w", "ld_res", "ld_y")] + [
+        ("flags", c_int32), ("kv_ctx", c_int32)]
+
+
 _PL = ctypes.c_void_p * DECODE_MAX_LAYERS
 
 
@@ -142,6 +151,9 @@ SIGNATURES = {
     "sm100_attn_prefill_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                         c_float, c_int32, c_void_p]),
     "sm100_attn_prefill_status": (c_uint32, []),
+    "sm100_skinny_bf16": (c_int, [c_void_p, c_void_p]),
+    "sm100_skinny_ws_bytes": (c_uint64, [c_int32]),
+    "sm100_skinny_status": (c_uint32, []),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),
