@@ -379,6 +379,27 @@ uint64_t sm100_skinny_ws_bytes(int32_t M);
  * synchronises the device and clears the word */
 uint32_t sm100_skinny_status(void);
 
+/* ---- the batched bf16 decode step around the skinny GEMM (config 3) ------- */
+/* GPT-2-XL-shaped decode of B sequences (bench/gpt2/thvm_gpt2.py:27-128 with
+ * bf16 weights): h f32 residual stream, bf16 matmul operands, bf16 KV cache
+ * [2, B, ctx, C] (C = heads * 64 of this rank).  Device pointers; launch on
+ * stream. */
+/* h[b] = wte[tok[b]] + wpe[*pos] (bf16 tables; ids outside [0, V) read zeros) */
+int sm100_xl_embed(const void *wte, const void *wpe, const int32_t *tok, const int32_t *pos, float *h,
+                   int32_t B, int32_t V, int32_t D, void *stream);
+/* y (bf16) = LayerNorm(x) * g + b per row (src/nn/layernorm.c:1-7) */
+int sm100_xl_layernorm(const float *x, const float *g, const float *b, void *y, int32_t M, int32_t D,
+                       float eps, void *stream);
+/* out (bf16 [B, C]) = softmax(q k^T * scale) v over cache rows 0..*pos, q the
+ * first C columns of qkv rows (f32, row stride ld_qkv); hd = 64 */
+int sm100_xl_attention(const float *qkv, int64_t ld_qkv, const void *kv_cache, const int32_t *pos, void *out,
+                       int32_t B, int32_t H, int32_t hd, int32_t ctx, float scale, void *stream);
+/* per row: largest value and its first index + idx_offset (py/thvm/tensor.py:998-1011) */
+int sm100_xl_argmax(const float *x, int64_t ld, int32_t M, int32_t N, float *val, int32_t *idx, int32_t idx_offset,
+                    void *stream);
+/* tok[b] = index of the largest of R candidates val/idx [R][B] (ties: smaller index) */
+int sm100_xl_pick(const float *val, const int32_t *idx, int32_t R, int32_t B, int32_t *tok, void *stream);
+
 /* ---- causal attention prefill on the tensor cores ------------------------ */
 /* O[B, H, S, D] (f32) = softmax(Q K^T * scale + causal mask) V for bf16 Q, K, V
  * [B, H, S, D] contiguous, D = 128, any S >= 0: the reference's

@@ -261,5 +261,54 @@ class GPT2:
             self._state = None
 
 
+class _OrcXL(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("n_layers", "dim", "heads", "vocab", "max_ctx", "batch")] + [
+        ("norm_eps", ctypes.c_float)] + [
+        (n, ctypes.c_void_p) for n in ("wte", "wpe", "lm_head", "ln_f_w", "ln_f_b")] + [
+        (n, ctypes.POINTER(ctypes.c_void_p)) for n in (
+            "ln_1_w", "ln_1_b", "ln_2_w", "ln_2_b", "c_attn_w", "c_proj_w", "c_fc_w", "mlp_proj_w",
+            "c_attn_b", "c_proj_b", "c_fc_b", "mlp_proj_b")]
+
+
+class XLModel:
+    """The oracle's batched bf16 decode step (orc_xl_step) over the weight
+    dict of thvm_b200.gpt2_xl.xl_weights (bf16 bits as uint16, f32 vectors)."""
+
+    _per_layer = {"ln_1_w": "ln_1.w", "ln_1_b": "ln_1.b", "ln_2_w": "ln_2.w", "ln_2_b": "ln_2.b",
+                  "c_attn_w": "attn.w", "c_proj_w": "proj.w", "c_fc_w": "fc.w", "mlp_proj_w": "p2.w",
+                  "c_attn_b": "attn.b", "c_proj_b": "proj.b", "c_fc_b": "fc.b", "mlp_proj_b": "p2.b"}
+
+    def __init__(self, cfg, weights: dict):
+        self.cfg = cfg
+        self._keep = {k: np.ascontiguousarray(v) for k, v in weights.items()}
+        w = self._keep
+        s = _OrcXL(n_layers=cfg.n_layers, dim=cfg.dim, heads=cfg.heads, vocab=cfg.vocab, max_ctx=cfg.max_ctx,
+                   batch=cfg.batch, norm_eps=cfg.norm_eps)
+        s.wte, s.wpe, s.lm_head = w["wte"].ctypes.data, w["wpe"].ctypes.data, w["lm_head"].ctypes.data
+        s.ln_f_w, s.ln_f_b = w["ln_f.w"].ctypes.data, w["ln_f.b"].ctypes.data
+        self._arrays = []
+        for field, suffix in self._per_layer.items():
+            arr = (ctypes.c_void_p * cfg.n_layers)(*[w[f"h.{i}.{suffix}"].ctypes.data for i in range(cfg.n_layers)])
+            self._arrays.append(arr)
+            setattr(s, field, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)))
+        self._s = s
+        self.kv = np.zeros((cfg.n_layers, 2, cfg.batch, cfg.max_ctx, cfg.dim), np.uint16)
+        L = lib()
+        if not getattr(L, "_xl_bound", False):
+            L.orc_xl_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                      ctypes.c_void_p, ctypes.c_void_p]
+            L.orc_xl_step.restype = None
+            L._xl_bound = True
+
+    def step(self, tok, pos: int):
+        """(logits [B, V], next ids [B]) of one decode step at row pos."""
+        t = np.ascontiguousarray(tok, np.int32)
+        lg = np.empty((self.cfg.batch, self.cfg.vocab), np.float32)
+        nxt = np.empty(self.cfg.batch, np.int32)
+        lib().orc_xl_step(ctypes.byref(self._s), self.kv.ctypes.data, t.ctypes.data, pos, lg.ctypes.data,
+                          nxt.ctypes.data)
+        return lg, nxt
+
+
 def num_threads() -> int:
     return int(lib().orc_num_threads())

@@ -124,6 +124,29 @@ int32_t orc_gpt2_forward(OrcGPT2State *s, const int32_t *tokens, int32_t n_tok,
 int orc_gpt2_generate(const OrcGPT2 *m, const int32_t *prompt, int32_t n_prompt,
                       int32_t n_new, int32_t *out);
 
+/* ---- batched bf16 GPT-2-XL-shaped decode step ----------
+ * The model of bench/gpt2/thvm_gpt2.py:27-128 with bf16 weights: the residual
+ * stream h is f32; each Linear's input (LayerNorm output, attention output,
+ * GELU output) is rounded to bf16 and multiplied by the bf16 weight with an
+ * f32 sum in k order, + f32 bias; k and v enter the cache as bf16; scores
+ * (q * scale) . k in f32, softmax max / exp / sum, out = (sum_j e_j v_j) / sum
+ * rounded to bf16.  Embedding tables bf16.  Weight matrices (out, in). */
+typedef struct {
+  int32_t n_layers, dim, heads, vocab, max_ctx, batch;
+  float norm_eps;
+  const uint16_t *wte, *wpe, *lm_head;            /* [V, D], [ctx, D], [V, D] */
+  const float *ln_f_w, *ln_f_b;
+  const float **ln_1_w, **ln_1_b, **ln_2_w, **ln_2_b;
+  const uint16_t **c_attn_w, **c_proj_w, **c_fc_w, **mlp_proj_w;   /* [3D,D] [D,D] [4D,D] [D,4D] */
+  const float **c_attn_b, **c_proj_b, **c_fc_b, **mlp_proj_b;
+} OrcXL;
+
+/* One decode step of `batch` sequences at position pos: kv is the bf16 cache
+ * [n_layers][2][batch][max_ctx][dim] (row pos written), h scratch is
+ * allocated inside.  logits [batch, vocab] (may be NULL); next [batch] gets
+ * each row's first-index argmax. */
+void orc_xl_step(const OrcXL *m, uint16_t *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next);
+
 /* threads the oracle's row-parallel loops use (pthreads), for reporting. */
 int orc_num_threads(void);
 

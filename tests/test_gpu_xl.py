@@ -1,0 +1,47 @@
+"""The batched bf16 decode step of the GPT-2-XL-shaped model (BASELINE
+config 3) on one GPU (thvm_b200.gpt2_xl.XLModel, tensor-parallel degree 1)
+against the CPU oracle (oracle.XLModel, orc_xl_step) on a reduced model
+(2 layers, d 256, 4 heads x 64, vocab 1000, batch 16): 8 prompt positions
+and 12 decode steps, both sides fed the oracle's ids.  The north star's bf16
+gates: logits within 2e-2 of the row scale and top-1 agreement >= 99 %; the
+bf16 KV cache rows within one bf16 rounding of the oracle's plus 1e-3 of
+their rms (the f32 summation order of LayerNorm and products can move a bf16
+operand by one step)."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def test_xl_decode_matches_oracle():
+    import torch
+    from thvm_b200.gpt2_xl import XLConfig, XLModel, shard_of, xl_weights
+    cfg = XLConfig(n_layers=2, dim=256, heads=4, vocab=1000, max_ctx=64, batch=16)
+    w = xl_weights(cfg, seed=0)
+    dev = XLModel(cfg, w, shard_of(cfg, 0, 1))
+    ref = O.XLModel(cfg, w)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, (cfg.batch, 8)).astype(np.int32)
+    tok = prompt[:, 0]
+    agree, total, worst = 0, 0, 0.0
+    for pos in range(20):
+        dev.tok.copy_(torch.from_numpy(tok))
+        dev.step()
+        torch.cuda.synchronize()
+        lg, nxt = ref.step(tok, pos)
+        dl = dev.logits.cpu().numpy()
+        worst = max(worst, float((np.abs(dl - lg).max(1) / np.abs(lg).max(1)).max()))
+        agree += int((dev.tok.cpu().numpy() == nxt).sum())
+        total += cfg.batch
+        assert int(dev.pos.item()) == pos + 1
+        tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt
+    assert worst <= 2e-2, worst
+    assert agree / total >= 0.99, agree / total
+    f32 = lambda b: (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    kv = f32(dev.kv[0].cpu().numpy().view(np.uint16)[:, :, :20])
+    rk = f32(ref.kv[0][:, :, :20])
+    # the f32 sums differ in order (LayerNorm, products), which can move a
+    # bf16 operand by one rounding step; each side then rounds k, v to bf16
+    excess = np.abs(kv - rk) - (2.0 ** -7 * np.abs(rk) + 1e-3 * np.sqrt(np.mean(rk * rk)))
+    assert excess.max() <= 0, excess.max()

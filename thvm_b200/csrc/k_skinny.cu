@@ -264,15 +264,36 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (*last_flag) {
           __threadfence();
+          // the parts in CTA order (deterministic); four slots' loads in
+          // flight at a time.  A part other than the tile's first starts inside
+          // the tile, so the tile is its first (slot 2cc); the first part's
+          // slot is 0 only when it starts exactly at the tile.
           float acc[MB];
 #pragma unroll
           for (int b = 0; b < MB; b++) acc[b] = 0.0f;
-          for (int cc = c_lo; cc <= c_hi; cc++) {
-            const int sl = 2 * cc + (t == sk_u0(cc, p.U, p.G) / p.KC ? 0 : 1);
-            const float *ws = p.ws + (size_t)sl * MB * kSkBM;
+          const int lo_slot = 2 * c_lo + (sk_u0(c_lo, p.U, p.G) < t * p.KC ? 1 : 0);
+          auto slot_ptr = [&](int cc) {
+            return p.ws + (size_t)(cc == c_lo ? lo_slot : 2 * cc) * MB * kSkBM + row;
+          };
+          int cc = c_lo;
+          for (; cc + 3 <= c_hi; cc += 4) {
+            float v4[4][MB];
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+              const float *ws = slot_ptr(cc + k);
+#pragma unroll
+              for (int b = 0; b < MB; b++) v4[k][b] = b < Mv ? __ldcg(ws + b * kSkBM) : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+#pragma unroll
+              for (int b = 0; b < MB; b++) acc[b] += v4[k][b];
+          }
+          for (; cc <= c_hi; cc++) {
+            const float *ws = slot_ptr(cc);
 #pragma unroll
             for (int b = 0; b < MB; b++)
-              if (b < Mv) acc[b] += __ldcg(ws + b * kSkBM + row);
+              if (b < Mv) acc[b] += __ldcg(ws + b * kSkBM);
           }
           if (n < p.N) {
 #pragma unroll

@@ -1,12 +1,14 @@
 """The standalone contraction sweep on the sm_100a device.
 
-    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm|prefill]
+    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm|prefill|skinny]
 
 Seeded N(0,1) inputs, fp32 accumulate:
   * decode matvec x[1, 4096] against W (11008 x 4096) in bf16, and in fp8 e4m3
     with one f32 scale per 128 x 128 block (scales uniform in [0.5, 2]);
   * bf16 GEMM C[M, N] = A[M, K] B[N, K]^T at M=N=K=4096 and M=8192, N=K=4096
     (when the tcgen05 GEMM is built into the library);
+  * the skinny bf16 GEMM of batched decode at the GPT-2-XL projection shapes
+    (batch 16);
   * causal attention prefill: bf16 Q, K, V [4, 16, 2048,
     128] N(0,1), f32 O, with P split into bf16 hi + lo (the parity setting)
     and as a single bf16 P; FLOPs counted as 2 B H S^2 D (the causal half of
@@ -187,10 +189,47 @@ def prefill_cases(dev: Device, timer: Timer, iters: int):
     return out
 
 
+def skinny_cases(dev: Device, timer: Timer, iters: int):
+    """The GPT-2-XL projections of BASELINE config 3 at batch 16 (bf16 weights
+    streamed once per launch; HBM-bound)."""
+    import ctypes
+    lib = dev.lib
+    hbm, _, kind = peaks()
+    rng = np.random.default_rng(5)
+    M = 16
+    out = []
+    for name, N, K in (("c_attn", 4800, 1600), ("attn.c_proj", 1600, 1600), ("c_fc", 6400, 1600),
+                       ("mlp.c_proj", 1600, 6400), ("lm_head", 50257, 1600)):
+        x = bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+        w = bf16_bits((0.02 * rng.standard_normal((N, K))).astype(np.float32))
+        xb, y = dev.upload(x), dev.alloc(M * N * 4)
+        ws, cnt = dev.alloc(lib.sm100_skinny_ws_bytes(M)), dev.alloc(((N + 127) // 128) * 4)
+        lib.sm100_buf_zero(cnt)
+        ws_ = [dev.upload(w) for _ in range(copies_for(w.nbytes))]
+        args = []
+        for wb in ws_:
+            a = L.Sm100SkinnyArgs()
+            a.x, a.w, a.y, a.ws, a.counters = dev.dptr(xb), dev.dptr(wb), dev.dptr(y), dev.dptr(ws), dev.dptr(cnt)
+            a.M, a.N, a.K = M, N, K
+            args.append(a)
+        ms = timer.time([lambda a=a: L.check(lib.sm100_skinny_bf16(ctypes.byref(a), dev.stream), "skinny")
+                         for a in args], iters)
+        assert lib.sm100_skinny_status() == 0
+        byts = w.nbytes + x.nbytes + M * N * 4
+        gbs = byts / (ms / 1e3) / 1e9
+        out.append({"case": f"skinny_{name}", "M": M, "N": N, "K": K, "kernel": "skinny_kernel",
+                    "us": round(ms * 1e3, 2), "bytes": byts, "achieved": round(gbs, 1), "unit": "GB/s",
+                    "peak": hbm, "frac": round(gbs / hbm, 4), "peak_source": kind,
+                    "l2": f"{len(ws_)} weight copies rotated (> 2x L2)"})
+        for bid in ws_ + [xb, y, ws, cnt]:
+            dev.free(bid)
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", choices=["matvec", "gemm", "prefill"], default=None)
+    ap.add_argument("--only", choices=["matvec", "gemm", "prefill", "skinny"], default=None)
     args = ap.parse_args()
     dev = Device.get()
     timer = Timer(dev)
@@ -199,6 +238,8 @@ def main():
         rows += matvec_cases(dev, timer, args.iters)
     if args.only in (None, "gemm"):
         rows += gemm_cases(dev, timer, args.iters)
+    if args.only in (None, "skinny"):
+        rows += skinny_cases(dev, timer, args.iters)
     if args.only in (None, "prefill"):
         rows += prefill_cases(dev, timer, args.iters)
     for r in rows:
