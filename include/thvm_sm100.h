@@ -357,7 +357,9 @@ enum {
   SM100_SK_GELU = 1u << 0,
   SM100_SK_RESIDUAL = 1u << 1,
   SM100_SK_OUT_BF16 = 1u << 2,
-  SM100_SK_KV = 1u << 3
+  SM100_SK_KV = 1u << 3,
+  SM100_SK_ACCUM = 1u << 4,   /* y (f32) += X W^T (+ bias once), unordered reductions; alone */
+  SM100_SK_X_GELU = 1u << 5   /* x is f32 [M, K]: the product uses bf16(gelu(x)) */
 };
 typedef struct {
   const void *x;          /* [M, K] bf16, row stride ld_x (0: K) */
@@ -387,16 +389,21 @@ uint32_t sm100_skinny_status(void);
 /* h[b] = wte[tok[b]] + wpe[*pos] (bf16 tables; ids outside [0, V) read zeros) */
 int sm100_xl_embed(const void *wte, const void *wpe, const int32_t *tok, const int32_t *pos, float *h,
                    int32_t B, int32_t V, int32_t D, void *stream);
-/* y (bf16) = LayerNorm(x) * g + b per row (src/nn/layernorm.c:1-7) */
-int sm100_xl_layernorm(const float *x, const float *g, const float *b, void *y, int32_t M, int32_t D,
-                       float eps, void *stream);
+/* y (bf16) = LayerNorm(x) * g + b per row (src/nn/layernorm.c:1-7); zero_x clears
+ * x after reading it, zero_buf[0..zero_n) is cleared (accumulators of the next
+ * products) */
+int sm100_xl_layernorm(float *x, const float *g, const float *b, void *y, int32_t M, int32_t D, float eps,
+                       int32_t zero_x, float *zero_buf, int64_t zero_n, void *stream);
 /* out (bf16 [B, C]) = softmax(q k^T * scale) v over cache rows 0..*pos, q the
- * first C columns of qkv rows (f32, row stride ld_qkv); hd = 64 */
-int sm100_xl_attention(const float *qkv, int64_t ld_qkv, const void *kv_cache, const int32_t *pos, void *out,
-                       int32_t B, int32_t H, int32_t hd, int32_t ctx, float scale, void *stream);
-/* per row: largest value and its first index + idx_offset (py/thvm/tensor.py:998-1011) */
-int sm100_xl_argmax(const float *x, int64_t ld, int32_t M, int32_t N, float *val, int32_t *idx, int32_t idx_offset,
-                    void *stream);
+ * first C columns of qkv rows (f32, row stride ld_qkv); hd = 64.  append: qkv
+ * rows are complete [q | k | v] sums; k, v enter cache row *pos first and the
+ * qkv rows are cleared after use */
+int sm100_xl_attention(float *qkv, int64_t ld_qkv, void *kv_cache, const int32_t *pos, void *out, int32_t B,
+                       int32_t H, int32_t hd, int32_t ctx, float scale, int32_t append, void *stream);
+/* per row: largest value and its first index + idx_offset (py/thvm/tensor.py:998-1011);
+ * zero_x clears the rows after reading */
+int sm100_xl_argmax(float *x, int64_t ld, int32_t M, int32_t N, float *val, int32_t *idx, int32_t idx_offset,
+                    int32_t zero_x, void *stream);
 /* tok[b] = index of the largest of R candidates val/idx [R][B] (ties: smaller index) */
 int sm100_xl_pick(const float *val, const int32_t *idx, int32_t R, int32_t B, int32_t *tok, void *stream);
 

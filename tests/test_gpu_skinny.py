@@ -27,7 +27,7 @@ def bf16_to_f32(b):
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-def run(device, x, w, bias=None, residual=None, flags=0, kv=None, pos=None, kv_ctx=0, repeat=1):
+def run(device, x, w, bias=None, residual=None, flags=0, kv=None, pos=None, kv_ctx=0, repeat=1, accumulate=1):
     from thvm_b200 import _lib as L
     M, K = x.shape
     N = w.shape[0]
@@ -45,13 +45,14 @@ def run(device, x, w, bias=None, residual=None, flags=0, kv=None, pos=None, kv_c
     a = L.Sm100SkinnyArgs()
     for k, v in ids.items():
         setattr(a, k, device.dptr(v))
-    if residual is not None:
+    if residual is not None and not flags & L.SK_ACCUM:
         a.residual = a.y
     a.M, a.N, a.K, a.flags, a.kv_ctx = M, N, K, flags, kv_ctx
     for _ in range(repeat):
         if residual is not None:
             device.write(ids["y"], residual)
-        L.check(device.lib.sm100_skinny_bf16(ctypes.byref(a), device.stream), "skinny")
+        for _ in range(accumulate):
+            L.check(device.lib.sm100_skinny_bf16(ctypes.byref(a), device.stream), "skinny")
     device.sync()
     assert device.lib.sm100_skinny_status() == 0
     if flags & L.SK_OUT_BF16:
@@ -108,6 +109,28 @@ def test_skinny_kv_append(device):
     np.testing.assert_array_equal(kv_out[0, :, pos], O.to_bf16(y[:, C:2 * C]))
     np.testing.assert_array_equal(kv_out[1, :, pos], O.to_bf16(y[:, 2 * C:]))
     assert not kv_out[:, :, :pos].any() and not kv_out[:, :, pos + 1:].any()
+
+
+def test_skinny_accumulate(device):
+    """SM100_SK_ACCUM: y += X W^T + bias, twice over the same y (the bias once per call)."""
+    from thvm_b200 import _lib as L
+    M, N, K = 16, 1600, 6400
+    x, w, b = operands(M, N, K, 6)
+    y0 = np.random.default_rng(7).standard_normal((M, N)).astype(np.float32)
+    y, _ = run(device, x, w, bias=b, residual=y0, flags=L.SK_ACCUM, repeat=1, accumulate=2)
+    close(y, y0 + 2 * (O.gemm_bf16(x, w) + b))
+
+
+def test_skinny_x_gelu(device):
+    """SM100_SK_X_GELU: the f32 operand enters the product as bf16(gelu(x)) (the MLP down-projection)."""
+    from thvm_b200 import _lib as L
+    for M, N, K in ((16, 1600, 6400), (5, 300, 520)):
+        rng = np.random.default_rng(K)
+        xf = rng.standard_normal((M, K)).astype(np.float32)
+        _, w, b = operands(M, N, K, 8)
+        y0 = np.zeros((M, N), np.float32)
+        y, _ = run(device, xf, w, bias=b, residual=y0, flags=L.SK_ACCUM | L.SK_X_GELU)
+        close(y, O.gemm_bf16(O.to_bf16(O.gelu(xf)), w) + b)
 
 
 def test_skinny_rejects(device):

@@ -68,7 +68,7 @@ class Sm100AttnArgs(ctypes.Structure):
         ("scale", c_float)]
 
 
-SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV = 1, 2, 4, 8
+SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV, SK_ACCUM, SK_X_GELU = 1, 2, 4, 8, 16, 32
 
 
 class Sm100SkinnyArgs(ctypes.Structure):
@@ -155,10 +155,12 @@ SIGNATURES = {
     "sm100_skinny_ws_bytes": (c_uint64, [c_int32]),
     "sm100_skinny_status": (c_uint32, []),
     "sm100_xl_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
-    "sm100_xl_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
+    "sm100_xl_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_int32,
+                                   c_void_p, c_int64, c_void_p]),
     "sm100_xl_attention": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
-                                   c_int32, c_float, c_void_p]),
-    "sm100_xl_argmax": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_void_p]),
+                                   c_int32, c_float, c_int32, c_void_p]),
+    "sm100_xl_argmax": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
+                                c_void_p]),
     "sm100_xl_pick": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),

@@ -15,21 +15,32 @@
 // last part to arrive (per-tile counter) adds the slots in CTA order and
 // finishes the tile: deterministic, no floating-point atomics.
 //   warp 0    TMA: W chunk [128 x 64] and X chunk [MB x 64] (128-byte swizzle)
-//             into an 8-stage ring;
+//             into a 5-stage ring (two CTAs fit an SM, so with programmatic
+//             dependent launch the next GEMM's CTAs prefetch their first
+//             weight chunks while this one finishes; activations are read
+//             only after griddepcontrol.wait);
 //   warp 1    MMA: 4 x tcgen05.mma (M=128, N=MB, K=16) per chunk into one of
 //             two TMEM accumulators (a run's epilogue overlaps the next run);
 //   warps 2-5 epilogue: tcgen05.ld a 32-row quarter; bias, tanh GELU,
 //             residual, f32 or bf16 store, and the KV-cache append of the
 //             attention projection's k / v columns.
+// SM100_SK_ACCUM skips the split-K finishing: every part adds its sums (and
+// the part holding k-chunk 0 the bias) into y with fire-and-forget
+// reductions, leaving the remaining epilogue to the consumer kernel.
+// SM100_SK_X_GELU takes X as f32 and feeds bf16(gelu(X)) to the MMA, staged in
+// shared memory by the epilogue warps before the products start.
 // Every wait is bounded; a timeout sets g_skinny_status.
 #include <cuda.h>
+
+#include <algorithm>
+#include <cstring>
 
 #include "common.cuh"
 #include "tma.cuh"
 
 namespace sm100 {
 
-constexpr int kSkBM = 128, kSkBK = 64, kSkStages = 8, kSkThreads = 6 * 32, kSkMaxGrid = 148;
+constexpr int kSkBM = 128, kSkBK = 64, kSkStages = 5, kSkThreads = 6 * 32, kSkMaxGrid = 148;
 constexpr int kSkWBytes = kSkBM * kSkBK * 2;   // 16 KB
 
 template <int MB>
@@ -37,8 +48,8 @@ __host__ __device__ constexpr int sk_stage_bytes() {
   return kSkWBytes + MB * kSkBK * 2;
 }
 template <int MB>
-__host__ __device__ constexpr int sk_smem() {
-  return kSkStages * sk_stage_bytes<MB>() + 1024 + 256;
+__host__ __device__ constexpr int sk_smem(int xslots = 0) {
+  return kSkStages * sk_stage_bytes<MB>() + xslots * MB * kSkBK * 2 + 1024 + 256;
 }
 
 __device__ uint32_t g_skinny_status;
@@ -58,6 +69,11 @@ struct SkParams {
   __nv_bfloat16 *kv;
   const int32_t *pos;
   int kv_ctx;
+  // SM100_SK_X_GELU: X is f32 [M, K] (row stride ld_x) and enters the MMA as
+  // bf16(gelu(X)), prepared in shared memory by the epilogue warps
+  const float *xf;
+  int64_t ld_x;
+  int xslots;   // X chunks held per CTA (min(KC, most units of a CTA))
 };
 
 __device__ __forceinline__ void sk_tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -137,16 +153,20 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                   const SkParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  constexpr int kStage = sk_stage_bytes<MB>();
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kSkStages * kStage);
+  constexpr int kStage = sk_stage_bytes<MB>(), kXTile = MB * kSkBK * 2;
+  const bool xg = (p.flags & SM100_SK_X_GELU) != 0;
+  unsigned char *xs = smem + kSkStages * kStage;   // X_GELU: the CTA's X chunks
+  uint64_t *bars = reinterpret_cast<uint64_t *>(xs + (xg ? p.xslots : 0) * kXTile);
   uint64_t *full = bars, *empty = bars + kSkStages, *acc_full = bars + 2 * kSkStages, *acc_empty = acc_full + 2;
-  uint64_t *done = acc_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint64_t *done = acc_empty + 2, *x_ready = done + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(x_ready + 1);
   volatile uint32_t *last_flag = tmem_slot + 1;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x, u0 = sk_u0(c, p.U, p.G), u1 = sk_u0(c + 1, p.U, p.G);
+  const int kc_first = u0 % p.KC;   // X_GELU: the X chunk of unit u sits in slot (u % KC - kc_first) mod KC
   uint32_t *status = &g_skinny_status;
 
+  pdl_trigger();
   if (threadIdx.x == 0) {
     for (int i = 0; i < kSkStages; i++) {
       mbar_init(&full[i], 1);
@@ -157,6 +177,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(done, 1);
+    mbar_init(x_ready, 4);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {   // two accumulators of MB columns
@@ -172,15 +193,28 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      int i = 0;
-      for (int u = u0; u < u1; u++, i++) {
+      // the first stages' weights do not depend on earlier kernels: issue them
+      // before waiting for the previous grid, their activations after
+      const int pre = min(kSkStages, u1 - u0);
+      const uint32_t tx = xg ? kSkWBytes : kStage;
+      for (int k = 0; k < pre; k++) {
+        const int u = u0 + k;
+        mbar_expect_tx(&full[k], tx);
+        sk_tma_2d(smem + k * kStage, &map_w, (u % p.KC) * kSkBK, (u / p.KC) * kSkBM, &full[k]);
+      }
+      pdl_wait();
+      if (!xg)
+        for (int k = 0; k < pre; k++)
+          sk_tma_2d(smem + k * kStage + kSkWBytes, &map_x, ((u0 + k) % p.KC) * kSkBK, 0, &full[k]);
+      int i = pre;
+      for (int u = u0 + pre; u < u1; u++, i++) {
         const int s = i % kSkStages;
         if (i >= kSkStages && !mbar_wait(&empty[s], (uint32_t)(((i / kSkStages) - 1) & 1), status)) break;
         unsigned char *st = smem + s * kStage;
-        mbar_expect_tx(&full[s], kStage);
+        mbar_expect_tx(&full[s], tx);
         const int t = u / p.KC, kc = u % p.KC;
         sk_tma_2d(st, &map_w, kc * kSkBK, t * kSkBM, &full[s]);
-        sk_tma_2d(st + kSkWBytes, &map_x, kc * kSkBK, 0, &full[s]);
+        if (!xg) sk_tma_2d(st + kSkWBytes, &map_x, kc * kSkBK, 0, &full[s]);
       }
       // the copies in flight land before the CTA may exit
       for (int k = i - kSkStages > 0 ? i - kSkStages : 0; k < i; k++)
@@ -191,7 +225,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MB >> 3) << 17) |
                                  ((uint32_t)(kSkBM >> 4) << 24);
       int i = 0, run = 0;
-      bool ok = true;
+      bool ok = !xg || mbar_wait(x_ready, 0, status);
       for (int u = u0; u < u1 && ok; run++) {
         const int t = u / p.KC, uend = min(u1, (t + 1) * p.KC);
         const int a = run & 1;
@@ -202,13 +236,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           if (!mbar_wait(&full[s], (uint32_t)((i / kSkStages) & 1), status)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const unsigned char *st = smem + s * kStage;
+          const unsigned char *xt = xg ? xs + ((k % p.KC - kc_first + p.KC) % p.KC) * kXTile : st + kSkWBytes;
 #pragma unroll
           for (int kk = 0; kk < kSkBK / 16; kk++) {
             const uint32_t acc = (k > u || kk > 0) ? 1u : 0u;
             asm volatile(
                 "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * MB)),
-                "l"(sk_desc(st) + 2 * kk), "l"(sk_desc(st + kSkWBytes) + 2 * kk), "r"(idesc), "r"(acc)
+                "l"(sk_desc(st) + 2 * kk), "l"(sk_desc(xt) + 2 * kk), "r"(idesc), "r"(acc)
                 : "memory");
           }
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -227,6 +262,31 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
   } else {
     // epilogue: warp quarter q = warp % 4 reads TMEM lanes 32q .. 32q + 31 = rows of the tile
+    pdl_wait();   // residual, outputs and the split-K workspace belong to the previous grid until it is done
+    if (xg) {
+      // bf16(gelu(X)) of this CTA's chunks in the MMA's K-major 128-byte
+      // swizzle: row b, 16-byte chunk c of a 2 KB tile at b * 128 + (c ^ (b & 7)) * 16
+      const int et = threadIdx.x - 64, nslots = min(p.KC, u1 - u0);
+      for (int sl = 0; sl < nslots; sl++) {
+        const int kc = (kc_first + sl) % p.KC;
+        for (int e = et; e < MB * 8; e += 128) {
+          const int b = e >> 3, ch = e & 7, k0 = kc * kSkBK + ch * 8;
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            float v0 = 0.0f, v1 = 0.0f;
+            if (b < p.M && k0 + 2 * j < p.K) v0 = gelu_tanh(p.xf[(int64_t)b * p.ld_x + k0 + 2 * j]);
+            if (b < p.M && k0 + 2 * j + 1 < p.K) v1 = gelu_tanh(p.xf[(int64_t)b * p.ld_x + k0 + 2 * j + 1]);
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            w[j] = *reinterpret_cast<const uint32_t *>(&h2);
+          }
+          *reinterpret_cast<uint4 *>(xs + sl * kXTile + b * 128 + ((ch ^ (b & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_ready);
+    }
     const int q = warp & 3, row = q * 32 + lane;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const int Mv = p.M < MB ? p.M : MB;
@@ -243,7 +303,17 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
       const int n = t * kSkBM + row;
-      if (u == t * p.KC && uend == (t + 1) * p.KC) {   // the whole row tile: finish it here
+      if (p.flags & SM100_SK_ACCUM) {
+        // y += this run's sums (the run holding k-chunk 0 adds the bias); the
+        // reductions are fire-and-forget, the next kernel sees them complete
+        if (n < p.N) {
+          const float bias = (p.bias && u == t * p.KC) ? p.bias[n] : 0.0f;
+          float *yc = reinterpret_cast<float *>(p.y) + n;
+#pragma unroll
+          for (int b = 0; b < MB; b++)
+            if (b < Mv) atomicAdd(yc + (int64_t)b * p.ld_y, v[b] + bias);
+        }
+      } else if (u == t * p.KC && uend == (t + 1) * p.KC) {   // the whole row tile: finish it here
         if (n < p.N) {
 #pragma unroll
           for (int b = 0; b < MB; b++)
@@ -318,6 +388,187 @@ __global__ void __launch_bounds__(kSkThreads, 1)
   }
 }
 
+
+// Cluster split-K (the default path): grid = C clusters x S CTAs.  With S > 1
+// each cluster owns one row tile and its S CTAs stream S contiguous parts of
+// its k-chunks; each CTA leaves its partial sums in its own shared memory, the
+// cluster synchronises, and CTA 0 of the cluster adds the S partials in rank
+// order over distributed shared memory (deterministic) and runs the full
+// epilogue.  With S = 1 the clusters are single CTAs walking tiles c, c + C...
+template <int MB>
+__global__ void __launch_bounds__(kSkThreads, 1)
+    skinny_cl_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_x,
+                     const SkParams p, int S) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int kStage = sk_stage_bytes<MB>();
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kSkStages * kStage);
+  uint64_t *full = bars, *empty = bars + kSkStages, *acc_full = bars + 2 * kSkStages, *acc_empty = acc_full + 2;
+  uint64_t *done = acc_empty + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  float *pbuf = reinterpret_cast<float *>(smem);   // S > 1: this CTA's partial [MB][128], over ring stage 0
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)(blockIdx.x % S), cl = (int)(blockIdx.x / S), ncl = (int)(gridDim.x / S);
+  const int kc0 = (rank * p.KC) / S, kc1 = ((rank + 1) * p.KC) / S, nk = kc1 - kc0;
+  uint32_t *status = &g_skinny_status;
+
+  pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSkStages; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(2 * MB)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // chunk i of this CTA: tile cl + (i / nk) * ncl, k-chunk kc0 + i % nk
+      const int n_tiles = nk > 0 ? (p.T - cl + ncl - 1) / ncl : 0, total = n_tiles * nk;
+      const int pre = min(kSkStages, total);
+      for (int i = 0; i < pre; i++) {
+        mbar_expect_tx(&full[i], kStage);
+        sk_tma_2d(smem + i * kStage, &map_w, (kc0 + i % nk) * kSkBK, (cl + (i / nk) * ncl) * kSkBM, &full[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; i++)
+        sk_tma_2d(smem + i * kStage + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[i]);
+      int i = pre;
+      for (; i < total; i++) {
+        const int s = i % kSkStages;
+        if (!mbar_wait(&empty[s], (uint32_t)(((i / kSkStages) - 1) & 1), status)) break;
+        unsigned char *st = smem + s * kStage;
+        mbar_expect_tx(&full[s], kStage);
+        sk_tma_2d(st, &map_w, (kc0 + i % nk) * kSkBK, (cl + (i / nk) * ncl) * kSkBM, &full[s]);
+        sk_tma_2d(st + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[s]);
+      }
+      for (int k = i - kSkStages > 0 ? i - kSkStages : 0; k < i; k++)
+        mbar_wait(&full[k % kSkStages], (uint32_t)((k / kSkStages) & 1), status, false);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MB >> 3) << 17) |
+                                 ((uint32_t)(kSkBM >> 4) << 24);
+      int i = 0, run = 0;
+      bool ok = true;
+      for (int t = cl; t < p.T && nk > 0 && ok; t += ncl, run++) {
+        const int a = run & 1;
+        if (run >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((run >> 1) - 1) & 1), status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int k = 0; k < nk; k++, i++) {
+          const int s = i % kSkStages;
+          if (!mbar_wait(&full[s], (uint32_t)((i / kSkStages) & 1), status)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const unsigned char *st = smem + s * kStage;
+#pragma unroll
+          for (int kk = 0; kk < kSkBK / 16; kk++) {
+            const uint32_t acc = (k > 0 || kk > 0) ? 1u : 0u;
+            asm volatile(
+                "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * MB)),
+                "l"(sk_desc(st) + 2 * kk), "l"(sk_desc(st + kSkWBytes) + 2 * kk), "r"(idesc), "r"(acc)
+                : "memory");
+          }
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(&empty[s]))
+                       : "memory");
+        }
+        if (!ok) break;
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&acc_full[a]))
+                     : "memory");
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(done))
+                   : "memory");
+    }
+  } else {
+    pdl_wait();
+    const int q = warp & 3, row = q * 32 + lane;
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    const int Mv = p.M < MB ? p.M : MB;
+    int run = 0;
+    for (int t = cl; t < p.T && nk > 0; t += ncl, run++) {
+      const int a = run & 1;
+      if (!sk_bar_and(2, 128, mbar_wait(&acc_full[a], (uint32_t)((run >> 1) & 1), status))) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      float v[MB];
+      sk_tmem_ld<MB>(tq + (uint32_t)(a * MB), v);
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      const int n = t * kSkBM + row;
+      if (S == 1) {
+        if (n < p.N) {
+#pragma unroll
+          for (int b = 0; b < MB; b++)
+            if (b < Mv) sk_store(p, b, n, v[b]);
+        }
+      } else {
+        // the ring is idle now (all products done): the partial goes over stage 0
+#pragma unroll
+        for (int b = 0; b < MB; b++) pbuf[b * kSkBM + row] = v[b];
+      }
+    }
+    if (nk == 0 && S > 1)   // an empty part contributes zeros
+      for (int b = 0; b < MB; b++) pbuf[b * kSkBM + row] = 0.0f;
+  }
+  if (S > 1) {
+    // every CTA of the cluster has its partial in shared memory (warps
+    // reconverge first: the cluster barrier is warp-aligned)
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+    if (rank == 0 && warp >= 2) {
+      const int row = (warp & 3) * 32 + lane, n = cl * kSkBM + row;
+      const int Mv = p.M < MB ? p.M : MB;
+      float acc[MB];
+#pragma unroll
+      for (int b = 0; b < MB; b++) acc[b] = 0.0f;
+      const uint32_t local = smem_u32(pbuf);
+      for (int r = 0; r < S; r++) {
+        uint32_t remote;
+        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(r));
+#pragma unroll
+        for (int b = 0; b < MB; b++) {
+          float x;
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(remote + (uint32_t)((b * kSkBM + row) * 4)));
+          acc[b] += x;
+        }
+      }
+      if (n < p.N) {
+#pragma unroll
+        for (int b = 0; b < MB; b++)
+          if (b < Mv) sk_store(p, b, n, acc[b]);
+      }
+    }
+    // the partials stay readable until CTA 0 is done with them
+    __syncwarp();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    if (lane == 0) mbar_wait(done, 0, status, false);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * MB) : "memory");
+  }
+}
+
 typedef CUresult (*SkEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -363,14 +614,45 @@ static int sk_launch(const Sm100SkinnyArgs *a, cudaStream_t st) {
   p.kv = reinterpret_cast<__nv_bfloat16 *>(a->kv_cache);
   p.pos = a->pos;
   p.kv_ctx = a->kv_ctx;
+  p.xf = reinterpret_cast<const float *>(a->x);
+  p.ld_x = a->ld_x ? a->ld_x : a->K;
+  p.xslots = (a->flags & SM100_SK_X_GELU) ? std::min(p.KC, (p.U + p.G - 1) / p.G) : 0;
   CUtensorMap mw, mx;
+  memset(&mx, 0, sizeof mx);
   if (!sk_map(&mw, a->w, a->N, a->K, a->ld_w ? a->ld_w : a->K, kSkBM) ||
-      !sk_map(&mx, a->x, a->M, a->K, a->ld_x ? a->ld_x : a->K, MB))
+      (!(a->flags & SM100_SK_X_GELU) && !sk_map(&mx, a->x, a->M, a->K, a->ld_x ? a->ld_x : a->K, MB)))
     return sm100_set_error(SM100_ERR_CUDA, "skinny: tensor map encoding failed");
-  constexpr int smem = sk_smem<MB>();
+  if (!(a->flags & (SM100_SK_ACCUM | SM100_SK_X_GELU))) {
+    // cluster split-K: S parts per row tile so that T x S fills the SMs (S <= 8)
+    const int S = std::max(1, std::min(8, kSkMaxGrid / p.T));
+    const int ncl = S > 1 ? p.T : std::min(p.T, kSkMaxGrid);
+    const int smem = sk_smem<MB>();
+    cudaError_t e = cudaFuncSetAttribute(skinny_cl_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "skinny: smem attribute: %s", cudaGetErrorString(e));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(ncl * S);
+    cfg.blockDim = dim3(kSkThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)S;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, skinny_cl_kernel<MB>, mw, mx, p, S);
+    if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "skinny: launch: %s", cudaGetErrorString(e));
+    return launch_status("skinny");
+  }
+  const int smem = sk_smem<MB>(p.xslots);
+  if (smem > 227 * 1024) return sm100_set_error(SM100_ERR_ARG, "skinny: %d X chunks do not fit", p.xslots);
   cudaError_t e = cudaFuncSetAttribute(skinny_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "skinny: smem attribute: %s", cudaGetErrorString(e));
-  skinny_kernel<MB><<<p.G, kSkThreads, smem, st>>>(mw, mx, p);
+  e = launch_pdl(skinny_kernel<MB>, dim3(p.G), dim3(kSkThreads), smem, st, mw, mx, p);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "skinny: launch: %s", cudaGetErrorString(e));
   return launch_status("skinny");
 }
 
@@ -385,7 +667,9 @@ extern "C" int sm100_skinny_bf16(const Sm100SkinnyArgs *a, void *stream) {
       a->K > (1 << 30) || (a->K % 8) || ((a->ld_w ? a->ld_w : a->K) % 8) || ((a->ld_x ? a->ld_x : a->K) % 8) ||
       ((uintptr_t)a->x & 15) || ((uintptr_t)a->w & 15) || !a->ws || !a->counters ||
       ((a->flags & SM100_SK_RESIDUAL) && !a->residual) ||
-      ((a->flags & SM100_SK_KV) && (!a->kv_cache || !a->pos || a->kv_ctx < 1 || a->N % 3)))
+      ((a->flags & SM100_SK_KV) && (!a->kv_cache || !a->pos || a->kv_ctx < 1 || a->N % 3)) ||
+      ((a->flags & SM100_SK_ACCUM) && (a->flags & (SM100_SK_GELU | SM100_SK_RESIDUAL | SM100_SK_OUT_BF16 | SM100_SK_KV))) ||
+      ((a->flags & SM100_SK_X_GELU) && ((uintptr_t)a->x & 3)))
     return sm100_set_error(SM100_ERR_ARG, "skinny: M %lld N %lld K %lld (M <= 32, K %% 8 == 0, aligned, workspace)",
                            (long long)(a ? a->M : 0), (long long)(a ? a->N : 0), (long long)(a ? a->K : 0));
   return a->M <= 16 ? sk_launch<16>(a, (cudaStream_t)stream) : sk_launch<32>(a, (cudaStream_t)stream);

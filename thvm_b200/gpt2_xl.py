@@ -164,7 +164,7 @@ class XLModel:
         self.xa = z(B, D, dt=torch.int16)          # bf16 LayerNorm outputs
         self.qkv = z(B, 3 * C)
         self.att = z(B, C, dt=torch.int16)
-        self.g = z(B, Fl, dt=torch.int16)
+        self.g = z(B, Fl, dt=torch.int16)            # bf16 gelu(c_fc)
         self.logits = z(B, Vl)
         self.kv = [z(2, B, ctx, C, dt=torch.int16) for _ in range(cfg.n_layers)]
         self.tok = z(B, dt=torch.int32)
@@ -197,9 +197,11 @@ class XLModel:
         L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
         self.launches += 1
 
-    def _ln(self, g, b):
+    def _ln(self, g, b, zero_h=False, zero_buf=None):
+        zp, zn = (zero_buf.data_ptr(), zero_buf.numel()) if zero_buf is not None else (None, 0)
         L.check(self.lib.sm100_xl_layernorm(self.h.data_ptr(), g.data_ptr(), b.data_ptr(), self.xa.data_ptr(),
-                                            self.cfg.batch, self.cfg.dim, self.cfg.norm_eps, self._stream()),
+                                            self.cfg.batch, self.cfg.dim, self.cfg.norm_eps, 1 if zero_h else 0,
+                                            zp, zn, self._stream()),
                 "xl_layernorm")
         self.launches += 1
 
@@ -223,9 +225,10 @@ class XLModel:
             self._skinny(self.xa, w[p + "attn.w"], self.qkv, D, 3 * C, bias=w[p + "attn.b"], flags=L.SK_KV,
                          kv=self.kv[i])
             L.check(lib.sm100_xl_attention(self.qkv.data_ptr(), 3 * C, self.kv[i].data_ptr(), self.pos.data_ptr(),
-                                           self.att.data_ptr(), B, sh.h1 - sh.h0, HEAD_DIM, cfg.max_ctx, scale,
+                                           self.att.data_ptr(), B, sh.h1 - sh.h0, HEAD_DIM, cfg.max_ctx, scale, 0,
                                            self._stream()), "xl_attention")
             self.launches += 1
+            # row-split: rank 0 adds bias + residual, the others leave their partial in h
             self._skinny(self.att, w[p + "proj.w"], self.h, C, D, bias=w[p + "proj.b"] if first else None,
                          residual=self.h if first else None, flags=res)
             self._all_reduce(self.h)
@@ -236,9 +239,9 @@ class XLModel:
             self._all_reduce(self.h)
         self._ln(w["ln_f.w"], w["ln_f.b"])
         Vl = sh.v1 - sh.v0
-        self._skinny(self.xa, w["lm_head"], self.logits, D, Vl)
+        self._skinny(self.xa, w["lm_head"], self.logits, D, Vl, flags=0)
         L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), Vl, B, Vl, self.val_me.data_ptr(),
-                                    self.idx_me.data_ptr(), sh.v0, self._stream()), "xl_argmax")
+                                    self.idx_me.data_ptr(), sh.v0, 0, self._stream()), "xl_argmax")
         self.launches += 1
         if sh.world > 1:
             dist = self.torch.distributed
