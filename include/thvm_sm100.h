@@ -359,7 +359,8 @@ enum {
   SM100_SK_OUT_BF16 = 1u << 2,
   SM100_SK_KV = 1u << 3,
   SM100_SK_ACCUM = 1u << 4,   /* y (f32) += X W^T (+ bias once), unordered reductions; alone */
-  SM100_SK_X_GELU = 1u << 5   /* x is f32 [M, K]: the product uses bf16(gelu(x)) */
+  SM100_SK_X_GELU = 1u << 5,  /* x is f32 [M, K]: the product uses bf16(gelu(x)) */
+  SM100_SK_X_LN = 1u << 6     /* x is f32 [M, K]: the product uses bf16(LayerNorm(x) * ln_g + ln_b) */
 };
 typedef struct {
   const void *x;          /* [M, K] bf16, row stride ld_x (0: K) */
@@ -373,6 +374,8 @@ typedef struct {
   const int32_t *pos;     /* SM100_SK_KV: device row of the cache to write */
   int64_t M, N, K, ld_x, ld_w, ld_res, ld_y;
   int32_t flags, kv_ctx;
+  const float *ln_g, *ln_b; /* SM100_SK_X_LN: the LayerNorm affine over K */
+  float eps;
 } Sm100SkinnyArgs;
 /* M in [1, 32]; K % 8 == 0; x and w 16-byte aligned.  Launches on stream. */
 int sm100_skinny_bf16(const Sm100SkinnyArgs *a, void *stream);

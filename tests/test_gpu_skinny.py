@@ -133,6 +133,36 @@ def test_skinny_x_gelu(device):
         close(y, O.gemm_bf16(O.to_bf16(O.gelu(xf)), w) + b)
 
 
+@pytest.mark.parametrize("M,N,K", [(16, 4800, 1600), (16, 6400, 1600), (16, 50257, 1600), (7, 640, 320)])
+def test_skinny_x_layernorm(device, M, N, K):
+    """SM100_SK_X_LN: the f32 operand enters the product as bf16(LayerNorm(x) * g + b), computed
+    inside the GEMM (the ln_1 / ln_2 / ln_f before c_attn, c_fc and lm_head).  A LayerNorm output
+    one f32 rounding from a bf16 tie may round the other way: 1e-3 of the scale."""
+    import ctypes as C
+    from thvm_b200 import _lib as L
+    rng = np.random.default_rng(M + N)
+    xf = (rng.standard_normal((M, K)) * 3 + 0.5).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(K)).astype(np.float32)
+    bb = (0.1 * rng.standard_normal(K)).astype(np.float32)
+    _, w, b = operands(M, N, K, 9)
+    ids = {"x": device.upload(xf), "w": device.upload(w), "bias": device.upload(b), "y": device.alloc(M * N * 4),
+           "ws": device.alloc(device.lib.sm100_skinny_ws_bytes(M)), "counters": device.alloc(((N + 127) // 128) * 4),
+           "g": device.upload(g), "bb": device.upload(bb)}
+    a = L.Sm100SkinnyArgs()
+    for k in ("x", "w", "bias", "y", "ws", "counters"):
+        setattr(a, k, device.dptr(ids[k]))
+    a.ln_g, a.ln_b, a.eps = device.dptr(ids["g"]), device.dptr(ids["bb"]), 1e-5
+    a.M, a.N, a.K, a.flags = M, N, K, L.SK_X_LN
+    L.check(device.lib.sm100_skinny_bf16(C.byref(a), device.stream), "skinny")
+    device.sync()
+    assert device.lib.sm100_skinny_status() == 0
+    y = device.read(ids["y"], np.float32, (M, N))
+    for v in ids.values():
+        device.free(v)
+    ln = O.layernorm(xf, g, bb, 1e-5)
+    close(y, O.gemm_bf16(O.to_bf16(ln), w) + b, tol=1e-3)
+
+
 def test_skinny_rejects(device):
     from thvm_b200 import _lib as L
     a = L.Sm100SkinnyArgs()

@@ -68,13 +68,13 @@ class Sm100AttnArgs(ctypes.Structure):
         ("scale", c_float)]
 
 
-SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV, SK_ACCUM, SK_X_GELU = 1, 2, 4, 8, 16, 32
+SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV, SK_ACCUM, SK_X_GELU, SK_X_LN = 1, 2, 4, 8, 16, 32, 64
 
 
 class Sm100SkinnyArgs(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("x", "w", "bias", "residual", "y", "ws", "counters", "kv_cache", "pos")] + [
         (n, c_int64) for n in ("M", "N", "K", "ld_x", "ld_w", "ld_res", "ld_y")] + [
-        ("flags", c_int32), ("kv_ctx", c_int32)]
+        ("flags", c_int32), ("kv_ctx", c_int32), ("ln_g", c_void_p), ("ln_b", c_void_p), ("eps", c_float)]
 
 
 _PL = ctypes.c_void_p * DECODE_MAX_LAYERS

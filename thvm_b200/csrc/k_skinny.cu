@@ -28,7 +28,9 @@
 // the part holding k-chunk 0 the bias) into y with fire-and-forget
 // reductions, leaving the remaining epilogue to the consumer kernel.
 // SM100_SK_X_GELU takes X as f32 and feeds bf16(gelu(X)) to the MMA, staged in
-// shared memory by the epilogue warps before the products start.
+// shared memory by the epilogue warps before the products start;
+// SM100_SK_X_LN likewise feeds bf16(LayerNorm(X)), so the LayerNorm before a
+// projection needs no kernel of its own.
 // Every wait is bounded; a timeout sets g_skinny_status.
 #include <cuda.h>
 
@@ -74,6 +76,8 @@ struct SkParams {
   const float *xf;
   int64_t ld_x;
   int xslots;   // X chunks held per CTA (min(KC, most units of a CTA))
+  const float *ln_g, *ln_b;   // SM100_SK_X_LN
+  float eps;
 };
 
 __device__ __forceinline__ void sk_tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -401,15 +405,18 @@ __global__ void __launch_bounds__(kSkThreads, 1)
                      const SkParams p, int S) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  constexpr int kStage = sk_stage_bytes<MB>();
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kSkStages * kStage);
+  constexpr int kStage = sk_stage_bytes<MB>(), kXTile = MB * kSkBK * 2;
+  const bool xln = (p.flags & SM100_SK_X_LN) != 0;
+  unsigned char *xs = smem + kSkStages * kStage;   // X_LN: this CTA's k-chunks of bf16(LayerNorm(x))
+  uint64_t *bars = reinterpret_cast<uint64_t *>(xs + (xln ? p.xslots : 0) * kXTile);
   uint64_t *full = bars, *empty = bars + kSkStages, *acc_full = bars + 2 * kSkStages, *acc_empty = acc_full + 2;
-  uint64_t *done = acc_empty + 2;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  uint64_t *done = acc_empty + 2, *x_ready = done + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(x_ready + 1);
   float *pbuf = reinterpret_cast<float *>(smem);   // S > 1: this CTA's partial [MB][128], over ring stage 0
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = (int)(blockIdx.x % S), cl = (int)(blockIdx.x / S), ncl = (int)(gridDim.x / S);
   const int kc0 = (rank * p.KC) / S, kc1 = ((rank + 1) * p.KC) / S, nk = kc1 - kc0;
+
   uint32_t *status = &g_skinny_status;
 
   pdl_trigger();
@@ -423,6 +430,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       mbar_init(&acc_empty[i], 4);
     }
     mbar_init(done, 1);
+    mbar_init(x_ready, 4);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -441,21 +449,23 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       // chunk i of this CTA: tile cl + (i / nk) * ncl, k-chunk kc0 + i % nk
       const int n_tiles = nk > 0 ? (p.T - cl + ncl - 1) / ncl : 0, total = n_tiles * nk;
       const int pre = min(kSkStages, total);
+      const uint32_t tx = xln ? kSkWBytes : kStage;
       for (int i = 0; i < pre; i++) {
-        mbar_expect_tx(&full[i], kStage);
+        mbar_expect_tx(&full[i], tx);
         sk_tma_2d(smem + i * kStage, &map_w, (kc0 + i % nk) * kSkBK, (cl + (i / nk) * ncl) * kSkBM, &full[i]);
       }
       pdl_wait();
-      for (int i = 0; i < pre; i++)
-        sk_tma_2d(smem + i * kStage + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[i]);
+      if (!xln)
+        for (int i = 0; i < pre; i++)
+          sk_tma_2d(smem + i * kStage + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[i]);
       int i = pre;
       for (; i < total; i++) {
         const int s = i % kSkStages;
         if (!mbar_wait(&empty[s], (uint32_t)(((i / kSkStages) - 1) & 1), status)) break;
         unsigned char *st = smem + s * kStage;
-        mbar_expect_tx(&full[s], kStage);
+        mbar_expect_tx(&full[s], tx);
         sk_tma_2d(st, &map_w, (kc0 + i % nk) * kSkBK, (cl + (i / nk) * ncl) * kSkBM, &full[s]);
-        sk_tma_2d(st + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[s]);
+        if (!xln) sk_tma_2d(st + kSkWBytes, &map_x, (kc0 + i % nk) * kSkBK, 0, &full[s]);
       }
       for (int k = i - kSkStages > 0 ? i - kSkStages : 0; k < i; k++)
         mbar_wait(&full[k % kSkStages], (uint32_t)((k / kSkStages) & 1), status, false);
@@ -465,7 +475,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
       constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(MB >> 3) << 17) |
                                  ((uint32_t)(kSkBM >> 4) << 24);
       int i = 0, run = 0;
-      bool ok = true;
+      bool ok = !xln || nk == 0 || mbar_wait(x_ready, 0, status);
       for (int t = cl; t < p.T && nk > 0 && ok; t += ncl, run++) {
         const int a = run & 1;
         if (run >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((run >> 1) - 1) & 1), status)) break;
@@ -475,13 +485,14 @@ __global__ void __launch_bounds__(kSkThreads, 1)
           if (!mbar_wait(&full[s], (uint32_t)((i / kSkStages) & 1), status)) { ok = false; break; }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           const unsigned char *st = smem + s * kStage;
+          const unsigned char *xt = xln ? xs + k * kXTile : st + kSkWBytes;
 #pragma unroll
           for (int kk = 0; kk < kSkBK / 16; kk++) {
             const uint32_t acc = (k > 0 || kk > 0) ? 1u : 0u;
             asm volatile(
                 "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * MB)),
-                "l"(sk_desc(st) + 2 * kk), "l"(sk_desc(st + kSkWBytes) + 2 * kk), "r"(idesc), "r"(acc)
+                "l"(sk_desc(st) + 2 * kk), "l"(sk_desc(xt) + 2 * kk), "r"(idesc), "r"(acc)
                 : "memory");
           }
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -498,6 +509,46 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     }
   } else {
     pdl_wait();
+    if (xln && nk > 0) {
+      // bf16(LayerNorm(x) * g + b) of this CTA's k-chunks, in the MMA's K-major
+      // 128-byte swizzle (row b, 16-byte chunk c of a tile at b * 128 + (c ^ (b & 7)) * 16).
+      // Statistics over the whole row as src/nn/layernorm.c:1-7: mean = sum *
+      // (1/K), var = sum((x - mean)^2) * (1/K), 1/sqrt(var + eps); a warp per row.
+      const float inv_k = 1.0f / (float)p.K;
+      for (int b = warp - 2; b < MB; b += 4) {
+        const float *xr = p.xf + (int64_t)b * p.ld_x;
+        float mean = 0.0f, r = 0.0f;
+        if (b < p.M) {
+          float s1 = 0.0f;
+          for (int k = lane; k < p.K; k += 32) s1 += xr[k];
+          mean = warp_sum(s1) * inv_k;
+          float s2 = 0.0f;
+          for (int k = lane; k < p.K; k += 32) {
+            const float d = xr[k] - mean;
+            s2 += d * d;
+          }
+          r = 1.0f / sqrtf(warp_sum(s2) * inv_k + p.eps);
+        }
+        for (int e = lane; e < nk * 8; e += 32) {   // 16-byte chunks: 8 per k-chunk
+          const int kc = e >> 3, ch = e & 7, k0 = (kc0 + kc) * kSkBK + ch * 8;
+          uint32_t w[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            float v0 = 0.0f, v1 = 0.0f;
+            const int ka = k0 + 2 * j, kb = ka + 1;
+            if (b < p.M && ka < p.K) v0 = (xr[ka] - mean) * r * p.ln_g[ka] + p.ln_b[ka];
+            if (b < p.M && kb < p.K) v1 = (xr[kb] - mean) * r * p.ln_g[kb] + p.ln_b[kb];
+            const __nv_bfloat162 h2 = __floats2bfloat162_rn(v0, v1);
+            w[j] = *reinterpret_cast<const uint32_t *>(&h2);
+          }
+          *reinterpret_cast<uint4 *>(xs + kc * kXTile + b * 128 + ((ch ^ (b & 7)) * 16)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(x_ready);
+    }
     const int q = warp & 3, row = q * 32 + lane;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     const int Mv = p.M < MB ? p.M : MB;
@@ -620,13 +671,19 @@ static int sk_launch(const Sm100SkinnyArgs *a, cudaStream_t st) {
   CUtensorMap mw, mx;
   memset(&mx, 0, sizeof mx);
   if (!sk_map(&mw, a->w, a->N, a->K, a->ld_w ? a->ld_w : a->K, kSkBM) ||
-      (!(a->flags & SM100_SK_X_GELU) && !sk_map(&mx, a->x, a->M, a->K, a->ld_x ? a->ld_x : a->K, MB)))
+      (!(a->flags & (SM100_SK_X_GELU | SM100_SK_X_LN)) &&
+       !sk_map(&mx, a->x, a->M, a->K, a->ld_x ? a->ld_x : a->K, MB)))
     return sm100_set_error(SM100_ERR_CUDA, "skinny: tensor map encoding failed");
   if (!(a->flags & (SM100_SK_ACCUM | SM100_SK_X_GELU))) {
     // cluster split-K: S parts per row tile so that T x S fills the SMs (S <= 8)
     const int S = std::max(1, std::min(8, kSkMaxGrid / p.T));
     const int ncl = S > 1 ? p.T : std::min(p.T, kSkMaxGrid);
-    const int smem = sk_smem<MB>();
+    p.xslots = (a->flags & SM100_SK_X_LN) ? (p.KC + S - 1) / S : 0;
+    p.ln_g = a->ln_g;
+    p.ln_b = a->ln_b;
+    p.eps = a->eps;
+    const int smem = sk_smem<MB>(p.xslots);
+    if (smem > 227 * 1024) return sm100_set_error(SM100_ERR_ARG, "skinny: %d LayerNorm chunks do not fit", p.xslots);
     cudaError_t e = cudaFuncSetAttribute(skinny_cl_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "skinny: smem attribute: %s", cudaGetErrorString(e));
     cudaLaunchConfig_t cfg = {};
@@ -669,7 +726,8 @@ extern "C" int sm100_skinny_bf16(const Sm100SkinnyArgs *a, void *stream) {
       ((a->flags & SM100_SK_RESIDUAL) && !a->residual) ||
       ((a->flags & SM100_SK_KV) && (!a->kv_cache || !a->pos || a->kv_ctx < 1 || a->N % 3)) ||
       ((a->flags & SM100_SK_ACCUM) && (a->flags & (SM100_SK_GELU | SM100_SK_RESIDUAL | SM100_SK_OUT_BF16 | SM100_SK_KV))) ||
-      ((a->flags & SM100_SK_X_GELU) && ((uintptr_t)a->x & 3)))
+      ((a->flags & SM100_SK_X_GELU) && ((uintptr_t)a->x & 3)) ||
+      ((a->flags & SM100_SK_X_LN) && (!a->ln_g || !a->ln_b || (a->flags & (SM100_SK_ACCUM | SM100_SK_X_GELU)))))
     return sm100_set_error(SM100_ERR_ARG, "skinny: M %lld N %lld K %lld (M <= 32, K %% 8 == 0, aligned, workspace)",
                            (long long)(a ? a->M : 0), (long long)(a ? a->N : 0), (long long)(a ? a->K : 0));
   return a->M <= 16 ? sk_launch<16>(a, (cudaStream_t)stream) : sk_launch<32>(a, (cudaStream_t)stream);

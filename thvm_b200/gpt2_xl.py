@@ -183,7 +183,7 @@ class XLModel:
     def _stream(self):
         return ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
 
-    def _skinny(self, x, w, y, K, N, bias=None, residual=None, flags=0, kv=None):
+    def _skinny(self, x, w, y, K, N, bias=None, residual=None, flags=0, kv=None, ln=None):
         a = self._args
         a.x, a.w, a.y = x.data_ptr(), w.data_ptr(), y.data_ptr()
         a.bias = bias.data_ptr() if bias is not None else None
@@ -194,6 +194,11 @@ class XLModel:
         a.M, a.N, a.K = self.cfg.batch, N, K
         a.ld_x = a.ld_w = a.ld_res = a.ld_y = 0
         a.flags, a.kv_ctx = flags, self.cfg.max_ctx
+        if ln is not None:   # the operand is bf16(LayerNorm(x)), computed inside the GEMM
+            a.flags |= L.SK_X_LN
+            a.ln_g, a.ln_b, a.eps = ln[0].data_ptr(), ln[1].data_ptr(), self.cfg.norm_eps
+        else:
+            a.ln_g = a.ln_b = None
         L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
         self.launches += 1
 
@@ -239,7 +244,7 @@ class XLModel:
             self._all_reduce(self.h)
         self._ln(w["ln_f.w"], w["ln_f.b"])
         Vl = sh.v1 - sh.v0
-        self._skinny(self.xa, w["lm_head"], self.logits, D, Vl, flags=0)
+        self._skinny(self.xa, w["lm_head"], self.logits, D, Vl)
         L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), Vl, B, Vl, self.val_me.data_ptr(),
                                     self.idx_me.data_ptr(), sh.v0, 0, self._stream()), "xl_argmax")
         self.launches += 1
