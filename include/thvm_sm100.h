@@ -410,6 +410,42 @@ int sm100_xl_argmax(float *x, int64_t ld, int32_t M, int32_t N, float *val, int3
 /* tok[b] = index of the largest of R candidates val/idx [R][B] (ties: smaller index) */
 int sm100_xl_pick(const float *val, const int32_t *idx, int32_t R, int32_t B, int32_t *tok, void *stream);
 
+/* ---- the batched MoE decode step pieces (config 5) ------------------------ */
+/* DeepSeek-V2-Lite-shaped decode of B <= 32 sequences (bench/dsv2_decode_bench.c
+ * :341-1110 at batch 1): f32 residual stream, bf16 matmul operands, bf16
+ * compressed KV cache (latent [B, ctx, KV] and rotary [B, ctx, DR]), fp8-e4m3
+ * experts with 128 x 128 f32 block scales.  Device pointers; launch on stream. */
+/* y (bf16) = x * rsqrt(mean(x^2) + eps) * g per row */
+int sm100_ds_rmsnorm(const float *x, const float *g, void *y, int32_t M, int32_t D, float eps, void *stream);
+/* h[b] = emb[tok[b]] (bf16 table; ids outside [0, V) read zeros) */
+int sm100_ds_embed(const void *emb, const int32_t *tok, float *h, int32_t B, int32_t V, int32_t D, void *stream);
+/* q rows [H][DN + DR] -> q_out bf16 (pe rotated by the cos / sin tables [ctx][DR]
+ * at row *pos); kva rows [KV + DR] -> RMSNorm(latent) * g_kv and rotated pe
+ * appended at cache row *pos.  q and kva rows have stride ld (elements). */
+int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, const float *g_kv, const float *cos_t,
+                      const float *sin_t, const int32_t *pos, void *q_out, void *cache_c, void *cache_pe,
+                      int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t KV, int32_t ctx, float eps,
+                      void *stream);
+/* absorbed multi-head latent attention over cache rows 0..*pos; w_uk / w_uv
+ * bf16 [H][DN or DV][KV]; o bf16 [B][H * DV] */
+int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c, const void *cache_pe,
+                 const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV,
+                 int32_t ctx, float scale, void *stream);
+/* softmax over E <= 64 router logits, the K largest (ties: lowest id), no
+ * renormalisation; sel / wsel [B][K]; slot lists of the experts [e0, e1):
+ * slot_off [e1 - e0 + 1], slot_tok / slot_w [B * K] (expert-major) */
+int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t *sel,
+                   float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
+/* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
+ * experts: w_gu fp8 [n_exp][2I][D] + scales [n_exp][ceil(2I/128)][D/128],
+ * w_d fp8 [n_exp][D][I] + scales [n_exp][D/128][ceil(I/128)]; x bf16 [B][D];
+ * a_scratch bf16 [slots][I]; y f32 [B][D] (float reductions) */
+int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,
+                     const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch, float *y,
+                     int32_t n_exp, int32_t D, int32_t I, void *stream);
+/* a (bf16 [M][I]) = silu(gu[:, :I]) * gu[:, I:] of f32 gate|up rows [M][2I] */
+int sm100_ds_silu_mul(const float *gu, void *a, int32_t M, int32_t I, void *stream);
+
 /* ---- causal attention prefill on the tensor cores ------------------------ */
 /* O[B, H, S, D] (f32) = softmax(Q K^T * scale + causal mask) V for bf16 Q, K, V
  * [B, H, S, D] contiguous, D = 128, any S >= 0: the reference's

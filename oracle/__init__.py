@@ -310,5 +310,59 @@ class XLModel:
         return lg, nxt
 
 
+class _OrcDS(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "dim", "n_layers", "heads", "kv_lora", "d_nope", "d_rope", "d_v", "n_exp", "top_k", "moe_inter",
+        "dense_inter", "n_dense", "n_shared", "vocab", "max_ctx", "batch")] + [
+        ("eps", ctypes.c_float), ("scale", ctypes.c_float)] + [
+        (n, ctypes.c_void_p) for n in ("embed", "lm_head", "norm_f", "cos_t", "sin_t")] + [
+        (n, ctypes.POINTER(ctypes.c_void_p)) for n in (
+            "attn_norm", "kv_norm", "ffn_norm", "w_qkva", "w_uk", "w_uv", "w_o", "d_gu", "d_down", "router",
+            "e_gu", "e_d", "e_gu_s", "e_d_s")]
+
+
+class DSModel:
+    """The oracle's batched MoE decode step (orc_ds_step) over the weight dict
+    of thvm_b200.dsv2.ds_weights (bf16 bits uint16, fp8 codes uint8, f32)."""
+
+    _per_layer = {"attn_norm": "attn_norm", "kv_norm": "kv_norm", "ffn_norm": "ffn_norm", "w_qkva": "w_qkva",
+                  "w_uk": "w_uk", "w_uv": "w_uv", "w_o": "w_o", "d_gu": "d_gu", "d_down": "d_down",
+                  "router": "router", "e_gu": "e_gu", "e_d": "e_d", "e_gu_s": "e_gu_s", "e_d_s": "e_d_s"}
+
+    def __init__(self, cfg, weights: dict, cos_t, sin_t):
+        self.cfg = cfg
+        self._keep = {k: np.ascontiguousarray(v) for k, v in weights.items()}
+        self._keep["cos"], self._keep["sin"] = np.ascontiguousarray(cos_t), np.ascontiguousarray(sin_t)
+        w = self._keep
+        s = _OrcDS(dim=cfg.dim, n_layers=cfg.n_layers, heads=cfg.heads, kv_lora=cfg.kv_lora, d_nope=cfg.d_nope,
+                   d_rope=cfg.d_rope, d_v=cfg.d_v, n_exp=cfg.n_exp, top_k=cfg.top_k, moe_inter=cfg.moe_inter,
+                   dense_inter=cfg.dense_inter, n_dense=cfg.n_dense, n_shared=cfg.n_shared, vocab=cfg.vocab,
+                   max_ctx=cfg.max_ctx, batch=cfg.batch, eps=cfg.eps, scale=cfg.scale)
+        s.embed, s.lm_head, s.norm_f = w["embed"].ctypes.data, w["lm_head"].ctypes.data, w["norm_f"].ctypes.data
+        s.cos_t, s.sin_t = w["cos"].ctypes.data, w["sin"].ctypes.data
+        self._arrays = []
+        for field, suffix in self._per_layer.items():
+            ptrs = [w[f"l{i}.{suffix}"].ctypes.data if f"l{i}.{suffix}" in w else None for i in range(cfg.n_layers)]
+            arr = (ctypes.c_void_p * cfg.n_layers)(*ptrs)
+            self._arrays.append(arr)
+            setattr(s, field, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)))
+        self._s = s
+        self.cache_c = np.zeros((cfg.n_layers, cfg.batch, cfg.max_ctx, cfg.kv_lora), np.uint16)
+        self.cache_pe = np.zeros((cfg.n_layers, cfg.batch, cfg.max_ctx, cfg.d_rope), np.uint16)
+        L = lib()
+        if not getattr(L, "_ds_bound", False):
+            L.orc_ds_step.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int32, ctypes.c_void_p, ctypes.c_void_p]
+            L.orc_ds_step.restype = None
+            L._ds_bound = True
+
+    def step(self, tok, pos: int):
+        t = np.ascontiguousarray(tok, np.int32)
+        lg = np.empty((self.cfg.batch, self.cfg.vocab), np.float32)
+        nxt = np.empty(self.cfg.batch, np.int32)
+        lib().orc_ds_step(ctypes.byref(self._s), self.cache_c.ctypes.data, self.cache_pe.ctypes.data, t.ctypes.data,
+                          pos, lg.ctypes.data, nxt.ctypes.data)
+        return lg, nxt
+
+
 def num_threads() -> int:
     return int(lib().orc_num_threads())

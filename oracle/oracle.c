@@ -599,3 +599,177 @@ out:
   free(e);
   if (!logits) free(lg);
 }
+
+/* ---- batched MoE decode step (oracle.h) ------------------------------------ */
+
+static float bfr_(float v) { return orc_bf16_to_f32(orc_f32_to_bf16(v)); }
+
+static void rms_bf16(const float *x, const float *g, float *y, int64_t M, int64_t D, float eps) {
+  for (int64_t m = 0; m < M; m++) {
+    float ss = 0.0f;
+    for (int64_t i = 0; i < D; i++) ss += x[m * D + i] * x[m * D + i];
+    const float inv = 1.0f / sqrtf(ss * (1.0f / (float)D) + eps);
+    for (int64_t i = 0; i < D; i++) y[m * D + i] = bfr_((x[m * D + i] * inv) * g[i]);
+  }
+}
+
+/* y[m][n] = sum_k x[m][k] * (fp8(w[n][k]) * scale[n/128][k/128]) */
+static void linear_fp8_rows(const float *x, const uint8_t *w, const float *sc, float *y, int64_t M, int64_t K,
+                            int64_t N) {
+  orc_linear_fp8bs(x, w, sc, y, M, K, N);
+}
+
+static float silu_(float g) { return g / (1.0f + expf(-g)); }
+
+void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const int32_t *tok, int32_t pos,
+                 float *logits, int32_t *next) {
+  const int64_t B = m->batch, D = m->dim, H = m->heads, KV = m->kv_lora, DN = m->d_nope, DR = m->d_rope,
+                DV = m->d_v, QS = DN + DR, ctx = m->max_ctx, V = m->vocab, E = m->n_exp, K = m->top_k,
+                I = m->moe_inter, DI = m->dense_inter, NQ = H * QS + KV + DR, half = DR / 2;
+  const int64_t big = (2 * DI > NQ ? 2 * DI : NQ) > 2 * I ? (2 * DI > NQ ? 2 * DI : NQ) : 2 * I;
+  float *h = (float *)calloc((size_t)(B * D), sizeof(float));
+  float *xn = (float *)malloc(sizeof(float) * (size_t)(B * (DI > D ? DI : D)));
+  float *y = (float *)malloc(sizeof(float) * (size_t)(B * big));
+  float *o = (float *)malloc(sizeof(float) * (size_t)(B * H * DV));
+  float *qo = (float *)malloc(sizeof(float) * (size_t)(B * H * QS));
+  float *lg = logits ? logits : (float *)malloc(sizeof(float) * (size_t)(B * V));
+  float *sc = (float *)malloc(sizeof(float) * (size_t)ctx), *qlat = (float *)malloc(sizeof(float) * (size_t)KV);
+  float *olat = (float *)malloc(sizeof(float) * (size_t)KV), *t1 = (float *)malloc(sizeof(float) * (size_t)(2 * I));
+  float *av = (float *)malloc(sizeof(float) * (size_t)I), *yv = (float *)malloc(sizeof(float) * (size_t)D);
+  float *rl = (float *)malloc(sizeof(float) * (size_t)(B * (E > 0 ? E : 1)));
+  if (!h || !xn || !y || !o || !qo || !lg || !sc || !qlat || !olat || !t1 || !av || !yv || !rl) goto out;
+  for (int64_t b = 0; b < B; b++)
+    for (int64_t d = 0; d < D; d++)
+      h[b * D + d] = (tok[b] >= 0 && tok[b] < V) ? orc_bf16_to_f32(m->embed[(int64_t)tok[b] * D + d]) : 0.0f;
+  for (int32_t l = 0; l < m->n_layers; l++) {
+    uint16_t *cc = cache_c + (int64_t)l * B * ctx * KV, *cp = cache_pe + (int64_t)l * B * ctx * DR;
+    rms_bf16(h, m->attn_norm[l], xn, B, D, m->eps);
+    orc_linear_bf16(xn, m->w_qkva[l], y, B, D, NQ);
+    for (int64_t b = 0; b < B; b++) {
+      const float *q = y + b * NQ, *kva = y + b * NQ + H * QS;
+      float *qb = qo + b * H * QS;
+      for (int64_t hh = 0; hh < H; hh++) {
+        for (int64_t d = 0; d < DN; d++) qb[hh * QS + d] = bfr_(q[hh * QS + d]);
+        for (int64_t j = 0; j < half; j++) {
+          const float xe = bfr_(q[hh * QS + DN + 2 * j]), xo = bfr_(q[hh * QS + DN + 2 * j + 1]);
+          const float c = m->cos_t[(int64_t)pos * DR + j], s = m->sin_t[(int64_t)pos * DR + j];
+          qb[hh * QS + DN + j] = bfr_(xe * c - xo * s);
+          qb[hh * QS + DN + half + j] = bfr_(xo * c + xe * s);
+        }
+      }
+      float ss = 0.0f;
+      for (int64_t i = 0; i < KV; i++) ss += bfr_(kva[i]) * bfr_(kva[i]);
+      const float inv = 1.0f / sqrtf(ss * (1.0f / (float)KV) + m->eps);
+      for (int64_t i = 0; i < KV; i++)
+        cc[(b * ctx + pos) * KV + i] = orc_f32_to_bf16((bfr_(kva[i]) * inv) * m->kv_norm[l][i]);
+      for (int64_t j = 0; j < half; j++) {
+        const float xe = bfr_(kva[KV + 2 * j]), xo = bfr_(kva[KV + 2 * j + 1]);
+        const float c = m->cos_t[(int64_t)pos * DR + j], s = m->sin_t[(int64_t)pos * DR + j];
+        cp[(b * ctx + pos) * DR + j] = orc_f32_to_bf16(xe * c - xo * s);
+        cp[(b * ctx + pos) * DR + half + j] = orc_f32_to_bf16(xo * c + xe * s);
+      }
+    }
+    for (int64_t b = 0; b < B; b++)
+      for (int64_t hh = 0; hh < H; hh++) {
+        const float *qb = qo + (b * H + hh) * QS;
+        const uint16_t *wk = m->w_uk[l] + hh * DN * KV, *wv = m->w_uv[l] + hh * DV * KV;
+        for (int64_t k = 0; k < KV; k++) {
+          float a = 0.0f;
+          for (int64_t d = 0; d < DN; d++) a += qb[d] * orc_bf16_to_f32(wk[d * KV + k]);
+          qlat[k] = a;
+        }
+        float mx = -INFINITY;
+        for (int64_t t = 0; t <= pos; t++) {
+          float s = 0.0f;
+          for (int64_t k = 0; k < KV; k++) s += qlat[k] * orc_bf16_to_f32(cc[(b * ctx + t) * KV + k]);
+          for (int64_t r = 0; r < DR; r++) s += qb[DN + r] * orc_bf16_to_f32(cp[(b * ctx + t) * DR + r]);
+          sc[t] = s * m->scale;
+          if (sc[t] > mx) mx = sc[t];
+        }
+        float sum = 0.0f;
+        for (int64_t t = 0; t <= pos; t++) {
+          sc[t] = expf(sc[t] - mx);
+          sum += sc[t];
+        }
+        const float inv = 1.0f / sum;
+        for (int64_t k = 0; k < KV; k++) {
+          float a = 0.0f;
+          for (int64_t t = 0; t <= pos; t++) a += sc[t] * orc_bf16_to_f32(cc[(b * ctx + t) * KV + k]);
+          olat[k] = a * inv;
+        }
+        for (int64_t r = 0; r < DV; r++) {
+          float a = 0.0f;
+          for (int64_t k = 0; k < KV; k++) a += olat[k] * orc_bf16_to_f32(wv[r * KV + k]);
+          o[b * H * DV + hh * DV + r] = bfr_(a);
+        }
+      }
+    orc_linear_bf16(o, m->w_o[l], y, B, H * DV, D);
+    for (int64_t i = 0; i < B * D; i++) h[i] += y[i];
+    rms_bf16(h, m->ffn_norm[l], xn, B, D, m->eps);
+    if (l < m->n_dense) {
+      float *gu = y;
+      orc_linear_bf16(xn, m->d_gu[l], gu, B, D, 2 * DI);
+      float *a = (float *)malloc(sizeof(float) * (size_t)(B * DI));
+      float *dn = (float *)malloc(sizeof(float) * (size_t)(B * D));
+      if (a && dn) {
+        for (int64_t b = 0; b < B; b++)
+          for (int64_t j = 0; j < DI; j++) a[b * DI + j] = bfr_(silu_(gu[b * 2 * DI + j]) * gu[b * 2 * DI + DI + j]);
+        orc_linear_bf16(a, m->d_down[l], dn, B, DI, D);
+        for (int64_t i = 0; i < B * D; i++) h[i] += dn[i];
+      }
+      free(a);
+      free(dn);
+    } else {
+      orc_linear_bf16(xn, m->router[l], rl, B, D, E);
+      for (int64_t b = 0; b < B; b++) {
+        float mx = -INFINITY, sum = 0.0f, pr[64];
+        for (int64_t e = 0; e < E; e++) mx = rl[b * E + e] > mx ? rl[b * E + e] : mx;
+        for (int64_t e = 0; e < E; e++) sum += expf(rl[b * E + e] - mx);
+        for (int64_t e = 0; e < E; e++) pr[e] = expf(rl[b * E + e] - mx) / sum;
+        int used[64] = {0};
+        const int64_t n_all = K + m->n_shared;
+        for (int64_t k = 0; k < n_all; k++) {
+          int64_t e;
+          float w;
+          if (k < K) {   /* the largest remaining prob; ties to the lowest id */
+            e = -1;
+            for (int64_t c = 0; c < E; c++)
+              if (!used[c] && (e < 0 || pr[c] > pr[e])) e = c;
+            used[e] = 1;
+            w = pr[e];
+          } else {
+            e = E + (k - K);
+            w = 1.0f;
+          }
+          const int64_t sgu = ((2 * I + 127) / 128) * (D / 128), sd = (D / 128) * ((I + 127) / 128);
+          linear_fp8_rows(xn + b * D, m->e_gu[l] + e * 2 * I * D, m->e_gu_s[l] + e * sgu, t1, 1, D, 2 * I);
+          for (int64_t j = 0; j < I; j++) av[j] = bfr_(silu_(t1[j]) * t1[I + j]);
+          linear_fp8_rows(av, m->e_d[l] + e * D * I, m->e_d_s[l] + e * sd, yv, 1, I, D);
+          for (int64_t d = 0; d < D; d++) h[b * D + d] += w * yv[d];
+        }
+      }
+    }
+  }
+  rms_bf16(h, m->norm_f, xn, B, D, m->eps);
+  orc_linear_bf16(xn, m->lm_head, lg, B, D, V);
+  for (int64_t b = 0; b < B; b++) {
+    int64_t bi = 0;
+    for (int64_t v = 1; v < V; v++)
+      if (lg[b * V + v] > lg[b * V + bi]) bi = v;
+    next[b] = (int32_t)bi;
+  }
+out:
+  free(h);
+  free(xn);
+  free(y);
+  free(o);
+  free(qo);
+  free(sc);
+  free(qlat);
+  free(olat);
+  free(t1);
+  free(av);
+  free(yv);
+  free(rl);
+  if (!logits) free(lg);
+}

@@ -147,6 +147,38 @@ typedef struct {
  * each row's first-index argmax. */
 void orc_xl_step(const OrcXL *m, uint16_t *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next);
 
+/* ---- batched MoE decode step ---------------------------
+ * A DeepSeek-V2-Lite-shaped decoder (bench/dsv2_decode_bench.c cfg :97-124)
+ * at batch B: f32 residual h; xn = bf16(rms(h) * g); q = xn W_q^T and
+ * kva = xn W_kva^T (f32); q nope -> bf16, q pe and k pe rounded to bf16, then
+ * rotated (pair (2j, 2j+1) -> columns j, DR/2 + j, YaRN tables); latent =
+ * bf16(rms(bf16(kva[:KV])) * g_kv); absorbed MLA per head: qlat = W_uk^T q_nope,
+ * scores (qlat . c_t + q_pe . pe_t) * scale, softmax, olat = sum p_t c_t,
+ * o = bf16(W_uv olat); h += o W_o^T; xn2 = bf16(rms(h) * g2); dense layers:
+ * h += bf16(silu(g) * u) W_down^T (bf16 weights); MoE layers: probs =
+ * softmax(xn2 W_router^T), top-K (ties: lowest id, no renormalisation), each
+ * chosen expert and each shared half (weight 1): h += w * bf16(silu(g) * u)
+ * W_d^T with fp8 weights * block scales; logits = bf16(rms(h) * g_f) W_lm^T. */
+typedef struct {
+  int32_t dim, n_layers, heads, kv_lora, d_nope, d_rope, d_v, n_exp, top_k, moe_inter, dense_inter, n_dense,
+      n_shared, vocab, max_ctx, batch;
+  float eps, scale;
+  const uint16_t *embed, *lm_head;
+  const float *norm_f, *cos_t, *sin_t;   /* [D], [ctx][DR], [ctx][DR] */
+  const float **attn_norm, **kv_norm, **ffn_norm;
+  const uint16_t **w_qkva;                /* [H*(DN+DR) + KV + DR][D] */
+  const uint16_t **w_uk, **w_uv, **w_o;   /* [H][DN][KV], [H][DV][KV], [D][H*DV] */
+  const uint16_t **d_gu, **d_down;        /* dense: [2*DI][D], [D][DI] */
+  const uint16_t **router;                /* [E][D] */
+  const uint8_t **e_gu, **e_d;            /* [E(+n_shared)][2I][D], [E(+n_shared)][D][I]: routed, then shared */
+  const float **e_gu_s, **e_d_s;          /* block scales as sm100_ds_experts takes them */
+} OrcDS;
+
+/* One step: cache_c [L][B][ctx][KV], cache_pe [L][B][ctx][DR] (bf16 bits, row
+ * pos written); logits [B][V] (may be NULL); next [B] = row argmax (first index). */
+void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const int32_t *tok, int32_t pos,
+                 float *logits, int32_t *next);
+
 /* threads the oracle's row-parallel loops use (pthreads), for reporting. */
 int orc_num_threads(void);
 

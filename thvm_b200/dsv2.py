@@ -1,0 +1,297 @@
+"""Batched decode of a DeepSeek-V2-Lite-shaped MoE decoder
+on the sm_100a kernels, expert-parallel over the GPUs of one box.
+
+Shapes (bench/dsv2_decode_bench.c cfg :97-124): 27 layers, d 2048, 16 heads,
+multi-head latent attention (kv_lora 512, rope 64, nope 128, v 128), layer 0
+a dense SiLU MLP (10944), layers 1-26 64 routed experts (1408) with top-6
+softmax routing (no renormalisation, ties to the lowest id) plus 2 shared
+experts, vocab 102400, batch 32.  Precision: routed and shared expert
+weights fp8-e4m3 with one f32 scale per 128 x 128 block; attention, router,
+dense layer 0, embedding and lm_head bf16; f32 residual stream, bf16 matmul
+operands (the oracle's orc_ds_step states the op order).  The two shared
+experts are one SiLU MLP of 2816 units, taken as two halves of 1408 whose
+outputs add (exact), so they ride the routed-expert kernel with weight 1.
+
+Per layer: RMSNorm -> fused q | kv_a projection (skinny tcgen05 GEMM) ->
+q / latent post-processing (bf16, RMSNorm of the latent, YaRN rotary, cache
+append) -> absorbed MLA over the compressed cache -> o projection into the
+residual -> RMSNorm -> dense MLP (layer 0) or router GEMM, routing, fp8
+experts (gate / up + SiLU, then down weighted into the MoE output).
+
+Expert parallelism: rank r of R holds routed experts split_even(64, R, r)
+and the shared halves k with k % R == r; attention, router, dense layer and
+lm_head are replicated (every rank computes the same h), and one all-reduce
+of the MoE output [B, D] per MoE layer combines the experts.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib as L
+from .gpt2_xl import split_even
+
+
+@dataclass(frozen=True)
+class DSConfig:
+    n_layers: int = 27
+    dim: int = 2048
+    heads: int = 16
+    kv_lora: int = 512
+    d_nope: int = 128
+    d_rope: int = 64
+    d_v: int = 128
+    n_exp: int = 64
+    top_k: int = 6
+    moe_inter: int = 1408
+    dense_inter: int = 10944
+    n_dense: int = 1
+    n_shared: int = 2
+    vocab: int = 102400
+    max_ctx: int = 1024
+    batch: int = 32
+    eps: float = 1e-6
+
+    @property
+    def q_cols(self) -> int:   # q rows of the fused projection
+        return self.heads * (self.d_nope + self.d_rope)
+
+    @property
+    def n_qkva(self) -> int:
+        return self.q_cols + self.kv_lora + self.d_rope
+
+    @property
+    def scale(self) -> float:
+        """(d_nope + d_rope)^-0.5 * mscale^2, mscale = 0.1 * 0.707 * ln(40) + 1 (YaRN)."""
+        mscale = 0.1 * 0.707 * math.log(40.0) + 1.0
+        return float((self.d_nope + self.d_rope) ** -0.5 * mscale * mscale)
+
+
+DSV2_LITE = DSConfig()
+
+
+def yarn_tables(d_rope: int, max_ctx: int, theta: float = 10000.0, factor: float = 40.0, orig: float = 4096.0,
+                beta_fast: float = 32.0, beta_slow: float = 1.0) -> tuple[np.ndarray, np.ndarray]:
+    """cos / sin [max_ctx, d_rope] f32 of YaRN-scaled rotary frequencies (Peng et al. 2023,
+    "YaRN"): dims below the beta_fast correction keep the base frequency theta^(-2j/d),
+    dims above beta_slow are divided by `factor`, a linear ramp between; halves duplicated."""
+    half = d_rope // 2
+    lo = math.floor(d_rope * math.log(orig / (beta_fast * 2 * math.pi)) / (2 * math.log(theta)))
+    hi = math.ceil(d_rope * math.log(orig / (beta_slow * 2 * math.pi)) / (2 * math.log(theta)))
+    lo, hi = max(lo, 0), min(hi, d_rope - 1)
+    j = np.arange(half, dtype=np.float64)
+    pf = theta ** (2 * j / d_rope)
+    ramp = np.clip((j - lo) / max(hi - lo, 1e-3), 0.0, 1.0)
+    freqs = (1.0 / (factor * pf)) * ramp + (1.0 / pf) * (1.0 - ramp)
+    ang = np.arange(max_ctx, dtype=np.float64)[:, None] * freqs[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    return np.concatenate([cos, cos], 1), np.concatenate([sin, sin], 1)
+
+
+def _bf16(a: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def _fp8(a: np.ndarray) -> np.ndarray:
+    """f32 (|a| < 448) -> e4m3 codes, round to nearest even."""
+    import torch
+    return torch.from_numpy(np.ascontiguousarray(a, np.float32)).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def ds_weights(cfg: DSConfig, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Synthetic weights: bf16 matrices N(0, std); fp8 expert codes of N(0, 1)
+    draws with block scales U[0.5, 2] * std (weights ~ N(0, std) per block);
+    RMSNorm gains 1."""
+    rng = np.random.default_rng(seed)
+    D, H, KV, DN, DR, DV = cfg.dim, cfg.heads, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v
+    E, I, NS, DI = cfg.n_exp, cfg.moe_inter, cfg.n_shared, cfg.dense_inter
+
+    def mat(*shape):
+        return _bf16(rng.standard_normal(shape, dtype=np.float32) * np.float32(std))
+
+    def fp8_blocks(n, rows, cols):
+        codes = _fp8(rng.standard_normal((n, rows, cols), dtype=np.float32))
+        sc = (rng.uniform(0.5, 2.0, (n, -(-rows // 128), -(-cols // 128))) * std).astype(np.float32)
+        return codes, sc
+
+    w = {"embed": mat(cfg.vocab, D), "lm_head": mat(cfg.vocab, D), "norm_f": np.ones(D, np.float32)}
+    for l in range(cfg.n_layers):
+        p = f"l{l}."
+        w[p + "attn_norm"], w[p + "ffn_norm"] = np.ones(D, np.float32), np.ones(D, np.float32)
+        w[p + "kv_norm"] = np.ones(KV, np.float32)
+        w[p + "w_qkva"] = mat(cfg.n_qkva, D)
+        w[p + "w_uk"], w[p + "w_uv"] = mat(H, DN, KV), mat(H, DV, KV)
+        w[p + "w_o"] = mat(D, H * DV)
+        if l < cfg.n_dense:
+            w[p + "d_gu"], w[p + "d_down"] = mat(2 * DI, D), mat(D, DI)
+        else:
+            w[p + "router"] = mat(E, D)
+            w[p + "e_gu"], w[p + "e_gu_s"] = fp8_blocks(E + NS, 2 * I, D)
+            w[p + "e_d"], w[p + "e_d_s"] = fp8_blocks(E + NS, D, I)
+    return w
+
+
+@dataclass(frozen=True)
+class EPShard:
+    rank: int
+    world: int
+    e0: int
+    e1: int
+    shared: tuple   # the shared halves this rank runs
+
+
+def ep_shard(cfg: DSConfig, rank: int, world: int) -> EPShard:
+    if not 0 <= rank < world or world > cfg.n_exp:
+        raise ValueError(f"rank {rank} of {world}")
+    e0, e1 = split_even(cfg.n_exp, world, rank)
+    return EPShard(rank, world, e0, e1, tuple(k for k in range(cfg.n_shared) if k % world == rank))
+
+
+def shard_experts(w: dict[str, np.ndarray], cfg: DSConfig, sh: EPShard) -> dict[str, np.ndarray]:
+    """This rank's weights: everything but the experts replicated; the experts
+    [e0, e1) followed by its shared halves."""
+    out = {}
+    keep = list(range(sh.e0, sh.e1)) + [cfg.n_exp + k for k in sh.shared]
+    for k, v in w.items():
+        if k.split(".", 1)[-1] in ("e_gu", "e_gu_s", "e_d", "e_d_s"):
+            out[k] = np.ascontiguousarray(v[keep])
+        else:
+            out[k] = v
+    return out
+
+
+class DSModel:
+    """One rank's part of the model on the current CUDA device (torch.distributed
+    group over the R ranks, None when R = 1)."""
+
+    def __init__(self, cfg: DSConfig, weights: dict[str, np.ndarray], shard: EPShard, group=None):
+        import torch
+        self.torch, self.cfg, self.sh, self.group = torch, cfg, shard, group
+        self.lib = L.lib()
+        dev = torch.device("cuda", torch.cuda.current_device())
+        B, D, ctx = cfg.batch, cfg.dim, cfg.max_ctx
+
+        def put(a):
+            t = torch.from_numpy(np.ascontiguousarray(a))
+            if t.dtype == torch.uint16:
+                t = t.view(torch.int16)
+            return t.to(dev)
+
+        self.w = {k: put(v) for k, v in weights.items()}
+        cos, sin = yarn_tables(cfg.d_rope, ctx)
+        self.cos, self.sin = put(cos), put(sin)
+        z = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=dev)
+        self.h = z(B, D)
+        self.xn = z(B, max(D, cfg.dense_inter), dt=torch.int16)
+        self.qkva = z(B, cfg.n_qkva)
+        self.qo = z(B, cfg.q_cols, dt=torch.int16)
+        self.o = z(B, cfg.heads * cfg.d_v, dt=torch.int16)
+        self.gu = z(B, 2 * cfg.dense_inter)
+        self.rl = z(B, cfg.n_exp)
+        self.moe = z(B, D)
+        self.logits = z(B, cfg.vocab)
+        self.cache_c = [z(B, ctx, cfg.kv_lora, dt=torch.int16) for _ in range(cfg.n_layers)]
+        self.cache_pe = [z(B, ctx, cfg.d_rope, dt=torch.int16) for _ in range(cfg.n_layers)]
+        self.tok = z(B, dt=torch.int32)
+        self.pos = z(1, dt=torch.int32)
+        K = cfg.top_k
+        self.sel, self.wsel = z(B * K, dt=torch.int32), z(B * K)
+        n_local = shard.e1 - shard.e0
+        self.slot_off, self.slot_tok, self.slot_w = z(n_local + 1, dt=torch.int32), z(B * K, dt=torch.int32), z(B * K)
+        ns = len(shard.shared)
+        self.sh_off = torch.arange(0, (ns + 1) * B, B, dtype=torch.int32, device=dev)
+        self.sh_tok = torch.arange(B, dtype=torch.int32, device=dev).repeat(max(ns, 1))
+        self.sh_w = torch.ones(max(ns, 1) * B, device=dev)
+        self.a = z(B * K, cfg.moe_inter, dt=torch.int16)
+        self.a_sh = z(max(ns, 1) * B, cfg.moe_inter, dt=torch.int16)
+        self.vals, self.idxs = z(1, B), z(1, B, dt=torch.int32)
+        self.ws = z(int(self.lib.sm100_skinny_ws_bytes(B)) // 4)
+        self.counters = z(cfg.vocab // 128 + 2, dt=torch.int32)
+        self._args = L.Sm100SkinnyArgs()
+        self.launches = 0
+
+    def _stream(self):
+        return ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
+
+    def _skinny(self, x, w, y, K, N, residual=False):
+        a = self._args
+        a.x, a.w, a.y = x.data_ptr(), w.data_ptr(), y.data_ptr()
+        a.bias = None
+        a.residual = y.data_ptr() if residual else None
+        a.ws, a.counters, a.kv_cache, a.pos = self.ws.data_ptr(), self.counters.data_ptr(), None, None
+        a.M, a.N, a.K = self.cfg.batch, N, K
+        a.ld_x = a.ld_w = a.ld_res = a.ld_y = 0
+        a.flags, a.kv_ctx = L.SK_RESIDUAL if residual else 0, 0
+        a.ln_g = a.ln_b = None
+        L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
+        self.launches += 1
+
+    def _rms(self, g, D):
+        L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                          self.cfg.eps, self._stream()), "ds_rmsnorm")
+        self.launches += 1
+
+    def step(self):
+        """One decode step: ids in self.tok at row self.pos -> next ids, pos + 1."""
+        cfg, sh, w, lib, st = self.cfg, self.sh, self.w, self.lib, self._stream
+        B, D, H, KV, DN, DR, DV = cfg.batch, cfg.dim, cfg.heads, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v
+        E, K, I, DI = cfg.n_exp, cfg.top_k, cfg.moe_inter, cfg.dense_inter
+        L.check(lib.sm100_ds_embed(w["embed"].data_ptr(), self.tok.data_ptr(), self.h.data_ptr(), B, cfg.vocab, D,
+                                   st()), "ds_embed")
+        self.launches += 1
+        for l in range(cfg.n_layers):
+            p = f"l{l}."
+            self._rms(w[p + "attn_norm"], D)
+            self._skinny(self.xn, w[p + "w_qkva"], self.qkva, D, cfg.n_qkva)
+            q = self.qkva.data_ptr()
+            L.check(lib.sm100_ds_qkv_post(q, q + 4 * cfg.q_cols, cfg.n_qkva, w[p + "kv_norm"].data_ptr(),
+                                          self.cos.data_ptr(), self.sin.data_ptr(), self.pos.data_ptr(),
+                                          self.qo.data_ptr(), self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(),
+                                          B, H, DN, DR, KV, cfg.max_ctx, cfg.eps, st()), "ds_qkv_post")
+            L.check(lib.sm100_ds_mla(self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
+                                     self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.pos.data_ptr(),
+                                     self.o.data_ptr(), B, H, DN, DR, DV, KV, cfg.max_ctx, cfg.scale, st()), "ds_mla")
+            self.launches += 2
+            self._skinny(self.o, w[p + "w_o"], self.h, H * DV, D, residual=True)
+            self._rms(w[p + "ffn_norm"], D)
+            if l < cfg.n_dense:
+                self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DI)
+                L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DI, st()), "ds_silu_mul")
+                self.launches += 1
+                self._skinny(self.xn, w[p + "d_down"], self.h, DI, D, residual=True)
+                continue
+            self._skinny(self.xn, w[p + "router"], self.rl, D, E)
+            L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, self.sel.data_ptr(),
+                                       self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
+                                       self.slot_w.data_ptr(), st()), "ds_route")
+            self.moe.zero_()
+            n_local = sh.e1 - sh.e0
+            egu, egs, ed, eds = w[p + "e_gu"], w[p + "e_gu_s"], w[p + "e_d"], w[p + "e_d_s"]
+            if n_local:
+                L.check(lib.sm100_ds_experts(self.xn.data_ptr(), egu.data_ptr(), egs.data_ptr(), ed.data_ptr(),
+                                             eds.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
+                                             self.slot_w.data_ptr(), self.a.data_ptr(), self.moe.data_ptr(), n_local,
+                                             D, I, st()), "ds_experts")
+            if sh.shared:   # the shared halves follow the routed experts in this rank's arrays
+                L.check(lib.sm100_ds_experts(self.xn.data_ptr(), egu[n_local:].data_ptr(), egs[n_local:].data_ptr(),
+                                             ed[n_local:].data_ptr(), eds[n_local:].data_ptr(),
+                                             self.sh_off.data_ptr(), self.sh_tok.data_ptr(), self.sh_w.data_ptr(),
+                                             self.a_sh.data_ptr(), self.moe.data_ptr(), len(sh.shared), D, I, st()),
+                        "ds_experts shared")
+            self.launches += 1 + 2 * (bool(n_local) + bool(sh.shared))
+            if sh.world > 1:
+                self.torch.distributed.all_reduce(self.moe, group=self.group)
+            L.check(lib.sm100_add(self.h.data_ptr(), self.moe.data_ptr(), self.h.data_ptr(), B * D, st()), "add")
+            self.launches += 1
+        self._rms(w["norm_f"], D)
+        self._skinny(self.xn, w["lm_head"], self.logits, D, cfg.vocab)
+        L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), cfg.vocab, B, cfg.vocab, self.vals.data_ptr(),
+                                    self.idxs.data_ptr(), 0, 0, st()), "xl_argmax")
+        L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(), st()),
+                "xl_pick")
+        L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, st()), "pos_add")
+        self.launches += 3
