@@ -12,6 +12,10 @@
 //
 // Every kernel is launched with programmatic dependent launch and reads its
 // inputs after griddepcontrol.wait.
+#include <cuda_fp8.h>
+
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sm100 {
@@ -22,15 +26,6 @@ constexpr int kDsMaxCtx = 2048;
 
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
-// e4m3 code -> f32 (bias 7, no infinities, 0x7f / 0xff NaN)
-__device__ __forceinline__ float fp8v(uint32_t c) {
-  const uint32_t e = (c >> 3) & 0xFu, m = c & 7u;
-  const float s = (c & 0x80u) ? -1.0f : 1.0f;
-  if (e == 15u && m == 7u) return __int_as_float(0x7fc00000);
-  if (e == 0u) return s * (float)m * 0.001953125f;   // m * 2^-9
-  return s * __uint_as_float(((e + 120u) << 23) | (m << 20));
-}
 
 // y = bf16(x * rsqrt(mean(x^2) + eps) * g) per row (RMSNorm, deepseek_v2.py's
 // RMSNorm as the reference folds it, dsv2_decode_bench.c:341-430).
@@ -235,134 +230,180 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {   // expert-major packing (token order within an expert)
-    int n = 0;
-    for (int e = e0; e < e1; e++) {
-      slot_off[e - e0] = n;
-      for (int i = 0; i < B * K; i++)
-        if (s_sel[i] == e) {
-          slot_tok[n] = i / K;
-          slot_w[n] = s_w[i];
-          n++;
-        }
+  // expert-major packing: thread e counts its slots, a scan gives the offsets,
+  // then it lists its tokens in order
+  __shared__ int cnt[64];
+  const int ne = e1 - e0;
+  if (threadIdx.x < 64) {
+    int c = 0;
+    if ((int)threadIdx.x < ne)
+      for (int i = 0; i < B * K; i++) c += (s_sel[i] == e0 + (int)threadIdx.x);
+    cnt[threadIdx.x] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x < 64 && (int)threadIdx.x < ne) {
+    int o = 0;
+    for (int i = 0; i < (int)threadIdx.x; i++) o += cnt[i];
+    slot_off[threadIdx.x] = o;
+    if ((int)threadIdx.x == ne - 1) slot_off[ne] = o + cnt[threadIdx.x];
+    for (int i = 0; i < B * K; i++)
+      if (s_sel[i] == e0 + (int)threadIdx.x) {
+        slot_tok[o] = i / K;
+        slot_w[o] = s_w[i];
+        o++;
+      }
+  }
+  if (ne == 0 && threadIdx.x == 0) slot_off[0] = 0;
+}
+
+// 16 fp8-e4m3 codes -> f32 times a block scale (hardware e4m3x2 -> f16x2
+// conversions; f16 holds every e4m3 value exactly).
+__device__ __forceinline__ void fp8x16(const uint4 w, float sc, float (&f)[16]) {
+  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+#pragma unroll
+    for (int hlf = 0; hlf < 2; hlf++) {
+      const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+      const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
+      f[4 * q + 2 * hlf] = v.x * sc;
+      f[4 * q + 2 * hlf + 1] = v.y * sc;
     }
-    slot_off[e1 - e0] = n;
   }
 }
 
-// Experts, phase 1: for expert e (blockIdx.y) and a block of 16 rows of its
-// gate and up weights (fp8 [2I][D] with f32 scales [ceil(2I/128)][D/128];
-// rows [0, I) gate, [I, 2I) up), a[slot][j] = bf16(silu(g) * u) for the
-// expert's tokens.  A warp per row pair (gate j, up j), lanes over D in
-// 16-byte fp8 chunks, the tokens' bf16 inputs staged in shared memory.
-constexpr int kDsRowsPerCta = 8;
+constexpr int kDsRows = 64;      // weight rows per work item
+constexpr int kDsTokChunk = 8;   // tokens staged in shared memory at a time
+
+// Experts, phase 1 (persistent, grid-stride over work items (expert e, block
+// of 64 rows); an expert without tokens costs one read of its slot count):
+// a[slot][j] = bf16(silu(x . gate_j) * (x . up_j)) for the expert's tokens,
+// gate / up fp8 rows [2I][D] with f32 scales [ceil(2I/128)][D/128].  Tokens
+// are staged 8 at a time in shared memory; a warp per row pair, lanes over
+// D in 16-byte fp8 chunks.
 __global__ void __launch_bounds__(256) ds_expert_up_kernel(const __nv_bfloat16 *x, const uint8_t *wgu,
                                                             const float *sgu, const int32_t *slot_off,
                                                             const int32_t *slot_tok, __nv_bfloat16 *a, int D, int I,
-                                                            int64_t w_stride, int64_t s_stride, int e_base) {
-  extern __shared__ __nv_bfloat16 xs[];   // [kDsMaxTok][D]
+                                                            int64_t w_stride, int64_t s_stride, int n_exp) {
+  extern __shared__ __nv_bfloat16 xs[];   // [kDsTokChunk][D]
   pdl_trigger();
   pdl_wait();
-  const int e = blockIdx.y, off = slot_off[e], n = slot_off[e + 1] - off;
-  if (n == 0) return;
-  for (int i = threadIdx.x; i < n * D / 8; i += 256) {
-    const int s = i / (D / 8), c = i % (D / 8);
-    reinterpret_cast<uint4 *>(xs)[(int64_t)s * (D / 8) + c] =
-        reinterpret_cast<const uint4 *>(x + (int64_t)slot_tok[off + s] * D)[c];
-  }
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int j = blockIdx.x * kDsRowsPerCta + warp;
-  if (j >= I) return;
-  const uint8_t *we = wgu + (int64_t)e * w_stride;
-  const float *se = sgu + (int64_t)e * s_stride;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rb_n = (I + kDsRows - 1) / kDsRows;
   const int sc_cols = D / 128;
-  float g[kDsMaxTok], u[kDsMaxTok];
-#pragma unroll
-  for (int s = 0; s < kDsMaxTok; s++) g[s] = u[s] = 0.0f;
-  for (int k0 = lane * 16; k0 < D; k0 += 512) {
-    const uint4 wg = *reinterpret_cast<const uint4 *>(we + (int64_t)j * D + k0);
-    const uint4 wu = *reinterpret_cast<const uint4 *>(we + (int64_t)(I + j) * D + k0);
-    const float sg = se[(j / 128) * sc_cols + k0 / 128], su = se[((I + j) / 128) * sc_cols + k0 / 128];
-    const uint32_t gw[4] = {wg.x, wg.y, wg.z, wg.w}, uw[4] = {wu.x, wu.y, wu.z, wu.w};
-    float fg[16], fu[16];
-#pragma unroll
-    for (int q = 0; q < 16; q++) {
-      fg[q] = fp8v((gw[q >> 2] >> (8 * (q & 3))) & 0xFFu) * sg;
-      fu[q] = fp8v((uw[q >> 2] >> (8 * (q & 3))) & 0xFFu) * su;
-    }
-#pragma unroll
-    for (int s = 0; s < kDsMaxTok; s++) {
-      if (s >= n) continue;
-      const __nv_bfloat16 *xr = xs + (int64_t)s * D + k0;
-      float ag = 0.0f, au = 0.0f;
-#pragma unroll
-      for (int q = 0; q < 16; q++) {
-        const float xv = bf(xr[q]);
-        ag = fmaf(fg[q], xv, ag);
-        au = fmaf(fu[q], xv, au);
+  for (int item = blockIdx.x; item < n_exp * rb_n; item += gridDim.x) {
+    const int e = item / rb_n, rb = item % rb_n, off = slot_off[e], n = slot_off[e + 1] - off;
+    if (n == 0) continue;
+    const uint8_t *we = wgu + (int64_t)e * w_stride;
+    const float *se = sgu + (int64_t)e * s_stride;
+    for (int t0 = 0; t0 < n; t0 += kDsTokChunk) {
+      const int nt = min(kDsTokChunk, n - t0);
+      __syncthreads();   // the previous chunk's readers are done
+      for (int i = threadIdx.x; i < nt * D / 8; i += 256) {
+        const int s = i / (D / 8), c = i % (D / 8);
+        reinterpret_cast<uint4 *>(xs)[(int64_t)s * (D / 8) + c] =
+            reinterpret_cast<const uint4 *>(x + (int64_t)slot_tok[off + t0 + s] * D)[c];
       }
-      g[s] += ag;
-      u[s] += au;
-    }
-  }
+      __syncthreads();
+      for (int r = warp; r < kDsRows; r += 8) {
+        const int j = rb * kDsRows + r;
+        if (j >= I) break;
+        float g[kDsTokChunk], u[kDsTokChunk];
 #pragma unroll
-  for (int s = 0; s < kDsMaxTok; s++) {
-    if (s >= n) continue;
-    const float gs = warp_sum(g[s]), us = warp_sum(u[s]);
-    if (lane == 0) {
-      const float silu = gs / (1.0f + expf(-gs));
-      a[(int64_t)(off + s) * I + j] = __float2bfloat16_rn(silu * us);
+        for (int s = 0; s < kDsTokChunk; s++) g[s] = u[s] = 0.0f;
+        for (int k0 = lane * 16; k0 < D; k0 += 512) {
+          float fg[16], fu[16];
+          fp8x16(*reinterpret_cast<const uint4 *>(we + (int64_t)j * D + k0), se[(j / 128) * sc_cols + k0 / 128], fg);
+          fp8x16(*reinterpret_cast<const uint4 *>(we + (int64_t)(I + j) * D + k0),
+                 se[((I + j) / 128) * sc_cols + k0 / 128], fu);
+#pragma unroll
+          for (int s = 0; s < kDsTokChunk; s++) {
+            if (s >= nt) continue;
+            const uint4 *xr = reinterpret_cast<const uint4 *>(xs + (int64_t)s * D + k0);
+            float ag = 0.0f, au = 0.0f;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              const uint4 xv = xr[h];
+              const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+              for (int q = 0; q < 4; q++) {
+                const float x0 = __uint_as_float(xw[q] << 16), x1 = __uint_as_float(xw[q] & 0xFFFF0000u);
+                ag = fmaf(fg[8 * h + 2 * q], x0, fmaf(fg[8 * h + 2 * q + 1], x1, ag));
+                au = fmaf(fu[8 * h + 2 * q], x0, fmaf(fu[8 * h + 2 * q + 1], x1, au));
+              }
+            }
+            g[s] += ag;
+            u[s] += au;
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < kDsTokChunk; s++) {
+          if (s >= nt) continue;
+          const float gs = warp_sum(g[s]), us = warp_sum(u[s]);
+          if (lane == 0) a[(int64_t)(off + t0 + s) * I + j] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
+        }
+      }
     }
   }
-  (void)e_base;
 }
 
-// Experts, phase 2: y[tok][r] += w_slot * sum_j a[slot][j] W_d[e][r][j] for a
-// block of output rows r of expert e (fp8 [D][I], scales [D/128][ceil(I/128)]);
-// the experts of a token meet in y by float reductions.
+// Experts, phase 2 (persistent over (expert, block of 64 output rows)):
+// y[tok][r] += w_slot * sum_j a[slot][j] W_d[e][r][j] (fp8 [D][I], scales
+// [D/128][ceil(I/128)]); the experts of a token meet in y by float reductions.
 __global__ void __launch_bounds__(256) ds_expert_down_kernel(const __nv_bfloat16 *a, const uint8_t *wd, const float *sd,
                                                               const int32_t *slot_off, const int32_t *slot_tok,
                                                               const float *slot_w, float *y, int D, int I,
-                                                              int64_t w_stride, int64_t s_stride) {
-  extern __shared__ __nv_bfloat16 as[];   // [kDsMaxTok][I]
+                                                              int64_t w_stride, int64_t s_stride, int n_exp) {
+  extern __shared__ __nv_bfloat16 as[];   // [kDsTokChunk][I]
   pdl_trigger();
   pdl_wait();
-  const int e = blockIdx.y, off = slot_off[e], n = slot_off[e + 1] - off;
-  if (n == 0) return;
-  for (int i = threadIdx.x; i < n * I; i += 256) as[i] = a[(int64_t)off * I + i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int r = blockIdx.x * kDsRowsPerCta + warp;
-  if (r >= D) return;
-  const uint8_t *we = wd + (int64_t)e * w_stride + (int64_t)r * I;
-  const float *se = sd + (int64_t)e * s_stride + (int64_t)(r / 128) * ((I + 127) / 128);
-  float acc[kDsMaxTok];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rb_n = (D + kDsRows - 1) / kDsRows;
+  const int sc_cols = (I + 127) / 128;
+  for (int item = blockIdx.x; item < n_exp * rb_n; item += gridDim.x) {
+    const int e = item / rb_n, rb = item % rb_n, off = slot_off[e], n = slot_off[e + 1] - off;
+    if (n == 0) continue;
+    for (int t0 = 0; t0 < n; t0 += kDsTokChunk) {
+      const int nt = min(kDsTokChunk, n - t0);
+      __syncthreads();
+      for (int i = threadIdx.x; i < nt * I / 8; i += 256)
+        reinterpret_cast<uint4 *>(as)[i] = reinterpret_cast<const uint4 *>(a + (int64_t)(off + t0) * I)[i];
+      __syncthreads();
+      for (int rr = warp; rr < kDsRows; rr += 8) {
+        const int r = rb * kDsRows + rr;
+        if (r >= D) break;
+        const uint8_t *we = wd + (int64_t)e * w_stride + (int64_t)r * I;
+        const float *se = sd + (int64_t)e * s_stride + (int64_t)(r / 128) * sc_cols;
+        float acc[kDsTokChunk];
 #pragma unroll
-  for (int s = 0; s < kDsMaxTok; s++) acc[s] = 0.0f;
-  for (int k0 = lane * 16; k0 < I; k0 += 512) {
-    float f[16];
-    const uint4 w = *reinterpret_cast<const uint4 *>(we + k0);
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    const float sc = se[k0 / 128];
+        for (int s = 0; s < kDsTokChunk; s++) acc[s] = 0.0f;
+        for (int k0 = lane * 16; k0 < I; k0 += 512) {
+          float f[16];
+          fp8x16(*reinterpret_cast<const uint4 *>(we + k0), se[k0 / 128], f);
 #pragma unroll
-    for (int q = 0; q < 16; q++) f[q] = (k0 + q < I) ? fp8v((ww[q >> 2] >> (8 * (q & 3))) & 0xFFu) * sc : 0.0f;
+          for (int s = 0; s < kDsTokChunk; s++) {
+            if (s >= nt) continue;
+            const uint4 *ar = reinterpret_cast<const uint4 *>(as + (int64_t)s * I + k0);
+            float t = 0.0f;
 #pragma unroll
-    for (int s = 0; s < kDsMaxTok; s++) {
-      if (s >= n) continue;
-      const __nv_bfloat16 *ar = as + (int64_t)s * I + k0;
-      float t = 0.0f;
+            for (int h = 0; h < 2; h++) {
+              const uint4 av = ar[h];
+              const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
 #pragma unroll
-      for (int q = 0; q < 16; q++)
-        if (k0 + q < I) t = fmaf(f[q], bf(ar[q]), t);
-      acc[s] += t;
+              for (int q = 0; q < 4; q++)
+                t = fmaf(f[8 * h + 2 * q], __uint_as_float(aw[q] << 16),
+                         fmaf(f[8 * h + 2 * q + 1], __uint_as_float(aw[q] & 0xFFFF0000u), t));
+            }
+            acc[s] += t;
+          }
+        }
+#pragma unroll
+        for (int s = 0; s < kDsTokChunk; s++) {
+          if (s >= nt) continue;
+          const float v = warp_sum(acc[s]);
+          if (lane == 0) atomicAdd(y + (int64_t)slot_tok[off + t0 + s] * D + r, slot_w[off + t0 + s] * v);
+        }
+      }
     }
-  }
-#pragma unroll
-  for (int s = 0; s < kDsMaxTok; s++) {
-    if (s >= n) continue;
-    const float v = warp_sum(acc[s]);
-    if (lane == 0) atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * v);
   }
 }
 
@@ -440,22 +481,23 @@ extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_
                                 const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch,
                                 float *y, int32_t n_exp, int32_t D, int32_t I, void *stream) {
   if (!x || !w_gu || !s_gu || !w_d || !s_d || !slot_off || !slot_tok || !slot_w || !a_scratch || !y || n_exp < 1 ||
-      D % 512 || I % 16 || (size_t)kDsMaxTok * D * 2 > 200 * 1024 || (size_t)kDsMaxTok * I * 2 > 200 * 1024)
+      D % 512 || I % 16 || D > 16384 || I > 16384)
     return sm100_set_error(SM100_ERR_ARG, "ds_experts: n_exp %d D %d I %d (D %% 512 == 0, I %% 16 == 0)", n_exp, D, I);
   const int64_t sc_gu = (int64_t)((2 * I + 127) / 128) * (D / 128), sc_d = (int64_t)(D / 128) * ((I + 127) / 128);
-  const size_t smem_up = (size_t)kDsMaxTok * D * 2, smem_dn = (size_t)kDsMaxTok * I * 2;
+  const size_t smem_up = (size_t)kDsTokChunk * D * 2, smem_dn = (size_t)kDsTokChunk * I * 2;
   cudaError_t e = cudaFuncSetAttribute(ds_expert_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_up);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(ds_expert_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dn);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: smem attribute: %s", cudaGetErrorString(e));
-  e = launch_pdl(ds_expert_up_kernel, dim3((I + kDsRowsPerCta - 1) / kDsRowsPerCta, n_exp), dim3(256), smem_up,
-                 (cudaStream_t)stream, (const __nv_bfloat16 *)x, (const uint8_t *)w_gu, s_gu, slot_off, slot_tok,
-                 (__nv_bfloat16 *)a_scratch, D, I, (int64_t)2 * I * D, sc_gu, 0);
+  const int items_up = n_exp * ((I + kDsRows - 1) / kDsRows), items_dn = n_exp * ((D + kDsRows - 1) / kDsRows);
+  e = launch_pdl(ds_expert_up_kernel, dim3(std::min(items_up, 4 * 148)), dim3(256), smem_up, (cudaStream_t)stream,
+                 (const __nv_bfloat16 *)x, (const uint8_t *)w_gu, s_gu, slot_off, slot_tok, (__nv_bfloat16 *)a_scratch,
+                 D, I, (int64_t)2 * I * D, sc_gu, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: up: %s", cudaGetErrorString(e));
   launch_status("ds_expert_up");
-  e = launch_pdl(ds_expert_down_kernel, dim3((D + kDsRowsPerCta - 1) / kDsRowsPerCta, n_exp), dim3(256), smem_dn,
-                 (cudaStream_t)stream, (const __nv_bfloat16 *)a_scratch, (const uint8_t *)w_d, s_d, slot_off, slot_tok,
-                 slot_w, y, D, I, (int64_t)D * I, sc_d);
+  e = launch_pdl(ds_expert_down_kernel, dim3(std::min(items_dn, 4 * 148)), dim3(256), smem_dn, (cudaStream_t)stream,
+                 (const __nv_bfloat16 *)a_scratch, (const uint8_t *)w_d, s_d, slot_off, slot_tok, slot_w, y, D, I,
+                 (int64_t)D * I, sc_d, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: down: %s", cudaGetErrorString(e));
   return launch_status("ds_expert_down");
 }
