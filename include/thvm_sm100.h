@@ -432,10 +432,12 @@ int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const vo
                  const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV,
                  int32_t ctx, float scale, void *stream);
 /* softmax over E <= 64 router logits, the K largest (ties: lowest id), no
- * renormalisation; sel / wsel [B][K]; slot lists of the experts [e0, e1):
- * slot_off [e1 - e0 + 1], slot_tok / slot_w [B * K] (expert-major) */
-int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t *sel,
-                   float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
+ * renormalisation; sel / wsel [B][K]; slot lists of the experts [e0, e1)
+ * followed by n_shared experts taking every token with weight 1:
+ * slot_off [e1 - e0 + n_shared + 1], slot_tok / slot_w [B * (K + n_shared)]
+ * (expert-major) */
+int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared,
+                   int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
 /* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
  * experts: w_gu fp8 [n_exp][2I][D] + scales [n_exp][ceil(2I/128)][D/128],
  * w_d fp8 [n_exp][D][I] + scales [n_exp][D/128][ceil(I/128)]; x bf16 [B][D];

@@ -60,7 +60,8 @@ def test_ds_decode_matches_oracle():
 
 
 def test_ds_route_matches_oracle_rule():
-    """The routing kernel alone: softmax, top-K with ties to the lowest id, expert-major slots."""
+    """The routing kernel alone: softmax, top-K with ties to the lowest id, expert-major slots,
+    then the shared experts' slots."""
     import ctypes
     import torch
     from thvm_b200 import _lib as L
@@ -72,9 +73,10 @@ def test_ds_route_matches_oracle_rule():
     d = lambda a: torch.from_numpy(a).cuda()
     lg = d(logits)
     sel, wsel = torch.zeros(B * K, dtype=torch.int32, device="cuda"), torch.zeros(B * K, device="cuda")
-    off = torch.zeros(E + 1, dtype=torch.int32, device="cuda")
-    stok, sw = torch.zeros(B * K, dtype=torch.int32, device="cuda"), torch.zeros(B * K, device="cuda")
-    L.check(lib.sm100_ds_route(lg.data_ptr(), E, K, B, 0, E, sel.data_ptr(), wsel.data_ptr(), off.data_ptr(),
+    NS = 2
+    off = torch.zeros(E + NS + 1, dtype=torch.int32, device="cuda")
+    stok, sw = torch.zeros(B * (K + NS), dtype=torch.int32, device="cuda"), torch.zeros(B * (K + NS), device="cuda")
+    L.check(lib.sm100_ds_route(lg.data_ptr(), E, K, B, 0, E, NS, sel.data_ptr(), wsel.data_ptr(), off.data_ptr(),
                                stok.data_ptr(), sw.data_ptr(), ctypes.c_void_p(0)), "ds_route")
     torch.cuda.synchronize()
     p = np.exp(logits - logits.max(1, keepdims=True))
@@ -83,7 +85,10 @@ def test_ds_route_matches_oracle_rule():
     np.testing.assert_array_equal(sel.cpu().numpy().reshape(B, K), ref)
     np.testing.assert_allclose(wsel.cpu().numpy().reshape(B, K), np.take_along_axis(p, ref, 1), rtol=1e-5)
     o = off.cpu().numpy()
-    assert o[0] == 0 and o[-1] == B * K and np.all(np.diff(o) >= 0)
+    assert o[0] == 0 and o[E] == B * K and o[-1] == B * (K + NS) and np.all(np.diff(o) >= 0)
     for e in range(E):
         toks = stok.cpu().numpy()[o[e]:o[e + 1]]
         np.testing.assert_array_equal(toks, np.nonzero((ref == e).any(1))[0])
+    for k in range(NS):   # the shared experts: every token, weight 1
+        np.testing.assert_array_equal(stok.cpu().numpy()[o[E + k]:o[E + k + 1]], np.arange(B))
+        assert np.all(sw.cpu().numpy()[o[E + k]:o[E + k + 1]] == 1.0)

@@ -187,9 +187,10 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
 // (max, exp, sum, divide), the K largest probs (ties: lowest expert id), no
 // renormalisation (DeepSeek-V2-Lite: norm_topk_prob false, scaling 1);
 // then per-expert lists of (token, weight) for the experts [e0, e1) this
-// rank holds, packed expert-major: slot_tok / slot_w / slot_of[e] offsets.
+// rank holds, packed expert-major: slot_tok / slot_w / slot_off[e] offsets,
+// followed by n_shared shared experts that take every token with weight 1.
 __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int E, int K, int B, int e0, int e1,
-                                                         int32_t *sel, float *wsel, int32_t *slot_off,
+                                                         int n_shared, int32_t *sel, float *wsel, int32_t *slot_off,
                                                          int32_t *slot_tok, float *slot_w) {
   __shared__ int s_sel[kDsMaxTok * kDsMaxK];
   __shared__ float s_w[kDsMaxTok * kDsMaxK];
@@ -254,6 +255,16 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
       }
   }
   if (ne == 0 && threadIdx.x == 0) slot_off[0] = 0;
+  // the shared experts (local ids ne ..) take every token with weight 1
+  __syncthreads();
+  if (n_shared > 0) {
+    for (int i = threadIdx.x; i < n_shared * B; i += blockDim.x) {
+      const int k = i / B, b = i % B, o = slot_off[ne] + i;
+      slot_tok[o] = b;
+      slot_w[o] = 1.0f;
+      if (b == 0) slot_off[ne + k + 1] = slot_off[ne] + (k + 1) * B;
+    }
+  }
 }
 
 // 16 fp8-e4m3 codes -> f32 times a block scale (hardware e4m3x2 -> f16x2
@@ -273,11 +284,11 @@ __device__ __forceinline__ void fp8x16(const uint4 w, float sc, float (&f)[16]) 
   }
 }
 
-constexpr int kDsRows = 64;      // weight rows per work item
+constexpr int kDsRows = 32;      // weight rows per work item
 constexpr int kDsTokChunk = 8;   // tokens staged in shared memory at a time
 
 // Experts, phase 1 (persistent, grid-stride over work items (expert e, block
-// of 64 rows); an expert without tokens costs one read of its slot count):
+// of 32 rows); an expert without tokens costs one read of its slot count):
 // a[slot][j] = bf16(silu(x . gate_j) * (x . up_j)) for the expert's tokens,
 // gate / up fp8 rows [2I][D] with f32 scales [ceil(2I/128)][D/128].  Tokens
 // are staged 8 at a time in shared memory; a warp per row pair, lanes over
@@ -347,7 +358,7 @@ __global__ void __launch_bounds__(256) ds_expert_up_kernel(const __nv_bfloat16 *
   }
 }
 
-// Experts, phase 2 (persistent over (expert, block of 64 output rows)):
+// Experts, phase 2 (persistent over (expert, block of 32 output rows)):
 // y[tok][r] += w_slot * sum_j a[slot][j] W_d[e][r][j] (fp8 [D][I], scales
 // [D/128][ceil(I/128)]); the experts of a token meet in y by float reductions.
 __global__ void __launch_bounds__(256) ds_expert_down_kernel(const __nv_bfloat16 *a, const uint8_t *wd, const float *sd,
@@ -468,13 +479,13 @@ extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_u
 }
 
 extern "C" int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1,
-                              int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w,
-                              void *stream) {
+                              int32_t n_shared, int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok,
+                              float *slot_w, void *stream) {
   if (!logits || !sel || !wsel || !slot_off || !slot_tok || !slot_w || E < 1 || E > 64 || K < 1 || K > kDsMaxK ||
-      K > E || B < 1 || B > kDsMaxTok || e0 < 0 || e1 > E || e0 > e1)
+      K > E || B < 1 || B > kDsMaxTok || e0 < 0 || e1 > E || e0 > e1 || n_shared < 0 || n_shared > 8)
     return sm100_set_error(SM100_ERR_ARG, "ds_route: E %d K %d B %d [%d, %d)", E, K, B, e0, e1);
-  DS_LAUNCH("ds_route", ds_route_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, E, K, B, e0, e1, sel,
-            wsel, slot_off, slot_tok, slot_w);
+  DS_LAUNCH("ds_route", ds_route_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, E, K, B, e0, e1,
+            n_shared, sel, wsel, slot_off, slot_tok, slot_w);
 }
 
 extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,

@@ -200,14 +200,11 @@ class DSModel:
         self.pos = z(1, dt=torch.int32)
         K = cfg.top_k
         self.sel, self.wsel = z(B * K, dt=torch.int32), z(B * K)
-        n_local = shard.e1 - shard.e0
-        self.slot_off, self.slot_tok, self.slot_w = z(n_local + 1, dt=torch.int32), z(B * K, dt=torch.int32), z(B * K)
-        ns = len(shard.shared)
-        self.sh_off = torch.arange(0, (ns + 1) * B, B, dtype=torch.int32, device=dev)
-        self.sh_tok = torch.arange(B, dtype=torch.int32, device=dev).repeat(max(ns, 1))
-        self.sh_w = torch.ones(max(ns, 1) * B, device=dev)
-        self.a = z(B * K, cfg.moe_inter, dt=torch.int16)
-        self.a_sh = z(max(ns, 1) * B, cfg.moe_inter, dt=torch.int16)
+        n_local, ns = shard.e1 - shard.e0, len(shard.shared)
+        # slot lists of the local routed experts, then the local shared halves (every token, weight 1)
+        self.slot_off = z(n_local + ns + 1, dt=torch.int32)
+        self.slot_tok, self.slot_w = z(B * (K + ns), dt=torch.int32), z(B * (K + ns))
+        self.a = z(B * (K + ns), cfg.moe_inter, dt=torch.int16)
         self.vals, self.idxs = z(1, B), z(1, B, dt=torch.int32)
         self.ws = z(int(self.lib.sm100_skinny_ws_bytes(B)) // 4)
         self.counters = z(cfg.vocab // 128 + 2, dt=torch.int32)
@@ -265,24 +262,17 @@ class DSModel:
                 self._skinny(self.xn, w[p + "d_down"], self.h, DI, D, residual=True)
                 continue
             self._skinny(self.xn, w[p + "router"], self.rl, D, E)
-            L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, self.sel.data_ptr(),
+            ns = len(sh.shared)
+            L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, ns, self.sel.data_ptr(),
                                        self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
                                        self.slot_w.data_ptr(), st()), "ds_route")
             self.moe.zero_()
-            n_local = sh.e1 - sh.e0
-            egu, egs, ed, eds = w[p + "e_gu"], w[p + "e_gu_s"], w[p + "e_d"], w[p + "e_d_s"]
-            if n_local:
-                L.check(lib.sm100_ds_experts(self.xn.data_ptr(), egu.data_ptr(), egs.data_ptr(), ed.data_ptr(),
-                                             eds.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
-                                             self.slot_w.data_ptr(), self.a.data_ptr(), self.moe.data_ptr(), n_local,
-                                             D, I, st()), "ds_experts")
-            if sh.shared:   # the shared halves follow the routed experts in this rank's arrays
-                L.check(lib.sm100_ds_experts(self.xn.data_ptr(), egu[n_local:].data_ptr(), egs[n_local:].data_ptr(),
-                                             ed[n_local:].data_ptr(), eds[n_local:].data_ptr(),
-                                             self.sh_off.data_ptr(), self.sh_tok.data_ptr(), self.sh_w.data_ptr(),
-                                             self.a_sh.data_ptr(), self.moe.data_ptr(), len(sh.shared), D, I, st()),
-                        "ds_experts shared")
-            self.launches += 1 + 2 * (bool(n_local) + bool(sh.shared))
+            # one launch pair over the local routed experts and shared halves (contiguous in this rank's arrays)
+            L.check(lib.sm100_ds_experts(self.xn.data_ptr(), w[p + "e_gu"].data_ptr(), w[p + "e_gu_s"].data_ptr(),
+                                         w[p + "e_d"].data_ptr(), w[p + "e_d_s"].data_ptr(), self.slot_off.data_ptr(),
+                                         self.slot_tok.data_ptr(), self.slot_w.data_ptr(), self.a.data_ptr(),
+                                         self.moe.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
+            self.launches += 3
             if sh.world > 1:
                 self.torch.distributed.all_reduce(self.moe, group=self.group)
             L.check(lib.sm100_add(self.h.data_ptr(), self.moe.data_ptr(), self.h.data_ptr(), B * D, st()), "add")
