@@ -439,12 +439,17 @@ int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const vo
 int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared,
                    int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
 /* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
- * experts: w_gu fp8 [n_exp][2I][D] + scales [n_exp][ceil(2I/128)][D/128],
- * w_d fp8 [n_exp][D][I] + scales [n_exp][D/128][ceil(I/128)]; x bf16 [B][D];
+ * experts on the tensor cores (fp8 weights times their block scale
+ * dequantised to bf16 tiles, tokens as the MMA's N <= 32): w_gu fp8
+ * [n_exp][2I][D] + scales [n_exp][2I/128][D/128], w_d fp8 [n_exp][D][I] +
+ * scales [n_exp][D/128][I/128]; D, I multiples of 128; x bf16 [B][D];
  * a_scratch bf16 [slots][I]; y f32 [B][D] (float reductions) */
 int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,
                      const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch, float *y,
                      int32_t n_exp, int32_t D, int32_t I, void *stream);
+/* non-zero when an expert launch since the last call gave up a bounded wait;
+ * synchronises the device and clears the word */
+uint32_t sm100_ds_status(void);
 /* a (bf16 [M][I]) = silu(gu[:, :I]) * gu[:, I:] of f32 gate|up rows [M][2I] */
 int sm100_ds_silu_mul(const float *gu, void *a, int32_t M, int32_t I, void *stream);
 

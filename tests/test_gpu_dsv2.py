@@ -47,6 +47,7 @@ def test_ds_decode_matches_oracle():
         tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt
     assert worst <= 2e-2, worst
     assert agree / total >= 0.99, agree / total
+    assert dev.lib.sm100_ds_status() == 0
     for l in range(cfg.n_layers):
         # layer 0's rows see identical inputs: a bf16 operand one rounding apart moves a value by
         # an ulp of its input, which the rotary can leave in a near-cancelled output (hence the

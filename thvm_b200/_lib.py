@@ -174,6 +174,7 @@ SIGNATURES = {
     "sm100_ds_experts": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                  c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
+    "sm100_ds_status": (c_uint32, []),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),

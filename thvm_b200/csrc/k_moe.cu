@@ -17,6 +17,7 @@
 #include <algorithm>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace sm100 {
 
@@ -267,154 +268,254 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
   }
 }
 
-// 16 fp8-e4m3 codes -> f32 times a block scale (hardware e4m3x2 -> f16x2
-// conversions; f16 holds every e4m3 value exactly).
-__device__ __forceinline__ void fp8x16(const uint4 w, float sc, float (&f)[16]) {
+// The experts on the 5th-generation tensor cores.  A work item is (expert e,
+// block of 128 weight rows); the weights stream from HBM as fp8 and are
+// dequantised (times their 128 x 128 block scale) to bf16 tiles in the MMA's
+// K-major 128-byte swizzle by 8 converter warps, one 128-column k-block at a
+// time into a 2-stage ring, next to the expert's tokens (up to 32, the MMA's N,
+// rows past the token count zero); one thread issues tcgen05.mma (M=128, N=32,
+// K=16, bf16) into a TMEM accumulator (two sets, so a work item's epilogue
+// overlaps the next one's products); 4 epilogue warps finish it:
+//   kUp:  rows j of gate and up (W_gu [2I][D]) -> a[slot][j] = bf16(silu(g) * u)
+//   down: rows r of W_d [D][I]               -> y[tok][r] += w_slot * sum
+// An expert without tokens costs one read of its slot count.  Every wait is
+// bounded; a timeout sets g_ds_status.
+__device__ uint32_t g_ds_status;
+
+constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-column swizzle halves)
+constexpr int kXmHalf = kXmTile / 2;
+constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
+constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
+
+template <bool kUp>
+__host__ __device__ constexpr int xm_stage() {
+  return (kUp ? 2 : 1) * kXmTile + kXmB;
+}
+template <bool kUp>
+__host__ __device__ constexpr int xm_smem() {
+  return 2 * xm_stage<kUp>() + 1024 + 256;
+}
+
+__device__ __forceinline__ uint64_t xm_desc(const void *p) {
+  const uint64_t a = smem_u32(p);
+  return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// 16 fp8-e4m3 codes times a scale -> 16 bf16 (8 words); e4m3 -> f16 is exact
+__device__ __forceinline__ void xm_dequant16(const uint4 w, float sc, uint32_t (&o)[8]) {
   const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int q = 0; q < 4; q++) {
 #pragma unroll
     for (int hlf = 0; hlf < 2; hlf++) {
-      const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu);
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+      const __half2_raw hr =
+          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu), __NV_E4M3);
       const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
-      f[4 * q + 2 * hlf] = v.x * sc;
-      f[4 * q + 2 * hlf + 1] = v.y * sc;
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v.x * sc, v.y * sc);
+      o[2 * q + hlf] = *reinterpret_cast<const uint32_t *>(&b2);
     }
   }
 }
 
-constexpr int kDsRows = 32;      // weight rows per work item
-constexpr int kDsTokChunk = 8;   // tokens staged in shared memory at a time
+template <bool kUp>
+__global__ void __launch_bounds__(kXmThreads, 1)
+    ds_xmma_kernel(const __nv_bfloat16 *xin, const uint8_t *w, const float *sc, const int32_t *slot_off,
+                   const int32_t *slot_tok, const float *slot_w, void *out, int D, int I, int64_t w_stride,
+                   int64_t s_stride, int n_exp) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  constexpr int kStage = xm_stage<kUp>(), kA = kUp ? 2 : 1;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kStage);
+  uint64_t *full = bars, *empty = bars + 2, *acc_full = bars + 4, *acc_empty = bars + 6, *done = bars + 8;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // rows of the product and its contraction: up: 128-row blocks of I, K = D; down: blocks of D, K = I
+  const int rows = kUp ? I : D, K = kUp ? D : I, nblk = rows / 128, nkb = K / 128;
+  const int sc_cols = kUp ? D / 128 : (I + 127) / 128;
+  uint32_t *status = &g_ds_status;
 
-// Experts, phase 1 (persistent, grid-stride over work items (expert e, block
-// of 32 rows); an expert without tokens costs one read of its slot count):
-// a[slot][j] = bf16(silu(x . gate_j) * (x . up_j)) for the expert's tokens,
-// gate / up fp8 rows [2I][D] with f32 scales [ceil(2I/128)][D/128].  Tokens
-// are staged 8 at a time in shared memory; a warp per row pair, lanes over
-// D in 16-byte fp8 chunks.
-__global__ void __launch_bounds__(256) ds_expert_up_kernel(const __nv_bfloat16 *x, const uint8_t *wgu,
-                                                            const float *sgu, const int32_t *slot_off,
-                                                            const int32_t *slot_tok, __nv_bfloat16 *a, int D, int I,
-                                                            int64_t w_stride, int64_t s_stride, int n_exp) {
-  extern __shared__ __nv_bfloat16 xs[];   // [kDsTokChunk][D]
   pdl_trigger();
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&full[i], kXmConv);
+      mbar_init(&empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kXmConv) {   // accumulators: 2 sets x kA x 32 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(128)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
   pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rb_n = (I + kDsRows - 1) / kDsRows;
-  const int sc_cols = D / 128;
-  for (int item = blockIdx.x; item < n_exp * rb_n; item += gridDim.x) {
-    const int e = item / rb_n, rb = item % rb_n, off = slot_off[e], n = slot_off[e + 1] - off;
-    if (n == 0) continue;
-    const uint8_t *we = wgu + (int64_t)e * w_stride;
-    const float *se = sgu + (int64_t)e * s_stride;
-    for (int t0 = 0; t0 < n; t0 += kDsTokChunk) {
-      const int nt = min(kDsTokChunk, n - t0);
-      __syncthreads();   // the previous chunk's readers are done
-      for (int i = threadIdx.x; i < nt * D / 8; i += 256) {
-        const int s = i / (D / 8), c = i % (D / 8);
-        reinterpret_cast<uint4 *>(xs)[(int64_t)s * (D / 8) + c] =
-            reinterpret_cast<const uint4 *>(x + (int64_t)slot_tok[off + t0 + s] * D)[c];
-      }
-      __syncthreads();
-      for (int r = warp; r < kDsRows; r += 8) {
-        const int j = rb * kDsRows + r;
-        if (j >= I) break;
-        float g[kDsTokChunk], u[kDsTokChunk];
+
+  if (warp < kXmConv) {
+    // converters: k-block kb of item: A tiles (dequantised rows) and the B tile (token rows)
+    const int ct = threadIdx.x;   // 0 .. 255
+    int g = 0;                    // k-blocks produced so far (ring position)
+    for (int item = blockIdx.x; item < n_exp * nblk; item += gridDim.x) {
+      const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
+      if (n == 0) continue;
+      const uint8_t *we = w + (int64_t)e * w_stride;
+      const float *se = sc + (int64_t)e * s_stride;
+      for (int kb = 0; kb < nkb; kb++, g++) {
+        const int s = g & 1;
+        if (g >= 2 && !mbar_wait(&empty[s], (uint32_t)(((g >> 1) - 1) & 1), status)) break;
+        unsigned char *st = smem + s * kStage;
+        // all of this k-block's loads first (one memory round trip), then convert:
+        // 128 rows x 128 fp8 per tile, 8 lanes per row (16 codes each), 32 rows per pass
+        const int c16 = ct & 7, h = c16 >> 2, c = (c16 & 3) * 2;
+        uint4 raw[kA][4];
+        float scl[kA];
 #pragma unroll
-        for (int s = 0; s < kDsTokChunk; s++) g[s] = u[s] = 0.0f;
-        for (int k0 = lane * 16; k0 < D; k0 += 512) {
-          float fg[16], fu[16];
-          fp8x16(*reinterpret_cast<const uint4 *>(we + (int64_t)j * D + k0), se[(j / 128) * sc_cols + k0 / 128], fg);
-          fp8x16(*reinterpret_cast<const uint4 *>(we + (int64_t)(I + j) * D + k0),
-                 se[((I + j) / 128) * sc_cols + k0 / 128], fu);
+        for (int t = 0; t < kA; t++) {
+          const int row0 = (t == 0 ? 0 : I) + blk * 128;
+          scl[t] = se[(row0 / 128) * sc_cols + kb];
 #pragma unroll
-          for (int s = 0; s < kDsTokChunk; s++) {
-            if (s >= nt) continue;
-            const uint4 *xr = reinterpret_cast<const uint4 *>(xs + (int64_t)s * D + k0);
-            float ag = 0.0f, au = 0.0f;
+          for (int pss = 0; pss < 4; pss++)
+            raw[t][pss] = *reinterpret_cast<const uint4 *>(we + (int64_t)(row0 + (ct >> 3) + 32 * pss) * K +
+                                                           kb * 128 + c16 * 16);
+        }
 #pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const uint4 xv = xr[h];
-              const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+        for (int t = 0; t < kA; t++)
 #pragma unroll
-              for (int q = 0; q < 4; q++) {
-                const float x0 = __uint_as_float(xw[q] << 16), x1 = __uint_as_float(xw[q] & 0xFFFF0000u);
-                ag = fmaf(fg[8 * h + 2 * q], x0, fmaf(fg[8 * h + 2 * q + 1], x1, ag));
-                au = fmaf(fu[8 * h + 2 * q], x0, fmaf(fu[8 * h + 2 * q + 1], x1, au));
-              }
-            }
-            g[s] += ag;
-            u[s] += au;
+          for (int pss = 0; pss < 4; pss++) {
+            const int rr = (ct >> 3) + 32 * pss;
+            uint32_t o[8];
+            xm_dequant16(raw[t][pss], scl[t], o);
+            unsigned char *dst = st + t * kXmTile + h * kXmHalf + rr * 128;
+            *reinterpret_cast<uint4 *>(dst + ((c ^ (rr & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (rr & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
+        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes
+        unsigned char *bt = st + kA * kXmTile;
+        for (int i = ct; i < 32 * 16; i += kXmConv * 32) {
+          const int r = i >> 4, cc = i & 15, h = cc >> 3, c = cc & 7;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (r < n) {
+            const int64_t src_row = kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r);
+            v = *reinterpret_cast<const uint4 *>(xin + src_row * K + kb * 128 + cc * 8);
+          }
+          *reinterpret_cast<uint4 *>(bt + h * (kXmB / 2) + r * 128 + ((c ^ (r & 7)) * 16)) = v;
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
+      }
+    }
+  } else if (warp == kXmConv) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(32 >> 3) << 17) |
+                                 ((uint32_t)(128 >> 4) << 24);
+      int g = 0, it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_exp * nblk && ok; item += gridDim.x) {
+        const int e = item / nblk, n = slot_off[e + 1] - slot_off[e];
+        if (n == 0) continue;
+        const int a = it & 1;
+        if (it >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((it >> 1) - 1) & 1), status)) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        for (int kb = 0; kb < nkb; kb++, g++) {
+          const int s = g & 1;
+          if (!mbar_wait(&full[s], (uint32_t)((g >> 1) & 1), status)) { ok = false; break; }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const unsigned char *st = smem + s * kStage, *bt = st + kA * kXmTile;
 #pragma unroll
-        for (int s = 0; s < kDsTokChunk; s++) {
-          if (s >= nt) continue;
-          const float gs = warp_sum(g[s]), us = warp_sum(u[s]);
-          if (lane == 0) a[(int64_t)(off + t0 + s) * I + j] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
+          for (int kk = 0; kk < 8; kk++) {
+            const int h = kk >> 2, o16 = 2 * (kk & 3);
+            const uint64_t db = xm_desc(bt + h * (kXmB / 2)) + o16;
+#pragma unroll
+            for (int t = 0; t < kA; t++)
+              asm volatile(
+                  "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
+                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * 64 + t * 32)),
+                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16), "l"(db), "r"(idesc),
+                  "r"((kb > 0 || kk > 0) ? 1u : 0u)
+                  : "memory");
+          }
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(&empty[s]))
+                       : "memory");
+        }
+        if (!ok) break;
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&acc_full[a]))
+                     : "memory");
+        it++;
+      }
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(done))
+                   : "memory");
+    }
+  } else {
+    // epilogue: warp % 4 = TMEM lane quarter = row quarter of the block
+    const int q = warp & 3, row = q * 32 + lane;
+    const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
+    int it = 0;
+    for (int item = blockIdx.x; item < n_exp * nblk; item += gridDim.x) {
+      const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
+      if (n == 0) continue;
+      const int a = it & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[a], (uint32_t)((it >> 1) & 1), status))) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      uint32_t v0[32], v1[32];
+      asm volatile(
+          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+          "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+          : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
+            "=r"(v0[8]), "=r"(v0[9]), "=r"(v0[10]), "=r"(v0[11]), "=r"(v0[12]), "=r"(v0[13]), "=r"(v0[14]),
+            "=r"(v0[15]), "=r"(v0[16]), "=r"(v0[17]), "=r"(v0[18]), "=r"(v0[19]), "=r"(v0[20]), "=r"(v0[21]),
+            "=r"(v0[22]), "=r"(v0[23]), "=r"(v0[24]), "=r"(v0[25]), "=r"(v0[26]), "=r"(v0[27]), "=r"(v0[28]),
+            "=r"(v0[29]), "=r"(v0[30]), "=r"(v0[31])
+          : "r"(tq + (uint32_t)(a * 64)));
+      if (kUp)
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+            "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
+              "=r"(v1[8]), "=r"(v1[9]), "=r"(v1[10]), "=r"(v1[11]), "=r"(v1[12]), "=r"(v1[13]), "=r"(v1[14]),
+              "=r"(v1[15]), "=r"(v1[16]), "=r"(v1[17]), "=r"(v1[18]), "=r"(v1[19]), "=r"(v1[20]), "=r"(v1[21]),
+              "=r"(v1[22]), "=r"(v1[23]), "=r"(v1[24]), "=r"(v1[25]), "=r"(v1[26]), "=r"(v1[27]), "=r"(v1[28]),
+              "=r"(v1[29]), "=r"(v1[30]), "=r"(v1[31])
+            : "r"(tq + (uint32_t)(a * 64 + 32)));
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      const int r = blk * 128 + row;
+      if (kUp) {
+        __nv_bfloat16 *ao = reinterpret_cast<__nv_bfloat16 *>(out);
+#pragma unroll
+        for (int s = 0; s < 32; s++) {
+          if (s >= n) continue;
+          const float gs = __uint_as_float(v0[s]), us = __uint_as_float(v1[s]);
+          ao[(int64_t)(off + s) * I + r] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
+        }
+      } else {
+        float *y = reinterpret_cast<float *>(out);
+#pragma unroll
+        for (int s = 0; s < 32; s++) {
+          if (s >= n) continue;
+          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * __uint_as_float(v0[s]));
         }
       }
+      it++;
     }
   }
-}
-
-// Experts, phase 2 (persistent over (expert, block of 32 output rows)):
-// y[tok][r] += w_slot * sum_j a[slot][j] W_d[e][r][j] (fp8 [D][I], scales
-// [D/128][ceil(I/128)]); the experts of a token meet in y by float reductions.
-__global__ void __launch_bounds__(256) ds_expert_down_kernel(const __nv_bfloat16 *a, const uint8_t *wd, const float *sd,
-                                                              const int32_t *slot_off, const int32_t *slot_tok,
-                                                              const float *slot_w, float *y, int D, int I,
-                                                              int64_t w_stride, int64_t s_stride, int n_exp) {
-  extern __shared__ __nv_bfloat16 as[];   // [kDsTokChunk][I]
-  pdl_trigger();
-  pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, rb_n = (D + kDsRows - 1) / kDsRows;
-  const int sc_cols = (I + 127) / 128;
-  for (int item = blockIdx.x; item < n_exp * rb_n; item += gridDim.x) {
-    const int e = item / rb_n, rb = item % rb_n, off = slot_off[e], n = slot_off[e + 1] - off;
-    if (n == 0) continue;
-    for (int t0 = 0; t0 < n; t0 += kDsTokChunk) {
-      const int nt = min(kDsTokChunk, n - t0);
-      __syncthreads();
-      for (int i = threadIdx.x; i < nt * I / 8; i += 256)
-        reinterpret_cast<uint4 *>(as)[i] = reinterpret_cast<const uint4 *>(a + (int64_t)(off + t0) * I)[i];
-      __syncthreads();
-      for (int rr = warp; rr < kDsRows; rr += 8) {
-        const int r = rb * kDsRows + rr;
-        if (r >= D) break;
-        const uint8_t *we = wd + (int64_t)e * w_stride + (int64_t)r * I;
-        const float *se = sd + (int64_t)e * s_stride + (int64_t)(r / 128) * sc_cols;
-        float acc[kDsTokChunk];
-#pragma unroll
-        for (int s = 0; s < kDsTokChunk; s++) acc[s] = 0.0f;
-        for (int k0 = lane * 16; k0 < I; k0 += 512) {
-          float f[16];
-          fp8x16(*reinterpret_cast<const uint4 *>(we + k0), se[k0 / 128], f);
-#pragma unroll
-          for (int s = 0; s < kDsTokChunk; s++) {
-            if (s >= nt) continue;
-            const uint4 *ar = reinterpret_cast<const uint4 *>(as + (int64_t)s * I + k0);
-            float t = 0.0f;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-              const uint4 av = ar[h];
-              const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
-#pragma unroll
-              for (int q = 0; q < 4; q++)
-                t = fmaf(f[8 * h + 2 * q], __uint_as_float(aw[q] << 16),
-                         fmaf(f[8 * h + 2 * q + 1], __uint_as_float(aw[q] & 0xFFFF0000u), t));
-            }
-            acc[s] += t;
-          }
-        }
-#pragma unroll
-        for (int s = 0; s < kDsTokChunk; s++) {
-          if (s >= nt) continue;
-          const float v = warp_sum(acc[s]);
-          if (lane == 0) atomicAdd(y + (int64_t)slot_tok[off + t0 + s] * D + r, slot_w[off + t0 + s] * v);
-        }
-      }
-    }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == kXmConv) {
+    if (lane == 0) mbar_wait(done, 0, status, false);
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
   }
 }
 
@@ -492,25 +593,33 @@ extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_
                                 const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch,
                                 float *y, int32_t n_exp, int32_t D, int32_t I, void *stream) {
   if (!x || !w_gu || !s_gu || !w_d || !s_d || !slot_off || !slot_tok || !slot_w || !a_scratch || !y || n_exp < 1 ||
-      D % 512 || I % 16 || D > 16384 || I > 16384)
-    return sm100_set_error(SM100_ERR_ARG, "ds_experts: n_exp %d D %d I %d (D %% 512 == 0, I %% 16 == 0)", n_exp, D, I);
-  const int64_t sc_gu = (int64_t)((2 * I + 127) / 128) * (D / 128), sc_d = (int64_t)(D / 128) * ((I + 127) / 128);
-  const size_t smem_up = (size_t)kDsTokChunk * D * 2, smem_dn = (size_t)kDsTokChunk * I * 2;
-  cudaError_t e = cudaFuncSetAttribute(ds_expert_up_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_up);
+      D % 128 || I % 128 || D < 128 || I < 128)
+    return sm100_set_error(SM100_ERR_ARG, "ds_experts: n_exp %d D %d I %d (D, I multiples of 128)", n_exp, D, I);
+  const int64_t sc_gu = (int64_t)(2 * I / 128) * (D / 128), sc_d = (int64_t)(D / 128) * (I / 128);
+  constexpr int smem_up = xm_smem<true>(), smem_dn = xm_smem<false>();
+  cudaError_t e = cudaFuncSetAttribute(ds_xmma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(ds_expert_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_dn);
+    e = cudaFuncSetAttribute(ds_xmma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dn);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: smem attribute: %s", cudaGetErrorString(e));
-  const int items_up = n_exp * ((I + kDsRows - 1) / kDsRows), items_dn = n_exp * ((D + kDsRows - 1) / kDsRows);
-  e = launch_pdl(ds_expert_up_kernel, dim3(std::min(items_up, 4 * 148)), dim3(256), smem_up, (cudaStream_t)stream,
-                 (const __nv_bfloat16 *)x, (const uint8_t *)w_gu, s_gu, slot_off, slot_tok, (__nv_bfloat16 *)a_scratch,
-                 D, I, (int64_t)2 * I * D, sc_gu, n_exp);
+  const int items_up = n_exp * (I / 128), items_dn = n_exp * (D / 128);
+  e = launch_pdl(ds_xmma_kernel<true>, dim3(std::min(items_up, 148)), dim3(kXmThreads), smem_up, (cudaStream_t)stream,
+                 (const __nv_bfloat16 *)x, (const uint8_t *)w_gu, s_gu, slot_off, slot_tok, slot_w, a_scratch, D, I,
+                 (int64_t)2 * I * D, sc_gu, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: up: %s", cudaGetErrorString(e));
   launch_status("ds_expert_up");
-  e = launch_pdl(ds_expert_down_kernel, dim3(std::min(items_dn, 4 * 148)), dim3(256), smem_dn, (cudaStream_t)stream,
-                 (const __nv_bfloat16 *)a_scratch, (const uint8_t *)w_d, s_d, slot_off, slot_tok, slot_w, y, D, I,
-                 (int64_t)D * I, sc_d, n_exp);
+  e = launch_pdl(ds_xmma_kernel<false>, dim3(std::min(items_dn, 148)), dim3(kXmThreads), smem_dn, (cudaStream_t)stream,
+                 (const __nv_bfloat16 *)a_scratch, (const uint8_t *)w_d, s_d, slot_off, slot_tok, slot_w, (void *)y, D,
+                 I, (int64_t)D * I, sc_d, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: down: %s", cudaGetErrorString(e));
   return launch_status("ds_expert_down");
+}
+
+extern "C" uint32_t sm100_ds_status(void) {
+  uint32_t v = 0, z = 0;
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(&v, g_ds_status, sizeof(v));
+  cudaMemcpyToSymbol(g_ds_status, &z, sizeof(z));
+  return v;
 }
 
 extern "C" int sm100_ds_silu_mul(const float *gu, void *a, int32_t M, int32_t I, void *stream) {
