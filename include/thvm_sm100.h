@@ -281,11 +281,12 @@ int sm100_pos_add(int32_t *counter, int32_t value, void *stream);
  * io = [position, token] int32 is read at the start and, unless an error
  * was flagged, the next token written to io[1] (and io[0] += 1 when bump). */
 #define SM100_DECODE_MAX_LAYERS 48
-#define SM100_DECODE_REPLICAS 8   /* copies of every step output a launch writes */
+#define SM100_DECODE_REPLICAS 8   /* copies of the per-CTA argmax partials a launch writes */
 enum {
   SM100_DECODE_ERR_STALL = 1u << 0,   /* a ring (mbarrier) wait timed out */
   SM100_DECODE_ERR_BARRIER = 1u << 1, /* a wait for another CTA's output timed out */
-  SM100_DECODE_ERR_ARG = 1u << 2      /* position outside [0, max_ctx) */
+  SM100_DECODE_ERR_ARG = 1u << 2,     /* position outside [0, max_ctx) */
+  SM100_DECODE_ERR_RANGE = 1u << 3    /* a split partial sum outside +-2048 (or NaN) */
 };
 typedef struct {
   int32_t n_layers, dim, hidden, vocab, max_ctx, heads, head_dim, bump;
@@ -293,41 +294,55 @@ typedef struct {
   const float *wte, *wpe, *ln_f_g, *ln_f_b, *lm_head;
   const float *ln1_g[SM100_DECODE_MAX_LAYERS], *ln1_b[SM100_DECODE_MAX_LAYERS];
   const float *w_qkv[SM100_DECODE_MAX_LAYERS], *b_qkv[SM100_DECODE_MAX_LAYERS];
-  const float *w_o[SM100_DECODE_MAX_LAYERS], *b_o[SM100_DECODE_MAX_LAYERS];
+  const float *b_o[SM100_DECODE_MAX_LAYERS];
   const float *ln2_g[SM100_DECODE_MAX_LAYERS], *ln2_b[SM100_DECODE_MAX_LAYERS];
   const float *w_fc[SM100_DECODE_MAX_LAYERS], *b_fc[SM100_DECODE_MAX_LAYERS];
-  const float *w_p2[SM100_DECODE_MAX_LAYERS], *b_p2[SM100_DECODE_MAX_LAYERS];
+  const float *b_p2[SM100_DECODE_MAX_LAYERS];
+  /* the two split projections, regrouped once at load (sm100_decode_regroup):
+   * c_proj [heads][dim][head_dim] (w_o_h[h][o][d] = W_o[o][h head_dim + d]),
+   * mlp.c_proj transposed [hidden][dim] (w_p2_t[k][o] = W_p2[o][k]) */
+  const float *w_o_h[SM100_DECODE_MAX_LAYERS], *w_p2_t[SM100_DECODE_MAX_LAYERS];
   float *kv_cache[SM100_DECODE_MAX_LAYERS]; /* [2, max_ctx, dim] each */
   int32_t *io;                              /* [position, token] */
-  /* step outputs as tagged words (float bits | tag << 32), zero-initialised,
-   * SM100_DECODE_REPLICAS copies of each: x [R][dim], qkv [R][3 dim],
-   * att [R][dim], fc [R][hidden] */
-  uint64_t *x_w, *qkv_w, *att_w, *fc_w;
+  /* zero-initialised scratch: q, k, v of the new row as tagged words (float
+   * bits | tag << 32), [3 dim]; the split sums' reduction words,
+   * sm100_decode_red_bytes() */
+  uint64_t *qkv_w, *red_w;
   uint64_t *part_w;                         /* per-CTA argmax partials, sm100_decode_part_bytes() */
   float *logits;                            /* [vocab], or NULL: not stored */
-  /* optional timeline of the last token of a launch, or NULL: [grid][5
-   * n_layers + 1][8] u64 global-timer ns per CTA and step: 0 step start, 1
-   * input landed, 2 weights landed (attention: scores done), 3 input in
-   * registers (attention: softmax done), 4 step done, 5 the step's weight
-   * transfer issued, 6 its issue began waiting for a free stage, 7 unused
+  /* optional timeline of the last token of a launch, or NULL: [grid][3
+   * n_layers + 1][8] u64 global-timer ns per CTA and step (per layer: c_attn,
+   * attention + c_proj, c_fc + mlp.c_proj; then lm_head): 0 step start, 1
+   * thread 0's input landed (attention: every input), 2 weights landed
+   * (attention: softmax done), 3 every input landed (attention: its output
+   * done), 4 step done, 5 the step's weight transfer issued, 6 its issue
+   * began waiting for a free stage, 7 LayerNorm done
    * (sm100_decode_trace_bytes) */
   uint64_t *trace;
-  /* zero-initialised scratch of sm100_decode_sync_bytes(): sync[1] completion
-   * counter (reset by the kernel), sync[2] the sticky status word
-   * (SM100_DECODE_ERR_* bits; cleared by the caller), sync[3] the launch
-   * epoch the tags derive from, then per-CTA argmax partials */
+  /* zero-initialised scratch of sm100_decode_sync_bytes(): sync[2] the sticky
+   * status word (SM100_DECODE_ERR_* bits; cleared by the caller), sync[3] the
+   * launch epoch the tags derive from, sync[4] the tokens decoded so far (a
+   * token uses reduction set sync[4] mod 3 and clears the next one) */
   uint32_t *sync;
 } Sm100DecodeModel;
 uint64_t sm100_decode_sync_bytes(void);
 uint64_t sm100_decode_part_bytes(void);
 uint64_t sm100_decode_trace_bytes(int32_t n_layers);
+uint64_t sm100_decode_red_bytes(int32_t n_layers, int32_t dim);
+/* CTAs of a decode launch on the current device (heads x members per head;
+ * 144 for GPT-2 small on 148 SMs), 0 when the shape has no split */
+int32_t sm100_decode_grid(int32_t heads, int32_t head_dim);
+/* the regrouped weights of one layer from the reference's layouts: w_o_h
+ * [heads][dim][head_dim] from c_proj W_o [dim][dim], w_p2_t [hidden][dim]
+ * from mlp.c_proj W_p2 [dim][hidden] (device pointers, f32) */
+int sm100_decode_regroup(const float *w_o, const float *w_p2, float *w_o_h, float *w_p2_t, int32_t dim,
+                         int32_t heads, int32_t hidden, void *stream);
 /* n_tokens greedy tokens in one launch (positions io[0] .. io[0]+n-1, each
  * token's argmax feeding the next).  The scalars repeat the descriptor's
- * (the host checks the shape with them): dim % 128 == 0 and dim in {512, 768,
- * 1024}, heads * 64 == dim or heads * 32 == dim, hidden = 4 dim,
- * 2 max_ctx + 3 head_dim + 512 <= 8192, n_tokens * (5 n_layers + 2) < 65536,
- * and one projection CTA's row slice of every projection within 88 KB
- * (GPT-2 small on 148 SMs: 12 attention CTAs + 136 projection CTAs). */
+ * (the host checks the shape with them): dim in {512, 768}, heads * 64 ==
+ * dim or heads * 32 == dim, hidden = 4 dim, n_tokens * (n_layers + 2) <
+ * 65536, and one CTA's slice of every projection within one 76 KB stage
+ * (GPT-2 small on 148 SMs: 12 heads x 12 members). */
 int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_tokens, int32_t n_layers,
                        int32_t dim, int32_t heads, int32_t vocab, int32_t max_ctx, void *stream);
 /* one token: sm100_decode_steps with n_tokens = 1 */

@@ -85,9 +85,9 @@ class Sm100DecodeModel(ctypes.Structure):
                                        "bump")] + [
         ("eps", c_float), ("attn_scale", c_float)] + [
         (n, c_void_p) for n in ("wte", "wpe", "ln_f_g", "ln_f_b", "lm_head")] + [
-        (n, _PL) for n in ("ln1_g", "ln1_b", "w_qkv", "b_qkv", "w_o", "b_o", "ln2_g", "ln2_b", "w_fc", "b_fc",
-                           "w_p2", "b_p2", "kv_cache")] + [
-        (n, c_void_p) for n in ("io", "x_w", "qkv_w", "att_w", "fc_w", "part_w", "logits", "trace", "sync")]
+        (n, _PL) for n in ("ln1_g", "ln1_b", "w_qkv", "b_qkv", "b_o", "ln2_g", "ln2_b", "w_fc", "b_fc",
+                           "b_p2", "w_o_h", "w_p2_t", "kv_cache")] + [
+        (n, c_void_p) for n in ("io", "qkv_w", "red_w", "part_w", "logits", "trace", "sync")]
 
 
 # name -> (restype, argtypes): every symbol include/thvm_sm100.h declares.
@@ -144,6 +144,9 @@ SIGNATURES = {
     "sm100_decode_sync_bytes": (c_uint64, []),
     "sm100_decode_trace_bytes": (c_uint64, [c_int32]),
     "sm100_decode_part_bytes": (c_uint64, []),
+    "sm100_decode_red_bytes": (c_uint64, [c_int32, c_int32]),
+    "sm100_decode_grid": (c_int32, [c_int32, c_int32]),
+    "sm100_decode_regroup": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),

@@ -167,8 +167,8 @@ class Transformer:
     @staticmethod
     def fused_fits(cfg: GPT2Config) -> bool:
         """Shapes the fused decode-step kernel takes (include/thvm_sm100.h)."""
-        return (cfg.n_layers <= L.DECODE_MAX_LAYERS and cfg.dim in (512, 768, 1024)
-                and cfg.head_dim in (32, 64) and 2 * cfg.max_ctx + 3 * cfg.head_dim + 512 <= 8192)
+        return (cfg.n_layers <= L.DECODE_MAX_LAYERS and cfg.dim in (512, 768)
+                and cfg.head_dim in (32, 64) and cfg.hidden == 4 * cfg.dim)
 
     def _build_fused(self) -> None:
         """The device-resident Sm100DecodeModel over this model's buffers."""
@@ -183,15 +183,24 @@ class Transformer:
         for i, blk in enumerate(self.h):
             m.ln1_g[i], m.ln1_b[i] = p(blk.ln_1.g), p(blk.ln_1.b)
             m.w_qkv[i], m.b_qkv[i] = p(blk.attn.c_attn.w), p(blk.attn.c_attn.b)
-            m.w_o[i], m.b_o[i] = p(blk.attn.c_proj.w), p(blk.attn.c_proj.b)
+            m.b_o[i] = p(blk.attn.c_proj.b)
             m.ln2_g[i], m.ln2_b[i] = p(blk.ln_2.g), p(blk.ln_2.b)
             m.w_fc[i], m.b_fc[i] = p(blk.mlp.c_fc.w), p(blk.mlp.c_fc.b)
-            m.w_p2[i], m.b_p2[i] = p(blk.mlp.c_proj.w), p(blk.mlp.c_proj.b)
+            m.b_p2[i] = p(blk.mlp.c_proj.b)
             m.kv_cache[i] = p(blk.attn.cache_kv)
-        # the kernel's step outputs: tagged 8-byte words, zero-initialised
-        self.words = [dev.alloc(8 * L.DECODE_REPLICAS * n) for n in (cfg.dim, 3 * cfg.dim, cfg.dim, cfg.hidden)]
+        # the split projections regrouped once: c_proj per head, mlp.c_proj transposed
+        self.regrouped = []
+        for i, blk in enumerate(self.h):
+            w_o_h, w_p2_t = dev.alloc(4 * cfg.dim * cfg.dim), dev.alloc(4 * cfg.hidden * cfg.dim)
+            L.check(dev.lib.sm100_decode_regroup(p(blk.attn.c_proj.w), p(blk.mlp.c_proj.w), p(w_o_h), p(w_p2_t),
+                                                 cfg.dim, cfg.n_heads, cfg.hidden, dev.stream), "decode_regroup")
+            self.regrouped += [w_o_h, w_p2_t]
+            m.w_o_h[i], m.w_p2_t[i] = p(w_o_h), p(w_p2_t)
+        dev.sync()
+        # the kernel's scratch words, zero-initialised: q/k/v of the new row, reduction sets
+        self.words = [dev.alloc(8 * 3 * cfg.dim), dev.alloc(dev.lib.sm100_decode_red_bytes(cfg.n_layers, cfg.dim))]
         m.io = p(s.io)
-        m.x_w, m.qkv_w, m.att_w, m.fc_w = (p(b) for b in self.words)
+        m.qkv_w, m.red_w = (p(b) for b in self.words)
         self.part = dev.alloc(dev.lib.sm100_decode_part_bytes())
         m.part_w = p(self.part)
         m.logits = p(s.logits)
@@ -222,10 +231,11 @@ class Transformer:
             m.trace = None
         L.check(self.dev.lib.sm100_buf_write(self.desc, ctypes.addressof(m), ctypes.sizeof(m)), "buf_write(desc)")
 
-    def read_trace(self, grid: int) -> np.ndarray:
-        """[grid, 5 n_layers + 1, 8] global-timer ns per CTA and step (the
+    def read_trace(self) -> np.ndarray:
+        """[grid, 3 n_layers + 1, 8] global-timer ns per CTA and step (the
         slots include/thvm_sm100.h lists for Sm100DecodeModel.trace)."""
-        n = grid * (5 * self.cfg.n_layers + 1) * 8
+        grid = self.dev.lib.sm100_decode_grid(self.cfg.n_heads, self.cfg.head_dim)
+        n = grid * (3 * self.cfg.n_layers + 1) * 8
         return self.dev.read(self.trace, np.uint64, (n,)).reshape(grid, -1, 8)
 
     def step_ops(self) -> list:
@@ -239,7 +249,9 @@ class Transformer:
             return 0
         st = int(self.dev.read(self.sync, np.uint32, (4,))[2])
         if clear and st:
-            self.dev.write(self.sync, np.zeros(4, np.uint32))
+            # the status word only: sync[3] (the launch epoch) selects the
+            # reduction set the next launch may use
+            self.dev.write(self.sync, np.zeros(1, np.uint32), byte_off=8)
         return st
 
     # ---- the schedule ---------------------------------------------------
