@@ -289,6 +289,10 @@ enum {
   SM100_DECODE_ERR_RANGE = 1u << 3    /* a split partial sum outside +-2048 (or NaN) */
 };
 typedef struct {
+  /* per layer a 2-D TMA tensor map over its KV cache viewed as [2 max_ctx,
+   * dim] f32, box [32 rows, head_dim]; filled by sm100_decode_prepare (the
+   * descriptor's device copy must be 64-byte aligned) */
+  uint8_t kv_map[SM100_DECODE_MAX_LAYERS][128];
   int32_t n_layers, dim, hidden, vocab, max_ctx, heads, head_dim, bump;
   float eps, attn_scale;
   const float *wte, *wpe, *ln_f_g, *ln_f_b, *lm_head;
@@ -329,6 +333,9 @@ uint64_t sm100_decode_sync_bytes(void);
 uint64_t sm100_decode_part_bytes(void);
 uint64_t sm100_decode_trace_bytes(int32_t n_layers);
 uint64_t sm100_decode_red_bytes(int32_t n_layers, int32_t dim);
+/* fills desc->kv_map from kv_cache, max_ctx, dim and head_dim (host memory;
+ * call before uploading the descriptor) */
+int sm100_decode_prepare(Sm100DecodeModel *desc);
 /* CTAs of a decode launch on the current device (heads x members per head;
  * 144 for GPT-2 small on 148 SMs), 0 when the shape has no split */
 int32_t sm100_decode_grid(int32_t heads, int32_t head_dim);

@@ -81,7 +81,7 @@ _PL = ctypes.c_void_p * DECODE_MAX_LAYERS
 
 
 class Sm100DecodeModel(ctypes.Structure):
-    _fields_ = [(n, c_int32) for n in ("n_layers", "dim", "hidden", "vocab", "max_ctx", "heads", "head_dim",
+    _fields_ = [("kv_map", (ctypes.c_uint8 * 128) * DECODE_MAX_LAYERS)] + [(n, c_int32) for n in ("n_layers", "dim", "hidden", "vocab", "max_ctx", "heads", "head_dim",
                                        "bump")] + [
         ("eps", c_float), ("attn_scale", c_float)] + [
         (n, c_void_p) for n in ("wte", "wpe", "ln_f_g", "ln_f_b", "lm_head")] + [
@@ -146,6 +146,7 @@ SIGNATURES = {
     "sm100_decode_part_bytes": (c_uint64, []),
     "sm100_decode_red_bytes": (c_uint64, [c_int32, c_int32]),
     "sm100_decode_grid": (c_int32, [c_int32, c_int32]),
+    "sm100_decode_prepare": (c_int, [c_void_p]),
     "sm100_decode_regroup": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),

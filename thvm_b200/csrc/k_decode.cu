@@ -46,6 +46,8 @@
 // returns at once, the kernel runs to its end, and every CTA waits (bounded)
 // for its in-flight bulk copies before it exits.  One CTA per SM, launched
 // cooperatively (the spin-waits need every CTA resident).
+#include <cuda.h>
+
 #include "common.cuh"
 #include "tma.cuh"
 
@@ -68,6 +70,9 @@ constexpr int kTraceSlots = 8;               // u64 timestamps per (CTA, step) i
 constexpr size_t kPartWords = 2 * 1024;      // argmax partials of one copy: (value, index) per CTA
 constexpr int kFixShift = 28;                // reduction words: fixed point with 28 fraction bits
 constexpr float kFixLimit = 2048.0f;         // |contribution| bound (sums stay below 2^47 / 2^28)
+constexpr int kBoxRows = 32;                 // KV staging: rows of one tensor-map box
+constexpr int kCpRows = 5;                   // c_proj rows per warp (a member has <= kCpRows kWarps)
+constexpr int kLmEarly = 6;                  // lm_head L2 prefetch spread over the last layers
 
 // Argmax partials go to kReplicas copies; consumer CTA c polls copy c % kReplicas
 // (every CTA reads every CTA's partial).
@@ -124,18 +129,26 @@ __device__ __forceinline__ void wait_words(const uint64_t *p, int stride, int n,
   for (int i = 0; i < N; i++) out[i] = (i < n && !((pending >> i) & 1u)) ? __uint_as_float((uint32_t)w[i]) : 0.0f;
 }
 
-// One pair of tagged words (p[0], p[1]) with a 16-byte load per poll (bounded).
+// One pair of tagged words (p[0], p[1]) with a 16-byte load per poll
+// (bounded); the re-poll loop is out of line (the hot path is one load).
+__device__ __noinline__ float2 wait_pair_slow(const uint64_t *p, uint32_t tag, uint32_t *status) {
+  uint64_t a, b;
+  for (uint32_t it = 0; it < (1u << 22); it++) {
+    if ((it & 15u) == 15u && *(volatile uint32_t *)status) return make_float2(0.0f, 0.0f);
+    ld_pair(p, a, b);
+    if ((uint32_t)(a >> 32) == tag && (uint32_t)(b >> 32) == tag)
+      return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+  }
+  atomicOr(status, SM100_DECODE_ERR_BARRIER);
+  return make_float2(0.0f, 0.0f);
+}
+
 __device__ __forceinline__ float2 wait_pair(const uint64_t *p, uint32_t tag, uint32_t *status) {
   uint64_t a, b;
   ld_pair(p, a, b);
-  for (uint32_t it = 0; (uint32_t)(a >> 32) != tag || (uint32_t)(b >> 32) != tag; it++) {
-    if (it >= (1u << 22) || ((it & 15u) == 15u && *(volatile uint32_t *)status)) {
-      if (it >= (1u << 22)) atomicOr(status, SM100_DECODE_ERR_BARRIER);
-      return make_float2(0.0f, 0.0f);
-    }
-    ld_pair(p, a, b);
-  }
-  return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+  if ((uint32_t)(a >> 32) == tag && (uint32_t)(b >> 32) == tag)
+    return make_float2(__uint_as_float((uint32_t)a), __uint_as_float((uint32_t)b));
+  return wait_pair_slow(p, tag, status);
 }
 
 // ---- reduction words -------------------------------------------------------
@@ -143,9 +156,11 @@ __device__ __forceinline__ float2 wait_pair(const uint64_t *p, uint32_t tag, uin
 // 2^64).  After C contributions (count taken mod 2^16) the word minus C << 48
 // is the exact fixed-point sum, |sum| < 2^47; with k < 2^15 contributions
 // still missing it lies at least 2^47 away from that range.
+__device__ __noinline__ void flag_range(uint32_t *status) { atomicOr(status, SM100_DECODE_ERR_RANGE); }
+
 __device__ __forceinline__ void red_word(uint64_t *p, float v, uint32_t *status) {
   if (!(fabsf(v) <= kFixLimit)) {   // also NaN: flagged, counted as 0
-    atomicOr(status, SM100_DECODE_ERR_RANGE);
+    flag_range(status);
     v = 0.0f;
   }
   const long long q = __float2ll_rn(v * (float)(1 << kFixShift));   // exact scaling by 2^28
@@ -162,18 +177,24 @@ __device__ __forceinline__ float red_value(uint64_t w, uint64_t C) {
   return __ll2float_rn((long long)(w - (C << 48))) * (1.0f / (float)(1 << kFixShift));
 }
 
-// The pair of reduction words (p[0], p[1]) once both counts reach C (bounded).
+// The pair of reduction words (p[0], p[1]) once both counts reach C
+// (bounded; the re-poll loop out of line).
+__device__ __noinline__ float2 wait_red_pair_slow(const uint64_t *p, uint64_t C, uint32_t *status) {
+  uint64_t a, b;
+  for (uint32_t it = 0; it < (1u << 22); it++) {
+    if ((it & 15u) == 15u && *(volatile uint32_t *)status) return make_float2(0.0f, 0.0f);
+    ld_pair(p, a, b);
+    if (red_done(a, C) && red_done(b, C)) return make_float2(red_value(a, C), red_value(b, C));
+  }
+  atomicOr(status, SM100_DECODE_ERR_BARRIER);
+  return make_float2(0.0f, 0.0f);
+}
+
 __device__ __forceinline__ float2 wait_red_pair(const uint64_t *p, uint64_t C, uint32_t *status) {
   uint64_t a, b;
   ld_pair(p, a, b);
-  for (uint32_t it = 0; !(red_done(a, C) && red_done(b, C)); it++) {
-    if (it >= (1u << 22) || ((it & 15u) == 15u && *(volatile uint32_t *)status)) {
-      if (it >= (1u << 22)) atomicOr(status, SM100_DECODE_ERR_BARRIER);
-      return make_float2(0.0f, 0.0f);
-    }
-    ld_pair(p, a, b);
-  }
-  return make_float2(red_value(a, C), red_value(b, C));
+  if (red_done(a, C) && red_done(b, C)) return make_float2(red_value(a, C), red_value(b, C));
+  return wait_red_pair_slow(p, C, status);
 }
 
 __device__ __forceinline__ uint64_t gtimer() {
@@ -183,6 +204,16 @@ __device__ __forceinline__ uint64_t gtimer() {
 }
 
 __device__ __forceinline__ void fence_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+// 2-D tensor copy (no multicast) of the box at (x, y) of a tensor map in
+// global memory into shared memory, completing on bar.
+__device__ __forceinline__ void tma_2d(void *dst, const void *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
 
 // barrier of the consumer warps only (the producer warp never joins it)
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
@@ -241,6 +272,7 @@ struct Geo {
   int f0, f1;          // c_fc rows = mlp.c_proj K slice
   int v0, v1, R, n_lm; // lm_head rows, rows per chunk, chunks
   int nx;              // transfers per token
+  int z0, z1;          // this CTA's share of a reduction set to zero (words)
 };
 
 __host__ __device__ __forceinline__ Geo geo_of(int c, int G, int heads, int D, int hd, int vocab, int n_layers) {
@@ -265,6 +297,8 @@ __host__ __device__ __forceinline__ Geo geo_of(int c, int G, int heads, int D, i
   const int n = g.R > 0 ? (g.v1 - g.v0 + g.R - 1) / g.R : 1;
   g.n_lm = n > 0 ? n : 1;
   g.nx = 4 * n_layers + g.n_lm;
+  rows_of((int64_t)2 * n_layers * D, c, G, a, b);
+  g.z0 = (int)a; g.z1 = (int)b;
   return g;
 }
 
@@ -273,7 +307,15 @@ struct Xfer {
   const float *w, *ln_g, *ln_b, *bx, *b;
   uint32_t wbytes, bbytes;
   int hdr;     // floats before the weight rows
+  int pad;
 };
+
+// Transfers per token of any CTA (the table in shared memory holds them).
+__host__ __device__ __forceinline__ int max_transfers(int n_layers, int vocab, int G, int D) {
+  const int R = lm_rows_per_chunk(D), rows = (vocab + G - 1) / G;
+  const int n_lm = R > 0 ? (rows + R - 1) / R : 1;
+  return 4 * n_layers + (n_lm > 0 ? n_lm : 1);
+}
 
 __device__ __forceinline__ Xfer xfer_of(const Sm100DecodeModel &m, const Geo &g, int i) {
   const int D = m.dim, hd = m.head_dim, nl = m.n_layers;
@@ -352,8 +394,9 @@ __device__ __forceinline__ void issue(const Xfer &x, int D, float *dst, uint64_t
 // keys / values of one head (as many positions as fit, smax).
 struct Smem {
   static constexpr size_t ring = 0;
-  static constexpr size_t xres = ring + (size_t)kStages * kStageBytes;  // [kMaxDim] residual stream
-  static constexpr size_t fv = xres + kMaxDim * 4;                        // [kMaxRows] c_fc outputs
+  static constexpr size_t xs = ring + (size_t)kStages * kStageBytes;    // [kMaxDim] LayerNorm output
+  static constexpr size_t lnp = xs + kMaxDim * 4;                         // [2][16] LayerNorm partial sums
+  static constexpr size_t fv = lnp + 32 * 4;                              // [kMaxRows] c_fc outputs
   static constexpr size_t qkvs = fv + 64 * 4;                             // [3 kMaxHd] q, k, v of the head
   static constexpr size_t atts = qkvs + 3 * kMaxHd * 4;                   // [kMaxHd] attention output
   static constexpr size_t acc = atts + kMaxHd * 4;                        // [kThreads] p @ v slices
@@ -362,13 +405,22 @@ struct Smem {
   static constexpr size_t tok = rbi + 16 * 4;                             // [4] i32
   static constexpr size_t bars = tok + 16;                                // full[2], empty[2], pfx
   static constexpr size_t kcs = bars + 8 * 8;                             // [kMaxLayers] cache pointers
-  static constexpr size_t sc = kcs + kMaxLayers * 8;                      // [2][max_ctx] scores, probabilities
-  static __host__ __device__ size_t kv(int max_ctx) { return (sc + 2 * (size_t)max_ctx * 4 + 127) & ~(size_t)127; }
-  static __host__ __device__ int smax(int max_ctx, int hd) {
-    const int64_t n = ((int64_t)kSmemLimit - (int64_t)kv(max_ctx)) / (8 * hd);
-    return (int)(n < max_ctx ? (n > 0 ? n : 0) : max_ctx);
+  static constexpr size_t cps = kcs + kMaxLayers * 8;                     // [kCpRows kWarps] c_proj partials
+  static constexpr size_t xt = cps + kCpRows * kWarps * 4 + 4;            // [nxt] transfer table (Xfer)
+  static __host__ __device__ size_t sc(int nxt) { return xt + (size_t)nxt * sizeof(Xfer); }   // [2][max_ctx]
+  static __host__ __device__ size_t kv(int nxt, int max_ctx) {
+    return (sc(nxt) + 2 * (size_t)max_ctx * 4 + 127) & ~(size_t)127;
   }
-  static __host__ __device__ size_t total(int max_ctx, int hd) { return kv(max_ctx) + (size_t)smax(max_ctx, hd) * 8 * hd; }
+  // staged positions: whole boxes (a box may run past max_ctx: V rows, or
+  // the fill value past 2 max_ctx)
+  static __host__ __device__ int smax(int nxt, int max_ctx, int hd) {
+    int64_t n = ((int64_t)kSmemLimit - (int64_t)kv(nxt, max_ctx)) / (8 * hd);
+    n = n / kBoxRows * kBoxRows;
+    return (int)(n > 0 ? n : 0);
+  }
+  static __host__ __device__ size_t total(int nxt, int max_ctx, int hd) {
+    return kv(nxt, max_ctx) + (size_t)smax(nxt, max_ctx, hd) * 8 * hd;
+  }
 };
 
 struct Launch {
@@ -385,35 +437,6 @@ __device__ __forceinline__ void load_x(const float *xb, int lane, float (&xr)[4 
   for (int j = 0; j < NK; j++) {
     const float4 v = reinterpret_cast<const float4 *>(xb)[lane + 32 * j];
     xr[4 * j] = v.x; xr[4 * j + 1] = v.y; xr[4 * j + 2] = v.z; xr[4 * j + 3] = v.w;
-  }
-}
-
-// LayerNorm of the vector in the lanes' registers (statistics by warp
-// shuffles), gamma / beta from the stage front.
-template <int NK>
-__device__ __forceinline__ void layernorm_regs(float (&xr)[4 * NK], const float *g, const float *b, int lane, int K,
-                                               float eps) {
-  const float inv_n = (float)(1.0 / (double)K);
-  float s = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4 * NK; i++) s += xr[i];
-  const float mean = __fmul_rn(warp_sum(s), inv_n);
-  float v2 = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 4 * NK; i++) {
-    const float dd = __fsub_rn(xr[i], mean);
-    v2 = fmaf(dd, dd, v2);
-  }
-  const float var = __fmul_rn(warp_sum(v2), inv_n);
-  const float rr = __frcp_rn(__fsqrt_rn(__fadd_rn(var, eps)));
-#pragma unroll
-  for (int j = 0; j < NK; j++) {
-    const float4 gv = reinterpret_cast<const float4 *>(g)[lane + 32 * j];
-    const float4 bv = reinterpret_cast<const float4 *>(b)[lane + 32 * j];
-    const float gg[4] = {gv.x, gv.y, gv.z, gv.w}, bb[4] = {bv.x, bv.y, bv.z, bv.w};
-#pragma unroll
-    for (int c = 0; c < 4; c++)
-      xr[4 * j + c] = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(xr[4 * j + c], mean), rr), gg[c]), bb[c]);
   }
 }
 
@@ -449,33 +472,272 @@ __device__ __forceinline__ void dot2(const float4 *w0, const float4 *w1, bool tw
   }
 }
 
-// This thread's pairs j = t + i kThreads of a set of D reduction words
-// (count C), decoded; pairs past D read as 0.
-constexpr int kPairsPerThread = (kMaxDim / 2 + kThreads - 1) / kThreads;
+// The per-layer path of the consumer warps is a handful of out-of-line
+// functions (one rows loop for c_attn, c_fc and lm_head, one LayerNorm, the
+// attention, the two split products): the kernel's code is executed once per
+// layer, so the path must stay small enough for the SM's instruction caches.
+//
+// Thread t < D / 2 owns the residual stream's pair (x[2 t], x[2 t + 1]) in
+// registers (D <= 2 kThreads): it adds the decoded sums to it and feeds it to
+// the LayerNorm, so the residual stream never needs a barrier.
 
-__device__ __forceinline__ void poll_reduced(const uint64_t *words, int D, uint64_t C, uint32_t *status, int t,
-                                             float2 (&sv)[kPairsPerThread]) {
+// The step input: x += (decoded sum of the reduction set `words` (count C)
+// + bias bx), the reference's order (the projection's bias, then the
+// residual; words == nullptr: x unchanged), then LayerNorm (two-pass
+// statistics, one partial sum per warp and a fixed-order fold) of x with
+// gamma / beta into xs.  The consumer warps meet three times.  Returns x.
+__device__ __noinline__ float2 input_ln(unsigned char *smem, const uint64_t *words, uint64_t C, const float *bx,
+                                        const float *gam, const float *bet, float2 xv, int D, float eps,
+                                        uint32_t *status) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  float *xs = reinterpret_cast<float *>(smem + Smem::xs);
+  float *lnp = reinterpret_cast<float *>(smem + Smem::lnp);
+  const bool live = 2 * t < D;
+  if (words && live) {
+    const float2 sv = wait_red_pair(words + 2 * t, C, status);
+    const float2 bb = reinterpret_cast<const float2 *>(bx)[t];
+    xv = make_float2(__fadd_rn(xv.x, __fadd_rn(sv.x, bb.x)), __fadd_rn(xv.y, __fadd_rn(sv.y, bb.y)));
+  }
+  const float inv_n = (float)(1.0 / (double)D);
+  const float s = warp_sum(live ? __fadd_rn(xv.x, xv.y) : 0.0f);
+  if (lane == 0) lnp[warp] = s;
+  csync();
+  float tot = 0.0f;
 #pragma unroll
-  for (int i = 0; i < kPairsPerThread; i++) {
-    const int j = t + i * kThreads;
-    sv[i] = 2 * j < D ? wait_red_pair(words + 2 * j, C, status) : make_float2(0.0f, 0.0f);
+  for (int w = 0; w < kWarps; w++) tot += lnp[w];
+  const float mean = __fmul_rn(tot, inv_n);
+  const float d0 = __fsub_rn(xv.x, mean), d1 = __fsub_rn(xv.y, mean);
+  const float v = warp_sum(live ? fmaf(d1, d1, __fmul_rn(d0, d0)) : 0.0f);
+  if (lane == 0) lnp[16 + warp] = v;
+  csync();
+  float vt = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kWarps; w++) vt += lnp[16 + w];
+  const float rr = __frcp_rn(__fsqrt_rn(__fadd_rn(__fmul_rn(vt, inv_n), eps)));
+  if (live) {
+    const float2 gg = reinterpret_cast<const float2 *>(gam)[t], bb = reinterpret_cast<const float2 *>(bet)[t];
+    reinterpret_cast<float2 *>(xs)[t] = make_float2(__fadd_rn(__fmul_rn(__fmul_rn(d0, rr), gg.x), bb.x),
+                                                    __fadd_rn(__fmul_rn(__fmul_rn(d1, rr), gg.y), bb.y));
+  }
+  csync();
+  return xv;
+}
+
+enum { ROWS_QKV = 0, ROWS_FC, ROWS_LM };
+
+// Rows [0, nr) of a stage (w: row-major, D floats a row) dotted with the
+// LayerNorm output: warp w takes rows w, w + kWarps (one pass of two), then
+// w + 2 kWarps, ...; lane 0 finishes a row:
+//  ROWS_QKV: y = dot + bias[i] published to dst[i] (tag) and, for k / v
+//            rows, written to the KV cache row (cache[i]);
+//  ROWS_FC:  fv[i] = GELU(dot + bias[i]);
+//  ROWS_LM:  logits[r0 + i] = dot (when logits), the warp's best (value,
+//            index) kept in rbv / rbi.
+template <int NK>
+__device__ __noinline__ void rows_step(unsigned char *smem, const float *w, const float *bias, int nr, int D, int kind,
+                                       uint64_t *dst, uint32_t tag, float *cache, float *logits, int r0) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const float *xs = reinterpret_cast<const float *>(smem + Smem::xs);
+  float *fv = reinterpret_cast<float *>(smem + Smem::fv);
+  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
+  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
+  float xr[4 * NK];
+  load_x<NK>(xs, lane, xr);
+  for (int i = warp; i < nr; i += 2 * kWarps) {
+    const int i2 = i + kWarps;
+    const bool two = i2 < nr;
+    float a, b;
+    dot2<NK>(reinterpret_cast<const float4 *>(w + (size_t)i * D),
+             reinterpret_cast<const float4 *>(w + (size_t)(two ? i2 : i) * D), two, xr, lane, a, b);
+    if (lane == 0) {
+#pragma unroll 1
+      for (int u = 0; u < 2; u++) {
+        if (u == 1 && !two) break;
+        const int row = u ? i2 : i;
+        const float d = u ? b : a;
+        if (kind == ROWS_QKV) {
+          const float y = __fadd_rn(d, bias[row]);
+          st_word(dst + row, __float_as_uint(y), tag);
+          if (cache) cache[row] = y;
+        } else if (kind == ROWS_FC) {
+          fv[row] = gelu_tanh(__fadd_rn(d, bias[row]));
+        } else {
+          const int n = r0 + row;
+          if (logits) logits[n] = d;
+          if (better(d, n, rbv[warp], rbi[warp])) {
+            rbv[warp] = d;
+            rbi[warp] = n;
+          }
+        }
+      }
+    }
   }
 }
 
-// x += (decoded sum + bias), the reference's order: the projection's bias
-// first, then the residual.
-__device__ __forceinline__ void add_reduced(float *xres, const float *bias, int D, int t,
-                                            const float2 (&sv)[kPairsPerThread]) {
-#pragma unroll
-  for (int i = 0; i < kPairsPerThread; i++) {
-    const int j = t + i * kThreads;
-    if (2 * j < D) {
-      const float2 bb = reinterpret_cast<const float2 *>(bias)[j];
-      float2 *xp = reinterpret_cast<float2 *>(xres) + j;
-      const float2 xv = *xp;
-      *xp = make_float2(__fadd_rn(xv.x, __fadd_rn(sv[i].x, bb.x)), __fadd_rn(xv.y, __fadd_rn(sv[i].y, bb.y)));
+// Attention of head h for the new row at pos (thvm_gpt2.py:49-61): q, k, v
+// from the group's tagged words (k, v also staged at pos), scores against the
+// staged keys Ks (positions < smax; later ones from the cache in L2),
+// softmax, p @ v into atts.  Then the next layer's prefix copies (map_next,
+// rows [0, next_rows); map_next == nullptr: none).  The loops stay rolled:
+// this runs once per layer and must stay small for the instruction caches.
+__device__ __noinline__ void attention_step(unsigned char *smem, float *sc, float *Ks, const uint64_t *qkv_src,
+                                            uint32_t tag, const float *kc, int pos, int smax, int hd, int D,
+                                            int max_ctx, int h, float scale, const void *map_next, int next_rows,
+                                            uint32_t *status) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31, L = pos + 1;
+  float *qs = reinterpret_cast<float *>(smem + Smem::qkvs), *kn = qs + hd, *vn = kn + hd;
+  float *atts = reinterpret_cast<float *>(smem + Smem::atts);
+  float *acc = reinterpret_cast<float *>(smem + Smem::acc);
+  float *pr = sc + max_ctx, *Vs = Ks + (size_t)smax * hd;
+  uint64_t *pfx = reinterpret_cast<uint64_t *>(smem + Smem::bars) + 4;
+  const float *vc = kc + (size_t)max_ctx * D;
+  if (2 * t < 3 * hd) {
+    const float2 v = wait_pair(qkv_src + 2 * t, tag, status);
+    reinterpret_cast<float2 *>(qs)[t] = v;
+    const int i = 2 * t, which = i / hd, dd = i % hd;
+    if (which > 0 && pos < smax) *reinterpret_cast<float2 *>((which == 1 ? Ks : Vs) + (size_t)pos * hd + dd) = v;
+  }
+  csync();
+  // scores: 8 lanes per key, hd / 8 floats per lane (two float4 at hd = 64)
+  {
+    const int grp = t >> 3, gl = t & 7, per4 = hd / 32;
+    const float4 qa = reinterpret_cast<const float4 *>(qs)[gl * per4];
+    const float4 qb = per4 > 1 ? reinterpret_cast<const float4 *>(qs)[gl * per4 + 1] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+    for (int j0 = 0; j0 < L; j0 += kThreads / 8) {
+      const int j = j0 + grp;
+      float s = 0.0f;
+      if (j < L) {
+        const float4 *kr = j < smax ? reinterpret_cast<const float4 *>(Ks + (size_t)j * hd) + gl * per4
+                         : j == pos ? reinterpret_cast<const float4 *>(kn) + gl * per4
+                                    : reinterpret_cast<const float4 *>(kc + (size_t)j * D + (size_t)h * hd) + gl * per4;
+        const float4 ka = j < smax || j == pos ? kr[0] : __ldcg(kr);
+        s = fmaf(qa.x, ka.x, fmaf(qa.y, ka.y, fmaf(qa.z, ka.z, __fmul_rn(qa.w, ka.w))));
+        if (per4 > 1) {
+          const float4 kb = j < smax || j == pos ? kr[1] : __ldcg(kr + 1);
+          s = fmaf(qb.x, kb.x, fmaf(qb.y, kb.y, fmaf(qb.z, kb.z, fmaf(qb.w, kb.w, s))));
+        }
+      }
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      if (j < L && gl == 0) sc[j] = __fmul_rn(s, scale);
     }
   }
+  csync();
+  // softmax by warp 0: p_j = exp(s_j - max) * recip(sum)
+  if (warp == 0) {
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int j = lane; j < L; j += 32) mx = fmaxf(mx, sc[j]);
+    mx = warp_max(mx);
+    float sum = 0.0f;
+#pragma unroll 1
+    for (int j = lane; j < L; j += 32) {
+      const float e = xexp(__fsub_rn(sc[j], mx));
+      pr[j] = e;
+      sum += e;
+    }
+    const float r = __frcp_rn(warp_sum(sum));
+#pragma unroll 1
+    for (int j = lane; j < L; j += 32) pr[j] = __fmul_rn(pr[j], r);
+  }
+  csync();
+  // p @ v: key slices x dims, then the slices in order
+  const int nslice = kThreads / hd;
+  {
+    const int slice = t / hd, d = t % hd;
+    if (slice < nslice) {
+      float a = 0.0f;
+#pragma unroll 1
+      for (int j = slice; j < L; j += nslice) {
+        const float v = j < smax ? Vs[(size_t)j * hd + d] : j == pos ? vn[d] : __ldcg(vc + (size_t)j * D + (size_t)h * hd + d);
+        a = fmaf(pr[j], v, a);
+      }
+      acc[slice * hd + d] = a;
+    }
+  }
+  const int nb = map_next ? (next_rows + kBoxRows - 1) / kBoxRows : 0;
+  if (nb && t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nb * kBoxRows * hd * 4));
+  csync();
+  if (t < hd) {
+    float a = 0.0f;
+#pragma unroll 1
+    for (int s2 = 0; s2 < nslice; s2++) a += acc[s2 * hd + t];
+    atts[t] = a;
+  }
+  if (t < 2 * nb) {   // keys then values, whole boxes of the next layer's map
+    const int v = t >= nb, b = v ? t - nb : t;
+    tma_2d((v ? Vs : Ks) + (size_t)b * kBoxRows * hd, map_next, h * hd, (v ? max_ctx : 0) + b * kBoxRows, pfx);
+  }
+  csync();
+}
+
+// c_proj partial: rows [0, nr) of the head's column block (w: nr x hd) times
+// the attention output, added to the reduction words out[0, nr); warp w takes
+// rows w, w + kWarps, ..., lanes over the dims.
+__device__ __noinline__ void cproj_step(unsigned char *smem, const float *w, int nr, int hd, uint64_t *out,
+                                        uint32_t *status) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const float *atts = reinterpret_cast<const float *>(smem + Smem::atts);
+  const float a0 = atts[lane], a1 = hd > 32 ? atts[lane + 32] : 0.0f;
+#pragma unroll 1
+  for (int i = warp; i < nr; i += kWarps) {
+    float s = __fmul_rn(w[(size_t)i * hd + lane], a0);
+    if (hd > 32) s = fmaf(w[(size_t)i * hd + lane + 32], a1, s);
+    s = warp_sum(s);
+    if (lane == 0) red_word(out + i, s, status);
+  }
+}
+
+// mlp.c_proj partial over this CTA's hidden rows: out[o] += sum_k fv[k]
+// wt[k][o] (wt: nr x D, the transposed weight's rows), outputs over threads.
+__device__ __noinline__ void mproj_step(unsigned char *smem, const float *wt, int nr, int D, uint64_t *out,
+                                        uint32_t *status) {
+  const int t = threadIdx.x;
+  const float *fv = reinterpret_cast<const float *>(smem + Smem::fv);
+  for (int o = t; o < D; o += kThreads) {
+    float a = 0.0f;
+#pragma unroll 8
+    for (int k = 0; k < nr; k++) a = fmaf(fv[k], wt[(size_t)k * D + o], a);
+    red_word(out + o, a, status);
+  }
+}
+
+// Argmax over the grid: each CTA publishes its best (value, index) as tagged
+// words (kReplicas copies) and folds every CTA's (first index of the max).
+// The fence before the publish releases this CTA's KV-cache rows of the token
+// (written by other warps before the barrier) and its zeroed reduction words;
+// the fence after the fold acquires every CTA's.  Returns the token.
+__device__ __noinline__ int argmax_step(unsigned char *smem, uint64_t *part_w, uint32_t tag, int G, uint32_t *status) {
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
+  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
+  int *tok_s = reinterpret_cast<int *>(smem + Smem::tok);
+  csync();
+  if (warp == 0) {
+    float bv = lane < kWarps ? rbv[lane] : -INFINITY;
+    int bi = lane < kWarps ? rbi[lane] : 0x7fffffff;
+    warp_best(bv, bi);
+    if (lane < kReplicas) {   // one copy per lane
+      fence_gpu();
+      st_word(part_w + (size_t)lane * kPartWords + 2 * blockIdx.x, __float_as_uint(bv), tag);
+      st_word(part_w + (size_t)lane * kPartWords + 2 * blockIdx.x + 1, (uint32_t)bi, tag);
+    }
+    bv = -INFINITY;
+    bi = 0x7fffffff;
+    for (int b = lane; b < G; b += 32) {
+      float pw[2];
+      wait_words<2>(part_w + (size_t)(blockIdx.x % kReplicas) * kPartWords + 2 * b, 1, 2, tag, status, pw);
+      const int ib = (int)__float_as_uint(pw[1]);
+      if (better(pw[0], ib, bv, bi)) { bv = pw[0]; bi = ib; }
+    }
+    warp_best(bv, bi);
+    fence_gpu();
+    if (lane == 0) tok_s[0] = bi == 0x7fffffff ? 0 : bi;
+  }
+  csync();
+  return tok_s[0];
 }
 
 // ---------------------------------------------------------------------------
@@ -486,418 +748,175 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int D = m.dim, hd = m.head_dim, nl = m.n_layers, max_ctx = m.max_ctx, H = m.heads;
   float *ring = reinterpret_cast<float *>(smem + Smem::ring);
-  float *xres = reinterpret_cast<float *>(smem + Smem::xres);
-  float *fv = reinterpret_cast<float *>(smem + Smem::fv);
-  float *qs = reinterpret_cast<float *>(smem + Smem::qkvs), *kn = qs + hd, *vn = kn + hd;
-  float *atts = reinterpret_cast<float *>(smem + Smem::atts);
-  float *acc = reinterpret_cast<float *>(smem + Smem::acc);
   float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
   int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
-  int *tok_s = reinterpret_cast<int *>(smem + Smem::tok);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars), *empty = full + 2, *pfx = full + 4;
   float *const *kcs = reinterpret_cast<float *const *>(smem + Smem::kcs);
-  float *sc = reinterpret_cast<float *>(smem + Smem::sc), *pr = sc + max_ctx;
-  const int smax = Smem::smax(max_ctx, hd);
-  float *Ks = reinterpret_cast<float *>(smem + Smem::kv(max_ctx));
-  float *Vs = Ks + (size_t)smax * hd;
+  const int nxt = max_transfers(nl, m.vocab, g.G, D);
+  const int smax = Smem::smax(nxt, max_ctx, hd);
+  float *sc = reinterpret_cast<float *>(smem + Smem::sc(nxt));
+  float *Ks = reinterpret_cast<float *>(smem + Smem::kv(nxt, max_ctx));
   uint32_t *status = ln.status;
-  const int vocab = m.vocab;
   const float eps = m.eps;
-  float *logits = m.logits;
-  uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * (3 * nl + 1) * kTraceSlots : nullptr;
+  uint64_t *tr0 = m.trace ? m.trace + (size_t)blockIdx.x * (3 * nl + 1) * kTraceSlots : nullptr;
   uint64_t *qkv_w = m.qkv_w + (size_t)g.h * 3 * hd;
   const int hdr = hdr_floats(D);
-
-  // prefix copies of (layer l, rows [0, n)) of head h; thread 0 armed pfx
-  auto issue_prefix = [&](int l, int n) {
-    const float *kc = kcs[l], *vc = kc + (size_t)max_ctx * D;
-    for (int j = t; j < n; j += kThreads) {
-      bulk_g2s(Ks + (size_t)j * hd, kc + (size_t)j * D + (size_t)g.h * hd, (uint32_t)hd * 4, pfx);
-      bulk_g2s(Vs + (size_t)j * hd, vc + (size_t)j * D + (size_t)g.h * hd, (uint32_t)hd * 4, pfx);
-    }
-  };
+  const size_t n_red = (size_t)2 * nl * D;
   auto staged = [&](int n) { return n < smax ? n : smax; };
+  auto stage = [&](int qq) { return ring + (size_t)(qq & 1) * (kStageBytes / 4); };
 
   int q = 0;            // next ring transfer (stage q & 1, phase (q >> 1) & 1)
   int pf = 0;           // prefix phases consumed
   bool pending = true;  // a prefix phase is armed and not yet waited for
   {
-    const int n = staged(ln.pos_ok ? ln.pos0 : 0);
-    if (t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * n * hd * 4));
+    const int n = staged(ln.pos_ok ? ln.pos0 : 0), nb = (n + kBoxRows - 1) / kBoxRows;
+    if (t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nb * kBoxRows * hd * 4));
     csync();
-    issue_prefix(0, n);
+    if (t < 2 * nb) {
+      const int v = t >= nb, b = v ? t - nb : t;
+      tma_2d(Ks + (v ? (size_t)smax * hd : 0) + (size_t)b * kBoxRows * hd, m.kv_map[0], g.h * hd,
+             (v ? max_ctx : 0) + b * kBoxRows, pfx);
+    }
   }
   int tok = m.io[1];
   for (int tk = 0; tk < ln.n_tokens; tk++) {
-    const int pos = ln.pos_ok ? ln.pos0 + tk : 0, L = pos + 1;
+    const int pos = ln.pos_ok ? ln.pos0 + tk : 0;
     const uint32_t tag_tok = ln.tag_base + (uint32_t)tk * ln.stride;
-    const bool trace = tr && t == 0 && tk == ln.n_tokens - 1;
+    uint64_t *tr = tr0 && t == 0 && tk == ln.n_tokens - 1 ? tr0 : nullptr;
     const uint64_t C_att = (uint64_t)H, C_mlp = (uint64_t)g.G;
     // reduction words of this token: set (tok0 + tk) mod 3.  This token
     // zeroes the next token's set (last read two tokens ago: every CTA has
     // passed that token's argmax; the zeros are released by this token's
     // argmax publish, before which no CTA starts the next token)
-    const size_t n_red = (size_t)2 * nl * D;
     uint64_t *red = m.red_w + (size_t)((ln.tok0 + (uint32_t)tk) % 3u) * n_red;
     {
-      uint64_t *nxt = m.red_w + (size_t)((ln.tok0 + (uint32_t)tk + 1u) % 3u) * n_red;
-      int64_t z0, z1;
-      rows_of((int64_t)n_red, blockIdx.x, g.G, z0, z1);
-      for (int64_t i = z0 + t; i < z1; i += kThreads) nxt[i] = 0ull;
+      uint64_t *nz = m.red_w + (size_t)((ln.tok0 + (uint32_t)tk + 1u) % 3u) * n_red;
+      for (int i = g.z0 + t; i < g.z1; i += kThreads) nz[i] = 0ull;
     }
-
-    // x = wte[tok] + wpe[pos] (thvm_gpt2.py:93-103)
-    {
-      const bool tok_ok = tok >= 0 && tok < vocab;
-      for (int k = t; k < D; k += kThreads)
-        xres[k] = __fadd_rn(tok_ok ? m.wte[(size_t)tok * D + k] : 0.0f, m.wpe[(size_t)pos * D + k]);
+    // x = wte[tok] + wpe[pos] (thvm_gpt2.py:93-103), this thread's pair
+    float2 xv = make_float2(0.0f, 0.0f);
+    if (2 * t < D) {
+      const float2 e = tok >= 0 && tok < m.vocab ? reinterpret_cast<const float2 *>(m.wte + (size_t)tok * D)[t]
+                                                 : make_float2(0.0f, 0.0f);
+      const float2 pp = reinterpret_cast<const float2 *>(m.wpe + (size_t)pos * D)[t];
+      xv = make_float2(__fadd_rn(e.x, pp.x), __fadd_rn(e.y, pp.y));
     }
 
     for (int l = 0; l < nl; l++) {
       uint64_t *red_att = red + (size_t)(2 * l) * D, *red_mlp = red_att + D;
       // ===== c_attn rows of this member (ln_1 of x; x += mlp output of l - 1)
       {
-        const int p = 3 * l;
-        if (trace) tr[p * kTraceSlots + 0] = gtimer();
-        float2 sv[kPairsPerThread];
-        if (l > 0) poll_reduced(red_mlp - 2 * D, D, C_mlp, status, t, sv);
-        if (trace) tr[p * kTraceSlots + 1] = gtimer();
+        uint64_t *ts = tr ? tr + (3 * l) * kTraceSlots : nullptr;
+        if (ts) ts[0] = gtimer();
         const bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-        const float *sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
-        if (trace) tr[p * kTraceSlots + 2] = gtimer();
-        if (l > 0) add_reduced(xres, sb + 2 * D, D, t, sv);
-        csync();
-        if (trace) tr[p * kTraceSlots + 3] = gtimer();
-        float xr[4 * NK];
-        load_x<NK>(xres, lane, xr);
-        layernorm_regs<NK>(xr, sb, sb + D, lane, D, eps);
-        if (trace) tr[p * kTraceSlots + 7] = gtimer();
-        const int nr = g.qn, bofs = 3 * D + (g.qrow0 & 3);
-        const uint32_t tag = tag_tok + (uint32_t)l;
-        float *cache = ln.pos_ok && g.kv_which > 0 ? kcs[l] + (size_t)(g.kv_which - 1) * max_ctx * D + (size_t)pos * D + g.qcol0
-                                                   : nullptr;
-        if (have) {
-#pragma unroll 1
-          for (int k = 0; k < kRowsPerWarp; k += 2) {
-            const int i = warp + kWarps * k, i2 = i + kWarps;
-            if (i < nr) {
-              const bool two = i2 < nr;
-              float a, b;
-              dot2<NK>(reinterpret_cast<const float4 *>(sb + hdr + (size_t)i * D),
-                       reinterpret_cast<const float4 *>(sb + hdr + (size_t)(two ? i2 : i) * D), two, xr, lane, a, b);
-              if (lane == 0) {
-                const float y = __fadd_rn(a, sb[bofs + i]);
-                st_word(qkv_w + g.ql0 + i, __float_as_uint(y), tag);
-                if (cache) cache[i] = y;
-                if (two) {
-                  const float y2 = __fadd_rn(b, sb[bofs + i2]);
-                  st_word(qkv_w + g.ql0 + i2, __float_as_uint(y2), tag);
-                  if (cache) cache[i2] = y2;
-                }
-              }
-            }
-          }
-        }
+        const float *sb = stage(q);
+        if (ts) ts[2] = gtimer();
+        xv = input_ln(smem, l > 0 ? red_mlp - 2 * D : nullptr, C_mlp, sb + 2 * D, sb, sb + D, xv, D, eps, status);
+        if (ts) ts[3] = ts[7] = gtimer();
+        float *cache = ln.pos_ok && g.kv_which > 0
+                           ? kcs[l] + (size_t)(g.kv_which - 1) * max_ctx * D + (size_t)pos * D + g.qcol0
+                           : nullptr;
+        if (have)
+          rows_step<NK>(smem, sb + hdr, sb + 3 * D + (g.qrow0 & 3), g.qn, D, ROWS_QKV, qkv_w + g.ql0,
+                        tag_tok + (uint32_t)l, cache, nullptr, 0);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
-        if (trace) tr[p * kTraceSlots + 4] = gtimer();
+        if (ts) ts[4] = gtimer();
       }
 
       // ===== attention of head h, then this member's rows of c_proj's head-h block
       {
-        const int p = 3 * l + 1;
-        const uint32_t tag = tag_tok + (uint32_t)l;
-        if (trace) tr[p * kTraceSlots + 0] = gtimer();
+        uint64_t *ts = tr ? tr + (3 * l + 1) * kTraceSlots : nullptr;
+        if (ts) ts[0] = gtimer();
         // the prefix copies are ours and always complete: wait for them even
         // after an error, so the staging area is never written by two phases
         mbar_wait(pfx, (uint32_t)(pf & 1), status, false);
         pf++;
         pending = false;
-        // q, k, v of the new row from the group (k, v also staged at pos)
-        for (int j = t; 2 * j < 3 * hd; j += kThreads) {
-          const float2 v = wait_pair(qkv_w + 2 * j, tag, status);
-          reinterpret_cast<float2 *>(qs)[j] = v;
-          const int i = 2 * j, which = i / hd, dd = i % hd;
-          if (which > 0 && pos < smax)
-            *reinterpret_cast<float2 *>((which == 1 ? Ks : Vs) + (size_t)pos * hd + dd) = v;
-        }
-        csync();
-        if (trace) tr[p * kTraceSlots + 1] = gtimer();
-        const float *kc = kcs[l], *vc = kc + (size_t)max_ctx * D;
-        // scores: 8 lanes per key, hd / 8 floats per lane
-        {
-          const int grp = t >> 3, gl = t & 7, per4 = hd / 32;
-          constexpr int NG = kThreads / 8;
-          float4 q4[2];
-#pragma unroll
-          for (int v = 0; v < 2; v++)
-            if (v < per4) q4[v] = reinterpret_cast<const float4 *>(qs)[gl * per4 + v];
-          for (int j0 = 0; j0 < L; j0 += NG) {
-            const int j = j0 + grp;
-            float s = 0.0f;
-            if (j < L) {
-              float4 k4[2];
-              if (j < smax) {
-#pragma unroll
-                for (int v = 0; v < 2; v++)
-                  if (v < per4) k4[v] = reinterpret_cast<const float4 *>(Ks + (size_t)j * hd)[gl * per4 + v];
-              } else if (j == pos) {
-#pragma unroll
-                for (int v = 0; v < 2; v++)
-                  if (v < per4) k4[v] = reinterpret_cast<const float4 *>(kn)[gl * per4 + v];
-              } else {
-#pragma unroll
-                for (int v = 0; v < 2; v++)
-                  if (v < per4)
-                    k4[v] = __ldcg(reinterpret_cast<const float4 *>(kc + (size_t)j * D + (size_t)g.h * hd) + gl * per4 + v);
-              }
-#pragma unroll
-              for (int v = 0; v < 2; v++) {
-                if (v < per4) {
-                  s = fmaf(q4[v].x, k4[v].x, s);
-                  s = fmaf(q4[v].y, k4[v].y, s);
-                  s = fmaf(q4[v].z, k4[v].z, s);
-                  s = fmaf(q4[v].w, k4[v].w, s);
-                }
-              }
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 4);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            if (j < L && gl == 0) sc[j] = __fmul_rn(s, m.attn_scale);
-          }
-        }
-        csync();
-        // softmax: every warp folds max and sum itself (no block reduction),
-        // then writes p_j = exp(s_j - max) * recip(sum) for its share of j
-        {
-          float mx = -INFINITY;
-          for (int j = lane; j < L; j += 32) mx = fmaxf(mx, sc[j]);
-          mx = warp_max(mx);
-          float sum = 0.0f;
-          for (int j = lane; j < L; j += 32) sum += xexp(__fsub_rn(sc[j], mx));
-          sum = warp_sum(sum);
-          const float r = __frcp_rn(sum);
-          for (int j = t; j < L; j += kThreads) pr[j] = __fmul_rn(xexp(__fsub_rn(sc[j], mx)), r);
-        }
-        csync();
-        if (trace) tr[p * kTraceSlots + 2] = gtimer();
-        // p @ v: key slices x dims, then the slices in order
-        const int nslice = kThreads / hd;
-        {
-          const int slice = t / hd, d = t % hd;
-          if (slice < nslice) {
-            float a = 0.0f;
-            for (int j = slice; j < L; j += nslice) {
-              const float v = j < smax ? Vs[(size_t)j * hd + d] : j == pos ? vn[d] : __ldcg(vc + (size_t)j * D + (size_t)g.h * hd + d);
-              a = fmaf(pr[j], v, a);
-            }
-            acc[slice * hd + d] = a;
-          }
-        }
+        if (ts) ts[7] = gtimer();
         // the next layer's prefix (rows < pos, written in earlier tokens); the
         // next token's layer 0 is staged after the argmax (it needs row pos)
         const bool more = l + 1 < nl;
-        const int nrows = more ? staged(pos) : 0;
-        if (more && t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nrows * hd * 4));
-        csync();
-        if (t < hd) {
-          float a = 0.0f;
-          for (int s2 = 0; s2 < nslice; s2++) a += acc[s2 * hd + t];
-          atts[t] = a;
-        }
-        if (more) {
-          issue_prefix(l + 1, nrows);
-          pending = true;
-        }
-        csync();
-        if (trace) tr[p * kTraceSlots + 3] = gtimer();
-        // c_proj partial: rows [o0, o1) of the head-h column block, four rows
-        // per warp at a time (lanes over the head's dims)
+        attention_step(smem, sc, Ks, qkv_w, tag_tok + (uint32_t)l, kcs[l], pos, smax, hd, D, max_ctx, g.h,
+                       m.attn_scale, more ? m.kv_map[l + 1] : nullptr, more ? staged(pos) : 0, status);
+        pending = more;
+        if (ts) ts[1] = ts[2] = ts[3] = gtimer();
         const bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-        const float *sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
-        if (have) {
-          const int nr = g.o1 - g.o0;
-          float av[kMaxHd / 32];
-#pragma unroll
-          for (int u = 0; u < kMaxHd / 32; u++) av[u] = lane + 32 * u < hd ? atts[lane + 32 * u] : 0.0f;
-          for (int i0 = warp * 4; i0 < nr; i0 += kWarps * 4) {
-            float s[4];
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-              s[r] = 0.0f;
-              const int i = i0 + r < nr ? i0 + r : i0;
-#pragma unroll
-              for (int u = 0; u < kMaxHd / 32; u++)
-                if (lane + 32 * u < hd) s[r] = fmaf(sb[(size_t)i * hd + lane + 32 * u], av[u], s[r]);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-              for (int r = 0; r < 4; r++) s[r] += __shfl_xor_sync(0xffffffffu, s[r], o);
-            if (lane < 4 && i0 + lane < nr) {
-              const float v = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : s[3];
-              red_word(red_att + g.o0 + i0 + lane, v, status);
-            }
-          }
-        } else {
+        if (have)
+          cproj_step(smem, stage(q), g.o1 - g.o0, hd, red_att + g.o0, status);
+        else
           for (int i = t; i < g.o1 - g.o0; i += kThreads) red_word(red_att + g.o0 + i, 0.0f, status);
-        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
-        if (trace) tr[p * kTraceSlots + 4] = gtimer();
+        if (ts) ts[4] = gtimer();
       }
 
       // ===== c_fc rows + GELU, then their K slice of mlp.c_proj
       {
-        const int p = 3 * l + 2;
-        if (trace) tr[p * kTraceSlots + 0] = gtimer();
-        float2 sv[kPairsPerThread];
-        poll_reduced(red_att, D, C_att, status, t, sv);
-        if (trace) tr[p * kTraceSlots + 1] = gtimer();
+        uint64_t *ts = tr ? tr + (3 * l + 2) * kTraceSlots : nullptr;
+        if (ts) ts[0] = gtimer();
         bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-        const float *sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
-        if (trace) tr[p * kTraceSlots + 2] = gtimer();
-        add_reduced(xres, sb + 2 * D, D, t, sv);   // x += (att c_proj + b)
-        csync();
-        if (trace) tr[p * kTraceSlots + 3] = gtimer();
-        float xr[4 * NK];
-        load_x<NK>(xres, lane, xr);
-        layernorm_regs<NK>(xr, sb, sb + D, lane, D, eps);
-        if (trace) tr[p * kTraceSlots + 7] = gtimer();
-        const int nr = g.f1 - g.f0, bofs = 3 * D + (g.f0 & 3);
-        if (have) {
-#pragma unroll 1
-          for (int k = 0; k < kRowsPerWarp; k += 2) {
-            const int i = warp + kWarps * k, i2 = i + kWarps;
-            if (i < nr) {
-              const bool two = i2 < nr;
-              float a, b;
-              dot2<NK>(reinterpret_cast<const float4 *>(sb + hdr + (size_t)i * D),
-                       reinterpret_cast<const float4 *>(sb + hdr + (size_t)(two ? i2 : i) * D), two, xr, lane, a, b);
-              if (lane == 0) {
-                fv[i] = gelu_tanh(__fadd_rn(a, sb[bofs + i]));
-                if (two) fv[i2] = gelu_tanh(__fadd_rn(b, sb[bofs + i2]));
-              }
-            }
-          }
-        }
+        const float *sb = stage(q);
+        if (ts) ts[2] = gtimer();
+        xv = input_ln(smem, red_att, C_att, sb + 2 * D, sb, sb + D, xv, D, eps, status);   // x += (att c_proj + b)
+        if (ts) ts[3] = ts[7] = gtimer();
+        const int nr = g.f1 - g.f0;
+        if (have)
+          rows_step<NK>(smem, sb + hdr, sb + 3 * D + (g.f0 & 3), nr, D, ROWS_FC, nullptr, 0u, nullptr, nullptr, 0);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
         csync();
-        // mlp.c_proj partial over this CTA's hidden rows: outputs over threads
         have = mbar_wait(&full[q & 1], (q >> 1) & 1, status) && have;
-        const float *wt = ring + (size_t)(q & 1) * (kStageBytes / 4);
-        for (int o = t; o < D; o += kThreads) {
-          float a = 0.0f;
-          if (have) {
-#pragma unroll 8
-            for (int k = 0; k < nr; k++) a = fmaf(fv[k], wt[(size_t)k * D + o], a);
-          }
-          red_word(red_mlp + o, a, status);
-        }
+        mproj_step(smem, stage(q), have ? nr : 0, D, red_mlp, status);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
-        if (trace) tr[p * kTraceSlots + 4] = gtimer();
+        if (ts) ts[4] = gtimer();
       }
     }
 
     // ===== ln_f + lm_head rows, argmax
-    float best = -INFINITY;
-    int bidx = 0x7fffffff;
     {
-      const int p = 3 * nl;
-      if (trace) tr[p * kTraceSlots + 0] = gtimer();
-      float2 sv[kPairsPerThread];
-      poll_reduced(red + (size_t)(2 * nl - 1) * D, D, C_mlp, status, t, sv);
-      if (trace) tr[p * kTraceSlots + 1] = gtimer();
+      uint64_t *ts = tr ? tr + (3 * nl) * kTraceSlots : nullptr;
+      if (ts) ts[0] = gtimer();
       bool have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-      const float *sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
-      if (trace) tr[p * kTraceSlots + 2] = gtimer();
-      add_reduced(xres, sb + 2 * D, D, t, sv);
-      csync();
-      if (trace) tr[p * kTraceSlots + 3] = gtimer();
-      float xr[4 * NK];
-      load_x<NK>(xres, lane, xr);
-      layernorm_regs<NK>(xr, sb, sb + D, lane, D, eps);
-      if (trace) tr[p * kTraceSlots + 7] = gtimer();
+      const float *sb = stage(q);
+      if (ts) ts[2] = gtimer();
+      xv = input_ln(smem, red + (size_t)(2 * nl - 1) * D, C_mlp, sb + 2 * D, sb, sb + D, xv, D, eps, status);
+      if (ts) ts[3] = ts[7] = gtimer();
+      if (lane == 0) {
+        rbv[warp] = -INFINITY;
+        rbi[warp] = 0x7fffffff;
+      }
       for (int j = 0; j < g.n_lm; j++) {
         if (j > 0) {
           have = mbar_wait(&full[q & 1], (q >> 1) & 1, status);
-          sb = ring + (size_t)(q & 1) * (kStageBytes / 4);
+          sb = stage(q);
         }
         const int r0 = g.v0 + j * g.R;
         const int cn = r0 + g.R <= g.v1 ? g.R : (g.v1 > r0 ? g.v1 - r0 : 0);
-        const float *w = sb + hdr;
-        if (have) {
-          for (int i = warp; i < cn; i += 2 * kWarps) {
-            const int i2 = i + kWarps;
-            const bool two = i2 < cn;
-            float a, b;
-            dot2<NK>(reinterpret_cast<const float4 *>(w + (size_t)i * D),
-                     reinterpret_cast<const float4 *>(w + (size_t)(two ? i2 : i) * D), two, xr, lane, a, b);
-            if (lane == 0) {
-              const int n = r0 + i;
-              if (logits) logits[n] = a;
-              if (better(a, n, best, bidx)) { best = a; bidx = n; }
-              if (two) {
-                if (logits) logits[n + kWarps] = b;
-                if (better(b, n + kWarps, best, bidx)) { best = b; bidx = n + kWarps; }
-              }
-            }
-          }
-        }
+        if (have) rows_step<NK>(smem, sb + hdr, nullptr, cn, D, ROWS_LM, nullptr, 0u, nullptr, m.logits, r0);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
       }
-      if (trace) tr[p * kTraceSlots + 4] = gtimer();
+      if (ts) ts[4] = gtimer();
     }
-
-    // ---- argmax: publish this CTA's best, fold every CTA's -----------------
-    // The fence before the publish releases this CTA's KV-cache rows of the
-    // token (written by other warps before the barrier); the one after the
-    // fold acquires every CTA's, which the next token's staging copies read.
-    if (lane == 0) {
-      rbv[warp] = best;
-      rbi[warp] = bidx;
-    }
-    csync();
-    if (warp == 0) {
-      const uint32_t tag_am = tag_tok + (uint32_t)nl;
-      float bv = lane < kWarps ? rbv[lane] : -INFINITY;
-      int bi = lane < kWarps ? rbi[lane] : 0x7fffffff;
-      warp_best(bv, bi);
-      if (lane == 0) {
-        fence_gpu();
-        st_word_rep(m.part_w + 2 * blockIdx.x, kPartWords, __float_as_uint(bv), tag_am);
-        st_word_rep(m.part_w + 2 * blockIdx.x + 1, kPartWords, (uint32_t)bi, tag_am);
-      }
-      bv = -INFINITY;
-      bi = 0x7fffffff;
-      for (int b = lane; b < g.G; b += 32) {
-        float pw[2];
-        wait_words<2>(m.part_w + (size_t)(blockIdx.x % kReplicas) * kPartWords + 2 * b, 1, 2, tag_am, status, pw);
-        const int ib = (int)__float_as_uint(pw[1]);
-        if (better(pw[0], ib, bv, bi)) { bv = pw[0]; bi = ib; }
-      }
-      warp_best(bv, bi);
-      fence_gpu();
-      if (lane == 0) tok_s[0] = bi == 0x7fffffff ? 0 : bi;
-    }
+    tok = argmax_step(smem, m.part_w, tag_tok + (uint32_t)nl, g.G, status);
     // the next token's layer-0 prefix: rows [0, pos] (row pos written this token)
-    const bool next = tk + 1 < ln.n_tokens;
-    const int nrows = next ? staged(ln.pos_ok ? pos + 1 : 0) : 0;
-    if (next && t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nrows * hd * 4));
-    csync();
-    tok = tok_s[0];
-    if (next) {
+    if (tk + 1 < ln.n_tokens) {
+      const int nb = (staged(ln.pos_ok ? pos + 1 : 0) + kBoxRows - 1) / kBoxRows;
+      if (t == 0) mbar_expect_tx(pfx, (uint32_t)(2 * nb * kBoxRows * hd * 4));
+      csync();
       asm volatile("fence.proxy.async.global;" ::: "memory");
-      issue_prefix(0, nrows);
+      if (t < 2 * nb) {
+        const int v = t >= nb, b = v ? t - nb : t;
+          tma_2d(Ks + (v ? (size_t)smax * hd : 0) + (size_t)b * kBoxRows * hd, m.kv_map[0], g.h * hd,
+               (v ? max_ctx : 0) + b * kBoxRows, pfx);
+      }
       pending = true;
     }
   }
@@ -914,32 +933,43 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
   }
 }
 
-// Producer warp: every weight transfer of the launch, in order, into the
-// stage its consumers released, plus L2 prefetches ahead.
+// Producer warp: every weight transfer of the launch, in order (from the
+// table built at launch), into the stage its consumers released, plus L2
+// prefetches ahead.
 __device__ __noinline__ void producer_role(const Sm100DecodeModel &m, const Launch &ln, const Geo &g,
                                            unsigned char *smem) {
   if ((threadIdx.x & 31) != 0) return;
   float *ring = reinterpret_cast<float *>(smem + Smem::ring);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars), *empty = full + 2;
+  const Xfer *xt = reinterpret_cast<const Xfer *>(smem + Smem::xt);
   const int nx = g.nx, total = nx * ln.n_tokens, nl = m.n_layers, D = m.dim;
   uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * (3 * nl + 1) * kTraceSlots : nullptr;
   const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
-  int issued = 0, ia = 0;
+  // the first half of this CTA's lm_head chunks go to L2 over the last
+  // kLmEarly layers (HBM is mostly idle while the layers wait on each other)
+  const int le = nl < kLmEarly ? nl : kLmEarly, l0 = nl - le, half = g.n_lm / 2, per = (half + le - 1) / le;
+  int issued = 0, qi = 0, pa = 0, pai = 0;   // pa: prefetched transfers (pai: its index in the token)
   for (int qq = 0; qq < total; qq++) {
-    const int s = qq & 1, qi = qq % nx;
-    // the step a transfer feeds (lm_head: its first chunk), traced on the last token
-    const int tp = qi < 4 * nl ? 3 * (qi >> 2) + ((qi & 3) == 0 ? 0 : (qi & 3) == 1 ? 1 : 2) : (qi == 4 * nl ? 3 * nl : -1);
-    const bool trace = tr && qq >= total - nx && tp >= 0 && (qi >= 4 * nl || (qi & 3) != 3);
+    const int s = qq & 1;
+    const bool trace = tr && qq >= total - nx && (qi < 4 * nl ? (qi & 3) != 3 : qi == 4 * nl);
+    const int tp = qi < 4 * nl ? 3 * (qi >> 2) + ((qi & 3) == 0 ? 0 : (qi & 3) == 1 ? 1 : 2) : 3 * nl;
     if (trace) tr[tp * kTraceSlots + 6] = gtimer();
     if (qq >= 2 && !mbar_wait(&empty[s], ((qq >> 1) - 1) & 1, ln.status)) break;
-    issue(xfer_of(m, g, qi), D, ring + (size_t)s * (kStageBytes / 4), &full[s], pol_stream, pol_keep);
+    issue(xt[qi], D, ring + (size_t)s * (kStageBytes / 4), &full[s], pol_stream, pol_keep);
     if (trace) tr[tp * kTraceSlots + 5] = gtimer();
     issued = qq + 1;
-    for (; ia < qq + 2 + kPrefetchAhead && ia < total; ia++) {
-      if (ia < 2) continue;
-      const Xfer x = xfer_of(m, g, ia % nx);
-      if (x.wbytes) bulk_prefetch_l2(x.w, x.wbytes);
+#pragma unroll 1
+    for (; pa < qq + 2 + kPrefetchAhead && pa < total; pa++) {
+      if (pa >= 2 && xt[pai].wbytes) bulk_prefetch_l2(xt[pai].w, xt[pai].wbytes);
+      if (++pai == nx) pai = 0;
     }
+    if (qi >= 4 * l0 && qi < 4 * nl && (qi & 3) == 0) {
+      const int k = (qi >> 2) - l0;
+#pragma unroll 1
+      for (int j = k * per; j < (k + 1) * per && j < half; j++)
+        if (xt[4 * nl + j].wbytes) bulk_prefetch_l2(xt[4 * nl + j].w, xt[4 * nl + j].wbytes);
+    }
+    if (++qi == nx) qi = 0;
   }
   // every issued transfer has landed before the CTA exits (bounded, not cut
   // short by the status)
@@ -972,6 +1002,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100Dec
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Smem::bars);
   float **kcs = reinterpret_cast<float **>(smem + Smem::kcs);
   for (int l = t; l < nl; l += kBlockThreads) kcs[l] = m.kv_cache[l];
+  Xfer *xt = reinterpret_cast<Xfer *>(smem + Smem::xt);
+  for (int i = t; i < g.nx; i += kBlockThreads) xt[i] = xfer_of(m, g, i);
   if (t == 0) {
     if (!ln.pos_ok && c == 0) atomicOr(ln.status, SM100_DECODE_ERR_ARG);
     mbar_init(&bars[0], 1);        // full[0], full[1]: armed by the producer
@@ -1032,6 +1064,39 @@ extern "C" int sm100_decode_regroup(const float *w_o, const float *w_p2, float *
   return launch_status("decode_regroup");
 }
 
+typedef CUresult (*DecEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+extern "C" int sm100_decode_prepare(Sm100DecodeModel *desc) {
+  static DecEncodeFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return sm100_set_error(SM100_ERR_CUDA, "decode_prepare: cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<DecEncodeFn>(p);
+  }
+  if (!desc || desc->n_layers <= 0 || desc->n_layers > kMaxLayers || desc->dim <= 0 || desc->max_ctx <= 0 ||
+      (desc->head_dim != 32 && desc->head_dim != 64))
+    return sm100_set_error(SM100_ERR_ARG, "decode_prepare: bad descriptor");
+  static_assert(sizeof(CUtensorMap) == 128, "tensor map size");
+  for (int l = 0; l < desc->n_layers; l++) {
+    const cuuint64_t dims[2] = {(cuuint64_t)desc->dim, 2 * (cuuint64_t)desc->max_ctx};
+    const cuuint64_t strides[1] = {(cuuint64_t)desc->dim * 4};
+    const cuuint32_t box[2] = {(cuuint32_t)desc->head_dim, (cuuint32_t)kBoxRows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUtensorMap *mp = reinterpret_cast<CUtensorMap *>(desc->kv_map[l]);
+    if (!desc->kv_cache[l] ||
+        fn(mp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, desc->kv_cache[l], dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return sm100_set_error(SM100_ERR_CUDA, "decode_prepare: tensor map of layer %d", l);
+  }
+  return SM100_OK;
+}
+
 extern "C" int32_t sm100_decode_grid(int32_t heads, int32_t head_dim) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1076,22 +1141,24 @@ extern "C" int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_t
   const int hd = heads > 0 ? dim / heads : 0;
   const int M = heads > 0 && hd > 0 ? members_per_head(heads, hd, g_num_sms[dev]) : 0, G = M * heads;
   bool ok = dev_model && M >= 3 && n_tokens > 0 && (int64_t)n_tokens * (n_layers + 2) < 65536 && n_layers > 0 &&
-            n_layers <= kMaxLayers && dim > 0 && dim % 128 == 0 && dim <= kMaxDim && hd * heads == dim &&
-            (hd == 32 || hd == 64) && vocab > 0 && max_ctx > 0 && Smem::smax(max_ctx, hd) >= 1;
+            n_layers <= kMaxLayers && dim > 0 && dim % 128 == 0 && dim <= 2 * kThreads && hd * heads == dim &&
+            (hd == 32 || hd == 64) && vocab > 0 && max_ctx > 0 &&
+            Smem::smax(max_transfers(n_layers, vocab, G, dim), max_ctx, hd) >= 1;
   if (ok) {
     // every CTA's transfers within one stage; row slices within the row slots
     const Geo g0 = geo_of(0, G, heads, dim, hd, vocab, n_layers);
     const int64_t D = dim, frow = (4 * D + G - 1) / G, orow = (D + M - 1) / M;
     const int64_t hdr = hdr_floats(dim);
     ok = g0.qn <= kMaxRows && g0.qn + 6 <= kBiasFloats && (hdr + g0.qn * D) * 4 <= kStageBytes &&
-         orow * hd * 4 <= kStageBytes && frow <= kMaxRows && frow <= 64 && frow + 6 <= kBiasFloats &&
-         (hdr + frow * D) * 4 <= kStageBytes && g0.R >= 1 && Smem::total(max_ctx, hd) <= (size_t)kSmemLimit;
+         orow * hd * 4 <= kStageBytes && orow <= kCpRows * kWarps && frow <= kMaxRows && frow <= 64 && frow + 6 <= kBiasFloats &&
+         (hdr + frow * D) * 4 <= kStageBytes && g0.R >= 1 &&
+         Smem::total(max_transfers(n_layers, vocab, G, dim), max_ctx, hd) <= (size_t)kSmemLimit;
   }
   if (!ok)
     return sm100_set_error(SM100_ERR_ARG,
                            "decode: unsupported shape (tokens %d, layers %d, dim %d, heads %d, vocab %d, ctx %d, %d SMs)",
                            n_tokens, n_layers, dim, heads, vocab, max_ctx, g_num_sms[dev]);
-  const size_t smem = Smem::total(max_ctx, hd);
+  const size_t smem = Smem::total(max_transfers(n_layers, vocab, G, dim), max_ctx, hd);
   switch (dim / 128) {
     case 4: return launch_decode<4>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
     case 6: return launch_decode<6>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);

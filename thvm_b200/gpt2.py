@@ -206,6 +206,7 @@ class Transformer:
         m.logits = p(s.logits)
         self.sync = dev.alloc(dev.lib.sm100_decode_sync_bytes())
         m.sync = p(self.sync)
+        L.check(dev.lib.sm100_decode_prepare(ctypes.addressof(m)), "decode_prepare")
         self.desc = dev.alloc(ctypes.sizeof(m))
         L.check(dev.lib.sm100_buf_write(self.desc, ctypes.addressof(m), ctypes.sizeof(m)), "buf_write(desc)")
         self._desc_host = m
