@@ -72,6 +72,7 @@ constexpr int kFixShift = 28;                // reduction words: fixed point wit
 constexpr float kFixLimit = 2048.0f;         // |contribution| bound (sums stay below 2^47 / 2^28)
 constexpr int kBoxRows = 32;                 // KV staging: rows of one tensor-map box
 constexpr int kCpRows = 5;                   // c_proj rows per warp (a member has <= kCpRows kWarps)
+static_assert(kCpRows == 5, "cproj_step selects among five rows");
 constexpr int kLmEarly = 6;                  // lm_head L2 prefetch spread over the last layers
 
 // Argmax partials go to kReplicas copies; consumer CTA c polls copy c % kReplicas
@@ -681,26 +682,50 @@ __device__ __noinline__ void cproj_step(unsigned char *smem, const float *w, int
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const float *atts = reinterpret_cast<const float *>(smem + Smem::atts);
   const float a0 = atts[lane], a1 = hd > 32 ? atts[lane + 32] : 0.0f;
-#pragma unroll 1
-  for (int i = warp; i < nr; i += kWarps) {
-    float s = __fmul_rn(w[(size_t)i * hd + lane], a0);
-    if (hd > 32) s = fmaf(w[(size_t)i * hd + lane + 32], a1, s);
-    s = warp_sum(s);
-    if (lane == 0) red_word(out + i, s, status);
+  float s[kCpRows];
+#pragma unroll
+  for (int r = 0; r < kCpRows; r++) {
+    const int i = warp + kWarps * r;
+    s[r] = 0.0f;
+    if (i < nr) {
+      s[r] = __fmul_rn(w[(size_t)i * hd + lane], a0);
+      if (hd > 32) s[r] = fmaf(w[(size_t)i * hd + lane + 32], a1, s[r]);
+    }
   }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < kCpRows; r++) s[r] += __shfl_xor_sync(0xffffffffu, s[r], o);
+  // lane r adds row warp + r kWarps
+  const float v = lane == 0 ? s[0] : lane == 1 ? s[1] : lane == 2 ? s[2] : lane == 3 ? s[3] : s[4];
+  const int i = warp + kWarps * lane;
+  if (lane < kCpRows && i < nr) red_word(out + i, v, status);
 }
 
 // mlp.c_proj partial over this CTA's hidden rows: out[o] += sum_k fv[k]
-// wt[k][o] (wt: nr x D, the transposed weight's rows), outputs over threads.
+// wt[k][o] (wt: nr x D, the transposed weight's rows); thread t takes the
+// outputs 2 t, 2 t + 1 (D <= 2 kThreads).
 __device__ __noinline__ void mproj_step(unsigned char *smem, const float *wt, int nr, int D, uint64_t *out,
                                         uint32_t *status) {
   const int t = threadIdx.x;
   const float *fv = reinterpret_cast<const float *>(smem + Smem::fv);
-  for (int o = t; o < D; o += kThreads) {
-    float a = 0.0f;
-#pragma unroll 8
-    for (int k = 0; k < nr; k++) a = fmaf(fv[k], wt[(size_t)k * D + o], a);
-    red_word(out + o, a, status);
+  if (2 * t < D) {
+    float a = 0.0f, b = 0.0f;
+#pragma unroll 4
+    for (int k = 0; k < nr; k++) {
+      const float2 w2 = reinterpret_cast<const float2 *>(wt + (size_t)k * D)[t];
+      const float f = fv[k];
+      a = fmaf(f, w2.x, a);
+      b = fmaf(f, w2.y, b);
+    }
+    // lane l adds words 64 w + l and 64 w + 32 + l (warp w = t / 32): each
+    // red instruction covers 32 consecutive words, so the L2 atomic units see
+    // whole lines (lane l's words belong to lanes l / 2 and 16 + l / 2)
+    const int lane = t & 31, w0 = 64 * (t >> 5);
+    const float pa = __shfl_sync(0xffffffffu, a, lane >> 1), pb = __shfl_sync(0xffffffffu, b, lane >> 1);
+    const float qa = __shfl_sync(0xffffffffu, a, 16 + (lane >> 1)), qb = __shfl_sync(0xffffffffu, b, 16 + (lane >> 1));
+    if (w0 + lane < D) red_word(out + w0 + lane, (lane & 1) ? pb : pa, status);
+    if (w0 + 32 + lane < D) red_word(out + w0 + 32 + lane, (lane & 1) ? qb : qa, status);
   }
 }
 
