@@ -73,7 +73,6 @@ constexpr float kFixLimit = 2048.0f;         // |contribution| bound (sums stay 
 constexpr int kBoxRows = 32;                 // KV staging: rows of one tensor-map box
 constexpr int kCpRows = 5;                   // c_proj rows per warp (a member has <= kCpRows kWarps)
 static_assert(kCpRows == 5, "cproj_step selects among five rows");
-constexpr int kLmEarly = 6;                  // lm_head L2 prefetch spread over the last layers
 
 // Argmax partials go to kReplicas copies; consumer CTA c polls copy c % kReplicas
 // (every CTA reads every CTA's partial).
@@ -323,6 +322,7 @@ __device__ __forceinline__ Xfer xfer_of(const Sm100DecodeModel &m, const Geo &g,
   Xfer x;
   x.ln_g = x.ln_b = x.bx = x.b = nullptr;
   x.bbytes = 0;
+  x.pad = 0;
   int r = 0, nr = 0;
   const float *bias = nullptr;
   if (i < 4 * nl) {
@@ -970,9 +970,6 @@ __device__ __noinline__ void producer_role(const Sm100DecodeModel &m, const Laun
   const int nx = g.nx, total = nx * ln.n_tokens, nl = m.n_layers, D = m.dim;
   uint64_t *tr = m.trace ? m.trace + (size_t)blockIdx.x * (3 * nl + 1) * kTraceSlots : nullptr;
   const uint64_t pol_stream = policy_evict_first(), pol_keep = policy_evict_last();
-  // the first half of this CTA's lm_head chunks go to L2 over the last
-  // kLmEarly layers (HBM is mostly idle while the layers wait on each other)
-  const int le = nl < kLmEarly ? nl : kLmEarly, l0 = nl - le, half = g.n_lm / 2, per = (half + le - 1) / le;
   int issued = 0, qi = 0, pa = 0, pai = 0;   // pa: prefetched transfers (pai: its index in the token)
   for (int qq = 0; qq < total; qq++) {
     const int s = qq & 1;
@@ -987,12 +984,6 @@ __device__ __noinline__ void producer_role(const Sm100DecodeModel &m, const Laun
     for (; pa < qq + 2 + kPrefetchAhead && pa < total; pa++) {
       if (pa >= 2 && xt[pai].wbytes) bulk_prefetch_l2(xt[pai].w, xt[pai].wbytes);
       if (++pai == nx) pai = 0;
-    }
-    if (qi >= 4 * l0 && qi < 4 * nl && (qi & 3) == 0) {
-      const int k = (qi >> 2) - l0;
-#pragma unroll 1
-      for (int j = k * per; j < (k + 1) * per && j < half; j++)
-        if (xt[4 * nl + j].wbytes) bulk_prefetch_l2(xt[4 * nl + j].w, xt[4 * nl + j].wbytes);
     }
     if (++qi == nx) qi = 0;
   }
