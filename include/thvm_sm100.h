@@ -295,12 +295,15 @@ typedef struct {
   uint8_t kv_map[SM100_DECODE_MAX_LAYERS][128];
   int32_t n_layers, dim, hidden, vocab, max_ctx, heads, head_dim, bump;
   float eps, attn_scale;
-  const float *wte, *wpe, *ln_f_g, *ln_f_b, *lm_head;
+  /* c_attn, c_fc and lm_head weights block-transposed for the decode grid
+   * (sm100_decode_block_transpose); the other matrices as the reference stores
+   * them, or regrouped (w_o_h, w_p2_t) */
+  const float *wte, *wpe, *ln_f_g, *ln_f_b, *lm_head_bt;
   const float *ln1_g[SM100_DECODE_MAX_LAYERS], *ln1_b[SM100_DECODE_MAX_LAYERS];
-  const float *w_qkv[SM100_DECODE_MAX_LAYERS], *b_qkv[SM100_DECODE_MAX_LAYERS];
+  const float *w_qkv_bt[SM100_DECODE_MAX_LAYERS], *b_qkv[SM100_DECODE_MAX_LAYERS];
   const float *b_o[SM100_DECODE_MAX_LAYERS];
   const float *ln2_g[SM100_DECODE_MAX_LAYERS], *ln2_b[SM100_DECODE_MAX_LAYERS];
-  const float *w_fc[SM100_DECODE_MAX_LAYERS], *b_fc[SM100_DECODE_MAX_LAYERS];
+  const float *w_fc_bt[SM100_DECODE_MAX_LAYERS], *b_fc[SM100_DECODE_MAX_LAYERS];
   const float *b_p2[SM100_DECODE_MAX_LAYERS];
   /* the two split projections, regrouped once at load (sm100_decode_regroup):
    * c_proj [heads][dim][head_dim] (w_o_h[h][o][d] = W_o[o][h head_dim + d]),
@@ -333,6 +336,12 @@ uint64_t sm100_decode_sync_bytes(void);
 uint64_t sm100_decode_part_bytes(void);
 uint64_t sm100_decode_trace_bytes(int32_t n_layers);
 uint64_t sm100_decode_red_bytes(int32_t n_layers, int32_t dim);
+/* block-transposed copy of a row-sliced weight for the decode grid on the
+ * current device: kind 0 c_attn [3 dim][dim], 1 c_fc [4 dim][dim], 2 lm_head
+ * [vocab][dim]; every slice [r, r + nr) a decode CTA streams is stored at
+ * offset r dim as [dim / 4][nr][4] (device pointers, f32) */
+int sm100_decode_block_transpose(const float *src, float *dst, int32_t kind, int32_t dim, int32_t heads,
+                                 int32_t vocab, void *stream);
 /* fills desc->kv_map from kv_cache, max_ctx, dim and head_dim (host memory;
  * call before uploading the descriptor) */
 int sm100_decode_prepare(Sm100DecodeModel *desc);

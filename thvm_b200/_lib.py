@@ -84,8 +84,8 @@ class Sm100DecodeModel(ctypes.Structure):
     _fields_ = [("kv_map", (ctypes.c_uint8 * 128) * DECODE_MAX_LAYERS)] + [(n, c_int32) for n in ("n_layers", "dim", "hidden", "vocab", "max_ctx", "heads", "head_dim",
                                        "bump")] + [
         ("eps", c_float), ("attn_scale", c_float)] + [
-        (n, c_void_p) for n in ("wte", "wpe", "ln_f_g", "ln_f_b", "lm_head")] + [
-        (n, _PL) for n in ("ln1_g", "ln1_b", "w_qkv", "b_qkv", "b_o", "ln2_g", "ln2_b", "w_fc", "b_fc",
+        (n, c_void_p) for n in ("wte", "wpe", "ln_f_g", "ln_f_b", "lm_head_bt")] + [
+        (n, _PL) for n in ("ln1_g", "ln1_b", "w_qkv_bt", "b_qkv", "b_o", "ln2_g", "ln2_b", "w_fc_bt", "b_fc",
                            "b_p2", "w_o_h", "w_p2_t", "kv_cache")] + [
         (n, c_void_p) for n in ("io", "qkv_w", "red_w", "part_w", "logits", "trace", "sync")]
 
@@ -147,6 +147,7 @@ SIGNATURES = {
     "sm100_decode_red_bytes": (c_uint64, [c_int32, c_int32]),
     "sm100_decode_grid": (c_int32, [c_int32, c_int32]),
     "sm100_decode_prepare": (c_int, [c_void_p]),
+    "sm100_decode_block_transpose": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_regroup": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),

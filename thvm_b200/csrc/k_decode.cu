@@ -59,8 +59,7 @@ constexpr int kBlockThreads = kThreads + 32; // + one producer warp (TMA issue)
 constexpr int kStages = 2;                   // weight ring stages
 constexpr int kStageBytes = 76 * 1024;       // one stage
 constexpr int kMaxDim = 1024;                // residual stream held in shared memory
-constexpr int kRowsPerWarp = 4;              // row slots of a warp in c_attn / c_fc steps (even)
-constexpr int kMaxRows = kRowsPerWarp * kWarps;
+constexpr int kMaxRows = 32;                 // rows of one c_attn / c_fc slice or lm_head chunk (a lane each)
 constexpr int kMaxHd = 64;
 constexpr int kPrefetchAhead = 4;            // L2 prefetch distance in transfers
 constexpr int kMaxLayers = SM100_DECODE_MAX_LAYERS;
@@ -330,7 +329,7 @@ __device__ __forceinline__ Xfer xfer_of(const Sm100DecodeModel &m, const Geo &g,
     switch (i & 3) {
       case 0:   // c_attn rows; header: ln_1, mlp.c_proj bias of layer l - 1
         r = g.qrow0; nr = g.qn;
-        x.w = m.w_qkv[l] + (size_t)r * D;
+        x.w = m.w_qkv_bt[l] + (size_t)r * D;
         x.ln_g = m.ln1_g[l]; x.ln_b = m.ln1_b[l];
         x.bx = l > 0 ? m.b_p2[l - 1] : nullptr;
         bias = m.b_qkv[l];
@@ -343,7 +342,7 @@ __device__ __forceinline__ Xfer xfer_of(const Sm100DecodeModel &m, const Geo &g,
         return x;
       case 2:   // c_fc rows; header: ln_2, c_proj bias
         r = g.f0; nr = g.f1 - g.f0;
-        x.w = m.w_fc[l] + (size_t)r * D;
+        x.w = m.w_fc_bt[l] + (size_t)r * D;
         x.ln_g = m.ln2_g[l]; x.ln_b = m.ln2_b[l];
         x.bx = m.b_o[l];
         bias = m.b_fc[l];
@@ -359,7 +358,7 @@ __device__ __forceinline__ Xfer xfer_of(const Sm100DecodeModel &m, const Geo &g,
     const int j = i - 4 * nl;
     r = g.v0 + j * g.R;
     nr = r + g.R <= g.v1 ? g.R : (g.v1 > r ? g.v1 - r : 0);
-    x.w = m.lm_head + (size_t)r * D;
+    x.w = m.lm_head_bt + (size_t)r * D;
     if (j == 0) {   // header: ln_f, mlp.c_proj bias of the last layer
       x.ln_g = m.ln_f_g; x.ln_b = m.ln_f_b;
       x.bx = m.b_p2[nl - 1];
@@ -398,12 +397,12 @@ struct Smem {
   static constexpr size_t xs = ring + (size_t)kStages * kStageBytes;    // [kMaxDim] LayerNorm output
   static constexpr size_t lnp = xs + kMaxDim * 4;                         // [2][16] LayerNorm partial sums
   static constexpr size_t fv = lnp + 32 * 4;                              // [kMaxRows] c_fc outputs
-  static constexpr size_t qkvs = fv + 64 * 4;                             // [3 kMaxHd] q, k, v of the head
+  static constexpr size_t rp = fv + kMaxRows * 4;                         // [2][2 kWarps][32] row partial sums
+  static constexpr size_t lmb = rp + 2 * 2 * kWarps * 32 * 4;             // [kMaxRows] f32 + [kMaxRows] i32: row bests
+  static constexpr size_t qkvs = lmb + 2 * kMaxRows * 4;                  // [3 kMaxHd] q, k, v of the head
   static constexpr size_t atts = qkvs + 3 * kMaxHd * 4;                   // [kMaxHd] attention output
   static constexpr size_t acc = atts + kMaxHd * 4;                        // [kThreads] p @ v slices
-  static constexpr size_t rbv = acc + kThreads * 4;                       // [kWarps] f32 (+1 pad)
-  static constexpr size_t rbi = rbv + 16 * 4;                             // [kWarps] i32
-  static constexpr size_t tok = rbi + 16 * 4;                             // [4] i32
+  static constexpr size_t tok = acc + kThreads * 4;                       // [4] i32
   static constexpr size_t bars = tok + 16;                                // full[2], empty[2], pfx
   static constexpr size_t kcs = bars + 8 * 8;                             // [kMaxLayers] cache pointers
   static constexpr size_t cps = kcs + kMaxLayers * 8;                     // [kCpRows kWarps] c_proj partials
@@ -431,47 +430,6 @@ struct Launch {
   uint32_t *status;
   uint32_t tok0;               // tokens decoded by earlier launches (selects the reduction sets)
 };
-
-template <int NK>
-__device__ __forceinline__ void load_x(const float *xb, int lane, float (&xr)[4 * NK]) {
-#pragma unroll
-  for (int j = 0; j < NK; j++) {
-    const float4 v = reinterpret_cast<const float4 *>(xb)[lane + 32 * j];
-    xr[4 * j] = v.x; xr[4 * j + 1] = v.y; xr[4 * j + 2] = v.z; xr[4 * j + 3] = v.w;
-  }
-}
-
-// Dot products of two rows (w0, w1: float4 rows in shared memory) with the
-// lanes' registers; every lane gets both sums.
-template <int NK>
-__device__ __forceinline__ void dot2(const float4 *w0, const float4 *w1, bool two, const float (&xr)[4 * NK], int lane,
-                                     float &a, float &b) {
-  float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
-#pragma unroll
-  for (int j = 0; j < NK; j++) {
-    const float4 u = w0[lane + 32 * j];
-    float &aa = (j & 1) ? a1 : a0;
-    aa = fmaf(u.x, xr[4 * j], aa);
-    aa = fmaf(u.y, xr[4 * j + 1], aa);
-    aa = fmaf(u.z, xr[4 * j + 2], aa);
-    aa = fmaf(u.w, xr[4 * j + 3], aa);
-    if (two) {
-      const float4 v = w1[lane + 32 * j];
-      float &bb = (j & 1) ? b1 : b0;
-      bb = fmaf(v.x, xr[4 * j], bb);
-      bb = fmaf(v.y, xr[4 * j + 1], bb);
-      bb = fmaf(v.z, xr[4 * j + 2], bb);
-      bb = fmaf(v.w, xr[4 * j + 3], bb);
-    }
-  }
-  a = a0 + a1;
-  b = b0 + b1;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    a += __shfl_xor_sync(0xffffffffu, a, o);
-    b += __shfl_xor_sync(0xffffffffu, b, o);
-  }
-}
 
 // The per-layer path of the consumer warps is a handful of out-of-line
 // functions (one rows loop for c_attn, c_fc and lm_head, one LayerNorm, the
@@ -526,50 +484,62 @@ __device__ __noinline__ float2 input_ln(unsigned char *smem, const uint64_t *wor
 
 enum { ROWS_QKV = 0, ROWS_FC, ROWS_LM };
 
-// Rows [0, nr) of a stage (w: row-major, D floats a row) dotted with the
-// LayerNorm output: warp w takes rows w, w + kWarps (one pass of two), then
-// w + 2 kWarps, ...; lane 0 finishes a row:
+// Rows [0, nr) (nr <= 32) of a block-transposed slice wt ([D / 4][nr][4]:
+// element (i, k) at ((k / 4) nr + i) 4 + k % 4, sm100_decode_block_transpose)
+// dotted with the LayerNorm output.  Lane i of a lane group (16 or 32 lanes)
+// takes row i over a K slice (the CTA's K range split over warps and groups:
+// the weights are read from shared memory once, the input as broadcasts);
+// thread i folds the slices' partial sums in a fixed order and finishes row i:
 //  ROWS_QKV: y = dot + bias[i] published to dst[i] (tag) and, for k / v
 //            rows, written to the KV cache row (cache[i]);
 //  ROWS_FC:  fv[i] = GELU(dot + bias[i]);
-//  ROWS_LM:  logits[r0 + i] = dot (when logits), the warp's best (value,
-//            index) kept in rbv / rbi.
-template <int NK>
-__device__ __noinline__ void rows_step(unsigned char *smem, const float *w, const float *bias, int nr, int D, int kind,
-                                       uint64_t *dst, uint32_t tag, float *cache, float *logits, int r0) {
+//  ROWS_LM:  logits[r0 + i] = dot (when logits), the row's running best
+//            (value, index) kept in lmb / lmi.
+// par alternates between consecutive calls (two partial-sum buffers).
+__device__ __noinline__ void rows_step(unsigned char *smem, const float *wt, const float *bias, int nr, int D, int kind,
+                                       uint64_t *dst, uint32_t tag, float *cache, float *logits, int r0, int par) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const float *xs = reinterpret_cast<const float *>(smem + Smem::xs);
-  float *fv = reinterpret_cast<float *>(smem + Smem::fv);
-  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
-  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
-  float xr[4 * NK];
-  load_x<NK>(xs, lane, xr);
-  for (int i = warp; i < nr; i += 2 * kWarps) {
-    const int i2 = i + kWarps;
-    const bool two = i2 < nr;
-    float a, b;
-    dot2<NK>(reinterpret_cast<const float4 *>(w + (size_t)i * D),
-             reinterpret_cast<const float4 *>(w + (size_t)(two ? i2 : i) * D), two, xr, lane, a, b);
-    if (lane == 0) {
-#pragma unroll 1
-      for (int u = 0; u < 2; u++) {
-        if (u == 1 && !two) break;
-        const int row = u ? i2 : i;
-        const float d = u ? b : a;
-        if (kind == ROWS_QKV) {
-          const float y = __fadd_rn(d, bias[row]);
-          st_word(dst + row, __float_as_uint(y), tag);
-          if (cache) cache[row] = y;
-        } else if (kind == ROWS_FC) {
-          fv[row] = gelu_tanh(__fadd_rn(d, bias[row]));
-        } else {
-          const int n = r0 + row;
-          if (logits) logits[n] = d;
-          if (better(d, n, rbv[warp], rbi[warp])) {
-            rbv[warp] = d;
-            rbi[warp] = n;
-          }
-        }
+  const float4 *x4 = reinterpret_cast<const float4 *>(smem + Smem::xs);
+  const float4 *w4 = reinterpret_cast<const float4 *>(wt);
+  float *rp = reinterpret_cast<float *>(smem + Smem::rp) + par * (2 * kWarps * 32);
+  const int RP = nr > 16 ? 32 : 16, parts = 32 / RP, np = kWarps * parts;
+  const int row = lane & (RP - 1), part = warp * parts + lane / RP, NG = D / 4;
+  const int g0 = NG * part / np, g1 = NG * (part + 1) / np;
+  float a0 = 0.0f, a1 = 0.0f;
+  if (row < nr) {
+#pragma unroll 4
+    for (int gq = g0; gq < g1; gq++) {
+      const float4 wv = w4[(size_t)gq * nr + row], xv = x4[gq];
+      a0 = fmaf(wv.x, xv.x, a0);
+      a1 = fmaf(wv.y, xv.y, a1);
+      a0 = fmaf(wv.z, xv.z, a0);
+      a1 = fmaf(wv.w, xv.w, a1);
+    }
+  }
+  rp[part * 32 + row] = __fadd_rn(a0, a1);
+  csync();
+  if (t < nr) {
+    // every partial loaded before the fixed-order fold (np <= 2 kWarps)
+    float pv[2 * kWarps];
+#pragma unroll
+    for (int q = 0; q < 2 * kWarps; q++) pv[q] = q < np ? rp[q * 32 + t] : 0.0f;
+    float d = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 2 * kWarps; q++) d += pv[q];
+    if (kind == ROWS_QKV) {
+      const float y = __fadd_rn(d, bias[t]);
+      st_word(dst + t, __float_as_uint(y), tag);
+      if (cache) cache[t] = y;
+    } else if (kind == ROWS_FC) {
+      reinterpret_cast<float *>(smem + Smem::fv)[t] = gelu_tanh(__fadd_rn(d, bias[t]));
+    } else {
+      float *lmb = reinterpret_cast<float *>(smem + Smem::lmb);
+      int *lmi = reinterpret_cast<int *>(lmb + kMaxRows);
+      const int n = r0 + t;
+      if (logits) logits[n] = d;
+      if (better(d, n, lmb[t], lmi[t])) {
+        lmb[t] = d;
+        lmi[t] = n;
       }
     }
   }
@@ -736,13 +706,13 @@ __device__ __noinline__ void mproj_step(unsigned char *smem, const float *wt, in
 // the fence after the fold acquires every CTA's.  Returns the token.
 __device__ __noinline__ int argmax_step(unsigned char *smem, uint64_t *part_w, uint32_t tag, int G, uint32_t *status) {
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
-  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
   int *tok_s = reinterpret_cast<int *>(smem + Smem::tok);
   csync();
   if (warp == 0) {
-    float bv = lane < kWarps ? rbv[lane] : -INFINITY;
-    int bi = lane < kWarps ? rbi[lane] : 0x7fffffff;
+    const float *lmb = reinterpret_cast<const float *>(smem + Smem::lmb);
+    const int *lmi = reinterpret_cast<const int *>(lmb + kMaxRows);
+    float bv = lmb[lane];
+    int bi = lmi[lane];
     warp_best(bv, bi);
     if (lane < kReplicas) {   // one copy per lane
       fence_gpu();
@@ -767,14 +737,11 @@ __device__ __noinline__ int argmax_step(unsigned char *smem, uint64_t *part_w, u
 
 // ---------------------------------------------------------------------------
 // Consumer warps of every CTA: the steps of every token.
-template <int NK>
 __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const Launch &ln, const Geo &g,
                                               unsigned char *smem) {
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int t = threadIdx.x, lane = t & 31;
   const int D = m.dim, hd = m.head_dim, nl = m.n_layers, max_ctx = m.max_ctx, H = m.heads;
   float *ring = reinterpret_cast<float *>(smem + Smem::ring);
-  float *rbv = reinterpret_cast<float *>(smem + Smem::rbv);
-  int *rbi = reinterpret_cast<int *>(smem + Smem::rbi);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + Smem::bars), *empty = full + 2, *pfx = full + 4;
   float *const *kcs = reinterpret_cast<float *const *>(smem + Smem::kcs);
   const int nxt = max_transfers(nl, m.vocab, g.G, D);
@@ -842,8 +809,8 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
                            ? kcs[l] + (size_t)(g.kv_which - 1) * max_ctx * D + (size_t)pos * D + g.qcol0
                            : nullptr;
         if (have)
-          rows_step<NK>(smem, sb + hdr, sb + 3 * D + (g.qrow0 & 3), g.qn, D, ROWS_QKV, qkv_w + g.ql0,
-                        tag_tok + (uint32_t)l, cache, nullptr, 0);
+          rows_step(smem, sb + hdr, sb + 3 * D + (g.qrow0 & 3), g.qn, D, ROWS_QKV, qkv_w + g.ql0,
+                    tag_tok + (uint32_t)l, cache, nullptr, 0, 0);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
@@ -889,7 +856,7 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
         if (ts) ts[3] = ts[7] = gtimer();
         const int nr = g.f1 - g.f0;
         if (have)
-          rows_step<NK>(smem, sb + hdr, sb + 3 * D + (g.f0 & 3), nr, D, ROWS_FC, nullptr, 0u, nullptr, nullptr, 0);
+          rows_step(smem, sb + hdr, sb + 3 * D + (g.f0 & 3), nr, D, ROWS_FC, nullptr, 0u, nullptr, nullptr, 0, 1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
@@ -912,9 +879,10 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
       if (ts) ts[2] = gtimer();
       xv = input_ln(smem, red + (size_t)(2 * nl - 1) * D, C_mlp, sb + 2 * D, sb, sb + D, xv, D, eps, status);
       if (ts) ts[3] = ts[7] = gtimer();
-      if (lane == 0) {
-        rbv[warp] = -INFINITY;
-        rbi[warp] = 0x7fffffff;
+      if (t < kMaxRows) {
+        float *lmb = reinterpret_cast<float *>(smem + Smem::lmb);
+        lmb[t] = -INFINITY;
+        reinterpret_cast<int *>(lmb + kMaxRows)[t] = 0x7fffffff;
       }
       for (int j = 0; j < g.n_lm; j++) {
         if (j > 0) {
@@ -923,7 +891,7 @@ __device__ __forceinline__ void consumer_role(const Sm100DecodeModel &m, const L
         }
         const int r0 = g.v0 + j * g.R;
         const int cn = r0 + g.R <= g.v1 ? g.R : (g.v1 > r0 ? g.v1 - r0 : 0);
-        if (have) rows_step<NK>(smem, sb + hdr, nullptr, cn, D, ROWS_LM, nullptr, 0u, nullptr, m.logits, r0);
+        if (have) rows_step(smem, sb + hdr, nullptr, cn, D, ROWS_LM, nullptr, 0u, nullptr, m.logits, r0, j & 1);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[q & 1]);
         q++;
@@ -993,7 +961,6 @@ __device__ __noinline__ void producer_role(const Sm100DecodeModel &m, const Laun
     if (qq >= 0) mbar_wait(&full[qq & 1], (qq >> 1) & 1, ln.status, false);
 }
 
-template <int NK>
 __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100DecodeModel *__restrict__ mp, int n_tokens) {
   extern __shared__ __align__(1024) unsigned char smem[];
   const Sm100DecodeModel &m = *mp;
@@ -1034,7 +1001,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100Dec
     producer_role(m, ln, g, smem);
     return;
   }
-  consumer_role<NK>(m, ln, g, smem);
+  consumer_role(m, ln, g, smem);
 }
 
 }  // namespace sm100
@@ -1042,6 +1009,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1) decode_kernel(const Sm100Dec
 using namespace sm100;
 
 static int g_num_sms[64];
+extern "C" int32_t sm100_decode_grid(int32_t heads, int32_t head_dim);
 
 extern "C" uint64_t sm100_decode_sync_bytes(void) { return (uint64_t)(4 + 2 * 1024) * 4; }
 
@@ -1078,6 +1046,40 @@ extern "C" int sm100_decode_regroup(const float *w_o, const float *w_p2, float *
                            hidden);
   regroup_kernel<<<592, 256, 0, (cudaStream_t)stream>>>(w_o, w_p2, w_o_h, w_p2_t, dim, dim / heads, hidden);
   return launch_status("decode_regroup");
+}
+
+// Block-transposed copies of the row-sliced weights: every slice [r, r + nr)
+// a decode CTA streams (c_attn: a member's rows, c_fc: a CTA's rows,
+// lm_head: a CTA's chunks) is stored at the same offset as [D / 4][nr][4]
+// (element (i, k) at r D + ((k / 4) nr + i) 4 + k % 4).  One block per CTA
+// of the decode grid, which it recomputes; one-time, at load.
+__global__ void block_transpose_kernel(const float *__restrict__ src, float *__restrict__ dst, int kind, int D,
+                                       int heads, int hd, int vocab) {
+  const Geo g = geo_of(blockIdx.x, (int)gridDim.x, heads, D, hd, vocab, 1);
+  const int nb = kind == 2 ? g.n_lm : 1;
+  for (int j = 0; j < nb; j++) {
+    int r, nr;
+    if (kind == 0) { r = g.qrow0; nr = g.qn; }
+    else if (kind == 1) { r = g.f0; nr = g.f1 - g.f0; }
+    else { r = g.v0 + j * g.R; nr = r + g.R <= g.v1 ? g.R : (g.v1 > r ? g.v1 - r : 0); }
+    const float *s0 = src + (size_t)r * D;
+    float *d0 = dst + (size_t)r * D;
+    for (int e = threadIdx.x; e < nr * D; e += blockDim.x) {
+      const int i = e / D, k = e - i * D;
+      d0[((size_t)(k >> 2) * nr + i) * 4 + (k & 3)] = s0[e];
+    }
+  }
+}
+
+extern "C" int sm100_decode_block_transpose(const float *src, float *dst, int32_t kind, int32_t dim, int32_t heads,
+                                            int32_t vocab, void *stream) {
+  const int hd = heads > 0 ? dim / heads : 0;
+  const int G = heads > 0 && hd > 0 ? sm100_decode_grid(heads, hd) : 0;
+  if (!src || !dst || kind < 0 || kind > 2 || G <= 0 || dim % 4 || vocab <= 0)
+    return sm100_set_error(SM100_ERR_ARG, "decode_block_transpose: bad arguments (kind %d, dim %d, heads %d)", kind,
+                           dim, heads);
+  block_transpose_kernel<<<G, 256, 0, (cudaStream_t)stream>>>(src, dst, kind, dim, heads, hd, vocab);
+  return launch_status("decode_block_transpose");
 }
 
 typedef CUresult (*DecEncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -1122,9 +1124,8 @@ extern "C" int32_t sm100_decode_grid(int32_t heads, int32_t head_dim) {
   return members_per_head(heads, head_dim, n) * heads;
 }
 
-template <int NK>
 static int launch_decode(const Sm100DecodeModel *dev_model, int n_tokens, int G, size_t smem, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(decode_kernel<NK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: smem attribute: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)G);
@@ -1136,7 +1137,7 @@ static int launch_decode(const Sm100DecodeModel *dev_model, int n_tokens, int G,
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, decode_kernel<NK>, dev_model, n_tokens);
+  e = cudaLaunchKernelEx(&cfg, decode_kernel, dev_model, n_tokens);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "decode: launch: %s", cudaGetErrorString(e));
   return launch_status("decode");
 }
@@ -1166,8 +1167,8 @@ extern "C" int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_t
     const int64_t D = dim, frow = (4 * D + G - 1) / G, orow = (D + M - 1) / M;
     const int64_t hdr = hdr_floats(dim);
     ok = g0.qn <= kMaxRows && g0.qn + 6 <= kBiasFloats && (hdr + g0.qn * D) * 4 <= kStageBytes &&
-         orow * hd * 4 <= kStageBytes && orow <= kCpRows * kWarps && frow <= kMaxRows && frow <= 64 && frow + 6 <= kBiasFloats &&
-         (hdr + frow * D) * 4 <= kStageBytes && g0.R >= 1 &&
+         orow * hd * 4 <= kStageBytes && orow <= kCpRows * kWarps && frow <= kMaxRows && frow + 6 <= kBiasFloats &&
+         (hdr + frow * D) * 4 <= kStageBytes && g0.R >= 1 && g0.R <= kMaxRows &&
          Smem::total(max_transfers(n_layers, vocab, G, dim), max_ctx, hd) <= (size_t)kSmemLimit;
   }
   if (!ok)
@@ -1175,12 +1176,7 @@ extern "C" int sm100_decode_steps(const Sm100DecodeModel *dev_model, int32_t n_t
                            "decode: unsupported shape (tokens %d, layers %d, dim %d, heads %d, vocab %d, ctx %d, %d SMs)",
                            n_tokens, n_layers, dim, heads, vocab, max_ctx, g_num_sms[dev]);
   const size_t smem = Smem::total(max_transfers(n_layers, vocab, G, dim), max_ctx, hd);
-  switch (dim / 128) {
-    case 4: return launch_decode<4>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
-    case 6: return launch_decode<6>(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
-    default:
-      return sm100_set_error(SM100_ERR_ARG, "decode: dim %d not built (512 or 768)", dim);
-  }
+  return launch_decode(dev_model, n_tokens, G, smem, (cudaStream_t)stream);
 }
 
 extern "C" int sm100_decode_step(const Sm100DecodeModel *dev_model, int32_t n_layers, int32_t dim, int32_t heads,

@@ -179,17 +179,25 @@ class Transformer:
         m.max_ctx, m.heads, m.head_dim, m.bump = cfg.max_ctx, cfg.n_heads, cfg.head_dim, 1
         m.eps, m.attn_scale = cfg.norm_eps, float(1.0 / np.sqrt(cfg.head_dim))
         m.wte, m.wpe = p(self.wte), p(self.wpe)
-        m.ln_f_g, m.ln_f_b, m.lm_head = p(self.ln_f.g), p(self.ln_f.b), p(self.lm_head.w)
+        m.ln_f_g, m.ln_f_b = p(self.ln_f.g), p(self.ln_f.b)
+        # row-sliced weights block-transposed for the decode grid (one-time copies)
+        def bt(w, kind: int, rows: int) -> int:
+            out = dev.alloc(4 * rows * cfg.dim)
+            L.check(dev.lib.sm100_decode_block_transpose(p(w), p(out), kind, cfg.dim, cfg.n_heads, cfg.vocab,
+                                                         dev.stream), "decode_block_transpose")
+            self.regrouped.append(out)
+            return p(out)
+        self.regrouped = []
+        m.lm_head_bt = bt(self.lm_head.w, 2, cfg.vocab)
         for i, blk in enumerate(self.h):
             m.ln1_g[i], m.ln1_b[i] = p(blk.ln_1.g), p(blk.ln_1.b)
-            m.w_qkv[i], m.b_qkv[i] = p(blk.attn.c_attn.w), p(blk.attn.c_attn.b)
+            m.w_qkv_bt[i], m.b_qkv[i] = bt(blk.attn.c_attn.w, 0, 3 * cfg.dim), p(blk.attn.c_attn.b)
             m.b_o[i] = p(blk.attn.c_proj.b)
             m.ln2_g[i], m.ln2_b[i] = p(blk.ln_2.g), p(blk.ln_2.b)
-            m.w_fc[i], m.b_fc[i] = p(blk.mlp.c_fc.w), p(blk.mlp.c_fc.b)
+            m.w_fc_bt[i], m.b_fc[i] = bt(blk.mlp.c_fc.w, 1, cfg.hidden), p(blk.mlp.c_fc.b)
             m.b_p2[i] = p(blk.mlp.c_proj.b)
             m.kv_cache[i] = p(blk.attn.cache_kv)
         # the split projections regrouped once: c_proj per head, mlp.c_proj transposed
-        self.regrouped = []
         for i, blk in enumerate(self.h):
             w_o_h, w_p2_t = dev.alloc(4 * cfg.dim * cfg.dim), dev.alloc(4 * cfg.hidden * cfg.dim)
             L.check(dev.lib.sm100_decode_regroup(p(blk.attn.c_proj.w), p(blk.mlp.c_proj.w), p(w_o_h), p(w_p2_t),
