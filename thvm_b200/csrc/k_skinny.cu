@@ -583,30 +583,32 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // reconverge first: the cluster barrier is warp-aligned)
     __syncwarp();
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-    if (rank == 0 && warp >= 2) {
-      const int row = (warp & 3) * 32 + lane, n = cl * kSkBM + row;
+    if (warp >= 2) {
+      // every CTA of the cluster folds a slice of the tile's rows: partial r
+      // of (row, b) from CTA r, added in rank order (deterministic); the S
+      // loads of an element are issued before its adds
+      const int r0 = (rank * kSkBM) / S, nr = ((rank + 1) * kSkBM) / S - r0;
       const int Mv = p.M < MB ? p.M : MB;
-      float acc[MB];
-#pragma unroll
-      for (int b = 0; b < MB; b++) acc[b] = 0.0f;
       const uint32_t local = smem_u32(pbuf);
-      for (int r = 0; r < S; r++) {
-        uint32_t remote;
-        asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(local), "r"(r));
+      uint32_t base[8];
 #pragma unroll
-        for (int b = 0; b < MB; b++) {
-          float x;
-          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(remote + (uint32_t)((b * kSkBM + row) * 4)));
-          acc[b] += x;
-        }
-      }
-      if (n < p.N) {
+      for (int r = 0; r < 8; r++)
+        if (r < S) asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(base[r]) : "r"(local), "r"(r));
+      for (int idx = threadIdx.x - 64; idx < nr * Mv; idx += 128) {
+        const int b = idx / nr, row = r0 + idx % nr, n = cl * kSkBM + row;
+        const uint32_t off = (uint32_t)((b * kSkBM + row) * 4);
+        float x[8];
 #pragma unroll
-        for (int b = 0; b < MB; b++)
-          if (b < Mv) sk_store(p, b, n, acc[b]);
+        for (int r = 0; r < 8; r++)
+          if (r < S) asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[r]) : "r"(base[r] + off));
+        float acc = 0.0f;
+#pragma unroll
+        for (int r = 0; r < 8; r++)
+          if (r < S) acc += x[r];
+        if (n < p.N) sk_store(p, b, n, acc);
       }
     }
-    // the partials stay readable until CTA 0 is done with them
+    // the partials stay readable until every CTA is done with them
     __syncwarp();
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   }

@@ -1,6 +1,6 @@
 """The standalone contraction sweep on the sm_100a device.
 
-    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm|prefill|skinny]
+    python -m thvm_b200.sweep [--iters N] [--only matvec|gemm|prefill|skinny|skinny_ds]
 
 Seeded N(0,1) inputs, fp32 accumulate:
   * decode matvec x[1, 4096] against W (11008 x 4096) in bf16, and in fp8 e4m3
@@ -189,17 +189,23 @@ def prefill_cases(dev: Device, timer: Timer, iters: int):
     return out
 
 
-def skinny_cases(dev: Device, timer: Timer, iters: int):
-    """The GPT-2-XL projections of BASELINE config 3 at batch 16 (bf16 weights
-    streamed once per launch; HBM-bound)."""
+XL_SHAPES = (("c_attn", 4800, 1600), ("attn.c_proj", 1600, 1600), ("c_fc", 6400, 1600),
+             ("mlp.c_proj", 1600, 6400), ("lm_head", 50257, 1600))
+# DeepSeek-V2-Lite-shaped projections of BASELINE config 5 (batch 32)
+DS_SHAPES = (("ds_qkva", 3648, 2048), ("ds_w_o", 2048, 2048), ("ds_router", 64, 2048),
+             ("ds_dense_gu", 21888, 2048), ("ds_dense_down", 2048, 10944), ("ds_lm_head", 102400, 2048))
+
+
+def skinny_cases(dev: Device, timer: Timer, iters: int, M: int = 16, shapes=XL_SHAPES):
+    """Skinny bf16 GEMM launches (bf16 weights streamed once per launch;
+    HBM-bound): the GPT-2-XL projections of BASELINE config 3 at batch 16, or
+    the given shapes at batch M."""
     import ctypes
     lib = dev.lib
     hbm, _, kind = peaks()
     rng = np.random.default_rng(5)
-    M = 16
     out = []
-    for name, N, K in (("c_attn", 4800, 1600), ("attn.c_proj", 1600, 1600), ("c_fc", 6400, 1600),
-                       ("mlp.c_proj", 1600, 6400), ("lm_head", 50257, 1600)):
+    for name, N, K in shapes:
         x = bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
         w = bf16_bits((0.02 * rng.standard_normal((N, K))).astype(np.float32))
         xb, y = dev.upload(x), dev.alloc(M * N * 4)
@@ -229,7 +235,7 @@ def skinny_cases(dev: Device, timer: Timer, iters: int):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--only", choices=["matvec", "gemm", "prefill", "skinny"], default=None)
+    ap.add_argument("--only", choices=["matvec", "gemm", "prefill", "skinny", "skinny_ds"], default=None)
     args = ap.parse_args()
     dev = Device.get()
     timer = Timer(dev)
@@ -240,6 +246,9 @@ def main():
         rows += gemm_cases(dev, timer, args.iters)
     if args.only in (None, "skinny"):
         rows += skinny_cases(dev, timer, args.iters)
+    if args.only in (None, "skinny_ds"):
+        rows += skinny_cases(dev, timer, args.iters, 32, DS_SHAPES)
+        rows += skinny_cases(dev, timer, args.iters, 16, DS_SHAPES[:2])
     if args.only in (None, "prefill"):
         rows += prefill_cases(dev, timer, args.iters)
     for r in rows:
