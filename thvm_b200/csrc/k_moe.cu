@@ -361,29 +361,49 @@ __global__ void __launch_bounds__(kXmThreads, 1)
     // converters: k-block kb of item: A tiles (dequantised rows) and the B tile (token rows)
     const int ct = threadIdx.x;   // 0 .. 255
     int g = 0;                    // k-blocks produced so far (ring position)
-    for (int item = blockIdx.x; item < n_exp * nblk; item += gridDim.x) {
+    const int c16 = ct & 7, h = c16 >> 2, c = (c16 & 3) * 2;
+    // the next item with tokens after `item` (n_exp * nblk: none)
+    auto next_item = [&](int item) {
+      for (item += gridDim.x; item < n_exp * nblk; item += gridDim.x)
+        if (slot_off[item / nblk + 1] > slot_off[item / nblk]) break;
+      return item;
+    };
+    // an item's weight rows are kA contiguous blocks of 128 rows x K fp8
+    auto prefetch_item = [&](int item) {
+      if (ct == 0 && item < n_exp * nblk) {
+        const uint8_t *we = w + (int64_t)(item / nblk) * w_stride;
+        for (int t = 0; t < kA; t++)
+          bulk_prefetch_l2(we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128) * K, (uint32_t)(128 * K));
+      }
+    };
+    // the fp8 codes of k-block kb of an item: 16 per thread per pass of 32 rows
+    auto load_kb = [&](const uint8_t *we, int blk, int kb, uint4 (&raw)[kA][4]) {
+#pragma unroll
+      for (int t = 0; t < kA; t++)
+#pragma unroll
+        for (int pss = 0; pss < 4; pss++)
+          raw[t][pss] = *reinterpret_cast<const uint4 *>(
+              we + (int64_t)((t == 0 ? 0 : I) + blk * 128 + (ct >> 3) + 32 * pss) * K + kb * 128 + c16 * 16);
+    };
+    int item = blockIdx.x;
+    if (item < n_exp * nblk && slot_off[item / nblk + 1] == slot_off[item / nblk]) item = next_item(item);
+    prefetch_item(item);
+    for (; item < n_exp * nblk; item = next_item(item)) {
       const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
-      if (n == 0) continue;
       const uint8_t *we = w + (int64_t)e * w_stride;
       const float *se = sc + (int64_t)e * s_stride;
+      prefetch_item(next_item(item));
+      uint4 raw[kA][4], nxt[kA][4];
+      load_kb(we, blk, 0, raw);
       for (int kb = 0; kb < nkb; kb++, g++) {
         const int s = g & 1;
+        // the next k-block's codes are requested before this one is converted
+        if (kb + 1 < nkb) load_kb(we, blk, kb + 1, nxt);
         if (g >= 2 && !mbar_wait(&empty[s], (uint32_t)(((g >> 1) - 1) & 1), status)) break;
         unsigned char *st = smem + s * kStage;
-        // all of this k-block's loads first (one memory round trip), then convert:
-        // 128 rows x 128 fp8 per tile, 8 lanes per row (16 codes each), 32 rows per pass
-        const int c16 = ct & 7, h = c16 >> 2, c = (c16 & 3) * 2;
-        uint4 raw[kA][4];
         float scl[kA];
 #pragma unroll
-        for (int t = 0; t < kA; t++) {
-          const int row0 = (t == 0 ? 0 : I) + blk * 128;
-          scl[t] = se[(row0 / 128) * sc_cols + kb];
-#pragma unroll
-          for (int pss = 0; pss < 4; pss++)
-            raw[t][pss] = *reinterpret_cast<const uint4 *>(we + (int64_t)(row0 + (ct >> 3) + 32 * pss) * K +
-                                                           kb * 128 + c16 * 16);
-        }
+        for (int t = 0; t < kA; t++) scl[t] = se[(((t == 0 ? 0 : I) + blk * 128) / 128) * sc_cols + kb];
 #pragma unroll
         for (int t = 0; t < kA; t++)
 #pragma unroll
@@ -395,6 +415,10 @@ __global__ void __launch_bounds__(kXmThreads, 1)
             *reinterpret_cast<uint4 *>(dst + ((c ^ (rr & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (rr & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
+#pragma unroll
+        for (int t = 0; t < kA; t++)
+#pragma unroll
+          for (int pss = 0; pss < 4; pss++) raw[t][pss] = nxt[t][pss];
         // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes
         unsigned char *bt = st + kA * kXmTile;
         for (int i = ct; i < 32 * 16; i += kXmConv * 32) {
