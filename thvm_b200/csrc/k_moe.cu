@@ -286,6 +286,7 @@ constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-colum
 constexpr int kXmHalf = kXmTile / 2;
 constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
 constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
+static_assert(kXmConv * 32 == 256, "a converter thread builds two of the token tile's 512 chunks");
 
 template <bool kUp>
 __host__ __device__ constexpr int xm_stage() {
@@ -393,12 +394,32 @@ __global__ void __launch_bounds__(kXmThreads, 1)
       const uint8_t *we = w + (int64_t)e * w_stride;
       const float *se = sc + (int64_t)e * s_stride;
       prefetch_item(next_item(item));
-      uint4 raw[kA][4], nxt[kA][4];
+      // this thread's two token-tile chunks (rows r0 and r0 + 16, the same
+      // for every k-block of the item): their source rows once per item
+      const int r0 = ct >> 4, cc = ct & 15;
+      int64_t src[2];
+#pragma unroll
+      for (int u = 0; u < 2; u++) {
+        const int r = r0 + 16 * u;
+        src[u] = r < n ? (kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r)) : -1;
+      }
+      auto load_x = [&](int kb, uint4 (&xv)[2]) {
+#pragma unroll
+        for (int u = 0; u < 2; u++)
+          xv[u] = src[u] >= 0 ? *reinterpret_cast<const uint4 *>(xin + src[u] * K + kb * 128 + cc * 8)
+                              : make_uint4(0, 0, 0, 0);
+      };
+      uint4 raw[kA][4], nxt[kA][4], xv[2], xn[2];
       load_kb(we, blk, 0, raw);
+      load_x(0, xv);
       for (int kb = 0; kb < nkb; kb++, g++) {
         const int s = g & 1;
-        // the next k-block's codes are requested before this one is converted
-        if (kb + 1 < nkb) load_kb(we, blk, kb + 1, nxt);
+        // the next k-block's codes and token chunks are requested before this
+        // one is converted
+        if (kb + 1 < nkb) {
+          load_kb(we, blk, kb + 1, nxt);
+          load_x(kb + 1, xn);
+        }
         if (g >= 2 && !mbar_wait(&empty[s], (uint32_t)(((g >> 1) - 1) & 1), status)) break;
         unsigned char *st = smem + s * kStage;
         float scl[kA];
@@ -419,16 +440,14 @@ __global__ void __launch_bounds__(kXmThreads, 1)
         for (int t = 0; t < kA; t++)
 #pragma unroll
           for (int pss = 0; pss < 4; pss++) raw[t][pss] = nxt[t][pss];
-        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes
+        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes,
+        // two per thread (rows r0, r0 + 16)
         unsigned char *bt = st + kA * kXmTile;
-        for (int i = ct; i < 32 * 16; i += kXmConv * 32) {
-          const int r = i >> 4, cc = i & 15, h = cc >> 3, c = cc & 7;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          if (r < n) {
-            const int64_t src_row = kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r);
-            v = *reinterpret_cast<const uint4 *>(xin + src_row * K + kb * 128 + cc * 8);
-          }
-          *reinterpret_cast<uint4 *>(bt + h * (kXmB / 2) + r * 128 + ((c ^ (r & 7)) * 16)) = v;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+          const int r = r0 + 16 * u, hh = cc >> 3, c8 = cc & 7;
+          *reinterpret_cast<uint4 *>(bt + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) = xv[u];
+          xv[u] = xn[u];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
