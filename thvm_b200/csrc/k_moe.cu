@@ -287,6 +287,7 @@ constexpr int kXmHalf = kXmTile / 2;
 constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
 constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
 static_assert(kXmConv * 32 == 256, "a converter thread builds two of the token tile's 512 chunks");
+constexpr int kXmAhead = 2;   // k-blocks prefetched into L2 beyond the one in registers
 
 template <bool kUp>
 __host__ __device__ constexpr int xm_stage() {
@@ -369,12 +370,17 @@ __global__ void __launch_bounds__(kXmThreads, 1)
         if (slot_off[item / nblk + 1] > slot_off[item / nblk]) break;
       return item;
     };
-    // an item's weight rows are kA contiguous blocks of 128 rows x K fp8
-    auto prefetch_item = [&](int item) {
-      if (ct == 0 && item < n_exp * nblk) {
+    // k-block kb of an item into L2: the 128-byte segment of each of the
+    // item's rows this thread loads (one lane of the eight that share a row)
+    auto prefetch_kb = [&](int item, int kb) {
+      if (c16 == 0 && item < n_exp * nblk) {
         const uint8_t *we = w + (int64_t)(item / nblk) * w_stride;
+#pragma unroll
         for (int t = 0; t < kA; t++)
-          bulk_prefetch_l2(we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128) * K, (uint32_t)(128 * K));
+#pragma unroll
+          for (int pss = 0; pss < 4; pss++)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(
+                we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128 + (ct >> 3) + 32 * pss) * K + kb * 128));
       }
     };
     // the fp8 codes of k-block kb of an item: 16 per thread per pass of 32 rows
@@ -388,12 +394,12 @@ __global__ void __launch_bounds__(kXmThreads, 1)
     };
     int item = blockIdx.x;
     if (item < n_exp * nblk && slot_off[item / nblk + 1] == slot_off[item / nblk]) item = next_item(item);
-    prefetch_item(item);
+    for (int kb = 1; kb <= kXmAhead && kb < nkb; kb++) prefetch_kb(item, kb);
     for (; item < n_exp * nblk; item = next_item(item)) {
       const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
       const uint8_t *we = w + (int64_t)e * w_stride;
       const float *se = sc + (int64_t)e * s_stride;
-      prefetch_item(next_item(item));
+      const int item2 = next_item(item);
       // this thread's two token-tile chunks (rows r0 and r0 + 16, the same
       // for every k-block of the item): their source rows once per item
       const int r0 = ct >> 4, cc = ct & 15;
@@ -420,6 +426,9 @@ __global__ void __launch_bounds__(kXmThreads, 1)
           load_kb(we, blk, kb + 1, nxt);
           load_x(kb + 1, xn);
         }
+        // kXmAhead + 1 k-blocks ahead into L2 (into the next item near the end)
+        if (kb + kXmAhead + 1 < nkb) prefetch_kb(item, kb + kXmAhead + 1);
+        else if (kb + kXmAhead + 1 - nkb < nkb) prefetch_kb(item2, kb + kXmAhead + 1 - nkb);
         if (g >= 2 && !mbar_wait(&empty[s], (uint32_t)(((g >> 1) - 1) & 1), status)) break;
         unsigned char *st = smem + s * kStage;
         float scl[kA];
