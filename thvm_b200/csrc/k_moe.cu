@@ -112,6 +112,9 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
 // over cache rows 0..pos = (qlat . c_t + q_pe . pe_t) * scale, softmax,
 // olat = sum_t p_t c_t, o = bf16(W_uv[h] olat) (DV).  W_uk / W_uv [H][DN or
 // DV][KV] bf16 (kv_b_proj split, deepseek_v2.py's absorb).
+// Sticky status of the kernels below with bounded waits (a timeout sets it).
+__device__ uint32_t g_ds_status;
+
 constexpr int kDsKV = 512;
 __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk,
                                                       const __nv_bfloat16 *wuv, const __nv_bfloat16 *cc,
@@ -184,6 +187,195 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
   }
 }
 
+// The same attention, one CTA per (head h, group of kMlaNB sequences), for
+// the DeepSeek-V2-Lite shapes (latent 512, rope 64, nope / v <= 128).  The
+// head's absorbed weights are read once per group instead of once per
+// sequence: W_uk[h] comes into shared memory by one bulk copy (issued before
+// the wait for the previous kernel), q_lat of the group's sequences is taken
+// from it, and W_uv[h] is copied into the same buffer while the cache rows
+// are walked.  Each warp walks a stripe of a sequence's rows once (16-byte
+// loads: lane l holds latent columns [8 l, 8 l + 8) and [256 + 8 l, ...),
+// lanes 0-7 the rope columns) with an online softmax, and the warps' (max,
+// sum, partial o_lat) are folded in a fixed order.  The softmax is exp(s -
+// running max) rescaled (expf), the order of the reference's max / exp / sum
+// / divide up to rounding.
+constexpr int kMlaNB = 4, kMlaWarps = 8, kMlaKV = 512, kMlaDR = 64, kMlaMaxD = 128;
+
+struct MlaSmem {
+  static constexpr size_t w = 0;                                              // [128][512] bf16 W_uk[h], then W_uv[h]
+  static constexpr size_t qn = w + kMlaMaxD * kMlaKV * 2;                     // [DN][kMlaNB] f32
+  static constexpr size_t qpe = qn + kMlaMaxD * kMlaNB * 4;                   // [kMlaNB][64] f32
+  static constexpr size_t qlat = qpe + kMlaNB * kMlaDR * 4;                   // [kMlaNB][512] f32 (then o_lat)
+  static constexpr size_t po = qlat + kMlaNB * kMlaKV * 4;                    // [warps][kMlaNB][512] f32
+  static constexpr size_t pm = po + (size_t)kMlaWarps * kMlaNB * kMlaKV * 4;  // [warps][kMlaNB] max
+  static constexpr size_t pl = pm + kMlaWarps * kMlaNB * 4;                   // [warps][kMlaNB] sum
+  static constexpr size_t bar = pl + kMlaWarps * kMlaNB * 4;
+  static constexpr size_t total = bar + 16;
+};
+
+__global__ void __launch_bounds__(kMlaWarps * 32, 1)
+    ds_mla_group_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk, const __nv_bfloat16 *wuv,
+                        const __nv_bfloat16 *cc, const __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o, int B,
+                        int H, int DN, int DV, int ctx, float scale) {
+  extern __shared__ __align__(128) unsigned char sm[];
+  __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(sm + MlaSmem::w);
+  float *qn = reinterpret_cast<float *>(sm + MlaSmem::qn), *qpe = reinterpret_cast<float *>(sm + MlaSmem::qpe);
+  float *qlat = reinterpret_cast<float *>(sm + MlaSmem::qlat), *po = reinterpret_cast<float *>(sm + MlaSmem::po);
+  float *pm = reinterpret_cast<float *>(sm + MlaSmem::pm), *pl = reinterpret_cast<float *>(sm + MlaSmem::pl);
+  uint64_t *bar = reinterpret_cast<uint64_t *>(sm + MlaSmem::bar);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int h = blockIdx.x % H, b0 = (blockIdx.x / H) * kMlaNB, nb = min(kMlaNB, B - b0), QS = DN + kMlaDR;
+  uint32_t *status = &g_ds_status;
+  if (t == 0) {
+    mbar_init(bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (t == 0) {   // the weights are static: their copy overlaps the previous kernel
+    mbar_expect_tx(bar, (uint32_t)(DN * kMlaKV * 2));
+    bulk_g2s(wb, wuk + (int64_t)h * DN * kMlaKV, (uint32_t)(DN * kMlaKV * 2), bar);
+  }
+  pdl_trigger();
+  pdl_wait();
+  const int T = *pos + 1;
+  for (int i = t; i < kMlaNB * QS; i += kMlaWarps * 32) {
+    const int b = i / QS, d = i % QS;
+    const float v = b < nb ? bf(qo[((int64_t)(b0 + b) * H + h) * QS + d]) : 0.0f;
+    if (d < DN) qn[d * kMlaNB + b] = v;
+    else qpe[b * kMlaDR + d - DN] = v;
+  }
+  __syncthreads();
+  const bool wk_ok = mbar_wait(bar, 0, status, false);
+  // q_lat[b][k] = sum_d q_nope[b][d] W_uk[h][d][k], k = t and t + 256
+  {
+    float a[kMlaNB][2] = {};
+    if (wk_ok) {
+#pragma unroll 4
+      for (int d = 0; d < DN; d++) {
+        const float4 q4 = reinterpret_cast<const float4 *>(qn)[d];
+        const float w0 = bf(wb[d * kMlaKV + t]), w1 = bf(wb[d * kMlaKV + t + 256]);
+        const float qq[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+        for (int b = 0; b < kMlaNB; b++) {
+          a[b][0] = fmaf(qq[b], w0, a[b][0]);
+          a[b][1] = fmaf(qq[b], w1, a[b][1]);
+        }
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kMlaNB; b++) {
+      qlat[b * kMlaKV + t] = a[b][0];
+      qlat[b * kMlaKV + t + 256] = a[b][1];
+    }
+  }
+  __syncthreads();
+  if (t == 0) {   // W_uv[h] into the same buffer (every read of W_uk is done)
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    mbar_expect_tx(bar, (uint32_t)(DV * kMlaKV * 2));
+    bulk_g2s(wb, wuv + (int64_t)h * DV * kMlaKV, (uint32_t)(DV * kMlaKV * 2), bar);
+  }
+  // one pass over each sequence's rows: warp w takes rows w, w + 8, ...
+  for (int b = 0; b < nb; b++) {
+    const float *ql = qlat + b * kMlaKV;
+    float qk[16], qp[8], oa[16];
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      qk[j] = ql[8 * lane + j];
+      qk[8 + j] = ql[256 + 8 * lane + j];
+      qp[j] = lane < 8 ? qpe[b * kMlaDR + 8 * lane + j] : 0.0f;
+      oa[j] = oa[8 + j] = 0.0f;
+    }
+    float m = -INFINITY, l = 0.0f;
+    const __nv_bfloat16 *cb = cc + (int64_t)(b0 + b) * ctx * kMlaKV, *pb = cpe + (int64_t)(b0 + b) * ctx * kMlaDR;
+#pragma unroll 2
+    for (int r = warp; r < T; r += kMlaWarps) {
+      const uint4 c0 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 8 * lane);
+      const uint4 c1 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 256 + 8 * lane);
+      const uint4 pe = lane < 8 ? *reinterpret_cast<const uint4 *>(pb + (int64_t)r * kMlaDR + 8 * lane)
+                                : make_uint4(0, 0, 0, 0);
+      const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const uint32_t pw[4] = {pe.x, pe.y, pe.z, pe.w};
+      float cv[16];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        cv[2 * j] = __uint_as_float(cw[j] << 16);
+        cv[2 * j + 1] = __uint_as_float(cw[j] & 0xFFFF0000u);
+      }
+      float sdot = 0.0f;
+#pragma unroll
+      for (int j = 0; j < 16; j++) sdot = fmaf(qk[j], cv[j], sdot);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        sdot = fmaf(qp[2 * j], __uint_as_float(pw[j] << 16), sdot);
+        sdot = fmaf(qp[2 * j + 1], __uint_as_float(pw[j] & 0xFFFF0000u), sdot);
+      }
+      const float sv = warp_sum(sdot) * scale;
+      const float mn = fmaxf(m, sv), cr = expf(m - mn), p = expf(sv - mn);
+      l = l * cr + p;
+#pragma unroll
+      for (int j = 0; j < 16; j++) oa[j] = fmaf(p, cv[j], oa[j] * cr);
+      m = mn;
+    }
+    float *pob = po + ((size_t)warp * kMlaNB + b) * kMlaKV;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      pob[8 * lane + j] = oa[j];
+      pob[256 + 8 * lane + j] = oa[8 + j];
+    }
+    if (lane == 0) {
+      pm[warp * kMlaNB + b] = m;
+      pl[warp * kMlaNB + b] = l;
+    }
+  }
+  __syncthreads();
+  // fold the warps in order: o_lat[b][k] = sum_w e^(m_w - M) o_w[k] / sum_w e^(m_w - M) l_w
+  for (int i = t; i < nb * kMlaKV; i += kMlaWarps * 32) {
+    const int b = i / kMlaKV, k = i % kMlaKV;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kMlaWarps; w++) M = fmaxf(M, pm[w * kMlaNB + b]);
+    float L = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMlaWarps; w++) {
+      const float mw = pm[w * kMlaNB + b], f = mw == -INFINITY ? 0.0f : expf(mw - M);
+      L = fmaf(f, pl[w * kMlaNB + b], L);
+      acc = fmaf(f, po[((size_t)w * kMlaNB + b) * kMlaKV + k], acc);
+    }
+    qlat[b * kMlaKV + k] = acc / L;
+  }
+  __syncthreads();
+  const bool wv_ok = mbar_wait(bar, 1, status, false);
+  // o[b][h][r] = sum_k o_lat[b][k] W_uv[h][r][k]: warp w takes rows w, w + 8,
+  // ..., lane l the columns 2 (l + 32 i) and 2 (l + 32 i) + 1
+  float ov[kMlaNB][16];
+#pragma unroll
+  for (int b = 0; b < kMlaNB; b++)
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      const float2 v = b < nb ? reinterpret_cast<const float2 *>(qlat + b * kMlaKV)[lane + 32 * i] : make_float2(0.f, 0.f);
+      ov[b][2 * i] = v.x;
+      ov[b][2 * i + 1] = v.y;
+    }
+  for (int r = warp; r < DV; r += kMlaWarps) {
+    float acc[kMlaNB] = {};
+    if (wv_ok) {
+#pragma unroll
+      for (int i = 0; i < 8; i++) {
+        const uint32_t w2 = reinterpret_cast<const uint32_t *>(wb + r * kMlaKV)[lane + 32 * i];
+        const float w0 = __uint_as_float(w2 << 16), w1 = __uint_as_float(w2 & 0xFFFF0000u);
+#pragma unroll
+        for (int b = 0; b < kMlaNB; b++) acc[b] = fmaf(ov[b][2 * i + 1], w1, fmaf(ov[b][2 * i], w0, acc[b]));
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < kMlaNB; b++) acc[b] = warp_sum(acc[b]);
+    if (lane < nb) {
+      const float v = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+      o[((int64_t)(b0 + lane) * H + h) * DV + r] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
 // Routing of every token (one CTA, a warp per token): probs = softmax(logits)
 // (max, exp, sum, divide), the K largest probs (ties: lowest expert id), no
 // renormalisation (DeepSeek-V2-Lite: norm_topk_prob false, scaling 1);
@@ -232,30 +424,51 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
     }
   }
   __syncthreads();
-  // expert-major packing: thread e counts its slots, a scan gives the offsets,
-  // then it lists its tokens in order
-  __shared__ int cnt[64];
-  const int ne = e1 - e0;
-  if (threadIdx.x < 64) {
-    int c = 0;
-    if ((int)threadIdx.x < ne)
-      for (int i = 0; i < B * K; i++) c += (s_sel[i] == e0 + (int)threadIdx.x);
-    cnt[threadIdx.x] = c;
+  // expert-major packing in entry order (token-major): entry i = (token i / K,
+  // choice i % K); a warp of entries groups equal experts (match), its lowest
+  // lane records the group's count, the counts' prefix sums give each
+  // (warp, expert) its base and an entry its slot: base + rank in its group
+  __shared__ int wcnt[kDsMaxTok * kDsMaxK / 32][64];
+  __shared__ int eoff[65];
+  const int ne = e1 - e0, n_ent = B * K, nw = (n_ent + 31) / 32;
+  for (int i = threadIdx.x; i < nw * 64; i += blockDim.x) (&wcnt[0][0])[i] = 0;
+  __syncthreads();
+  int ent_e = -1, rank = 0;
+  if (warp < nw) {
+    const int i = warp * 32 + lane;
+    const int ex = i < n_ent ? s_sel[i] - e0 : -1;
+    ent_e = ex >= 0 && ex < ne ? ex : -1;
+    const unsigned mask = __match_any_sync(0xffffffffu, ent_e);
+    rank = __popc(mask & ((1u << lane) - 1u));
+    if (ent_e >= 0 && rank == 0) wcnt[warp][ent_e] = __popc(mask);
   }
   __syncthreads();
-  if (threadIdx.x < 64 && (int)threadIdx.x < ne) {
-    int o = 0;
-    for (int i = 0; i < (int)threadIdx.x; i++) o += cnt[i];
-    slot_off[threadIdx.x] = o;
-    if ((int)threadIdx.x == ne - 1) slot_off[ne] = o + cnt[threadIdx.x];
-    for (int i = 0; i < B * K; i++)
-      if (s_sel[i] == e0 + (int)threadIdx.x) {
-        slot_tok[o] = i / K;
-        slot_w[o] = s_w[i];
-        o++;
-      }
+  if (warp == 0) {   // exclusive scan of the expert totals (64 experts, two per lane)
+    int c0 = 0, c1 = 0;
+    for (int w = 0; w < nw; w++) {
+      c0 += 2 * lane < ne ? wcnt[w][2 * lane] : 0;
+      c1 += 2 * lane + 1 < ne ? wcnt[w][2 * lane + 1] : 0;
+    }
+    int incl = c0 + c1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    const int excl = incl - c0 - c1;
+    eoff[2 * lane] = excl;
+    eoff[2 * lane + 1] = excl + c0;
+    if (lane == 31) eoff[64] = incl;
   }
-  if (ne == 0 && threadIdx.x == 0) slot_off[0] = 0;
+  __syncthreads();
+  if (threadIdx.x <= ne) slot_off[threadIdx.x] = eoff[threadIdx.x];
+  if (ent_e >= 0) {
+    int o = eoff[ent_e] + rank;
+    for (int w = 0; w < warp; w++) o += wcnt[w][ent_e];
+    const int i = warp * 32 + lane;
+    slot_tok[o] = i / K;
+    slot_w[o] = s_w[i];
+  }
   // the shared experts (local ids ne ..) take every token with weight 1
   __syncthreads();
   if (n_shared > 0) {
@@ -280,18 +493,20 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
 //   down: rows r of W_d [D][I]               -> y[tok][r] += w_slot * sum
 // An expert without tokens costs one read of its slot count.  Every wait is
 // bounded; a timeout sets g_ds_status.
-__device__ uint32_t g_ds_status;
 
-constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-column swizzle halves)
+constexpr int kXmTile = 128 * 128 * 2;   // f16 [128 rows][128 k] (two 64-column swizzle halves)
 constexpr int kXmHalf = kXmTile / 2;
-constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
+constexpr int kXmB = 32 * 128 * 2;       // f16 [32 tokens][128 k]
+// The token tiles carry the weight block's scale times 2^6 (kept in f16's
+// normal range for small activations), undone exactly in the epilogue.
+constexpr float kXmPre = 64.0f, kXmPreInv = 1.0f / 64.0f;
 constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
 static_assert(kXmConv * 32 == 256, "a converter thread builds two of the token tile's 512 chunks");
 constexpr int kXmAhead = 2;   // k-blocks prefetched into L2 beyond the one in registers
 
 template <bool kUp>
 __host__ __device__ constexpr int xm_stage() {
-  return (kUp ? 2 : 1) * kXmTile + kXmB;
+  return (kUp ? 2 : 1) * (kXmTile + kXmB);   // per weight tile: its token tile (own scale)
 }
 template <bool kUp>
 __host__ __device__ constexpr int xm_smem() {
@@ -303,8 +518,8 @@ __device__ __forceinline__ uint64_t xm_desc(const void *p) {
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// 16 fp8-e4m3 codes times a scale -> 16 bf16 (8 words); e4m3 -> f16 is exact
-__device__ __forceinline__ void xm_dequant16(const uint4 w, float sc, uint32_t (&o)[8]) {
+// 16 fp8-e4m3 codes -> 16 f16 (8 words), exact (e4m3 is a subset of f16)
+__device__ __forceinline__ void xm_cvt16(const uint4 w, uint32_t (&o)[8]) {
   const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int q = 0; q < 4; q++) {
@@ -312,11 +527,21 @@ __device__ __forceinline__ void xm_dequant16(const uint4 w, float sc, uint32_t (
     for (int hlf = 0; hlf < 2; hlf++) {
       const __half2_raw hr =
           __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu), __NV_E4M3);
-      const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
-      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v.x * sc, v.y * sc);
-      o[2 * q + hlf] = *reinterpret_cast<const uint32_t *>(&b2);
+      o[2 * q + hlf] = (uint32_t)hr.x | ((uint32_t)hr.y << 16);
     }
   }
+}
+
+// 8 bf16 activations times a scale -> 8 f16 (4 words)
+__device__ __forceinline__ uint4 xm_scale8(const uint4 v, float sc) {
+  const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; q++) {
+    const __half2 h2 = __floats2half2_rn(__uint_as_float(vv[q] << 16) * sc, __uint_as_float(vv[q] & 0xFFFF0000u) * sc);
+    o[q] = *reinterpret_cast<const uint32_t *>(&h2);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <bool kUp>
@@ -440,7 +665,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
           for (int pss = 0; pss < 4; pss++) {
             const int rr = (ct >> 3) + 32 * pss;
             uint32_t o[8];
-            xm_dequant16(raw[t][pss], scl[t], o);
+            xm_cvt16(raw[t][pss], o);
             unsigned char *dst = st + t * kXmTile + h * kXmHalf + rr * 128;
             *reinterpret_cast<uint4 *>(dst + ((c ^ (rr & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (rr & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -455,7 +680,10 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int u = 0; u < 2; u++) {
           const int r = r0 + 16 * u, hh = cc >> 3, c8 = cc & 7;
-          *reinterpret_cast<uint4 *>(bt + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) = xv[u];
+#pragma unroll
+          for (int t = 0; t < kA; t++)
+            *reinterpret_cast<uint4 *>(bt + t * kXmB + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) =
+                xm_scale8(xv[u], scl[t] * kXmPre);
           xv[u] = xn[u];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -465,8 +693,8 @@ __global__ void __launch_bounds__(kXmThreads, 1)
     }
   } else if (warp == kXmConv) {
     if (lane == 0) {
-      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(32 >> 3) << 17) |
-                                 ((uint32_t)(128 >> 4) << 24);
+      // f32 accumulate, f16 A and B, N = 32, M = 128
+      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(32 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
       int g = 0, it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_exp * nblk && ok; item += gridDim.x) {
@@ -483,13 +711,13 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; kk++) {
             const int h = kk >> 2, o16 = 2 * (kk & 3);
-            const uint64_t db = xm_desc(bt + h * (kXmB / 2)) + o16;
 #pragma unroll
             for (int t = 0; t < kA; t++)
               asm volatile(
                   "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * 64 + t * 32)),
-                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16), "l"(db), "r"(idesc),
+                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16),
+                  "l"(xm_desc(bt + t * kXmB + h * (kXmB / 2)) + o16), "r"(idesc),
                   "r"((kb > 0 || kk > 0) ? 1u : 0u)
                   : "memory");
           }
@@ -547,7 +775,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          const float gs = __uint_as_float(v0[s]), us = __uint_as_float(v1[s]);
+          const float gs = __uint_as_float(v0[s]) * kXmPreInv, us = __uint_as_float(v1[s]) * kXmPreInv;
           ao[(int64_t)(off + s) * I + r] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
         }
       } else {
@@ -555,7 +783,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * __uint_as_float(v0[s]));
+          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * (__uint_as_float(v0[s]) * kXmPreInv));
         }
       }
       it++;
@@ -626,6 +854,19 @@ extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_u
       KV > kDsKV || ctx > kDsMaxCtx)
     return sm100_set_error(SM100_ERR_ARG, "ds_mla: bad arguments (DN <= 256, DR <= 128, KV <= %d, ctx <= %d)",
                            kDsKV, kDsMaxCtx);
+  if (KV == kMlaKV && DR == kMlaDR && DN <= kMlaMaxD && DV <= kMlaMaxD) {
+    static bool attr = false;
+    if (!attr) {
+      const cudaError_t e = cudaFuncSetAttribute(ds_mla_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 (int)MlaSmem::total);
+      if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_mla: smem attribute: %s", cudaGetErrorString(e));
+      attr = true;
+    }
+    DS_LAUNCH("ds_mla", ds_mla_group_kernel, dim3(H * ((B + kMlaNB - 1) / kMlaNB)), dim3(kMlaWarps * 32),
+              MlaSmem::total, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,
+              (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c, (const __nv_bfloat16 *)cache_pe, pos,
+              (__nv_bfloat16 *)o, B, H, DN, DV, ctx, scale);
+  }
   DS_LAUNCH("ds_mla", ds_mla_kernel, dim3(B * H), dim3(256), 0, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out,
             (const __nv_bfloat16 *)w_uk, (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c,
             (const __nv_bfloat16 *)cache_pe, pos, (__nv_bfloat16 *)o, H, DN, DR, DV, KV, ctx, scale);
