@@ -494,19 +494,16 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
 // An expert without tokens costs one read of its slot count.  Every wait is
 // bounded; a timeout sets g_ds_status.
 
-constexpr int kXmTile = 128 * 128 * 2;   // f16 [128 rows][128 k] (two 64-column swizzle halves)
+constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-column swizzle halves)
 constexpr int kXmHalf = kXmTile / 2;
-constexpr int kXmB = 32 * 128 * 2;       // f16 [32 tokens][128 k]
-// The token tiles carry the weight block's scale times 2^6 (kept in f16's
-// normal range for small activations), undone exactly in the epilogue.
-constexpr float kXmPre = 64.0f, kXmPreInv = 1.0f / 64.0f;
+constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
 constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
 static_assert(kXmConv * 32 == 256, "a converter thread builds two of the token tile's 512 chunks");
 constexpr int kXmAhead = 2;   // k-blocks prefetched into L2 beyond the one in registers
 
 template <bool kUp>
 __host__ __device__ constexpr int xm_stage() {
-  return (kUp ? 2 : 1) * (kXmTile + kXmB);   // per weight tile: its token tile (own scale)
+  return (kUp ? 2 : 1) * kXmTile + kXmB;
 }
 template <bool kUp>
 __host__ __device__ constexpr int xm_smem() {
@@ -518,8 +515,8 @@ __device__ __forceinline__ uint64_t xm_desc(const void *p) {
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// 16 fp8-e4m3 codes -> 16 f16 (8 words), exact (e4m3 is a subset of f16)
-__device__ __forceinline__ void xm_cvt16(const uint4 w, uint32_t (&o)[8]) {
+// 16 fp8-e4m3 codes times a scale -> 16 bf16 (8 words); e4m3 -> f16 is exact
+__device__ __forceinline__ void xm_dequant16(const uint4 w, float sc, uint32_t (&o)[8]) {
   const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
   for (int q = 0; q < 4; q++) {
@@ -527,21 +524,11 @@ __device__ __forceinline__ void xm_cvt16(const uint4 w, uint32_t (&o)[8]) {
     for (int hlf = 0; hlf < 2; hlf++) {
       const __half2_raw hr =
           __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu), __NV_E4M3);
-      o[2 * q + hlf] = (uint32_t)hr.x | ((uint32_t)hr.y << 16);
+      const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
+      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v.x * sc, v.y * sc);
+      o[2 * q + hlf] = *reinterpret_cast<const uint32_t *>(&b2);
     }
   }
-}
-
-// 8 bf16 activations times a scale -> 8 f16 (4 words)
-__device__ __forceinline__ uint4 xm_scale8(const uint4 v, float sc) {
-  const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int q = 0; q < 4; q++) {
-    const __half2 h2 = __floats2half2_rn(__uint_as_float(vv[q] << 16) * sc, __uint_as_float(vv[q] & 0xFFFF0000u) * sc);
-    o[q] = *reinterpret_cast<const uint32_t *>(&h2);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 template <bool kUp>
@@ -665,7 +652,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
           for (int pss = 0; pss < 4; pss++) {
             const int rr = (ct >> 3) + 32 * pss;
             uint32_t o[8];
-            xm_cvt16(raw[t][pss], o);
+            xm_dequant16(raw[t][pss], scl[t], o);
             unsigned char *dst = st + t * kXmTile + h * kXmHalf + rr * 128;
             *reinterpret_cast<uint4 *>(dst + ((c ^ (rr & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (rr & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -680,10 +667,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int u = 0; u < 2; u++) {
           const int r = r0 + 16 * u, hh = cc >> 3, c8 = cc & 7;
-#pragma unroll
-          for (int t = 0; t < kA; t++)
-            *reinterpret_cast<uint4 *>(bt + t * kXmB + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) =
-                xm_scale8(xv[u], scl[t] * kXmPre);
+          *reinterpret_cast<uint4 *>(bt + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) = xv[u];
           xv[u] = xn[u];
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -693,8 +677,8 @@ __global__ void __launch_bounds__(kXmThreads, 1)
     }
   } else if (warp == kXmConv) {
     if (lane == 0) {
-      // f32 accumulate, f16 A and B, N = 32, M = 128
-      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(32 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(32 >> 3) << 17) |
+                                 ((uint32_t)(128 >> 4) << 24);
       int g = 0, it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_exp * nblk && ok; item += gridDim.x) {
@@ -711,13 +695,13 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < 8; kk++) {
             const int h = kk >> 2, o16 = 2 * (kk & 3);
+            const uint64_t db = xm_desc(bt + h * (kXmB / 2)) + o16;
 #pragma unroll
             for (int t = 0; t < kA; t++)
               asm volatile(
                   "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
                   "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * 64 + t * 32)),
-                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16),
-                  "l"(xm_desc(bt + t * kXmB + h * (kXmB / 2)) + o16), "r"(idesc),
+                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16), "l"(db), "r"(idesc),
                   "r"((kb > 0 || kk > 0) ? 1u : 0u)
                   : "memory");
           }
@@ -775,7 +759,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          const float gs = __uint_as_float(v0[s]) * kXmPreInv, us = __uint_as_float(v1[s]) * kXmPreInv;
+          const float gs = __uint_as_float(v0[s]), us = __uint_as_float(v1[s]);
           ao[(int64_t)(off + s) * I + r] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
         }
       } else {
@@ -783,7 +767,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * (__uint_as_float(v0[s]) * kXmPreInv));
+          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * __uint_as_float(v0[s]));
         }
       }
       it++;
