@@ -484,7 +484,7 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
 // The experts on the 5th-generation tensor cores.  A work item is (expert e,
 // block of 128 weight rows); the weights stream from HBM as fp8 and are
 // dequantised (times their 128 x 128 block scale) to bf16 tiles in the MMA's
-// K-major 128-byte swizzle by 8 converter warps, one 128-column k-block at a
+// K-major 128-byte swizzle by 16 converter warps, one 128-column k-block at a
 // time into a 2-stage ring, next to the expert's tokens (up to 32, the MMA's N,
 // rows past the token count zero); one thread issues tcgen05.mma (M=128, N=32,
 // K=16, bf16) into a TMEM accumulator (two sets, so a work item's epilogue
@@ -497,8 +497,12 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
 constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-column swizzle halves)
 constexpr int kXmHalf = kXmTile / 2;
 constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
-constexpr int kXmConv = 8, kXmThreads = (kXmConv + 1 + 4) * 32;
-static_assert(kXmConv * 32 == 256, "a converter thread builds two of the token tile's 512 chunks");
+constexpr int kXmConv = 16, kXmThreads = (kXmConv + 1 + 4) * 32;
+// a converter thread widens 16 codes of a row per pass (8 threads a row);
+// kXmPass passes of kXmConv * 4 rows cover the 128-row tile, and it builds
+// kXmTokC of the token tile's 512 16-byte chunks
+constexpr int kXmRowsPass = kXmConv * 4, kXmPass = 128 / kXmRowsPass, kXmTokC = 512 / (kXmConv * 32);
+static_assert(128 % kXmRowsPass == 0 && 512 % (kXmConv * 32) == 0, "converter split");
 constexpr int kXmAhead = 2;   // k-blocks prefetched into L2 beyond the one in registers
 
 template <bool kUp>
@@ -573,7 +577,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 
   if (warp < kXmConv) {
     // converters: k-block kb of item: A tiles (dequantised rows) and the B tile (token rows)
-    const int ct = threadIdx.x;   // 0 .. 255
+    const int ct = threadIdx.x;   // 0 .. kXmConv * 32 - 1
     int g = 0;                    // k-blocks produced so far (ring position)
     const int c16 = ct & 7, h = c16 >> 2, c = (c16 & 3) * 2;
     // the next item with tokens after `item` (n_exp * nblk: none)
@@ -590,19 +594,19 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int t = 0; t < kA; t++)
 #pragma unroll
-          for (int pss = 0; pss < 4; pss++)
+          for (int pss = 0; pss < kXmPass; pss++)
             asm volatile("prefetch.global.L2 [%0];" ::"l"(
-                we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128 + (ct >> 3) + 32 * pss) * K + kb * 128));
+                we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128 + (ct >> 3) + kXmRowsPass * pss) * K + kb * 128));
       }
     };
-    // the fp8 codes of k-block kb of an item: 16 per thread per pass of 32 rows
-    auto load_kb = [&](const uint8_t *we, int blk, int kb, uint4 (&raw)[kA][4]) {
+    // the fp8 codes of k-block kb of an item: 16 per thread per pass
+    auto load_kb = [&](const uint8_t *we, int blk, int kb, uint4 (&raw)[kA][kXmPass]) {
 #pragma unroll
       for (int t = 0; t < kA; t++)
 #pragma unroll
-        for (int pss = 0; pss < 4; pss++)
+        for (int pss = 0; pss < kXmPass; pss++)
           raw[t][pss] = *reinterpret_cast<const uint4 *>(
-              we + (int64_t)((t == 0 ? 0 : I) + blk * 128 + (ct >> 3) + 32 * pss) * K + kb * 128 + c16 * 16);
+              we + (int64_t)((t == 0 ? 0 : I) + blk * 128 + (ct >> 3) + kXmRowsPass * pss) * K + kb * 128 + c16 * 16);
     };
     int item = blockIdx.x;
     if (item < n_exp * nblk && slot_off[item / nblk + 1] == slot_off[item / nblk]) item = next_item(item);
@@ -612,22 +616,22 @@ __global__ void __launch_bounds__(kXmThreads, 1)
       const uint8_t *we = w + (int64_t)e * w_stride;
       const float *se = sc + (int64_t)e * s_stride;
       const int item2 = next_item(item);
-      // this thread's two token-tile chunks (rows r0 and r0 + 16, the same
+      // this thread's token-tile chunks (rows r0 + 32 u / kXmTokC, the same
       // for every k-block of the item): their source rows once per item
       const int r0 = ct >> 4, cc = ct & 15;
-      int64_t src[2];
+      int64_t src[kXmTokC];
 #pragma unroll
-      for (int u = 0; u < 2; u++) {
-        const int r = r0 + 16 * u;
+      for (int u = 0; u < kXmTokC; u++) {
+        const int r = r0 + (32 / kXmTokC) * u;
         src[u] = r < n ? (kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r)) : -1;
       }
-      auto load_x = [&](int kb, uint4 (&xv)[2]) {
+      auto load_x = [&](int kb, uint4 (&xv)[kXmTokC]) {
 #pragma unroll
-        for (int u = 0; u < 2; u++)
+        for (int u = 0; u < kXmTokC; u++)
           xv[u] = src[u] >= 0 ? *reinterpret_cast<const uint4 *>(xin + src[u] * K + kb * 128 + cc * 8)
                               : make_uint4(0, 0, 0, 0);
       };
-      uint4 raw[kA][4], nxt[kA][4], xv[2], xn[2];
+      uint4 raw[kA][kXmPass], nxt[kA][kXmPass], xv[kXmTokC], xn[kXmTokC];
       load_kb(we, blk, 0, raw);
       load_x(0, xv);
       for (int kb = 0; kb < nkb; kb++, g++) {
@@ -649,8 +653,8 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int t = 0; t < kA; t++)
 #pragma unroll
-          for (int pss = 0; pss < 4; pss++) {
-            const int rr = (ct >> 3) + 32 * pss;
+          for (int pss = 0; pss < kXmPass; pss++) {
+            const int rr = (ct >> 3) + kXmRowsPass * pss;
             uint32_t o[8];
             xm_dequant16(raw[t][pss], scl[t], o);
             unsigned char *dst = st + t * kXmTile + h * kXmHalf + rr * 128;
@@ -660,13 +664,12 @@ __global__ void __launch_bounds__(kXmThreads, 1)
 #pragma unroll
         for (int t = 0; t < kA; t++)
 #pragma unroll
-          for (int pss = 0; pss < 4; pss++) raw[t][pss] = nxt[t][pss];
-        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes,
-        // two per thread (rows r0, r0 + 16)
+          for (int pss = 0; pss < kXmPass; pss++) raw[t][pss] = nxt[t][pss];
+        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes
         unsigned char *bt = st + kA * kXmTile;
 #pragma unroll
-        for (int u = 0; u < 2; u++) {
-          const int r = r0 + 16 * u, hh = cc >> 3, c8 = cc & 7;
+        for (int u = 0; u < kXmTokC; u++) {
+          const int r = r0 + (32 / kXmTokC) * u, hh = cc >> 3, c8 = cc & 7;
           *reinterpret_cast<uint4 *>(bt + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) = xv[u];
           xv[u] = xn[u];
         }
