@@ -298,10 +298,12 @@ constexpr int kGvRows = 32;                       // most rows per stage (KS = 1
 constexpr int kGvThreads = (kGvWarps + 1) * 32;   // + producer warp
 constexpr int kGvSmem = 200 * 1024;               // ring + scales + partials + barriers
 constexpr int kGvMaxStages = 8;
+constexpr int kGvPart = 4 * kGvRows;              // partials of a stage: KS (<= 4) slices x R (<= kGvRows) rows
 
 template <typename WT, int NJ, int KS, int RW>
 __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, int stages, int stage_floats) {
   constexpr int R = kGvWarps / KS * RW;   // rows per stage (RW rows per warp)
+  static_assert(R <= kGvRows && KS * R <= kGvPart, "stage rows / partials");
   extern __shared__ __align__(1024) unsigned char smem[];
   constexpr int V = WVec<WT>::n;
   const int64_t K = p.K;
@@ -311,7 +313,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
   float *ring = reinterpret_cast<float *>(smem);
   float *ss = ring + (size_t)stages * stage_floats;                          // [2][scale_cols]: this CTA's scale rows
   float *part = ss + 2 * (size_t)p.scale_cols;                                // [stages][KS][R] partials
-  int *cnt = reinterpret_cast<int *>(part + (size_t)kGvMaxStages * 2 * kGvWarps);  // [stages][R] slices done
+  int *cnt = reinterpret_cast<int *>(part + (size_t)kGvMaxStages * kGvPart);  // [stages][R] slices done
   uint64_t *full = reinterpret_cast<uint64_t *>(cnt + (size_t)kGvMaxStages * kGvRows);   // [stages]
   uint64_t *empty = full + kGvMaxStages;                                      // [stages]
   if (threadIdx.x == 0) {
@@ -396,7 +398,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
 #pragma unroll
       for (int i = 0; i < RW; i++) acc[i] = warp_sum(acc[i]);
       if (lane == 0) {
-        float *ps = part + (size_t)s * 2 * kGvWarps;
+        float *ps = part + (size_t)s * kGvPart;
 #pragma unroll
         for (int i = 0; i < RW; i++) {
           const int64_t n = nb + i;
@@ -427,9 +429,16 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
 
 // Stages of the streamed matvec for this shape (0: it does not fit), KS
 // (K slices per row: the fewest that keep x within 32 registers a lane) and
+// Rows per warp per stage: fp8 rows are short, so four (two when a row is
+// one slice) per warp per stage.
+template <typename WT>
+__host__ __device__ constexpr int gemv_rw(int ks) {
+  return sizeof(WT) == 1 ? (ks >= 2 ? 4 : 2) : 1;
+}
+
 // NJ, the 16-byte vectors per lane of a slice (K = KS * 32 * NJ * V).
 template <typename WT>
-static int gemv_tma_stages(const LinParams &p, int &stage_floats, int &nj, int &ks, int rw) {
+static int gemv_tma_stages(const LinParams &p, int &stage_floats, int &nj, int &ks) {
   constexpr int V = WVec<WT>::n;
   nj = 0;
   for (ks = 1; ks <= 4; ks *= 2) {
@@ -441,8 +450,8 @@ static int gemv_tma_stages(const LinParams &p, int &stage_floats, int &nj, int &
     }
   }
   if (!nj) return 0;
-  const size_t stage = (size_t)(kGvWarps / ks * rw) * (size_t)p.K * sizeof(WT);
-  const size_t fixed = 2 * (size_t)p.scale_cols * 4 + (size_t)kGvMaxStages * (2 * kGvWarps + kGvRows) * 4 +
+  const size_t stage = (size_t)(kGvWarps / ks * gemv_rw<WT>(ks)) * (size_t)p.K * sizeof(WT);
+  const size_t fixed = 2 * (size_t)p.scale_cols * 4 + (size_t)kGvMaxStages * (kGvPart + kGvRows) * 4 +
                        2 * kGvMaxStages * 8 + 64;
   if (stage % 16 || fixed + 2 * stage > (size_t)kGvSmem) return 0;
   stage_floats = (int)(stage / 4);
@@ -452,7 +461,7 @@ static int gemv_tma_stages(const LinParams &p, int &stage_floats, int &nj, int &
 
 template <typename WT, int NJ, int KS>
 static int launch_gemv_tma_nj(const LinParams &p, int stages, int stage_floats, cudaStream_t st) {
-  constexpr int RW = sizeof(WT) == 1 ? 2 : 1;   // fp8 rows are short: two per warp per stage
+  constexpr int RW = gemv_rw<WT>(KS);   // rows per warp per stage
   constexpr int R = kGvWarps / KS * RW;
   static int num_sms[64];
   int dev = 0;
@@ -555,7 +564,7 @@ static int launch_w(const LinParams &p, cudaStream_t st) {
   // multiple of 32 vectors with an instantiated count
   if (p.M == 1 && vec && !(p.flags & SM100_LIN_LN) && ((reinterpret_cast<uintptr_t>(p.x) & 15) == 0)) {
     int stage_floats = 0, nj = 0, ks = 1;
-    const int stages = gemv_tma_stages<WT>(p, stage_floats, nj, ks, sizeof(WT) == 1 ? 2 : 1);
+    const int stages = gemv_tma_stages<WT>(p, stage_floats, nj, ks);
     if (stages >= 2 && p.N >= 1024) return launch_gemv_tma<WT>(p, stages, stage_floats, nj, ks, st);
     const int nv = p.K * sizeof(float) <= 200 * 1024 ? gemv_nv<WT>(p) : 0;
     if (nv) return launch_gemv<WT>(p, nv, st);
