@@ -470,11 +470,14 @@ int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const vo
 int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared,
                    int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
 /* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
- * experts on the tensor cores (fp8 weights times their block scale
- * dequantised to bf16 tiles, tokens as the MMA's N <= 32): w_gu fp8
- * [n_exp][2I][D] + scales [n_exp][2I/128][D/128], w_d fp8 [n_exp][D][I] +
- * scales [n_exp][D/128][I/128]; D, I multiples of 128; x bf16 [B][D];
- * a_scratch bf16 [slots][I]; y f32 [B][D] (float reductions) */
+ * experts on the tensor cores, fp8 x fp8: the weights stream by TMA as the
+ * MMA's e4m3 operand; each token's row times the 128 x 128 block scale and
+ * a per-token power of two is split into e4m3 hi + lo terms (about 2^-8 of
+ * each value), tokens as the MMA's N <= 32.  w_gu fp8 [n_exp][2I][D] +
+ * scales [n_exp][2I/128][D/128], w_d fp8 [n_exp][D][I] + scales
+ * [n_exp][D/128][I/128]; D, I multiples of 128 up to 4096; x bf16 [B][D];
+ * a_scratch bf16 [slots][I]; y f32 [B][D] (float reductions); w_gu, w_d, x
+ * and a_scratch 16-byte aligned */
 int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,
                      const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch, float *y,
                      int32_t n_exp, int32_t D, int32_t I, void *stream);

@@ -12,6 +12,7 @@
 //
 // Every kernel is launched with programmatic dependent launch and reads its
 // inputs after griddepcontrol.wait.
+#include <cuda.h>
 #include <cuda_fp8.h>
 
 #include <algorithm>
@@ -481,89 +482,141 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
   }
 }
 
-// The experts on the 5th-generation tensor cores.  A work item is (expert e,
-// block of 128 weight rows); the weights stream from HBM as fp8 and are
-// dequantised (times their 128 x 128 block scale) to bf16 tiles in the MMA's
-// K-major 128-byte swizzle by 16 converter warps, one 128-column k-block at a
-// time into a 2-stage ring, next to the expert's tokens (up to 32, the MMA's N,
-// rows past the token count zero); one thread issues tcgen05.mma (M=128, N=32,
-// K=16, bf16) into a TMEM accumulator (two sets, so a work item's epilogue
-// overlaps the next one's products); 4 epilogue warps finish it:
+// The experts on the 5th-generation tensor cores, fp8 in both operands.  A
+// work item is (expert e, block of 128 weight rows).  The weights are the
+// MMA's A operand as stored: fp8-e4m3 tiles of 128 rows x 128 k that TMA
+// copies from HBM into a ring (4 stages up, 8 down) in the 128-byte swizzle,
+// with no conversion.  The tokens (up to 32, the MMA's N; rows past the
+// count zero) become the B operand: for k-block kb of weight row block t,
+// v = x * s[t][kb] * 2^p[t][tok] is split into two e4m3 terms, hi = e4m3(v)
+// and lo = e4m3(v - hi), whose sum carries v to about 2^-8 of |v| (bf16's
+// precision); 2^p[t][tok] is the power of two that puts the token's largest
+// |x| times the row block's largest block scale in [128, 256), so neither
+// term saturates.  8 warps build those tiles; one thread issues tcgen05.mma
+// kind::f8f6f4 (M=128, N=32, K=32) over the hi and lo tiles into one TMEM
+// accumulator (two sets, so an item's epilogue overlaps the next item's
+// products); 4 epilogue warps multiply by 2^-p[t][tok] and finish it:
 //   kUp:  rows j of gate and up (W_gu [2I][D]) -> a[slot][j] = bf16(silu(g) * u)
 //   down: rows r of W_d [D][I]               -> y[tok][r] += w_slot * sum
 // An expert without tokens costs one read of its slot count.  Every wait is
-// bounded; a timeout sets g_ds_status.
+// bounded; a timeout sets g_ds_status, and the TMA thread drains its copies
+// before the CTA exits.
 
-constexpr int kXmTile = 128 * 128 * 2;   // bf16 [128 rows][128 k] (two 64-column swizzle halves)
-constexpr int kXmHalf = kXmTile / 2;
-constexpr int kXmB = 32 * 128 * 2;       // bf16 [32 tokens][128 k]
-constexpr int kXmConv = 16, kXmThreads = (kXmConv + 1 + 4) * 32;
-// a converter thread widens 16 codes of a row per pass (8 threads a row);
-// kXmPass passes of kXmConv * 4 rows cover the 128-row tile, and it builds
-// kXmTokC of the token tile's 512 16-byte chunks
-constexpr int kXmRowsPass = kXmConv * 4, kXmPass = 128 / kXmRowsPass, kXmTokC = 512 / (kXmConv * 32);
-static_assert(128 % kXmRowsPass == 0 && 512 % (kXmConv * 32) == 0, "converter split");
-constexpr int kXmAhead = 2;   // k-blocks prefetched into L2 beyond the one in registers
+constexpr int kX8Prep = 8;                              // token-tile warps
+constexpr int kX8Tma = kX8Prep, kX8Mma = kX8Prep + 1;   // then 4 epilogue warps
+constexpr int kX8Threads = (kX8Prep + 2 + 4) * 32;
+constexpr int kX8A = 128 * 128;   // fp8 [128 rows][128 k]: one 128-byte swizzle row per weight row
+constexpr int kX8B = 32 * 128;    // fp8 [32 tokens][128 k]
+constexpr int kX8MaxKb = 32;      // k-blocks per item (K <= 4096): one block scale per lane
 
 template <bool kUp>
-__host__ __device__ constexpr int xm_stage() {
-  return (kUp ? 2 : 1) * kXmTile + kXmB;
+__host__ __device__ constexpr int x8_stages() {
+  return kUp ? 4 : 8;
+}
+// stage: A tiles [kA], then B tiles [kA][hi, lo]
+template <bool kUp>
+__host__ __device__ constexpr int x8_stage() {
+  return (kUp ? 2 : 1) * (kX8A + 2 * kX8B);
 }
 template <bool kUp>
-__host__ __device__ constexpr int xm_smem() {
-  return 2 * xm_stage<kUp>() + 1024 + 256;
+__host__ __device__ constexpr int x8_smem() {
+  return x8_stages<kUp>() * x8_stage<kUp>() + 1024 /* alignment */ + 1024 /* barriers, scales */;
 }
 
-__device__ __forceinline__ uint64_t xm_desc(const void *p) {
+__device__ __forceinline__ uint64_t x8_desc(const void *p) {
   const uint64_t a = smem_u32(p);
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
-// 16 fp8-e4m3 codes times a scale -> 16 bf16 (8 words); e4m3 -> f16 is exact
-__device__ __forceinline__ void xm_dequant16(const uint4 w, float sc, uint32_t (&o)[8]) {
-  const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+__device__ __forceinline__ void x8_tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// 2^p with m * 2^p in [128, 256) for a positive finite m (clamped to
+// [2^-126, 2^126]); 1 for zero, inf or nan
+__device__ __forceinline__ float x8_pow2(float m) {
+  const int eb = (int)((__float_as_uint(m) >> 23) & 0xFFu);
+  if (!(m > 0.0f) || eb == 0xFF) return 1.0f;
+  return __uint_as_float((uint32_t)min(max(261 - eb, 1), 253) << 23);
+}
+
+// |x| max of 8 bf16
+__device__ __forceinline__ float x8_absmax8(const uint4 v) {
+  float r = 0.0f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int q = 0; q < 4; q++) r = fmaxf(r, fmaxf(fabsf(bf16_lo(w[q])), fabsf(bf16_hi(w[q]))));
+  return r;
+}
+
+// 16 bf16 (a, b) times cf -> e4m3 hi and lo terms (16 bytes each, element
+// order kept: the lower k in the lower byte)
+__device__ __forceinline__ void x8_split16(const uint4 a, const uint4 b, float cf, uint4 &hi, uint4 &lo) {
+  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  uint32_t h[4], l[4];
 #pragma unroll
   for (int q = 0; q < 4; q++) {
+    uint32_t hh = 0, ll = 0;
 #pragma unroll
-    for (int hlf = 0; hlf < 2; hlf++) {
-      const __half2_raw hr =
-          __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)((ww[q] >> (16 * hlf)) & 0xFFFFu), __NV_E4M3);
-      const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
-      const __nv_bfloat162 b2 = __floats2bfloat162_rn(v.x * sc, v.y * sc);
-      o[2 * q + hlf] = *reinterpret_cast<const uint32_t *>(&b2);
+    for (int p = 0; p < 2; p++) {
+      const uint32_t ww = w[2 * q + p];
+      const float v0 = bf16_lo(ww) * cf, v1 = bf16_hi(ww) * cf;
+      const __nv_fp8x2_storage_t h2 = __nv_cvt_float2_to_fp8x2(make_float2(v0, v1), __NV_SATFINITE, __NV_E4M3);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(h2, __NV_E4M3);
+      const float2 hf = __half22float2(*reinterpret_cast<const __half2 *>(&hr));
+      const __nv_fp8x2_storage_t l2 =
+          __nv_cvt_float2_to_fp8x2(make_float2(v0 - hf.x, v1 - hf.y), __NV_SATFINITE, __NV_E4M3);
+      hh |= (uint32_t)h2 << (16 * p);
+      ll |= (uint32_t)l2 << (16 * p);
     }
+    h[q] = hh;
+    l[q] = ll;
   }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 template <bool kUp>
-__global__ void __launch_bounds__(kXmThreads, 1)
-    ds_xmma_kernel(const __nv_bfloat16 *xin, const uint8_t *w, const float *sc, const int32_t *slot_off,
-                   const int32_t *slot_tok, const float *slot_w, void *out, int D, int I, int64_t w_stride,
-                   int64_t s_stride, int n_exp) {
+__global__ void __launch_bounds__(kX8Threads, 1)
+    ds_x8_kernel(const __grid_constant__ CUtensorMap wmap, const __nv_bfloat16 *xin, const float *sc,
+                 const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *out, int D, int I,
+                 int64_t s_stride, int n_exp) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  constexpr int kStage = xm_stage<kUp>(), kA = kUp ? 2 : 1;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kStage);
-  uint64_t *full = bars, *empty = bars + 2, *acc_full = bars + 4, *acc_empty = bars + 6, *done = bars + 8;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 9);
+  constexpr int kS = x8_stages<kUp>(), kStage = x8_stage<kUp>(), kA = kUp ? 2 : 1;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kS * kStage);
+  uint64_t *full_a = bars, *full_b = bars + kS, *empty = bars + 2 * kS, *acc_full = bars + 3 * kS,
+           *acc_empty = acc_full + 2, *sc_full = acc_empty + 2, *done = sc_full + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+  float *sout = reinterpret_cast<float *>(smem + kS * kStage + 512);   // [2 sets][kA][32 tokens]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // rows of the product and its contraction: up: 128-row blocks of I, K = D; down: blocks of D, K = I
   const int rows = kUp ? I : D, K = kUp ? D : I, nblk = rows / 128, nkb = K / 128;
+  const int rows_w = kUp ? 2 * I : D;   // weight rows of one expert in the tensor map
   const int sc_cols = kUp ? D / 128 : (I + 127) / 128;
+  const int n_items = n_exp * nblk;
   uint32_t *status = &g_ds_status;
 
   pdl_trigger();
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 2; i++) {
-      mbar_init(&full[i], kXmConv);
+    for (int i = 0; i < kS; i++) {
+      mbar_init(&full_a[i], 1);
+      mbar_init(&full_b[i], kX8Prep);
       mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
+      mbar_init(&sc_full[i], kX8Prep);
     }
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kXmConv) {   // accumulators: 2 sets x kA x 32 columns
+  if (warp == kX8Mma) {   // accumulators: 2 sets x kA x 32 columns
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(128)
                  : "memory");
@@ -575,139 +628,139 @@ __global__ void __launch_bounds__(kXmThreads, 1)
   const uint32_t tmem = *tmem_slot;
   pdl_wait();
 
-  if (warp < kXmConv) {
-    // converters: k-block kb of item: A tiles (dequantised rows) and the B tile (token rows)
-    const int ct = threadIdx.x;   // 0 .. kXmConv * 32 - 1
-    int g = 0;                    // k-blocks produced so far (ring position)
-    const int c16 = ct & 7, h = c16 >> 2, c = (c16 & 3) * 2;
-    // the next item with tokens after `item` (n_exp * nblk: none)
-    auto next_item = [&](int item) {
-      for (item += gridDim.x; item < n_exp * nblk; item += gridDim.x)
-        if (slot_off[item / nblk + 1] > slot_off[item / nblk]) break;
-      return item;
-    };
-    // k-block kb of an item into L2: the 128-byte segment of each of the
-    // item's rows this thread loads (one lane of the eight that share a row)
-    auto prefetch_kb = [&](int item, int kb) {
-      if (c16 == 0 && item < n_exp * nblk) {
-        const uint8_t *we = w + (int64_t)(item / nblk) * w_stride;
-#pragma unroll
-        for (int t = 0; t < kA; t++)
-#pragma unroll
-          for (int pss = 0; pss < kXmPass; pss++)
-            asm volatile("prefetch.global.L2 [%0];" ::"l"(
-                we + (int64_t)((t == 0 ? 0 : I) + (item % nblk) * 128 + (ct >> 3) + kXmRowsPass * pss) * K + kb * 128));
-      }
-    };
-    // the fp8 codes of k-block kb of an item: 16 per thread per pass
-    auto load_kb = [&](const uint8_t *we, int blk, int kb, uint4 (&raw)[kA][kXmPass]) {
-#pragma unroll
-      for (int t = 0; t < kA; t++)
-#pragma unroll
-        for (int pss = 0; pss < kXmPass; pss++)
-          raw[t][pss] = *reinterpret_cast<const uint4 *>(
-              we + (int64_t)((t == 0 ? 0 : I) + blk * 128 + (ct >> 3) + kXmRowsPass * pss) * K + kb * 128 + c16 * 16);
-    };
-    int item = blockIdx.x;
-    if (item < n_exp * nblk && slot_off[item / nblk + 1] == slot_off[item / nblk]) item = next_item(item);
-    for (int kb = 1; kb <= kXmAhead && kb < nkb; kb++) prefetch_kb(item, kb);
-    for (; item < n_exp * nblk; item = next_item(item)) {
+  if (warp < kX8Prep) {
+    // token tiles: thread (row r, 16-element chunk c) of every k-block
+    const int r = threadIdx.x >> 3, c = threadIdx.x & 7;
+    int g = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
-      const uint8_t *we = w + (int64_t)e * w_stride;
+      if (n == 0) continue;
+      const int a = it & 1;
       const float *se = sc + (int64_t)e * s_stride;
-      const int item2 = next_item(item);
-      // this thread's token-tile chunks (rows r0 + 32 u / kXmTokC, the same
-      // for every k-block of the item): their source rows once per item
-      const int r0 = ct >> 4, cc = ct & 15;
-      int64_t src[kXmTokC];
+      // block scales of the item's row blocks: lane l holds k-block l's
+      float sl[kA], mt[kA];
 #pragma unroll
-      for (int u = 0; u < kXmTokC; u++) {
-        const int r = r0 + (32 / kXmTokC) * u;
-        src[u] = r < n ? (kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r)) : -1;
+      for (int t = 0; t < kA; t++) {
+        sl[t] = lane < nkb ? se[(((t == 0 ? 0 : I) + blk * 128) / 128) * sc_cols + lane] : 0.0f;
+        mt[t] = warp_max(sl[t]);
       }
-      auto load_x = [&](int kb, uint4 (&xv)[kXmTokC]) {
+      const int64_t src = r < n ? (kUp ? (int64_t)slot_tok[off + r] : (int64_t)(off + r)) : -1;
+      const __nv_bfloat16 *xr = xin + (src >= 0 ? src : 0) * K + c * 16;
+      // the token's largest |x| (the 8 threads of a row share it)
+      float am = 0.0f;
+      if (src >= 0) {
+#pragma unroll 4
+        for (int k = 0; k < K; k += 128) {
+          am = fmaxf(am, x8_absmax8(*reinterpret_cast<const uint4 *>(xr + k)));
+          am = fmaxf(am, x8_absmax8(*reinterpret_cast<const uint4 *>(xr + k + 8)));
+        }
+      }
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 4));
+      float inv[kA];
 #pragma unroll
-        for (int u = 0; u < kXmTokC; u++)
-          xv[u] = src[u] >= 0 ? *reinterpret_cast<const uint4 *>(xin + src[u] * K + kb * 128 + cc * 8)
-                              : make_uint4(0, 0, 0, 0);
-      };
-      uint4 raw[kA][kXmPass], nxt[kA][kXmPass], xv[kXmTokC], xn[kXmTokC];
-      load_kb(we, blk, 0, raw);
-      load_x(0, xv);
+      for (int t = 0; t < kA; t++) inv[t] = x8_pow2(am * mt[t]);
+      // the epilogue has read this accumulator set's previous scales
+      if (it >= 2 && !__all_sync(0xffffffffu, mbar_wait(&acc_empty[a], (uint32_t)(((it >> 1) - 1) & 1), status))) {
+        ok = false;
+        break;
+      }
+      if (c == 0)
+#pragma unroll
+        for (int t = 0; t < kA; t++) sout[(a * kA + t) * 32 + r] = 1.0f / inv[t];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sc_full[a]);
+      uint4 x0 = make_uint4(0, 0, 0, 0), x1 = x0, n0 = x0, n1 = x0;
+      if (src >= 0) {
+        x0 = *reinterpret_cast<const uint4 *>(xr);
+        x1 = *reinterpret_cast<const uint4 *>(xr + 8);
+      }
       for (int kb = 0; kb < nkb; kb++, g++) {
-        const int s = g & 1;
-        // the next k-block's codes and token chunks are requested before this
-        // one is converted
-        if (kb + 1 < nkb) {
-          load_kb(we, blk, kb + 1, nxt);
-          load_x(kb + 1, xn);
+        const int s = g % kS;
+        if (src >= 0 && kb + 1 < nkb) {   // the next k-block's chunk is requested before this one is split
+          n0 = *reinterpret_cast<const uint4 *>(xr + (kb + 1) * 128);
+          n1 = *reinterpret_cast<const uint4 *>(xr + (kb + 1) * 128 + 8);
         }
-        // kXmAhead + 1 k-blocks ahead into L2 (into the next item near the end)
-        if (kb + kXmAhead + 1 < nkb) prefetch_kb(item, kb + kXmAhead + 1);
-        else if (kb + kXmAhead + 1 - nkb < nkb) prefetch_kb(item2, kb + kXmAhead + 1 - nkb);
-        if (g >= 2 && !mbar_wait(&empty[s], (uint32_t)(((g >> 1) - 1) & 1), status)) break;
-        unsigned char *st = smem + s * kStage;
-        float scl[kA];
-#pragma unroll
-        for (int t = 0; t < kA; t++) scl[t] = se[(((t == 0 ? 0 : I) + blk * 128) / 128) * sc_cols + kb];
-#pragma unroll
-        for (int t = 0; t < kA; t++)
-#pragma unroll
-          for (int pss = 0; pss < kXmPass; pss++) {
-            const int rr = (ct >> 3) + kXmRowsPass * pss;
-            uint32_t o[8];
-            xm_dequant16(raw[t][pss], scl[t], o);
-            unsigned char *dst = st + t * kXmTile + h * kXmHalf + rr * 128;
-            *reinterpret_cast<uint4 *>(dst + ((c ^ (rr & 7)) * 16)) = make_uint4(o[0], o[1], o[2], o[3]);
-            *reinterpret_cast<uint4 *>(dst + (((c + 1) ^ (rr & 7)) * 16)) = make_uint4(o[4], o[5], o[6], o[7]);
-          }
-#pragma unroll
-        for (int t = 0; t < kA; t++)
-#pragma unroll
-          for (int pss = 0; pss < kXmPass; pss++) raw[t][pss] = nxt[t][pss];
-        // B: 32 token rows x 128 k (rows past n zero): 512 chunks of 16 bytes
-        unsigned char *bt = st + kA * kXmTile;
-#pragma unroll
-        for (int u = 0; u < kXmTokC; u++) {
-          const int r = r0 + (32 / kXmTokC) * u, hh = cc >> 3, c8 = cc & 7;
-          *reinterpret_cast<uint4 *>(bt + hh * (kXmB / 2) + r * 128 + ((c8 ^ (r & 7)) * 16)) = xv[u];
-          xv[u] = xn[u];
+        if (g >= kS && !__all_sync(0xffffffffu, mbar_wait(&empty[s], (uint32_t)(((g / kS) - 1) & 1), status))) {
+          ok = false;
+          break;
         }
+        unsigned char *bt = smem + s * kStage + kA * kX8A;
+        const int o16 = r * 128 + ((c ^ (r & 7)) * 16);
+#pragma unroll
+        for (int t = 0; t < kA; t++) {
+          uint4 hi, lo;
+          x8_split16(x0, x1, __shfl_sync(0xffffffffu, sl[t], kb) * inv[t], hi, lo);
+          *reinterpret_cast<uint4 *>(bt + (2 * t) * kX8B + o16) = hi;
+          *reinterpret_cast<uint4 *>(bt + (2 * t + 1) * kX8B + o16) = lo;
+        }
+        x0 = n0;
+        x1 = n1;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
+        if (lane == 0) mbar_arrive(&full_b[s]);
       }
+      it++;
     }
-  } else if (warp == kXmConv) {
+  } else if (warp == kX8Tma) {
     if (lane == 0) {
-      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(32 >> 3) << 17) |
-                                 ((uint32_t)(128 >> 4) << 24);
+      int g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const int e = item / nblk, blk = item % nblk;
+        if (slot_off[e + 1] == slot_off[e]) continue;
+        for (int kb = 0; kb < nkb; kb++, g++) {
+          const int s = g % kS;
+          if (g >= kS && !mbar_wait(&empty[s], (uint32_t)(((g / kS) - 1) & 1), status)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full_a[s], kA * kX8A);
+#pragma unroll
+          for (int t = 0; t < kA; t++)
+            x8_tma_2d(smem + s * kStage + t * kX8A, &wmap, kb * 128, e * rows_w + (t == 0 ? 0 : I) + blk * 128,
+                      &full_a[s]);
+        }
+      }
+      // the copies of the last use of each stage have landed before the CTA exits
+      for (int j = max(g - kS, 0); j < g; j++) mbar_wait(&full_a[j % kS], (uint32_t)((j / kS) & 1), status, false);
+    }
+  } else if (warp == kX8Mma) {
+    if (lane == 0) {
+      // f32 accumulate, A and B e4m3, K-major, N = 32, M = 128
+      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(32 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
       int g = 0, it = 0;
       bool ok = true;
-      for (int item = blockIdx.x; item < n_exp * nblk && ok; item += gridDim.x) {
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const int e = item / nblk, n = slot_off[e + 1] - slot_off[e];
         if (n == 0) continue;
         const int a = it & 1;
         if (it >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((it >> 1) - 1) & 1), status)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         for (int kb = 0; kb < nkb; kb++, g++) {
-          const int s = g & 1;
-          if (!mbar_wait(&full[s], (uint32_t)((g >> 1) & 1), status)) { ok = false; break; }
-          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const unsigned char *st = smem + s * kStage, *bt = st + kA * kXmTile;
-#pragma unroll
-          for (int kk = 0; kk < 8; kk++) {
-            const int h = kk >> 2, o16 = 2 * (kk & 3);
-            const uint64_t db = xm_desc(bt + h * (kXmB / 2)) + o16;
-#pragma unroll
-            for (int t = 0; t < kA; t++)
-              asm volatile(
-                  "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
-                  "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem + (uint32_t)(a * 64 + t * 32)),
-                  "l"(xm_desc(st + t * kXmTile + h * kXmHalf) + o16), "l"(db), "r"(idesc),
-                  "r"((kb > 0 || kk > 0) ? 1u : 0u)
-                  : "memory");
+          const int s = g % kS;
+          if (!mbar_wait(&full_a[s], (uint32_t)((g / kS) & 1), status) ||
+              !mbar_wait(&full_b[s], (uint32_t)((g / kS) & 1), status)) {
+            ok = false;
+            break;
           }
+          asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+          const unsigned char *st = smem + s * kStage;
+#pragma unroll
+          for (int t = 0; t < kA; t++)
+#pragma unroll
+            for (int hl = 0; hl < 2; hl++)
+#pragma unroll
+              for (int k4 = 0; k4 < 4; k4++)
+                asm volatile(
+                    "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem +
+                                                                                        (uint32_t)(a * 64 + t * 32)),
+                    "l"(x8_desc(st + t * kX8A) + 2 * k4), "l"(x8_desc(st + kA * kX8A + (2 * t + hl) * kX8B) + 2 * k4),
+                    "r"(idesc), "r"((kb > 0 || hl > 0 || k4 > 0) ? 1u : 0u)
+                    : "memory");
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                            smem_u32(&empty[s]))
                        : "memory");
@@ -726,7 +779,7 @@ __global__ void __launch_bounds__(kXmThreads, 1)
     const int q = warp & 3, row = q * 32 + lane;
     const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16);
     int it = 0;
-    for (int item = blockIdx.x; item < n_exp * nblk; item += gridDim.x) {
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
       const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
       if (n == 0) continue;
       const int a = it & 1;
@@ -753,24 +806,32 @@ __global__ void __launch_bounds__(kXmThreads, 1)
               "=r"(v1[29]), "=r"(v1[30]), "=r"(v1[31])
             : "r"(tq + (uint32_t)(a * 64 + 32)));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      // the token scales of this set (written before the set's first k-block)
+      const bool sok = __all_sync(0xffffffffu, mbar_wait(&sc_full[a], (uint32_t)((it >> 1) & 1), status));
+      float f0[32], f1[32];
+#pragma unroll
+      for (int s = 0; s < 32; s++) {
+        f0[s] = __uint_as_float(v0[s]) * sout[(a * kA) * 32 + s];
+        f1[s] = kUp ? __uint_as_float(v1[s]) * sout[(a * kA + 1) * 32 + s] : 0.0f;
+      }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (!sok) break;
       const int r = blk * 128 + row;
       if (kUp) {
         __nv_bfloat16 *ao = reinterpret_cast<__nv_bfloat16 *>(out);
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          const float gs = __uint_as_float(v0[s]), us = __uint_as_float(v1[s]);
-          ao[(int64_t)(off + s) * I + r] = __float2bfloat16_rn(gs / (1.0f + expf(-gs)) * us);
+          ao[(int64_t)(off + s) * I + r] = __float2bfloat16_rn(f0[s] / (1.0f + expf(-f0[s])) * f1[s]);
         }
       } else {
         float *y = reinterpret_cast<float *>(out);
 #pragma unroll
         for (int s = 0; s < 32; s++) {
           if (s >= n) continue;
-          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * __uint_as_float(v0[s]));
+          atomicAdd(y + (int64_t)slot_tok[off + s] * D + r, slot_w[off + s] * f0[s]);
         }
       }
       it++;
@@ -778,12 +839,36 @@ __global__ void __launch_bounds__(kXmThreads, 1)
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == kXmConv) {
+  if (warp == kX8Mma) {
     if (lane == 0) mbar_wait(done, 0, status, false);
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
   }
+}
+
+typedef CUresult (*X8EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                               const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// 2-D map of the fp8 weights of all experts, [rows][K] bytes, box 128 x 128, 128-byte swizzle
+static bool x8_map(CUtensorMap *m, const void *w, int64_t rows, int64_t K) {
+  static X8EncodeFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return false;
+    fn = reinterpret_cast<X8EncodeFn>(p);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K};
+  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(w), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // a = bf16(silu(gu[:, :I]) * gu[:, I:]) for the dense MLP (f32 gate|up rows)
@@ -873,23 +958,37 @@ extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_
                                 const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch,
                                 float *y, int32_t n_exp, int32_t D, int32_t I, void *stream) {
   if (!x || !w_gu || !s_gu || !w_d || !s_d || !slot_off || !slot_tok || !slot_w || !a_scratch || !y || n_exp < 1 ||
-      D % 128 || I % 128 || D < 128 || I < 128)
-    return sm100_set_error(SM100_ERR_ARG, "ds_experts: n_exp %d D %d I %d (D, I multiples of 128)", n_exp, D, I);
+      D % 128 || I % 128 || D < 128 || I < 128 || D > 128 * kX8MaxKb || I > 128 * kX8MaxKb ||
+      ((uintptr_t)w_gu & 15) || ((uintptr_t)w_d & 15) || ((uintptr_t)x & 15) || ((uintptr_t)a_scratch & 15))
+    return sm100_set_error(SM100_ERR_ARG,
+                           "ds_experts: n_exp %d D %d I %d (D, I multiples of 128 up to %d; 16-byte aligned operands)",
+                           n_exp, D, I, 128 * kX8MaxKb);
   const int64_t sc_gu = (int64_t)(2 * I / 128) * (D / 128), sc_d = (int64_t)(D / 128) * (I / 128);
-  constexpr int smem_up = xm_smem<true>(), smem_dn = xm_smem<false>();
-  cudaError_t e = cudaFuncSetAttribute(ds_xmma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(ds_xmma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dn);
-  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: smem attribute: %s", cudaGetErrorString(e));
+  CUtensorMap map_gu, map_d;
+  if (!x8_map(&map_gu, w_gu, (int64_t)n_exp * 2 * I, D) || !x8_map(&map_d, w_d, (int64_t)n_exp * D, I))
+    return sm100_set_error(SM100_ERR_CUDA, "ds_experts: tensor map encoding failed");
+  constexpr int smem_up = x8_smem<true>(), smem_dn = x8_smem<false>();
+  static bool attr[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "ds_experts: device %d", dev);
+  if (!attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(ds_x8_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_up);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(ds_x8_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_dn);
+    if (e != cudaSuccess)
+      return sm100_set_error(SM100_ERR_CUDA, "ds_experts: smem attribute: %s", cudaGetErrorString(e));
+    attr[dev] = true;
+  }
   const int items_up = n_exp * (I / 128), items_dn = n_exp * (D / 128);
-  e = launch_pdl(ds_xmma_kernel<true>, dim3(std::min(items_up, 148)), dim3(kXmThreads), smem_up, (cudaStream_t)stream,
-                 (const __nv_bfloat16 *)x, (const uint8_t *)w_gu, s_gu, slot_off, slot_tok, slot_w, a_scratch, D, I,
-                 (int64_t)2 * I * D, sc_gu, n_exp);
+  cudaError_t e = launch_pdl(ds_x8_kernel<true>, dim3(std::min(items_up, 148)), dim3(kX8Threads), smem_up,
+                             (cudaStream_t)stream, map_gu, (const __nv_bfloat16 *)x, s_gu, slot_off, slot_tok, slot_w,
+                             a_scratch, D, I, sc_gu, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: up: %s", cudaGetErrorString(e));
   launch_status("ds_expert_up");
-  e = launch_pdl(ds_xmma_kernel<false>, dim3(std::min(items_dn, 148)), dim3(kXmThreads), smem_dn, (cudaStream_t)stream,
-                 (const __nv_bfloat16 *)a_scratch, (const uint8_t *)w_d, s_d, slot_off, slot_tok, slot_w, (void *)y, D,
-                 I, (int64_t)D * I, sc_d, n_exp);
+  e = launch_pdl(ds_x8_kernel<false>, dim3(std::min(items_dn, 148)), dim3(kX8Threads), smem_dn, (cudaStream_t)stream,
+                 map_d, (const __nv_bfloat16 *)a_scratch, s_d, slot_off, slot_tok, slot_w, (void *)y, D, I, sc_d,
+                 n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: down: %s", cudaGetErrorString(e));
   return launch_status("ds_expert_down");
 }
