@@ -266,17 +266,21 @@ class DSModel:
             L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, ns, self.sel.data_ptr(),
                                        self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
                                        self.slot_w.data_ptr(), st()), "ds_route")
-            self.moe.zero_()
-            # one launch pair over the local routed experts and shared halves (contiguous in this rank's arrays)
+            # one launch pair over the local routed experts and shared halves (contiguous in this rank's
+            # arrays); on one rank they add into the residual stream itself, on several into a zeroed
+            # buffer that is summed over the ranks and then added
+            y = self.h if sh.world == 1 else self.moe
+            if sh.world > 1:
+                self.moe.zero_()
             L.check(lib.sm100_ds_experts(self.xn.data_ptr(), w[p + "e_gu"].data_ptr(), w[p + "e_gu_s"].data_ptr(),
                                          w[p + "e_d"].data_ptr(), w[p + "e_d_s"].data_ptr(), self.slot_off.data_ptr(),
                                          self.slot_tok.data_ptr(), self.slot_w.data_ptr(), self.a.data_ptr(),
-                                         self.moe.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
+                                         y.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
             self.launches += 3
             if sh.world > 1:
                 self.torch.distributed.all_reduce(self.moe, group=self.group)
-            L.check(lib.sm100_add(self.h.data_ptr(), self.moe.data_ptr(), self.h.data_ptr(), B * D, st()), "add")
-            self.launches += 1
+                L.check(lib.sm100_add(self.h.data_ptr(), self.moe.data_ptr(), self.h.data_ptr(), B * D, st()), "add")
+                self.launches += 1
         self._rms(w["norm_f"], D)
         self._skinny(self.xn, w["lm_head"], self.logits, D, cfg.vocab)
         L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), cfg.vocab, B, cfg.vocab, self.vals.data_ptr(),
