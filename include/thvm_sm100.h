@@ -481,8 +481,10 @@ int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t
 int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,
                      const int32_t *slot_off, const int32_t *slot_tok, const float *slot_w, void *a_scratch, float *y,
                      int32_t n_exp, int32_t D, int32_t I, void *stream);
-/* non-zero when an expert launch since the last call gave up a bounded wait;
- * synchronises the device and clears the word */
+/* non-zero when an expert launch since the last call gave up a bounded wait
+ * (SM100_DECODE_ERR_STALL) or met an expert with more than 32 slots
+ * (SM100_DECODE_ERR_ARG; the MMA's N); synchronises the device and clears
+ * the word */
 uint32_t sm100_ds_status(void);
 /* a (bf16 [M][I]) = silu(gu[:, :I]) * gu[:, I:] of f32 gate|up rows [M][2I] */
 int sm100_ds_silu_mul(const float *gu, void *a, int32_t M, int32_t I, void *stream);

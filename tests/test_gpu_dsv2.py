@@ -93,3 +93,63 @@ def test_ds_route_matches_oracle_rule():
     for k in range(NS):   # the shared experts: every token, weight 1
         np.testing.assert_array_equal(stok.cpu().numpy()[o[E + k]:o[E + k + 1]], np.arange(B))
         assert np.all(sw.cpu().numpy()[o[E + k]:o[E + k + 1]] == 1.0)
+
+
+def _experts_case(B, D, I, slots, seed):
+    """sm100_ds_experts on explicit slot lists against the oracle's fp8 block-scaled linear."""
+    import ctypes
+    import torch
+    from thvm_b200 import _lib as L
+    from thvm_b200.dsv2 import _bf16, _fp8
+    lib = L.lib()
+    rng = np.random.default_rng(seed)
+    E = len(slots)
+    x = _bf16(rng.standard_normal((B, D), dtype=np.float32))
+    w_gu = _fp8(rng.standard_normal((E, 2 * I, D), dtype=np.float32))
+    s_gu = (rng.uniform(0.5, 2.0, (E, 2 * I // 128, D // 128)) * 0.02).astype(np.float32)
+    w_d = _fp8(rng.standard_normal((E, D, I), dtype=np.float32))
+    s_d = (rng.uniform(0.5, 2.0, (E, D // 128, I // 128)) * 0.02).astype(np.float32)
+    off = np.concatenate([[0], np.cumsum([len(s) for s in slots])]).astype(np.int32)
+    tok = np.concatenate([np.asarray(s, np.int32) for s in slots])
+    wts = rng.uniform(0.1, 1.0, int(off[-1])).astype(np.float32)
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    t = {k: dev(v) for k, v in dict(x=x.view(np.int16), w_gu=w_gu, s_gu=s_gu, w_d=w_d, s_d=s_d, off=off, tok=tok,
+                                      w=wts).items()}
+    a = torch.zeros(int(off[-1]), I, dtype=torch.int16, device="cuda")
+    y = torch.zeros(B, D, dtype=torch.float32, device="cuda")
+    L.check(lib.sm100_ds_experts(t["x"].data_ptr(), t["w_gu"].data_ptr(), t["s_gu"].data_ptr(), t["w_d"].data_ptr(),
+                                 t["s_d"].data_ptr(), t["off"].data_ptr(), t["tok"].data_ptr(), t["w"].data_ptr(),
+                                 a.data_ptr(), y.data_ptr(), E, D, I, ctypes.c_void_p(0)), "ds_experts")
+    status = int(lib.sm100_ds_status())
+    xf = O.bf16_to_f32(x)
+    ref = np.zeros((B, D), np.float64)
+    for e in range(E):
+        for j in range(off[e], min(off[e + 1], off[e] + 32)):
+            gu = O.linear_fp8bs(xf[tok[j]][None], w_gu[e], s_gu[e])[0].astype(np.float64)
+            g, u = gu[:I], gu[I:]
+            h = O.bf16_to_f32(_bf16((g / (1.0 + np.exp(-g)) * u).astype(np.float32)))
+            ref[tok[j]] += wts[j] * O.linear_fp8bs(h[None], w_d[e], s_d[e])[0]
+    return y.cpu().numpy(), ref, status
+
+
+def test_ds_experts_match_oracle():
+    """Routed slot lists of 10, 0, 15 and 32 tokens (an empty expert, a full
+    N = 32 tile), D = 384 and I = 256 (3 and 2 k-blocks): the fp8 x fp8
+    products (token rows split into e4m3 hi + lo) within 5e-3 of the largest
+    output of the float64 oracle sum."""
+    rng = np.random.default_rng(3)
+    B = 32
+    slots = [list(range(10)), [], sorted(rng.choice(B, 15, replace=False)), list(range(B))]
+    y, ref, status = _experts_case(B, 384, 256, slots, 4)
+    assert status == 0, status
+    np.testing.assert_allclose(y, ref, rtol=0, atol=5e-3 * np.abs(ref).max())
+
+
+def test_ds_experts_flags_more_than_32_slots():
+    """An expert with 40 slots: the first 32 tokens are served and the status
+    word carries SM100_DECODE_ERR_ARG (the MMA's N is 32)."""
+    from thvm_b200 import _lib as L
+    y, ref, status = _experts_case(40, 256, 128, [list(range(40))], 6)
+    assert status & L.DECODE_ERR_ARG, status
+    np.testing.assert_allclose(y[:32], ref[:32], rtol=0, atol=5e-3 * np.abs(ref).max())
+    assert not np.any(y[32:])

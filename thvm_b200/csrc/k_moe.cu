@@ -636,6 +636,7 @@ __global__ void __launch_bounds__(kX8Threads, 1)
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const int e = item / nblk, blk = item % nblk, off = slot_off[e], n = slot_off[e + 1] - off;
       if (n == 0) continue;
+      if (threadIdx.x == 0 && n > 32) atomicOr(status, SM100_DECODE_ERR_ARG);   // tokens past 32 are not served
       const int a = it & 1;
       const float *se = sc + (int64_t)e * s_stride;
       // block scales of the item's row blocks: lane l holds k-block l's
