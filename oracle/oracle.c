@@ -600,9 +600,129 @@ out:
   if (!logits) free(lg);
 }
 
-/* ---- batched MoE decode step (oracle.h) ------------------------------------ */
+/* ---- DeepSeek-V2 decode stages shared by the two MoE steps below ------------
+ * Each restates one CPU twin of the reference's decode step
+ * (bench/dsv2_decode_bench.c, the plain-C sources its custom kernels carry for
+ * the CPU backend); both orc_ds_ref_step (the reference's batch-1 bf16 step,
+ * pinned to its own output) and orc_ds_step (the batched config-5
+ * composition) call them, so the attention, rotary, cache and routing
+ * arithmetic of the batched step is the pinned one. */
 
 static float bfr_(float v) { return orc_bf16_to_f32(orc_f32_to_bf16(v)); }
+
+/* gred_q (bench/dsv2_decode_bench.c:435-485): the q row [H][DN + DR] as f32
+ * projection outputs -> qb: nope columns rounded to bf16; each rope pair
+ * (2j, 2j + 1) rounded to bf16, rotated by the YaRN table row p into columns
+ * j and DR/2 + j, rounded to bf16. */
+static void ds_q_post(const float *q, float *qb, int64_t H, int64_t DN, int64_t DR, const float *cos_t,
+                      const float *sin_t, int64_t p) {
+  const int64_t QS = DN + DR, half = DR / 2;
+  for (int64_t hh = 0; hh < H; hh++) {
+    for (int64_t d = 0; d < DN; d++) qb[hh * QS + d] = bfr_(q[hh * QS + d]);
+    for (int64_t j = 0; j < half; j++) {
+      const float xe = bfr_(q[hh * QS + DN + 2 * j]), xo = bfr_(q[hh * QS + DN + 2 * j + 1]);
+      const float c = cos_t[p * DR + j], s = sin_t[p * DR + j];
+      qb[hh * QS + DN + j] = bfr_(xe * c - xo * s);
+      qb[hh * QS + DN + half + j] = bfr_(xo * c + xe * s);
+    }
+  }
+}
+
+/* kv_prep (bench/dsv2_decode_bench.c:487-556): kva = [latent KV | rope DR] f32
+ * projection outputs; v = bf16(latent), inv = 1 / sqrt(sum v^2 / KV + eps) (one
+ * f32 sum in index order), cache row = bf16(v * inv * g); the rope pair rotated
+ * as in ds_q_post into the key row. */
+static void ds_kv_post(const float *kva, const float *g, uint16_t *c_row, uint16_t *pe_row, int64_t KV,
+                       int64_t DR, const float *cos_t, const float *sin_t, int64_t p, float eps) {
+  const int64_t half = DR / 2;
+  float ss = 0.0f;
+  for (int64_t t = 0; t < KV; t++) {
+    const float v = bfr_(kva[t]);
+    ss += v * v;
+  }
+  const float inv = 1.0f / sqrtf(ss * (1.0f / (float)KV) + eps);
+  for (int64_t t = 0; t < KV; t++) c_row[t] = orc_f32_to_bf16((bfr_(kva[t]) * inv) * g[t]);
+  for (int64_t j = 0; j < half; j++) {
+    const float xe = bfr_(kva[KV + 2 * j]), xo = bfr_(kva[KV + 2 * j + 1]);
+    const float c = cos_t[p * DR + j], s = sin_t[p * DR + j];
+    pe_row[j] = orc_f32_to_bf16(xe * c - xo * s);
+    pe_row[half + j] = orc_f32_to_bf16(xo * c + xe * s);
+  }
+}
+
+/* One head of the absorbed MLA (mla_qlat / mla_score / mla_mix / mla_o,
+ * bench/dsv2_decode_bench.c:638-785), over the L cache rows c [L][KV] and
+ * pe [L][DR] (bf16): qlat[k] = sum_d q_nope[d] * W_uk[d][k]; score_j =
+ * (sum_k qlat[k] c_j[k] + sum_r q_pe[r] pe_j[r]) * scale (one accumulator);
+ * max (strict >), e_j = expf(score_j - max), sum in j order, p_j = e_j / sum;
+ * olat[k] = sum_j p_j c_j[k]; o[r] = bf16(sum_k olat[k] W_uv[r][k]).  qb holds
+ * the head's bf16-rounded q (DN nope then DR rope values); sm (>= L) gets the
+ * p_j; qlat_out / olat_out (KV each) may be scratch. */
+static void ds_mla_head(const float *qb, const uint16_t *wuk, const uint16_t *wuv, const uint16_t *c,
+                        const uint16_t *pe, int64_t L, int64_t KV, int64_t DN, int64_t DR, int64_t DV, float scale,
+                        float *qlat, float *sm, float *olat, float *o) {
+  for (int64_t k = 0; k < KV; k++) {
+    float acc = 0.0f;
+    for (int64_t d = 0; d < DN; d++) acc += qb[d] * orc_bf16_to_f32(wuk[d * KV + k]);
+    qlat[k] = acc;
+  }
+  float gmax = -1e30f;
+  for (int64_t j = 0; j < L; j++) {
+    float s = 0.0f;
+    for (int64_t k = 0; k < KV; k++) s += qlat[k] * orc_bf16_to_f32(c[j * KV + k]);
+    for (int64_t r = 0; r < DR; r++) s += qb[DN + r] * orc_bf16_to_f32(pe[j * DR + r]);
+    sm[j] = s * scale;
+    if (sm[j] > gmax) gmax = sm[j];
+  }
+  float gsum = 0.0f;
+  for (int64_t j = 0; j < L; j++) {
+    sm[j] = expf(sm[j] - gmax);
+    gsum += sm[j];
+  }
+  for (int64_t j = 0; j < L; j++) sm[j] = sm[j] / gsum;
+  for (int64_t k = 0; k < KV; k++) {
+    float a = 0.0f;
+    for (int64_t j = 0; j < L; j++) a += sm[j] * orc_bf16_to_f32(c[j * KV + k]);
+    olat[k] = a;
+  }
+  for (int64_t r = 0; r < DV; r++) {
+    float acc = 0.0f;
+    for (int64_t k = 0; k < KV; k++) acc += olat[k] * orc_bf16_to_f32(wuv[r * KV + k]);
+    o[r] = bfr_(acc);
+  }
+}
+
+/* route (bench/dsv2_decode_bench.c:787-863): over the E router logits g, mx =
+ * the max (strict > from g[0]), sum = sum_e expf(g[e] - mx) in e order; K
+ * rounds each take the largest remaining LOGIT (strict >, so ties go to the
+ * lowest id) with weight expf(g - mx) / sum (no renormalisation). */
+static void ds_route(const float *g, int64_t E, int64_t K, int32_t *sel, float *probs) {
+  float mx = g[0];
+  for (int64_t e = 1; e < E; e++)
+    if (g[e] > mx) mx = g[e];
+  float sum = 0.0f;
+  for (int64_t e = 0; e < E; e++) sum += expf(g[e] - mx);
+  for (int64_t kk = 0; kk < K; kk++) {
+    int64_t best = -1;
+    float bv = -3.4e38f;
+    for (int64_t e = 0; e < E; e++) {
+      int used = 0;
+      for (int64_t j = 0; j < kk; j++) used |= sel[j] == e;
+      if (!used && g[e] > bv) {
+        bv = g[e];
+        best = e;
+      }
+    }
+    sel[kk] = (int32_t)best;
+    probs[kk] = best >= 0 ? expf(g[best] - mx) / sum : 0.0f;
+  }
+}
+
+void orc_ds_route(const float *g, int64_t B, int64_t E, int64_t K, int32_t *sel, float *probs) {
+  for (int64_t b = 0; b < B; b++) ds_route(g + b * E, E, K, sel + b * K, probs + b * K);
+}
+
+/* ---- batched MoE decode step (oracle.h) ------------------------------------ */
 
 static void rms_bf16(const float *x, const float *g, float *y, int64_t M, int64_t D, float eps) {
   for (int64_t m = 0; m < M; m++) {
@@ -625,7 +745,7 @@ void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const in
                  float *logits, int32_t *next) {
   const int64_t B = m->batch, D = m->dim, H = m->heads, KV = m->kv_lora, DN = m->d_nope, DR = m->d_rope,
                 DV = m->d_v, QS = DN + DR, ctx = m->max_ctx, V = m->vocab, E = m->n_exp, K = m->top_k,
-                I = m->moe_inter, DI = m->dense_inter, NQ = H * QS + KV + DR, half = DR / 2;
+                I = m->moe_inter, DI = m->dense_inter, NQ = H * QS + KV + DR;
   const int64_t big = (2 * DI > NQ ? 2 * DI : NQ) > 2 * I ? (2 * DI > NQ ? 2 * DI : NQ) : 2 * I;
   float *h = (float *)calloc((size_t)(B * D), sizeof(float));
   float *xn = (float *)malloc(sizeof(float) * (size_t)(B * (DI > D ? DI : D)));
@@ -646,63 +766,15 @@ void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const in
     rms_bf16(h, m->attn_norm[l], xn, B, D, m->eps);
     orc_linear_bf16(xn, m->w_qkva[l], y, B, D, NQ);
     for (int64_t b = 0; b < B; b++) {
-      const float *q = y + b * NQ, *kva = y + b * NQ + H * QS;
-      float *qb = qo + b * H * QS;
-      for (int64_t hh = 0; hh < H; hh++) {
-        for (int64_t d = 0; d < DN; d++) qb[hh * QS + d] = bfr_(q[hh * QS + d]);
-        for (int64_t j = 0; j < half; j++) {
-          const float xe = bfr_(q[hh * QS + DN + 2 * j]), xo = bfr_(q[hh * QS + DN + 2 * j + 1]);
-          const float c = m->cos_t[(int64_t)pos * DR + j], s = m->sin_t[(int64_t)pos * DR + j];
-          qb[hh * QS + DN + j] = bfr_(xe * c - xo * s);
-          qb[hh * QS + DN + half + j] = bfr_(xo * c + xe * s);
-        }
-      }
-      float ss = 0.0f;
-      for (int64_t i = 0; i < KV; i++) ss += bfr_(kva[i]) * bfr_(kva[i]);
-      const float inv = 1.0f / sqrtf(ss * (1.0f / (float)KV) + m->eps);
-      for (int64_t i = 0; i < KV; i++)
-        cc[(b * ctx + pos) * KV + i] = orc_f32_to_bf16((bfr_(kva[i]) * inv) * m->kv_norm[l][i]);
-      for (int64_t j = 0; j < half; j++) {
-        const float xe = bfr_(kva[KV + 2 * j]), xo = bfr_(kva[KV + 2 * j + 1]);
-        const float c = m->cos_t[(int64_t)pos * DR + j], s = m->sin_t[(int64_t)pos * DR + j];
-        cp[(b * ctx + pos) * DR + j] = orc_f32_to_bf16(xe * c - xo * s);
-        cp[(b * ctx + pos) * DR + half + j] = orc_f32_to_bf16(xo * c + xe * s);
-      }
+      ds_q_post(y + b * NQ, qo + b * H * QS, H, DN, DR, m->cos_t, m->sin_t, pos);
+      ds_kv_post(y + b * NQ + H * QS, m->kv_norm[l], cc + (b * ctx + pos) * KV, cp + (b * ctx + pos) * DR, KV, DR,
+                 m->cos_t, m->sin_t, pos, m->eps);
     }
     for (int64_t b = 0; b < B; b++)
-      for (int64_t hh = 0; hh < H; hh++) {
-        const float *qb = qo + (b * H + hh) * QS;
-        const uint16_t *wk = m->w_uk[l] + hh * DN * KV, *wv = m->w_uv[l] + hh * DV * KV;
-        for (int64_t k = 0; k < KV; k++) {
-          float a = 0.0f;
-          for (int64_t d = 0; d < DN; d++) a += qb[d] * orc_bf16_to_f32(wk[d * KV + k]);
-          qlat[k] = a;
-        }
-        float mx = -INFINITY;
-        for (int64_t t = 0; t <= pos; t++) {
-          float s = 0.0f;
-          for (int64_t k = 0; k < KV; k++) s += qlat[k] * orc_bf16_to_f32(cc[(b * ctx + t) * KV + k]);
-          for (int64_t r = 0; r < DR; r++) s += qb[DN + r] * orc_bf16_to_f32(cp[(b * ctx + t) * DR + r]);
-          sc[t] = s * m->scale;
-          if (sc[t] > mx) mx = sc[t];
-        }
-        float sum = 0.0f;
-        for (int64_t t = 0; t <= pos; t++) {
-          sc[t] = expf(sc[t] - mx);
-          sum += sc[t];
-        }
-        const float inv = 1.0f / sum;
-        for (int64_t k = 0; k < KV; k++) {
-          float a = 0.0f;
-          for (int64_t t = 0; t <= pos; t++) a += sc[t] * orc_bf16_to_f32(cc[(b * ctx + t) * KV + k]);
-          olat[k] = a * inv;
-        }
-        for (int64_t r = 0; r < DV; r++) {
-          float a = 0.0f;
-          for (int64_t k = 0; k < KV; k++) a += olat[k] * orc_bf16_to_f32(wv[r * KV + k]);
-          o[b * H * DV + hh * DV + r] = bfr_(a);
-        }
-      }
+      for (int64_t hh = 0; hh < H; hh++)
+        ds_mla_head(qo + (b * H + hh) * QS, m->w_uk[l] + hh * DN * KV, m->w_uv[l] + hh * DV * KV,
+                    cc + b * ctx * KV, cp + b * ctx * DR, (int64_t)pos + 1, KV, DN, DR, DV, m->scale, qlat, sc,
+                    olat, o + b * H * DV + hh * DV);
     orc_linear_bf16(o, m->w_o[l], y, B, H * DV, D);
     for (int64_t i = 0; i < B * D; i++) h[i] += y[i];
     rms_bf16(h, m->ffn_norm[l], xn, B, D, m->eps);
@@ -722,25 +794,13 @@ void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const in
     } else {
       orc_linear_bf16(xn, m->router[l], rl, B, D, E);
       for (int64_t b = 0; b < B; b++) {
-        float mx = -INFINITY, sum = 0.0f, pr[64];
-        for (int64_t e = 0; e < E; e++) mx = rl[b * E + e] > mx ? rl[b * E + e] : mx;
-        for (int64_t e = 0; e < E; e++) sum += expf(rl[b * E + e] - mx);
-        for (int64_t e = 0; e < E; e++) pr[e] = expf(rl[b * E + e] - mx) / sum;
-        int used[64] = {0};
+        int32_t sel[64];
+        float pr[64];
+        ds_route(rl + b * E, E, K, sel, pr);
         const int64_t n_all = K + m->n_shared;
         for (int64_t k = 0; k < n_all; k++) {
-          int64_t e;
-          float w;
-          if (k < K) {   /* the largest remaining prob; ties to the lowest id */
-            e = -1;
-            for (int64_t c = 0; c < E; c++)
-              if (!used[c] && (e < 0 || pr[c] > pr[e])) e = c;
-            used[e] = 1;
-            w = pr[e];
-          } else {
-            e = E + (k - K);
-            w = 1.0f;
-          }
+          const int64_t e = k < K ? sel[k] : E + (k - K);
+          const float w = k < K ? pr[k] : 1.0f;
           const int64_t sgu = ((2 * I + 127) / 128) * (D / 128), sd = (D / 128) * ((I + 127) / 128);
           linear_fp8_rows(xn + b * D, m->e_gu[l] + e * 2 * I * D, m->e_gu_s[l] + e * sgu, t1, 1, D, 2 * I);
           for (int64_t j = 0; j < I; j++) av[j] = bfr_(silu_(t1[j]) * t1[I + j]);
@@ -772,4 +832,178 @@ out:
   free(yv);
   free(rl);
   if (!logits) free(lg);
+}
+
+/* ---- the reference's own batch-1 bf16 decode step (oracle.h) ---------------- */
+
+/* gemv_pick_sk (bench/dsv2_decode_bench.c:1043-1048): the K split of a
+ * [K] x [K, N] product. */
+static int64_t ref_pick_sk(int64_t K, int64_t N) {
+  const int64_t gx = (N + 255) / 256;
+  int64_t sk = 1;
+  while (gx * sk < 232 && sk * 64 < K) sk *= 2;
+  return sk;
+}
+
+/* gemv phase 1 + the in-order fold of its partials (src_gemv / src_gred,
+ * bench/dsv2_decode_bench.c:1054-1110): chunk = ceil(K / sk); part_s[n] = f32
+ * sum over k in chunk s of x[k] * w[k][n] (w {in, out}, bf16 or f32); y[n] =
+ * sum_s part_s[n] in s order from 0.  Folds that round (gred's bf16 output)
+ * round y afterwards. */
+static void ref_gemv(const float *x, const void *w, int w_f32, float *y, int64_t K, int64_t N, int64_t sk) {
+  const int64_t chunk = (K + sk - 1) / sk;
+  const uint16_t *wb = (const uint16_t *)w;
+  const float *wf = (const float *)w;
+  for (int64_t n = 0; n < N; n++) {
+    float s = 0.0f;
+    for (int64_t p = 0; p < sk; p++) {
+      const int64_t k0 = p * chunk, k1 = k0 + chunk > K ? K : k0 + chunk;
+      float acc = 0.0f;
+      for (int64_t k = k0; k < k1; k++) acc += x[k] * (w_f32 ? wf[k * N + n] : orc_bf16_to_f32(wb[k * N + n]));
+      s += acc;
+    }
+    y[n] = s;
+  }
+}
+
+/* rms1 / rms_f CPU twins (bench/dsv2_decode_bench.c:397-429): one f32 sum of
+ * squares in index order, inv = 1 / sqrtf(ss * (1/K) + eps), y = x * inv * w
+ * (rounded to bf16 when round_bf16). */
+static void ref_rms(const float *x, const float *w, float *y, int64_t K, float eps, int round_bf16) {
+  float ss = 0.0f;
+  for (int64_t i = 0; i < K; i++) ss += x[i] * x[i];
+  const float inv = 1.0f / sqrtf(ss * (1.0f / (float)K) + eps);
+  for (int64_t i = 0; i < K; i++) {
+    const float v = (x[i] * inv) * w[i];
+    y[i] = round_bf16 ? bfr_(v) : v;
+  }
+}
+
+int32_t orc_ds_ref_step(const OrcDSRef *m, uint16_t *ckv, uint16_t *kpe, int32_t tok, int32_t len, float *logits,
+                        OrcDSRefTrace *tr) {
+  const int64_t D = m->dim, H = m->heads, KV = m->kv_lora, DN = m->d_nope, DR = m->d_rope, DV = m->d_v,
+                QS = DN + DR, ML = m->max_seq, V = m->vocab, E = m->n_exp, K = m->top_k, MI = m->moe_inter,
+                SI = m->moe_inter * m->n_shared, DI = m->dense_inter, NQ = H * QS, NQKV = NQ + KV + DR;
+  const int64_t p = (int64_t)len - 1;
+  const int64_t sk_qkv = ref_pick_sk(D, NQ), sk_o = ref_pick_sk(H * DV, D), sk_gate = ref_pick_sk(D, E),
+                sk_ffw = ref_pick_sk(D, DI), sk_down = ref_pick_sk(DI, D), sk_lm = ref_pick_sk(D, V);
+  int64_t wide = DI > NQKV ? DI : NQKV;
+  wide = wide > D ? wide : D;
+  wide = wide > E ? wide : E;
+  float *x = (float *)malloc(sizeof(float) * (size_t)D), *x1 = (float *)malloc(sizeof(float) * (size_t)D);
+  float *xn = (float *)malloc(sizeof(float) * (size_t)D), *xn2f = (float *)malloc(sizeof(float) * (size_t)D);
+  float *xn2b = (float *)malloc(sizeof(float) * (size_t)D), *y = (float *)malloc(sizeof(float) * (size_t)wide);
+  float *u = (float *)malloc(sizeof(float) * (size_t)wide), *qb = (float *)malloc(sizeof(float) * (size_t)NQ);
+  float *ql = (float *)malloc(sizeof(float) * (size_t)(H * KV)), *ol = (float *)malloc(sizeof(float) * (size_t)(H * KV));
+  float *sm = (float *)calloc((size_t)(H * ML), sizeof(float)), *ob = (float *)malloc(sizeof(float) * (size_t)(H * DV));
+  float *hbuf = (float *)malloc(sizeof(float) * (size_t)(K * MI + SI));
+  float *lg = logits ? logits : (float *)malloc(sizeof(float) * (size_t)V);
+  int32_t next = -1;
+  if (!x || !x1 || !xn || !xn2f || !xn2b || !y || !u || !qb || !ql || !ol || !sm || !ob || !hbuf || !lg) goto out;
+  if (tr && tr->sm) memcpy(sm, tr->sm, sizeof(float) * (size_t)(H * ML));
+  for (int64_t i = 0; i < D; i++) x[i] = orc_bf16_to_f32(m->embed[(int64_t)tok * D + i]);   /* embed_row */
+  for (int32_t l = 0; l < m->n_layers; l++) {
+    uint16_t *cl = ckv + (int64_t)l * ML * KV, *pl = kpe + (int64_t)l * ML * DR;
+    ref_rms(x, m->win[l], xn, D, m->eps, 1);
+    /* q | kv GEMV: the split factor is the q projection's pick (model_init :2228) */
+    ref_gemv(xn, m->wqkv[l], 0, y, D, NQKV, sk_qkv);
+    ds_q_post(y, qb, H, DN, DR, m->cos_t, m->sin_t, p);
+    ds_kv_post(y + NQ, m->wkvn[l], cl + p * KV, pl + p * DR, KV, DR, m->cos_t, m->sin_t, p, m->eps);
+    for (int64_t hh = 0; hh < H; hh++)
+      ds_mla_head(qb + hh * QS, m->wuk[l] + hh * DN * KV, m->wuv[l] + hh * DV * KV, cl, pl, len, KV, DN, DR, DV,
+                  m->scale, ql + hh * KV, sm + hh * ML, ol + hh * KV, ob + hh * DV);
+    /* gemv_o + gred_o_rms (:558-611): x1 = bf16(x + bf16(o W_o)); xn2 = rms(x1) as f32 and bf16 */
+    ref_gemv(ob, m->wo[l], 0, y, H * DV, D, sk_o);
+    for (int64_t i = 0; i < D; i++) x1[i] = bfr_(x[i] + bfr_(y[i]));
+    ref_rms(x1, m->wpost[l], xn2f, D, m->eps, 0);
+    for (int64_t i = 0; i < D; i++) xn2b[i] = bfr_(xn2f[i]);
+    if (l < m->first_dense) {
+      /* gemv_run (gate, up) with bf16 outputs, the scheduler's silu(g) * u
+       * (:2042-2050: x * recip(1 + exp2(x * -log2e)) with bf16 CONSTs: the
+       * constant is -log2e rounded through bf16 storage, -1.4453125
+       * (src/uop/const.c:28), and the CPU backend holds a non-f32 CONST as a
+       * double, so the chain runs in doubles with libm's exp2
+       * (src/backend/cpu/uop_walk.c:354-356, :720-729), rounded once to bf16;
+       * then gemv_sk + gred_down (:613-636) */
+      ref_gemv(xn2b, m->wg1[l], 0, y, D, DI, sk_ffw);
+      ref_gemv(xn2b, m->wu1[l], 0, u, D, DI, sk_ffw);
+      const double c = (double)bfr_(-1.4426950408889634f);
+      for (int64_t j = 0; j < DI; j++) {
+        y[j] = bfr_(y[j]);
+        u[j] = bfr_(u[j]);
+        if (tr && tr->g1o) tr->g1o[j] = orc_f32_to_bf16(y[j]);
+        if (tr && tr->u1o) tr->u1o[j] = orc_f32_to_bf16(u[j]);
+        const double g = (double)y[j];
+        const double sig = 1.0 / (1.0 + exp2(g * c));
+        y[j] = bfr_((float)((g * sig) * (double)u[j]));
+      }
+      float *dn = u;
+      ref_gemv(y, m->wd1[l], 0, dn, DI, D, sk_down);
+      for (int64_t i = 0; i < D; i++) x[i] = bfr_(x1[i] + bfr_(dn[i]));
+    } else {
+      /* gemv_sk(gate) on the f32 xn2 with f32 weights, route, moe_full_h,
+       * moe_full_out (:865-965) */
+      int32_t sel[64];
+      float probs[64];
+      ref_gemv(xn2f, m->gate[l], 1, y, D, E, sk_gate);
+      ds_route(y, E, K, sel, probs);
+      for (int64_t w = 0; w < K * MI + SI; w++) {
+        const uint16_t *wgi, *wui;
+        if (w < K * MI) {
+          const int64_t se = sel[w / MI], i = w % MI;
+          wgi = m->wg[l] + (se * MI + i) * D;
+          wui = m->wu[l] + (se * MI + i) * D;
+        } else {
+          wgi = m->swg[l] + (w - K * MI) * D;
+          wui = m->swu[l] + (w - K * MI) * D;
+        }
+        float g = 0.0f, uu = 0.0f;
+        for (int64_t k = 0; k < D; k++) {
+          g += xn2b[k] * orc_bf16_to_f32(wgi[k]);
+          uu += xn2b[k] * orc_bf16_to_f32(wui[k]);
+        }
+        hbuf[w] = (g / (1.0f + expf(-g))) * uu;
+      }
+      for (int64_t d = 0; d < D; d++) {
+        float acc = 0.0f;
+        for (int64_t e = 0; e < K; e++) {
+          const uint16_t *wde = m->wd[l] + ((int64_t)sel[e] * D + d) * MI;
+          float s = 0.0f;
+          for (int64_t i = 0; i < MI; i++) s += hbuf[e * MI + i] * orc_bf16_to_f32(wde[i]);
+          acc += probs[e] * s;
+        }
+        float s = 0.0f;
+        for (int64_t i = 0; i < SI; i++) s += hbuf[K * MI + i] * orc_bf16_to_f32(m->swd[l][d * SI + i]);
+        acc += s;
+        x[d] = bfr_(x1[d] + bfr_(acc));
+      }
+    }
+  }
+  ref_rms(x, m->norm, xn, D, m->eps, 0);   /* rms_f, f32 out */
+  ref_gemv(xn, m->lm_head, 0, lg, D, V, sk_lm);
+  next = 0;
+  for (int64_t v = 1; v < V; v++)
+    if (lg[v] > lg[next]) next = (int32_t)v;
+  if (tr) {
+    if (tr->ql) memcpy(tr->ql, ql, sizeof(float) * (size_t)(H * KV));
+    if (tr->sm) memcpy(tr->sm, sm, sizeof(float) * (size_t)(H * ML));
+    if (tr->ol) memcpy(tr->ol, ol, sizeof(float) * (size_t)(H * KV));
+    if (tr->ob) orc_f32_to_bf16_n(ob, tr->ob, H * DV);
+  }
+out:
+  free(x);
+  free(x1);
+  free(xn);
+  free(xn2f);
+  free(xn2b);
+  free(y);
+  free(u);
+  free(qb);
+  free(ql);
+  free(ol);
+  free(sm);
+  free(ob);
+  free(hbuf);
+  if (!logits) free(lg);
+  return next;
 }

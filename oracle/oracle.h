@@ -155,10 +155,15 @@ void orc_xl_step(const OrcXL *m, uint16_t *kv, const int32_t *tok, int32_t pos, 
  * bf16(rms(bf16(kva[:KV])) * g_kv); absorbed MLA per head: qlat = W_uk^T q_nope,
  * scores (qlat . c_t + q_pe . pe_t) * scale, softmax, olat = sum p_t c_t,
  * o = bf16(W_uv olat); h += o W_o^T; xn2 = bf16(rms(h) * g2); dense layers:
- * h += bf16(silu(g) * u) W_down^T (bf16 weights); MoE layers: probs =
- * softmax(xn2 W_router^T), top-K (ties: lowest id, no renormalisation), each
- * chosen expert and each shared half (weight 1): h += w * bf16(silu(g) * u)
- * W_d^T with fp8 weights * block scales; logits = bf16(rms(h) * g_f) W_lm^T. */
+ * h += bf16(silu(g) * u) W_down^T (bf16 weights); MoE layers: the router
+ * logits xn2 W_router^T routed by orc_ds_route (top-K logits, softmax weights,
+ * no renormalisation), each chosen expert and each shared half (weight 1):
+ * h += w * bf16(silu(g) * u) W_d^T with fp8 weights * block scales; logits =
+ * bf16(rms(h) * g_f) W_lm^T.  The rotary, cache, attention and routing stages
+ * are the functions orc_ds_ref_step (below) runs, which is pinned bit for bit
+ * to the reference's own step; this step differs from it only in the f32
+ * residual stream, the fp8 block-scaled experts with a bf16 intermediate, the
+ * bf16 router and lm_head inputs and single-accumulator projections. */
 typedef struct {
   int32_t dim, n_layers, heads, kv_lora, d_nope, d_rope, d_v, n_exp, top_k, moe_inter, dense_inter, n_dense,
       n_shared, vocab, max_ctx, batch;
@@ -174,10 +179,54 @@ typedef struct {
   const float **e_gu_s, **e_d_s;          /* block scales as sm100_ds_experts takes them */
 } OrcDS;
 
+/* The routing rule of the reference's route kernel (bench/dsv2_decode_bench.c
+ * :787-863) per row of g [B][E]: the K largest logits (strict >, so ties go to
+ * the lowest id), probs = expf(g - max) / sum_e expf(g_e - max), no
+ * renormalisation.  sel, probs [B][K]. */
+void orc_ds_route(const float *g, int64_t B, int64_t E, int64_t K, int32_t *sel, float *probs);
+
 /* One step: cache_c [L][B][ctx][KV], cache_pe [L][B][ctx][DR] (bf16 bits, row
  * pos written); logits [B][V] (may be NULL); next [B] = row argmax (first index). */
 void orc_ds_step(const OrcDS *m, uint16_t *cache_c, uint16_t *cache_pe, const int32_t *tok, int32_t pos,
                  float *logits, int32_t *next);
+
+/* ---- the reference's own batch-1 bf16 MoE decode step ----------------------
+ * bench/dsv2_decode_bench.c step_build (:2328-2417) with the CPU twins of its
+ * custom kernels, op for op: bf16 residual stream (x1 = bf16(x + bf16(o W_o)),
+ * x = bf16(x1 + bf16(moe))), every M = 1 projection a split-K GEMV whose
+ * partial sums fold in chunk order (gemv_pick_sk), the router on the f32 rms
+ * output with f32 weights, top-K over the router logits, bf16 routed and
+ * shared experts with an f32 intermediate, the dense MLP's silu as the
+ * scheduler evaluates it, the lm_head on the f32 rms output.  Weight layouts
+ * are the DSV2PK01 pack's (bench/dsv2_decode_bench.c:229-300): projections
+ * {in, out}; w_qkv the q | kv row concatenation [D][H*(DN+DR) + KV + DR];
+ * w_uk [H][DN][KV], w_uv [H][DV][KV]; experts wg / wu [E*MI][D], wd
+ * [E*D][MI], swg / swu [SI][D], swd [D][SI] (SI = n_shared * MI). */
+typedef struct {
+  int32_t dim, n_layers, heads, kv_lora, d_nope, d_rope, d_v, n_exp, n_shared, top_k, moe_inter, dense_inter,
+      first_dense, vocab, max_seq;
+  float eps, scale;
+  const uint16_t *embed, *lm_head;        /* [V][D], [D][V] */
+  const float *norm, *cos_t, *sin_t;      /* [D], [max_seq][DR] x 2 */
+  const float **win, **wkvn, **wpost, **gate;   /* [D], [KV], [D], [D][E] */
+  const uint16_t **wqkv, **wuk, **wuv, **wo, **wg1, **wu1, **wd1, **wg, **wu, **wd, **swg, **swu, **swd;
+} OrcDSRef;
+
+/* Optional views of the step's intermediates as the reference keeps them
+ * (its DSV2_DUMP buffers): the last layer's qlat [H*KV] f32, attention
+ * weights [H*max_seq] f32 (read and written in place: rows past len keep
+ * what they held), olat [H*KV] f32 and o [H*DV] bf16, and the last dense
+ * layer's gate / up outputs [DI] bf16.  Any pointer may be NULL. */
+typedef struct {
+  float *ql, *sm, *ol;
+  uint16_t *ob, *g1o, *u1o;
+} OrcDSRefTrace;
+
+/* One decode step of token `tok` with `len` positions (row len - 1 written):
+ * ckv [L][max_seq][KV], kpe [L][max_seq][DR] bf16; logits [V] (may be NULL);
+ * returns the first-index argmax. */
+int32_t orc_ds_ref_step(const OrcDSRef *m, uint16_t *ckv, uint16_t *kpe, int32_t tok, int32_t len, float *logits,
+                        OrcDSRefTrace *tr);
 
 /* threads the oracle's row-parallel loops use (pthreads), for reporting. */
 int orc_num_threads(void);

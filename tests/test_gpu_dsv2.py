@@ -61,8 +61,10 @@ def test_ds_decode_matches_oracle():
 
 
 def test_ds_route_matches_oracle_rule():
-    """The routing kernel alone: softmax, top-K with ties to the lowest id, expert-major slots,
-    then the shared experts' slots."""
+    """The routing kernel alone against the oracle's orc_ds_route (the reference's rule: top-K of
+    the logits with ties to the lowest id, softmax weights): an exact tie, two distinct logits
+    with equal f32 probabilities (the larger logit wins), expert-major slots, then the shared
+    experts' slots."""
     import ctypes
     import torch
     from thvm_b200 import _lib as L
@@ -71,6 +73,9 @@ def test_ds_route_matches_oracle_rule():
     rng = np.random.default_rng(2)
     logits = rng.standard_normal((B, E)).astype(np.float32)
     logits[0, 5] = logits[0, 9] = logits[0].max() + 1.0   # a tie: 5 before 9
+    logits[1] = -20.0                                        # equal probabilities, distinct logits
+    logits[1, 0], logits[1, 1:5] = 6.0, 5.0
+    logits[1, 7], logits[1, 40] = -2.0, np.nextafter(np.float32(-2.0), np.float32(0.0))
     d = lambda a: torch.from_numpy(a).cuda()
     lg = d(logits)
     sel, wsel = torch.zeros(B * K, dtype=torch.int32, device="cuda"), torch.zeros(B * K, device="cuda")
@@ -80,11 +85,10 @@ def test_ds_route_matches_oracle_rule():
     L.check(lib.sm100_ds_route(lg.data_ptr(), E, K, B, 0, E, NS, sel.data_ptr(), wsel.data_ptr(), off.data_ptr(),
                                stok.data_ptr(), sw.data_ptr(), ctypes.c_void_p(0)), "ds_route")
     torch.cuda.synchronize()
-    p = np.exp(logits - logits.max(1, keepdims=True))
-    p /= p.sum(1, keepdims=True)
-    ref = np.argsort(-p, axis=1, kind="stable")[:, :K]   # stable: ties keep the lower id first
+    ref, ref_w = O.ds_route(logits, K)
+    assert ref[0, 0] == 5 and ref[1, 5] == 40   # a top-K of probabilities would take 7
     np.testing.assert_array_equal(sel.cpu().numpy().reshape(B, K), ref)
-    np.testing.assert_allclose(wsel.cpu().numpy().reshape(B, K), np.take_along_axis(p, ref, 1), rtol=1e-5)
+    np.testing.assert_allclose(wsel.cpu().numpy().reshape(B, K), ref_w, rtol=1e-5)
     o = off.cpu().numpy()
     assert o[0] == 0 and o[E] == B * K and o[-1] == B * (K + NS) and np.all(np.diff(o) >= 0)
     for e in range(E):
@@ -117,6 +121,8 @@ def _experts_case(B, D, I, slots, seed):
                                       w=wts).items()}
     a = torch.zeros(int(off[-1]), I, dtype=torch.int16, device="cuda")
     y = torch.zeros(B, D, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    lib.sm100_ds_status()   # reading clears the sticky word: start from this call's own status
     L.check(lib.sm100_ds_experts(t["x"].data_ptr(), t["w_gu"].data_ptr(), t["s_gu"].data_ptr(), t["w_d"].data_ptr(),
                                  t["s_d"].data_ptr(), t["off"].data_ptr(), t["tok"].data_ptr(), t["w"].data_ptr(),
                                  a.data_ptr(), y.data_ptr(), E, D, I, ctypes.c_void_p(0)), "ds_experts")

@@ -5,6 +5,7 @@ import numpy as np
 import pytest
 
 import oracle as O
+from conftest import GOLDEN
 
 
 @pytest.mark.parametrize("name", ["lin_a", "lin_b", "lin_c"])
@@ -125,3 +126,89 @@ def test_lowp_linears_are_the_f32_loop_on_widened_weights():
     assert np.array_equal(O.linear_fp8bs(x, w8, sc), O.linear(x, wide))
     a = O.to_bf16(rng.standard_normal((7, K)).astype(np.float32))
     assert np.array_equal(O.gemm_bf16(a, wb), O.linear(O.bf16_to_f32(a), O.bf16_to_f32(wb)))
+
+
+# ---- DeepSeek-V2 decode ---------------------------------
+
+def _bytesum(a):
+    """The DSV2_DUMP fingerprint of a buffer: sum of byte[i] * (1 + (i & 7))."""
+    b = np.frombuffer(np.ascontiguousarray(a).tobytes(), np.uint8).astype(np.uint64)
+    return int((b * (1 + (np.arange(b.size) & 7)).astype(np.uint64)).sum())
+
+
+@pytest.fixture(scope="module")
+def golden_dsv2():
+    g = dict(np.load(GOLDEN / "dsv2.npz"))
+    cfg = O.DSREF_SMALL
+    assert {k[4:]: int(v) for k, v in g.items() if k.startswith("cfg_")} == {k: int(v) for k, v in cfg.env().items()}
+    return g, cfg
+
+
+def test_ds_ref_step_is_the_reference_step_bit_for_bit(golden_dsv2):
+    """orc_ds_ref_step against the reference's own decode bench run on the same
+    pack (tests/golden/make_dsv2_golden.py): after the first step every
+    DSV2_DUMP fingerprint (the last layer's qlat, attention weights, olat and o,
+    the dense layer's gate / up outputs, each layer's cache row 0, the logits'
+    bit sum) is identical; then the 8-id prompt fed token by token and 23
+    greedy steps give the same 24 ids and the same printed top-2 logits."""
+    g, cfg = golden_dsv2
+    m = O.DSRef(cfg, O.ds_ref_weights(cfg, seed=int(g["seed"])))
+    prompt = [int(t) for t in g["prompt"]]
+    lg, nxt = m.step(prompt[0], 1)
+    tr = m.trace
+    mine = {"T_ql": tr["ql"], "T_sm": tr["sm"], "T_ol": tr["ol"], "T_ob": tr["ob"], "T_g1o": tr["g1o"],
+            "T_u1o": tr["u1o"]}
+    for name, want in zip(g["dump_names"], g["dump_sums"]):
+        assert _bytesum(mine[str(name)]) == int(want), name
+    assert [int(m.ckv[l, 0].astype(np.uint64).sum()) for l in range(cfg.n_layers)] == g["dump_ckv"].tolist()
+    assert [int(m.kpe[l, 0].astype(np.uint64).sum()) for l in range(cfg.n_layers)] == g["dump_kpe"].tolist()
+    assert int(lg.view(np.uint32).astype(np.uint64).sum()) == int(g["dump_logits_bitsum"])
+    for i in range(1, len(prompt)):
+        lg, nxt = m.step(prompt[i], i + 1)
+    gen = [nxt]
+    for i in range(1, len(g["gen_ids"])):
+        lg, nxt = m.step(gen[-1], len(prompt) + i)
+        gen.append(nxt)
+        top = np.argsort(-lg, kind="stable")[:2]
+        assert top.tolist() == g["top2_ids"][i - 1].tolist(), i
+        assert [f"{float(lg[t]):.6f}" for t in top] == g["top2_txt"][i - 1].tolist(), i
+    assert gen == g["gen_ids"].tolist()
+
+
+def test_ds_batched_step_agrees_with_the_pinned_step():
+    """The batched config-5 oracle (orc_ds_step: f32 residual, fp8 block-scaled
+    experts, bf16 router) on the same model as the pinned reference step
+    (expert weights chosen fp8-exact): per step logits within the north star's
+    2e-2 of the row's largest, and the same greedy id at every step, over 8
+    prompt positions and 24 greedy steps at batch 1."""
+    cfg = O.DSREF_SMALL
+    rw = O.ds_ref_weights(cfg, seed=3, fp8_experts=True)
+    c5, w5 = O.ds_from_ref(cfg, rw)
+    cos, sin = O.ds_rope_tables(cfg.d_rope, cfg.max_seq)
+    mine, ref = O.DSModel(c5, w5, cos, sin), O.DSRef(cfg, rw)
+    seq = np.random.default_rng(5).integers(0, cfg.vocab, 8).tolist()
+    tok, worst = seq[0], 0.0
+    for pos in range(32):
+        lr, nr = ref.step(tok, pos + 1)
+        lm, nm = mine.step(np.array([tok], np.int32), pos)
+        worst = max(worst, float(np.abs(lm[0] - lr).max() / np.abs(lr).max()))
+        assert int(nm[0]) == nr, pos
+        tok = seq[pos + 1] if pos + 1 < len(seq) else nr
+    assert worst <= 2e-2, worst
+
+
+def test_ds_route_takes_top_k_of_logits():
+    """The reference's routing rule: top-K over the router logits with ties to
+    the lowest id, weights exp(l - max) / sum.  Two distinct logits whose
+    probabilities are equal in f32 (both 8.0 below the max) resolve to the
+    larger logit, where a top-K over probabilities would take the lower id."""
+    g = np.full((2, 8), -20.0, np.float32)
+    g[:, 0] = 6.0
+    g[:, 1:5] = 5.0
+    g[0, 5], g[0, 6] = -2.0, np.nextafter(np.float32(-2.0), np.float32(0.0))
+    g[1, 5] = g[1, 6] = -2.0                         # an exact tie: the lower id
+    sel, pr = O.ds_route(g, 6)
+    assert sel[0].tolist() == [0, 1, 2, 3, 4, 6] and sel[1].tolist() == [0, 1, 2, 3, 4, 5]
+    p = np.exp(g[0] - 6.0, dtype=np.float32)
+    assert np.float32(g[0, 5] - 6.0) == np.float32(g[0, 6] - 6.0)   # equal probabilities
+    np.testing.assert_allclose(pr[0], p[[0, 1, 2, 3, 4, 6]] / p.sum(), rtol=1e-6)

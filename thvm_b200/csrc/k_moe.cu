@@ -377,9 +377,11 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   }
 }
 
-// Routing of every token (one CTA, a warp per token): probs = softmax(logits)
-// (max, exp, sum, divide), the K largest probs (ties: lowest expert id), no
-// renormalisation (DeepSeek-V2-Lite: norm_topk_prob false, scaling 1);
+// Routing of every token (one CTA, a warp per token), the rule of the
+// reference's route kernel (bench/dsv2_decode_bench.c:787-863): the K largest
+// router LOGITS (ties: lowest expert id), each weighted by its softmax
+// probability exp(l - max) / sum (no renormalisation; DeepSeek-V2-Lite:
+// norm_topk_prob false, scaling 1);
 // then per-expert lists of (token, weight) for the experts [e0, e1) this
 // rank holds, packed expert-major: slot_tok / slot_w / slot_off[e] offsets,
 // followed by n_shared shared experts that take every token with weight 1.
@@ -399,12 +401,15 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
     float sum = 0.0f;
     for (int e = lane; e < E; e += 32) sum += expf(lg[e] - m);
     sum = warp_sum(sum);
-    // greedy top-K over E <= 64 probabilities held two per lane
-    float p0 = lane < E ? expf(lg[lane] - m) / sum : -1.0f;
-    float p1 = lane + 32 < E ? expf(lg[lane + 32] - m) / sum : -1.0f;
+    // greedy top-K over E <= 64 logits held two per lane (a taken or absent
+    // expert is out of the contest); a lane offers its larger logit, the
+    // lower id on a tie, and the warp keeps the larger, the lower id on a tie
+    const float l0 = lane < E ? lg[lane] : 0.0f, l1 = lane + 32 < E ? lg[lane + 32] : 0.0f;
+    bool live0 = lane < E, live1 = lane + 32 < E;
     for (int k = 0; k < K; k++) {
-      float bv = p0 >= p1 ? p0 : p1;
-      int bi = p0 >= p1 ? lane : lane + 32;
+      const bool take0 = live0 && (!live1 || l0 >= l1);
+      float bv = take0 ? l0 : live1 ? l1 : -INFINITY;
+      int bi = take0 ? lane : live1 ? lane + 32 : 0x7FFFFFFF;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -414,14 +419,15 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
           bi = oi;
         }
       }
+      const float w = expf(bv - m) / sum;
       if (lane == 0) {
         s_sel[b * K + k] = bi;
-        s_w[b * K + k] = bv;
+        s_w[b * K + k] = w;
         sel[b * K + k] = bi;
-        wsel[b * K + k] = bv;
+        wsel[b * K + k] = w;
       }
-      if (bi == lane) p0 = -2.0f;
-      if (bi == lane + 32) p1 = -2.0f;
+      if (bi == lane) live0 = false;
+      if (bi == lane + 32) live1 = false;
     }
   }
   __syncthreads();
@@ -986,7 +992,8 @@ extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_
                              (cudaStream_t)stream, map_gu, (const __nv_bfloat16 *)x, s_gu, slot_off, slot_tok, slot_w,
                              a_scratch, D, I, sc_gu, n_exp);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_experts: up: %s", cudaGetErrorString(e));
-  launch_status("ds_expert_up");
+  const int rc = launch_status("ds_expert_up");
+  if (rc != SM100_OK) return rc;
   e = launch_pdl(ds_x8_kernel<false>, dim3(std::min(items_dn, 148)), dim3(kX8Threads), smem_dn, (cudaStream_t)stream,
                  map_d, (const __nv_bfloat16 *)a_scratch, s_d, slot_off, slot_tok, slot_w, (void *)y, D, I, sc_d,
                  n_exp);
