@@ -270,7 +270,7 @@ class _OrcXL(ctypes.Structure):
         (n, ctypes.c_void_p) for n in ("wte", "wpe", "lm_head", "ln_f_w", "ln_f_b")] + [
         (n, ctypes.POINTER(ctypes.c_void_p)) for n in (
             "ln_1_w", "ln_1_b", "ln_2_w", "ln_2_b", "c_attn_w", "c_proj_w", "c_fc_w", "mlp_proj_w",
-            "c_attn_b", "c_proj_b", "c_fc_b", "mlp_proj_b")]
+            "c_attn_b", "c_proj_b", "c_fc_b", "mlp_proj_b")] + [("exact", ctypes.c_int32)]
 
 
 class XLModel:
@@ -281,12 +281,14 @@ class XLModel:
                   "c_attn_w": "attn.w", "c_proj_w": "proj.w", "c_fc_w": "fc.w", "mlp_proj_w": "p2.w",
                   "c_attn_b": "attn.b", "c_proj_b": "proj.b", "c_fc_b": "fc.b", "mlp_proj_b": "p2.b"}
 
-    def __init__(self, cfg, weights: dict):
+    def __init__(self, cfg, weights: dict, exact: bool = False):
+        """exact: no bf16 rounding of activations or cache rows (an f32 cache):
+        the pinned f32 GPT-2 forward on the bf16-valued weights."""
         self.cfg = cfg
         self._keep = {k: np.ascontiguousarray(v) for k, v in weights.items()}
         w = self._keep
         s = _OrcXL(n_layers=cfg.n_layers, dim=cfg.dim, heads=cfg.heads, vocab=cfg.vocab, max_ctx=cfg.max_ctx,
-                   batch=cfg.batch, norm_eps=cfg.norm_eps)
+                   batch=cfg.batch, norm_eps=cfg.norm_eps, exact=int(exact))
         s.wte, s.wpe, s.lm_head = w["wte"].ctypes.data, w["wpe"].ctypes.data, w["lm_head"].ctypes.data
         s.ln_f_w, s.ln_f_b = w["ln_f.w"].ctypes.data, w["ln_f.b"].ctypes.data
         self._arrays = []
@@ -295,7 +297,7 @@ class XLModel:
             self._arrays.append(arr)
             setattr(s, field, ctypes.cast(arr, ctypes.POINTER(ctypes.c_void_p)))
         self._s = s
-        self.kv = np.zeros((cfg.n_layers, 2, cfg.batch, cfg.max_ctx, cfg.dim), np.uint16)
+        self.kv = np.zeros((cfg.n_layers, 2, cfg.batch, cfg.max_ctx, cfg.dim), np.float32 if exact else np.uint16)
         L = lib()
         if not getattr(L, "_xl_bound", False):
             L.orc_xl_step.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,

@@ -520,83 +520,87 @@ static void add_bias_rows(float *y, const float *b, int64_t M, int64_t N) {
     for (int64_t n = 0; n < N; n++) y[m * N + n] += b[n];
 }
 
-void orc_xl_step(const OrcXL *m, uint16_t *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next) {
+void orc_xl_step(const OrcXL *m, void *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next) {
   const int64_t B = m->batch, D = m->dim, H = m->heads, hd = D / H, F = 4 * D, V = m->vocab, ctx = m->max_ctx;
+  const int exact = m->exact != 0;
+  /* activations stored as bf16 by the device round here; `exact` keeps f32 */
+#define XL_ROUND(ptr, n) \
+  do {                                 \
+    if (!exact) round_bf16_inplace((ptr), (n)); \
+  } while (0)
   float *h = (float *)calloc((size_t)(B * D), sizeof(float));
   float *x = (float *)malloc(sizeof(float) * (size_t)(B * F));
   float *y = (float *)malloc(sizeof(float) * (size_t)(B * (F > 3 * D ? F : 3 * D)));
   float *lg = logits ? logits : (float *)malloc(sizeof(float) * (size_t)(B * V));
   float *e = (float *)malloc(sizeof(float) * (size_t)ctx);
-  if (!h || !x || !y || !lg || !e) goto out;
+  float *kr = (float *)malloc(sizeof(float) * (size_t)(ctx * hd)), *vr = (float *)malloc(sizeof(float) * (size_t)(ctx * hd));
+  if (!h || !x || !y || !lg || !e || !kr || !vr) goto out;
   for (int64_t b = 0; b < B; b++)
     for (int64_t d = 0; d < D; d++) {
       const float t = (tok[b] >= 0 && tok[b] < V) ? orc_bf16_to_f32(m->wte[(int64_t)tok[b] * D + d]) : 0.0f;
       h[b * D + d] = t + orc_bf16_to_f32(m->wpe[(int64_t)pos * D + d]);
     }
+  const float scale = (float)(1.0 / sqrt((double)hd));
   for (int32_t l = 0; l < m->n_layers; l++) {
-    uint16_t *kc = kv + (int64_t)l * 2 * B * ctx * D, *vc = kc + B * ctx * D;
+    const int64_t lo = (int64_t)l * 2 * B * ctx * D, vo = lo + B * ctx * D;
+    uint16_t *kc = (uint16_t *)kv + lo, *vc = (uint16_t *)kv + vo;
+    float *kcf = (float *)kv + lo, *vcf = (float *)kv + vo;
     /* attention block */
     orc_layernorm_f32(h, m->ln_1_w[l], m->ln_1_b[l], x, B, D, m->norm_eps);
-    round_bf16_inplace(x, B * D);
+    XL_ROUND(x, B * D);
     orc_linear_bf16(x, m->c_attn_w[l], y, B, D, 3 * D);
     add_bias_rows(y, m->c_attn_b[l], B, 3 * D);
     for (int64_t b = 0; b < B; b++)
       for (int64_t d = 0; d < D; d++) {
-        kc[(b * ctx + pos) * D + d] = orc_f32_to_bf16(y[b * 3 * D + D + d]);
-        vc[(b * ctx + pos) * D + d] = orc_f32_to_bf16(y[b * 3 * D + 2 * D + d]);
+        const int64_t at = (b * ctx + pos) * D + d;
+        if (exact) {
+          kcf[at] = y[b * 3 * D + D + d];
+          vcf[at] = y[b * 3 * D + 2 * D + d];
+        } else {
+          kc[at] = orc_f32_to_bf16(y[b * 3 * D + D + d]);
+          vc[at] = orc_f32_to_bf16(y[b * 3 * D + 2 * D + d]);
+        }
       }
-    const float scale = (float)(1.0 / sqrt((double)hd));
+    /* the reference's attention row (the GPT-2 forward's attn_row: (q . k) *
+     * scale, softmax, mix) over the cached rows 0..pos */
     for (int64_t b = 0; b < B; b++)
       for (int64_t hh = 0; hh < H; hh++) {
-        const float *q = y + b * 3 * D + hh * hd;
-        float mx = -INFINITY;
-        for (int64_t j = 0; j <= pos; j++) {
-          const uint16_t *kr = kc + (b * ctx + j) * D + hh * hd;
-          float s = 0.0f;
-          for (int64_t d = 0; d < hd; d++) s += (q[d] * scale) * orc_bf16_to_f32(kr[d]);
-          e[j] = s;
-          if (s > mx) mx = s;
-        }
-        float sum = 0.0f;
-        for (int64_t j = 0; j <= pos; j++) {
-          e[j] = expf(e[j] - mx);
-          sum += e[j];
-        }
-        const float inv = 1.0f / sum;
-        for (int64_t d = 0; d < hd; d++) {
-          float acc = 0.0f;
-          for (int64_t j = 0; j <= pos; j++) acc += e[j] * orc_bf16_to_f32(vc[(b * ctx + j) * D + hh * hd + d]);
-          x[b * D + hh * hd + d] = orc_bf16_to_f32(orc_f32_to_bf16(acc * inv));
-        }
+        for (int64_t j = 0; j <= pos; j++)
+          for (int64_t d = 0; d < hd; d++) {
+            const int64_t at = (b * ctx + j) * D + hh * hd + d;
+            kr[j * hd + d] = exact ? kcf[at] : orc_bf16_to_f32(kc[at]);
+            vr[j * hd + d] = exact ? vcf[at] : orc_bf16_to_f32(vc[at]);
+          }
+        attn_row(y + b * 3 * D + hh * hd, kr, vr, hd, NULL, (int64_t)pos + 1, e, x + b * D + hh * hd,
+                 (int64_t)pos + 1, hd, scale);
       }
+    XL_ROUND(x, B * D);
     orc_linear_bf16(x, m->c_proj_w[l], y, B, D, D);
     add_bias_rows(y, m->c_proj_b[l], B, D);
     for (int64_t i = 0; i < B * D; i++) h[i] += y[i];
     /* MLP block */
     orc_layernorm_f32(h, m->ln_2_w[l], m->ln_2_b[l], x, B, D, m->norm_eps);
-    round_bf16_inplace(x, B * D);
+    XL_ROUND(x, B * D);
     orc_linear_bf16(x, m->c_fc_w[l], y, B, D, F);
     add_bias_rows(y, m->c_fc_b[l], B, F);
     orc_gelu_f32(y, x, B * F);
-    round_bf16_inplace(x, B * F);
+    XL_ROUND(x, B * F);
     orc_linear_bf16(x, m->mlp_proj_w[l], y, B, F, D);
     add_bias_rows(y, m->mlp_proj_b[l], B, D);
     for (int64_t i = 0; i < B * D; i++) h[i] += y[i];
   }
   orc_layernorm_f32(h, m->ln_f_w, m->ln_f_b, x, B, D, m->norm_eps);
-  round_bf16_inplace(x, B * D);
+  XL_ROUND(x, B * D);
+#undef XL_ROUND
   orc_linear_bf16(x, m->lm_head, lg, B, D, V);
-  for (int64_t b = 0; b < B; b++) {
-    int64_t bi = 0;
-    for (int64_t v = 1; v < V; v++)
-      if (lg[b * V + v] > lg[b * V + bi]) bi = v;
-    next[b] = (int32_t)bi;
-  }
+  for (int64_t b = 0; b < B; b++) orc_argmax_f32(lg + b * V, next + b, 1, V);
 out:
   free(h);
   free(x);
   free(y);
   free(e);
+  free(kr);
+  free(vr);
   if (!logits) free(lg);
 }
 

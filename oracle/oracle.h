@@ -125,12 +125,15 @@ int orc_gpt2_generate(const OrcGPT2 *m, const int32_t *prompt, int32_t n_prompt,
                       int32_t n_new, int32_t *out);
 
 /* ---- batched bf16 GPT-2-XL-shaped decode step ----------
- * The model of bench/gpt2/thvm_gpt2.py:27-128 with bf16 weights: the residual
- * stream h is f32; each Linear's input (LayerNorm output, attention output,
- * GELU output) is rounded to bf16 and multiplied by the bf16 weight with an
- * f32 sum in k order, + f32 bias; k and v enter the cache as bf16; scores
- * (q * scale) . k in f32, softmax max / exp / sum, out = (sum_j e_j v_j) / sum
- * rounded to bf16.  Embedding tables bf16.  Weight matrices (out, in). */
+ * The model of bench/gpt2/thvm_gpt2.py:27-128 with bf16 weights, computed
+ * with the GPT-2 forward's own operations (orc_gpt2_forward: LayerNorm, the
+ * Linear loop, the attention row (q . k) * scale -> softmax -> mix, GELU,
+ * argmax) on the widened weights, the residual stream h in f32, plus a bf16
+ * rounding where the device stores bf16: each Linear's input (LayerNorm
+ * output, attention output, GELU output) and the k, v cache rows.  With
+ * `exact` set those roundings are skipped and the cache holds f32, so the
+ * step is the pinned f32 GPT-2 forward on bf16-valued weights, bit for bit.
+ * Embedding tables bf16.  Weight matrices (out, in). */
 typedef struct {
   int32_t n_layers, dim, heads, vocab, max_ctx, batch;
   float norm_eps;
@@ -139,13 +142,14 @@ typedef struct {
   const float **ln_1_w, **ln_1_b, **ln_2_w, **ln_2_b;
   const uint16_t **c_attn_w, **c_proj_w, **c_fc_w, **mlp_proj_w;   /* [3D,D] [D,D] [4D,D] [D,4D] */
   const float **c_attn_b, **c_proj_b, **c_fc_b, **mlp_proj_b;
+  int32_t exact;
 } OrcXL;
 
-/* One decode step of `batch` sequences at position pos: kv is the bf16 cache
- * [n_layers][2][batch][max_ctx][dim] (row pos written), h scratch is
- * allocated inside.  logits [batch, vocab] (may be NULL); next [batch] gets
- * each row's first-index argmax. */
-void orc_xl_step(const OrcXL *m, uint16_t *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next);
+/* One decode step of `batch` sequences at position pos: kv is the cache
+ * [n_layers][2][batch][max_ctx][dim] (row pos written), bf16 bits, or f32
+ * when m->exact; logits [batch, vocab] (may be NULL); next [batch] gets each
+ * row's first-index argmax. */
+void orc_xl_step(const OrcXL *m, void *kv, const int32_t *tok, int32_t pos, float *logits, int32_t *next);
 
 /* ---- batched MoE decode step ---------------------------
  * A DeepSeek-V2-Lite-shaped decoder (bench/dsv2_decode_bench.c cfg :97-124)

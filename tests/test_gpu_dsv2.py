@@ -25,10 +25,11 @@ def f32(b):
 
 def test_ds_decode_matches_oracle():
     import torch
-    from thvm_b200.dsv2 import DSConfig, DSModel, ep_shard, ds_weights, yarn_tables
+    from thvm_b200.dsv2 import DSConfig, DSModel, ds_shard, ds_weights, shard_ds_weights, yarn_tables
     cfg = DSConfig(**CFG)
     w = ds_weights(cfg, seed=0)
-    dev = DSModel(cfg, w, ep_shard(cfg, 0, 1))
+    sh = ds_shard(cfg, 0, 1)
+    dev = DSModel(cfg, shard_ds_weights(w, cfg, sh), sh)
     cos, sin = yarn_tables(cfg.d_rope, cfg.max_ctx)
     ref = O.DSModel(cfg, w, cos, sin)
     prompt = np.random.default_rng(1).integers(0, cfg.vocab, (cfg.batch, 6)).astype(np.int32)
@@ -47,7 +48,7 @@ def test_ds_decode_matches_oracle():
         tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt
     assert worst <= 2e-2, worst
     assert agree / total >= 0.99, agree / total
-    assert dev.lib.sm100_ds_status() == 0
+    assert dev.status() == 0
     for l in range(cfg.n_layers):
         # layer 0's rows see identical inputs: a bf16 operand one rounding apart moves a value by
         # an ulp of its input, which the rotary can leave in a near-cancelled output (hence the

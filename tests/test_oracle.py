@@ -212,3 +212,44 @@ def test_ds_route_takes_top_k_of_logits():
     p = np.exp(g[0] - 6.0, dtype=np.float32)
     assert np.float32(g[0, 5] - 6.0) == np.float32(g[0, 6] - 6.0)   # equal probabilities
     np.testing.assert_allclose(pr[0], p[[0, 1, 2, 3, 4, 6]] / p.sum(), rtol=1e-6)
+
+
+# ---- GPT-2-XL-shaped batched decode ---------------------
+
+def test_xl_step_without_rounding_is_the_pinned_gpt2_forward():
+    """orc_xl_step with its bf16 roundings off (f32 cache) is the f32 GPT-2
+    forward pinned to the reference (orc_gpt2_forward) on the bf16-valued
+    weights, bit for bit: logits and ids of two sequences decoded side by side
+    over 12 positions (a prompt of 6 fed one id per step, then 6 greedy)."""
+    from types import SimpleNamespace
+    from thvm_b200.gpt2_xl import XLConfig, xl_weights
+    cfg = XLConfig(n_layers=2, dim=128, heads=2, vocab=500, max_ctx=32, batch=2)
+    w = xl_weights(cfg, seed=4)
+    rng = np.random.default_rng(7)
+    for k in w:   # LayerNorm affine parameters off their identity defaults
+        if ".ln_" in k or k.startswith("ln_f"):
+            w[k] = (w[k] + rng.uniform(-0.1, 0.1, w[k].shape)).astype(np.float32)
+    xl = O.XLModel(cfg, w, exact=True)
+    wide = lambda b: O.bf16_to_f32(b)
+    names = {"attn.w": "attn.c_attn.weight", "attn.b": "attn.c_attn.bias", "proj.w": "attn.c_proj.weight",
+             "proj.b": "attn.c_proj.bias", "fc.w": "mlp.c_fc.weight", "fc.b": "mlp.c_fc.bias",
+             "p2.w": "mlp.c_proj.weight", "p2.b": "mlp.c_proj.bias", "ln_1.w": "ln_1.weight", "ln_1.b": "ln_1.bias",
+             "ln_2.w": "ln_2.weight", "ln_2.b": "ln_2.bias"}
+    g = {"wte.weight": wide(w["wte"]), "wpe.weight": wide(w["wpe"]), "lm_head.weight": wide(w["lm_head"]),
+         "ln_f.weight": w["ln_f.w"], "ln_f.bias": w["ln_f.b"]}
+    for i in range(cfg.n_layers):
+        for a, b in names.items():
+            v = w[f"h.{i}.{a}"]
+            g[f"h.{i}.{b}"] = wide(v) if v.dtype == np.uint16 else v
+    gc = SimpleNamespace(n_layers=cfg.n_layers, n_heads=cfg.heads, dim=cfg.dim, vocab=cfg.vocab,
+                         max_ctx=cfg.max_ctx, norm_eps=cfg.norm_eps)
+    refs = [O.GPT2(gc, g) for _ in range(cfg.batch)]
+    prompt = rng.integers(0, cfg.vocab, (cfg.batch, 6)).astype(np.int32)
+    tok = prompt[:, 0]
+    for pos in range(12):
+        lg, nxt = xl.step(tok, pos)
+        for b, r in enumerate(refs):
+            t, rl = r.forward([int(tok[b])], pos, want_logits=True)
+            assert int(nxt[b]) == t
+            assert np.array_equal(lg[b].view(np.uint32), rl.view(np.uint32)), (pos, b)
+        tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt

@@ -1,6 +1,6 @@
-"""Host logic of the multi-GPU config-4 prefill bench: the (batch, head) pairs
+"""Host logic of the multi-GPU config-4 prefill bench (bench.py --workload prefill): the (batch, head) pairs
 are split into contiguous, disjoint, covering shares (no GPU needed)."""
-from thvm_b200.bench_prefill import pair_range
+from bench import pair_range
 
 
 def test_pair_ranges_cover_every_pair_once():

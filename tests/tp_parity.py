@@ -1,0 +1,136 @@
+"""Multi-rank parity of the sharded decode steps against the CPU oracle, one
+process per GPU (run by tests/test_gpu_multi.py under torch.distributed.run):
+
+  ds   config 5 (thvm_b200.dsv2.DSModel): heads, dense units, experts and
+       vocabulary split over the ranks, NCCL all-reduces of the residual;
+  xl   config 3 (thvm_b200.gpt2_xl.XLModel): Megatron column / row splits.
+
+Each rank holds its shard of one seeded model, both sides are fed the
+oracle's ids (teacher forcing), and rank 0 checks the gathered logits (within
+2e-2 of each row's largest), the ids (top-1 agreement >= 99 %) and its cache
+rows against the oracle.  Exit status 0 when every check passes.
+
+    python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 tests/tp_parity.py ds
+"""
+import datetime
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parents[1]
+sys.path.insert(0, str(ROOT))
+
+
+def gathered_logits(model, dist, world):
+    """The full [B, V] logits from every rank's vocabulary rows [v0, v1)."""
+    import torch
+    # vocabulary shards can differ by one row: pad to the largest
+    n = torch.tensor([model.logits.shape[1]], device="cuda")
+    sizes = [torch.zeros_like(n) for _ in range(world)]
+    dist.all_gather(sizes, n)
+    vmax = int(max(int(s.item()) for s in sizes))
+    pad = torch.zeros(model.logits.shape[0], vmax, device="cuda")
+    pad[:, :model.logits.shape[1]] = model.logits
+    outs = [torch.zeros_like(pad) for _ in range(world)]
+    dist.all_gather(outs, pad)
+    return np.concatenate([o[:, :int(s.item())].cpu().numpy() for o, s in zip(outs, sizes)], 1)
+
+
+def run_ds(rank, world, dist):
+    import torch
+    import oracle as O
+    from thvm_b200.dsv2 import DSConfig, DSModel, ds_shard, ds_weights, shard_ds_weights, yarn_tables
+    cfg = DSConfig(n_layers=2, dim=512, heads=4, kv_lora=128, d_nope=32, d_rope=16, d_v=32, n_exp=8, top_k=3,
+                   moe_inter=128, dense_inter=256, n_dense=1, n_shared=2, vocab=1000, max_ctx=64, batch=32)
+    w = ds_weights(cfg, seed=0)
+    sh = ds_shard(cfg, rank, world)
+    dev = DSModel(cfg, shard_ds_weights(w, cfg, sh), sh, dist.group.WORLD)
+    ref = None
+    if rank == 0:
+        cos, sin = yarn_tables(cfg.d_rope, cfg.max_ctx)
+        ref = O.DSModel(cfg, w, cos, sin)
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, (cfg.batch, 6)).astype(np.int32)
+    tok = prompt[:, 0]
+    agree, total, worst = 0, 0, 0.0
+    for pos in range(12):
+        dev.tok.copy_(torch.from_numpy(tok))
+        dev.step()
+        torch.cuda.synchronize()
+        lg_all = gathered_logits(dev, dist, world)
+        got = dev.tok.cpu().numpy()
+        nxt = np.zeros(cfg.batch, np.int32)
+        if rank == 0:
+            lg, nxt = ref.step(tok, pos)
+            worst = max(worst, float((np.abs(lg_all - lg).max(1) / np.abs(lg).max(1)).max()))
+            agree += int((got == nxt).sum())
+            total += cfg.batch
+        t = torch.from_numpy(nxt).cuda()
+        dist.broadcast(t, 0)
+        nxt = t.cpu().numpy()
+        tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt
+    status = dev.status()
+    if rank == 0:
+        print(f"ds world {world}: worst logit error {worst:.3e}, top-1 agreement {agree}/{total}, status {status}")
+        assert worst <= 2e-2, worst
+        assert agree / total >= 0.99, agree / total
+        f32 = lambda b: (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+        a = f32(dev.cache_c[0].cpu().numpy().view(np.uint16)[:, :12])
+        r = f32(ref.cache_c[0][:, :12])
+        excess = np.abs(a - r) - (2.0 ** -6 * np.abs(r) + 2.0 ** -6 * np.sqrt(np.mean(r * r)))
+        assert excess.max() <= 0, excess.max()
+    assert status == 0, status
+
+
+def run_xl(rank, world, dist):
+    import torch
+    import oracle as O
+    from thvm_b200.gpt2_xl import XLConfig, XLModel, shard_of, shard_weights, xl_weights
+    cfg = XLConfig(n_layers=2, dim=256, heads=4, vocab=1000, max_ctx=64, batch=16)
+    w = xl_weights(cfg, seed=0)
+    sh = shard_of(cfg, rank, world)
+    dev = XLModel(cfg, shard_weights(w, cfg, sh), sh, dist.group.WORLD)
+    ref = O.XLModel(cfg, w) if rank == 0 else None
+    prompt = np.random.default_rng(1).integers(0, cfg.vocab, (cfg.batch, 8)).astype(np.int32)
+    tok = prompt[:, 0]
+    agree, total, worst = 0, 0, 0.0
+    for pos in range(16):
+        dev.tok.copy_(torch.from_numpy(tok))
+        dev.step()
+        torch.cuda.synchronize()
+        lg_all = gathered_logits(dev, dist, world)
+        got = dev.tok.cpu().numpy()
+        nxt = np.zeros(cfg.batch, np.int32)
+        if rank == 0:
+            lg, nxt = ref.step(tok, pos)
+            worst = max(worst, float((np.abs(lg_all - lg).max(1) / np.abs(lg).max(1)).max()))
+            agree += int((got == nxt).sum())
+            total += cfg.batch
+        t = torch.from_numpy(nxt).cuda()
+        dist.broadcast(t, 0)
+        nxt = t.cpu().numpy()
+        tok = prompt[:, pos + 1] if pos + 1 < prompt.shape[1] else nxt
+    if rank == 0:
+        print(f"xl world {world}: worst logit error {worst:.3e}, top-1 agreement {agree}/{total}")
+        assert worst <= 2e-2, worst
+        assert agree / total >= 0.99, agree / total
+
+
+def main():
+    import torch
+    import torch.distributed as dist
+    which = sys.argv[1]
+    rank, world, local = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"]), int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    os.environ["THVM_SM100_DEVICE"] = str(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
+    try:
+        {"ds": run_ds, "xl": run_xl}[which](rank, world, dist)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

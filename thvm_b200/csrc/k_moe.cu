@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
   }
 }
 
-// The same attention, one CTA per (head h, group of kMlaNB sequences), for
+// The same attention, one CTA per (head h, group of NB <= kMlaNB sequences), for
 // the DeepSeek-V2-Lite shapes (latent 512, rope 64, nope / v <= 128).  The
 // head's absorbed weights are read once per group instead of once per
 // sequence: W_uk[h] comes into shared memory by one bulk copy (issued before
@@ -214,6 +214,7 @@ struct MlaSmem {
   static constexpr size_t total = bar + 16;
 };
 
+template <int NB>
 __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     ds_mla_group_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk, const __nv_bfloat16 *wuv,
                         const __nv_bfloat16 *cc, const __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o, int B,
@@ -225,7 +226,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   float *pm = reinterpret_cast<float *>(sm + MlaSmem::pm), *pl = reinterpret_cast<float *>(sm + MlaSmem::pl);
   uint64_t *bar = reinterpret_cast<uint64_t *>(sm + MlaSmem::bar);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  const int h = blockIdx.x % H, b0 = (blockIdx.x / H) * kMlaNB, nb = min(kMlaNB, B - b0), QS = DN + kMlaDR;
+  const int h = blockIdx.x % H, b0 = (blockIdx.x / H) * NB, nb = min(NB, B - b0), QS = DN + kMlaDR;
   uint32_t *status = &g_ds_status;
   if (t == 0) {
     mbar_init(bar, 1);
@@ -249,7 +250,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   const bool wk_ok = mbar_wait(bar, 0, status, false);
   // q_lat[b][k] = sum_d q_nope[b][d] W_uk[h][d][k], k = t and t + 256
   {
-    float a[kMlaNB][2] = {};
+    float a[NB][2] = {};
     if (wk_ok) {
 #pragma unroll 4
       for (int d = 0; d < DN; d++) {
@@ -257,14 +258,14 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
         const float w0 = bf(wb[d * kMlaKV + t]), w1 = bf(wb[d * kMlaKV + t + 256]);
         const float qq[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int b = 0; b < kMlaNB; b++) {
+        for (int b = 0; b < NB; b++) {
           a[b][0] = fmaf(qq[b], w0, a[b][0]);
           a[b][1] = fmaf(qq[b], w1, a[b][1]);
         }
       }
     }
 #pragma unroll
-    for (int b = 0; b < kMlaNB; b++) {
+    for (int b = 0; b < NB; b++) {
       qlat[b * kMlaKV + t] = a[b][0];
       qlat[b * kMlaKV + t + 256] = a[b][1];
     }
@@ -348,9 +349,9 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   const bool wv_ok = mbar_wait(bar, 1, status, false);
   // o[b][h][r] = sum_k o_lat[b][k] W_uv[h][r][k]: warp w takes rows w, w + 8,
   // ..., lane l the columns 2 (l + 32 i) and 2 (l + 32 i) + 1
-  float ov[kMlaNB][16];
+  float ov[NB][16];
 #pragma unroll
-  for (int b = 0; b < kMlaNB; b++)
+  for (int b = 0; b < NB; b++)
 #pragma unroll
     for (int i = 0; i < 8; i++) {
       const float2 v = b < nb ? reinterpret_cast<const float2 *>(qlat + b * kMlaKV)[lane + 32 * i] : make_float2(0.f, 0.f);
@@ -358,20 +359,22 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
       ov[b][2 * i + 1] = v.y;
     }
   for (int r = warp; r < DV; r += kMlaWarps) {
-    float acc[kMlaNB] = {};
+    float acc[NB] = {};
     if (wv_ok) {
 #pragma unroll
       for (int i = 0; i < 8; i++) {
         const uint32_t w2 = reinterpret_cast<const uint32_t *>(wb + r * kMlaKV)[lane + 32 * i];
         const float w0 = __uint_as_float(w2 << 16), w1 = __uint_as_float(w2 & 0xFFFF0000u);
 #pragma unroll
-        for (int b = 0; b < kMlaNB; b++) acc[b] = fmaf(ov[b][2 * i + 1], w1, fmaf(ov[b][2 * i], w0, acc[b]));
+        for (int b = 0; b < NB; b++) acc[b] = fmaf(ov[b][2 * i + 1], w1, fmaf(ov[b][2 * i], w0, acc[b]));
       }
     }
 #pragma unroll
-    for (int b = 0; b < kMlaNB; b++) acc[b] = warp_sum(acc[b]);
+    for (int b = 0; b < NB; b++) acc[b] = warp_sum(acc[b]);
     if (lane < nb) {
-      const float v = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+      float v = acc[0];
+#pragma unroll
+      for (int b = 1; b < NB; b++) v = lane == b ? acc[b] : v;
       o[((int64_t)(b0 + lane) * H + h) * DV + r] = __float2bfloat16_rn(v);
     }
   }
@@ -934,17 +937,28 @@ extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_u
     return sm100_set_error(SM100_ERR_ARG, "ds_mla: bad arguments (DN <= 256, DR <= 128, KV <= %d, ctx <= %d)",
                            kDsKV, kDsMaxCtx);
   if (KV == kMlaKV && DR == kMlaDR && DN <= kMlaMaxD && DV <= kMlaMaxD) {
-    static bool attr = false;
-    if (!attr) {
-      const cudaError_t e = cudaFuncSetAttribute(ds_mla_group_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (int)MlaSmem::total);
+    // sequences per CTA: the most (fewer re-reads of the head's W_uk / W_uv)
+    // that still gives the grid at least 96 CTAs, so a tensor-parallel rank
+    // with few heads still spreads its cache walks over the SMs
+    const int nb = H * ((B + 3) / 4) >= 96 ? 4 : H * ((B + 1) / 2) >= 96 ? 2 : 1;
+    static bool attr[3] = {false, false, false};
+    const int ai = nb == 4 ? 2 : nb == 2 ? 1 : 0;
+    if (!attr[ai]) {
+      const void *fn = nb == 4 ? (const void *)ds_mla_group_kernel<4>
+                       : nb == 2 ? (const void *)ds_mla_group_kernel<2> : (const void *)ds_mla_group_kernel<1>;
+      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MlaSmem::total);
       if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_mla: smem attribute: %s", cudaGetErrorString(e));
-      attr = true;
+      attr[ai] = true;
     }
-    DS_LAUNCH("ds_mla", ds_mla_group_kernel, dim3(H * ((B + kMlaNB - 1) / kMlaNB)), dim3(kMlaWarps * 32),
-              MlaSmem::total, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,
-              (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c, (const __nv_bfloat16 *)cache_pe, pos,
-              (__nv_bfloat16 *)o, B, H, DN, DV, ctx, scale);
+#define DS_MLA_GROUP(NBV)                                                                                         \
+  DS_LAUNCH("ds_mla", ds_mla_group_kernel<NBV>, dim3(H * ((B + NBV - 1) / NBV)), dim3(kMlaWarps * 32), MlaSmem::total, \
+            (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,                        \
+            (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c, (const __nv_bfloat16 *)cache_pe, pos,     \
+            (__nv_bfloat16 *)o, B, H, DN, DV, ctx, scale)
+    if (nb == 4) DS_MLA_GROUP(4);
+    if (nb == 2) DS_MLA_GROUP(2);
+    DS_MLA_GROUP(1);
+#undef DS_MLA_GROUP
   }
   DS_LAUNCH("ds_mla", ds_mla_kernel, dim3(B * H), dim3(256), 0, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out,
             (const __nv_bfloat16 *)w_uk, (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c,

@@ -1,27 +1,41 @@
 """Batched decode of a DeepSeek-V2-Lite-shaped MoE decoder
-on the sm_100a kernels, expert-parallel over the GPUs of one box.
+on the sm_100a kernels, tensor- and expert-parallel over the GPUs of one box.
 
 Shapes (bench/dsv2_decode_bench.c cfg :97-124): 27 layers, d 2048, 16 heads,
 multi-head latent attention (kv_lora 512, rope 64, nope 128, v 128), layer 0
 a dense SiLU MLP (10944), layers 1-26 64 routed experts (1408) with top-6
-softmax routing (no renormalisation, ties to the lowest id) plus 2 shared
-experts, vocab 102400, batch 32.  Precision: routed and shared expert
-weights fp8-e4m3 with one f32 scale per 128 x 128 block; attention, router,
-dense layer 0, embedding and lm_head bf16; f32 residual stream, bf16 matmul
-operands (the oracle's orc_ds_step states the op order).  The two shared
-experts are one SiLU MLP of 2816 units, taken as two halves of 1408 whose
-outputs add (exact), so they ride the routed-expert kernel with weight 1.
+routing over the router logits (softmax weights, no renormalisation, ties to
+the lowest id) plus 2 shared experts, vocab 102400, batch 32.  Precision:
+routed and shared expert weights fp8-e4m3 with one f32 scale per 128 x 128
+block; attention, router, dense layer 0, embedding and lm_head bf16; f32
+residual stream, bf16 matmul operands (the oracle's orc_ds_step states the op
+order).  The two shared experts are one SiLU MLP of 2816 units, taken as two
+halves of 1408 whose outputs add (exact), so they ride the routed-expert
+kernel with weight 1.
 
 Per layer: RMSNorm -> fused q | kv_a projection (skinny tcgen05 GEMM) ->
 q / latent post-processing (bf16, RMSNorm of the latent, YaRN rotary, cache
 append) -> absorbed MLA over the compressed cache -> o projection into the
 residual -> RMSNorm -> dense MLP (layer 0) or router GEMM, routing, fp8
-experts (gate / up + SiLU, then down weighted into the MoE output).
+experts (gate / up + SiLU, then down weighted into the residual).
 
-Expert parallelism: rank r of R holds routed experts split_even(64, R, r)
-and the shared halves k with k % R == r; attention, router, dense layer and
-lm_head are replicated (every rank computes the same h), and one all-reduce
-of the MoE output [B, D] per MoE layer combines the experts.
+Parallelism over R ranks (rank r), every weight byte read by one rank:
+  * attention by heads: heads split_even(16, R, r); the q rows of those
+    heads and the whole kv_a block (the latent every head reads) in the
+    fused projection, their W_uk / W_uv, and their columns of W_o (a
+    row-split product whose partial sums meet in one all-reduce);
+  * dense layer 0 by hidden units: gate / up rows and down columns of
+    split_even(10944, R, r), one all-reduce;
+  * experts by expert: routed experts split_even(64, R, r) and the shared
+    halves k with k % R == r; every rank routes every token (the router is
+    replicated, 256 KB) and keeps the slots of its experts; one all-reduce;
+  * lm_head by vocabulary rows split_even(102400, R, r); each rank's (max,
+    index) per row are all-gathered and the smallest index of the largest
+    value wins.
+The residual stream h is replicated: after each all-reduce every rank holds
+the same h.  Rank 0 adds its partial sums into h; the other ranks overwrite
+h with theirs (or zero it before the experts add into it), so the all-reduce
+sum is h + sum of the partials.
 """
 from __future__ import annotations
 
@@ -136,44 +150,75 @@ def ds_weights(cfg: DSConfig, seed: int = 0, std: float = 0.02) -> dict[str, np.
 
 
 @dataclass(frozen=True)
-class EPShard:
+class DSShard:
+    """What rank r of R holds: heads [h0, h1), dense hidden units [f0, f1),
+    routed experts [e0, e1) and the shared halves `shared`, vocab rows
+    [v0, v1)."""
     rank: int
     world: int
+    h0: int
+    h1: int
+    f0: int
+    f1: int
     e0: int
     e1: int
-    shared: tuple   # the shared halves this rank runs
+    shared: tuple
+    v0: int
+    v1: int
+
+    @property
+    def heads(self) -> int:
+        return self.h1 - self.h0
 
 
-def ep_shard(cfg: DSConfig, rank: int, world: int) -> EPShard:
-    if not 0 <= rank < world or world > cfg.n_exp:
-        raise ValueError(f"rank {rank} of {world}")
-    e0, e1 = split_even(cfg.n_exp, world, rank)
-    return EPShard(rank, world, e0, e1, tuple(k for k in range(cfg.n_shared) if k % world == rank))
+def ds_shard(cfg: DSConfig, rank: int, world: int) -> DSShard:
+    if not 0 <= rank < world or world > cfg.heads or world > cfg.n_exp:
+        raise ValueError(f"rank {rank} of {world} (heads {cfg.heads}, experts {cfg.n_exp})")
+    return DSShard(rank, world, *split_even(cfg.heads, world, rank), *split_even(cfg.dense_inter, world, rank),
+                   *split_even(cfg.n_exp, world, rank), tuple(k for k in range(cfg.n_shared) if k % world == rank),
+                   *split_even(cfg.vocab, world, rank))
 
 
-def shard_experts(w: dict[str, np.ndarray], cfg: DSConfig, sh: EPShard) -> dict[str, np.ndarray]:
-    """This rank's weights: everything but the experts replicated; the experts
-    [e0, e1) followed by its shared halves."""
-    out = {}
+def shard_ds_weights(w: dict[str, np.ndarray], cfg: DSConfig, sh: DSShard) -> dict[str, np.ndarray]:
+    """This rank's slices (contiguous copies) of the full weights."""
+    QS, DV, DI = cfg.d_nope + cfg.d_rope, cfg.d_v, cfg.dense_inter
     keep = list(range(sh.e0, sh.e1)) + [cfg.n_exp + k for k in sh.shared]
-    for k, v in w.items():
-        if k.split(".", 1)[-1] in ("e_gu", "e_gu_s", "e_d", "e_d_s"):
-            out[k] = np.ascontiguousarray(v[keep])
+    c = np.ascontiguousarray
+    out = {"embed": w["embed"], "norm_f": w["norm_f"], "lm_head": c(w["lm_head"][sh.v0:sh.v1])}
+    for l in range(cfg.n_layers):
+        p = f"l{l}."
+        for k in ("attn_norm", "ffn_norm", "kv_norm", "router"):
+            if p + k in w:
+                out[p + k] = w[p + k]
+        wq = w[p + "w_qkva"]
+        out[p + "w_qkva"] = c(np.concatenate([wq[sh.h0 * QS:sh.h1 * QS], wq[cfg.q_cols:]]))
+        out[p + "w_uk"], out[p + "w_uv"] = c(w[p + "w_uk"][sh.h0:sh.h1]), c(w[p + "w_uv"][sh.h0:sh.h1])
+        out[p + "w_o"] = c(w[p + "w_o"][:, sh.h0 * DV:sh.h1 * DV])
+        if l < cfg.n_dense:
+            gu = w[p + "d_gu"]
+            out[p + "d_gu"] = c(np.concatenate([gu[sh.f0:sh.f1], gu[DI + sh.f0:DI + sh.f1]]))
+            out[p + "d_down"] = c(w[p + "d_down"][:, sh.f0:sh.f1])
         else:
-            out[k] = v
+            for k in ("e_gu", "e_gu_s", "e_d", "e_d_s"):
+                out[p + k] = c(w[p + k][keep])
     return out
 
 
 class DSModel:
     """One rank's part of the model on the current CUDA device (torch.distributed
-    group over the R ranks, None when R = 1)."""
+    group over the R ranks, None when R = 1); `weights` are this rank's slices
+    (shard_ds_weights)."""
 
-    def __init__(self, cfg: DSConfig, weights: dict[str, np.ndarray], shard: EPShard, group=None):
+    def __init__(self, cfg: DSConfig, weights: dict[str, np.ndarray], shard: DSShard, group=None):
         import torch
         self.torch, self.cfg, self.sh, self.group = torch, cfg, shard, group
         self.lib = L.lib()
         dev = torch.device("cuda", torch.cuda.current_device())
-        B, D, ctx = cfg.batch, cfg.dim, cfg.max_ctx
+        B, D, ctx, Hl = cfg.batch, cfg.dim, cfg.max_ctx, shard.heads
+        QS = cfg.d_nope + cfg.d_rope
+        self.n_q = Hl * QS                               # local q columns of the fused projection
+        self.n_qkva = self.n_q + cfg.kv_lora + cfg.d_rope
+        DIl, Vl = shard.f1 - shard.f0, shard.v1 - shard.v0
 
         def put(a):
             t = torch.from_numpy(np.ascontiguousarray(a))
@@ -186,14 +231,13 @@ class DSModel:
         self.cos, self.sin = put(cos), put(sin)
         z = lambda *s, dt=torch.float32: torch.zeros(*s, dtype=dt, device=dev)
         self.h = z(B, D)
-        self.xn = z(B, max(D, cfg.dense_inter), dt=torch.int16)
-        self.qkva = z(B, cfg.n_qkva)
-        self.qo = z(B, cfg.q_cols, dt=torch.int16)
-        self.o = z(B, cfg.heads * cfg.d_v, dt=torch.int16)
-        self.gu = z(B, 2 * cfg.dense_inter)
+        self.xn = z(B, max(D, DIl), dt=torch.int16)
+        self.qkva = z(B, self.n_qkva)
+        self.qo = z(B, max(self.n_q, 1), dt=torch.int16)
+        self.o = z(B, max(Hl * cfg.d_v, 1), dt=torch.int16)
+        self.gu = z(B, 2 * DIl)
         self.rl = z(B, cfg.n_exp)
-        self.moe = z(B, D)
-        self.logits = z(B, cfg.vocab)
+        self.logits = z(B, Vl)
         self.cache_c = [z(B, ctx, cfg.kv_lora, dt=torch.int16) for _ in range(cfg.n_layers)]
         self.cache_pe = [z(B, ctx, cfg.d_rope, dt=torch.int16) for _ in range(cfg.n_layers)]
         self.tok = z(B, dt=torch.int32)
@@ -205,9 +249,12 @@ class DSModel:
         self.slot_off = z(n_local + ns + 1, dt=torch.int32)
         self.slot_tok, self.slot_w = z(B * (K + ns), dt=torch.int32), z(B * (K + ns))
         self.a = z(B * (K + ns), cfg.moe_inter, dt=torch.int16)
-        self.vals, self.idxs = z(1, B), z(1, B, dt=torch.int32)
+        self.vals, self.idxs = z(shard.world, B), z(shard.world, B, dt=torch.int32)
+        # this rank's (max, index) per row; with one rank it is the gathered row itself
+        self.val_me = self.vals[0] if shard.world == 1 else z(B)
+        self.idx_me = self.idxs[0] if shard.world == 1 else z(B, dt=torch.int32)
         self.ws = z(int(self.lib.sm100_skinny_ws_bytes(B)) // 4)
-        self.counters = z(cfg.vocab // 128 + 2, dt=torch.int32)
+        self.counters = z(max(Vl, self.n_qkva, 2 * DIl, D) // 128 + 2, dt=torch.int32)
         self._args = L.Sm100SkinnyArgs()
         self.launches = 0
 
@@ -232,34 +279,47 @@ class DSModel:
                                           self.cfg.eps, self._stream()), "ds_rmsnorm")
         self.launches += 1
 
+    def _all_reduce(self):
+        if self.sh.world > 1:
+            self.torch.distributed.all_reduce(self.h, group=self.group)
+
+    def status(self) -> int:
+        """The kernels' sticky status word (non-zero: a bounded wait gave up or an
+        expert met more than 32 slots); synchronises the device and clears it."""
+        return int(self.lib.sm100_ds_status())
+
     def step(self):
         """One decode step: ids in self.tok at row self.pos -> next ids, pos + 1."""
         cfg, sh, w, lib, st = self.cfg, self.sh, self.w, self.lib, self._stream
-        B, D, H, KV, DN, DR, DV = cfg.batch, cfg.dim, cfg.heads, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v
-        E, K, I, DI = cfg.n_exp, cfg.top_k, cfg.moe_inter, cfg.dense_inter
+        B, D, KV, DN, DR, DV = cfg.batch, cfg.dim, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v
+        E, K, I, Hl = cfg.n_exp, cfg.top_k, cfg.moe_inter, sh.heads
+        DIl, Vl, first = sh.f1 - sh.f0, sh.v1 - sh.v0, sh.rank == 0
         L.check(lib.sm100_ds_embed(w["embed"].data_ptr(), self.tok.data_ptr(), self.h.data_ptr(), B, cfg.vocab, D,
                                    st()), "ds_embed")
         self.launches += 1
         for l in range(cfg.n_layers):
             p = f"l{l}."
             self._rms(w[p + "attn_norm"], D)
-            self._skinny(self.xn, w[p + "w_qkva"], self.qkva, D, cfg.n_qkva)
+            self._skinny(self.xn, w[p + "w_qkva"], self.qkva, D, self.n_qkva)
             q = self.qkva.data_ptr()
-            L.check(lib.sm100_ds_qkv_post(q, q + 4 * cfg.q_cols, cfg.n_qkva, w[p + "kv_norm"].data_ptr(),
+            L.check(lib.sm100_ds_qkv_post(q, q + 4 * self.n_q, self.n_qkva, w[p + "kv_norm"].data_ptr(),
                                           self.cos.data_ptr(), self.sin.data_ptr(), self.pos.data_ptr(),
                                           self.qo.data_ptr(), self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(),
-                                          B, H, DN, DR, KV, cfg.max_ctx, cfg.eps, st()), "ds_qkv_post")
+                                          B, Hl, DN, DR, KV, cfg.max_ctx, cfg.eps, st()), "ds_qkv_post")
             L.check(lib.sm100_ds_mla(self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
                                      self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.pos.data_ptr(),
-                                     self.o.data_ptr(), B, H, DN, DR, DV, KV, cfg.max_ctx, cfg.scale, st()), "ds_mla")
+                                     self.o.data_ptr(), B, Hl, DN, DR, DV, KV, cfg.max_ctx, cfg.scale, st()), "ds_mla")
             self.launches += 2
-            self._skinny(self.o, w[p + "w_o"], self.h, H * DV, D, residual=True)
+            # the o projection's partial sums: rank 0 into the residual, the others over it
+            self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
+            self._all_reduce()
             self._rms(w[p + "ffn_norm"], D)
             if l < cfg.n_dense:
-                self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DI)
-                L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DI, st()), "ds_silu_mul")
+                self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DIl)
+                L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DIl, st()), "ds_silu_mul")
                 self.launches += 1
-                self._skinny(self.xn, w[p + "d_down"], self.h, DI, D, residual=True)
+                self._skinny(self.xn, w[p + "d_down"], self.h, DIl, D, residual=first)
+                self._all_reduce()
                 continue
             self._skinny(self.xn, w[p + "router"], self.rl, D, E)
             ns = len(sh.shared)
@@ -267,25 +327,25 @@ class DSModel:
                                        self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
                                        self.slot_w.data_ptr(), st()), "ds_route")
             # one launch pair over the local routed experts and shared halves (contiguous in this rank's
-            # arrays); on one rank they add into the residual stream itself, on several into a zeroed
-            # buffer that is summed over the ranks and then added
-            y = self.h if sh.world == 1 else self.moe
-            if sh.world > 1:
-                self.moe.zero_()
+            # arrays), adding into the residual on rank 0 and into a zeroed h on the others
+            if not first:
+                self.h.zero_()
             L.check(lib.sm100_ds_experts(self.xn.data_ptr(), w[p + "e_gu"].data_ptr(), w[p + "e_gu_s"].data_ptr(),
                                          w[p + "e_d"].data_ptr(), w[p + "e_d_s"].data_ptr(), self.slot_off.data_ptr(),
                                          self.slot_tok.data_ptr(), self.slot_w.data_ptr(), self.a.data_ptr(),
-                                         y.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
+                                         self.h.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
             self.launches += 3
-            if sh.world > 1:
-                self.torch.distributed.all_reduce(self.moe, group=self.group)
-                L.check(lib.sm100_add(self.h.data_ptr(), self.moe.data_ptr(), self.h.data_ptr(), B * D, st()), "add")
-                self.launches += 1
+            self._all_reduce()
         self._rms(w["norm_f"], D)
-        self._skinny(self.xn, w["lm_head"], self.logits, D, cfg.vocab)
-        L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), cfg.vocab, B, cfg.vocab, self.vals.data_ptr(),
-                                    self.idxs.data_ptr(), 0, 0, st()), "xl_argmax")
-        L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(), st()),
+        self._skinny(self.xn, w["lm_head"], self.logits, D, Vl)
+        L.check(lib.sm100_xl_argmax(self.logits.data_ptr(), Vl, B, Vl, self.val_me.data_ptr(), self.idx_me.data_ptr(),
+                                    sh.v0, 0, st()), "xl_argmax")
+        self.launches += 1
+        if sh.world > 1:
+            dist = self.torch.distributed
+            dist.all_gather_into_tensor(self.vals.view(-1), self.val_me, group=self.group)
+            dist.all_gather_into_tensor(self.idxs.view(-1), self.idx_me, group=self.group)
+        L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), sh.world, B, self.tok.data_ptr(), st()),
                 "xl_pick")
         L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, st()), "pos_add")
-        self.launches += 3
+        self.launches += 2
