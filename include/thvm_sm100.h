@@ -505,6 +505,28 @@ int sm100_attn_prefill_bf16(const void *q, const void *k, const void *v, float *
  * synchronises the device and clears the word */
 uint32_t sm100_attn_prefill_status(void);
 
+/* ---- custom-kernel ABI: raw CUDA-C programs -------------------------------
+ * Replaces cuda_custom_dispatch (src/backend/cuda/jit.c:802-893) for the
+ * programs kernel_emit_custom_program records (src/schedule/kernel_custom.c:
+ * 47-136; the ABI of src/thvm.h's custom_* KernelEntry fields):
+ * `extern "C" __global__ void name(T *arg0, ...)`, one device address per
+ * argument, launched grid[3] x block[3] with shared_bytes of dynamic shared
+ * memory (above 48 KiB opted in per kernel).  sm100_custom_program compiles
+ * the source once with NVRTC for sm_100a and loads it (registering the same
+ * name and source again returns the same id, recompiling nothing; the launch
+ * shape is the latest registration's); it returns the program id (> 0) or a
+ * negative SM100_ERR_* with the compiler's log in sm100_last_error.
+ * Dispatching only launches, on the backend stream (so graph capture records
+ * it): args are buffer ids, and a non-zero out_buf_id rebinds argument slot
+ * primary_out_slot (the reference's rebinding of the lowest output slot at
+ * replay, kernel_custom.c:11-30).  At most 64 arguments. */
+int32_t sm100_custom_program(const char *name, const char *src, const uint32_t grid[3], const uint32_t block[3],
+                             uint32_t shared_bytes);
+int sm100_custom_dispatch(int32_t prog, const uint32_t *arg_buf_ids, uint32_t n_args, uint32_t primary_out_slot,
+                          uint32_t out_buf_id);
+/* the same launch over raw device addresses on `stream` */
+int sm100_custom_launch(int32_t prog, void *const *arg_ptrs, uint32_t n_args, void *stream);
+
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into
  * graph slot `slot` (0..63); replay launches it. */

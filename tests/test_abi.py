@@ -50,3 +50,23 @@ def test_init_without_gpu_reports_error():
     rc = _lib.lib().sm100_init()
     assert rc != 0
     assert _lib.lib().sm100_last_error()
+
+
+def test_custom_program_compiles_for_sm100a_without_a_gpu():
+    """The custom-kernel ABI compiles with NVRTC before it needs the device:
+    a broken program fails with the compiler's log, a good one compiles for
+    sm_100a and then reports that the device is not initialised."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    from ctypes import c_uint32
+    from thvm_b200 import _lib
+    lib = _lib.lib()
+    g, b = (c_uint32 * 3)(1, 1, 1), (c_uint32 * 3)(32, 1, 1)
+    bad = b'extern "C" __global__ void broken(float *y) { y[0] = undefined_name; }\n'
+    assert lib.sm100_custom_program(b"broken", bad, g, b, 0) == _lib.ERR_UNSUPPORTED
+    assert b"undefined_name" in lib.sm100_last_error()
+    good = b'extern "C" __global__ void fine(float *y) { y[threadIdx.x] = 1.0f; }\n'
+    assert lib.sm100_custom_program(b"fine", good, g, b, 0) == _lib.ERR_STATE
+    assert b"compiled" in lib.sm100_last_error()
+    assert lib.sm100_custom_program(b"fine", good, g, (c_uint32 * 3)(2048, 1, 1), 0) == _lib.ERR_ARG

@@ -180,6 +180,10 @@ SIGNATURES = {
                                  c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     "sm100_ds_status": (c_uint32, []),
+    "sm100_custom_program": (c_int32, [ctypes.c_char_p, ctypes.c_char_p, POINTER(c_uint32), POINTER(c_uint32),
+                                       c_uint32]),
+    "sm100_custom_dispatch": (c_int, [c_int32, POINTER(c_uint32), c_uint32, c_uint32, c_uint32]),
+    "sm100_custom_launch": (c_int, [c_int32, POINTER(c_void_p), c_uint32, c_void_p]),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),
