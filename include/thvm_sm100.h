@@ -489,6 +489,37 @@ uint32_t sm100_ds_status(void);
 /* a (bf16 [M][I]) = silu(gu[:, :I]) * gu[:, I:] of f32 gate|up rows [M][2I] */
 int sm100_ds_silu_mul(const float *gu, void *a, int32_t M, int32_t I, void *stream);
 
+/* ---- collectives over peer memory (tensor / expert parallel decode) -------
+ * One process per GPU.  Each rank allocates a comm buffer of
+ * sm100_comm_bytes(cols) with sm100_peer_alloc (zero-filled; handle_out gets
+ * its 64-byte CUDA IPC handle), the ranks exchange handles on the host, each
+ * maps the others' with sm100_peer_open and records every rank's address in
+ * its own buffer with sm100_comm_set_peers (peer_ptrs[rank] = its own).  The
+ * kernels push data into the peers' buffers with plain stores over NVLink and
+ * wait on flags with a bounded spin (a timeout sets sm100_comm_status and the
+ * kernel finishes without the missing data).  Every rank must issue the same
+ * sequence of these calls.  They are the all-reduce after each row-split
+ * projection and the gather of the vocabulary-split argmax; rows <= 32,
+ * cols % 4 == 0, cols <= 8192, world <= 8. */
+uint64_t sm100_comm_bytes(int32_t cols);
+int sm100_peer_alloc(uint64_t nbytes, void **dptr, void *handle_out);
+int sm100_peer_open(const void *handle, void **peer_dptr);
+int sm100_peer_close(void *peer_dptr);
+int sm100_peer_free(void *dptr);
+int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t world);
+/* h [rows, cols] f32 holds this rank's partial sums; afterwards h = the sum of
+ * every rank's partials in rank order (the same on every rank) and y (bf16)
+ * = h * rsqrt(mean(h^2) + eps) * g per row */
+int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
+                                 int32_t rows, int32_t cols, float eps, void *stream);
+/* tok[b] = the index of the largest val over the ranks' (val[b], idx[b])
+ * (ties: the smaller index) */
+int sm100_comm_pick(const float *val, const int32_t *idx, void *own, int32_t rank, int32_t world, int32_t rows,
+                    int32_t *tok, void *stream);
+/* non-zero when a comm kernel since the last call gave up a bounded wait;
+ * synchronises the device and clears the word */
+uint32_t sm100_comm_status(void);
+
 /* ---- causal attention prefill on the tensor cores ------------------------ */
 /* O[B, H, S, D] (f32) = softmax(Q K^T * scale + causal mask) V for bf16 Q, K, V
  * [B, H, S, D] contiguous, D = 128, any S >= 0: the reference's

@@ -117,6 +117,40 @@ def run_xl(rank, world, dist):
         assert agree / total >= 0.99, agree / total
 
 
+def run_comm(rank, world, dist):
+    """The peer collectives alone: the fused all-reduce + RMSNorm sums the
+    ranks' rows in rank order (bit for bit what an f32 sum in that order
+    gives), over several uses; the argmax pick takes the largest value, the
+    smaller index on ties across ranks."""
+    import torch
+    from thvm_b200.comm import PeerComm
+    B, D = 32, 2048
+    comm = PeerComm(rank, world, D, dist.group.WORLD)
+    g = torch.from_numpy(np.random.default_rng(9).uniform(0.5, 1.5, D).astype(np.float32)).cuda()
+    y = torch.zeros(B, D, dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    for use in range(5):
+        parts = [np.random.default_rng(100 * use + r).standard_normal((B, D)).astype(np.float32) for r in range(world)]
+        h = torch.from_numpy(parts[rank].copy()).cuda()
+        comm.allreduce_rmsnorm(h.data_ptr(), g.data_ptr(), y.data_ptr(), B, D, 1e-6, st)
+        torch.cuda.synchronize()
+        want = parts[0].copy()
+        for r in range(1, world):
+            want = want + parts[r]
+        assert np.array_equal(h.cpu().numpy(), want), use
+    val = torch.full((B,), float(rank % 2), device="cuda")            # ranks 1, 3, .. hold the maximum
+    idx = torch.arange(B, dtype=torch.int32, device="cuda") + 1000 * (world - rank)   # the last of them the smallest index
+    tok = torch.zeros(B, dtype=torch.int32, device="cuda")
+    comm.pick(val.data_ptr(), idx.data_ptr(), B, tok.data_ptr(), st)
+    torch.cuda.synchronize()
+    best = max(r for r in range(world) if r % 2 == 1) if world > 1 else 0
+    assert np.array_equal(tok.cpu().numpy(), np.arange(B) + 1000 * (world - best))
+    assert comm.status() == 0
+    comm.close()
+    if rank == 0:
+        print(f"comm world {world}: five all-reduces bit-exact, pick ok")
+
+
 def main():
     import torch
     import torch.distributed as dist
@@ -126,7 +160,7 @@ def main():
     os.environ["THVM_SM100_DEVICE"] = str(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     try:
-        {"ds": run_ds, "xl": run_xl}[which](rank, world, dist)
+        {"ds": run_ds, "xl": run_xl, "comm": run_comm}[which](rank, world, dist)
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -180,6 +180,16 @@ SIGNATURES = {
                                  c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_silu_mul": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     "sm100_ds_status": (c_uint32, []),
+    "sm100_comm_bytes": (c_uint64, [c_int32]),
+    "sm100_peer_alloc": (c_int, [c_uint64, POINTER(c_void_p), c_void_p]),
+    "sm100_peer_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "sm100_peer_close": (c_int, [c_void_p]),
+    "sm100_peer_free": (c_int, [c_void_p]),
+    "sm100_comm_set_peers": (c_int, [c_void_p, POINTER(c_void_p), c_int32]),
+    "sm100_comm_allreduce_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                             c_int32, c_float, c_void_p]),
+    "sm100_comm_pick": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
+    "sm100_comm_status": (c_uint32, []),
     "sm100_custom_program": (c_int32, [ctypes.c_char_p, ctypes.c_char_p, POINTER(c_uint32), POINTER(c_uint32),
                                        c_uint32]),
     "sm100_custom_dispatch": (c_int, [c_int32, POINTER(c_uint32), c_uint32, c_uint32, c_uint32]),

@@ -35,7 +35,12 @@ Parallelism over R ranks (rank r), every weight byte read by one rank:
 The residual stream h is replicated: after each all-reduce every rank holds
 the same h.  Rank 0 adds its partial sums into h; the other ranks overwrite
 h with theirs (or zero it before the experts add into it), so the all-reduce
-sum is h + sum of the partials.
+sum is h + sum of the partials.  Each all-reduce is the library's
+peer-memory kernel fused with the RMSNorm that consumes h (thvm_b200/comm.py,
+sm100_comm_allreduce_rmsnorm: the ranks' rows summed in rank order, the same
+h on every rank), and the argmax candidates meet in sm100_comm_pick, so a
+step issues no library collective; torch.distributed only exchanges the IPC
+handles at set-up.
 """
 from __future__ import annotations
 
@@ -257,6 +262,11 @@ class DSModel:
         self.counters = z(max(Vl, self.n_qkva, 2 * DIl, D) // 128 + 2, dt=torch.int32)
         self._args = L.Sm100SkinnyArgs()
         self.launches = 0
+        self.comm = None
+        if shard.world > 1:
+            from .comm import PeerComm
+            self.comm = PeerComm(shard.rank, shard.world, D, group)
+        self._pending = False   # h holds this rank's partial sums until the next norm's all-reduce
 
     def _stream(self):
         return ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
@@ -275,18 +285,30 @@ class DSModel:
         self.launches += 1
 
     def _rms(self, g, D):
-        L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
-                                          self.cfg.eps, self._stream()), "ds_rmsnorm")
+        """xn = bf16(rms(h) * g); when h holds partial sums, the all-reduce
+        over the ranks is fused into the same kernel."""
+        if self._pending:
+            self.comm.allreduce_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                        self.cfg.eps, self._stream())
+            self._pending = False
+        else:
+            L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                              self.cfg.eps, self._stream()), "ds_rmsnorm")
         self.launches += 1
 
     def _all_reduce(self):
-        if self.sh.world > 1:
-            self.torch.distributed.all_reduce(self.h, group=self.group)
+        self._pending = self.sh.world > 1
 
     def status(self) -> int:
-        """The kernels' sticky status word (non-zero: a bounded wait gave up or an
-        expert met more than 32 slots); synchronises the device and clears it."""
-        return int(self.lib.sm100_ds_status())
+        """The kernels' sticky status words (non-zero: a bounded wait gave up or an
+        expert met more than 32 slots); synchronises the device and clears them."""
+        s = int(self.lib.sm100_ds_status())
+        return s | (int(self.comm.status()) << 8 if self.comm is not None else 0)
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def step(self):
         """One decode step: ids in self.tok at row self.pos -> next ids, pos + 1."""
@@ -342,10 +364,9 @@ class DSModel:
                                     sh.v0, 0, st()), "xl_argmax")
         self.launches += 1
         if sh.world > 1:
-            dist = self.torch.distributed
-            dist.all_gather_into_tensor(self.vals.view(-1), self.val_me, group=self.group)
-            dist.all_gather_into_tensor(self.idxs.view(-1), self.idx_me, group=self.group)
-        L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), sh.world, B, self.tok.data_ptr(), st()),
-                "xl_pick")
+            self.comm.pick(self.val_me.data_ptr(), self.idx_me.data_ptr(), B, self.tok.data_ptr(), st())
+        else:
+            L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(), st()),
+                    "xl_pick")
         L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, st()), "pos_add")
         self.launches += 2
