@@ -509,9 +509,10 @@ int sm100_peer_free(void *dptr);
 int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t world);
 /* h [rows, cols] f32 holds this rank's partial sums; afterwards h = the sum of
  * every rank's partials in rank order (the same on every rank) and y (bf16)
- * = h * rsqrt(mean(h^2) + eps) * g per row */
+ * = h * rsqrt(mean(h^2) + eps) * g per row; with zero_rest != 0 the ranks
+ * other than 0 keep zeros in h instead (y is the same) */
 int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
-                                 int32_t rows, int32_t cols, float eps, void *stream);
+                                 int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream);
 /* tok[b] = the index of the largest val over the ranks' (val[b], idx[b])
  * (ties: the smaller index) */
 int sm100_comm_pick(const float *val, const int32_t *idx, void *own, int32_t rank, int32_t world, int32_t rows,

@@ -32,7 +32,7 @@ def test_one_rank_allreduce_is_the_rmsnorm(device):
     y = torch.zeros(B, D, dtype=torch.bfloat16, device="cuda")
     for _ in range(3):   # epochs advance; every use sees its own row
         L.check(lib.sm100_comm_allreduce_rmsnorm(h.data_ptr(), gt.data_ptr(), y.data_ptr(), own, 0, 1, B, D, 1e-6,
-                                                 None), "allreduce_rmsnorm")
+                                                 0, None), "allreduce_rmsnorm")
     torch.cuda.synchronize()
     assert lib.sm100_comm_status() == 0
     np.testing.assert_array_equal(h.cpu().numpy(), h0)
@@ -51,8 +51,8 @@ def test_missing_rank_times_out_with_status(device):
     g = torch.ones(D, device="cuda")
     y = torch.zeros(B, D, dtype=torch.bfloat16, device="cuda")
     lib.sm100_comm_status()
-    L.check(lib.sm100_comm_allreduce_rmsnorm(h.data_ptr(), g.data_ptr(), y.data_ptr(), own, 0, 2, B, D, 1e-6, None),
-            "allreduce_rmsnorm")
+    L.check(lib.sm100_comm_allreduce_rmsnorm(h.data_ptr(), g.data_ptr(), y.data_ptr(), own, 0, 2, B, D, 1e-6, 0,
+                                             None), "allreduce_rmsnorm")
     assert lib.sm100_comm_status() != 0   # gave up waiting for rank 1
     assert lib.sm100_comm_status() == 0   # and the word was cleared
     z = torch.arange(8, device="cuda") * 2   # the context still runs work

@@ -138,6 +138,13 @@ def run_comm(rank, world, dist):
         for r in range(1, world):
             want = want + parts[r]
         assert np.array_equal(h.cpu().numpy(), want), use
+        # zero_rest: the same y, and zeros in h on the ranks other than 0
+        y0 = y.clone()
+        h = torch.from_numpy(parts[rank].copy()).cuda()
+        comm.allreduce_rmsnorm(h.data_ptr(), g.data_ptr(), y.data_ptr(), B, D, 1e-6, st, zero_rest=True)
+        torch.cuda.synchronize()
+        assert torch.equal(y, y0)
+        assert np.array_equal(h.cpu().numpy(), want if rank == 0 else np.zeros_like(want)), use
     val = torch.full((B,), float(rank % 2), device="cuda")            # ranks 1, 3, .. hold the maximum
     idx = torch.arange(B, dtype=torch.int32, device="cuda") + 1000 * (world - rank)   # the last of them the smallest index
     tok = torch.zeros(B, dtype=torch.int32, device="cuda")

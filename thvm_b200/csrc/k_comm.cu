@@ -9,7 +9,9 @@
 //       rank's buffer, raises its flag there, waits for every rank's flag in
 //       its own buffer, sums the slots in rank order (so every rank computes
 //       the same h, bit for bit, independent of arrival order), stores h and
-//       y = bf16(h * rsqrt(mean(h^2) + eps) * g).
+//       y = bf16(h * rsqrt(mean(h^2) + eps) * g); with zero_rest the ranks
+//       other than 0 store zeros into h instead (their next partial sums
+//       accumulate from zero, rank 0's from the residual).
 //   sm100_comm_pick  the vocabulary-split argmax: every rank's (max, index)
 //       per row gathered the same way, the largest value with the smallest
 //       index wins (the reference's first-index rule).
@@ -68,7 +70,7 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t e) {
 }
 
 __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const float *g, __nv_bfloat16 *y, char *own,
-                                                            int rank, int R, int cols, float eps) {
+                                                            int rank, int R, int cols, float eps, int zero_rest) {
   __shared__ uint32_t s_e;
   __shared__ float red[8];
   pdl_trigger();
@@ -111,6 +113,7 @@ __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const floa
     reinterpret_cast<float4 *>(h + (int64_t)b * cols)[i] = a;
     ss += a.x * a.x + a.y * a.y + a.z * a.z + a.w * a.w;
   }
+  __syncthreads();
   ss = warp_sum(ss);
   if ((t & 31) == 0) red[t >> 5] = ss;
   __syncthreads();
@@ -118,12 +121,15 @@ __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const floa
 #pragma unroll
   for (int w = 0; w < 8; w++) tot += red[w];
   const float inv = 1.0f / sqrtf(tot * (1.0f / (float)cols) + eps);
+  const bool zero = zero_rest && rank != 0;
   for (int i = t; i < n4; i += 256) {
-    const float4 a = reinterpret_cast<const float4 *>(h + (int64_t)b * cols)[i];
+    float4 *hp = reinterpret_cast<float4 *>(h + (int64_t)b * cols) + i;
+    const float4 a = *hp;
     const float4 gg = reinterpret_cast<const float4 *>(g)[i];
     __nv_bfloat162 *yo = reinterpret_cast<__nv_bfloat162 *>(y + (int64_t)b * cols + 4 * i);
     yo[0] = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
     yo[1] = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
+    if (zero) *hp = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (t == 0) *epoch = e;
 }
@@ -224,13 +230,13 @@ extern "C" int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t w
 }
 
 extern "C" int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
-                                            int32_t rows, int32_t cols, float eps, void *stream) {
+                                            int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream) {
   if (!h || !g || !y || !own || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 ||
       rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 || ((uintptr_t)h | (uintptr_t)g | (uintptr_t)y) % 16)
     return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
                                           "16-byte aligned)", rank, world, rows, cols, kMaxRows);
   const cudaError_t e = launch_pdl(allreduce_rms_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
-                                   (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps);
+                                   (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, zero_rest);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm: %s", cudaGetErrorString(e));
   return launch_status("comm_allreduce_rmsnorm");
 }

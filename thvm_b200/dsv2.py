@@ -284,12 +284,13 @@ class DSModel:
         L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
         self.launches += 1
 
-    def _rms(self, g, D):
+    def _rms(self, g, D, zero_rest=False):
         """xn = bf16(rms(h) * g); when h holds partial sums, the all-reduce
-        over the ranks is fused into the same kernel."""
+        over the ranks is fused into the same kernel (zero_rest: ranks other
+        than 0 keep zeros in h, for partial sums that accumulate into it)."""
         if self._pending:
             self.comm.allreduce_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
-                                        self.cfg.eps, self._stream())
+                                        self.cfg.eps, self._stream(), zero_rest)
             self._pending = False
         else:
             L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
@@ -335,7 +336,8 @@ class DSModel:
             # the o projection's partial sums: rank 0 into the residual, the others over it
             self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
             self._all_reduce()
-            self._rms(w[p + "ffn_norm"], D)
+            # the experts add into h: on ranks other than 0 it must start from zero
+            self._rms(w[p + "ffn_norm"], D, zero_rest=l >= cfg.n_dense)
             if l < cfg.n_dense:
                 self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DIl)
                 L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DIl, st()), "ds_silu_mul")
@@ -349,9 +351,8 @@ class DSModel:
                                        self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
                                        self.slot_w.data_ptr(), st()), "ds_route")
             # one launch pair over the local routed experts and shared halves (contiguous in this rank's
-            # arrays), adding into the residual on rank 0 and into a zeroed h on the others
-            if not first:
-                self.h.zero_()
+            # arrays), adding into the residual on rank 0 and into the zeros the all-reduce left in h on
+            # the others
             L.check(lib.sm100_ds_experts(self.xn.data_ptr(), w[p + "e_gu"].data_ptr(), w[p + "e_gu_s"].data_ptr(),
                                          w[p + "e_d"].data_ptr(), w[p + "e_d_s"].data_ptr(), self.slot_off.data_ptr(),
                                          self.slot_tok.data_ptr(), self.slot_w.data_ptr(), self.a.data_ptr(),
