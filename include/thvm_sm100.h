@@ -448,10 +448,6 @@ int sm100_xl_pick(const float *val, const int32_t *idx, int32_t R, int32_t B, in
  * experts with 128 x 128 f32 block scales.  Device pointers; launch on stream. */
 /* y (bf16) = x * rsqrt(mean(x^2) + eps) * g per row */
 int sm100_ds_rmsnorm(const float *x, const float *g, void *y, int32_t M, int32_t D, float eps, void *stream);
-/* the same RMSNorm with the router product fused: also logits [M][E] =
- * y . router[e] (bf16 router [E][D], f32 sums); D % 8 == 0, D <= 8192 */
-int sm100_ds_rmsnorm_router(const float *x, const float *g, void *y, const void *router, float *logits, int32_t M,
-                            int32_t D, int32_t E, float eps, void *stream);
 /* h[b] = emb[tok[b]] (bf16 table; ids outside [0, V) read zeros) */
 int sm100_ds_embed(const void *emb, const int32_t *tok, float *h, int32_t B, int32_t V, int32_t D, void *stream);
 /* q rows [H][DN + DR] -> q_out bf16 (pe rotated by the cos / sin tables [ctx][DR]
@@ -514,11 +510,9 @@ int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t world);
 /* h [rows, cols] f32 holds this rank's partial sums; afterwards h = the sum of
  * every rank's partials in rank order (the same on every rank) and y (bf16)
  * = h * rsqrt(mean(h^2) + eps) * g per row; with zero_rest != 0 the ranks
- * other than 0 keep zeros in h instead (y is the same); with a router (bf16
- * [E][cols], else NULL) also logits [rows][E] = y . router[e] */
+ * other than 0 keep zeros in h instead (y is the same) */
 int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
-                                 int32_t rows, int32_t cols, float eps, int32_t zero_rest, const void *router,
-                                 float *logits, int32_t E, void *stream);
+                                 int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream);
 /* tok[b] = the index of the largest val over the ranks' (val[b], idx[b])
  * (ties: the smaller index) */
 int sm100_comm_pick(const float *val, const int32_t *idx, void *own, int32_t rank, int32_t world, int32_t rows,

@@ -36,11 +36,9 @@ class PeerComm:
         L.check(self.lib.sm100_comm_set_peers(self.own, (ctypes.c_void_p * world)(*ptrs), world), "comm_set_peers")
         dist.barrier(group=group)   # every table is written before any rank's first exchange
 
-    def allreduce_rmsnorm(self, h, g, y, rows: int, cols: int, eps: float, stream, zero_rest: bool = False,
-                          router=None, logits=None, n_router: int = 0):
+    def allreduce_rmsnorm(self, h, g, y, rows: int, cols: int, eps: float, stream, zero_rest: bool = False):
         L.check(self.lib.sm100_comm_allreduce_rmsnorm(h, g, y, self.own, self.rank, self.world, rows, cols, eps,
-                                                      int(zero_rest), router, logits, n_router, stream),
-                "comm_allreduce_rmsnorm")
+                                                      int(zero_rest), stream), "comm_allreduce_rmsnorm")
 
     def pick(self, val, idx, rows: int, tok, stream):
         L.check(self.lib.sm100_comm_pick(val, idx, self.own, self.rank, self.world, rows, tok, stream), "comm_pick")

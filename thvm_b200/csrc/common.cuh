@@ -103,29 +103,6 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// logits[e] = sum_k y[k] * w[e][k] for one bf16 row y [D] in shared memory
-// against bf16 weights w [E][D] (f32 products and a warp-tree sum): one warp
-// per output, 16-byte loads; D % 8 == 0, rows 16-byte aligned.
-__device__ __forceinline__ void row_logits(const __nv_bfloat16 *ys, const __nv_bfloat16 *w, float *logits, int E,
-                                           int D) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  for (int e = warp; e < E; e += nw) {
-    const __nv_bfloat16 *we = w + (int64_t)e * D;
-    float acc = 0.0f;
-    for (int k = lane * 8; k < D; k += 256) {
-      const uint4 wv = *reinterpret_cast<const uint4 *>(we + k), yv = *reinterpret_cast<const uint4 *>(ys + k);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, yy[4] = {yv.x, yv.y, yv.z, yv.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        acc = fmaf(__uint_as_float(yy[j] << 16), __uint_as_float(ww[j] << 16), acc);
-        acc = fmaf(__uint_as_float(yy[j] & 0xFFFF0000u), __uint_as_float(ww[j] & 0xFFFF0000u), acc);
-      }
-    }
-    acc = warp_sum(acc);
-    if (lane == 0) logits[e] = acc;
-  }
-}
-
 // Block-wide sum / max over blockDim.x threads (a multiple of 32, <= 1024).
 // `red` is >= 32 floats of shared memory; every thread gets the result.
 __device__ __forceinline__ float block_sum(float v, float *red) {

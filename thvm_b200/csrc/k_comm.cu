@@ -11,8 +11,7 @@
 //       the same h, bit for bit, independent of arrival order), stores h and
 //       y = bf16(h * rsqrt(mean(h^2) + eps) * g); with zero_rest the ranks
 //       other than 0 store zeros into h instead (their next partial sums
-//       accumulate from zero, rank 0's from the residual); with a router the
-//       row's router logits y . router[e] follow from y in shared memory.
+//       accumulate from zero, rank 0's from the residual).
 //   sm100_comm_pick  the vocabulary-split argmax: every rank's (max, index)
 //       per row gathered the same way, the largest value with the smallest
 //       index wins (the reference's first-index rule).
@@ -71,11 +70,9 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t e) {
 }
 
 __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const float *g, __nv_bfloat16 *y, char *own,
-                                                            int rank, int R, int cols, float eps, int zero_rest,
-                                                            const __nv_bfloat16 *router, float *logits, int E) {
+                                                            int rank, int R, int cols, float eps, int zero_rest) {
   __shared__ uint32_t s_e;
   __shared__ float red[8];
-  __shared__ __align__(16) __nv_bfloat16 ys[kMaxCols];
   pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, t = threadIdx.x;
@@ -130,19 +127,11 @@ __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const floa
     const float4 a = *hp;
     const float4 gg = reinterpret_cast<const float4 *>(g)[i];
     __nv_bfloat162 *yo = reinterpret_cast<__nv_bfloat162 *>(y + (int64_t)b * cols + 4 * i);
-    const __nv_bfloat162 y0 = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
-    const __nv_bfloat162 y1 = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
-    yo[0] = y0;
-    yo[1] = y1;
-    reinterpret_cast<__nv_bfloat162 *>(ys)[2 * i] = y0;
-    reinterpret_cast<__nv_bfloat162 *>(ys)[2 * i + 1] = y1;
+    yo[0] = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
+    yo[1] = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
     if (zero) *hp = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (t == 0) *epoch = e;
-  if (router) {   // the router product of the normalised row (the MoE layers' ffn norm)
-    __syncthreads();
-    row_logits(ys, router, logits + (int64_t)b * E, E, cols);
-  }
 }
 
 __global__ void pick_kernel(const float *val, const int32_t *idx, char *own, int rank, int R, int rows, int32_t *tok) {
@@ -241,17 +230,13 @@ extern "C" int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t w
 }
 
 extern "C" int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
-                                            int32_t rows, int32_t cols, float eps, int32_t zero_rest,
-                                            const void *router, float *logits, int32_t E, void *stream) {
-  if (router && (!logits || E < 1 || cols % 8 || (uintptr_t)router % 16))
-    return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm: router needs logits, E >= 1, cols %% 8");
+                                            int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream) {
   if (!h || !g || !y || !own || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 ||
       rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 || ((uintptr_t)h | (uintptr_t)g | (uintptr_t)y) % 16)
     return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
                                           "16-byte aligned)", rank, world, rows, cols, kMaxRows);
   const cudaError_t e = launch_pdl(allreduce_rms_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
-                                   (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, zero_rest,
-                                   (const __nv_bfloat16 *)router, logits, E);
+                                   (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, zero_rest);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm: %s", cudaGetErrorString(e));
   return launch_status("comm_allreduce_rmsnorm");
 }

@@ -50,36 +50,6 @@ __global__ void __launch_bounds__(256) ds_rms_kernel(const float *x, const float
     y[(int64_t)blockIdx.x * D + i] = __float2bfloat16_rn((xr[i] * inv) * g[i]);
 }
 
-// The RMSNorm feeding the router, with the router product fused: y as above,
-// and logits[b][e] = y[b] . router[e] (bf16 x bf16, f32 sums) from the row
-// kept in shared memory.
-constexpr int kDsMaxD = 8192;
-__global__ void __launch_bounds__(256) ds_rms_router_kernel(const float *x, const float *g, __nv_bfloat16 *y,
-                                                            const __nv_bfloat16 *router, float *logits, int D, int E,
-                                                            float eps) {
-  __shared__ float red[8];
-  __shared__ __align__(16) __nv_bfloat16 ys[kDsMaxD];
-  pdl_trigger();
-  pdl_wait();
-  const float *xr = x + (int64_t)blockIdx.x * D;
-  float s = 0.0f;
-  for (int i = threadIdx.x; i < D; i += 256) s += xr[i] * xr[i];
-  s = warp_sum(s);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
-  __syncthreads();
-  float t = 0.0f;
-#pragma unroll
-  for (int w = 0; w < 8; w++) t += red[w];
-  const float inv = 1.0f / sqrtf(t * (1.0f / (float)D) + eps);
-  for (int i = threadIdx.x; i < D; i += 256) {
-    const __nv_bfloat16 v = __float2bfloat16_rn((xr[i] * inv) * g[i]);
-    ys[i] = v;
-    y[(int64_t)blockIdx.x * D + i] = v;
-  }
-  __syncthreads();
-  row_logits(ys, router, logits + (int64_t)blockIdx.x * E, E, D);
-}
-
 // h[b] = embed[tok[b]] (bf16 table; ids outside [0, V) read zeros)
 __global__ void ds_embed_kernel(const __nv_bfloat16 *emb, const int32_t *tok, float *h, int V, int D) {
   pdl_trigger();
@@ -938,15 +908,6 @@ extern "C" int sm100_ds_rmsnorm(const float *x, const float *g, void *y, int32_t
   if (!x || !g || !y || M < 1 || D < 1) return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm: bad arguments");
   DS_LAUNCH("ds_rmsnorm", ds_rms_kernel, dim3(M), dim3(256), 0, (cudaStream_t)stream, x, g, (__nv_bfloat16 *)y, D,
             eps);
-}
-
-extern "C" int sm100_ds_rmsnorm_router(const float *x, const float *g, void *y, const void *router, float *logits,
-                                       int32_t M, int32_t D, int32_t E, float eps, void *stream) {
-  if (!x || !g || !y || !router || !logits || M < 1 || D < 8 || D > kDsMaxD || D % 8 || E < 1 ||
-      (uintptr_t)router % 16 || (uintptr_t)y % 16)
-    return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm_router: bad arguments (D %% 8, D <= %d, aligned)", kDsMaxD);
-  DS_LAUNCH("ds_rmsnorm_router", ds_rms_router_kernel, dim3(M), dim3(256), 0, (cudaStream_t)stream, x, g,
-            (__nv_bfloat16 *)y, (const __nv_bfloat16 *)router, logits, D, E, eps);
 }
 
 extern "C" int sm100_ds_embed(const void *emb, const int32_t *tok, float *h, int32_t B, int32_t V, int32_t D,

@@ -16,9 +16,8 @@ kernel with weight 1.
 Per layer: RMSNorm -> fused q | kv_a projection (skinny tcgen05 GEMM) ->
 q / latent post-processing (bf16, RMSNorm of the latent, YaRN rotary, cache
 append) -> absorbed MLA over the compressed cache -> o projection into the
-residual -> RMSNorm -> dense MLP (layer 0) or, in the MoE layers, the
-router product (fused into the RMSNorm kernel), routing, fp8 experts (gate /
-up + SiLU, then down weighted into the residual).
+residual -> RMSNorm -> dense MLP (layer 0) or router GEMM, routing, fp8
+experts (gate / up + SiLU, then down weighted into the residual).
 
 Parallelism over R ranks (rank r), every weight byte read by one rank:
   * attention by heads: heads split_even(16, R, r); the q rows of those
@@ -285,24 +284,17 @@ class DSModel:
         L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
         self.launches += 1
 
-    def _rms(self, g, D, zero_rest=False, router=None):
-        """xn = bf16(rms(h) * g); with a router also its logits into self.rl
-        (the router product fused into the norm kernel).  When h holds partial
-        sums, the all-reduce over the ranks is fused into the same kernel
-        (zero_rest: ranks other than 0 keep zeros in h, for partial sums that
-        accumulate into it)."""
-        cfg, st = self.cfg, self._stream()
-        rp, lp = (router.data_ptr(), self.rl.data_ptr()) if router is not None else (None, None)
+    def _rms(self, g, D, zero_rest=False):
+        """xn = bf16(rms(h) * g); when h holds partial sums, the all-reduce
+        over the ranks is fused into the same kernel (zero_rest: ranks other
+        than 0 keep zeros in h, for partial sums that accumulate into it)."""
         if self._pending:
-            self.comm.allreduce_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), cfg.batch, D, cfg.eps, st,
-                                        zero_rest, rp, lp, cfg.n_exp if router is not None else 0)
+            self.comm.allreduce_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                        self.cfg.eps, self._stream(), zero_rest)
             self._pending = False
-        elif router is not None:
-            L.check(self.lib.sm100_ds_rmsnorm_router(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), rp, lp,
-                                                     cfg.batch, D, cfg.n_exp, cfg.eps, st), "ds_rmsnorm_router")
         else:
-            L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), cfg.batch, D,
-                                              cfg.eps, st), "ds_rmsnorm")
+            L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                              self.cfg.eps, self._stream()), "ds_rmsnorm")
         self.launches += 1
 
     def _all_reduce(self):
@@ -344,10 +336,8 @@ class DSModel:
             # the o projection's partial sums: rank 0 into the residual, the others over it
             self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
             self._all_reduce()
-            # MoE layers: the router product rides the norm kernel, and the experts add into h, which
-            # on ranks other than 0 must start from zero
-            moe = l >= cfg.n_dense
-            self._rms(w[p + "ffn_norm"], D, zero_rest=moe, router=w[p + "router"] if moe else None)
+            # the experts add into h: on ranks other than 0 it must start from zero
+            self._rms(w[p + "ffn_norm"], D, zero_rest=l >= cfg.n_dense)
             if l < cfg.n_dense:
                 self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DIl)
                 L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DIl, st()), "ds_silu_mul")
@@ -355,6 +345,7 @@ class DSModel:
                 self._skinny(self.xn, w[p + "d_down"], self.h, DIl, D, residual=first)
                 self._all_reduce()
                 continue
+            self._skinny(self.xn, w[p + "router"], self.rl, D, E)
             ns = len(sh.shared)
             L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, ns, self.sel.data_ptr(),
                                        self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
