@@ -172,13 +172,13 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def ncu_traffic(kernel):
+def ncu_traffic(kernel, key="traffic_bytes_per_launch"):
     """DRAM bytes (read + write) of one launch of `kernel` from its committed
     ncu summary (a `traffic_bytes_per_launch:` line in profiles/<kernel>_*.md),
     or None when no capture of the current kernel is committed."""
     for p in sorted((ROOT / "profiles").glob(f"{kernel}_*.md")):
         for line in p.read_text().splitlines():
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith(key + ":"):
                 try:
                     return int(line.split(":", 1)[1].strip())
                 except ValueError:
@@ -398,12 +398,17 @@ def moe_run(args, ctx):
         slots = int(off[-1])
         kb = touched * ds_expert_bytes(cfg) + B * cfg.dim * 2 + 2 * slots * cfg.moe_inter * 2 + 2 * B * cfg.dim * 4
         ach = kb / (us / 1e6) / 1e9
-        traffic = ncu_traffic("ds_x8_kernel")
+        # the ncu capture's launch pair touched a different set of experts: its
+        # DRAM bytes per algorithmic byte, times this launch's algorithmic bytes
+        t_ncu, a_ncu = ncu_traffic("ds_x8_kernel"), ncu_traffic("ds_x8_kernel", "algorithmic_bytes_per_launch")
+        traffic = round(t_ncu / a_ncu * kb) if t_ncu and a_ncu else None
         roof = {"bound": "hbm", "kernel": "ds_x8_kernel<up> + ds_x8_kernel<down> (one MoE layer's fp8 experts)",
                 "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
                 "peak_source": peak_kind, "bytes_per_launch": kb, "avg_launch_us": round(us, 2),
                 "experts_touched": touched, "experts_local": n_local, "slots": slots,
-                "traffic": traffic, "traffic_note": "ncu dram bytes of the up + down pair, one layer",
+                "traffic": traffic,
+                "traffic_note": "ncu DRAM read + write bytes of one up + down pair (profiles/ds_x8_kernel_moe_config5.md) "
+                                "per algorithmic byte, times this pair's algorithmic bytes",
                 "step": {"algorithmic_bytes_per_step": byts // args.steps, "achieved_gbs": round(step_gbs, 1),
                          "peak_gbs": round(hbm * ctx.world, 1), "frac": round(step_gbs / (hbm * ctx.world), 4)}}
         del y

@@ -513,6 +513,10 @@ int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t world);
  * other than 0 keep zeros in h instead (y is the same) */
 int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
                                  int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream);
+/* the same exchange with LayerNorm: y = bf16((h - mean) * rsqrt(var + eps) * g
+ * + b), mean and biased variance in two passes (src/nn/layernorm.c:1-7) */
+int sm100_comm_allreduce_layernorm(float *h, const float *g, const float *b, void *y, void *own, int32_t rank,
+                                   int32_t world, int32_t rows, int32_t cols, float eps, void *stream);
 /* tok[b] = the index of the largest val over the ranks' (val[b], idx[b])
  * (ties: the smaller index) */
 int sm100_comm_pick(const float *val, const int32_t *idx, void *own, int32_t rank, int32_t world, int32_t rows,

@@ -121,7 +121,7 @@ def run_comm(rank, world, dist):
     """The peer collectives alone: the fused all-reduce + RMSNorm sums the
     ranks' rows in rank order (bit for bit what an f32 sum in that order
     gives), over several uses; the argmax pick takes the largest value, the
-    smaller index on ties across ranks."""
+    smaller index on ties across ranks; the LayerNorm variant sums alike."""
     import torch
     from thvm_b200.comm import PeerComm
     B, D = 32, 2048
@@ -152,6 +152,20 @@ def run_comm(rank, world, dist):
     torch.cuda.synchronize()
     best = max(r for r in range(world) if r % 2 == 1) if world > 1 else 0
     assert np.array_equal(tok.cpu().numpy(), np.arange(B) + 1000 * (world - best))
+    # the LayerNorm variant: the same sum, y within a bf16 rounding of the f64 LayerNorm
+    b = torch.from_numpy(np.random.default_rng(10).uniform(-0.5, 0.5, D).astype(np.float32)).cuda()
+    parts = [np.random.default_rng(700 + r).standard_normal((B, D)).astype(np.float32) for r in range(world)]
+    h = torch.from_numpy(parts[rank].copy()).cuda()
+    comm.allreduce_layernorm(h.data_ptr(), g.data_ptr(), b.data_ptr(), y.data_ptr(), B, D, 1e-5, st)
+    torch.cuda.synchronize()
+    want = parts[0].copy()
+    for r in range(1, world):
+        want = want + parts[r]
+    assert np.array_equal(h.cpu().numpy(), want)
+    w64 = want.astype(np.float64)
+    mu = w64.mean(1, keepdims=True)
+    ref = (w64 - mu) / np.sqrt(((w64 - mu) ** 2).mean(1, keepdims=True) + 1e-5) * g.cpu().numpy() + b.cpu().numpy()
+    np.testing.assert_allclose(y.float().cpu().numpy(), ref, rtol=2 ** -7, atol=2 ** -7)
     assert comm.status() == 0
     comm.close()
     if rank == 0:

@@ -188,6 +188,8 @@ SIGNATURES = {
     "sm100_comm_set_peers": (c_int, [c_void_p, POINTER(c_void_p), c_int32]),
     "sm100_comm_allreduce_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                              c_int32, c_float, c_int32, c_void_p]),
+    "sm100_comm_allreduce_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
+                                               c_int32, c_int32, c_float, c_void_p]),
     "sm100_comm_pick": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "sm100_comm_status": (c_uint32, []),
     "sm100_custom_program": (c_int32, [ctypes.c_char_p, ctypes.c_char_p, POINTER(c_uint32), POINTER(c_uint32),

@@ -40,6 +40,10 @@ class PeerComm:
         L.check(self.lib.sm100_comm_allreduce_rmsnorm(h, g, y, self.own, self.rank, self.world, rows, cols, eps,
                                                       int(zero_rest), stream), "comm_allreduce_rmsnorm")
 
+    def allreduce_layernorm(self, h, g, b, y, rows: int, cols: int, eps: float, stream):
+        L.check(self.lib.sm100_comm_allreduce_layernorm(h, g, b, y, self.own, self.rank, self.world, rows, cols, eps,
+                                                        stream), "comm_allreduce_layernorm")
+
     def pick(self, val, idx, rows: int, tok, stream):
         L.check(self.lib.sm100_comm_pick(val, idx, self.own, self.rank, self.world, rows, tok, stream), "comm_pick")
 

@@ -12,6 +12,8 @@
 //       y = bf16(h * rsqrt(mean(h^2) + eps) * g); with zero_rest the ranks
 //       other than 0 store zeros into h instead (their next partial sums
 //       accumulate from zero, rank 0's from the residual).
+//   sm100_comm_allreduce_layernorm  the same exchange fused with a LayerNorm
+//       (y = bf16((h - mean) * rsqrt(var + eps) * g + b), two passes).
 //   sm100_comm_pick  the vocabulary-split argmax: every rank's (max, index)
 //       per row gathered the same way, the largest value with the smallest
 //       index wins (the reference's first-index rule).
@@ -69,8 +71,10 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t e) {
   return true;
 }
 
-__global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const float *g, __nv_bfloat16 *y, char *own,
-                                                            int rank, int R, int cols, float eps, int zero_rest) {
+template <bool kLN>
+__global__ void __launch_bounds__(256) allreduce_norm_kernel(float *h, const float *g, const float *bt,
+                                                             __nv_bfloat16 *y, char *own, int rank, int R, int cols,
+                                                             float eps, int zero_rest) {
   __shared__ uint32_t s_e;
   __shared__ float red[8];
   pdl_trigger();
@@ -120,15 +124,56 @@ __global__ void __launch_bounds__(256) allreduce_rms_kernel(float *h, const floa
   float tot = 0.0f;
 #pragma unroll
   for (int w = 0; w < 8; w++) tot += red[w];
-  const float inv = 1.0f / sqrtf(tot * (1.0f / (float)cols) + eps);
+  const float inv_n = 1.0f / (float)cols;
+  float mean = 0.0f, inv;
+  if constexpr (kLN) {
+    // LayerNorm: ss above summed squares; the reference's two passes instead:
+    // mean = sum * (1/D), then the biased variance of (h - mean)
+    // (src/nn/layernorm.c:1-7), over the row this thread just wrote
+    float sum = 0.0f;
+    for (int i = t; i < n4; i += 256) {
+      const float4 a = reinterpret_cast<const float4 *>(h + (int64_t)b * cols)[i];
+      sum += (a.x + a.y) + (a.z + a.w);
+    }
+    sum = warp_sum(sum);
+    __syncthreads();
+    if ((t & 31) == 0) red[t >> 5] = sum;
+    __syncthreads();
+    float st = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) st += red[w];
+    mean = st * inv_n;
+    float v = 0.0f;
+    for (int i = t; i < n4; i += 256) {
+      const float4 a = reinterpret_cast<const float4 *>(h + (int64_t)b * cols)[i];
+      const float c0 = a.x - mean, c1 = a.y - mean, c2 = a.z - mean, c3 = a.w - mean;
+      v += (c0 * c0 + c1 * c1) + (c2 * c2 + c3 * c3);
+    }
+    v = warp_sum(v);
+    __syncthreads();
+    if ((t & 31) == 0) red[t >> 5] = v;
+    __syncthreads();
+    float vt = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) vt += red[w];
+    inv = 1.0f / sqrtf(vt * inv_n + eps);
+  } else {
+    inv = 1.0f / sqrtf(tot * inv_n + eps);
+  }
   const bool zero = zero_rest && rank != 0;
   for (int i = t; i < n4; i += 256) {
     float4 *hp = reinterpret_cast<float4 *>(h + (int64_t)b * cols) + i;
     const float4 a = *hp;
     const float4 gg = reinterpret_cast<const float4 *>(g)[i];
     __nv_bfloat162 *yo = reinterpret_cast<__nv_bfloat162 *>(y + (int64_t)b * cols + 4 * i);
-    yo[0] = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
-    yo[1] = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
+    if constexpr (kLN) {
+      const float4 bb = reinterpret_cast<const float4 *>(bt)[i];
+      yo[0] = __floats2bfloat162_rn((a.x - mean) * inv * gg.x + bb.x, (a.y - mean) * inv * gg.y + bb.y);
+      yo[1] = __floats2bfloat162_rn((a.z - mean) * inv * gg.z + bb.z, (a.w - mean) * inv * gg.w + bb.w);
+    } else {
+      yo[0] = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
+      yo[1] = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
+    }
     if (zero) *hp = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (t == 0) *epoch = e;
@@ -235,10 +280,25 @@ extern "C" int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, v
       rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 || ((uintptr_t)h | (uintptr_t)g | (uintptr_t)y) % 16)
     return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
                                           "16-byte aligned)", rank, world, rows, cols, kMaxRows);
-  const cudaError_t e = launch_pdl(allreduce_rms_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
-                                   (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, zero_rest);
+  const cudaError_t e = launch_pdl(allreduce_norm_kernel<false>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
+                                   (const float *)nullptr, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps,
+                                   zero_rest);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm: %s", cudaGetErrorString(e));
   return launch_status("comm_allreduce_rmsnorm");
+}
+
+extern "C" int sm100_comm_allreduce_layernorm(float *h, const float *g, const float *b, void *y, void *own,
+                                              int32_t rank, int32_t world, int32_t rows, int32_t cols, float eps,
+                                              void *stream) {
+  if (!h || !g || !b || !y || !own || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 ||
+      rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 ||
+      ((uintptr_t)h | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) % 16)
+    return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_layernorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
+                                          "16-byte aligned)", rank, world, rows, cols, kMaxRows);
+  const cudaError_t e = launch_pdl(allreduce_norm_kernel<true>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
+                                   b, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, 0);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_layernorm: %s", cudaGetErrorString(e));
+  return launch_status("comm_allreduce_layernorm");
 }
 
 extern "C" int sm100_comm_pick(const float *val, const int32_t *idx, void *own, int32_t rank, int32_t world,

@@ -18,10 +18,14 @@ c_proj the matching input columns), a slice of the MLP hidden units (c_fc
 rows, mlp c_proj columns) and a slice of the vocabulary (lm_head rows).  The
 row-split projections leave partial sums: rank 0 adds bias and residual in
 its GEMM epilogue, the others overwrite their copy of h with their partial,
-and one all-reduce (sum) per block restores the same h everywhere.  The
-token pick all-gathers each rank's (max, index) pair and takes the largest
-(ties: smaller index).  PyTorch provides device memory, the stream, CUDA
-graphs and torch.distributed (NCCL); every kernel is the library's.
+and one all-reduce (sum) per block restores the same h everywhere: the
+library's peer-memory kernel fused with the LayerNorm that consumes h
+(thvm_b200/comm.py, sm100_comm_allreduce_layernorm: the ranks' rows summed
+in rank order).  The token pick gathers each rank's (max, index) pair over
+peer memory and takes the largest (ties: smaller index).  PyTorch provides
+device memory, the stream and CUDA graphs, and torch.distributed exchanges
+the IPC handles at set-up; every kernel and collective of a step is the
+library's.
 """
 from __future__ import annotations
 
@@ -178,6 +182,11 @@ class XLModel:
         self.counters = z(max(3 * C, Fl, D, Vl) // 128 + 1, dt=torch.int32)
         self._args = L.Sm100SkinnyArgs()
         self.launches = 0
+        self.comm = None
+        if shard.world > 1:
+            from .comm import PeerComm
+            self.comm = PeerComm(shard.rank, shard.world, D, group)
+        self._pending = False   # h holds this rank's partial sums until the next LayerNorm's all-reduce
 
     # -- one launcher per kernel ------------------------------------------------
     def _stream(self):
@@ -203,6 +212,14 @@ class XLModel:
         self.launches += 1
 
     def _ln(self, g, b, zero_h=False, zero_buf=None):
+        """xa = bf16(LayerNorm(h) * g + b); when h holds partial sums, the
+        all-reduce over the ranks is fused into the same kernel (peer memory)."""
+        if self._pending:
+            self.comm.allreduce_layernorm(self.h.data_ptr(), g.data_ptr(), b.data_ptr(), self.xa.data_ptr(),
+                                          self.cfg.batch, self.cfg.dim, self.cfg.norm_eps, self._stream())
+            self._pending = False
+            self.launches += 1
+            return
         zp, zn = (zero_buf.data_ptr(), zero_buf.numel()) if zero_buf is not None else (None, 0)
         L.check(self.lib.sm100_xl_layernorm(self.h.data_ptr(), g.data_ptr(), b.data_ptr(), self.xa.data_ptr(),
                                             self.cfg.batch, self.cfg.dim, self.cfg.norm_eps, 1 if zero_h else 0,
@@ -211,8 +228,12 @@ class XLModel:
         self.launches += 1
 
     def _all_reduce(self, t):
-        if self.sh.world > 1:
-            self.torch.distributed.all_reduce(t, group=self.group)
+        self._pending = self.sh.world > 1
+
+    def close(self):
+        if self.comm is not None:
+            self.comm.close()
+            self.comm = None
 
     def step(self):
         """One decode step: ids in self.tok at row self.pos -> next ids in self.tok, pos + 1."""
@@ -249,10 +270,9 @@ class XLModel:
                                     self.idx_me.data_ptr(), sh.v0, 0, self._stream()), "xl_argmax")
         self.launches += 1
         if sh.world > 1:
-            dist = self.torch.distributed
-            dist.all_gather_into_tensor(self.vals.view(-1), self.val_me, group=self.group)
-            dist.all_gather_into_tensor(self.idxs.view(-1), self.idx_me, group=self.group)
-        L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), sh.world, B, self.tok.data_ptr(),
-                                  self._stream()), "xl_pick")
+            self.comm.pick(self.val_me.data_ptr(), self.idx_me.data_ptr(), B, self.tok.data_ptr(), self._stream())
+        else:
+            L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(),
+                                      self._stream()), "xl_pick")
         L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, self._stream()), "pos_add")
         self.launches += 2
