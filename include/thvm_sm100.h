@@ -256,9 +256,12 @@ int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
  * counters with cudaMemsetAsync on `stream` before each launch.  The first
  * call on a device looks up the array's device address (cudaGetSymbolAddress,
  * which may load the module), so make that first call before any stream
- * capture.  Every call shares the one array: calls that can overlap on the
- * GPU (other streams, other host threads) race and must be serialised by the
- * caller. */
+ * capture.  The address is kept per device ordinal for the life of the
+ * process: after cudaDeviceReset (which unloads this library's module from
+ * that device) the kept address is stale, so do not use this entry point on
+ * a device that was reset.  Every call shares the one array: calls that can
+ * overlap on the GPU (other streams, other host threads) race and must be
+ * serialised by the caller. */
 #define SM100_ARGMAX_NOALLOC_MAX_ROWS 64
 int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
                          int32_t *bump, void *stream);
@@ -462,13 +465,22 @@ int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, const float 
 int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c, const void *cache_pe,
                  const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV,
                  int32_t ctx, float scale, void *stream);
-/* softmax over E <= 64 router logits, the K largest (ties: lowest id), no
- * renormalisation; sel / wsel [B][K]; slot lists of the experts [e0, e1)
+/* the K largest of E <= 64 router logits (ties: lowest id) weighted by their
+ * softmax probabilities, no renormalisation (the reference's route kernel,
+ * bench/dsv2_decode_bench.c:787-863); sel / wsel [B][K]; slot lists of the
+ * experts [e0, e1)
  * followed by n_shared experts taking every token with weight 1:
  * slot_off [e1 - e0 + n_shared + 1], slot_tok / slot_w [B * (K + n_shared)]
  * (expert-major) */
 int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared,
                    int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
+/* the router product and the routing in one launch: logits [B][E] = x .
+ * router[e] (x, router bf16 [B][D], [E][D]; f32 sums), then the routing of
+ * sm100_ds_route; counter is one int32 of device memory that starts at zero
+ * and is left at zero (the launch's CTAs count themselves off on it) */
+int sm100_ds_router_route(const void *x, const void *router, float *logits, int32_t *counter, int32_t D, int32_t E,
+                          int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared, int32_t *sel, float *wsel,
+                          int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
 /* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
  * experts on the tensor cores, fp8 x fp8: the weights stream by TMA as the
  * MMA's e4m3 operand; each token's row times the 128 x 128 block scale and

@@ -100,6 +100,46 @@ def test_ds_route_matches_oracle_rule():
         assert np.all(sw.cpu().numpy()[o[E + k]:o[E + k + 1]] == 1.0)
 
 
+def test_ds_router_route_matches_oracle_rule():
+    """The router product and the routing in one launch (sm100_ds_router_route):
+    its logits within 1e-5 of the f64 product of the bf16 operands, its
+    choices the oracle's rule on those logits, the slot lists as
+    sm100_ds_route builds them from the same logits, twice in a row (the
+    launch leaves its CTA counter at zero)."""
+    import ctypes
+    import torch
+    from thvm_b200 import _lib as L
+    lib = L.lib()
+    B, E, K, D, NS = 32, 64, 6, 2048, 2
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = (torch.randn(B, D, generator=g, device="cuda")).to(torch.bfloat16)
+    w = (torch.randn(E, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    z = lambda n, dt=torch.float32: torch.zeros(n, dtype=dt, device="cuda")
+    logits, counter = z(B * E), z(1, torch.int32)
+    outs = [(z(B * K, torch.int32), z(B * K), z(E + NS + 1, torch.int32), z(B * (K + NS), torch.int32),
+             z(B * (K + NS))) for _ in range(2)]
+    for sel, wsel, off, stok, sw in outs:
+        L.check(lib.sm100_ds_router_route(x.data_ptr(), w.data_ptr(), logits.data_ptr(), counter.data_ptr(), D, E, K,
+                                          B, 0, E, NS, sel.data_ptr(), wsel.data_ptr(), off.data_ptr(),
+                                          stok.data_ptr(), sw.data_ptr(), ctypes.c_void_p(0)), "ds_router_route")
+    torch.cuda.synchronize()
+    assert int(counter.item()) == 0
+    lg = logits.cpu().numpy().reshape(B, E)
+    want = x.double().cpu().numpy() @ w.double().cpu().numpy().T
+    np.testing.assert_allclose(lg, want, rtol=0, atol=1e-5 * np.abs(want).max())
+    ref, ref_w = O.ds_route(lg, K)
+    ref_outs = (z(B * K, torch.int32), z(B * K), z(E + NS + 1, torch.int32), z(B * (K + NS), torch.int32),
+                z(B * (K + NS)))
+    L.check(lib.sm100_ds_route(logits.data_ptr(), E, K, B, 0, E, NS, *[t.data_ptr() for t in ref_outs],
+                               ctypes.c_void_p(0)), "ds_route")
+    torch.cuda.synchronize()
+    for sel, wsel, off, stok, sw in outs:
+        np.testing.assert_array_equal(sel.cpu().numpy().reshape(B, K), ref)
+        np.testing.assert_allclose(wsel.cpu().numpy().reshape(B, K), ref_w, rtol=1e-5)
+        for a, b in zip((sel, wsel, off, stok, sw), ref_outs):
+            assert torch.equal(a, b)
+
+
 def _experts_case(B, D, I, slots, seed):
     """sm100_ds_experts on explicit slot lists against the oracle's fp8 block-scaled linear."""
     import ctypes

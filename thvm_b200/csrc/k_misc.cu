@@ -349,15 +349,18 @@ extern "C" int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "argmax_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_UNSUPPORTED, "argmax_noalloc: device %d", dev);
-  if (!g_argmax_noalloc_dev[dev]) {
-    // once per device, with that device current
+  char *ws = (char *)__atomic_load_n(&g_argmax_noalloc_dev[dev], __ATOMIC_ACQUIRE);
+  if (!ws) {
+    // once per device, with that device current (two host threads that race
+    // here look up the same address; the first store wins)
     void *p = NULL;
     e = cudaGetSymbolAddress(&p, g_argmax_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return sm100_set_error(SM100_ERR_CUDA, "argmax_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_argmax_noalloc_dev[dev] = p;
+    void *expected = NULL;
+    __atomic_compare_exchange_n(&g_argmax_noalloc_dev[dev], &expected, p, false, __ATOMIC_ACQ_REL, __ATOMIC_ACQUIRE);
+    ws = (char *)__atomic_load_n(&g_argmax_noalloc_dev[dev], __ATOMIC_ACQUIRE);
   }
-  char *ws = (char *)g_argmax_noalloc_dev[dev];
   uint32_t *counter = (uint32_t *)ws;
   float *pv = (float *)(ws + ARGMAX_NOALLOC_COUNTER_BYTES);
   int32_t *pi = (int32_t *)(ws + ARGMAX_NOALLOC_COUNTER_BYTES + (size_t)M * kArgmaxMaxBlocks * 4);

@@ -388,26 +388,24 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
 // then per-expert lists of (token, weight) for the experts [e0, e1) this
 // rank holds, packed expert-major: slot_tok / slot_w / slot_off[e] offsets,
 // followed by n_shared shared experts that take every token with weight 1.
-__global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int E, int K, int B, int e0, int e1,
-                                                         int n_shared, int32_t *sel, float *wsel, int32_t *slot_off,
-                                                         int32_t *slot_tok, float *slot_w) {
+// The routing of every token by one CTA of >= 256 threads (warps over the
+// tokens); the logits are read at L2 (they may come from other CTAs).
+__device__ __forceinline__ void ds_route_block(const float *logits, int E, int K, int B, int e0, int e1, int n_shared,
+                                               int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok,
+                                               float *slot_w) {
   __shared__ int s_sel[kDsMaxTok * kDsMaxK];
   __shared__ float s_w[kDsMaxTok * kDsMaxK];
-  pdl_trigger();
-  pdl_wait();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int b = warp; b < B; b += 32) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int b = warp; b < B; b += nwarps) {
     const float *lg = logits + (int64_t)b * E;
-    float m = -INFINITY;
-    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);
+    const float l0 = lane < E ? __ldcg(lg + lane) : 0.0f, l1 = lane + 32 < E ? __ldcg(lg + lane + 32) : 0.0f;
+    float m = fmaxf(lane < E ? l0 : -INFINITY, lane + 32 < E ? l1 : -INFINITY);
     m = warp_max(m);
-    float sum = 0.0f;
-    for (int e = lane; e < E; e += 32) sum += expf(lg[e] - m);
+    float sum = (lane < E ? expf(l0 - m) : 0.0f) + (lane + 32 < E ? expf(l1 - m) : 0.0f);
     sum = warp_sum(sum);
     // greedy top-K over E <= 64 logits held two per lane (a taken or absent
     // expert is out of the contest); a lane offers its larger logit, the
     // lower id on a tie, and the warp keeps the larger, the lower id on a tie
-    const float l0 = lane < E ? lg[lane] : 0.0f, l1 = lane + 32 < E ? lg[lane + 32] : 0.0f;
     bool live0 = lane < E, live1 = lane + 32 < E;
     for (int k = 0; k < K; k++) {
       const bool take0 = live0 && (!live1 || l0 >= l1);
@@ -483,12 +481,60 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
   __syncthreads();
   if (n_shared > 0) {
     for (int i = threadIdx.x; i < n_shared * B; i += blockDim.x) {
-      const int k = i / B, b = i % B, o = slot_off[ne] + i;
+      const int k = i / B, b = i % B, o = eoff[ne] + i;
       slot_tok[o] = b;
       slot_w[o] = 1.0f;
-      if (b == 0) slot_off[ne + k + 1] = slot_off[ne] + (k + 1) * B;
+      if (b == 0) slot_off[ne + k + 1] = eoff[ne] + (k + 1) * B;
     }
   }
+}
+
+__global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int E, int K, int B, int e0, int e1,
+                                                         int n_shared, int32_t *sel, float *wsel, int32_t *slot_off,
+                                                         int32_t *slot_tok, float *slot_w) {
+  pdl_trigger();
+  pdl_wait();
+  ds_route_block(logits, E, K, B, e0, e1, n_shared, sel, wsel, slot_off, slot_tok, slot_w);
+}
+
+// The router product and the routing in one launch: CTA e computes the
+// logits of expert e for every token (x . router[e], bf16 x bf16 with f32
+// sums, one warp per token), and the last CTA to finish (a device counter,
+// no waiting) routes every token as ds_route_kernel does and resets the
+// counter for the next launch.
+__global__ void __launch_bounds__(256) ds_router_route_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *router,
+                                                              float *logits, int32_t *counter, int D, int E, int K,
+                                                              int B, int e0, int e1, int n_shared, int32_t *sel,
+                                                              float *wsel, int32_t *slot_off, int32_t *slot_tok,
+                                                              float *slot_w) {
+  __shared__ int s_last;
+  pdl_trigger();
+  pdl_wait();
+  const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const __nv_bfloat16 *we = router + (int64_t)e * D;
+  for (int b = warp; b < B; b += 8) {
+    const __nv_bfloat16 *xb = x + (int64_t)b * D;
+    float acc = 0.0f;
+    for (int k = lane * 8; k < D; k += 256) {
+      const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k)), xv = *reinterpret_cast<const uint4 *>(xb + k);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
+        acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(int64_t)b * E + e] = acc;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == E - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  ds_route_block(logits, E, K, B, e0, e1, n_shared, sel, wsel, slot_off, slot_tok, slot_w);
+  if (threadIdx.x == 0) *counter = 0;
 }
 
 // The experts on the 5th-generation tensor cores, fp8 in both operands.  A
@@ -973,6 +1019,19 @@ extern "C" int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t
     return sm100_set_error(SM100_ERR_ARG, "ds_route: E %d K %d B %d [%d, %d)", E, K, B, e0, e1);
   DS_LAUNCH("ds_route", ds_route_kernel, dim3(1), dim3(1024), 0, (cudaStream_t)stream, logits, E, K, B, e0, e1,
             n_shared, sel, wsel, slot_off, slot_tok, slot_w);
+}
+
+extern "C" int sm100_ds_router_route(const void *x, const void *router, float *logits, int32_t *counter, int32_t D,
+                                     int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared,
+                                     int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok, float *slot_w,
+                                     void *stream) {
+  if (!x || !router || !logits || !counter || !sel || !wsel || !slot_off || !slot_tok || !slot_w || E < 1 ||
+      E > 64 || K < 1 || K > kDsMaxK || K > E || B < 1 || B > kDsMaxTok || e0 < 0 || e1 > E || e0 > e1 ||
+      n_shared < 0 || n_shared > 8 || D < 8 || D % 8 || ((uintptr_t)x | (uintptr_t)router) % 16)
+    return sm100_set_error(SM100_ERR_ARG, "ds_router_route: D %d E %d K %d B %d [%d, %d)", D, E, K, B, e0, e1);
+  DS_LAUNCH("ds_router_route", ds_router_route_kernel, dim3(E), dim3(256), 0, (cudaStream_t)stream,
+            (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)router, logits, counter, D, E, K, B, e0, e1, n_shared,
+            sel, wsel, slot_off, slot_tok, slot_w);
 }
 
 extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,

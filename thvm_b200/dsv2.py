@@ -16,8 +16,9 @@ kernel with weight 1.
 Per layer: RMSNorm -> fused q | kv_a projection (skinny tcgen05 GEMM) ->
 q / latent post-processing (bf16, RMSNorm of the latent, YaRN rotary, cache
 append) -> absorbed MLA over the compressed cache -> o projection into the
-residual -> RMSNorm -> dense MLP (layer 0) or router GEMM, routing, fp8
-experts (gate / up + SiLU, then down weighted into the residual).
+residual -> RMSNorm -> dense MLP (layer 0) or the router product and the
+routing (one launch), fp8 experts (gate / up + SiLU, then down weighted into
+the residual).
 
 Parallelism over R ranks (rank r), every weight byte read by one rank:
   * attention by heads: heads split_even(16, R, r); the q rows of those
@@ -249,6 +250,7 @@ class DSModel:
         self.pos = z(1, dt=torch.int32)
         K = cfg.top_k
         self.sel, self.wsel = z(B * K, dt=torch.int32), z(B * K)
+        self.route_counter = z(1, dt=torch.int32)   # the fused router + routing launch's CTA count
         n_local, ns = shard.e1 - shard.e0, len(shard.shared)
         # slot lists of the local routed experts, then the local shared halves (every token, weight 1)
         self.slot_off = z(n_local + ns + 1, dt=torch.int32)
@@ -345,11 +347,14 @@ class DSModel:
                 self._skinny(self.xn, w[p + "d_down"], self.h, DIl, D, residual=first)
                 self._all_reduce()
                 continue
-            self._skinny(self.xn, w[p + "router"], self.rl, D, E)
             ns = len(sh.shared)
-            L.check(lib.sm100_ds_route(self.rl.data_ptr(), E, K, B, sh.e0, sh.e1, ns, self.sel.data_ptr(),
-                                       self.wsel.data_ptr(), self.slot_off.data_ptr(), self.slot_tok.data_ptr(),
-                                       self.slot_w.data_ptr(), st()), "ds_route")
+            # the router product and the routing in one launch
+            L.check(lib.sm100_ds_router_route(self.xn.data_ptr(), w[p + "router"].data_ptr(), self.rl.data_ptr(),
+                                              self.route_counter.data_ptr(), D, E, K, B, sh.e0, sh.e1, ns,
+                                              self.sel.data_ptr(), self.wsel.data_ptr(), self.slot_off.data_ptr(),
+                                              self.slot_tok.data_ptr(), self.slot_w.data_ptr(), st()),
+                    "ds_router_route")
+            self.launches += 1
             # one launch pair over the local routed experts and shared halves (contiguous in this rank's
             # arrays), adding into the residual on rank 0 and into the zeros the all-reduce left in h on
             # the others
@@ -357,7 +362,7 @@ class DSModel:
                                          w[p + "e_d"].data_ptr(), w[p + "e_d_s"].data_ptr(), self.slot_off.data_ptr(),
                                          self.slot_tok.data_ptr(), self.slot_w.data_ptr(), self.a.data_ptr(),
                                          self.h.data_ptr(), sh.e1 - sh.e0 + ns, D, I, st()), "ds_experts")
-            self.launches += 3
+            self.launches += 2
             self._all_reduce()
         self._rms(w["norm_f"], D)
         self._skinny(self.xn, w["lm_head"], self.logits, D, Vl)
