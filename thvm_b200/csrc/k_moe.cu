@@ -289,7 +289,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     }
     float m = -INFINITY, l = 0.0f;
     const __nv_bfloat16 *cb = cc + (int64_t)(b0 + b) * ctx * kMlaKV, *pb = cpe + (int64_t)(b0 + b) * ctx * kMlaDR;
-#pragma unroll 2
+#pragma unroll 4
     for (int r = warp; r < T; r += kMlaWarps) {
       const uint4 c0 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 8 * lane);
       const uint4 c1 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 256 + 8 * lane);
@@ -512,20 +512,34 @@ __global__ void __launch_bounds__(256) ds_router_route_kernel(const __nv_bfloat1
   pdl_wait();
   const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const __nv_bfloat16 *we = router + (int64_t)e * D;
-  for (int b = warp; b < B; b += 8) {
-    const __nv_bfloat16 *xb = x + (int64_t)b * D;
-    float acc = 0.0f;
-    for (int k = lane * 8; k < D; k += 256) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k)), xv = *reinterpret_cast<const uint4 *>(xb + k);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+  // warp w: tokens w, w + 8, w + 16, w + 24 together (five 16-byte loads in
+  // flight per step, two steps unrolled)
+  float acc[4] = {};
+#pragma unroll 2
+  for (int k = lane * 8; k < D; k += 256) {
+    const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k));
+    uint4 xv[4];
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const int b = warp + 8 * t;
+      xv[t] = b < B ? *reinterpret_cast<const uint4 *>(x + (int64_t)b * D + k) : make_uint4(0, 0, 0, 0);
+    }
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int t = 0; t < 4; t++) {
+      const uint32_t xx[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
-        acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
+        acc[t] = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc[t]);
+        acc[t] = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc[t]);
       }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) logits[(int64_t)b * E + e] = acc;
+  }
+#pragma unroll
+  for (int t = 0; t < 4; t++) {
+    const float v = warp_sum(acc[t]);
+    const int b = warp + 8 * t;
+    if (lane == 0 && b < B) logits[(int64_t)b * E + e] = v;
   }
   __threadfence();
   __syncthreads();
