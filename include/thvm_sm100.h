@@ -465,6 +465,17 @@ int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, const float 
 int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c, const void *cache_pe,
                  const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV,
                  int32_t ctx, float scale, void *stream);
+/* sm100_ds_qkv_post then sm100_ds_mla in one launch for the DeepSeek-V2-Lite
+ * shapes (KV 512, DR 64, DN and DV <= 128): qkva holds the projection's f32
+ * rows (stride ld): the H heads' q [H][DN + DR] from column 0 and the latent
+ * and key rope [KV + DR] from column kva_off.  Each CTA post-processes its
+ * sequences' q and current cache row itself (the same operations) and walks
+ * that row from shared memory; the CTAs of head 0 store it in the caches.
+ * Other shapes run the two launches (q_out then holds the processed q). */
+int sm100_ds_mla_post(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv, const float *cos_t,
+                      const float *sin_t, const int32_t *pos, void *q_out, const void *w_uk, const void *w_uv,
+                      void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV,
+                      int32_t KV, int32_t ctx, float eps, float scale, void *stream);
 /* the K largest of E <= 64 router logits (ties: lowest id) weighted by their
  * softmax probabilities, no renormalisation (the reference's route kernel,
  * bench/dsv2_decode_bench.c:787-863); sel / wsel [B][K]; slot lists of the

@@ -200,3 +200,56 @@ def test_ds_experts_flags_more_than_32_slots():
     assert status & L.DECODE_ERR_ARG, status
     np.testing.assert_allclose(y[:32], ref[:32], rtol=0, atol=5e-3 * np.abs(ref).max())
     assert not np.any(y[32:])
+
+
+@pytest.mark.parametrize("H", [16, 4, 2])
+def test_ds_mla_post_is_post_then_mla(H):
+    """sm100_ds_mla_post (the q / latent post-processing done inside the MLA
+    group kernel, the current row walked from shared memory) against the two
+    launches it replaces (sm100_ds_qkv_post, sm100_ds_mla) on the same inputs
+    at the DeepSeek-V2-Lite MLA shapes: the attention output and both cache
+    rows bit for bit, at positions 0, 1 and 37 (16, 4 and 2 heads: 4, 1 and 1
+    sequences per CTA)."""
+    import ctypes
+    import torch
+    from thvm_b200 import _lib as L
+    from thvm_b200.dsv2 import yarn_tables
+    lib = L.lib()
+    B, DN, DR, DV, KV, ctx = 32, 128, 64, 128, 512, 64
+    nq = H * (DN + DR)
+    ld = nq + KV + DR
+    g = torch.Generator(device="cuda").manual_seed(11)
+    cos, sin = (torch.from_numpy(t).cuda() for t in yarn_tables(DR, ctx))
+    gkv = torch.rand(KV, generator=g, device="cuda") + 0.5
+    wuk = (torch.randn(H, DN, KV, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    wuv = (torch.randn(H, DV, KV, generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    cache0 = (torch.randn(B, ctx, KV, generator=g, device="cuda")).to(torch.bfloat16)
+    pe0 = (torch.randn(B, ctx, DR, generator=g, device="cuda")).to(torch.bfloat16)
+    scale = 0.1
+    st = ctypes.c_void_p(0)
+    for p in (0, 1, 37):
+        qkva = torch.randn(B, ld, generator=g, device="cuda")
+        pos = torch.tensor([p], dtype=torch.int32, device="cuda")
+        outs = []
+        for fused in (False, True):
+            cc, cp = cache0.clone(), pe0.clone()
+            qo = torch.zeros(B, nq, dtype=torch.bfloat16, device="cuda")
+            o = torch.zeros(B, H * DV, dtype=torch.bfloat16, device="cuda")
+            if fused:
+                rc = lib.sm100_ds_mla_post(qkva.data_ptr(), ld, nq, gkv.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                           pos.data_ptr(), qo.data_ptr(), wuk.data_ptr(), wuv.data_ptr(),
+                                           cc.data_ptr(), cp.data_ptr(), o.data_ptr(), B, H, DN, DR, DV, KV, ctx,
+                                           1e-6, scale, st)
+                L.check(rc, "ds_mla_post")
+            else:
+                q = qkva.data_ptr()
+                L.check(lib.sm100_ds_qkv_post(q, q + 4 * nq, ld, gkv.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                              pos.data_ptr(), qo.data_ptr(), cc.data_ptr(), cp.data_ptr(), B, H, DN,
+                                              DR, KV, ctx, 1e-6, st), "ds_qkv_post")
+                L.check(lib.sm100_ds_mla(qo.data_ptr(), wuk.data_ptr(), wuv.data_ptr(), cc.data_ptr(), cp.data_ptr(),
+                                         pos.data_ptr(), o.data_ptr(), B, H, DN, DR, DV, KV, ctx, scale, st), "ds_mla")
+            torch.cuda.synchronize()
+            outs.append((o, cc, cp))
+        assert lib.sm100_ds_status() == 0
+        for a, b in zip(*outs):
+            assert torch.equal(a.view(torch.int16), b.view(torch.int16)), p

@@ -82,14 +82,14 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
     const int h = i / half, j = i % half;
     const float xe = bfr(qb[h * QS + DN + 2 * j]), xo = bfr(qb[h * QS + DN + 2 * j + 1]);
     const float c = cs[(int64_t)p * DR + j], s = sn[(int64_t)p * DR + j];
-    qob[h * QS + DN + j] = __float2bfloat16_rn(xe * c - xo * s);
-    qob[h * QS + DN + half + j] = __float2bfloat16_rn(xo * c + xe * s);
+    qob[h * QS + DN + j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, s)));
+    qob[h * QS + DN + half + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, s)));
   }
   const float *kb = kva + (int64_t)b * ld;
   float ss = 0.0f;
   for (int i = threadIdx.x; i < KV; i += 256) {
     const float v = bfr(kb[i]);
-    ss += v * v;
+    ss = __fmaf_rn(v, v, ss);
   }
   ss = warp_sum(ss);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
@@ -97,15 +97,15 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
   float t = 0.0f;
 #pragma unroll
   for (int w = 0; w < 8; w++) t += red[w];
-  const float inv = 1.0f / sqrtf(t * (1.0f / (float)KV) + eps);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(t, 1.0f / (float)KV), eps)));
   __nv_bfloat16 *crow = cc + ((int64_t)b * ctx + p) * KV;
-  for (int i = threadIdx.x; i < KV; i += 256) crow[i] = __float2bfloat16_rn((bfr(kb[i]) * inv) * g_kv[i]);
+  for (int i = threadIdx.x; i < KV; i += 256) crow[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(bfr(kb[i]), inv), g_kv[i]));
   __nv_bfloat16 *prow = cpe + ((int64_t)b * ctx + p) * DR;
   for (int j = threadIdx.x; j < half; j += 256) {
     const float xe = bfr(kb[KV + 2 * j]), xo = bfr(kb[KV + 2 * j + 1]);
     const float c = cs[(int64_t)p * DR + j], s = sn[(int64_t)p * DR + j];
-    prow[j] = __float2bfloat16_rn(xe * c - xo * s);
-    prow[half + j] = __float2bfloat16_rn(xo * c + xe * s);
+    prow[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, s)));
+    prow[half + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, s)));
   }
 }
 
@@ -210,15 +210,30 @@ struct MlaSmem {
   static constexpr size_t po = qlat + kMlaNB * kMlaKV * 4;                    // [warps][kMlaNB][512] f32
   static constexpr size_t pm = po + (size_t)kMlaWarps * kMlaNB * kMlaKV * 4;  // [warps][kMlaNB] max
   static constexpr size_t pl = pm + kMlaWarps * kMlaNB * 4;                   // [warps][kMlaNB] sum
-  static constexpr size_t bar = pl + kMlaWarps * kMlaNB * 4;
+  static constexpr size_t cur = pl + kMlaWarps * kMlaNB * 4;               // [kMlaNB][512 + 64] bf16 current rows
+  static constexpr size_t bar = cur + kMlaNB * (kMlaKV + kMlaDR) * 2;
   static constexpr size_t total = bar + 16;
 };
 
-template <int NB>
+// MlaPost: the projection outputs (f32 rows of stride ld: the H heads' q
+// [H][DN + DR], then the latent [KV] and the key's rope pair [DR]) come in
+// instead of the post-processed q; the CTA does ds_qkv_post's work for its
+// sequences itself (same operations, same order): q rounded and rotated,
+// the current latent row RMSNormed and the key rotated into shared memory,
+// which the walk reads for the current position; the head-0 CTAs store that
+// row into the caches for the later steps.
+struct MlaPost {
+  const float *qkva;
+  int64_t ld, kva_off;
+  const float *g_kv, *cs, *sn;
+  float eps;
+};
+
+template <int NB, bool kPost>
 __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     ds_mla_group_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk, const __nv_bfloat16 *wuv,
-                        const __nv_bfloat16 *cc, const __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o, int B,
-                        int H, int DN, int DV, int ctx, float scale) {
+                        __nv_bfloat16 *cc, __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o, int B,
+                        int H, int DN, int DV, int ctx, float scale, MlaPost post) {
   extern __shared__ __align__(128) unsigned char sm[];
   __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(sm + MlaSmem::w);
   float *qn = reinterpret_cast<float *>(sm + MlaSmem::qn), *qpe = reinterpret_cast<float *>(sm + MlaSmem::qpe);
@@ -239,12 +254,66 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   }
   pdl_trigger();
   pdl_wait();
-  const int T = *pos + 1;
+  const int p = *pos, T = p + 1;
+  __nv_bfloat16 *cur = reinterpret_cast<__nv_bfloat16 *>(sm + MlaSmem::cur);   // [NB][512 latent | 64 rope]
   for (int i = t; i < kMlaNB * QS; i += kMlaWarps * 32) {
     const int b = i / QS, d = i % QS;
-    const float v = b < nb ? bf(qo[((int64_t)(b0 + b) * H + h) * QS + d]) : 0.0f;
+    float v = 0.0f;
+    if (b < nb) {
+      if constexpr (kPost) {   // ds_qkv_post's q: nope rounded; rope pairs rounded, rotated, rounded
+        const float *qr = post.qkva + (int64_t)(b0 + b) * post.ld + h * QS;
+        constexpr int half = kMlaDR / 2;
+        if (d < DN) {
+          v = bfr(qr[d]);
+        } else {
+          const int j = (d - DN) % half;
+          const float xe = bfr(qr[DN + 2 * j]), xo = bfr(qr[DN + 2 * j + 1]);
+          const float c = post.cs[(int64_t)p * kMlaDR + j], sv = post.sn[(int64_t)p * kMlaDR + j];
+          v = bfr(d - DN < half ? __fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, sv))
+                                : __fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, sv)));
+        }
+      } else {
+        v = bf(qo[((int64_t)(b0 + b) * H + h) * QS + d]);
+      }
+    }
     if (d < DN) qn[d * kMlaNB + b] = v;
     else qpe[b * kMlaDR + d - DN] = v;
+  }
+  if constexpr (kPost) {   // the current latent / key rows (ds_qkv_post's, thread for thread)
+    __shared__ float red[kMlaWarps];
+    for (int b = 0; b < nb; b++) {
+      const float *kb = post.qkva + (int64_t)(b0 + b) * post.ld + post.kva_off;
+      float ss = 0.0f;
+      for (int i = t; i < kMlaKV; i += kMlaWarps * 32) {
+        const float v = bfr(kb[i]);
+        ss = __fmaf_rn(v, v, ss);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      __syncthreads();
+      float tot = 0.0f;
+#pragma unroll
+      for (int w = 0; w < kMlaWarps; w++) tot += red[w];
+      __syncthreads();
+      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)kMlaKV), post.eps)));
+      __nv_bfloat16 *crow = cur + b * (kMlaKV + kMlaDR), *prow = crow + kMlaKV;
+      for (int i = t; i < kMlaKV; i += kMlaWarps * 32)
+        crow[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(bfr(kb[i]), inv), post.g_kv[i]));
+      for (int j = t; j < kMlaDR / 2; j += kMlaWarps * 32) {
+        const float xe = bfr(kb[kMlaKV + 2 * j]), xo = bfr(kb[kMlaKV + 2 * j + 1]);
+        const float c = post.cs[(int64_t)p * kMlaDR + j], sv = post.sn[(int64_t)p * kMlaDR + j];
+        prow[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, sv)));
+        prow[kMlaDR / 2 + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, sv)));
+      }
+    }
+    __syncthreads();
+    if (h == 0)   // one head's CTAs keep the rows for the later steps
+      for (int i = t; i < nb * (kMlaKV + kMlaDR); i += kMlaWarps * 32) {
+        const int b = i / (kMlaKV + kMlaDR), c = i % (kMlaKV + kMlaDR);
+        const __nv_bfloat16 v = cur[i];
+        if (c < kMlaKV) cc[((int64_t)(b0 + b) * ctx + p) * kMlaKV + c] = v;
+        else cpe[((int64_t)(b0 + b) * ctx + p) * kMlaDR + c - kMlaKV] = v;
+      }
   }
   __syncthreads();
   const bool wk_ok = mbar_wait(bar, 0, status, false);
@@ -291,10 +360,12 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     const __nv_bfloat16 *cb = cc + (int64_t)(b0 + b) * ctx * kMlaKV, *pb = cpe + (int64_t)(b0 + b) * ctx * kMlaDR;
 #pragma unroll 4
     for (int r = warp; r < T; r += kMlaWarps) {
-      const uint4 c0 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 8 * lane);
-      const uint4 c1 = *reinterpret_cast<const uint4 *>(cb + (int64_t)r * kMlaKV + 256 + 8 * lane);
-      const uint4 pe = lane < 8 ? *reinterpret_cast<const uint4 *>(pb + (int64_t)r * kMlaDR + 8 * lane)
-                                : make_uint4(0, 0, 0, 0);
+      // with kPost the current row is the one in shared memory
+      const __nv_bfloat16 *crow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) : cb + (int64_t)r * kMlaKV;
+      const __nv_bfloat16 *prow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) + kMlaKV : pb + (int64_t)r * kMlaDR;
+      const uint4 c0 = *reinterpret_cast<const uint4 *>(crow + 8 * lane);
+      const uint4 c1 = *reinterpret_cast<const uint4 *>(crow + 256 + 8 * lane);
+      const uint4 pe = lane < 8 ? *reinterpret_cast<const uint4 *>(prow + 8 * lane) : make_uint4(0, 0, 0, 0);
       const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
       const uint32_t pw[4] = {pe.x, pe.y, pe.z, pe.w};
       float cv[16];
@@ -497,49 +568,37 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
   ds_route_block(logits, E, K, B, e0, e1, n_shared, sel, wsel, slot_off, slot_tok, slot_w);
 }
 
-// The router product and the routing in one launch: CTA e computes the
-// logits of expert e for every token (x . router[e], bf16 x bf16 with f32
-// sums, one warp per token), and the last CTA to finish (a device counter,
-// no waiting) routes every token as ds_route_kernel does and resets the
-// counter for the next launch.
-__global__ void __launch_bounds__(256) ds_router_route_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *router,
-                                                              float *logits, int32_t *counter, int D, int E, int K,
-                                                              int B, int e0, int e1, int n_shared, int32_t *sel,
-                                                              float *wsel, int32_t *slot_off, int32_t *slot_tok,
-                                                              float *slot_w) {
+// The router product and the routing in one launch: CTA e (1024 threads)
+// computes the logits of expert e for every token (x . router[e], bf16 x
+// bf16 with f32 sums, one warp per token), and the last CTA to finish (a
+// device counter, no waiting) routes every token as ds_route_kernel does, a
+// warp per token, and resets the counter for the next launch.
+__global__ void __launch_bounds__(1024) ds_router_route_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *router,
+                                                               float *logits, int32_t *counter, int D, int E, int K,
+                                                               int B, int e0, int e1, int n_shared, int32_t *sel,
+                                                               float *wsel, int32_t *slot_off, int32_t *slot_tok,
+                                                               float *slot_w) {
   __shared__ int s_last;
   pdl_trigger();
   pdl_wait();
-  const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int e = blockIdx.x, lane = threadIdx.x & 31, b = threadIdx.x >> 5;
   const __nv_bfloat16 *we = router + (int64_t)e * D;
-  // warp w: tokens w, w + 8, w + 16, w + 24 together (five 16-byte loads in
-  // flight per step, two steps unrolled)
-  float acc[4] = {};
-#pragma unroll 2
-  for (int k = lane * 8; k < D; k += 256) {
-    const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k));
-    uint4 xv[4];
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const int b = warp + 8 * t;
-      xv[t] = b < B ? *reinterpret_cast<const uint4 *>(x + (int64_t)b * D + k) : make_uint4(0, 0, 0, 0);
-    }
-    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-      const uint32_t xx[4] = {xv[t].x, xv[t].y, xv[t].z, xv[t].w};
+  // warp b: token b, its 16-byte loads two steps ahead
+  if (b < B) {
+    const __nv_bfloat16 *xb = x + (int64_t)b * D;
+    float acc = 0.0f;
+#pragma unroll 4
+    for (int k = lane * 8; k < D; k += 256) {
+      const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k)), xv = *reinterpret_cast<const uint4 *>(xb + k);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
       for (int q = 0; q < 4; q++) {
-        acc[t] = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc[t]);
-        acc[t] = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc[t]);
+        acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
+        acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
       }
     }
-  }
-#pragma unroll
-  for (int t = 0; t < 4; t++) {
-    const float v = warp_sum(acc[t]);
-    const int b = warp + 8 * t;
-    if (lane == 0 && b < B) logits[(int64_t)b * E + e] = v;
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(int64_t)b * E + e] = acc;
   }
   __threadfence();
   __syncthreads();
@@ -989,6 +1048,40 @@ extern "C" int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, c
             ctx, eps, ld);
 }
 
+// The group kernel's launch: sequences per CTA the most (fewer re-reads of
+// the head's W_uk / W_uv) that still gives the grid at least 96 CTAs, so a
+// tensor-parallel rank with few heads still spreads its cache walks over the
+// SMs.
+template <bool kPost>
+static int mla_group_launch(const void *q_out, const void *w_uk, const void *w_uv, void *cache_c, void *cache_pe,
+                            const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DV, int32_t ctx,
+                            float scale, const MlaPost &post, void *stream) {
+  const int nb = H * ((B + 3) / 4) >= 96 ? 4 : H * ((B + 1) / 2) >= 96 ? 2 : 1;
+  static bool attr[3] = {false, false, false};
+  const int ai = nb == 4 ? 2 : nb == 2 ? 1 : 0;
+  if (!attr[ai]) {
+    const void *fn = nb == 4   ? (const void *)ds_mla_group_kernel<4, kPost>
+                     : nb == 2 ? (const void *)ds_mla_group_kernel<2, kPost>
+                               : (const void *)ds_mla_group_kernel<1, kPost>;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MlaSmem::total);
+    if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_mla: smem attribute: %s", cudaGetErrorString(e));
+    attr[ai] = true;
+  }
+#define DS_MLA_GROUP(NBV)                                                                                           \
+  DS_LAUNCH("ds_mla", (ds_mla_group_kernel<NBV, kPost>), dim3(H * ((B + NBV - 1) / NBV)), dim3(kMlaWarps * 32),     \
+            MlaSmem::total, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,        \
+            (const __nv_bfloat16 *)w_uv, (__nv_bfloat16 *)cache_c, (__nv_bfloat16 *)cache_pe, pos, (__nv_bfloat16 *)o, \
+            B, H, DN, DV, ctx, scale, post)
+  if (nb == 4) DS_MLA_GROUP(4);
+  if (nb == 2) DS_MLA_GROUP(2);
+  DS_MLA_GROUP(1);
+#undef DS_MLA_GROUP
+}
+
+static bool mla_group_shape(int32_t DN, int32_t DR, int32_t DV, int32_t KV) {
+  return KV == kMlaKV && DR == kMlaDR && DN <= kMlaMaxD && DV <= kMlaMaxD;
+}
+
 extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c,
                             const void *cache_pe, const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN,
                             int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float scale, void *stream) {
@@ -996,33 +1089,30 @@ extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_u
       KV > kDsKV || ctx > kDsMaxCtx)
     return sm100_set_error(SM100_ERR_ARG, "ds_mla: bad arguments (DN <= 256, DR <= 128, KV <= %d, ctx <= %d)",
                            kDsKV, kDsMaxCtx);
-  if (KV == kMlaKV && DR == kMlaDR && DN <= kMlaMaxD && DV <= kMlaMaxD) {
-    // sequences per CTA: the most (fewer re-reads of the head's W_uk / W_uv)
-    // that still gives the grid at least 96 CTAs, so a tensor-parallel rank
-    // with few heads still spreads its cache walks over the SMs
-    const int nb = H * ((B + 3) / 4) >= 96 ? 4 : H * ((B + 1) / 2) >= 96 ? 2 : 1;
-    static bool attr[3] = {false, false, false};
-    const int ai = nb == 4 ? 2 : nb == 2 ? 1 : 0;
-    if (!attr[ai]) {
-      const void *fn = nb == 4 ? (const void *)ds_mla_group_kernel<4>
-                       : nb == 2 ? (const void *)ds_mla_group_kernel<2> : (const void *)ds_mla_group_kernel<1>;
-      const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MlaSmem::total);
-      if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "ds_mla: smem attribute: %s", cudaGetErrorString(e));
-      attr[ai] = true;
-    }
-#define DS_MLA_GROUP(NBV)                                                                                         \
-  DS_LAUNCH("ds_mla", ds_mla_group_kernel<NBV>, dim3(H * ((B + NBV - 1) / NBV)), dim3(kMlaWarps * 32), MlaSmem::total, \
-            (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,                        \
-            (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c, (const __nv_bfloat16 *)cache_pe, pos,     \
-            (__nv_bfloat16 *)o, B, H, DN, DV, ctx, scale)
-    if (nb == 4) DS_MLA_GROUP(4);
-    if (nb == 2) DS_MLA_GROUP(2);
-    DS_MLA_GROUP(1);
-#undef DS_MLA_GROUP
-  }
+  if (mla_group_shape(DN, DR, DV, KV))
+    return mla_group_launch<false>(q_out, w_uk, w_uv, (void *)cache_c, (void *)cache_pe, pos, o, B, H, DN, DV, ctx,
+                                   scale, MlaPost{}, stream);
   DS_LAUNCH("ds_mla", ds_mla_kernel, dim3(B * H), dim3(256), 0, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out,
             (const __nv_bfloat16 *)w_uk, (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c,
             (const __nv_bfloat16 *)cache_pe, pos, (__nv_bfloat16 *)o, H, DN, DR, DV, KV, ctx, scale);
+}
+
+extern "C" int sm100_ds_mla_post(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv, const float *cos_t,
+                                 const float *sin_t, const int32_t *pos, void *q_out, const void *w_uk,
+                                 const void *w_uv, void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H,
+                                 int32_t DN, int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float eps, float scale,
+                                 void *stream) {
+  if (!qkva || !g_kv || !cos_t || !sin_t || !pos || !q_out || !w_uk || !w_uv || !cache_c || !cache_pe || !o || B < 1 ||
+      H < 1 || kva_off < (int64_t)H * (DN + DR) || ld < kva_off + KV + DR)
+    return sm100_set_error(SM100_ERR_ARG, "ds_mla_post: bad arguments");
+  if (!mla_group_shape(DN, DR, DV, KV) || ctx > kDsMaxCtx) {   // the two launches it fuses
+    int rc = sm100_ds_qkv_post(qkva, qkva + kva_off, ld, g_kv, cos_t, sin_t, pos, q_out, cache_c, cache_pe, B, H, DN,
+                               DR, KV, ctx, eps, stream);
+    if (rc != SM100_OK) return rc;
+    return sm100_ds_mla(q_out, w_uk, w_uv, cache_c, cache_pe, pos, o, B, H, DN, DR, DV, KV, ctx, scale, stream);
+  }
+  const MlaPost post{qkva, ld, kva_off, g_kv, cos_t, sin_t, eps};
+  return mla_group_launch<true>(q_out, w_uk, w_uv, cache_c, cache_pe, pos, o, B, H, DN, DV, ctx, scale, post, stream);
 }
 
 extern "C" int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1,
@@ -1043,7 +1133,7 @@ extern "C" int sm100_ds_router_route(const void *x, const void *router, float *l
       E > 64 || K < 1 || K > kDsMaxK || K > E || B < 1 || B > kDsMaxTok || e0 < 0 || e1 > E || e0 > e1 ||
       n_shared < 0 || n_shared > 8 || D < 8 || D % 8 || ((uintptr_t)x | (uintptr_t)router) % 16)
     return sm100_set_error(SM100_ERR_ARG, "ds_router_route: D %d E %d K %d B %d [%d, %d)", D, E, K, B, e0, e1);
-  DS_LAUNCH("ds_router_route", ds_router_route_kernel, dim3(E), dim3(256), 0, (cudaStream_t)stream,
+  DS_LAUNCH("ds_router_route", ds_router_route_kernel, dim3(E), dim3(1024), 0, (cudaStream_t)stream,
             (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)router, logits, counter, D, E, K, B, e0, e1, n_shared,
             sel, wsel, slot_off, slot_tok, slot_w);
 }

@@ -15,8 +15,8 @@ kernel with weight 1.
 
 Per layer: RMSNorm -> fused q | kv_a projection (skinny tcgen05 GEMM) ->
 q / latent post-processing (bf16, RMSNorm of the latent, YaRN rotary, cache
-append) -> absorbed MLA over the compressed cache -> o projection into the
-residual -> RMSNorm -> dense MLP (layer 0) or the router product and the
+append) and the absorbed MLA over the compressed cache (one launch at the
+model's shapes) -> o projection into the residual -> RMSNorm -> dense MLP (layer 0) or the router product and the
 routing (one launch), fp8 experts (gate / up + SiLU, then down weighted into
 the residual).
 
@@ -326,15 +326,15 @@ class DSModel:
             p = f"l{l}."
             self._rms(w[p + "attn_norm"], D)
             self._skinny(self.xn, w[p + "w_qkva"], self.qkva, D, self.n_qkva)
-            q = self.qkva.data_ptr()
-            L.check(lib.sm100_ds_qkv_post(q, q + 4 * self.n_q, self.n_qkva, w[p + "kv_norm"].data_ptr(),
+            # q / latent post-processing (rotary, latent norm, cache append) and the absorbed MLA:
+            # one launch for the DeepSeek-V2-Lite shapes, two otherwise
+            L.check(lib.sm100_ds_mla_post(self.qkva.data_ptr(), self.n_qkva, self.n_q, w[p + "kv_norm"].data_ptr(),
                                           self.cos.data_ptr(), self.sin.data_ptr(), self.pos.data_ptr(),
-                                          self.qo.data_ptr(), self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(),
-                                          B, Hl, DN, DR, KV, cfg.max_ctx, cfg.eps, st()), "ds_qkv_post")
-            L.check(lib.sm100_ds_mla(self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
-                                     self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.pos.data_ptr(),
-                                     self.o.data_ptr(), B, Hl, DN, DR, DV, KV, cfg.max_ctx, cfg.scale, st()), "ds_mla")
-            self.launches += 2
+                                          self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
+                                          self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.o.data_ptr(),
+                                          B, Hl, DN, DR, DV, KV, cfg.max_ctx, cfg.eps, cfg.scale, st()), "ds_mla_post")
+            fused = KV == 512 and DR == 64 and DN <= 128 and DV <= 128
+            self.launches += 1 if fused else 2
             # the o projection's partial sums: rank 0 into the residual, the others over it
             self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
             self._all_reduce()
