@@ -564,6 +564,26 @@ int sm100_attn_prefill_bf16(const void *q, const void *k, const void *v, float *
  * synchronises the device and clears the word */
 uint32_t sm100_attn_prefill_status(void);
 
+/* ---- weight files straight into device buffers ---------------------------
+ * .safetensors (the format py/thvm/nn_state.py safe_load / safe_save read
+ * and write, :44-85: an 8-byte little-endian header length, a JSON header of
+ * name -> {dtype, shape, data_offsets}, the raw tensor bytes) and the
+ * DSV2PK01 pack of the reference's DeepSeek-V2 bench (bench/
+ * dsv2_decode_bench.c:229-262).  The file is mapped read-only and each
+ * tensor's bytes go into a fresh backend buffer by one copy from the mapping;
+ * entries[i] describes tensor i (the pack's shape is the flat element count)
+ * and the caller owns the buffers.  On an error no buffer is left allocated. */
+typedef struct {
+  char name[128];
+  char dtype[12];     /* the file's tag: "F32", "BF16", "F8_E4M3", "I32", ... */
+  int32_t ndim;
+  int64_t shape[8];
+  uint64_t nbytes;
+  uint32_t buf_id;
+} Sm100TensorEntry;
+int sm100_safetensors_load(const char *path, Sm100TensorEntry *entries, int32_t max_entries, int32_t *n_out);
+int sm100_dsv2pack_load(const char *path, Sm100TensorEntry *entries, int32_t max_entries, int32_t *n_out);
+
 /* ---- custom-kernel ABI: raw CUDA-C programs -------------------------------
  * Replaces cuda_custom_dispatch (src/backend/cuda/jit.c:802-893) for the
  * programs kernel_emit_custom_program records (src/schedule/kernel_custom.c:

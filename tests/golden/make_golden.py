@@ -20,6 +20,8 @@ package finds its library beside itself) and the reference's GPT-2 model code
                seeded normals, random bit patterns (NaN payloads, subnormals,
                infinities) and the e4m3 rounding / saturation edges; every e4m3
                code decoded.
+  state.safetensors  a few seeded tensors of several dtypes written by the
+               reference's own safe_save (the weight-file loader's fixture).
   gpt2.npz     GPT-2 small (12 layers, fp32, MAX_CONTEXT=1024) greedy decode:
                the 16 prompt ids, the 64 generated ids, per-step top-1 / top-2
                logits, and the full logits of the prompt step and the first
@@ -219,13 +221,48 @@ def make_dtypes() -> None:
     print("wrote", OUT / "dtypes.npz")
 
 
+def state_tensors() -> dict:
+    """The tensors of state.safetensors as numpy arrays (bf16 and fp8 as their
+    raw codes): seeded, several dtypes and ranks, an empty one."""
+    rng = np.random.default_rng(77)
+    return {
+        "wte.weight": rng.standard_normal((7, 5)).astype(np.float32),
+        "h.0.attn.c_attn.bias": rng.standard_normal(12).astype(np.float32),
+        "h.0.ln_1.weight": (rng.standard_normal(9) * 0.5).astype(np.float16),
+        "experts.codes": rng.integers(0, 255, (3, 4, 2)).astype(np.uint8),
+        "positions": rng.integers(-1000, 1000, (2, 3)).astype(np.int32),
+        "lm_head.weight.bf16": rng.integers(0, 65535, (4, 6)).astype(np.uint16),
+        "empty": np.zeros((0, 4), np.float32),
+    }
+
+
+def make_state() -> None:
+    """state.safetensors, written by the reference's own safe_save
+    (py/thvm/nn_state.py:64-85) from reference Tensors of several dtypes."""
+    from thvm import Tensor, dtypes
+    from thvm.nn_state import safe_save
+    t = state_tensors()
+    ts = {}
+    for k, v in t.items():
+        if k.endswith(".bf16"):
+            ts[k] = Tensor(v.astype(np.int16)).bitcast(dtypes.bfloat16)
+        elif k == "experts.codes":
+            ts[k] = Tensor(v).bitcast(dtypes.fp8e4m3)
+        else:
+            ts[k] = Tensor(v)
+    safe_save(ts, OUT / "state.safetensors", metadata={"format": "thvm", "note": "golden"})
+    print("wrote", OUT / "state.safetensors")
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["ops", "gpt2", "dtypes"]
+    which = sys.argv[1:] or ["ops", "gpt2", "dtypes", "state"]
     if "dtypes" in which:
         make_dtypes()
-    if "ops" in which or "gpt2" in which:
+    if "ops" in which or "gpt2" in which or "state" in which:
         _setup()
     if "ops" in which:
         make_ops()
     if "gpt2" in which:
         make_gpt2()
+    if "state" in which:
+        make_state()

@@ -1,0 +1,84 @@
+"""Weight files straight into device buffers (thvm_b200/weights.py over
+sm100_safetensors_load / sm100_dsv2pack_load), on the CPU in host-memory
+mode: the .safetensors file the reference's own safe_save wrote
+(tests/golden/make_golden.py state) loads tensor for tensor, byte for byte,
+with its dtypes and shapes and the __metadata__ entry skipped; a DSV2PK01
+pack written by the oracle's pack writer loads likewise; malformed files are
+rejected and leave no buffer behind."""
+import subprocess
+import sys
+import textwrap
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parents[1]
+
+PRELUDE = """
+import numpy as np
+from thvm_b200 import _lib as L
+from thvm_b200.device import Device
+from thvm_b200 import weights as W
+d = Device(host_memory=True)
+lib = d.lib
+"""
+
+
+def run(body: str):
+    code = PRELUDE + textwrap.dedent(body)
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+def test_safetensors_from_the_reference_loads_byte_for_byte():
+    run("""
+    import sys
+    sys.path.insert(0, "tests/golden")
+    from make_golden import state_tensors
+    want = state_tensors()
+    got = W.load_safetensors("tests/golden/state.safetensors")
+    assert sorted(got) == sorted(want)
+    tags = {"wte.weight": "F32", "h.0.attn.c_attn.bias": "F32", "h.0.ln_1.weight": "F16", "experts.codes": "F8_E4M3",
+            "positions": "I32", "lm_head.weight.bf16": "BF16", "empty": "F32"}
+    for k, v in want.items():
+        t = got[k]
+        assert t.dtype == tags[k] and t.shape == v.shape and t.nbytes == v.nbytes, (k, t)
+        if v.size:
+            assert np.array_equal(W.read(d, t).view(np.uint8), v.view(np.uint8)), k
+    before = lib.sm100_buf_live_count()
+    for t in got.values():
+        lib.sm100_buf_free(t.buf_id)
+    assert lib.sm100_buf_live_count() == before - len(got)
+    """)
+
+
+def test_dsv2_pack_loads_and_bad_files_leave_nothing():
+    run("""
+    import tempfile, os
+    import oracle as O
+    w = {"embed": (np.arange(24, dtype=np.uint16) * 7), "norm": np.linspace(-1, 1, 5, dtype=np.float32),
+         "l0.wq": np.arange(6, dtype=np.uint16)}
+    with tempfile.TemporaryDirectory() as td:
+        p = os.path.join(td, "x.pack")
+        O.write_dsv2_pack(p, w)
+        got = W.load_dsv2_pack(p)
+        assert sorted(got) == sorted(w)
+        for k, v in w.items():
+            t = got[k]
+            assert t.dtype == ("BF16" if v.dtype == np.uint16 else "F32") and t.shape == (v.size,)
+            assert np.array_equal(W.read(d, t), v)
+        before = lib.sm100_buf_live_count()
+        bad = os.path.join(td, "bad.safetensors")
+        hdr = b'{"a":{"dtype":"F32","shape":[2],"data_offsets":[0,8]},"b":{"dtype":"F32","shape":[9],"data_offsets":[8,44]}}'
+        open(bad, "wb").write(len(hdr).to_bytes(8, "little") + hdr + bytes(16))   # b's bytes run past the file
+        try:
+            W.load_safetensors(bad)
+            raise SystemExit("a truncated file was accepted")
+        except L.Sm100Error as e:
+            assert "bad entry b" in str(e), e
+        assert lib.sm100_buf_live_count() == before   # a's buffer was dropped again
+        open(bad, "wb").write(b"DSV2PK01" + (5).to_bytes(8, "little"))
+        try:
+            W.load_dsv2_pack(bad)
+            raise SystemExit("a bad pack was accepted")
+        except L.Sm100Error:
+            pass
+    """)

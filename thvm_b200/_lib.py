@@ -71,6 +71,11 @@ class Sm100AttnArgs(ctypes.Structure):
 SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV, SK_ACCUM, SK_X_GELU, SK_X_LN = 1, 2, 4, 8, 16, 32, 64
 
 
+class Sm100TensorEntry(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 128), ("dtype", ctypes.c_char * 12), ("ndim", c_int32),
+                ("shape", c_int64 * 8), ("nbytes", c_uint64), ("buf_id", c_uint32)]
+
+
 class Sm100SkinnyArgs(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("x", "w", "bias", "residual", "y", "ws", "counters", "kv_cache", "pos")] + [
         (n, c_int64) for n in ("M", "N", "K", "ld_x", "ld_w", "ld_res", "ld_y")] + [
@@ -198,6 +203,8 @@ SIGNATURES = {
                                                c_int32, c_int32, c_float, c_void_p]),
     "sm100_comm_pick": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),
     "sm100_comm_status": (c_uint32, []),
+    "sm100_safetensors_load": (c_int, [ctypes.c_char_p, POINTER(Sm100TensorEntry), c_int32, POINTER(c_int32)]),
+    "sm100_dsv2pack_load": (c_int, [ctypes.c_char_p, POINTER(Sm100TensorEntry), c_int32, POINTER(c_int32)]),
     "sm100_custom_program": (c_int32, [ctypes.c_char_p, ctypes.c_char_p, POINTER(c_uint32), POINTER(c_uint32),
                                        c_uint32]),
     "sm100_custom_dispatch": (c_int, [c_int32, POINTER(c_uint32), c_uint32, c_uint32, c_uint32]),
