@@ -325,6 +325,10 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
   }
   for (int i = threadIdx.x; i < kGvMaxStages * kGvRows; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
+  // programmatic dependent launch: the weights are static, so the producer
+  // streams them at once, overlapping the previous kernel's tail; the
+  // consumers read x and write y only after that kernel has completed
+  pdl_trigger();
   const size_t row_bytes = (size_t)K * sizeof(WT);
   if (warp == kGvWarps) {
     // producer: chunk c -> stage c % stages, rows [r0 + R c, ...)
@@ -352,6 +356,7 @@ __global__ void __launch_bounds__(kGvThreads, 1) gemv_tma_kernel(LinParams p, in
   const int ks = warp / WPS, rw = warp % WPS;
   const int vbase = ks * NJ * 32 + lane;   // vector j of this lane: vbase + 32 j
   float xr[NJ * V];
+  pdl_wait();
 #pragma unroll
   for (int j = 0; j < NJ; j++) {
     const float4 *src = reinterpret_cast<const float4 *>(p.x + (int64_t)(vbase + 32 * j) * V);
@@ -473,7 +478,8 @@ static int launch_gemv_tma_nj(const LinParams &p, int stages, int stage_floats, 
   cudaError_t e =
       cudaFuncSetAttribute(gemv_tma_kernel<WT, NJ, KS, RW>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGvSmem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemv: smem attribute: %s", cudaGetErrorString(e));
-  gemv_tma_kernel<WT, NJ, KS, RW><<<grid, kGvThreads, kGvSmem, st>>>(p, stages, stage_floats);
+  e = launch_pdl(gemv_tma_kernel<WT, NJ, KS, RW>, dim3(grid), dim3(kGvThreads), kGvSmem, st, p, stages, stage_floats);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemv_tma: %s", cudaGetErrorString(e));
   return launch_status("gemv_tma");
 }
 

@@ -174,20 +174,39 @@ __global__ void __launch_bounds__(128) xl_attn_kernel(float *qkv, int64_t ld_qkv
 // Per row of x [M, N] (row stride ld): the largest value and its first index
 // + idx_offset (a vocabulary shard's place in the whole): the reference's
 // argmax picks the first index of the row maximum (py/thvm/tensor.py:998-1011).
-__global__ void __launch_bounds__(256) xl_argmax_kernel(float *x, int64_t ld, int N, float *val, int32_t *idx,
-                                                         int idx_offset, int zero_x) {
-  __shared__ float sv[8];
-  __shared__ int si[8];
+// one CTA of 1024 threads per row; kVec: 16-byte loads (ld, N multiples of 4
+// and a 16-byte aligned x), each thread's candidates in increasing index
+// order, so the strict compare keeps the first index of the maximum
+template <bool kVec>
+__global__ void __launch_bounds__(1024) xl_argmax_kernel(float *x, int64_t ld, int N, float *val, int32_t *idx,
+                                                          int idx_offset, int zero_x) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
   pdl_trigger();
   pdl_wait();
   const float *xr = x + (int64_t)blockIdx.x * ld;
   float bv = -INFINITY;
   int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < N; i += 256) {
-    const float v = xr[i];
-    if (v > bv || (v == bv && i < bi)) {
-      bv = v;
-      bi = i;
+  if constexpr (kVec) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(xr);
+#pragma unroll 4
+    for (int c = threadIdx.x; c < N / 4; c += 1024) {
+      const float4 f = x4[c];
+      const float v[4] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++)
+        if (v[q] > bv || (v[q] == bv && 4 * c + q < bi)) {   // a thread's indices only grow
+          bv = v[q];
+          bi = 4 * c + q;
+        }
+    }
+  } else {
+    for (int i = threadIdx.x; i < N; i += 1024) {
+      const float v = xr[i];
+      if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+      }
     }
   }
 #pragma unroll
@@ -206,17 +225,23 @@ __global__ void __launch_bounds__(256) xl_argmax_kernel(float *x, int64_t ld, in
   }
   __syncthreads();
   if (zero_x)   // the row is consumed: the next product accumulates into zeros
-    for (int i = threadIdx.x; i < N; i += 256) const_cast<float *>(xr)[i] = 0.0f;
-  if (threadIdx.x == 0) {
-    bv = sv[0];
-    bi = si[0];
-    for (int w = 1; w < 8; w++)
-      if (sv[w] > bv || (sv[w] == bv && si[w] < bi)) {
-        bv = sv[w];
-        bi = si[w];
+    for (int i = threadIdx.x; i < N; i += 1024) const_cast<float *>(xr)[i] = 0.0f;
+  if (warp == 0) {
+    bv = sv[lane];
+    bi = si[lane];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
       }
-    val[blockIdx.x] = bv;
-    idx[blockIdx.x] = bi + idx_offset;
+    }
+    if (lane == 0) {
+      val[blockIdx.x] = bv;
+      idx[blockIdx.x] = bi + idx_offset;
+    }
   }
 }
 
@@ -281,9 +306,12 @@ extern "C" int sm100_xl_attention(float *qkv, int64_t ld_qkv, void *kv_cache, co
 extern "C" int sm100_xl_argmax(float *x, int64_t ld, int32_t M, int32_t N, float *val, int32_t *idx,
                                int32_t idx_offset, int32_t zero_x, void *stream) {
   if (!x || !val || !idx || M < 1 || N < 1 || ld < N) return sm100_set_error(SM100_ERR_ARG, "xl_argmax: bad arguments");
+  const bool vec = ld % 4 == 0 && N % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0;
   const cudaError_t e =
-      launch_pdl(xl_argmax_kernel, dim3(M), dim3(256), 0, (cudaStream_t)stream, x, ld, N, val, idx, idx_offset,
-                 (int)zero_x);
+      vec ? launch_pdl(xl_argmax_kernel<true>, dim3(M), dim3(1024), 0, (cudaStream_t)stream, x, ld, N, val, idx,
+                       idx_offset, (int)zero_x)
+          : launch_pdl(xl_argmax_kernel<false>, dim3(M), dim3(1024), 0, (cudaStream_t)stream, x, ld, N, val, idx,
+                       idx_offset, (int)zero_x);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "xl_argmax: %s", cudaGetErrorString(e));
   return launch_status("xl_argmax");
 }
