@@ -606,6 +606,72 @@ int sm100_custom_dispatch(int32_t prog, const uint32_t *arg_buf_ids, uint32_t n_
 /* the same launch over raw device addresses on `stream` */
 int sm100_custom_launch(int32_t prog, void *const *arg_ptrs, uint32_t n_args, void *stream);
 
+/* ---- generic device interpreter for lifted UOp DAGs ----------------------
+ * Stands in for the rendered kernel (src/codegen/render_uop.c:4964-5113
+ * cg_render_uop_kernel_cuda_root) of a DAG no hand-written kernel covers.
+ * The host compiles the DAG once into a register program (sm100_ref.c); the
+ * device runs it with one thread per output element: the thread's output
+ * coordinates fill the first n_glob range slots (slot n_glob - 1 fastest),
+ * and every REDUCE is a counted loop over its range slots, evaluated in order
+ * as the reference's CPU walker does (src/backend/cpu/uop_walk.c).
+ * Registers hold an int64 or the bits of an f32.  Float arithmetic is f32
+ * rounded per operation; exp2 is the reference's xexp2 decomposition. */
+enum {
+  SM100_IOP_CONST = 1,  /* dst = imm: i32 sign-extended (dt 0), u32 zero-extended (dt 1), f32 bits (dt 2) */
+  SM100_IOP_RANGE,      /* dst = range slot a */
+  SM100_IOP_VAR,        /* dst = vars[a] */
+  SM100_IOP_LOAD,       /* dst = buf a [reg b], buffer dtype dt (SM100_UDT_*) */
+  SM100_IOP_STORE,      /* buf a [reg b] = reg c (float when imm != 0), buffer dtype dt */
+  SM100_IOP_FADD, SM100_IOP_FMUL, SM100_IOP_FNEG, SM100_IOP_FRECIP, SM100_IOP_FEXP2, SM100_IOP_FLOG2,
+  SM100_IOP_FSQRT, SM100_IOP_FSIN, SM100_IOP_FLT, SM100_IOP_FEQ,
+  SM100_IOP_IADD, SM100_IOP_ISUB, SM100_IOP_IMUL, SM100_IOP_INEG,
+  SM100_IOP_IDIV, SM100_IOP_IMOD,  /* in dtype dt (signedness, width); divisor 0 gives 0 */
+  SM100_IOP_ILT, SM100_IOP_ULT, SM100_IOP_IEQ, SM100_IOP_IAND, SM100_IOP_IOR, SM100_IOP_IXOR,
+  SM100_IOP_ISHL, SM100_IOP_ISHR,  /* in dtype dt */
+  SM100_IOP_WRAP,       /* dst = reg a wrapped to int dtype dt (SM100_UDT_*; bool: != 0) */
+  SM100_IOP_I2F,        /* dst = f32(reg a), a of int dtype dt */
+  SM100_IOP_F2I,        /* dst = int dtype dt of f32 reg a, toward zero */
+  SM100_IOP_NARROW,     /* dst = f32 reg a rounded through float dtype dt (f16 / bf16) */
+  SM100_IOP_SEL,        /* dst = reg a != 0 ? reg b : reg c */
+  SM100_IOP_LOOP,       /* slot a = 0; if reg b <= 0 jump past the ENDLOOP at imm */
+  SM100_IOP_ENDLOOP,    /* if ++slot a < reg b jump to imm + 1 (the body after its LOOP) */
+  SM100_IOP_ACCF,       /* dst = dst (+ | max | *) f32 reg a, kind dt (0 sum, 1 max, 2 prod) */
+  SM100_IOP_ACCI,       /* dst = dst (+ | max | *) int reg a, kind imm, wrapped to int dtype dt */
+  SM100_IOP_THREEFRY,   /* dst = threefry2x32 (20 rounds) of u64 reg a keyed by u64 reg b */
+  SM100_IOP_COUNT
+};
+
+/* the interpreter's dtype codes: the reference's DT_* numbering (src/thvm.h:254-271) */
+enum {
+  SM100_UDT_BOOL = 0, SM100_UDT_I8, SM100_UDT_U8, SM100_UDT_I16, SM100_UDT_U16, SM100_UDT_I32, SM100_UDT_U32,
+  SM100_UDT_I64, SM100_UDT_U64, SM100_UDT_FP8E4M3, SM100_UDT_FP8E5M2, SM100_UDT_F16, SM100_UDT_BF16,
+  SM100_UDT_F32, SM100_UDT_F64
+};
+
+typedef struct {
+  uint8_t op, dt;
+  uint16_t dst, a, b, c;
+  int32_t imm;
+} Sm100Insn;
+
+#define SM100_INTERP_MAX_CODE 1280
+#define SM100_INTERP_MAX_REGS 192
+#define SM100_INTERP_MAX_AXES 16
+#define SM100_INTERP_MAX_BUFS 64
+#define SM100_INTERP_MAX_VARS 16
+#define SM100_INTERP_MAX_STEPS (1ll << 26) /* loop iterations per output element */
+
+/* Runs the program once per output element: total = prod(glob_ext[0..n_glob)).
+ * bufs are device addresses (slot 0 is conventionally the output) and
+ * buf_bytes their sizes: a load outside its buffer reads 0, a store outside
+ * is dropped. */
+int sm100_interp_run(const Sm100Insn *code, uint32_t n_code, uint32_t n_regs, uint32_t n_axes, uint32_t n_glob,
+                     const int64_t *glob_ext, void *const *bufs, const int64_t *buf_bytes, uint32_t n_bufs,
+                     const int64_t *vars, uint32_t n_vars, void *stream);
+/* Non-zero when an element's program stopped at SM100_INTERP_MAX_STEPS loop
+ * iterations since the last call (its output is then incomplete); clears. */
+int sm100_interp_status(void);
+
 /* ---- 4. TinyJit replay as CUDA graphs ------------------------------------ */
 /* Capture every launch on the backend stream between begin and end into
  * graph slot `slot` (0..63); replay launches it. */

@@ -26,6 +26,8 @@ package finds its library beside itself) and the reference's GPT-2 model code
                the 16 prompt ids, the 64 generated ids, per-step top-1 / top-2
                logits, and the full logits of the prompt step and the first
                decode step.
+  gpt2_l2.npz  the same model cut to 2 layers: 16 prompt ids and 8 greedy ids
+               (the reference-side router's end-to-end fixture).
 
 Nothing under tests/ reads the reference at test time: only these files.
 """
@@ -196,6 +198,33 @@ def make_gpt2(n_new: int = 64) -> None:
     print("wrote", OUT / "gpt2.npz")
 
 
+def make_gpt2_l2(n_new: int = 8) -> None:
+    """gpt2_l2.npz: the same model code and weight generator cut to 2 layers
+    (seed 0, the same 16 prompt ids), n_new greedy ids: the fixture of the
+    reference-side router's end-to-end tests, which run this model through
+    the reference's own package on the sm_100a device."""
+    import thvm_gpt2 as G
+    from thvm import Tensor, Variable
+    from thvm.nn.state import load_state_dict
+    from thvm_b200.synthetic import GPT2Config, gpt2_weights, prompt_tokens
+
+    cfg = GPT2Config(n_layers=2)
+    params = dict(G.MODEL_PARAMS["gpt2"], n_layers=2)
+    model = G.Transformer(**params)
+    load_state_dict(model, {k: Tensor(v) for k, v in gpt2_weights(cfg, seed=0).items()}, verbose=False)
+    toks = prompt_tokens(16, cfg.vocab, seed=1)
+    prompt = list(toks)
+    start_pos = 0
+    for _ in range(n_new):
+        tk = Tensor([toks]) if start_pos == 0 else Variable("tokens", 0, cfg.vocab - 1).bind(toks[start_pos])
+        sp = Variable("start_pos", 1 if start_pos else 0, cfg.max_ctx - 1).bind(start_pos)
+        nxt = model(tk, sp, 0.0).tolist()[0]
+        start_pos = len(toks)
+        toks.append(nxt)
+    np.savez_compressed(OUT / "gpt2_l2.npz", prompt=np.array(prompt, np.int32), tokens=np.array(toks[16:], np.int32))
+    print("wrote", OUT / "gpt2_l2.npz", toks[16:])
+
+
 def make_dtypes() -> None:
     """bf16 / fp8 e4m3 conversions of the reference library, bit for bit."""
     import ctypes
@@ -255,14 +284,16 @@ def make_state() -> None:
 
 
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["ops", "gpt2", "dtypes", "state"]
+    which = sys.argv[1:] or ["ops", "gpt2", "gpt2_l2", "dtypes", "state"]
     if "dtypes" in which:
         make_dtypes()
-    if "ops" in which or "gpt2" in which or "state" in which:
+    if "ops" in which or "gpt2" in which or "gpt2_l2" in which or "state" in which:
         _setup()
     if "ops" in which:
         make_ops()
     if "gpt2" in which:
         make_gpt2()
+    if "gpt2_l2" in which:
+        make_gpt2_l2()
     if "state" in which:
         make_state()

@@ -76,6 +76,12 @@ class Sm100TensorEntry(ctypes.Structure):
                 ("shape", c_int64 * 8), ("nbytes", c_uint64), ("buf_id", c_uint32)]
 
 
+class Sm100Insn(ctypes.Structure):
+    """One instruction of the generic device interpreter (include/thvm_sm100.h)."""
+    _fields_ = [("op", ctypes.c_uint8), ("dt", ctypes.c_uint8), ("dst", ctypes.c_uint16), ("a", ctypes.c_uint16),
+                ("b", ctypes.c_uint16), ("c", ctypes.c_uint16), ("imm", c_int32)]
+
+
 class Sm100SkinnyArgs(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("x", "w", "bias", "residual", "y", "ws", "counters", "kv_cache", "pos")] + [
         (n, c_int64) for n in ("M", "N", "K", "ld_x", "ld_w", "ld_res", "ld_y")] + [
@@ -209,6 +215,10 @@ SIGNATURES = {
                                        c_uint32]),
     "sm100_custom_dispatch": (c_int, [c_int32, POINTER(c_uint32), c_uint32, c_uint32, c_uint32]),
     "sm100_custom_launch": (c_int, [c_int32, POINTER(c_void_p), c_uint32, c_void_p]),
+    "sm100_interp_run": (c_int, [POINTER(Sm100Insn), c_uint32, c_uint32, c_uint32, c_uint32, POINTER(c_int64),
+                                 POINTER(c_void_p), POINTER(c_int64), c_uint32, POINTER(c_int64), c_uint32,
+                                 c_void_p]),
+    "sm100_interp_status": (c_int, []),
     "sm100_graph_capture_begin": (c_int, [c_uint32]),
     "sm100_graph_capture_end": (c_int, [c_uint32]),
     "sm100_graph_replay": (c_int, [c_uint32]),
