@@ -200,17 +200,18 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
 // sum, partial o_lat) are folded in a fixed order.  The softmax is exp(s -
 // running max) rescaled (expf), the order of the reference's max / exp / sum
 // / divide up to rounding.
-constexpr int kMlaNB = 4, kMlaWarps = 8, kMlaKV = 512, kMlaDR = 64, kMlaMaxD = 128;
+constexpr int kMlaNB = 4, kMlaWarps = 16, kMlaKV = 512, kMlaDR = 64, kMlaMaxD = 128;
+static_assert(kMlaWarps * 32 == kMlaKV, "q_lat: one latent column per thread");
 
 struct MlaSmem {
   static constexpr size_t w = 0;                                              // [128][512] bf16 W_uk[h], then W_uv[h]
   static constexpr size_t qn = w + kMlaMaxD * kMlaKV * 2;                     // [DN][kMlaNB] f32
   static constexpr size_t qpe = qn + kMlaMaxD * kMlaNB * 4;                   // [kMlaNB][64] f32
   static constexpr size_t qlat = qpe + kMlaNB * kMlaDR * 4;                   // [kMlaNB][512] f32 (then o_lat)
-  static constexpr size_t po = qlat + kMlaNB * kMlaKV * 4;                    // [warps][kMlaNB][512] f32
-  static constexpr size_t pm = po + (size_t)kMlaWarps * kMlaNB * kMlaKV * 4;  // [warps][kMlaNB] max
-  static constexpr size_t pl = pm + kMlaWarps * kMlaNB * 4;                   // [warps][kMlaNB] sum
-  static constexpr size_t cur = pl + kMlaWarps * kMlaNB * 4;               // [kMlaNB][512 + 64] bf16 current rows
+  static constexpr size_t po = qlat + kMlaNB * kMlaKV * 4;                    // [warps][512] f32 (one sequence a warp)
+  static constexpr size_t pm = po + (size_t)kMlaWarps * kMlaKV * 4;           // [warps] max
+  static constexpr size_t pl = pm + kMlaWarps * 4;                            // [warps] sum
+  static constexpr size_t cur = pl + kMlaWarps * 4;                        // [kMlaNB][512 + 64] bf16 current rows
   static constexpr size_t bar = cur + kMlaNB * (kMlaKV + kMlaDR) * 2;
   static constexpr size_t total = bar + 16;
 };
@@ -279,32 +280,44 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     if (d < DN) qn[d * kMlaNB + b] = v;
     else qpe[b * kMlaDR + d - DN] = v;
   }
-  if constexpr (kPost) {   // the current latent / key rows (ds_qkv_post's, thread for thread)
-    __shared__ float red[kMlaWarps];
-    for (int b = 0; b < nb; b++) {
+  if constexpr (kPost) {   // the current latent / key rows (ds_qkv_post's arithmetic, in its order)
+    // each 256-thread half takes sequences half, half + 2: thread u sums
+    // elements u and u + 256 and the 8 warp sums are added in order, as
+    // ds_qkv_post_kernel's 256 threads do for one sequence
+    __shared__ float red[kMlaNB][8];
+    __shared__ float s_inv[kMlaNB];
+    const int half = t >> 8, u = t & 255;
+    for (int b = half; b < nb; b += 2) {
       const float *kb = post.qkva + (int64_t)(b0 + b) * post.ld + post.kva_off;
       float ss = 0.0f;
-      for (int i = t; i < kMlaKV; i += kMlaWarps * 32) {
+      for (int i = u; i < kMlaKV; i += 256) {
         const float v = bfr(kb[i]);
         ss = __fmaf_rn(v, v, ss);
       }
       ss = warp_sum(ss);
-      if (lane == 0) red[warp] = ss;
-      __syncthreads();
+      if (lane == 0) red[b][(u >> 5)] = ss;
+    }
+    __syncthreads();
+    if (t < nb) {
       float tot = 0.0f;
 #pragma unroll
-      for (int w = 0; w < kMlaWarps; w++) tot += red[w];
-      __syncthreads();
-      const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)kMlaKV), post.eps)));
-      __nv_bfloat16 *crow = cur + b * (kMlaKV + kMlaDR), *prow = crow + kMlaKV;
-      for (int i = t; i < kMlaKV; i += kMlaWarps * 32)
-        crow[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(bfr(kb[i]), inv), post.g_kv[i]));
-      for (int j = t; j < kMlaDR / 2; j += kMlaWarps * 32) {
-        const float xe = bfr(kb[kMlaKV + 2 * j]), xo = bfr(kb[kMlaKV + 2 * j + 1]);
-        const float c = post.cs[(int64_t)p * kMlaDR + j], sv = post.sn[(int64_t)p * kMlaDR + j];
-        prow[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, sv)));
-        prow[kMlaDR / 2 + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, sv)));
-      }
+      for (int w = 0; w < 8; w++) tot += red[t][w];
+      s_inv[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(tot, 1.0f / (float)kMlaKV), post.eps)));
+    }
+    __syncthreads();
+    for (int i = t; i < nb * kMlaKV; i += kMlaWarps * 32) {
+      const int b = i / kMlaKV, k = i % kMlaKV;
+      const float *kb = post.qkva + (int64_t)(b0 + b) * post.ld + post.kva_off;
+      cur[b * (kMlaKV + kMlaDR) + k] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(bfr(kb[k]), s_inv[b]), post.g_kv[k]));
+    }
+    for (int i = t; i < nb * (kMlaDR / 2); i += kMlaWarps * 32) {
+      const int b = i / (kMlaDR / 2), j = i % (kMlaDR / 2);
+      const float *kb = post.qkva + (int64_t)(b0 + b) * post.ld + post.kva_off;
+      __nv_bfloat16 *prow = cur + b * (kMlaKV + kMlaDR) + kMlaKV;
+      const float xe = bfr(kb[kMlaKV + 2 * j]), xo = bfr(kb[kMlaKV + 2 * j + 1]);
+      const float c = post.cs[(int64_t)p * kMlaDR + j], sv = post.sn[(int64_t)p * kMlaDR + j];
+      prow[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, sv)));
+      prow[kMlaDR / 2 + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, sv)));
     }
     __syncthreads();
     if (h == 0)   // one head's CTAs keep the rows for the later steps
@@ -317,27 +330,21 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   }
   __syncthreads();
   const bool wk_ok = mbar_wait(bar, 0, status, false);
-  // q_lat[b][k] = sum_d q_nope[b][d] W_uk[h][d][k], k = t and t + 256
+  // q_lat[b][k] = sum_d q_nope[b][d] W_uk[h][d][k], k = t
   {
-    float a[NB][2] = {};
+    float a[NB] = {};
     if (wk_ok) {
-#pragma unroll 4
+#pragma unroll 8
       for (int d = 0; d < DN; d++) {
         const float4 q4 = reinterpret_cast<const float4 *>(qn)[d];
-        const float w0 = bf(wb[d * kMlaKV + t]), w1 = bf(wb[d * kMlaKV + t + 256]);
+        const float w0 = bf(wb[d * kMlaKV + t]);
         const float qq[4] = {q4.x, q4.y, q4.z, q4.w};
 #pragma unroll
-        for (int b = 0; b < NB; b++) {
-          a[b][0] = fmaf(qq[b], w0, a[b][0]);
-          a[b][1] = fmaf(qq[b], w1, a[b][1]);
-        }
+        for (int b = 0; b < NB; b++) a[b] = fmaf(qq[b], w0, a[b]);
       }
     }
 #pragma unroll
-    for (int b = 0; b < NB; b++) {
-      qlat[b * kMlaKV + t] = a[b][0];
-      qlat[b * kMlaKV + t + 256] = a[b][1];
-    }
+    for (int b = 0; b < NB; b++) qlat[b * kMlaKV + t] = a[b];
   }
   __syncthreads();
   if (t == 0) {   // W_uv[h] into the same buffer (every read of W_uk is done)
@@ -345,8 +352,12 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     mbar_expect_tx(bar, (uint32_t)(DV * kMlaKV * 2));
     bulk_g2s(wb, wuv + (int64_t)h * DV * kMlaKV, (uint32_t)(DV * kMlaKV * 2), bar);
   }
-  // one pass over each sequence's rows: warp w takes rows w, w + 8, ...
-  for (int b = 0; b < nb; b++) {
+  // one pass over each sequence's rows: the warps are split evenly over the
+  // NB sequences (kMlaWarps / NB each), and warp j of sequence b takes its
+  // rows j, j + kMlaWarps / NB, ...
+  constexpr int kWpb = kMlaWarps / NB;
+  {
+    const int b = warp / kWpb, j0 = warp % kWpb;
     const float *ql = qlat + b * kMlaKV;
     float qk[16], qp[8], oa[16];
 #pragma unroll
@@ -359,7 +370,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     float m = -INFINITY, l = 0.0f;
     const __nv_bfloat16 *cb = cc + (int64_t)(b0 + b) * ctx * kMlaKV, *pb = cpe + (int64_t)(b0 + b) * ctx * kMlaDR;
 #pragma unroll 4
-    for (int r = warp; r < T; r += kMlaWarps) {
+    for (int r = j0; r < T && b < nb; r += kWpb) {
       // with kPost the current row is the one in shared memory
       const __nv_bfloat16 *crow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) : cb + (int64_t)r * kMlaKV;
       const __nv_bfloat16 *prow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) + kMlaKV : pb + (int64_t)r * kMlaDR;
@@ -389,32 +400,39 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
       for (int j = 0; j < 16; j++) oa[j] = fmaf(p, cv[j], oa[j] * cr);
       m = mn;
     }
-    float *pob = po + ((size_t)warp * kMlaNB + b) * kMlaKV;
+    float *pob = po + (size_t)warp * kMlaKV;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
       pob[8 * lane + j] = oa[j];
       pob[256 + 8 * lane + j] = oa[8 + j];
     }
     if (lane == 0) {
-      pm[warp * kMlaNB + b] = m;
-      pl[warp * kMlaNB + b] = l;
+      pm[warp] = m;
+      pl[warp] = l;
     }
   }
   __syncthreads();
-  // fold the warps in order: o_lat[b][k] = sum_w e^(m_w - M) o_w[k] / sum_w e^(m_w - M) l_w
+  // fold a sequence's warps in order: o_lat[b][k] = sum_w f_w o_w[k] / sum_w f_w l_w,
+  // f_w = e^(m_w - M); the factors once per warp, then one pass over the columns
+  __shared__ float s_f[kMlaWarps], s_L[kMlaNB];
+  if (t < nb) {
+    float M = -INFINITY;
+    for (int w = t * kWpb; w < (t + 1) * kWpb; w++) M = fmaxf(M, pm[w]);
+    float L = 0.0f;
+    for (int w = t * kWpb; w < (t + 1) * kWpb; w++) {
+      const float f = pm[w] == -INFINITY ? 0.0f : expf(pm[w] - M);
+      s_f[w] = f;
+      L = fmaf(f, pl[w], L);
+    }
+    s_L[t] = L;
+  }
+  __syncthreads();
   for (int i = t; i < nb * kMlaKV; i += kMlaWarps * 32) {
     const int b = i / kMlaKV, k = i % kMlaKV;
-    float M = -INFINITY;
+    float acc = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kMlaWarps; w++) M = fmaxf(M, pm[w * kMlaNB + b]);
-    float L = 0.0f, acc = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kMlaWarps; w++) {
-      const float mw = pm[w * kMlaNB + b], f = mw == -INFINITY ? 0.0f : expf(mw - M);
-      L = fmaf(f, pl[w * kMlaNB + b], L);
-      acc = fmaf(f, po[((size_t)w * kMlaNB + b) * kMlaKV + k], acc);
-    }
-    qlat[b * kMlaKV + k] = acc / L;
+    for (int w = 0; w < kWpb; w++) acc = fmaf(s_f[b * kWpb + w], po[(size_t)(b * kWpb + w) * kMlaKV + k], acc);
+    qlat[b * kMlaKV + k] = acc / s_L[b];
   }
   __syncthreads();
   const bool wv_ok = mbar_wait(bar, 1, status, false);
