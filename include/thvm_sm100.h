@@ -638,6 +638,7 @@ enum {
   SM100_IOP_ACCF,       /* dst = dst (+ | max | *) f32 reg a, kind dt (0 sum, 1 max, 2 prod) */
   SM100_IOP_ACCI,       /* dst = dst (+ | max | *) int reg a, kind imm, wrapped to int dtype dt */
   SM100_IOP_THREEFRY,   /* dst = threefry2x32 (20 rounds) of u64 reg a keyed by u64 reg b */
+  SM100_IOP_SETR,       /* range slot a = reg b (a range bound to a computed index: a gather) */
   SM100_IOP_COUNT
 };
 

@@ -126,12 +126,13 @@ SM100_HD int sm100_i_isfloat(int dt) {
   return dt == SM100_UDT_F16 || dt == SM100_UDT_BF16 || dt == SM100_UDT_F32 || dt == SM100_UDT_F64;
 }
 
-SM100_HD int64_t sm100_i_size(int dt) {
+/* log2 of the element size of dtype dt */
+SM100_HD int sm100_i_shift(int dt) {
   switch (dt) {
-    case SM100_UDT_BOOL: case SM100_UDT_I8: case SM100_UDT_U8: return 1;
-    case SM100_UDT_I16: case SM100_UDT_U16: case SM100_UDT_F16: case SM100_UDT_BF16: return 2;
-    case SM100_UDT_I64: case SM100_UDT_U64: case SM100_UDT_F64: return 8;
-    default: return 4;
+    case SM100_UDT_BOOL: case SM100_UDT_I8: case SM100_UDT_U8: return 0;
+    case SM100_UDT_I16: case SM100_UDT_U16: case SM100_UDT_F16: case SM100_UDT_BF16: return 1;
+    case SM100_UDT_I64: case SM100_UDT_U64: case SM100_UDT_F64: return 3;
+    default: return 2;
   }
 }
 
@@ -209,7 +210,9 @@ SM100_HD int sm100_interp_exec(const Sm100Insn *code, uint32_t n_code, int64_t *
   int64_t steps = 0; /* loop back-edges taken: a program past the budget stops (returns 1) */
   for (uint32_t pc = 0; pc < n_code; pc++) {
     const Sm100Insn in = code[pc];
-    const int64_t A = r[in.a], B = r[in.b];
+    /* operand registers are read by the ops that use them */
+#define A r[in.a]
+#define B r[in.b]
     switch (in.op) {
       case SM100_IOP_CONST:
         r[in.dst] = in.dt == 0 ? (int64_t)in.imm : (int64_t)(uint32_t)in.imm;
@@ -217,13 +220,13 @@ SM100_HD int sm100_interp_exec(const Sm100Insn *code, uint32_t n_code, int64_t *
       case SM100_IOP_RANGE: r[in.dst] = idx[in.a]; break;
       case SM100_IOP_VAR: r[in.dst] = vars[in.a]; break;
       case SM100_IOP_LOAD: {
-        const int64_t sz = sm100_i_size(in.dt);
-        r[in.dst] = (B >= 0 && B < buf_bytes[in.a] / sz) ? sm100_i_load(bufs[in.a], B, in.dt) : 0;
+        const int64_t off = B;
+        r[in.dst] = (off >= 0 && off < (buf_bytes[in.a] >> sm100_i_shift(in.dt))) ? sm100_i_load(bufs[in.a], off, in.dt) : 0;
         break;
       }
       case SM100_IOP_STORE: {
-        const int64_t sz = sm100_i_size(in.dt);
-        if (B >= 0 && B < buf_bytes[in.a] / sz) sm100_i_store(bufs[in.a], B, in.dt, r[in.c]);
+        const int64_t off = B;
+        if (off >= 0 && off < (buf_bytes[in.a] >> sm100_i_shift(in.dt))) sm100_i_store(bufs[in.a], off, in.dt, r[in.c]);
         break;
       }
       case SM100_IOP_FADD: r[in.dst] = sm100_i_r(SM100_FADD(sm100_i_f(A), sm100_i_f(B))); break;
@@ -308,8 +311,11 @@ SM100_HD int sm100_interp_exec(const Sm100Insn *code, uint32_t n_code, int64_t *
         break;
       }
       case SM100_IOP_THREEFRY: r[in.dst] = (int64_t)sm100_i_threefry((uint64_t)A, (uint64_t)B); break;
+      case SM100_IOP_SETR: idx[in.a] = B; break;
       default: break;
     }
+#undef A
+#undef B
   }
   return 0;
 }

@@ -181,8 +181,13 @@ static void sm100_dump(FILE *f, Term t, int depth) {
 /* ---- the DAG -> register program compiler ---------------------------------- */
 
 #define SM100_MEMO_CAP 1024
+#define SM100_MAX_PRE 16   /* pre-pass programs of a family */
+#define SM100_MAX_SCR 16   /* scratch buffers of a family */
+#define SM100_AX_CHUNK 62  /* axis ids of the pre-pass programs' own ranges */
+#define SM100_AX_STEP 63
 
-typedef struct {
+typedef struct Sm100Prog Sm100Prog;
+struct Sm100Prog {
   /* the program */
   Sm100Insn code[SM100_INTERP_MAX_CODE];
   u32 n_code, n_regs;
@@ -199,7 +204,28 @@ typedef struct {
   u32 n_dep;
   int bad;
   char why[160];
-} Sm100Prog;
+  /* Reduces that every output element would recompute (they read no range
+   * of this program's fastest output axis, or run long) move to pre-pass
+   * programs of the family: P1 folds chunks of about sqrt(E) iterations into
+   * partials, P2 folds each output row's partials in chunk order, and the
+   * readers load the result from scratch.  The family lives on its root
+   * program: pre-passes run in list order before it, each with buffer slot
+   * 0 bound to its scratch output, slots 1..n_in to the kernel's inputs and
+   * slots n_in + 1 + j to scratch j. */
+  Sm100Prog *root;
+  u32 n_in;
+  int allow_pre;
+  Sm100Prog *pre[SM100_MAX_PRE];
+  int pre_out[SM100_MAX_PRE];
+  u32 n_pre;
+  u64 scr_bytes[SM100_MAX_SCR];
+  void *scr_ptr[SM100_MAX_SCR];
+  u32 n_scr;
+  Term ur_t[SM100_MAX_PRE];    /* hoisted reduces and their result scratch / row axes */
+  u32 ur_scr[SM100_MAX_PRE], ur_dt[SM100_MAX_PRE];
+  u64 ur_dmask[SM100_MAX_PRE];
+  u32 n_ur;
+};
 
 static void sp_fail(Sm100Prog *p, const char *fmt, ...) {
   if (p->bad) return;
@@ -387,12 +413,308 @@ static u16 sp_memo_get(Sm100Prog *p, Term t, int *hit) {
 
 static void sp_hoist(Sm100Prog *p, Term t, int depth);
 
+/* f at range `axis` = x, for an int expression of that range and constants
+ * only (no load); *ok cleared for anything else */
+static i64 sp_eval_pure(Term t, u32 axis, i64 x, int *ok, int depth) {
+  if (!*ok || depth > 48 || term_tag(t) != TAG_UOP) {
+    *ok = 0;
+    return 0;
+  }
+  const u64 loc = term_val(t);
+  switch (term_ext(t)) {
+    case UOP_CONST: {
+      const u32 dt = term_ext(heap_read(loc)), bits = (u32)term_val(heap_read(loc));
+      if (sp_isfloat(dt)) break;
+      return dtype_kind(dt) == DK_UINT ? (i64)bits : (i64)(i32)bits;
+    }
+    case UOP_RANGE:
+      if (uop_range_axis_id(t) == axis) return x;
+      break;
+    case UOP_OPT: return sp_eval_pure(heap_read(loc), axis, x, ok, depth + 1);
+    case UOP_NEG: return -sp_eval_pure(heap_read(loc), axis, x, ok, depth + 1);
+    case UOP_ADD: case UOP_IADD: case UOP_ISUB: case UOP_MUL: case UOP_IMUL: case UOP_IDIV: case UOP_IMOD: {
+      const i64 a = sp_eval_pure(heap_read(loc), axis, x, ok, depth + 1);
+      const i64 b = sp_eval_pure(heap_read(loc + 1), axis, x, ok, depth + 1);
+      switch (term_ext(t)) {
+        case UOP_ADD: case UOP_IADD: return a + b;
+        case UOP_ISUB: return a - b;
+        case UOP_MUL: case UOP_IMUL: return a * b;
+        case UOP_IDIV: return b ? a / b : 0;
+        default: return b ? a % b : 0;
+      }
+    }
+    default: break;
+  }
+  *ok = 0;
+  return 0;
+}
+
+/* A one-hot reduce: SUM over v of IWHERE(f(v) == key, a(v), 0) with f the
+ * identity over v's range (checked at every v) and key not reading v is the
+ * gather a(key) for 0 <= key < extent, else 0: exactly the sum's one
+ * non-zero term (the tinygrad embedding, py/thvm/tensor.py's one-hot
+ * product).  Returns the register, or -1 when t is not of that form. */
+static int sp_onehot(Sm100Prog *p, Term t, int is_int) {
+  if (uop_reduce_kind(t) != REDUCE_SUM || uop_reduce_n_axes(t) != 1) return -1;
+  const u32 ax = uop_reduce_axis(t, 0);
+  Term body = uop_reduce_src(t);
+  if (!sm100_is(body, UOP_IWHERE)) return -1;
+  Term c = heap_read(term_val(body)), a = heap_read(term_val(body) + 1), z = heap_read(term_val(body) + 2);
+  u32 zbits = 1;
+  if (!(sm100_is(z, UOP_INVALID) || (sm100_is(z, UOP_CONST) && (zbits = (u32)term_val(heap_read(term_val(z)))) == 0)))
+    return -1;
+  while (sm100_is(c, UOP_CAST)) c = heap_read(term_val(c));
+  if (!sm100_is(c, UOP_CMPEQ)) return -1;
+  Term f = heap_read(term_val(c)), key = heap_read(term_val(c) + 1);
+  const u64 bit = 1ull << (ax & 63);
+  if (sp_deps(p, f) != bit) {
+    Term tmp = f;
+    f = key, key = tmp;
+  }
+  if (sp_deps(p, f) != bit || (sp_deps(p, key) & bit) || sp_isfloat(sp_ty(p, f)) || sp_isfloat(sp_ty(p, key)))
+    return -1;
+  Term rg = sp_find_range(a, ax, 0);
+  if (!rg) rg = sp_find_range(f, ax, 0);
+  if (!rg) return -1;
+  const u32 ext = uop_range_extent(rg);
+  if ((ext & KVAR_FLAG) || ext == 0 || ext > (1u << 24) || sp_slot(p, ax) >= 0) return -1;
+  int ok = 1;
+  for (u32 v = 0; v < ext && ok; v++) {
+    const i64 fv = sp_eval_pure(f, ax, v, &ok, 0);
+    ok = ok && fv == (i64)v;
+  }
+  if (!ok) return -1;
+  const u16 k = sp_int(p, key);
+  const u16 inb = sp_op(p, SM100_IOP_IAND, 0, sp_op(p, SM100_IOP_ILT, 0, sp_const_i(p, -1), k, 0, 0),
+                        sp_op(p, SM100_IOP_ILT, 0, k, sp_const_i(p, ext), 0, 0), 0, 0);
+  const u16 zero_i = sp_const_i(p, 0);
+  const int slot = sp_new_slot(p, ax);
+  sp_emit(p, SM100_IOP_SETR, 0, 0, (u16)slot, sp_op(p, SM100_IOP_SEL, 0, inb, k, zero_i, 0), 0, 0);
+  const u32 memo0 = p->n_memo;
+  const u64 bound0 = p->bound;
+  p->bound |= bit;
+  u16 r;
+  if (!is_int) {
+    const u16 zf = sp_const_f(p, 0.0f);
+    /* 0 + a(key), as the sum's first non-zero step rounds it (a -0 becomes +0) */
+    r = sp_op(p, SM100_IOP_FADD, 0, zf, sp_op(p, SM100_IOP_SEL, 0, inb, sp_float(p, a), zf, 0), 0, 0);
+  } else {
+    r = sp_op(p, SM100_IOP_SEL, 0, inb, sp_int(p, a), zero_i, 0);
+  }
+  p->n_memo = memo0;
+  p->bound = bound0;
+  return p->bad ? -1 : r;
+}
+
+static void sp_compile_family(Sm100Prog *p, Sm100Prog *root, u32 n_in);
+static u16 sp_reduce(Sm100Prog *p, Term t);
+
+/* the chain of same-kind REDUCEs at t: its axes, extents (static) and body */
+static int sp_chain(Term t, u32 *axes, u32 *ext, u32 *n, Term *body) {
+  const u32 kind = uop_reduce_kind(t);
+  Term cur = t;
+  *n = 0;
+  while (sm100_is(cur, UOP_REDUCE) && uop_reduce_kind(cur) == kind) {
+    Term src = uop_reduce_src(cur);
+    for (u32 i = 0; i < uop_reduce_n_axes(cur); i++) {
+      const u32 ax = uop_reduce_axis(cur, i);
+      Term rg = sp_find_range(src, ax, 0);
+      if (!rg || *n >= 4) return 0;
+      const u32 e = uop_range_extent(rg);
+      if (e & KVAR_FLAG) return 0;
+      axes[*n] = ax, ext[(*n)++] = e;
+    }
+    *body = src;
+    cur = src;
+  }
+  return *n > 0;
+}
+
+static int sp_new_scratch(Sm100Prog *root, u64 bytes) {
+  if (root->n_scr >= SM100_MAX_SCR || root->n_in + 1 + root->n_scr >= SM100_INTERP_MAX_BUFS) return -1;
+  root->scr_bytes[root->n_scr] = bytes ? bytes : 8;
+  return (int)root->n_scr++;
+}
+
+/* linear index of this program's output coordinates on the axes in dmask
+ * (in slot order), and the number of rows it spans (static upper bound) */
+static u16 sp_row_index(Sm100Prog *p, u64 dmask, u64 *rows) {
+  u16 lin = sp_const_i(p, 0);
+  *rows = 1;
+  for (u32 s2 = 0; s2 < p->n_glob; s2++) {
+    if (!(dmask & (1ull << (p->axis_id[s2] & 63)))) continue;
+    lin = sp_op(p, SM100_IOP_IMUL, 0, lin, sp_extent(p, p->glob_packed[s2]), 0, 0);
+    lin = sp_op(p, SM100_IOP_IADD, 0, lin, sp_op(p, SM100_IOP_RANGE, 0, (u16)s2, 0, 0, 0), 0, 0);
+    *rows *= kvar_extent_static(p->glob_packed[s2]);
+  }
+  return lin;
+}
+
+/* a new program of the family over the root program's output axes in dmask
+ * (same axis ids, slot order, packed extents), plus the chunk axis when
+ * nchunk > 0 */
+static Sm100Prog *sp_child(Sm100Prog *p, u64 dmask, u32 nchunk) {
+  Sm100Prog *c = (Sm100Prog *)malloc(sizeof(Sm100Prog));
+  if (!c) return NULL;
+  sp_compile_family(c, p->root, p->root->n_in);
+  for (u32 s2 = 0; s2 < p->n_glob; s2++) {
+    if (!(dmask & (1ull << (p->axis_id[s2] & 63)))) continue;
+    const int k = sp_new_slot(c, p->axis_id[s2]);
+    c->glob_packed[k] = p->glob_packed[s2];
+    c->bound |= 1ull << (p->axis_id[s2] & 63);
+  }
+  if (nchunk) {
+    const int k = sp_new_slot(c, SM100_AX_CHUNK);
+    c->glob_packed[k] = nchunk;
+    c->bound |= 1ull << SM100_AX_CHUNK;
+  }
+  c->n_glob = c->n_axes;
+  return c;
+}
+
+static int sp_add_pre(Sm100Prog *root, Sm100Prog *c, int out_scr) {
+  if (root->n_pre >= SM100_MAX_PRE || c->bad) return 0;
+  root->pre[root->n_pre] = c;
+  root->pre_out[root->n_pre++] = out_scr;
+  return 1;
+}
+
+/* The reduce t as a load of its pre-pass result, or -1 when it stays inline. */
+static int sp_prepass(Sm100Prog *p, Term t, int is_int, u32 dt) {
+  Sm100Prog *root = p->root;
+  if (!root || !root->allow_pre || p->bad) return -1;
+  const u64 d = sp_deps(p, t);
+  u64 gmask = 0;
+  for (u32 s2 = 0; s2 < p->n_glob; s2++) gmask |= 1ull << (p->axis_id[s2] & 63);
+  if (d & ~gmask) return -1;   /* reads a range of an enclosing loop: stays inline */
+  u32 axes[4], ext[4], n;
+  Term body;
+  if (!sp_chain(t, axes, ext, &n, &body)) return -1;
+  u64 E = 1;
+  for (u32 i = 0; i < n; i++) E *= ext[i];
+  /* worth it: the reduce is the same for every element of some output axis, or long */
+  if (E < 64 || (d == gmask && E < 4096)) return -1;
+  for (u32 i = 0; i < n; i++)
+    if (axes[i] >= SM100_AX_CHUNK) return -1;
+  const u32 kind = uop_reduce_kind(t);
+  const u8 sdt = is_int ? (u8)DT_INT64 : (u8)DT_FP32;
+  for (u32 i = 0; i < root->n_ur; i++)
+    if (root->ur_t[i] == t) {
+      u64 rows;
+      const u16 lin = sp_row_index(p, root->ur_dmask[i], &rows);
+      return sp_op(p, SM100_IOP_LOAD, sdt, (u16)(root->n_in + 1 + root->ur_scr[i]), lin, 0, 0);
+    }
+  if (root->n_ur >= SM100_MAX_PRE || root->n_pre + 2 > SM100_MAX_PRE) return -1;
+  u32 L = 1;
+  while ((u64)L * L < E) L++;
+  const u32 NC = (u32)((E + L - 1) / L);
+  u64 rows = 1;
+  for (u32 s2 = 0; s2 < p->n_glob; s2++)
+    if (d & (1ull << (p->axis_id[s2] & 63))) rows *= kvar_extent_static(p->glob_packed[s2]);
+  const int s_part = sp_new_scratch(root, rows * NC * 8), s_res = sp_new_scratch(root, rows * 8);
+  if (s_part < 0 || s_res < 0) return -1;
+  /* P1: partial[row][c] = fold over the chunk's iterations */
+  Sm100Prog *p1 = sp_child(p, d, NC);
+  if (!p1) return -1;
+  {
+    const int cs = p1->n_glob - 1;
+    u64 r1;
+    const u16 lin = sp_row_index(p1, d, &r1);
+    const u16 cidx = sp_op(p1, SM100_IOP_RANGE, 0, (u16)cs, 0, 0, 0);
+    const u16 Lr = sp_const_i(p1, L), Er = sp_const_i(p1, (i64)E);
+    sp_hoist(p1, body, 0);
+    /* the accumulator and the identity the padded iterations add: two registers */
+    u16 acc, ident;
+    if (!is_int) {
+      const float id = kind == REDUCE_MAX ? -INFINITY : kind == REDUCE_PROD ? 1.0f : 0.0f;
+      acc = sp_const_f(p1, id), ident = sp_const_f(p1, id);
+    } else {
+      const i64 id = kind == REDUCE_PROD ? 1 : (kind == REDUCE_MAX && dtype_is_signed(dt))
+                                                 ? sm100_i_wrap((int)dt, (i64)((u64)1 << (dtype_info(dt)->bits - 1)))
+                                                 : 0;
+      acc = sp_const_i(p1, id), ident = sp_const_i(p1, id);
+    }
+    const u16 base = sp_op(p1, SM100_IOP_IMUL, 0, cidx, Lr, 0, 0);
+    const int js = sp_new_slot(p1, SM100_AX_STEP);
+    const u32 loop_pc = sp_emit(p1, SM100_IOP_LOOP, 0, 0, (u16)js, Lr, 0, 0);
+    const u32 memo0 = p1->n_memo;
+    p1->bound |= 1ull << SM100_AX_STEP;
+    u16 vf = sp_op(p1, SM100_IOP_IADD, 0, base, sp_op(p1, SM100_IOP_RANGE, 0, (u16)js, 0, 0, 0), 0, 0);
+    const u16 valid = sp_op(p1, SM100_IOP_ILT, 0, vf, Er, 0, 0);
+    for (int i = (int)n - 1; i >= 0; i--) {   /* the flat index into the chain's axes, last fastest */
+      const int as = sp_new_slot(p1, axes[i]);
+      const u16 er = sp_const_i(p1, ext[i]);
+      sp_emit(p1, SM100_IOP_SETR, 0, 0, (u16)as, sp_op(p1, SM100_IOP_IMOD, DT_INT64, vf, er, 0, 0), 0, 0);
+      vf = sp_op(p1, SM100_IOP_IDIV, DT_INT64, vf, er, 0, 0);
+      p1->bound |= 1ull << (axes[i] & 63);
+    }
+    if (!is_int) {
+      const u16 v = sp_float(p1, body);
+      sp_emit(p1, SM100_IOP_ACCF, (u8)(kind == REDUCE_MAX ? 1 : kind == REDUCE_PROD ? 2 : 0), acc,
+              sp_op(p1, SM100_IOP_SEL, 0, valid, v, ident, 0), 0, 0, 0);
+    } else {
+      const u16 v = sp_int(p1, body);
+      sp_emit(p1, SM100_IOP_ACCI, (u8)dt, acc, sp_op(p1, SM100_IOP_SEL, 0, valid, v, ident, 0), 0, 0, (i32)kind);
+    }
+    const u32 end = sp_emit(p1, SM100_IOP_ENDLOOP, 0, 0, (u16)js, Lr, 0, (i32)loop_pc);
+    if (!p1->bad) p1->code[loop_pc].imm = (i32)end;
+    p1->n_memo = memo0;
+    const u16 off = sp_op(p1, SM100_IOP_IADD, 0, sp_op(p1, SM100_IOP_IMUL, 0, lin, sp_const_i(p1, NC), 0, 0), cidx, 0, 0);
+    sp_emit(p1, SM100_IOP_STORE, sdt, 0, 0, off, acc, !is_int);
+  }
+  if (p1->bad || !sp_add_pre(root, p1, s_part)) {
+    free(p1);
+    return -1;
+  }
+  /* P2: result[row] = fold over the row's partials in chunk order */
+  Sm100Prog *p2 = sp_child(p, d, 0);
+  if (!p2) return -1;
+  {
+    u64 r2;
+    const u16 lin = sp_row_index(p2, d, &r2);
+    const u16 base = sp_op(p2, SM100_IOP_IMUL, 0, lin, sp_const_i(p2, NC), 0, 0), NCr = sp_const_i(p2, NC);
+    u16 acc;
+    if (!is_int) acc = sp_const_f(p2, kind == REDUCE_MAX ? -INFINITY : kind == REDUCE_PROD ? 1.0f : 0.0f);
+    else acc = sp_const_i(p2, kind == REDUCE_PROD ? 1 : (kind == REDUCE_MAX && dtype_is_signed(dt))
+                                                            ? sm100_i_wrap((int)dt, (i64)((u64)1 << (dtype_info(dt)->bits - 1)))
+                                                            : 0);
+    const int cs = sp_new_slot(p2, SM100_AX_CHUNK);
+    const u32 loop_pc = sp_emit(p2, SM100_IOP_LOOP, 0, 0, (u16)cs, NCr, 0, 0);
+    const u16 v = sp_op(p2, SM100_IOP_LOAD, sdt, (u16)(root->n_in + 1 + s_part),
+                        sp_op(p2, SM100_IOP_IADD, 0, base, sp_op(p2, SM100_IOP_RANGE, 0, (u16)cs, 0, 0, 0), 0, 0), 0, 0);
+    if (!is_int) sp_emit(p2, SM100_IOP_ACCF, (u8)(kind == REDUCE_MAX ? 1 : kind == REDUCE_PROD ? 2 : 0), acc, v, 0, 0, 0);
+    else sp_emit(p2, SM100_IOP_ACCI, (u8)dt, acc, v, 0, 0, (i32)kind);
+    const u32 end = sp_emit(p2, SM100_IOP_ENDLOOP, 0, 0, (u16)cs, NCr, 0, (i32)loop_pc);
+    if (!p2->bad) p2->code[loop_pc].imm = (i32)end;
+    sp_emit(p2, SM100_IOP_STORE, sdt, 0, 0, lin, acc, !is_int);
+  }
+  if (p2->bad || !sp_add_pre(root, p2, s_res)) {
+    free(p2);
+    root->n_pre--;   /* P1 without its P2 is useless; it is freed with the family */
+    free(p1);
+    return -1;
+  }
+  root->ur_t[root->n_ur] = t, root->ur_scr[root->n_ur] = (u32)s_res, root->ur_dt[root->n_ur] = sdt;
+  root->ur_dmask[root->n_ur++] = d;
+  u64 rows3;
+  const u16 lin = sp_row_index(p, d, &rows3);
+  return sp_op(p, SM100_IOP_LOAD, sdt, (u16)(root->n_in + 1 + (u32)s_res), lin, 0, 0);
+}
+
 static u16 sp_reduce(Sm100Prog *p, Term t) {
   const u32 kind = uop_reduce_kind(t);
   u32 dt = DT_FP32;
   (void)term_dtype_in(t, 0, &dt);
   const int is_int = dtype_is_bool(dt) || dtype_is_int(dt);
   if (!is_int && dt == DT_FP64) sp_fail(p, "f64 reduce");
+  if (!is_int || !dtype_is_bool(dt)) {
+    const int g = sp_onehot(p, t, is_int);
+    if (g >= 0) return (u16)g;
+  }
+  {
+    const int h = sp_prepass(p, t, is_int, dt);
+    if (h >= 0) return (u16)h;
+  }
   /* a chain of same-kind REDUCEs is one loop nest with one accumulator, as
    * the walker folds it (uop_walk.c uwalk_run_reduce) */
   u32 axes[SM100_INTERP_MAX_AXES], n = 0;
@@ -686,9 +1008,23 @@ static int sp_collect_glob(Sm100Prog *p, Term t, int depth) {
  * buffer slot out_slot (dtype out_dt).  With `lin_glob` the address is not
  * taken from the DAG: the output is the dense row-major block over the given
  * axes (used for a linear's A-side scratch). */
-static void sp_compile(Sm100Prog *p, Term addr, Term value, u32 out_slot, u32 out_dt, const Term *lin_glob,
-                       u32 n_lin) {
+/* an empty program of root's family (root == p: a family of its own) */
+static void sp_compile_family(Sm100Prog *p, Sm100Prog *root, u32 n_in) {
   memset(p, 0, sizeof *p);
+  p->root = root ? root : p;
+  p->n_in = n_in;
+}
+
+static void sp_free_family(Sm100Prog *p) {
+  if (!p) return;
+  for (u32 i = 0; i < p->n_pre; i++) free(p->pre[i]);
+  free(p);
+}
+
+static void sp_compile(Sm100Prog *p, Term addr, Term value, u32 out_slot, u32 out_dt, const Term *lin_glob,
+                       u32 n_lin, u32 n_in, int allow_pre) {
+  sp_compile_family(p, NULL, n_in);
+  p->allow_pre = allow_pre;
   if (lin_glob) {
     for (u32 i = 0; i < n_lin; i++) {
       int s = sp_new_slot(p, uop_range_axis_id(lin_glob[i]));
@@ -744,8 +1080,8 @@ static Sm100Plan SM100_PLANS[SM100_PLAN_CAP];
 static u32 SM100_N_PLANS;
 
 static void sm100_plan_free(Sm100Plan *pl) {
-  free(pl->pro);
-  free(pl->prog);
+  sp_free_family(pl->pro);
+  sp_free_family(pl->prog);
   pl->pro = pl->prog = NULL;
 }
 
@@ -831,10 +1167,10 @@ static int sm100_plan_linear(struct KernelEntry *ke, Term root, Sm100Plan *pl) {
       glob[ng++] = rk;
       pl->pro = (Sm100Prog *)malloc(sizeof(Sm100Prog));
       if (!pl->pro) return 0;
-      sp_compile(pl->pro, 0, pa, 0, DT_FP32, glob, ng);
+      sp_compile(pl->pro, 0, pa, 0, DT_FP32, glob, ng, ke->n_inputs, sm100_env_on("THVM_SM100_PREPASS", 1));
       if (pl->pro->bad) {
         snprintf(pl->why, sizeof pl->why, "linear A side: %s", pl->pro->why);
-        free(pl->pro);
+        sp_free_family(pl->pro);
         pl->pro = NULL;
         return 0;
       }
@@ -891,10 +1227,11 @@ static Sm100Plan *sm100_ref_plan(struct KernelEntry *ke) {
     free(pg);
     return pl;
   }
-  sp_compile(pg, heap_read(term_val(root) + 1), heap_read(term_val(root) + 2), 0, odt, NULL, 0);
+  sp_compile(pg, heap_read(term_val(root) + 1), heap_read(term_val(root) + 2), 0, odt, NULL, 0, ke->n_inputs,
+             sm100_env_on("THVM_SM100_PREPASS", 1));
   if (pg->bad) {
     snprintf(pl->why, sizeof pl->why, "%s", pg->why);
-    free(pg);
+    sp_free_family(pg);
     return pl;
   }
   pl->prog = pg;
@@ -927,6 +1264,19 @@ static void sm100_log(struct KernelEntry *ke, const Sm100Plan *pl) {
   if (sm100_env_on("THVM_SM100_DUMP", 0) && pl->root) {
     fputs("\n    ", fp);
     sm100_dump(fp, pl->root, 0);
+  }
+  if (sm100_env_on("THVM_SM100_DUMP_PROG", 0)) {   /* the register programs, one instruction a line */
+    const Sm100Prog *root = pl->kind == SM100_R_INTERP ? pl->prog : pl->pro;
+    for (u32 k = 0; root && k <= root->n_pre; k++) {
+      const Sm100Prog *pg = k < root->n_pre ? root->pre[k] : root;
+      fprintf(fp, "\n   program %u%s: out scratch %d, %u glob axes", k, k < root->n_pre ? " (pre-pass)" : "",
+              k < root->n_pre ? root->pre_out[k] : -1, pg->n_glob);
+      for (u32 i = 0; i < pg->n_code; i++) {
+        const Sm100Insn *in = &pg->code[i];
+        fprintf(fp, "\n    %3u: op %2u dt %2u r%-3u a %-3u b %-3u c %-3u imm %d", i, in->op, in->dt, in->dst, in->a,
+                in->b, in->c, in->imm);
+      }
+    }
   }
   fputc('\n', fp);
   fflush(fp);
@@ -967,6 +1317,33 @@ static void sm100_cpu_run(const Sm100Prog *pg, void **bufs, const int64_t *bytes
   }
 }
 
+/* a program and its pre-passes over host buffers (slots 0..n_in given; the
+ * family's scratch in fresh host blocks for this run) */
+static int sm100_cpu_run_family(const Sm100Prog *pg, void **bufs, int64_t *bytes, u32 n_in) {
+  void *scr[SM100_MAX_SCR] = {0};
+  int ok = 1;
+  for (u32 j = 0; j < pg->n_scr && ok; j++) {
+    scr[j] = calloc(1, pg->scr_bytes[j] + 16);
+    ok = scr[j] != NULL;
+    bufs[n_in + 1 + j] = scr[j];
+    bytes[n_in + 1 + j] = (int64_t)pg->scr_bytes[j];
+  }
+  if (ok) {
+    void *out0 = bufs[0];
+    const int64_t ob0 = bytes[0];
+    for (u32 i = 0; i < pg->n_pre; i++) {
+      bufs[0] = scr[pg->pre_out[i]];
+      bytes[0] = (int64_t)pg->scr_bytes[pg->pre_out[i]];
+      sm100_cpu_run(pg->pre[i], bufs, bytes);
+    }
+    bufs[0] = out0;
+    bytes[0] = ob0;
+    sm100_cpu_run(pg, bufs, bytes);
+  }
+  for (u32 j = 0; j < pg->n_scr; j++) free(scr[j]);
+  return ok;
+}
+
 static int sm100_cpu_check(struct KernelEntry *ke, const Sm100Plan *pl, u32 *in, u32 out, int *exact) {
   const u32 n_in = ke->n_inputs;
   void *bufs[SM100_INTERP_MAX_BUFS] = {0};
@@ -986,7 +1363,7 @@ static int sm100_cpu_check(struct KernelEntry *ke, const Sm100Plan *pl, u32 *in,
     memcpy(bufs[0], ref, nb[0]);
     for (u32 i = 0; i <= n_in; i++) bytes[i] = (int64_t)nb[i];
     if (pl->kind == SM100_R_INTERP) {
-      sm100_cpu_run(pl->prog, bufs, bytes);
+      sm100_cpu_run_family(pl->prog, bufs, bytes, n_in);
     } else {
       float *x = pl->x_in >= 0 ? (float *)bufs[1 + pl->x_in] : (float *)calloc((size_t)pl->M * pl->K + 4, 4);
       if (pl->x_in < 0) {
@@ -996,7 +1373,7 @@ static int sm100_cpu_check(struct KernelEntry *ke, const Sm100Plan *pl, u32 *in,
         memcpy(sbytes, bytes, sizeof sbytes);
         sb[0] = x;
         sbytes[0] = (int64_t)pl->M * pl->K * 4;
-        sm100_cpu_run(pl->pro, sb, sbytes);
+        sm100_cpu_run_family(pl->pro, sb, sbytes, n_in);
       }
       const float *w = (const float *)bufs[1 + pl->w_in];
       float *y = (float *)bufs[0];
@@ -1087,6 +1464,57 @@ static int sm100_scratch(u64 need) {
 
 static int sm100_buf_ok(u32 id) { return id != 0 && id < CUDA_BUFS_NEXT && cuda_buf_dptr(id) != 0; }
 
+/* Scratch of the pre-pass families: bump allocations from 64 MiB device
+ * blocks, never freed (a captured graph keeps the addresses it recorded), and
+ * none made while the stream captures. */
+static void *sm100_arena(u64 bytes) {
+  static CUdeviceptr blk;
+  static u64 used, cap;
+  bytes = (bytes + 255) & ~(u64)255;
+  if (!blk || used + bytes > cap) {
+    CUstreamCaptureStatus cs = CU_STREAM_CAPTURE_STATUS_NONE;
+    if (CUDA_CUR_STREAM && cuStreamIsCapturing(CUDA_CUR_STREAM, &cs) == CUDA_SUCCESS &&
+        cs != CU_STREAM_CAPTURE_STATUS_NONE)
+      return NULL;
+    const u64 n = bytes > (64ull << 20) ? bytes : (64ull << 20);
+    CUdeviceptr p = 0;
+    if (cuMemAlloc(&p, n) != CUDA_SUCCESS) return NULL;
+    blk = p, used = 0, cap = n;
+  }
+  void *r = (void *)(uintptr_t)(blk + used);
+  used += bytes;
+  return r;
+}
+
+/* a program and its pre-passes on the device (slots 0..n_in given) */
+static int sm100_run_family(Sm100Prog *pg, void **bufs, int64_t *bytes, u32 n_in, void *stream) {
+  for (u32 j = 0; j < pg->n_scr; j++) {
+    if (!pg->scr_ptr[j] && !(pg->scr_ptr[j] = sm100_arena(pg->scr_bytes[j])))
+      return sm100_set_error(SM100_ERR_STATE, "router: no scratch for a pre-pass (%llu B)",
+                             (unsigned long long)pg->scr_bytes[j]);
+    bufs[n_in + 1 + j] = pg->scr_ptr[j];
+    bytes[n_in + 1 + j] = (int64_t)pg->scr_bytes[j];
+  }
+  const u32 nb = n_in + 1 + pg->n_scr;
+  int64_t ge[SM100_INTERP_MAX_AXES], vars[SM100_INTERP_MAX_VARS];
+  void *out0 = bufs[0];
+  const int64_t ob0 = bytes[0];
+  for (u32 i = 0; i < pg->n_pre; i++) {
+    const Sm100Prog *q = pg->pre[i];
+    bufs[0] = pg->scr_ptr[pg->pre_out[i]];
+    bytes[0] = (int64_t)pg->scr_bytes[pg->pre_out[i]];
+    sm100_prog_runtime(q, ge, vars);
+    const int rc = sm100_interp_run(q->code, q->n_code, q->n_regs, q->n_axes, q->n_glob, ge, bufs, bytes, nb, vars,
+                                    q->n_vars, stream);
+    if (rc != SM100_OK) return rc;
+  }
+  bufs[0] = out0;
+  bytes[0] = ob0;
+  sm100_prog_runtime(pg, ge, vars);
+  return sm100_interp_run(pg->code, pg->n_code, pg->n_regs, pg->n_axes, pg->n_glob, ge, bufs, bytes, nb, vars,
+                          pg->n_vars, stream);
+}
+
 static int sm100_ref_dispatch(struct KernelEntry *ke, u32 *in_buf_ids, u32 out_buf_id) {
   SM100_N_DISPATCH++;
   if (!CUDA_READY || kernel_is_custom(ke) || !sm100_env_on("THVM_SM100", 1)) {
@@ -1114,10 +1542,7 @@ static int sm100_ref_dispatch(struct KernelEntry *ke, u32 *in_buf_ids, u32 out_b
   int64_t ge[SM100_INTERP_MAX_AXES], vars[SM100_INTERP_MAX_VARS];
   int rc = SM100_OK;
   if (pl->kind == SM100_R_INTERP) {
-    const Sm100Prog *pg = pl->prog;
-    sm100_prog_runtime(pg, ge, vars);
-    rc = sm100_interp_run(pg->code, pg->n_code, pg->n_regs, pg->n_axes, pg->n_glob, ge, bufs, bytes, n_in + 1, vars,
-                          pg->n_vars, stream);
+    rc = sm100_run_family(pl->prog, bufs, bytes, n_in, stream);
     if (rc == SM100_OK) SM100_N_INTERP++;
   } else {
     const u64 xb = (u64)pl->M * pl->K * 4, wb = (u64)pl->N * pl->K * 4, yb = (u64)pl->M * pl->N * 4;
@@ -1128,16 +1553,13 @@ static int sm100_ref_dispatch(struct KernelEntry *ke, u32 *in_buf_ids, u32 out_b
     } else if (!sm100_scratch(xb)) {
       rc = SM100_ERR_STATE;
     } else {
-      const Sm100Prog *pg = pl->pro;
       void *sb[SM100_INTERP_MAX_BUFS];
       int64_t sbytes[SM100_INTERP_MAX_BUFS];
       memcpy(sb, bufs, sizeof sb);
       memcpy(sbytes, bytes, sizeof sbytes);
       sb[0] = (void *)(uintptr_t)SM100_SCRATCH;
       sbytes[0] = (int64_t)xb;
-      sm100_prog_runtime(pg, ge, vars);
-      rc = sm100_interp_run(pg->code, pg->n_code, pg->n_regs, pg->n_axes, pg->n_glob, ge, sb, sbytes, n_in + 1, vars,
-                            pg->n_vars, stream);
+      rc = sm100_run_family(pl->pro, sb, sbytes, n_in, stream);
       x = (const float *)(uintptr_t)SM100_SCRATCH;
     }
     if (rc == SM100_OK && ((u64)bytes[1 + pl->w_in] < wb || (u64)bytes[0] < yb)) rc = SM100_ERR_ARG;
