@@ -616,9 +616,11 @@ __global__ void __launch_bounds__(1024) ds_router_route_kernel(const __nv_bfloat
       }
     }
     acc = warp_sum(acc);
-    if (lane == 0) logits[(int64_t)b * E + e] = acc;
+    if (lane == 0) {
+      logits[(int64_t)b * E + e] = acc;
+      __threadfence();   // each writer's logit is visible device-wide before the CTA counts itself done
+    }
   }
-  __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == E - 1;
   __syncthreads();
@@ -672,6 +674,11 @@ __host__ __device__ constexpr int x8_smem() {
 __device__ __forceinline__ uint64_t x8_desc(const void *p) {
   const uint64_t a = smem_u32(p);
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// a weight tile into L2 only (no shared memory, no barrier)
+__device__ __forceinline__ void x8_prefetch_2d(const CUtensorMap *map, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
 }
 
 __device__ __forceinline__ void x8_tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -772,6 +779,16 @@ __global__ void __launch_bounds__(kX8Threads, 1)
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
+  // The weights are static, the routing is not known yet: while the previous
+  // kernel (the routing) finishes, this CTA's first item's leading tiles come
+  // into L2, whether or not its expert gets tokens (most do).
+  if (warp == kX8Tma && lane == 0 && blockIdx.x < n_items) {
+    const int e = blockIdx.x / nblk, blk = blockIdx.x % nblk;
+    const int pre_kb = min(nkb, kUp ? 8 : 12);
+    for (int kb = 0; kb < pre_kb; kb++)
+#pragma unroll
+      for (int t = 0; t < kA; t++) x8_prefetch_2d(&wmap, kb * 128, e * rows_w + (t == 0 ? 0 : I) + blk * 128);
+  }
   pdl_wait();
 
   if (warp < kX8Prep) {
