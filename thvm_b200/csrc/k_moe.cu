@@ -676,6 +676,18 @@ __device__ __forceinline__ uint64_t x8_desc(const void *p) {
   return ((a >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// 32 consecutive TMEM columns of this warp's 32 lanes (one f32 each)
+__device__ __forceinline__ void x8_tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+
 // a weight tile into L2 only (no shared memory, no barrier)
 __device__ __forceinline__ void x8_prefetch_2d(const CUtensorMap *map, int x, int y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y) : "memory");
@@ -769,9 +781,9 @@ __global__ void __launch_bounds__(kX8Threads, 1)
     mbar_init(done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == kX8Mma) {   // accumulators: 2 sets x kA x 32 columns
+  if (warp == kX8Mma) {   // accumulators: 2 sets x kA x 64 columns (hi | lo)
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(128)
+                 "r"(256)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -893,8 +905,10 @@ __global__ void __launch_bounds__(kX8Threads, 1)
     }
   } else if (warp == kX8Mma) {
     if (lane == 0) {
-      // f32 accumulate, A and B e4m3, K-major, N = 32, M = 128
-      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(32 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+      // f32 accumulate, A and B e4m3, K-major, M = 128, N = 64: the hi and lo
+      // token tiles are adjacent 32-row K-major tiles, one 64-row operand, so
+      // one product gives hi in columns [0, 32) and lo in [32, 64)
+      constexpr uint32_t idesc = (1u << 4) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
       int g = 0, it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -911,20 +925,26 @@ __global__ void __launch_bounds__(kX8Threads, 1)
             break;
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-          const unsigned char *st = smem + s * kStage;
+          // one shared-memory descriptor per stage; a tile's is the stage's
+          // plus its byte offset / 16 in the 14-bit address field (the
+          // stages lie below 256 KB, so the field cannot carry over)
+          const uint64_t da = x8_desc(smem + s * kStage), db = da + (uint64_t)((kA * kX8A) >> 4);
 #pragma unroll
-          for (int t = 0; t < kA; t++)
-#pragma unroll
-            for (int hl = 0; hl < 2; hl++)
-#pragma unroll
-              for (int k4 = 0; k4 < 4; k4++)
-                asm volatile(
-                    "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, q;\n\t}" ::"r"(tmem +
-                                                                                        (uint32_t)(a * 64 + t * 32)),
-                    "l"(x8_desc(st + t * kX8A) + 2 * k4), "l"(x8_desc(st + kA * kX8A + (2 * t + hl) * kX8B) + 2 * k4),
-                    "r"(idesc), "r"((kb > 0 || hl > 0 || k4 > 0) ? 1u : 0u)
-                    : "memory");
+          for (int t = 0; t < kA; t++) {
+            const uint64_t at = da + (uint64_t)((t * kX8A) >> 4), bt = db + (uint64_t)((2 * t * kX8B) >> 4);
+            asm volatile(
+                "{\n\t.reg .pred q, pt;\n\t"
+                "setp.ne.b32 q, %4, 0;\n\t"
+                "setp.eq.b32 pt, 0, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, q;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %5, %6, %3, pt;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %7, %8, %3, pt;\n\t"
+                "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %9, %10, %3, pt;\n\t}" ::"r"(tmem +
+                                                                                     (uint32_t)(a * 128 + t * 64)),
+                "l"(at), "l"(bt), "r"(idesc), "r"(kb > 0 ? 1u : 0u), "l"(at + 2), "l"(bt + 2), "l"(at + 4), "l"(bt + 4),
+                "l"(at + 6), "l"(bt + 6)
+                : "memory");
+          }
           asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                            smem_u32(&empty[s]))
                        : "memory");
@@ -949,35 +969,24 @@ __global__ void __launch_bounds__(kX8Threads, 1)
       const int a = it & 1;
       if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[a], (uint32_t)((it >> 1) & 1), status))) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      uint32_t v0[32], v1[32];
-      asm volatile(
-          "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-          "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-          : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
-            "=r"(v0[8]), "=r"(v0[9]), "=r"(v0[10]), "=r"(v0[11]), "=r"(v0[12]), "=r"(v0[13]), "=r"(v0[14]),
-            "=r"(v0[15]), "=r"(v0[16]), "=r"(v0[17]), "=r"(v0[18]), "=r"(v0[19]), "=r"(v0[20]), "=r"(v0[21]),
-            "=r"(v0[22]), "=r"(v0[23]), "=r"(v0[24]), "=r"(v0[25]), "=r"(v0[26]), "=r"(v0[27]), "=r"(v0[28]),
-            "=r"(v0[29]), "=r"(v0[30]), "=r"(v0[31])
-          : "r"(tq + (uint32_t)(a * 64)));
-      if (kUp)
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-            "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
-              "=r"(v1[8]), "=r"(v1[9]), "=r"(v1[10]), "=r"(v1[11]), "=r"(v1[12]), "=r"(v1[13]), "=r"(v1[14]),
-              "=r"(v1[15]), "=r"(v1[16]), "=r"(v1[17]), "=r"(v1[18]), "=r"(v1[19]), "=r"(v1[20]), "=r"(v1[21]),
-              "=r"(v1[22]), "=r"(v1[23]), "=r"(v1[24]), "=r"(v1[25]), "=r"(v1[26]), "=r"(v1[27]), "=r"(v1[28]),
-              "=r"(v1[29]), "=r"(v1[30]), "=r"(v1[31])
-            : "r"(tq + (uint32_t)(a * 64 + 32)));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
       // the token scales of this set (written before the set's first k-block)
       const bool sok = __all_sync(0xffffffffu, mbar_wait(&sc_full[a], (uint32_t)((it >> 1) & 1), status));
+      // tile t's 64 columns: hi in [0, 32), lo in [32, 64); their sum is the product
       float f0[32], f1[32];
 #pragma unroll
-      for (int s = 0; s < 32; s++) {
-        f0[s] = __uint_as_float(v0[s]) * sout[(a * kA) * 32 + s];
-        f1[s] = kUp ? __uint_as_float(v1[s]) * sout[(a * kA + 1) * 32 + s] : 0.0f;
+      for (int t = 0; t < kA; t++) {
+        uint32_t vh[32], vl[32];
+        x8_tmem_ld32(tq + (uint32_t)(a * 128 + t * 64), vh);
+        x8_tmem_ld32(tq + (uint32_t)(a * 128 + t * 64 + 32), vl);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float *f = t == 0 ? f0 : f1;
+#pragma unroll
+        for (int c = 0; c < 32; c++)
+          f[c] = (__uint_as_float(vh[c]) + __uint_as_float(vl[c])) * sout[(a * kA + t) * 32 + c];
       }
+      if (!kUp)
+#pragma unroll
+        for (int c = 0; c < 32; c++) f1[c] = 0.0f;
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
@@ -1007,7 +1016,7 @@ __global__ void __launch_bounds__(kX8Threads, 1)
     if (lane == 0) mbar_wait(done, 0, status, false);
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(128) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(256) : "memory");
   }
 }
 
