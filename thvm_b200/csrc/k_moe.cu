@@ -13,11 +13,15 @@
 // Every kernel is launched with programmatic dependent launch and reads its
 // inputs after griddepcontrol.wait.
 #include <cuda.h>
+
+#include <cstddef>
+#include <cstring>
 #include <cuda_fp8.h>
 
 #include <algorithm>
 
 #include "common.cuh"
+#include "ds_route.cuh"
 #include "tma.cuh"
 
 namespace sm100 {
@@ -26,19 +30,66 @@ constexpr int kDsMaxTok = 32;     // decode batch
 constexpr int kDsMaxK = 8;        // experts per token
 constexpr int kDsMaxCtx = 2048;
 
+// Sticky status of the kernels of this file with bounded waits (a timeout sets it).
+__device__ uint32_t g_ds_status;
+
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
 // y = bf16(x * rsqrt(mean(x^2) + eps) * g) per row (RMSNorm, deepseek_v2.py's
-// RMSNorm as the reference folds it, dsv2_decode_bench.c:341-430).
-__global__ void __launch_bounds__(256) ds_rms_kernel(const float *x, const float *g, __nv_bfloat16 *y, int D,
-                                                      float eps) {
+// RMSNorm as the reference folds it, dsv2_decode_bench.c:341-430), one CTA of
+// 256 threads per row.  Rows of D % 4 == 0, D <= 4096 go in float4 chunks
+// (thread t: chunks t, t + 256, ..), every load of the row issued before the
+// first is used, the gains read before the wait on the previous kernel; ys
+// (shared, may be null) receives the row as well.
+constexpr int kRmsV = 4;
+__device__ __forceinline__ bool ds_rms_vec(int D) { return D % 4 == 0 && D <= 1024 * kRmsV; }
+
+__device__ __forceinline__ void ds_rms_gains(const float *g, int D, float4 (&gv)[kRmsV]) {
+#pragma unroll
+  for (int i = 0; i < kRmsV; i++) {
+    const int c = threadIdx.x + 256 * i;
+    gv[i] = 4 * c < D ? __ldg(reinterpret_cast<const float4 *>(g) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+__device__ __forceinline__ void ds_rms_row(const float *xr, const float *g, const float4 (&gv)[kRmsV],
+                                           __nv_bfloat16 *yr, __nv_bfloat16 *ys, int D, float eps) {
   __shared__ float red[8];
-  pdl_trigger();
-  pdl_wait();
-  const float *xr = x + (int64_t)blockIdx.x * D;
   float s = 0.0f;
-  for (int i = threadIdx.x; i < D; i += 256) s += xr[i] * xr[i];
+  if (ds_rms_vec(D)) {
+    float4 xv[kRmsV];
+#pragma unroll
+    for (int i = 0; i < kRmsV; i++) {
+      const int c = threadIdx.x + 256 * i;
+      xv[i] = 4 * c < D ? reinterpret_cast<const float4 *>(xr)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int i = 0; i < kRmsV; i++)
+      s = fmaf(xv[i].w, xv[i].w, fmaf(xv[i].z, xv[i].z, fmaf(xv[i].y, xv[i].y, fmaf(xv[i].x, xv[i].x, s))));
+    s = warp_sum(s);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; w++) t += red[w];
+    const float inv = 1.0f / sqrtf(t * (1.0f / (float)D) + eps);
+#pragma unroll
+    for (int i = 0; i < kRmsV; i++) {
+      const int c = threadIdx.x + 256 * i;
+      if (4 * c >= D) break;
+      const __nv_bfloat162 y0 = __floats2bfloat162_rn((xv[i].x * inv) * gv[i].x, (xv[i].y * inv) * gv[i].y);
+      const __nv_bfloat162 y1 = __floats2bfloat162_rn((xv[i].z * inv) * gv[i].z, (xv[i].w * inv) * gv[i].w);
+      reinterpret_cast<__nv_bfloat162 *>(yr)[2 * c] = y0;
+      reinterpret_cast<__nv_bfloat162 *>(yr)[2 * c + 1] = y1;
+      if (ys) {
+        reinterpret_cast<__nv_bfloat162 *>(ys)[2 * c] = y0;
+        reinterpret_cast<__nv_bfloat162 *>(ys)[2 * c + 1] = y1;
+      }
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < D; i += 256) s = fmaf(xr[i], xr[i], s);
   s = warp_sum(s);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
   __syncthreads();
@@ -46,8 +97,45 @@ __global__ void __launch_bounds__(256) ds_rms_kernel(const float *x, const float
 #pragma unroll
   for (int w = 0; w < 8; w++) t += red[w];
   const float inv = 1.0f / sqrtf(t * (1.0f / (float)D) + eps);
-  for (int i = threadIdx.x; i < D; i += 256)
-    y[(int64_t)blockIdx.x * D + i] = __float2bfloat16_rn((xr[i] * inv) * g[i]);
+  for (int i = threadIdx.x; i < D; i += 256) {
+    const __nv_bfloat16 v = __float2bfloat16_rn((xr[i] * inv) * g[i]);
+    yr[i] = v;
+    if (ys) ys[i] = v;
+  }
+}
+
+__global__ void __launch_bounds__(256) ds_rms_kernel(const float *x, const float *g, __nv_bfloat16 *y, int D,
+                                                      float eps) {
+  float4 gv[kRmsV];
+  if (ds_rms_vec(D)) ds_rms_gains(g, D, gv);
+  pdl_trigger();
+  pdl_wait();
+  ds_rms_row(x + (int64_t)blockIdx.x * D, g, gv, y + (int64_t)blockIdx.x * D, nullptr, D, eps);
+}
+
+// The RMSNorm before the experts with the router product and the routing in
+// the same launch: CTA b normalises row b, computes its E logits from the row
+// staged in shared memory (the router weights stream through shared memory,
+// the first chunks requested before the wait on the previous kernel) and its
+// top-K; the last CTA packs every
+// token's choices (ds_route.cuh).  Bit-identical to ds_rms_kernel followed by
+// ds_router_route_kernel.
+__global__ void __launch_bounds__(256) ds_rms_route_kernel(const float *x, const float *g, __nv_bfloat16 *y, int D,
+                                                            float eps, const DsRouteArgs ra) {
+  extern __shared__ __align__(128) unsigned char rt_ring[];   // ds_route_ring_bytes(D)
+  __shared__ uint4 ys[kRtMaxD / 8];
+  __shared__ uint64_t rt_bars[kRtStages];
+  float4 gv[kRmsV];
+  ds_route_start(ra, rt_ring, rt_bars, D);
+  ds_rms_gains(g, D, gv);   // D % 8 == 0, D <= kRtMaxD: the vector path
+  pdl_wait();
+  ds_rms_row(x + (int64_t)blockIdx.x * D, g, gv, y + (int64_t)blockIdx.x * D, reinterpret_cast<__nv_bfloat16 *>(ys),
+             D, eps);
+  __syncthreads();
+  ds_route_row(ra, ys, rt_ring, rt_bars, blockIdx.x, gridDim.x, D, &g_ds_status);
+  // the expert kernel that follows fits beside this one on an SM; let it in
+  // only now (its weight prefetch would slow this launch's copies)
+  pdl_trigger();
 }
 
 // h[b] = embed[tok[b]] (bf16 table; ids outside [0, V) read zeros)
@@ -113,8 +201,6 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
 // over cache rows 0..pos = (qlat . c_t + q_pe . pe_t) * scale, softmax,
 // olat = sum_t p_t c_t, o = bf16(W_uv[h] olat) (DV).  W_uk / W_uv [H][DN or
 // DV][KV] bf16 (kv_b_proj split, deepseek_v2.py's absorb).
-// Sticky status of the kernels below with bounded waits (a timeout sets it).
-__device__ uint32_t g_ds_status;
 
 constexpr int kDsKV = 512;
 __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk,
@@ -469,113 +555,22 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   }
 }
 
-// Routing of every token (one CTA, a warp per token), the rule of the
-// reference's route kernel (bench/dsv2_decode_bench.c:787-863): the K largest
-// router LOGITS (ties: lowest expert id), each weighted by its softmax
-// probability exp(l - max) / sum (no renormalisation; DeepSeek-V2-Lite:
-// norm_topk_prob false, scaling 1);
-// then per-expert lists of (token, weight) for the experts [e0, e1) this
-// rank holds, packed expert-major: slot_tok / slot_w / slot_off[e] offsets,
-// followed by n_shared shared experts that take every token with weight 1.
-// The routing of every token by one CTA of >= 256 threads (warps over the
-// tokens); the logits are read at L2 (they may come from other CTAs).
+// Routing of every token by one CTA of >= 256 threads (a warp per token; the
+// logits are read at L2: they may come from other CTAs), the rule and the
+// packing of ds_route.cuh.
 __device__ __forceinline__ void ds_route_block(const float *logits, int E, int K, int B, int e0, int e1, int n_shared,
                                                int32_t *sel, float *wsel, int32_t *slot_off, int32_t *slot_tok,
                                                float *slot_w) {
-  __shared__ int s_sel[kDsMaxTok * kDsMaxK];
+  __shared__ int32_t s_sel[kDsMaxTok * kDsMaxK];
   __shared__ float s_w[kDsMaxTok * kDsMaxK];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   for (int b = warp; b < B; b += nwarps) {
     const float *lg = logits + (int64_t)b * E;
     const float l0 = lane < E ? __ldcg(lg + lane) : 0.0f, l1 = lane + 32 < E ? __ldcg(lg + lane + 32) : 0.0f;
-    float m = fmaxf(lane < E ? l0 : -INFINITY, lane + 32 < E ? l1 : -INFINITY);
-    m = warp_max(m);
-    float sum = (lane < E ? expf(l0 - m) : 0.0f) + (lane + 32 < E ? expf(l1 - m) : 0.0f);
-    sum = warp_sum(sum);
-    // greedy top-K over E <= 64 logits held two per lane (a taken or absent
-    // expert is out of the contest); a lane offers its larger logit, the
-    // lower id on a tie, and the warp keeps the larger, the lower id on a tie
-    bool live0 = lane < E, live1 = lane + 32 < E;
-    for (int k = 0; k < K; k++) {
-      const bool take0 = live0 && (!live1 || l0 >= l1);
-      float bv = take0 ? l0 : live1 ? l1 : -INFINITY;
-      int bi = take0 ? lane : live1 ? lane + 32 : 0x7FFFFFFF;
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-          bv = ov;
-          bi = oi;
-        }
-      }
-      const float w = expf(bv - m) / sum;
-      if (lane == 0) {
-        s_sel[b * K + k] = bi;
-        s_w[b * K + k] = w;
-        sel[b * K + k] = bi;
-        wsel[b * K + k] = w;
-      }
-      if (bi == lane) live0 = false;
-      if (bi == lane + 32) live1 = false;
-    }
+    ds_route_select(l0, l1, E, K, sel + (int64_t)b * K, wsel + (int64_t)b * K, s_sel + b * K, s_w + b * K);
   }
   __syncthreads();
-  // expert-major packing in entry order (token-major): entry i = (token i / K,
-  // choice i % K); a warp of entries groups equal experts (match), its lowest
-  // lane records the group's count, the counts' prefix sums give each
-  // (warp, expert) its base and an entry its slot: base + rank in its group
-  __shared__ int wcnt[kDsMaxTok * kDsMaxK / 32][64];
-  __shared__ int eoff[65];
-  const int ne = e1 - e0, n_ent = B * K, nw = (n_ent + 31) / 32;
-  for (int i = threadIdx.x; i < nw * 64; i += blockDim.x) (&wcnt[0][0])[i] = 0;
-  __syncthreads();
-  int ent_e = -1, rank = 0;
-  if (warp < nw) {
-    const int i = warp * 32 + lane;
-    const int ex = i < n_ent ? s_sel[i] - e0 : -1;
-    ent_e = ex >= 0 && ex < ne ? ex : -1;
-    const unsigned mask = __match_any_sync(0xffffffffu, ent_e);
-    rank = __popc(mask & ((1u << lane) - 1u));
-    if (ent_e >= 0 && rank == 0) wcnt[warp][ent_e] = __popc(mask);
-  }
-  __syncthreads();
-  if (warp == 0) {   // exclusive scan of the expert totals (64 experts, two per lane)
-    int c0 = 0, c1 = 0;
-    for (int w = 0; w < nw; w++) {
-      c0 += 2 * lane < ne ? wcnt[w][2 * lane] : 0;
-      c1 += 2 * lane + 1 < ne ? wcnt[w][2 * lane + 1] : 0;
-    }
-    int incl = c0 + c1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const int excl = incl - c0 - c1;
-    eoff[2 * lane] = excl;
-    eoff[2 * lane + 1] = excl + c0;
-    if (lane == 31) eoff[64] = incl;
-  }
-  __syncthreads();
-  if (threadIdx.x <= ne) slot_off[threadIdx.x] = eoff[threadIdx.x];
-  if (ent_e >= 0) {
-    int o = eoff[ent_e] + rank;
-    for (int w = 0; w < warp; w++) o += wcnt[w][ent_e];
-    const int i = warp * 32 + lane;
-    slot_tok[o] = i / K;
-    slot_w[o] = s_w[i];
-  }
-  // the shared experts (local ids ne ..) take every token with weight 1
-  __syncthreads();
-  if (n_shared > 0) {
-    for (int i = threadIdx.x; i < n_shared * B; i += blockDim.x) {
-      const int k = i / B, b = i % B, o = eoff[ne] + i;
-      slot_tok[o] = b;
-      slot_w[o] = 1.0f;
-      if (b == 0) slot_off[ne + k + 1] = eoff[ne] + (k + 1) * B;
-    }
-  }
+  ds_route_pack(s_sel, s_w, B, K, e0, e1, n_shared, slot_off, slot_tok, slot_w);
 }
 
 __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int E, int K, int B, int e0, int e1,
@@ -601,21 +596,9 @@ __global__ void __launch_bounds__(1024) ds_router_route_kernel(const __nv_bfloat
   pdl_wait();
   const int e = blockIdx.x, lane = threadIdx.x & 31, b = threadIdx.x >> 5;
   const __nv_bfloat16 *we = router + (int64_t)e * D;
-  // warp b: token b, its 16-byte loads two steps ahead
+  // warp b: token b
   if (b < B) {
-    const __nv_bfloat16 *xb = x + (int64_t)b * D;
-    float acc = 0.0f;
-#pragma unroll 4
-    for (int k = lane * 8; k < D; k += 256) {
-      const uint4 wv = __ldg(reinterpret_cast<const uint4 *>(we + k)), xv = *reinterpret_cast<const uint4 *>(xb + k);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-      for (int q = 0; q < 4; q++) {
-        acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
-        acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
-      }
-    }
-    acc = warp_sum(acc);
+    const float acc = ds_router_dot(reinterpret_cast<const uint4 *>(x + (int64_t)b * D), we, D);
     if (lane == 0) {
       logits[(int64_t)b * E + e] = acc;
       __threadfence();   // each writer's logit is visible device-wide before the CTA counts itself done
@@ -1180,6 +1163,42 @@ extern "C" int sm100_ds_router_route(const void *x, const void *router, float *l
   DS_LAUNCH("ds_router_route", ds_router_route_kernel, dim3(E), dim3(1024), 0, (cudaStream_t)stream,
             (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)router, logits, counter, D, E, K, B, e0, e1, n_shared,
             sel, wsel, slot_off, slot_tok, slot_w);
+}
+
+static_assert(sizeof(DsRouteArgs) == sizeof(Sm100DsRoute) && offsetof(DsRouteArgs, E) == offsetof(Sm100DsRoute, E),
+              "the device and public routing structs share one layout");
+
+// the routing arguments of a fused norm + router launch, checked
+int sm100::ds_route_args(const Sm100DsRoute *r, int B, int D, const char *who, DsRouteArgs *out) {
+  if (!r || !r->router || !r->logits || !r->counter || !r->sel || !r->wsel || !r->slot_off || !r->slot_tok ||
+      !r->slot_w || r->E < 1 || r->E > kRtMaxE || r->K < 1 || r->K > kRtMaxK || r->K > r->E || B < 1 ||
+      B > kRtMaxTok || r->e0 < 0 || r->e1 > r->E || r->e0 > r->e1 || r->n_shared < 0 || r->n_shared > 8 || D < 8 ||
+      D > kRtMaxD || D % 8 || (uintptr_t)r->router % 16)
+    return sm100_set_error(SM100_ERR_ARG, "%s: routing D %d E %d K %d B %d [%d, %d)", who, D, r ? r->E : 0,
+                           r ? r->K : 0, B, r ? r->e0 : 0, r ? r->e1 : 0);
+  memcpy(out, r, sizeof *out);
+  return SM100_OK;
+}
+
+extern "C" int sm100_ds_rmsnorm_route(const float *x, const float *g, void *y, int32_t M, int32_t D, float eps,
+                                      const Sm100DsRoute *route, void *stream) {
+  if (!x || !g || !y || M < 1 || D < 1) return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm_route: bad arguments");
+  DsRouteArgs ra;
+  const int rc = ds_route_args(route, M, D, "ds_rmsnorm_route", &ra);
+  if (rc != SM100_OK) return rc;
+  static bool attr[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm_route: device %d", dev);
+  if (!attr[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(ds_rms_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               ds_route_ring_bytes(kRtMaxD));
+    if (e != cudaSuccess)
+      return sm100_set_error(SM100_ERR_CUDA, "ds_rmsnorm_route: smem attribute: %s", cudaGetErrorString(e));
+    attr[dev] = true;
+  }
+  DS_LAUNCH("ds_rmsnorm_route", ds_rms_route_kernel, dim3(M), dim3(256), ds_route_ring_bytes(D), (cudaStream_t)stream,
+            x, g, (__nv_bfloat16 *)y, D, eps, ra);
 }
 
 extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,
