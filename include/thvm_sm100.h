@@ -265,6 +265,27 @@ int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
 #define SM100_ARGMAX_NOALLOC_MAX_ROWS 64
 int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
                          int32_t *bump, void *stream);
+/* ---- blind speculative decode of the batched MoE step --------------------- */
+/* n_seq sequences of S rows each (row i S + s) verify S tokens per step
+ * (bench/dsv2_decode_bench.c:1110-1195 draft_prep / accept_commit).  Device
+ * state per sequence i: the token stream ids [n_seq][ctx] and len[i] = P + 1,
+ * P the index of the pending token.  draft: cand[i][0] = ids[i][P],
+ * cand[i][1..S) the tokens after the most recent earlier occurrence of the
+ * bigram (ids[P-1], ids[P]) in ids[0..P-1] (-1 where there are none), or with
+ * forced != 0 the ids already stored at P + 1 ..; tok[i S + s] = cand (the
+ * pending token for a -1), row_pos = P + s, row_seq = i (Sm100DsRows with
+ * shared_slots).  accept (am: the step's argmax per row): k = the longest
+ * prefix with cand[s + 1] == am[s]; ids[P + 1 .. P + k] = cand[1 .. k],
+ * ids[P + k + 1] = am[k], len += k + 1, *committed += k + 1 (may be null).
+ * A sequence with P + S >= ctx is left as it is (its rows sit at P) and
+ * sm100_spec_status reports 1.  S <= 16. */
+int sm100_spec_draft(const int32_t *ids, const int32_t *len, int32_t n_seq, int32_t ctx, int32_t S, int32_t forced,
+                     int32_t *tok, int32_t *cand, int32_t *row_pos, int32_t *row_seq, void *stream);
+int sm100_spec_accept(int32_t *ids, int32_t *len, int32_t n_seq, int32_t ctx, int32_t S, const int32_t *cand,
+                      const int32_t *am, uint64_t *committed, void *stream);
+/* the sticky status of the two (synchronises the device, clears it) */
+uint32_t sm100_spec_status(void);
+
 /* dst[idx[i]] = src[i], rows of D elements of elem_bytes; idx outside [0, V) skipped. */
 int sm100_scatter_rows(void *dst, const int32_t *idx, const void *src, int64_t n_idx,
                        int64_t V, int64_t D, int32_t elem_bytes, void *stream);
@@ -476,6 +497,26 @@ int sm100_ds_mla_post(const float *qkva, int64_t ld, int64_t kva_off, const floa
                       const float *sin_t, const int32_t *pos, void *q_out, const void *w_uk, const void *w_uv,
                       void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV,
                       int32_t KV, int32_t ctx, float eps, float scale, void *stream);
+/* Rows of a step that are not one sequence each at one shared position: row
+ * b appends its latent / key row to cache slot seq[b] at position pos[b] and
+ * attends over that slot's rows 0..pos[b] (caches [n_seq][ctx][...]).  With
+ * shared_slots != 0 several rows may use one slot (the draft rows of a
+ * speculative verify, at consecutive positions): every append then completes
+ * before any attention starts (two launches), so a row sees the rows the
+ * others append in the same step.  A row outside [0, n_seq) x [0, ctx) is
+ * skipped, its attention output is zero, and the status word of
+ * sm100_ds_status gets SM100_DECODE_ERR_ARG. */
+typedef struct Sm100DsRows {
+  const int32_t *pos; /* [B] device */
+  const int32_t *seq; /* [B] device */
+  int32_t n_seq;
+  int32_t shared_slots;
+} Sm100DsRows;
+/* sm100_ds_mla_post with per-row cache slots and positions */
+int sm100_ds_mla_post_rows(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv, const float *cos_t,
+                           const float *sin_t, const Sm100DsRows *rows, void *q_out, const void *w_uk,
+                           const void *w_uv, void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H, int32_t DN,
+                           int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float eps, float scale, void *stream);
 /* the K largest of E <= 64 router logits (ties: lowest id) weighted by their
  * softmax probabilities, no renormalisation (the reference's route kernel,
  * bench/dsv2_decode_bench.c:787-863); sel / wsel [B][K]; slot lists of the

@@ -88,6 +88,11 @@ class Sm100DsRoute(ctypes.Structure):
                                         "slot_w")] + [(n, c_int32) for n in ("E", "K", "e0", "e1", "n_shared")]
 
 
+class Sm100DsRows(ctypes.Structure):
+    """include/thvm_sm100.h Sm100DsRows: per-row cache slots and positions."""
+    _fields_ = [("pos", c_void_p), ("seq", c_void_p), ("n_seq", c_int32), ("shared_slots", c_int32)]
+
+
 class Sm100SkinnyArgs(ctypes.Structure):
     _fields_ = [(n, c_void_p) for n in ("x", "w", "bias", "residual", "y", "ws", "counters", "kv_cache", "pos")] + [
         (n, c_int64) for n in ("M", "N", "K", "ld_x", "ld_w", "ld_res", "ld_y")] + [
@@ -197,6 +202,14 @@ SIGNATURES = {
     "sm100_ds_mla_post": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                   c_int32, c_int32, c_int32, c_float, c_float, c_void_p]),
+    "sm100_ds_mla_post_rows": (c_int, [c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                       c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                       c_int32, c_int32, c_int32, c_int32, c_float, c_float, c_void_p]),
+    "sm100_spec_draft": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_void_p]),
+    "sm100_spec_accept": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                  c_void_p]),
+    "sm100_spec_status": (c_uint32, []),
     "sm100_ds_router_route": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                       c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_void_p]),

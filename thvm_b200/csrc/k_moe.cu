@@ -33,6 +33,24 @@ constexpr int kDsMaxCtx = 2048;
 // Sticky status of the kernels of this file with bounded waits (a timeout sets it).
 __device__ uint32_t g_ds_status;
 
+// Where row b of a step reads and appends the compressed KV cache: slot
+// seq[b] (b when seq is null) at position pos[b * pos_stride] (one shared
+// position: stride 0).  A row outside [0, n_seq) x [0, ctx) is skipped (its
+// outputs zero) and sets SM100_DECODE_ERR_ARG.
+struct DsRows {
+  const int32_t *pos;
+  const int32_t *seq;
+  int32_t pos_stride, n_seq;
+};
+
+__device__ __forceinline__ bool ds_row(const DsRows &r, int b, int ctx, int &seq, int &p) {
+  p = r.pos[(int64_t)b * r.pos_stride];
+  seq = r.seq ? r.seq[b] : b;
+  if (p >= 0 && p < ctx && seq >= 0 && seq < r.n_seq) return true;
+  atomicOr(&g_ds_status, SM100_DECODE_ERR_ARG);
+  return false;
+}
+
 __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162float(v); }
 __device__ __forceinline__ float bfr(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
@@ -152,14 +170,16 @@ __global__ void ds_embed_kernel(const __nv_bfloat16 *emb, const int32_t *tok, fl
 // DR/2 + j); kva [KV + DR] -> the latent rounded to bf16, RMSNormed with
 // g_kv, and the rotary k_pe, both appended to the caches at row pos.
 __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const float *kva, const float *g_kv,
-                                                           const float *cs, const float *sn, const int32_t *pos,
+                                                           const float *cs, const float *sn, const DsRows rows,
                                                            __nv_bfloat16 *qo, __nv_bfloat16 *cc, __nv_bfloat16 *cpe,
                                                            int H, int DN, int DR, int KV, int ctx, float eps,
                                                            int64_t ld) {
   __shared__ float red[8];
   pdl_trigger();
   pdl_wait();
-  const int b = blockIdx.x, p = *pos, half = DR / 2, QS = DN + DR;
+  const int b = blockIdx.x, half = DR / 2, QS = DN + DR;
+  int seq, p;
+  if (!ds_row(rows, b, ctx, seq, p)) return;
   const float *qb = q + (int64_t)b * ld;
   __nv_bfloat16 *qob = qo + (int64_t)b * H * QS;
   for (int i = threadIdx.x; i < H * DN; i += 256) {
@@ -186,9 +206,9 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
 #pragma unroll
   for (int w = 0; w < 8; w++) t += red[w];
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fmul_rn(t, 1.0f / (float)KV), eps)));
-  __nv_bfloat16 *crow = cc + ((int64_t)b * ctx + p) * KV;
+  __nv_bfloat16 *crow = cc + ((int64_t)seq * ctx + p) * KV;
   for (int i = threadIdx.x; i < KV; i += 256) crow[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(bfr(kb[i]), inv), g_kv[i]));
-  __nv_bfloat16 *prow = cpe + ((int64_t)b * ctx + p) * DR;
+  __nv_bfloat16 *prow = cpe + ((int64_t)seq * ctx + p) * DR;
   for (int j = threadIdx.x; j < half; j += 256) {
     const float xe = bfr(kb[KV + 2 * j]), xo = bfr(kb[KV + 2 * j + 1]);
     const float c = cs[(int64_t)p * DR + j], s = sn[(int64_t)p * DR + j];
@@ -205,7 +225,7 @@ __global__ void __launch_bounds__(256) ds_qkv_post_kernel(const float *q, const 
 constexpr int kDsKV = 512;
 __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk,
                                                       const __nv_bfloat16 *wuv, const __nv_bfloat16 *cc,
-                                                      const __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o,
+                                                      const __nv_bfloat16 *cpe, const DsRows rows, __nv_bfloat16 *o,
                                                       int H, int DN, int DR, int DV, int KV, int ctx, float scale) {
   __shared__ float qlat[kDsKV];
   __shared__ float qn[256];
@@ -215,8 +235,14 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
   __shared__ float red[8];
   pdl_trigger();
   pdl_wait();
-  const int b = blockIdx.x / H, h = blockIdx.x % H, QS = DN + DR, T = *pos + 1;
+  const int b = blockIdx.x / H, h = blockIdx.x % H, QS = DN + DR;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int seq, p;
+  if (!ds_row(rows, b, ctx, seq, p)) {
+    for (int r = threadIdx.x; r < DV; r += 256) o[((int64_t)b * H + h) * DV + r] = __float2bfloat16_rn(0.0f);
+    return;
+  }
+  const int T = p + 1;
   const __nv_bfloat16 *qrow = qo + ((int64_t)b * H + h) * QS;
   for (int i = threadIdx.x; i < DN; i += 256) qn[i] = bf(qrow[i]);
   for (int i = threadIdx.x; i < DR; i += 256) qpe[i] = bf(qrow[DN + i]);
@@ -228,7 +254,7 @@ __global__ void __launch_bounds__(256) ds_mla_kernel(const __nv_bfloat16 *qo, co
     qlat[k] = a;
   }
   __syncthreads();
-  const __nv_bfloat16 *cb = cc + (int64_t)b * ctx * KV, *pb = cpe + (int64_t)b * ctx * DR;
+  const __nv_bfloat16 *cb = cc + (int64_t)seq * ctx * KV, *pb = cpe + (int64_t)seq * ctx * DR;
   for (int t = warp; t < T; t += 8) {   // a warp per cache row
     float s = 0.0f;
     for (int k = lane; k < KV; k += 32) s += qlat[k] * bf(cb[(int64_t)t * KV + k]);
@@ -319,7 +345,7 @@ struct MlaPost {
 template <int NB, bool kPost>
 __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     ds_mla_group_kernel(const __nv_bfloat16 *qo, const __nv_bfloat16 *wuk, const __nv_bfloat16 *wuv,
-                        __nv_bfloat16 *cc, __nv_bfloat16 *cpe, const int32_t *pos, __nv_bfloat16 *o, int B,
+                        __nv_bfloat16 *cc, __nv_bfloat16 *cpe, const DsRows rows, __nv_bfloat16 *o, int B,
                         int H, int DN, int DV, int ctx, float scale, MlaPost post) {
   extern __shared__ __align__(128) unsigned char sm[];
   __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(sm + MlaSmem::w);
@@ -341,7 +367,17 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
   }
   pdl_trigger();
   pdl_wait();
-  const int p = *pos, T = p + 1;
+  // each sequence's cache slot and position (rows outside the caches: T = 0,
+  // o = 0)
+  __shared__ int s_seq[kMlaNB], s_pos[kMlaNB], s_T[kMlaNB];
+  if (t < nb) {
+    int sq, pp;
+    const bool ok = ds_row(rows, b0 + t, ctx, sq, pp);
+    s_seq[t] = ok ? sq : 0;
+    s_pos[t] = ok ? pp : 0;
+    s_T[t] = ok ? pp + 1 : 0;
+  }
+  __syncthreads();
   __nv_bfloat16 *cur = reinterpret_cast<__nv_bfloat16 *>(sm + MlaSmem::cur);   // [NB][512 latent | 64 rope]
   for (int i = t; i < kMlaNB * QS; i += kMlaWarps * 32) {
     const int b = i / QS, d = i % QS;
@@ -349,6 +385,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     if (b < nb) {
       if constexpr (kPost) {   // ds_qkv_post's q: nope rounded; rope pairs rounded, rotated, rounded
         const float *qr = post.qkva + (int64_t)(b0 + b) * post.ld + h * QS;
+        const int p = s_pos[b];
         constexpr int half = kMlaDR / 2;
         if (d < DN) {
           v = bfr(qr[d]);
@@ -401,6 +438,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
       const float *kb = post.qkva + (int64_t)(b0 + b) * post.ld + post.kva_off;
       __nv_bfloat16 *prow = cur + b * (kMlaKV + kMlaDR) + kMlaKV;
       const float xe = bfr(kb[kMlaKV + 2 * j]), xo = bfr(kb[kMlaKV + 2 * j + 1]);
+      const int p = s_pos[b];
       const float c = post.cs[(int64_t)p * kMlaDR + j], sv = post.sn[(int64_t)p * kMlaDR + j];
       prow[j] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, sv)));
       prow[kMlaDR / 2 + j] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(xo, c), __fmul_rn(xe, sv)));
@@ -409,9 +447,11 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     if (h == 0)   // one head's CTAs keep the rows for the later steps
       for (int i = t; i < nb * (kMlaKV + kMlaDR); i += kMlaWarps * 32) {
         const int b = i / (kMlaKV + kMlaDR), c = i % (kMlaKV + kMlaDR);
+        if (s_T[b] == 0) continue;
         const __nv_bfloat16 v = cur[i];
-        if (c < kMlaKV) cc[((int64_t)(b0 + b) * ctx + p) * kMlaKV + c] = v;
-        else cpe[((int64_t)(b0 + b) * ctx + p) * kMlaDR + c - kMlaKV] = v;
+        const int64_t row = (int64_t)s_seq[b] * ctx + s_pos[b];
+        if (c < kMlaKV) cc[row * kMlaKV + c] = v;
+        else cpe[row * kMlaDR + c - kMlaKV] = v;
       }
   }
   __syncthreads();
@@ -454,9 +494,10 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
       oa[j] = oa[8 + j] = 0.0f;
     }
     float m = -INFINITY, l = 0.0f;
-    const __nv_bfloat16 *cb = cc + (int64_t)(b0 + b) * ctx * kMlaKV, *pb = cpe + (int64_t)(b0 + b) * ctx * kMlaDR;
+    const int sb = b < nb ? b : 0, p = s_pos[sb], T = b < nb ? s_T[sb] : 0;
+    const __nv_bfloat16 *cb = cc + (int64_t)s_seq[sb] * ctx * kMlaKV, *pb = cpe + (int64_t)s_seq[sb] * ctx * kMlaDR;
 #pragma unroll 4
-    for (int r = j0; r < T && b < nb; r += kWpb) {
+    for (int r = j0; r < T; r += kWpb) {
       // with kPost the current row is the one in shared memory
       const __nv_bfloat16 *crow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) : cb + (int64_t)r * kMlaKV;
       const __nv_bfloat16 *prow = kPost && r == p ? cur + b * (kMlaKV + kMlaDR) + kMlaKV : pb + (int64_t)r * kMlaDR;
@@ -518,7 +559,7 @@ __global__ void __launch_bounds__(kMlaWarps * 32, 1)
     float acc = 0.0f;
 #pragma unroll
     for (int w = 0; w < kWpb; w++) acc = fmaf(s_f[b * kWpb + w], po[(size_t)(b * kWpb + w) * kMlaKV + k], acc);
-    qlat[b * kMlaKV + k] = acc / s_L[b];
+    qlat[b * kMlaKV + k] = s_L[b] > 0.0f ? acc / s_L[b] : 0.0f;   // a skipped row: o = 0
   }
   __syncthreads();
   const bool wv_ok = mbar_wait(bar, 1, status, false);
@@ -1063,16 +1104,23 @@ extern "C" int sm100_ds_embed(const void *emb, const int32_t *tok, float *h, int
             tok, h, V, D);
 }
 
+static int qkv_post_rows(const float *q, const float *kva, int64_t ld, const float *g_kv, const float *cos_t,
+                         const float *sin_t, const DsRows &rows, void *q_out, void *cache_c, void *cache_pe, int32_t B,
+                         int32_t H, int32_t DN, int32_t DR, int32_t KV, int32_t ctx, float eps, void *stream) {
+  if (!q || !kva || !g_kv || !cos_t || !sin_t || !rows.pos || !q_out || !cache_c || !cache_pe || B < 1 || H < 1 ||
+      (DR & 1) || KV < 1 || ctx < 1 || rows.n_seq < 1)
+    return sm100_set_error(SM100_ERR_ARG, "ds_qkv_post: bad arguments");
+  DS_LAUNCH("ds_qkv_post", ds_qkv_post_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, q, kva, g_kv, cos_t,
+            sin_t, rows, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)cache_c, (__nv_bfloat16 *)cache_pe, H, DN, DR, KV,
+            ctx, eps, ld);
+}
+
 extern "C" int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, const float *g_kv, const float *cos_t,
                                  const float *sin_t, const int32_t *pos, void *q_out, void *cache_c, void *cache_pe,
                                  int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t KV, int32_t ctx, float eps,
                                  void *stream) {
-  if (!q || !kva || !g_kv || !cos_t || !sin_t || !pos || !q_out || !cache_c || !cache_pe || B < 1 || H < 1 ||
-      (DR & 1) || KV < 1 || ctx < 1)
-    return sm100_set_error(SM100_ERR_ARG, "ds_qkv_post: bad arguments");
-  DS_LAUNCH("ds_qkv_post", ds_qkv_post_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, q, kva, g_kv, cos_t,
-            sin_t, pos, (__nv_bfloat16 *)q_out, (__nv_bfloat16 *)cache_c, (__nv_bfloat16 *)cache_pe, H, DN, DR, KV,
-            ctx, eps, ld);
+  return qkv_post_rows(q, kva, ld, g_kv, cos_t, sin_t, DsRows{pos, nullptr, 0, B}, q_out, cache_c, cache_pe, B, H, DN,
+                       DR, KV, ctx, eps, stream);
 }
 
 // The group kernel's launch: sequences per CTA the most (fewer re-reads of
@@ -1081,7 +1129,7 @@ extern "C" int sm100_ds_qkv_post(const float *q, const float *kva, int64_t ld, c
 // SMs.
 template <bool kPost>
 static int mla_group_launch(const void *q_out, const void *w_uk, const void *w_uv, void *cache_c, void *cache_pe,
-                            const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN, int32_t DV, int32_t ctx,
+                            const DsRows &rows, void *o, int32_t B, int32_t H, int32_t DN, int32_t DV, int32_t ctx,
                             float scale, const MlaPost &post, void *stream) {
   const int nb = H * ((B + 3) / 4) >= 96 ? 4 : H * ((B + 1) / 2) >= 96 ? 2 : 1;
   static bool attr[3] = {false, false, false};
@@ -1097,8 +1145,8 @@ static int mla_group_launch(const void *q_out, const void *w_uk, const void *w_u
 #define DS_MLA_GROUP(NBV)                                                                                           \
   DS_LAUNCH("ds_mla", (ds_mla_group_kernel<NBV, kPost>), dim3(H * ((B + NBV - 1) / NBV)), dim3(kMlaWarps * 32),     \
             MlaSmem::total, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out, (const __nv_bfloat16 *)w_uk,        \
-            (const __nv_bfloat16 *)w_uv, (__nv_bfloat16 *)cache_c, (__nv_bfloat16 *)cache_pe, pos, (__nv_bfloat16 *)o, \
-            B, H, DN, DV, ctx, scale, post)
+            (const __nv_bfloat16 *)w_uv, (__nv_bfloat16 *)cache_c, (__nv_bfloat16 *)cache_pe, rows,                  \
+            (__nv_bfloat16 *)o, B, H, DN, DV, ctx, scale, post)
   if (nb == 4) DS_MLA_GROUP(4);
   if (nb == 2) DS_MLA_GROUP(2);
   DS_MLA_GROUP(1);
@@ -1109,19 +1157,46 @@ static bool mla_group_shape(int32_t DN, int32_t DR, int32_t DV, int32_t KV) {
   return KV == kMlaKV && DR == kMlaDR && DN <= kMlaMaxD && DV <= kMlaMaxD;
 }
 
-extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c,
-                            const void *cache_pe, const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN,
-                            int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float scale, void *stream) {
-  if (!q_out || !w_uk || !w_uv || !cache_c || !cache_pe || !pos || !o || B < 1 || H < 1 || DN > 256 || DR > 128 ||
-      KV > kDsKV || ctx > kDsMaxCtx)
+static int mla_rows(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c, const void *cache_pe,
+                    const DsRows &rows, void *o, int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV,
+                    int32_t ctx, float scale, void *stream) {
+  if (!q_out || !w_uk || !w_uv || !cache_c || !cache_pe || !rows.pos || !o || B < 1 || H < 1 || DN > 256 ||
+      DR > 128 || KV > kDsKV || ctx > kDsMaxCtx || rows.n_seq < 1)
     return sm100_set_error(SM100_ERR_ARG, "ds_mla: bad arguments (DN <= 256, DR <= 128, KV <= %d, ctx <= %d)",
                            kDsKV, kDsMaxCtx);
   if (mla_group_shape(DN, DR, DV, KV))
-    return mla_group_launch<false>(q_out, w_uk, w_uv, (void *)cache_c, (void *)cache_pe, pos, o, B, H, DN, DV, ctx,
+    return mla_group_launch<false>(q_out, w_uk, w_uv, (void *)cache_c, (void *)cache_pe, rows, o, B, H, DN, DV, ctx,
                                    scale, MlaPost{}, stream);
   DS_LAUNCH("ds_mla", ds_mla_kernel, dim3(B * H), dim3(256), 0, (cudaStream_t)stream, (const __nv_bfloat16 *)q_out,
             (const __nv_bfloat16 *)w_uk, (const __nv_bfloat16 *)w_uv, (const __nv_bfloat16 *)cache_c,
-            (const __nv_bfloat16 *)cache_pe, pos, (__nv_bfloat16 *)o, H, DN, DR, DV, KV, ctx, scale);
+            (const __nv_bfloat16 *)cache_pe, rows, (__nv_bfloat16 *)o, H, DN, DR, DV, KV, ctx, scale);
+}
+
+extern "C" int sm100_ds_mla(const void *q_out, const void *w_uk, const void *w_uv, const void *cache_c,
+                            const void *cache_pe, const int32_t *pos, void *o, int32_t B, int32_t H, int32_t DN,
+                            int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float scale, void *stream) {
+  return mla_rows(q_out, w_uk, w_uv, cache_c, cache_pe, DsRows{pos, nullptr, 0, B}, o, B, H, DN, DR, DV, KV, ctx,
+                  scale, stream);
+}
+
+// one_launch: the fused group kernel, whose CTAs walk their own rows' new
+// cache rows from shared memory; otherwise the two launches (every row's
+// cache append completes before any walk starts)
+static int mla_post_rows(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv, const float *cos_t,
+                         const float *sin_t, const DsRows &rows, bool one_launch, void *q_out, const void *w_uk,
+                         const void *w_uv, void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H, int32_t DN,
+                         int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float eps, float scale, void *stream) {
+  if (!qkva || !g_kv || !cos_t || !sin_t || !rows.pos || !q_out || !w_uk || !w_uv || !cache_c || !cache_pe || !o ||
+      B < 1 || H < 1 || kva_off < (int64_t)H * (DN + DR) || ld < kva_off + KV + DR || rows.n_seq < 1)
+    return sm100_set_error(SM100_ERR_ARG, "ds_mla_post: bad arguments");
+  if (!one_launch || !mla_group_shape(DN, DR, DV, KV) || ctx > kDsMaxCtx) {   // the two launches it fuses
+    int rc = qkv_post_rows(qkva, qkva + kva_off, ld, g_kv, cos_t, sin_t, rows, q_out, cache_c, cache_pe, B, H, DN, DR,
+                           KV, ctx, eps, stream);
+    if (rc != SM100_OK) return rc;
+    return mla_rows(q_out, w_uk, w_uv, cache_c, cache_pe, rows, o, B, H, DN, DR, DV, KV, ctx, scale, stream);
+  }
+  const MlaPost post{qkva, ld, kva_off, g_kv, cos_t, sin_t, eps};
+  return mla_group_launch<true>(q_out, w_uk, w_uv, cache_c, cache_pe, rows, o, B, H, DN, DV, ctx, scale, post, stream);
 }
 
 extern "C" int sm100_ds_mla_post(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv, const float *cos_t,
@@ -1129,17 +1204,20 @@ extern "C" int sm100_ds_mla_post(const float *qkva, int64_t ld, int64_t kva_off,
                                  const void *w_uv, void *cache_c, void *cache_pe, void *o, int32_t B, int32_t H,
                                  int32_t DN, int32_t DR, int32_t DV, int32_t KV, int32_t ctx, float eps, float scale,
                                  void *stream) {
-  if (!qkva || !g_kv || !cos_t || !sin_t || !pos || !q_out || !w_uk || !w_uv || !cache_c || !cache_pe || !o || B < 1 ||
-      H < 1 || kva_off < (int64_t)H * (DN + DR) || ld < kva_off + KV + DR)
-    return sm100_set_error(SM100_ERR_ARG, "ds_mla_post: bad arguments");
-  if (!mla_group_shape(DN, DR, DV, KV) || ctx > kDsMaxCtx) {   // the two launches it fuses
-    int rc = sm100_ds_qkv_post(qkva, qkva + kva_off, ld, g_kv, cos_t, sin_t, pos, q_out, cache_c, cache_pe, B, H, DN,
-                               DR, KV, ctx, eps, stream);
-    if (rc != SM100_OK) return rc;
-    return sm100_ds_mla(q_out, w_uk, w_uv, cache_c, cache_pe, pos, o, B, H, DN, DR, DV, KV, ctx, scale, stream);
-  }
-  const MlaPost post{qkva, ld, kva_off, g_kv, cos_t, sin_t, eps};
-  return mla_group_launch<true>(q_out, w_uk, w_uv, cache_c, cache_pe, pos, o, B, H, DN, DV, ctx, scale, post, stream);
+  return mla_post_rows(qkva, ld, kva_off, g_kv, cos_t, sin_t, DsRows{pos, nullptr, 0, B}, true, q_out, w_uk, w_uv,
+                       cache_c, cache_pe, o, B, H, DN, DR, DV, KV, ctx, eps, scale, stream);
+}
+
+extern "C" int sm100_ds_mla_post_rows(const float *qkva, int64_t ld, int64_t kva_off, const float *g_kv,
+                                      const float *cos_t, const float *sin_t, const Sm100DsRows *rows, void *q_out,
+                                      const void *w_uk, const void *w_uv, void *cache_c, void *cache_pe, void *o,
+                                      int32_t B, int32_t H, int32_t DN, int32_t DR, int32_t DV, int32_t KV, int32_t ctx,
+                                      float eps, float scale, void *stream) {
+  if (!rows || !rows->pos || !rows->seq || rows->n_seq < 1)
+    return sm100_set_error(SM100_ERR_ARG, "ds_mla_post_rows: rows need pos, seq and n_seq >= 1");
+  return mla_post_rows(qkva, ld, kva_off, g_kv, cos_t, sin_t, DsRows{rows->pos, rows->seq, 1, rows->n_seq},
+                       rows->shared_slots == 0, q_out, w_uk, w_uv, cache_c, cache_pe, o, B, H, DN, DR, DV, KV, ctx, eps,
+                       scale, stream);
 }
 
 extern "C" int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t e0, int32_t e1,

@@ -215,7 +215,8 @@ class DSModel:
     group over the R ranks, None when R = 1); `weights` are this rank's slices
     (shard_ds_weights)."""
 
-    def __init__(self, cfg: DSConfig, weights: dict[str, np.ndarray], shard: DSShard, group=None):
+    def __init__(self, cfg: DSConfig, weights: dict[str, np.ndarray], shard: DSShard, group=None,
+                 n_slots: int | None = None):
         import torch
         self.torch, self.cfg, self.sh, self.group = torch, cfg, shard, group
         self.lib = L.lib()
@@ -244,8 +245,10 @@ class DSModel:
         self.gu = z(B, 2 * DIl)
         self.rl = z(B, cfg.n_exp)
         self.logits = z(B, Vl)
-        self.cache_c = [z(B, ctx, cfg.kv_lora, dt=torch.int16) for _ in range(cfg.n_layers)]
-        self.cache_pe = [z(B, ctx, cfg.d_rope, dt=torch.int16) for _ in range(cfg.n_layers)]
+        self.n_slots = n_slots or B   # cache slots: one per row unless rows share them (use_rows)
+        self.cache_c = [z(self.n_slots, ctx, cfg.kv_lora, dt=torch.int16) for _ in range(cfg.n_layers)]
+        self.cache_pe = [z(self.n_slots, ctx, cfg.d_rope, dt=torch.int16) for _ in range(cfg.n_layers)]
+        self.rows = None   # L.Sm100DsRows when rows carry their own slots and positions
         self.tok = z(B, dt=torch.int32)
         self.pos = z(1, dt=torch.int32)
         K = cfg.top_k
@@ -324,6 +327,16 @@ class DSModel:
     def _all_reduce(self):
         self._pending = self.sh.world > 1
 
+    def use_rows(self, row_pos, row_seq, shared_slots: bool):
+        """From now on row b reads and appends cache slot row_seq[b] at
+        position row_pos[b] (int32 device tensors [batch], kept by the
+        caller, read by every step); the step leaves the positions alone.
+        shared_slots: rows may share a slot (speculative verify rows)."""
+        self._row_bufs = (row_pos, row_seq)
+        r = L.Sm100DsRows()
+        r.pos, r.seq, r.n_seq, r.shared_slots = row_pos.data_ptr(), row_seq.data_ptr(), self.n_slots, int(shared_slots)
+        self.rows = r
+
     def status(self) -> int:
         """The kernels' sticky status words (non-zero: a bounded wait gave up or an
         expert met more than 32 slots); synchronises the device and clears them."""
@@ -336,7 +349,9 @@ class DSModel:
             self.comm = None
 
     def step(self):
-        """One decode step: ids in self.tok at row self.pos -> next ids, pos + 1."""
+        """One decode step: ids in self.tok at row self.pos -> next ids, pos + 1
+        (after use_rows: each row at its own slot and position, which the step
+        leaves unchanged)."""
         cfg, sh, w, lib, st = self.cfg, self.sh, self.w, self.lib, self._stream
         B, D, KV, DN, DR, DV = cfg.batch, cfg.dim, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v
         E, K, I, Hl = cfg.n_exp, cfg.top_k, cfg.moe_inter, sh.heads
@@ -350,12 +365,18 @@ class DSModel:
             self._skinny(self.xn, w[p + "w_qkva"], self.qkva, D, self.n_qkva)
             # q / latent post-processing (rotary, latent norm, cache append) and the absorbed MLA:
             # one launch for the DeepSeek-V2-Lite shapes, two otherwise
-            L.check(lib.sm100_ds_mla_post(self.qkva.data_ptr(), self.n_qkva, self.n_q, w[p + "kv_norm"].data_ptr(),
-                                          self.cos.data_ptr(), self.sin.data_ptr(), self.pos.data_ptr(),
-                                          self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
-                                          self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.o.data_ptr(),
-                                          B, Hl, DN, DR, DV, KV, cfg.max_ctx, cfg.eps, cfg.scale, st()), "ds_mla_post")
-            fused = KV == 512 and DR == 64 and DN <= 128 and DV <= 128
+            mla_args = (self.qo.data_ptr(), w[p + "w_uk"].data_ptr(), w[p + "w_uv"].data_ptr(),
+                        self.cache_c[l].data_ptr(), self.cache_pe[l].data_ptr(), self.o.data_ptr(), B, Hl, DN, DR, DV,
+                        KV, cfg.max_ctx, cfg.eps, cfg.scale, st())
+            if self.rows is None:
+                L.check(lib.sm100_ds_mla_post(self.qkva.data_ptr(), self.n_qkva, self.n_q, w[p + "kv_norm"].data_ptr(),
+                                              self.cos.data_ptr(), self.sin.data_ptr(), self.pos.data_ptr(), *mla_args),
+                        "ds_mla_post")
+            else:
+                L.check(lib.sm100_ds_mla_post_rows(self.qkva.data_ptr(), self.n_qkva, self.n_q,
+                                                   w[p + "kv_norm"].data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(),
+                                                   ctypes.byref(self.rows), *mla_args), "ds_mla_post_rows")
+            fused = KV == 512 and DR == 64 and DN <= 128 and DV <= 128 and not (self.rows and self.rows.shared_slots)
             self.launches += 1 if fused else 2
             # the o projection's partial sums: rank 0 into the residual, the others over it
             self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
@@ -391,5 +412,7 @@ class DSModel:
         else:
             L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(), st()),
                     "xl_pick")
-        L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, st()), "pos_add")
-        self.launches += 2
+        self.launches += 1
+        if self.rows is None:
+            L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, st()), "pos_add")
+            self.launches += 1
