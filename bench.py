@@ -449,6 +449,81 @@ def moe_run(args, ctx):
     return line
 
 
+def spec_run(args, ctx):
+    """Blind speculative decode of the config-5 model (thvm_b200.spec.SpecDecoder,
+    the reference's DSV2_SPEC step): 8 sequences x S = 4 verify rows (the 32
+    rows of the base batch), prompts of 64 ids prefilled 4 positions per pass,
+    then W untimed and K timed steps of draft / verify / accept, captured as
+    one graph.  value = committed tokens / s over the timed steps; with forced
+    (seeded) drafts every step would commit 32 tokens, the base batch-32 rate."""
+    import torch
+    from thvm_b200.dsv2 import DSConfig, ds_shard
+    from thvm_b200.spec import SpecDecoder
+    ctx.init_cuda()
+    n_seq, S = 8, 4
+    cfg = DSConfig(n_layers=args.layers or DSConfig().n_layers, batch=n_seq * S)
+    sh = ds_shard(cfg, ctx.rank, ctx.world)
+    sd = SpecDecoder(cfg, {}, sh, n_seq, S, group=ctx.group)
+    sd.model.w = ds_device_weights(cfg, sh)
+    prompts = np.random.default_rng(1).integers(0, cfg.vocab, (n_seq, N_PROMPT_DS)).astype(np.int32)
+    if ctx.world > 1:
+        t = torch.zeros(1, device="cuda")
+        ctx.dist.all_reduce(t)
+    sd.prefill(prompts)
+    n0 = sd.model.launches
+    sd.capture()
+    per_step = sd.model.launches - n0
+    limit = cfg.max_ctx - S - 1
+    sd.replay(args.warmup)
+    torch.cuda.synchronize()
+    c0 = int(sd.committed.item())
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(ctx.local) as clk:
+        ctx.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        sd.replay(args.steps)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ctx.barrier()
+    ms = ctx.max(e0.elapsed_time(e1))
+    ids, ln = sd.stream_ids()
+    if ctx.max(float(sd.status())) != 0 or ln.max() >= limit:
+        raise RuntimeError(f"speculative steps did not finish cleanly (status {sd.status()}, lengths {ln.tolist()})")
+    committed = int(sd.committed.item()) - c0
+    value = committed / (ms / 1e3)
+    # e2e: every step also reads the sequences' lengths back to pinned host memory
+    host_len = torch.empty(n_seq, dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, min(args.steps, 10))
+    c1 = int(sd.committed.item())
+    ctx.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        sd.replay()
+        host_len.copy_(sd.len, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    e2e_s = ctx.max(time.perf_counter() - t0)
+    e2e = (int(sd.committed.item()) - c1) / e2e_s
+    line = base_line(
+        args, ctx.world, round(value, 1), ms, scaling="strong", dtype="fp8 e4m3 experts, bf16 activations / weights",
+        config={"workload": "config 5 model, blind speculative decode: 8 sequences x 4 verify rows (32 rows a step), "
+                            "64 prompt ids, bigram drafts (bench/dsv2_decode_bench.c DSV2_SPEC)",
+                "global_batch": n_seq * S, "sequences": n_seq, "verify_rows": S,
+                "positions": [int(ln.min()), int(ln.max())],
+                "parallelism": f"tp{ctx.world} attention heads / dense units / vocab, ep{ctx.world} experts"},
+        committed_per_sequence_step=round(committed / (n_seq * args.steps), 3),
+        forced_upper_bound_tok_s=round(n_seq * S * args.steps / (ms / 1e3), 1),
+        gpu_launches=per_step * args.steps, gpu_launches_per_step=per_step,
+        e2e={"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 4 * n_seq,
+             "steps": e2e_steps},
+        clocks=clk.summary())
+    del sd
+    torch.cuda.empty_cache()
+    return line
+
+
 def moe_reference(args, ctx):
     """The reference's own DeepSeek-V2 decode bench (bench/dsv2_decode_bench.c,
     built CPU-only into oracle/_ref) at full width, batch 1 (the only batch it
@@ -1055,7 +1130,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="sm100", choices=["sm100", "reference"])
-    ap.add_argument("--workload", default="moe", choices=["moe", "gpt2", "xl", "prefill", "kernels"])
+    ap.add_argument("--workload", default="moe", choices=["moe", "spec", "gpt2", "xl", "prefill", "kernels"])
     ap.add_argument("--layers", type=int, default=0, help="moe / xl: fewer layers (0 = the full model)")
     ap.add_argument("--no-extras", action="store_true", help="moe at N = 1: skip the config-1 and kernel lines")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1075,6 +1150,8 @@ def main():
             if ctx.world == 1 and not args.no_extras:
                 line["gpt2_small"] = gpt2_run(args, ctx, cpu)
                 line["kernels"] = kernel_cases()
+        elif args.workload == "spec":
+            line = spec_run(args, ctx)
         elif args.workload == "gpt2":
             line = gpt2_run(args, ctx, cpu)
         elif args.workload == "xl":
