@@ -285,6 +285,17 @@ int sm100_spec_accept(int32_t *ids, int32_t *len, int32_t n_seq, int32_t ctx, in
                       const int32_t *am, uint64_t *committed, void *stream);
 /* the sticky status of the two (synchronises the device, clears it) */
 uint32_t sm100_spec_status(void);
+/* The bookkeeping of a continuous-batching serve loop after a step of B rows,
+ * row b its own request in cache slot b at position row_pos[b]
+ * (bench/dsv2_decode_bench.c:2760-2900 serves one request at a time): for an
+ * active row, inside its prompt (prompt [B][ctx], plen) the next input is the
+ * prompt's next id; after it the step's argmax am[b] is appended to out
+ * [B][ctx] (n_out[b] ids) and is the next input, and the row stops (active
+ * 0, position 0) at eos[b], at its max_new[b]-th id or at the end of the
+ * cache.  row_pos / tok advance for the next step. */
+int sm100_serve_advance(int32_t *row_pos, int32_t *tok, const int32_t *am, const int32_t *prompt,
+                        const int32_t *plen, int32_t *out, int32_t *n_out, const int32_t *max_new, const int32_t *eos,
+                        int32_t *active, int32_t B, int32_t ctx, void *stream);
 
 /* dst[idx[i]] = src[i], rows of D elements of elem_bytes; idx outside [0, V) skipped. */
 int sm100_scatter_rows(void *dst, const int32_t *idx, const void *src, int64_t n_idx,

@@ -210,6 +210,7 @@ SIGNATURES = {
     "sm100_spec_accept": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   c_void_p]),
     "sm100_spec_status": (c_uint32, []),
+    "sm100_serve_advance": (c_int, [c_void_p] * 10 + [c_int32, c_int32, c_void_p]),
     "sm100_ds_router_route": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                       c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                       c_void_p]),

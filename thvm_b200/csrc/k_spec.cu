@@ -1,4 +1,7 @@
-// Blind speculative decode of the batched MoE step (bench/dsv2_decode_bench.c
+// Serving the batched MoE step: blind speculative decode and the per-row
+// bookkeeping of a continuous-batching serve loop.
+//
+// Blind speculative decode (bench/dsv2_decode_bench.c
 // :1110-1195 draft_prep / accept_commit, at batch 1 there): n_seq sequences
 // of S rows each verify S tokens per step.  Device state per sequence i: the
 // token stream ids[i][0..ctx) and its length len[i] = P + 1, P the index of
@@ -17,6 +20,13 @@
 // stream is the base greedy stream; drafts only change how many positions a
 // step commits.  A sequence whose next window would pass ctx is left as it is
 // (no draft rows are written past the cache) and sets the status word.
+//
+//   sm100_serve_advance  after a step of B rows, each its own request (the
+//       reference's serve loop, bench/dsv2_decode_bench.c:2760-2900, one
+//       request at a time there): a row still inside its prompt takes the
+//       prompt's next id (the step's argmax is dropped); otherwise the argmax
+//       is appended to the row's output and the row stops at its eos id, its
+//       max_new-th id or the end of the cache; the row's position advances.
 #include "common.cuh"
 
 using namespace sm100;
@@ -88,6 +98,33 @@ __global__ void spec_accept_kernel(int32_t *ids, int32_t *len, int ctx, int S, c
   if (committed) atomicAdd(committed, (unsigned long long)(k + 1));
 }
 
+__global__ void serve_advance_kernel(int32_t *row_pos, int32_t *tok, const int32_t *am, const int32_t *prompt,
+                                     const int32_t *plen, int32_t *out, int32_t *n_out, const int32_t *max_new,
+                                     const int32_t *eos, int32_t *active, int B, int ctx) {
+  pdl_trigger();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B || !active[b]) return;
+  const int p = row_pos[b];
+  int nxt;
+  if (p + 1 < plen[b] && p + 1 < ctx) {
+    nxt = prompt[(int64_t)b * ctx + p + 1];
+  } else {
+    nxt = am[b];
+    const int o = n_out[b];
+    if (o >= 0 && o < ctx) out[(int64_t)b * ctx + o] = nxt;
+    n_out[b] = o + 1;
+    if (nxt == eos[b] || o + 1 >= max_new[b] || p + 2 >= ctx) {   // done: the slot idles at position 0
+      active[b] = 0;
+      row_pos[b] = 0;
+      tok[b] = 0;
+      return;
+    }
+  }
+  row_pos[b] = p + 1;
+  tok[b] = nxt;
+}
+
 }  // namespace
 
 extern "C" int sm100_spec_draft(const int32_t *ids, const int32_t *len, int32_t n_seq, int32_t ctx, int32_t S,
@@ -109,6 +146,18 @@ extern "C" int sm100_spec_accept(int32_t *ids, int32_t *len, int32_t n_seq, int3
                                    S, cand, am, reinterpret_cast<unsigned long long *>(committed));
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "spec_accept: %s", cudaGetErrorString(e));
   return launch_status("spec_accept");
+}
+
+extern "C" int sm100_serve_advance(int32_t *row_pos, int32_t *tok, const int32_t *am, const int32_t *prompt,
+                                   const int32_t *plen, int32_t *out, int32_t *n_out, const int32_t *max_new,
+                                   const int32_t *eos, int32_t *active, int32_t B, int32_t ctx, void *stream) {
+  if (!row_pos || !tok || !am || !prompt || !plen || !out || !n_out || !max_new || !eos || !active || B < 1 ||
+      ctx < 2)
+    return sm100_set_error(SM100_ERR_ARG, "serve_advance: B %d ctx %d", B, ctx);
+  const cudaError_t e = launch_pdl(serve_advance_kernel, dim3((B + 127) / 128), dim3(128), 0, (cudaStream_t)stream,
+                                   row_pos, tok, am, prompt, plen, out, n_out, max_new, eos, active, B, ctx);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "serve_advance: %s", cudaGetErrorString(e));
+  return launch_status("serve_advance");
 }
 
 extern "C" uint32_t sm100_spec_status(void) {
