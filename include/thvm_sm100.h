@@ -544,26 +544,6 @@ int sm100_ds_route(const float *logits, int32_t E, int32_t K, int32_t B, int32_t
 int sm100_ds_router_route(const void *x, const void *router, float *logits, int32_t *counter, int32_t D, int32_t E,
                           int32_t K, int32_t B, int32_t e0, int32_t e1, int32_t n_shared, int32_t *sel, float *wsel,
                           int32_t *slot_off, int32_t *slot_tok, float *slot_w, void *stream);
-/* The router product and the routing appended to the RMSNorm that feeds the
- * experts (sm100_ds_rmsnorm_route, sm100_comm_allreduce_rmsnorm_route): the
- * normalised bf16 row y[b] takes the place of x[b] in sm100_ds_router_route
- * (the same bits for logits, sel, wsel and the slot lists).  router [E][D]
- * bf16 with D <= 4096, E <= 64, K <= 8, B <= 32; counter as for
- * sm100_ds_router_route. */
-typedef struct Sm100DsRoute {
-  const void *router;
-  float *logits;      /* [B][E] */
-  int32_t *counter;
-  int32_t *sel;       /* [B][K] */
-  float *wsel;        /* [B][K] */
-  int32_t *slot_off;  /* [e1 - e0 + n_shared + 1] */
-  int32_t *slot_tok;  /* [B (K + n_shared)] */
-  float *slot_w;
-  int32_t E, K, e0, e1, n_shared;
-} Sm100DsRoute;
-/* sm100_ds_rmsnorm (M rows) then the routing of its output, one launch */
-int sm100_ds_rmsnorm_route(const float *x, const float *g, void *y, int32_t M, int32_t D, float eps,
-                           const Sm100DsRoute *route, void *stream);
 /* y[tok] += w * down(bf16(silu(gate x) * (up x))) for the slots of n_exp
  * experts on the tensor cores, fp8 x fp8: the weights stream by TMA as the
  * MMA's e4m3 operand; each token's row times the 128 x 128 block scale and
@@ -608,10 +588,6 @@ int sm100_comm_set_peers(void *own, void *const *peer_ptrs, int32_t world);
  * other than 0 keep zeros in h instead (y is the same) */
 int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
                                  int32_t rows, int32_t cols, float eps, int32_t zero_rest, void *stream);
-/* sm100_comm_allreduce_rmsnorm then the routing of y (Sm100DsRoute), one launch */
-int sm100_comm_allreduce_rmsnorm_route(float *h, const float *g, void *y, void *own, int32_t rank, int32_t world,
-                                       int32_t rows, int32_t cols, float eps, int32_t zero_rest,
-                                       const Sm100DsRoute *route, void *stream);
 /* the same exchange with LayerNorm: y = bf16((h - mean) * rsqrt(var + eps) * g
  * + b), mean and biased variance in two passes (src/nn/layernorm.c:1-7) */
 int sm100_comm_allreduce_layernorm(float *h, const float *g, const float *b, void *y, void *own, int32_t rank,

@@ -140,51 +140,6 @@ def test_ds_router_route_matches_oracle_rule():
             assert torch.equal(a, b)
 
 
-@pytest.mark.parametrize("e0,e1,NS", [(0, 64, 2), (16, 24, 1)])
-def test_ds_rmsnorm_route_is_rmsnorm_then_router_route(e0, e1, NS):
-    """The RMSNorm with the router product and the routing in the same launch
-    (sm100_ds_rmsnorm_route) against sm100_ds_rmsnorm followed by
-    sm100_ds_router_route: xn, logits, choices, weights and slot lists equal
-    bit for bit, for all experts and for one rank's range, twice in a row (the
-    CTA counter is left at zero)."""
-    import ctypes
-    import torch
-    from thvm_b200 import _lib as L
-    lib = L.lib()
-    B, E, K, D = 32, 64, 6, 2048
-    g = torch.Generator(device="cuda").manual_seed(4)
-    h = torch.randn(B, D, generator=g, device="cuda") * 3.0
-    gam = torch.rand(D, generator=g, device="cuda") + 0.5
-    w = (torch.randn(E, D, generator=g, device="cuda") * 0.02).to(torch.bfloat16)
-    z = lambda n, dt=torch.float32: torch.zeros(n, dtype=dt, device="cuda")
-    n_slot = (e1 - e0) + NS + 1
-
-    def outs():
-        return dict(xn=z(B * D, torch.int16), logits=z(B * E), counter=z(1, torch.int32), sel=z(B * K, torch.int32),
-                    wsel=z(B * K), off=z(n_slot, torch.int32), stok=z(B * (K + NS), torch.int32), sw=z(B * (K + NS)))
-    ref = outs()
-    L.check(lib.sm100_ds_rmsnorm(h.data_ptr(), gam.data_ptr(), ref["xn"].data_ptr(), B, D, 1e-6, ctypes.c_void_p(0)),
-            "ds_rmsnorm")
-    L.check(lib.sm100_ds_router_route(ref["xn"].data_ptr(), w.data_ptr(), ref["logits"].data_ptr(),
-                                      ref["counter"].data_ptr(), D, E, K, B, e0, e1, NS, ref["sel"].data_ptr(),
-                                      ref["wsel"].data_ptr(), ref["off"].data_ptr(), ref["stok"].data_ptr(),
-                                      ref["sw"].data_ptr(), ctypes.c_void_p(0)), "ds_router_route")
-    for _ in range(2):
-        got = outs()
-        r = L.Sm100DsRoute()
-        r.router, r.logits, r.counter = w.data_ptr(), got["logits"].data_ptr(), got["counter"].data_ptr()
-        r.sel, r.wsel, r.slot_off = got["sel"].data_ptr(), got["wsel"].data_ptr(), got["off"].data_ptr()
-        r.slot_tok, r.slot_w = got["stok"].data_ptr(), got["sw"].data_ptr()
-        r.E, r.K, r.e0, r.e1, r.n_shared = E, K, e0, e1, NS
-        L.check(lib.sm100_ds_rmsnorm_route(h.data_ptr(), gam.data_ptr(), got["xn"].data_ptr(), B, D, 1e-6,
-                                           ctypes.byref(r), ctypes.c_void_p(0)), "ds_rmsnorm_route")
-        torch.cuda.synchronize()
-        for k in ref:
-            assert torch.equal(got[k], ref[k]), k
-        assert int(got["counter"].item()) == 0
-    assert int(lib.sm100_ds_status()) == 0
-
-
 def _experts_case(B, D, I, slots, seed):
     """sm100_ds_experts on explicit slot lists against the oracle's fp8 block-scaled linear."""
     import ctypes

@@ -3,7 +3,7 @@ process per GPU (run by tests/test_gpu_multi.py under torch.distributed.run):
 
   ds   config 5 (thvm_b200.dsv2.DSModel): heads, dense units, experts and
        vocabulary split over the ranks, the library's peer all-reduces of the
-       residual (fused with the RMSNorm, and before the experts with the routing);
+       residual (fused with the RMSNorm);
   xl   config 3 (thvm_b200.gpt2_xl.XLModel): Megatron column / row splits.
 
 Each rank holds its shard of one seeded model, both sides are fed the
@@ -146,43 +146,6 @@ def run_comm(rank, world, dist):
         torch.cuda.synchronize()
         assert torch.equal(y, y0)
         assert np.array_equal(h.cpu().numpy(), want if rank == 0 else np.zeros_like(want)), use
-    # the route variant: the same sum and y, then each rank's routing of y equals the single-GPU
-    # router + routing launch on that y for the rank's expert range
-    import ctypes
-    from thvm_b200 import _lib as L
-    from thvm_b200.gpt2_xl import split_even
-    lib = L.lib()
-    E, K, NS = 64, 6, 1
-    e0, e1 = split_even(E, world, rank)
-    wr = (torch.from_numpy(np.random.default_rng(11).standard_normal((E, D)).astype(np.float32)).cuda() * 0.02
-          ).to(torch.bfloat16)
-    z = lambda n, dt=torch.float32: torch.zeros(n, dtype=dt, device="cuda")
-    n_slot = (e1 - e0) + NS + 1
-    bufs = lambda: [z(B * E), z(1, torch.int32), z(B * K, torch.int32), z(B * K), z(n_slot, torch.int32),
-                    z(B * (K + NS), torch.int32), z(B * (K + NS))]
-    got, ref = bufs(), bufs()
-    r = L.Sm100DsRoute()
-    (r.logits, r.counter, r.sel, r.wsel, r.slot_off, r.slot_tok, r.slot_w) = [t.data_ptr() for t in got]
-    r.router, r.E, r.K, r.e0, r.e1, r.n_shared = wr.data_ptr(), E, K, e0, e1, NS
-    parts = [np.random.default_rng(800 + r_).standard_normal((B, D)).astype(np.float32) for r_ in range(world)]
-    h = torch.from_numpy(parts[rank].copy()).cuda()
-    comm.allreduce_rmsnorm_route(h.data_ptr(), g.data_ptr(), y.data_ptr(), B, D, 1e-6, r, ctypes.c_void_p(st),
-                                 zero_rest=True)
-    torch.cuda.synchronize()
-    want = parts[0].copy()
-    for r_ in range(1, world):
-        want = want + parts[r_]
-    assert np.array_equal(h.cpu().numpy(), want if rank == 0 else np.zeros_like(want))
-    y_fused = y.clone()
-    h = torch.from_numpy(parts[rank].copy()).cuda()
-    comm.allreduce_rmsnorm(h.data_ptr(), g.data_ptr(), y.data_ptr(), B, D, 1e-6, st, zero_rest=True)
-    L.check(lib.sm100_ds_router_route(y_fused.data_ptr(), wr.data_ptr(), ref[0].data_ptr(), ref[1].data_ptr(), D, E,
-                                      K, B, e0, e1, NS, *[t.data_ptr() for t in ref[2:]], ctypes.c_void_p(st)),
-            "ds_router_route")
-    torch.cuda.synchronize()
-    assert torch.equal(y, y_fused)
-    for a, b_ in zip(got, ref):
-        assert torch.equal(a, b_)
     val = torch.full((B,), float(rank % 2), device="cuda")            # ranks 1, 3, .. hold the maximum
     idx = torch.arange(B, dtype=torch.int32, device="cuda") + 1000 * (world - rank)   # the last of them the smallest index
     tok = torch.zeros(B, dtype=torch.int32, device="cuda")

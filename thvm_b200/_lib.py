@@ -82,12 +82,6 @@ class Sm100Insn(ctypes.Structure):
                 ("b", ctypes.c_uint16), ("c", ctypes.c_uint16), ("imm", c_int32)]
 
 
-class Sm100DsRoute(ctypes.Structure):
-    """include/thvm_sm100.h Sm100DsRoute: the routing that ends a fused RMSNorm."""
-    _fields_ = [(n, c_void_p) for n in ("router", "logits", "counter", "sel", "wsel", "slot_off", "slot_tok",
-                                        "slot_w")] + [(n, c_int32) for n in ("E", "K", "e0", "e1", "n_shared")]
-
-
 class Sm100DsRows(ctypes.Structure):
     """include/thvm_sm100.h Sm100DsRows: per-row cache slots and positions."""
     _fields_ = [("pos", c_void_p), ("seq", c_void_p), ("n_seq", c_int32), ("shared_slots", c_int32)]
@@ -190,7 +184,6 @@ SIGNATURES = {
                                 c_void_p]),
     "sm100_xl_pick": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "sm100_ds_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
-    "sm100_ds_rmsnorm_route": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p, c_void_p]),
     "sm100_ds_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_qkv_post": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float,
@@ -226,8 +219,6 @@ SIGNATURES = {
     "sm100_comm_set_peers": (c_int, [c_void_p, POINTER(c_void_p), c_int32]),
     "sm100_comm_allreduce_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                              c_int32, c_float, c_int32, c_void_p]),
-    "sm100_comm_allreduce_rmsnorm_route": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
-                                                   c_int32, c_float, c_int32, c_void_p, c_void_p]),
     "sm100_comm_allreduce_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                                                c_int32, c_int32, c_float, c_void_p]),
     "sm100_comm_pick": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p]),

@@ -40,13 +40,6 @@ class PeerComm:
         L.check(self.lib.sm100_comm_allreduce_rmsnorm(h, g, y, self.own, self.rank, self.world, rows, cols, eps,
                                                       int(zero_rest), stream), "comm_allreduce_rmsnorm")
 
-    def allreduce_rmsnorm_route(self, h, g, y, rows: int, cols: int, eps: float, route, stream,
-                                zero_rest: bool = False):
-        """allreduce_rmsnorm, then the routing of y (route: an L.Sm100DsRoute)."""
-        L.check(self.lib.sm100_comm_allreduce_rmsnorm_route(h, g, y, self.own, self.rank, self.world, rows, cols, eps,
-                                                            int(zero_rest), ctypes.byref(route), stream),
-                "comm_allreduce_rmsnorm_route")
-
     def allreduce_layernorm(self, h, g, b, y, rows: int, cols: int, eps: float, stream):
         L.check(self.lib.sm100_comm_allreduce_layernorm(h, g, b, y, self.own, self.rank, self.world, rows, cols, eps,
                                                         stream), "comm_allreduce_layernorm")

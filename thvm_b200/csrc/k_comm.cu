@@ -28,7 +28,6 @@
 #include <cstring>
 
 #include "common.cuh"
-#include "ds_route.cuh"
 
 using namespace sm100;
 
@@ -72,22 +71,13 @@ __device__ bool wait_flag(const uint32_t *flag, uint32_t e) {
   return true;
 }
 
-// kRoute (RMSNorm only): the row's router logits and top-K follow, and the
-// last CTA packs the routing (ds_route.cuh), from y staged in shared memory.
-template <bool kLN, bool kRoute>
+template <bool kLN>
 __global__ void __launch_bounds__(256) allreduce_norm_kernel(float *h, const float *g, const float *bt,
                                                              __nv_bfloat16 *y, char *own, int rank, int R, int cols,
-                                                             float eps, int zero_rest, const DsRouteArgs ra) {
+                                                             float eps, int zero_rest) {
   __shared__ uint32_t s_e;
   __shared__ float red[8];
-  __shared__ uint4 ys[kRoute ? kRtMaxD / 8 : 1];
-  __shared__ uint64_t rt_bars[kRtStages];
-  extern __shared__ __align__(128) unsigned char rt_ring[];   // kRoute: ds_route_ring_bytes(cols)
-  if constexpr (kRoute) {
-    ds_route_start(ra, rt_ring, rt_bars, cols);
-  } else {
-    pdl_trigger();
-  }
+  pdl_trigger();
   pdl_wait();
   const int b = blockIdx.x, t = threadIdx.x;
   char *const *peers = reinterpret_cast<char *const *>(own + kOffPeers);
@@ -181,25 +171,12 @@ __global__ void __launch_bounds__(256) allreduce_norm_kernel(float *h, const flo
       yo[0] = __floats2bfloat162_rn((a.x - mean) * inv * gg.x + bb.x, (a.y - mean) * inv * gg.y + bb.y);
       yo[1] = __floats2bfloat162_rn((a.z - mean) * inv * gg.z + bb.z, (a.w - mean) * inv * gg.w + bb.w);
     } else {
-      const __nv_bfloat162 y0 = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
-      const __nv_bfloat162 y1 = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
-      yo[0] = y0;
-      yo[1] = y1;
-      if constexpr (kRoute) {
-        reinterpret_cast<__nv_bfloat162 *>(ys)[2 * i] = y0;
-        reinterpret_cast<__nv_bfloat162 *>(ys)[2 * i + 1] = y1;
-      }
+      yo[0] = __floats2bfloat162_rn((a.x * inv) * gg.x, (a.y * inv) * gg.y);
+      yo[1] = __floats2bfloat162_rn((a.z * inv) * gg.z, (a.w * inv) * gg.w);
     }
     if (zero) *hp = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   if (t == 0) *epoch = e;
-  if constexpr (kRoute) {
-    __syncthreads();
-    ds_route_row(ra, ys, rt_ring, rt_bars, b, gridDim.x, cols, &g_comm_status);
-    // the expert kernel that follows fits beside this one on an SM; let it
-    // in only now (its weight prefetch would slow this launch's copies)
-    pdl_trigger();
-  }
 }
 
 __global__ void pick_kernel(const float *val, const int32_t *idx, char *own, int rank, int R, int rows, int32_t *tok) {
@@ -303,40 +280,11 @@ extern "C" int sm100_comm_allreduce_rmsnorm(float *h, const float *g, void *y, v
       rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 || ((uintptr_t)h | (uintptr_t)g | (uintptr_t)y) % 16)
     return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
                                           "16-byte aligned)", rank, world, rows, cols, kMaxRows);
-  const cudaError_t e = launch_pdl(allreduce_norm_kernel<false, false>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h,
-                                   g, (const float *)nullptr, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps,
-                                   zero_rest, DsRouteArgs{});
+  const cudaError_t e = launch_pdl(allreduce_norm_kernel<false>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
+                                   (const float *)nullptr, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps,
+                                   zero_rest);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm: %s", cudaGetErrorString(e));
   return launch_status("comm_allreduce_rmsnorm");
-}
-
-extern "C" int sm100_comm_allreduce_rmsnorm_route(float *h, const float *g, void *y, void *own, int32_t rank,
-                                                  int32_t world, int32_t rows, int32_t cols, float eps,
-                                                  int32_t zero_rest, const Sm100DsRoute *route, void *stream) {
-  if (!h || !g || !y || !own || world < 1 || world > kMaxRanks || rank < 0 || rank >= world || rows < 1 ||
-      rows > kMaxRows || cols < 4 || cols > kMaxCols || cols % 4 || ((uintptr_t)h | (uintptr_t)g | (uintptr_t)y) % 16)
-    return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm_route: rank %d of %d, %d x %d (rows <= %d, "
-                                          "cols %% 4, 16-byte aligned)", rank, world, rows, cols, kMaxRows);
-  DsRouteArgs ra;
-  const int rc = ds_route_args(route, rows, cols, "comm_allreduce_rmsnorm_route", &ra);
-  if (rc != SM100_OK) return rc;
-  static bool attr[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_rmsnorm_route: device %d", dev);
-  if (!attr[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(allreduce_norm_kernel<false, true>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize, ds_route_ring_bytes(kRtMaxD));
-    if (e != cudaSuccess)
-      return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm_route: smem attribute: %s", cudaGetErrorString(e));
-    attr[dev] = true;
-  }
-  const cudaError_t e = launch_pdl(allreduce_norm_kernel<false, true>, dim3(rows), dim3(256), ds_route_ring_bytes(cols),
-                                   (cudaStream_t)stream, h, g, (const float *)nullptr, (__nv_bfloat16 *)y, (char *)own,
-                                   rank, world, cols, eps, zero_rest, ra);
-  if (e != cudaSuccess)
-    return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_rmsnorm_route: %s", cudaGetErrorString(e));
-  return launch_status("comm_allreduce_rmsnorm_route");
 }
 
 extern "C" int sm100_comm_allreduce_layernorm(float *h, const float *g, const float *b, void *y, void *own,
@@ -347,8 +295,8 @@ extern "C" int sm100_comm_allreduce_layernorm(float *h, const float *g, const fl
       ((uintptr_t)h | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) % 16)
     return sm100_set_error(SM100_ERR_ARG, "comm_allreduce_layernorm: rank %d of %d, %d x %d (rows <= %d, cols %% 4, "
                                           "16-byte aligned)", rank, world, rows, cols, kMaxRows);
-  const cudaError_t e = launch_pdl(allreduce_norm_kernel<true, false>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h,
-                                   g, b, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, 0, DsRouteArgs{});
+  const cudaError_t e = launch_pdl(allreduce_norm_kernel<true>, dim3(rows), dim3(256), 0, (cudaStream_t)stream, h, g,
+                                   b, (__nv_bfloat16 *)y, (char *)own, rank, world, cols, eps, 0);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "comm_allreduce_layernorm: %s", cudaGetErrorString(e));
   return launch_status("comm_allreduce_layernorm");
 }

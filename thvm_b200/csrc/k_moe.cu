@@ -131,31 +131,6 @@ __global__ void __launch_bounds__(256) ds_rms_kernel(const float *x, const float
   ds_rms_row(x + (int64_t)blockIdx.x * D, g, gv, y + (int64_t)blockIdx.x * D, nullptr, D, eps);
 }
 
-// The RMSNorm before the experts with the router product and the routing in
-// the same launch: CTA b normalises row b, computes its E logits from the row
-// staged in shared memory (the router weights stream through shared memory,
-// the first chunks requested before the wait on the previous kernel) and its
-// top-K; the last CTA packs every
-// token's choices (ds_route.cuh).  Bit-identical to ds_rms_kernel followed by
-// ds_router_route_kernel.
-__global__ void __launch_bounds__(256) ds_rms_route_kernel(const float *x, const float *g, __nv_bfloat16 *y, int D,
-                                                            float eps, const DsRouteArgs ra) {
-  extern __shared__ __align__(128) unsigned char rt_ring[];   // ds_route_ring_bytes(D)
-  __shared__ uint4 ys[kRtMaxD / 8];
-  __shared__ uint64_t rt_bars[kRtStages];
-  float4 gv[kRmsV];
-  ds_route_start(ra, rt_ring, rt_bars, D);
-  ds_rms_gains(g, D, gv);   // D % 8 == 0, D <= kRtMaxD: the vector path
-  pdl_wait();
-  ds_rms_row(x + (int64_t)blockIdx.x * D, g, gv, y + (int64_t)blockIdx.x * D, reinterpret_cast<__nv_bfloat16 *>(ys),
-             D, eps);
-  __syncthreads();
-  ds_route_row(ra, ys, rt_ring, rt_bars, blockIdx.x, gridDim.x, D, &g_ds_status);
-  // the expert kernel that follows fits beside this one on an SM; let it in
-  // only now (its weight prefetch would slow this launch's copies)
-  pdl_trigger();
-}
-
 // h[b] = embed[tok[b]] (bf16 table; ids outside [0, V) read zeros)
 __global__ void ds_embed_kernel(const __nv_bfloat16 *emb, const int32_t *tok, float *h, int V, int D) {
   pdl_trigger();
@@ -626,30 +601,68 @@ __global__ void __launch_bounds__(1024) ds_route_kernel(const float *logits, int
 // computes the logits of expert e for every token (x . router[e], bf16 x
 // bf16 with f32 sums, one warp per token), and the last CTA to finish (a
 // device counter, no waiting) routes every token as ds_route_kernel does, a
-// warp per token, and resets the counter for the next launch.
+// warp per token, and resets the counter for the next launch.  The router
+// row does not depend on the previous kernel: each lane holds its chunks of
+// it in registers before the wait (rows of D <= 8 x 256; longer rows load
+// the rest after).  Thread 0 counts the CTA off with an acq_rel atomic
+// after a barrier, which releases every warp's logit.
+constexpr int kRtPre = 8;
 __global__ void __launch_bounds__(1024) ds_router_route_kernel(const __nv_bfloat16 *x, const __nv_bfloat16 *router,
                                                                float *logits, int32_t *counter, int D, int E, int K,
                                                                int B, int e0, int e1, int n_shared, int32_t *sel,
                                                                float *wsel, int32_t *slot_off, int32_t *slot_tok,
                                                                float *slot_w) {
   __shared__ int s_last;
-  pdl_trigger();
-  pdl_wait();
   const int e = blockIdx.x, lane = threadIdx.x & 31, b = threadIdx.x >> 5;
   const __nv_bfloat16 *we = router + (int64_t)e * D;
-  // warp b: token b
+  uint4 wpre[kRtPre];
+#pragma unroll
+  for (int i = 0; i < kRtPre; i++) {
+    const int k = lane * 8 + 256 * i;
+    wpre[i] = b < B && k < D ? __ldg(reinterpret_cast<const uint4 *>(we + k)) : make_uint4(0, 0, 0, 0);
+  }
+  pdl_trigger();
+  pdl_wait();
+  // warp b: token b; lane l sums its chunks l, l + 32, .. in order, then the
+  // lanes by the butterfly
   if (b < B) {
-    const float acc = ds_router_dot(reinterpret_cast<const uint4 *>(x + (int64_t)b * D), we, D);
-    if (lane == 0) {
-      logits[(int64_t)b * E + e] = acc;
-      __threadfence();   // each writer's logit is visible device-wide before the CTA counts itself done
+    const uint4 *xs = reinterpret_cast<const uint4 *>(x + (int64_t)b * D);
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kRtPre; i++) {
+      const int k = lane * 8 + 256 * i;
+      if (k < D) {
+        const uint4 xv = xs[k / 8], wv = wpre[i];
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
+          acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
+        }
+      }
     }
+    for (int k = lane * 8 + 256 * kRtPre; k < D; k += 256) {
+      const uint4 xv = xs[k / 8], wv = __ldg(reinterpret_cast<const uint4 *>(we + k));
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, xx[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        acc = fmaf(__uint_as_float(xx[q] << 16), __uint_as_float(ww[q] << 16), acc);
+        acc = fmaf(__uint_as_float(xx[q] & 0xFFFF0000u), __uint_as_float(ww[q] & 0xFFFF0000u), acc);
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) logits[(int64_t)b * E + e] = acc;
   }
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(counter, 1) == E - 1;
+  if (threadIdx.x == 0) {
+    int32_t prev;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+    s_last = prev == E - 1;
+  }
+  // the last CTA's thread 0 acquired every CTA's release; the barrier carries
+  // that to the CTA's other threads, whose loads go to L2
   __syncthreads();
   if (!s_last) return;
-  __threadfence();
   ds_route_block(logits, E, K, B, e0, e1, n_shared, sel, wsel, slot_off, slot_tok, slot_w);
   if (threadIdx.x == 0) *counter = 0;
 }
@@ -1241,42 +1254,6 @@ extern "C" int sm100_ds_router_route(const void *x, const void *router, float *l
   DS_LAUNCH("ds_router_route", ds_router_route_kernel, dim3(E), dim3(1024), 0, (cudaStream_t)stream,
             (const __nv_bfloat16 *)x, (const __nv_bfloat16 *)router, logits, counter, D, E, K, B, e0, e1, n_shared,
             sel, wsel, slot_off, slot_tok, slot_w);
-}
-
-static_assert(sizeof(DsRouteArgs) == sizeof(Sm100DsRoute) && offsetof(DsRouteArgs, E) == offsetof(Sm100DsRoute, E),
-              "the device and public routing structs share one layout");
-
-// the routing arguments of a fused norm + router launch, checked
-int sm100::ds_route_args(const Sm100DsRoute *r, int B, int D, const char *who, DsRouteArgs *out) {
-  if (!r || !r->router || !r->logits || !r->counter || !r->sel || !r->wsel || !r->slot_off || !r->slot_tok ||
-      !r->slot_w || r->E < 1 || r->E > kRtMaxE || r->K < 1 || r->K > kRtMaxK || r->K > r->E || B < 1 ||
-      B > kRtMaxTok || r->e0 < 0 || r->e1 > r->E || r->e0 > r->e1 || r->n_shared < 0 || r->n_shared > 8 || D < 8 ||
-      D > kRtMaxD || D % 8 || (uintptr_t)r->router % 16)
-    return sm100_set_error(SM100_ERR_ARG, "%s: routing D %d E %d K %d B %d [%d, %d)", who, D, r ? r->E : 0,
-                           r ? r->K : 0, B, r ? r->e0 : 0, r ? r->e1 : 0);
-  memcpy(out, r, sizeof *out);
-  return SM100_OK;
-}
-
-extern "C" int sm100_ds_rmsnorm_route(const float *x, const float *g, void *y, int32_t M, int32_t D, float eps,
-                                      const Sm100DsRoute *route, void *stream) {
-  if (!x || !g || !y || M < 1 || D < 1) return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm_route: bad arguments");
-  DsRouteArgs ra;
-  const int rc = ds_route_args(route, M, D, "ds_rmsnorm_route", &ra);
-  if (rc != SM100_OK) return rc;
-  static bool attr[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "ds_rmsnorm_route: device %d", dev);
-  if (!attr[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(ds_rms_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               ds_route_ring_bytes(kRtMaxD));
-    if (e != cudaSuccess)
-      return sm100_set_error(SM100_ERR_CUDA, "ds_rmsnorm_route: smem attribute: %s", cudaGetErrorString(e));
-    attr[dev] = true;
-  }
-  DS_LAUNCH("ds_rmsnorm_route", ds_rms_route_kernel, dim3(M), dim3(256), ds_route_ring_bytes(D), (cudaStream_t)stream,
-            x, g, (__nv_bfloat16 *)y, D, eps, ra);
 }
 
 extern "C" int sm100_ds_experts(const void *x, const void *w_gu, const float *s_gu, const void *w_d, const float *s_d,

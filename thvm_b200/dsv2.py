@@ -272,7 +272,6 @@ class DSModel:
             from .comm import PeerComm
             self.comm = PeerComm(shard.rank, shard.world, D, group)
         self._pending = False   # h holds this rank's partial sums until the next norm's all-reduce
-        self._routes = {}       # layer -> its Sm100DsRoute
 
     def _stream(self):
         return ctypes.c_void_p(self.torch.cuda.current_stream().cuda_stream)
@@ -290,38 +289,17 @@ class DSModel:
         L.check(self.lib.sm100_skinny_bf16(ctypes.byref(a), self._stream()), "skinny")
         self.launches += 1
 
-    def _route_args(self, l: int, router) -> L.Sm100DsRoute:
-        """The routing of layer l's router (this rank's experts and shared
-        halves), for the norm launch that ends in it."""
-        r = self._routes.get(l)
-        if r is None:
-            r = self._routes[l] = L.Sm100DsRoute()
-            r.logits, r.counter = self.rl.data_ptr(), self.route_counter.data_ptr()
-            r.sel, r.wsel = self.sel.data_ptr(), self.wsel.data_ptr()
-            r.slot_off, r.slot_tok, r.slot_w = self.slot_off.data_ptr(), self.slot_tok.data_ptr(), self.slot_w.data_ptr()
-            r.E, r.K, r.e0, r.e1, r.n_shared = (self.cfg.n_exp, self.cfg.top_k, self.sh.e0, self.sh.e1,
-                                                len(self.sh.shared))
-        r.router = router.data_ptr()
-        return r
-
-    def _rms(self, g, D, zero_rest=False, route=None):
+    def _rms(self, g, D, zero_rest=False):
         """xn = bf16(rms(h) * g); when h holds partial sums, the all-reduce
         over the ranks is fused into the same kernel (zero_rest: ranks other
-        than 0 keep zeros in h, for partial sums that accumulate into it);
-        with route (an L.Sm100DsRoute) the router product and the routing of
-        xn end the same launch."""
-        h, gp, xn, B, eps = self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, self.cfg.eps
+        than 0 keep zeros in h, for partial sums that accumulate into it)."""
         if self._pending:
-            if route is None:
-                self.comm.allreduce_rmsnorm(h, gp, xn, B, D, eps, self._stream(), zero_rest)
-            else:
-                self.comm.allreduce_rmsnorm_route(h, gp, xn, B, D, eps, route, self._stream(), zero_rest)
+            self.comm.allreduce_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                        self.cfg.eps, self._stream(), zero_rest)
             self._pending = False
-        elif route is None:
-            L.check(self.lib.sm100_ds_rmsnorm(h, gp, xn, B, D, eps, self._stream()), "ds_rmsnorm")
         else:
-            L.check(self.lib.sm100_ds_rmsnorm_route(h, gp, xn, B, D, eps, ctypes.byref(route), self._stream()),
-                    "ds_rmsnorm_route")
+            L.check(self.lib.sm100_ds_rmsnorm(self.h.data_ptr(), g.data_ptr(), self.xn.data_ptr(), self.cfg.batch, D,
+                                              self.cfg.eps, self._stream()), "ds_rmsnorm")
         self.launches += 1
 
     def _all_reduce(self):
@@ -381,11 +359,9 @@ class DSModel:
             # the o projection's partial sums: rank 0 into the residual, the others over it
             self._skinny(self.o, w[p + "w_o"], self.h, Hl * DV, D, residual=first)
             self._all_reduce()
-            # the experts add into h: on ranks other than 0 it must start from zero.  Before the experts
-            # the norm launch also runs the router product and the routing
-            moe = l >= cfg.n_dense
-            self._rms(w[p + "ffn_norm"], D, zero_rest=moe, route=self._route_args(l, w[p + "router"]) if moe else None)
-            if not moe:
+            # the experts add into h: on ranks other than 0 it must start from zero
+            self._rms(w[p + "ffn_norm"], D, zero_rest=l >= cfg.n_dense)
+            if l < cfg.n_dense:
                 self._skinny(self.xn, w[p + "d_gu"], self.gu, D, 2 * DIl)
                 L.check(lib.sm100_ds_silu_mul(self.gu.data_ptr(), self.xn.data_ptr(), B, DIl, st()), "ds_silu_mul")
                 self.launches += 1
@@ -393,6 +369,13 @@ class DSModel:
                 self._all_reduce()
                 continue
             ns = len(sh.shared)
+            # the router product and the routing in one launch
+            L.check(lib.sm100_ds_router_route(self.xn.data_ptr(), w[p + "router"].data_ptr(), self.rl.data_ptr(),
+                                              self.route_counter.data_ptr(), D, E, K, B, sh.e0, sh.e1, ns,
+                                              self.sel.data_ptr(), self.wsel.data_ptr(), self.slot_off.data_ptr(),
+                                              self.slot_tok.data_ptr(), self.slot_w.data_ptr(), st()),
+                    "ds_router_route")
+            self.launches += 1
             # one launch pair over the local routed experts and shared halves (contiguous in this rank's
             # arrays), adding into the residual on rank 0 and into the zeros the all-reduce left in h on
             # the others
