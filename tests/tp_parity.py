@@ -4,7 +4,9 @@ process per GPU (run by tests/test_gpu_multi.py under torch.distributed.run):
   ds   config 5 (thvm_b200.dsv2.DSModel): heads, dense units, experts and
        vocabulary split over the ranks, the library's peer all-reduces of the
        residual (fused with the RMSNorm);
-  xl   config 3 (thvm_b200.gpt2_xl.XLModel): Megatron column / row splits.
+  xl   config 3 (thvm_b200.gpt2_xl.XLModel): Megatron column / row splits;
+  spec speculative decode (forced drafts) and the serve loop over the split
+       config-5 model, against its base greedy stream.
 
 Each rank holds its shard of one seeded model, both sides are fed the
 oracle's ids (teacher forcing), and rank 0 checks the gathered logits (within
@@ -82,6 +84,60 @@ def run_ds(rank, world, dist):
         excess = np.abs(a - r) - (2.0 ** -6 * np.abs(r) + 2.0 ** -6 * np.sqrt(np.mean(r * r)))
         assert excess.max() <= 0, excess.max()
     assert status == 0, status
+
+
+def run_spec(rank, world, dist):
+    """Speculative decode and the serve loop with the model split over the
+    ranks: the committed streams (forced drafts: S per step) and a served
+    request's ids equal the base greedy stream of the same split model."""
+    import torch
+    from thvm_b200.dsv2 import DSConfig, DSModel, ds_shard, ds_weights, shard_ds_weights
+    from thvm_b200.serve import Server
+    from thvm_b200.spec import SpecDecoder
+    kw = dict(n_layers=2, dim=512, heads=4, kv_lora=128, d_nope=32, d_rope=16, d_v=32, n_exp=8, top_k=3,
+              moe_inter=128, dense_inter=256, n_dense=1, n_shared=2, vocab=1000, max_ctx=64)
+    n_seq, S, n_p, n_new = 4, 4, 6, 16
+    base_cfg = DSConfig(**kw, batch=n_seq)
+    w = ds_weights(base_cfg, seed=0)
+    sh = ds_shard(base_cfg, rank, world)
+    prompts = np.random.default_rng(5).integers(0, base_cfg.vocab, (n_seq, n_p)).astype(np.int32)
+    m = DSModel(base_cfg, shard_ds_weights(w, base_cfg, sh), sh, dist.group.WORLD)
+    base = np.zeros((n_seq, n_p + n_new), np.int32)
+    base[:, :n_p] = prompts
+    for pos in range(n_p + n_new - 1):
+        if pos < n_p:
+            m.tok.copy_(torch.from_numpy(prompts[:, pos]))
+        m.step()
+        if pos + 1 >= n_p:
+            base[:, pos + 1] = m.tok.cpu().numpy()
+    torch.cuda.synchronize()
+    scfg = DSConfig(**kw, batch=n_seq * S)
+    sd = SpecDecoder(scfg, shard_ds_weights(w, scfg, sh), sh, n_seq, S, group=dist.group.WORLD, forced=True)
+    sd.prefill(prompts, seed_ids=base)
+    sd.capture()
+    want = n_p
+    while want < n_p + n_new:
+        sd.replay()
+        want += S
+        ids, ln = sd.stream_ids()
+        assert np.all(ln == want), (ln, want)
+    assert np.array_equal(ids[:, :n_p + n_new], base)
+    # one request of the serve loop on a 2-row server
+    vcfg = DSConfig(**kw, batch=2)
+    srv = Server(vcfg, shard_ds_weights(w, vcfg, sh), sh, dist.group.WORLD)
+    srv.capture()
+    rid = srv.submit(prompts[1], n_new)
+    got = {}
+    for _ in range(64):
+        srv.run(2)
+        got.update(srv.poll())
+        if not srv.busy():
+            break
+    assert np.array_equal(got[rid], base[1, n_p:]), (got.get(rid), base[1, n_p:])
+    status = sd.status() | srv.status() | m.status()
+    assert status == 0, status
+    if rank == 0:
+        print(f"spec world {world}: forced drafts committed {S} a step, the base stream; served request matches")
 
 
 def run_xl(rank, world, dist):
@@ -182,7 +238,7 @@ def main():
     os.environ["THVM_SM100_DEVICE"] = str(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", local))
     try:
-        {"ds": run_ds, "xl": run_xl, "comm": run_comm}[which](rank, world, dist)
+        {"ds": run_ds, "xl": run_xl, "comm": run_comm, "spec": run_spec}[which](rank, world, dist)
         dist.barrier()
     finally:
         dist.destroy_process_group()
