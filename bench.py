@@ -413,23 +413,47 @@ def moe_run(args, ctx):
                          "peak_gbs": round(hbm * ctx.world, 1), "frac": round(step_gbs / (hbm * ctx.world), 4)}}
         del y
 
-    # ---- e2e: ids in from pinned host memory and the next ids back, every step
+    # ---- e2e: ids in from host memory and the next ids back, every step.  One
+    # GPU: through the C host (sm100_ds_model_step: the ids copied in, the
+    # captured step replayed, the next ids copied out, all inside the call);
+    # several: through this rank's captured step with pinned copies
     e2e_steps = max(1, min(args.steps, 10))
-    host_in = torch.from_numpy(np.random.default_rng(2).integers(0, cfg.vocab, B).astype(np.int32)).pin_memory()
-    host_out = torch.empty(B, dtype=torch.int32).pin_memory()
-    ctx.barrier()
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        model.tok.copy_(host_in, non_blocking=True)
-        graph.replay()
-        host_out.copy_(model.tok, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        host_in.copy_(host_out)
-    e2e_s = ctx.max(time.perf_counter() - t0)
+    e2e_path = "python host: pinned copies around the captured step"
+    if ctx.world == 1:
+        from thvm_b200.ds_host import CDSModel
+        del graph
+        torch.cuda.synchronize()
+        cm = CDSModel(cfg, {**model.w, "cos": model.cos, "sin": model.sin})
+        pr = prompts.cpu().numpy()
+        for t in range(N_PROMPT_DS):
+            cm.step(pr[:, t], read=False)
+        ids = None
+        for _ in range(args.warmup):
+            ids = cm.step(ids)
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            ids = cm.step(ids)
+        e2e_s = time.perf_counter() - t0
+        cm.close()
+        if model.status() != 0:
+            raise RuntimeError("MoE kernels' status word set in the C host's steps")
+        e2e_path = "C host: sm100_ds_model_step (ids host -> device, the captured step, next ids device -> host)"
+    else:
+        host_in = torch.from_numpy(np.random.default_rng(2).integers(0, cfg.vocab, B).astype(np.int32)).pin_memory()
+        host_out = torch.empty(B, dtype=torch.int32).pin_memory()
+        ctx.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            model.tok.copy_(host_in, non_blocking=True)
+            graph.replay()
+            host_out.copy_(model.tok, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+            host_in.copy_(host_out)
+        e2e_s = ctx.max(time.perf_counter() - t0)
+        del graph
     e2e = B * e2e_steps / e2e_s
     launches = per_step * args.steps
-    del graph
     torch.cuda.synchronize()
     line = base_line(
         args, ctx.world, round(value, 1), ms, scaling="strong", dtype="fp8 e4m3 experts, bf16 activations / weights",
@@ -442,7 +466,7 @@ def moe_run(args, ctx):
         ms_per_token=round(ms / args.steps / B, 5), gpu_launches=int(launches), gpu_launches_per_step=per_step,
         roofline=roof,
         e2e={"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * B, "d2h_bytes_per_step": 4 * B,
-             "steps": e2e_steps},
+             "steps": e2e_steps, "path": e2e_path},
         clocks=clk.summary())
     del model
     torch.cuda.empty_cache()

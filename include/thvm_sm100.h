@@ -108,7 +108,7 @@ uint32_t sm100_buf_live_count(void);
 void *sm100_stream(void);
 int sm100_set_stream(void *stream);
 
-/* dispatch_begin / flush / end (src/backend/dispatch/*.c): end synchronises
+/* dispatch_begin / flush / end (src/backend/dispatch/ *.c): end synchronises
  * the stream at the realize boundary unless a capture is open
  * (cuda_dispatch_end, src/backend/cuda/_.c:23-27). */
 void sm100_dispatch_begin(void);
@@ -265,6 +265,33 @@ int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
 #define SM100_ARGMAX_NOALLOC_MAX_ROWS 64
 int sm100_argmax_noalloc(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
                          int32_t *bump, void *stream);
+/* ---- the config-5 decode step with its host in C --------------------------- */
+/* The step of thvm_b200/dsv2.py on one GPU over this ABI only: weights from a
+ * .safetensors file in the device layout (bf16 / fp8 codes / f32 tensors
+ * named as thvm_b200.dsv2.ds_weights, plus "cos" / "sin" [max_ctx][d_rope]
+ * f32 rotary tables), activations and compressed KV caches in backend
+ * buffers, the step captured into graph slot graph_slot on its first call and
+ * replayed after (bench/dsv2_decode_bench.c's emit + replay loop, :2014 and
+ * :2586-2610).  Call sm100_init first.  step: tok_in [batch] (host; null
+ * keeps the ids the last step chose) at the model's position, then the next
+ * ids into tok_out (host; null: no read-back, nothing waits); position + 1. */
+typedef struct Sm100DsCfg {
+  int32_t n_layers, dim, heads, kv_lora, d_nope, d_rope, d_v, n_exp, top_k, moe_inter, dense_inter, n_dense,
+      n_shared, vocab, max_ctx, batch;
+  float eps, scale;
+} Sm100DsCfg;
+typedef struct Sm100DsModel Sm100DsModel;
+int sm100_ds_model_open(const Sm100DsCfg *cfg, const char *weights_path, uint32_t graph_slot, Sm100DsModel **out);
+/* the same with the weights already on the device: n named tensors at ptrs
+ * (nbytes each), which the caller keeps alive and owns */
+int sm100_ds_model_open_ptrs(const Sm100DsCfg *cfg, const char *const *names, void *const *ptrs,
+                             const uint64_t *nbytes, int32_t n, uint32_t graph_slot, Sm100DsModel **out);
+int sm100_ds_model_step(Sm100DsModel *m, const int32_t *tok_in, int32_t *tok_out);
+int32_t sm100_ds_model_pos(const Sm100DsModel *m);     /* the next step's position (-1 on error) */
+int sm100_ds_model_reset(Sm100DsModel *m);             /* position 0 (the caches are overwritten as it advances) */
+uint32_t sm100_ds_model_logits(const Sm100DsModel *m); /* buffer id of the last step's f32 logits [batch][vocab] */
+void sm100_ds_model_close(Sm100DsModel *m);
+
 /* ---- blind speculative decode of the batched MoE step --------------------- */
 /* n_seq sequences of S rows each (row i S + s) verify S tokens per step
  * (bench/dsv2_decode_bench.c:1110-1195 draft_prep / accept_commit).  Device

@@ -82,3 +82,23 @@ def test_dsv2_pack_loads_and_bad_files_leave_nothing():
         except L.Sm100Error:
             pass
     """)
+
+
+def test_save_safetensors_round_trips_through_the_loader():
+    """thvm_b200.weights.save_safetensors (the writer of the C host's weight
+    files) -> sm100_safetensors_load: names, tags, shapes and bytes."""
+    run("""
+    import os, tempfile
+    rng = np.random.default_rng(3)
+    t = {"a": rng.standard_normal((3, 5)).astype(np.float32), "b.bf16": rng.integers(0, 65535, (7,), dtype=np.uint16),
+         "c.fp8": rng.integers(0, 255, (2, 2, 4), dtype=np.uint8), "d": np.arange(6, dtype=np.int32)}
+    with tempfile.TemporaryDirectory() as tmp:
+        p = os.path.join(tmp, "w.safetensors")
+        W.save_safetensors(p, t)
+        got = W.load_safetensors(p)
+    assert sorted(got) == sorted(t)
+    for k, a in t.items():
+        g = got[k]
+        assert g.dtype == {"a": "F32", "b.bf16": "BF16", "c.fp8": "F8_E4M3", "d": "I32"}[k] and g.shape == a.shape
+        assert np.array_equal(W.read(d, g), a)
+    """)

@@ -82,6 +82,13 @@ class Sm100Insn(ctypes.Structure):
                 ("b", ctypes.c_uint16), ("c", ctypes.c_uint16), ("imm", c_int32)]
 
 
+class Sm100DsCfg(ctypes.Structure):
+    """include/thvm_sm100.h Sm100DsCfg: the config-5 model of the C host."""
+    _fields_ = [(n, c_int32) for n in ("n_layers", "dim", "heads", "kv_lora", "d_nope", "d_rope", "d_v", "n_exp",
+                                       "top_k", "moe_inter", "dense_inter", "n_dense", "n_shared", "vocab", "max_ctx",
+                                       "batch")] + [("eps", c_float), ("scale", c_float)]
+
+
 class Sm100DsRows(ctypes.Structure):
     """include/thvm_sm100.h Sm100DsRows: per-row cache slots and positions."""
     _fields_ = [("pos", c_void_p), ("seq", c_void_p), ("n_seq", c_int32), ("shared_slots", c_int32)]
@@ -203,6 +210,13 @@ SIGNATURES = {
     "sm100_spec_accept": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   c_void_p]),
     "sm100_spec_status": (c_uint32, []),
+    "sm100_ds_model_open": (c_int, [c_void_p, ctypes.c_char_p, c_uint32, c_void_p]),
+    "sm100_ds_model_open_ptrs": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_uint32, c_void_p]),
+    "sm100_ds_model_step": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "sm100_ds_model_pos": (c_int32, [c_void_p]),
+    "sm100_ds_model_reset": (c_int, [c_void_p]),
+    "sm100_ds_model_logits": (c_uint32, [c_void_p]),
+    "sm100_ds_model_close": (None, [c_void_p]),
     "sm100_serve_advance": (c_int, [c_void_p] * 10 + [c_int32, c_int32, c_void_p]),
     "sm100_ds_router_route": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                       c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -51,3 +51,31 @@ def load_dsv2_pack(path, max_tensors: int = 4096) -> dict[str, DeviceTensor]:
 def read(device, t: DeviceTensor) -> np.ndarray:
     """The tensor's bytes back from the device, shaped."""
     return device.read(t.buf_id, t.np_dtype, t.shape)
+
+
+_TAG = {np.dtype(np.float32): "F32", np.dtype(np.uint16): "BF16", np.dtype(np.uint8): "F8_E4M3",
+        np.dtype(np.int32): "I32", np.dtype(np.int64): "I64", np.dtype(np.float16): "F16"}
+
+
+def save_safetensors(path, tensors: dict[str, np.ndarray]) -> None:
+    """Writes tensors in the .safetensors layout load_safetensors reads (an
+    8-byte little-endian header length, a JSON header of name -> {dtype,
+    shape, data_offsets}, the raw bytes; py/thvm/nn_state.py:44-85).  uint16
+    arrays are tagged BF16 (bf16 bits), uint8 arrays F8_E4M3 (e4m3 codes)."""
+    import json
+    header, blobs, off = {}, [], 0
+    for name, a in tensors.items():
+        a = np.ascontiguousarray(a)
+        tag = _TAG.get(a.dtype)
+        if tag is None:
+            raise ValueError(f"{name}: dtype {a.dtype} has no safetensors tag here")
+        header[name] = {"dtype": tag, "shape": list(a.shape), "data_offsets": [off, off + a.nbytes]}
+        blobs.append(a.tobytes())
+        off += a.nbytes
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * (-len(h) % 8)
+    with open(path, "wb") as f:
+        f.write(len(h).to_bytes(8, "little"))
+        f.write(h)
+        for b in blobs:
+            f.write(b)
