@@ -247,9 +247,10 @@ int sm100_argmax(const float *x, int64_t M, int64_t N, int64_t ld, int32_t *out,
 /* sm100_argmax without any device allocation.  This entry point has no
  * counterpart in the reference: it is for callers that cannot allocate device
  * memory (a plugin whose device memory all belongs to a host framework's
- * allocator, code recording a CUDA graph that must add no allocation nodes,
- * a process whose device budget is spent).  Its scratch is a fixed array
- * compiled into this library (about 33 KB per GPU that loads the library,
+ * allocator, a service that fixes its memory plan at start-up and allocates
+ * nothing after it, a process whose device budget is spent).  Its scratch is
+ * a fixed array compiled into this library (about 33 KB per GPU that loads
+ * the library,
  * held until the process exits): at most SM100_ARGMAX_NOALLOC_MAX_ROWS rows
  * per call, more is rejected with SM100_ERR_ARG.  Same results as
  * sm100_argmax.  It calls no cudaMalloc / cudaFree; it clears the array's

@@ -1,9 +1,9 @@
 """sm100_argmax_noalloc: the argmax entry point that allocates no device memory.
 
 It exists for callers that cannot call cudaMalloc: a plugin whose device
-memory belongs to a host framework's allocator, code that records a CUDA
-graph and must add no allocation node, a process whose device budget is
-spent.  Its scratch is a fixed array inside the library (at most
+memory belongs to a host framework's allocator, a service that fixes its
+memory plan at start-up and allocates nothing after it, a process whose
+device budget is spent.  Its scratch is a fixed array inside the library (at most
 SM100_ARGMAX_NOALLOC_MAX_ROWS = 64 rows per call).  Its ids must equal those
 of the allocating entry point sm100_argmax, exactly (argmax is index work),
 on two calls in a row (the shared array keeps the previous call's contents).

@@ -321,8 +321,8 @@ extern "C" int sm100_gather_strided_dev(void *dst, const void *src, const Sm100V
 
 // ---- argmax without device allocation ------------------------------------
 // For callers that cannot allocate device memory: a plugin whose device
-// memory all belongs to a host framework's allocator, code that runs while a
-// CUDA graph is being captured and must add no allocation nodes, or a process
+// memory all belongs to a host framework's allocator, a service that fixes
+// its memory plan at start-up and allocates nothing after it, or a process
 // whose device-memory budget is already spent.  The scratch that argmax needs
 // (per-row completion counters and per-CTA partials) lives in this fixed
 // array instead, which every GPU that loads this library holds until the
