@@ -4,23 +4,32 @@
 // (src/nn/dot.c:1-20, src/nn/linear.c:1-6); the reference renders this shape
 // as a WMMA 16x16x16 kernel (src/codegen/render_uop.c:1784-1986).
 //
-// One persistent CTA per SM, warp-specialised:
+// One persistent CTA per SM, warp-specialised, tiles of 256 x 256:
 //   warp 0  TMA producer: 2-D tensor copies (cp.async.bulk.tensor, 128-byte
-//           swizzle, no multicast) of A [128 x 64] and B [256 x 64] k-blocks
-//           into a 4-stage shared-memory ring (48 KB per stage);
+//           swizzle, no multicast) of A [256 x 64] and B [256 x 64] k-blocks
+//           into a 3-stage shared-memory ring (64 KB per stage);
 //   warp 1  MMA issuer: one thread issues tcgen05.mma (M=128, N=256, K=16,
-//           kind::f16, bf16 in / f32 accumulate) four times per k-block from
-//           shared-memory descriptors into a TMEM accumulator, then
-//           tcgen05.commit frees the stage; the tile's last commit signals the
-//           epilogue;
-//   warps 2-5 epilogue: tcgen05.ld the accumulator (each warp its 32-lane
-//           quarter = 32 rows), store f32 rows to global memory.
-// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
-// the MMAs of tile i+1.  Tiles are walked round-robin over the CTAs.
+//           kind::f16, bf16 in / f32 accumulate) for each 128-row half of
+//           the A block against the same B block, four K steps per k-block,
+//           into the two halves of TMEM (columns [0, 256) and [256, 512)),
+//           then tcgen05.commit frees the stage; the tile's last commit
+//           signals the epilogue;
+//   warps 2-9 epilogue: tcgen05.ld both accumulators (a warp its 32-lane
+//           quarter = 32 rows of each half, and half of the columns), store
+//           f32 rows to global memory.
+// A 256 x 256 tile reads 64 KB of operands per k-block for 8.4 MFLOP, a
+// third less per FLOP than a 128 x 256 tile, which is what bounds the
+// product at these sizes (L2 -> shared-memory traffic).  The two halves fill
+// TMEM, so the next tile's products wait for the epilogue to drain it (eight
+// epilogue warps keep that short).  Tiles are walked round-robin over the
+// CTAs; when the last round would leave at least half the CTAs idle, its
+// tiles are cut into 128 x 256 halves (one product chain each), so up to
+// twice as many CTAs share it.
 //
 // Every wait is bounded: a timeout sets a status word (sm100_gemm_status)
 // and the kernel runs to its end.  Shapes: M % 128 == 0, N % 256 == 0,
-// K % 64 == 0, 16-byte aligned rows.
+// K % 64 == 0, 16-byte aligned rows (a last tile row of 128 reads zeros past
+// M and stores only its rows).
 #include <cuda.h>
 
 #include "common.cuh"
@@ -28,14 +37,15 @@
 
 namespace sm100 {
 
-constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64;   // tile; BK = one 128-byte swizzle row of bf16
-constexpr int kGmStages = 4;
-constexpr int kGmABytes = kGmBM * kGmBK * 2;          // 16 KB
+constexpr int kGmBM = 128, kGmBN = 256, kGmBK = 64;   // one MMA's M and N; BK = one 128-byte swizzle row of bf16
+constexpr int kGmTM = 2 * kGmBM;                        // tile rows: two MMA halves
+constexpr int kGmStages = 3;
+constexpr int kGmABytes = kGmTM * kGmBK * 2;          // 32 KB
 constexpr int kGmBBytes = kGmBN * kGmBK * 2;          // 32 KB
 constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
-constexpr int kGmThreads = 6 * 32;
-constexpr int kGmEpiWarps = 4;
-constexpr int kGmTmemCols = 2 * kGmBN;                 // two accumulators
+constexpr int kGmEpiWarps = 8;
+constexpr int kGmThreads = (2 + kGmEpiWarps) * 32;
+constexpr int kGmTmemCols = 2 * kGmBN;                 // the two halves' accumulators
 constexpr int kGmSmem = kGmStages * kGmStageBytes + 1024 /* alignment */ + 256 /* barriers */;
 
 __device__ uint32_t g_gemm_status;   // set when a bounded wait gave up
@@ -92,9 +102,28 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// Work item i: below n_full a whole 256 x 256 tile (row-major tile order);
+// past it the remaining tiles in 128-row halves (item n_full + 2 j + h: half
+// h of tile n_full + j).  First row r0 and rows (256 or 128).
+struct GmItem {
+  int r0, tn, rows;
+};
+__device__ __forceinline__ GmItem gm_item(int item, int tiles_n, int n_full) {
+  int tile = item, h = -1;
+  if (item >= n_full) {
+    tile = n_full + (item - n_full) / 2;
+    h = (item - n_full) % 2;
+  }
+  GmItem r;
+  r.r0 = (tile / tiles_n) * kGmTM + (h > 0 ? kGmBM : 0);
+  r.tn = tile % tiles_n;
+  r.rows = h < 0 ? kGmTM : kGmBM;
+  return r;
+}
+
 __global__ void __launch_bounds__(kGmThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, float *c,
-                     int M, int N, int K) {
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a_half,
+                     const __grid_constant__ CUtensorMap map_b, float *c, int M, int N, int K, int n_full) {
   extern __shared__ unsigned char smem_raw[];
   // the 128-byte swizzle atoms want 1024-byte aligned tiles
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -105,7 +134,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   uint64_t *mma_done = acc_empty + 2;                                                 // all MMAs retired
   uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(mma_done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_m = M / kGmBM, tiles_n = N / kGmBN, n_tiles = tiles_m * tiles_n, kb_n = K / kGmBK;
+  const int tiles_m = (M + kGmTM - 1) / kGmTM, tiles_n = N / kGmBN, kb_n = K / kGmBK;
+  const int n_tiles = n_full + 2 * (tiles_m * tiles_n - n_full);   // work items: whole tiles, then halves
   uint32_t *status = &g_gemm_status;
 
   if (threadIdx.x == 0) {
@@ -113,10 +143,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int a = 0; a < 2; a++) {
-      mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], kGmEpiWarps);
-    }
+    mbar_init(&acc_full[0], 1);
+    mbar_init(&acc_empty[0], kGmEpiWarps);
     mbar_init(mma_done, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -137,7 +165,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-        const int tm = tile / tiles_n, tn = tile % tiles_n;
+        const GmItem w = gm_item(tile, tiles_n, n_full);
         for (int kb = 0; kb < kb_n; kb++, it++) {
           const int s = it % kGmStages;
           if (it >= kGmStages && !mbar_wait(&empty[s], (uint32_t)(((it / kGmStages) - 1) & 1), status)) {
@@ -145,9 +173,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
             break;
           }
           unsigned char *st = smem + (size_t)s * kGmStageBytes;
-          mbar_expect_tx(&full[s], kGmStageBytes);
-          tma_load_2d(st, &map_a, kb * kGmBK, tm * kGmBM, &full[s]);
-          tma_load_2d(st + kGmABytes, &map_b, kb * kGmBK, tn * kGmBN, &full[s]);
+          mbar_expect_tx(&full[s], (uint32_t)(w.rows * kGmBK * 2 + kGmBBytes));
+          tma_load_2d(st, w.rows == kGmTM ? &map_a : &map_a_half, kb * kGmBK, w.r0, &full[s]);
+          tma_load_2d(st + kGmABytes, &map_b, kb * kGmBK, w.tn * kGmBN, &full[s]);
         }
       }
       // the last copies have landed before the CTA may exit
@@ -160,11 +188,10 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       int it = 0, t_local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, t_local++) {
-        const int a = t_local & 1;
-        // the epilogue has drained this accumulator (its use two tiles ago)
-        if (t_local >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)(((t_local >> 1) - 1) & 1), status)) break;
+        // the epilogue has drained TMEM (the previous tile)
+        if (t_local >= 1 && !mbar_wait(&acc_empty[0], (uint32_t)((t_local - 1) & 1), status)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t tmem_d = tmem_base + (uint32_t)(a * kGmBN);   // column offset
+        const bool both = gm_item(tile, tiles_n, n_full).rows == kGmTM;
         for (int kb = 0; kb < kb_n; kb++, it++) {
           const int s = it % kGmStages;
           if (!mbar_wait(&full[s], (uint32_t)((it / kGmStages) & 1), status)) {
@@ -173,44 +200,54 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           }
           asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
           unsigned char *st = smem + (size_t)s * kGmStageBytes;
-          const uint64_t da = smem_desc_sw128(st), db = smem_desc_sw128(st + kGmABytes);
+          // the second half's rows start 128 rows (16 KB) into the A block
+          const uint64_t da0 = smem_desc_sw128(st), da1 = smem_desc_sw128(st + kGmBM * kGmBK * 2),
+                         db = smem_desc_sw128(st + kGmABytes);
 #pragma unroll
-          for (int k = 0; k < kGmBK / 16; k++)   // K = 16 per MMA: 32 bytes along the swizzled row
-            umma_bf16(tmem_d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), (kb > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < kGmBK / 16; k++) {   // K = 16 per MMA: 32 bytes along the swizzled row
+            const uint32_t acc = (kb > 0 || k > 0) ? 1u : 0u;
+            umma_bf16(tmem_base, da0 + (uint64_t)(2 * k), db + (uint64_t)(2 * k), acc);
+            if (both) umma_bf16(tmem_base + (uint32_t)kGmBN, da1 + (uint64_t)(2 * k), db + (uint64_t)(2 * k), acc);
+          }
           umma_commit(&empty[s]);   // the stage is free once these MMAs have read it
         }
-        umma_commit(&acc_full[a]);  // the accumulator is complete
+        umma_commit(&acc_full[0]);  // the accumulators are complete
       }
       // every MMA issued has retired before TMEM is released (also after a timeout)
       umma_commit(mma_done);
       mbar_wait(mma_done, 0, status, false);
     }
   } else {
-    // ---- epilogue: warps 2..5, TMEM lane quarter = warp % 4 -----------------
-    const int q = warp & 3;
+    // ---- epilogue: warps 2..9, TMEM lane quarter = warp % 4, column half
+    // (warp - 2) / 4 ----------------------------------------------------------
+    const int q = warp & 3, c0 = ((warp - 2) >> 2) * (kGmBN / 2);
     int t_local = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, t_local++) {
-      const int a = t_local & 1;
-      const int tm = tile / tiles_n, tn = tile % tiles_n;
-      if (!mbar_wait(&acc_full[a], (uint32_t)((t_local >> 1) & 1), status)) break;
+      const GmItem w = gm_item(tile, tiles_n, n_full);
+      if (!mbar_wait(&acc_full[0], (uint32_t)(t_local & 1), status)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const int row = tm * kGmBM + q * 32 + lane;
-      float *crow = c + (size_t)row * N + (size_t)tn * kGmBN;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * kGmBN);
 #pragma unroll 1
-      for (int cc = 0; cc < kGmBN; cc += 32) {
-        uint32_t r[32];
-        tmem_ld32(taddr + (uint32_t)cc, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        float4 *dst = reinterpret_cast<float4 *>(crow + cc);
+      for (int h = 0; h < w.rows / kGmBM; h++) {
+        const int row = w.r0 + h * kGmBM + q * 32 + lane;
+        float *crow = c + (size_t)row * N + (size_t)w.tn * kGmBN;
+        const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kGmBN);
+#pragma unroll 1
+        for (int cc = c0; cc < c0 + kGmBN / 2; cc += 32) {
+          uint32_t r[32];
+          tmem_ld32(taddr + (uint32_t)cc, r);   // every lane of the warp takes part (rows past M included)
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          if (row < M) {
+            float4 *dst = reinterpret_cast<float4 *>(crow + cc);
 #pragma unroll
-        for (int j = 0; j < 8; j++)
-          dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]), __uint_as_float(r[4 * j + 2]),
-                               __uint_as_float(r[4 * j + 3]));
+            for (int j = 0; j < 8; j++)
+              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          }
+        }
       }
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (lane == 0) mbar_arrive(&acc_empty[0]);
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -262,19 +299,23 @@ extern "C" int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M
     return sm100_set_error(SM100_ERR_ARG,
                            "gemm_bf16: shape %lld x %lld x %lld (M %% 128, N %% 256, K %% 64 must be 0; 16-byte aligned)",
                            (long long)M, (long long)N, (long long)K);
-  CUtensorMap ma, mb;
-  if (!make_map(&ma, a, M, K, kGmBM) || !make_map(&mb, b, N, K, kGmBN))
+  CUtensorMap ma, mah, mb;
+  if (!make_map(&ma, a, M, K, kGmTM) || !make_map(&mah, a, M, K, kGmBM) || !make_map(&mb, b, N, K, kGmBN))
     return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: tensor map encoding failed");
   static int num_sms[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "gemm_bf16: device %d", dev);
   if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  const int64_t tiles = (M / kGmBM) * (N / kGmBN);
+  const int64_t tiles = ((M + kGmTM - 1) / kGmTM) * (N / kGmBN);
   const int grid = (int)(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+  // the last round in 128-row halves when its halves fit one round
+  const int64_t full_rounds = tiles / grid, tail = tiles - full_rounds * grid;
+  const int n_full = (int)(tail > 0 && 2 * tail <= grid ? full_rounds * grid : tiles);
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: smem attribute: %s", cudaGetErrorString(e));
-  gemm_bf16_kernel<<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mb, c, (int)M, (int)N, (int)K);
+  gemm_bf16_kernel<<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N, (int)K,
+                                                                        n_full);
   return launch_status("gemm_bf16");
 }
 
