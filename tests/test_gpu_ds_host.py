@@ -49,3 +49,43 @@ def test_c_host_matches_the_python_host(tmp_path):
     finally:
         cm.close()
         cp.close()
+
+
+def test_pure_c_program_decodes_the_python_hosts_ids(tmp_path):
+    """thvm_b200/examples/ds_decode.c, compiled with gcc against the header
+    and the library and run as its own process (no Python in it): its ids,
+    prompt fed then greedy, equal the Python host's every step."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    import torch
+    from thvm_b200.ds_host import save_ds_weights
+    from thvm_b200.dsv2 import DSConfig, DSModel, ds_shard, ds_weights, shard_ds_weights
+    root = Path(__file__).resolve().parents[1]
+    cfg = DSConfig(**{**CFG, "batch": 4})
+    sh = ds_shard(cfg, 0, 1)
+    w = shard_ds_weights(ds_weights(cfg, seed=0), cfg, sh)
+    path = tmp_path / "ds.safetensors"
+    save_ds_weights(path, cfg, w)
+    exe = tmp_path / "ds_decode"
+    cc = shutil.which("gcc") or "gcc"
+    subprocess.run([cc, "-std=c11", "-O2", f"-I{root / 'include'}", str(root / "thvm_b200/examples/ds_decode.c"),
+                    f"-L{root / 'thvm_b200'}", "-lthvm_sm100", f"-Wl,-rpath,{root / 'thvm_b200'}", "-o", str(exe)],
+                   check=True)
+    np_, steps = 5, 12
+    prompt = np.random.default_rng(4).integers(0, cfg.vocab, (cfg.batch, np_)).astype(np.int32)
+    fields = [cfg.n_layers, cfg.dim, cfg.heads, cfg.kv_lora, cfg.d_nope, cfg.d_rope, cfg.d_v, cfg.n_exp, cfg.top_k,
+              cfg.moe_inter, cfg.dense_inter, cfg.n_dense, cfg.n_shared, cfg.vocab, cfg.max_ctx, cfg.batch]
+    args = [str(exe), str(path)] + [str(v) for v in fields] + [repr(cfg.eps), repr(cfg.scale), str(np_), str(steps)]
+    args += [str(v) for v in prompt.reshape(-1)]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    got = np.array([[int(v) for v in line.split()] for line in r.stdout.strip().splitlines()], np.int32)
+    ref = DSModel(cfg, w, sh)
+    out = None
+    for t in range(steps):
+        ref.tok.copy_(torch.from_numpy(prompt[:, t] if t < np_ else out))
+        ref.step()
+        out = ref.tok.cpu().numpy()
+        np.testing.assert_array_equal(got[t], out, err_msg=f"step {t}")
+    assert ref.status() == 0
