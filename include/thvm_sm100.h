@@ -439,6 +439,21 @@ int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N
  * synchronises the device and clears the word */
 uint32_t sm100_gemm_status(void);
 
+/* The same product with its epilogue fused, for the prompt (prefill) pass of
+ * the batched decoders: C = epilogue(A . B^T) with, in this order, + bias[n]
+ * (f32 [N], or NULL), GELU (SM100_GEMM_GELU; the tanh form of src/nn/gelu.c),
+ * + residual (f32 [M, N], or NULL; may be C itself when C is f32), and the
+ * store as f32 or, with SM100_GEMM_OUT_BF16, bf16 (round to nearest even):
+ * nn_linear's matmul + bias (src/nn/linear.c:1-6) with the elementwise ops
+ * that follow it.  Any M >= 1; N and K multiples of 8 (rows past M, N and K
+ * read as zeros); 16-byte aligned pointers.  Device pointers. */
+enum {
+  SM100_GEMM_GELU = 1u << 0,
+  SM100_GEMM_OUT_BF16 = 1u << 1
+};
+int sm100_gemm_bf16_ep(const void *a, const void *b, void *c, int64_t M, int64_t N, int64_t K, const float *bias,
+                       const float *residual, int32_t flags, void *stream);
+
 /* ---- skinny bf16 GEMM for batched decode (M <= 32) ------------------------ */
 /* Y[M, N] = epilogue(X[M, K] . W[N, K]^T), bf16 X and W, f32 accumulate: nn_linear
  * on a [B, 1, K] activation (src/nn/linear.c:1-6, py/thvm/nn.py:12-25) at the
@@ -503,6 +518,24 @@ int sm100_xl_argmax(float *x, int64_t ld, int32_t M, int32_t N, float *val, int3
                     int32_t zero_x, void *stream);
 /* tok[b] = index of the largest of R candidates val/idx [R][B] (ties: smaller index) */
 int sm100_xl_pick(const float *val, const int32_t *idx, int32_t R, int32_t B, int32_t *tok, void *stream);
+
+/* The prompt pass of the same model (thvm_gpt2.py:98-128 on the [B, P] prompt
+ * with start_pos 0): rows r = b P + s of all P positions per layer, the
+ * projections by sm100_gemm_bf16_ep and the causal attention by
+ * sm100_attn_prefill_bf16 over q, k, v [B, H, P, 128] bf16 whose upper 64
+ * columns stay zero (head dimension 64).  Device pointers. */
+/* h[b P + s] = wte[tok[b P + s]] + wpe[s] (ids outside [0, V) read zeros) */
+int sm100_xl_prefill_embed(const void *wte, const void *wpe, const int32_t *tok, float *h, int32_t B, int32_t P,
+                           int32_t V, int32_t D, void *stream);
+/* qkv bf16 [B P, 3 C] (C = H * 64) -> q, k, v columns 0..63 of [B, H, P, 128]
+ * and k, v into kv_cache [2, B, ctx, C] rows 0..P-1 */
+int sm100_xl_prefill_split(const void *qkv, void *q, void *k, void *v, void *kv_cache, int32_t B, int32_t P,
+                           int32_t H, int32_t ctx, void *stream);
+/* att bf16 [B P, C] = columns 0..63 of o f32 [B, H, P, 128] */
+int sm100_xl_prefill_merge(const float *o, void *att, int32_t B, int32_t P, int32_t H, void *stream);
+/* h_last [B, D] = h [B P, D] rows b P + P - 1; *pos = P */
+int sm100_xl_prefill_last(const float *h, float *h_last, int32_t *pos, int32_t B, int32_t P, int32_t D,
+                          void *stream);
 
 /* ---- the batched MoE decode step pieces (config 5) ------------------------ */
 /* DeepSeek-V2-Lite-shaped decode of B <= 32 sequences (bench/dsv2_decode_bench.c

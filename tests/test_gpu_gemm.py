@@ -57,3 +57,63 @@ def test_gemm_config2_rows(device, M, N, K):
 def test_gemm_rejects_ragged_shapes(device):
     from thvm_b200 import _lib as L
     assert device.lib.sm100_gemm_bf16(None, None, None, 100, 256, 64, device.stream) == L.ERR_ARG
+
+
+@pytest.mark.parametrize("M,N,K,flags,use_bias,use_res", [
+    (300, 104, 200, 0, True, True),        # ragged M, N, K (N, K multiples of 8)
+    (208, 960, 320, 2, True, False),       # the prompt pass's qkv product shape class, bf16 out
+    (256, 1280, 320, 3, True, False),      # + GELU, bf16 out
+    (520, 808, 800, 0, False, True),       # K = 800 (6400 split 8 ways), in-place residual
+])
+def test_gemm_ep_matches_oracle(device, M, N, K, flags, use_bias, use_res):
+    """sm100_gemm_bf16_ep: the product, then + bias, GELU, + residual and the
+    bf16 store of round to nearest even, against the oracle's product with
+    the same epilogue in f32 (GELU: oracle.gelu, the reference's tanh form);
+    bf16 outputs within one bf16 step of the oracle's f32 value."""
+    from thvm_b200 import _lib as L
+    a, b = operands(M, N, K, M + N + K + flags)
+    rng = np.random.default_rng(7)
+    bias = rng.standard_normal(N).astype(np.float32) if use_bias else None
+    res = rng.standard_normal((M, N)).astype(np.float32) if use_res else None
+    ref = O.gemm_bf16(a, b)
+    if bias is not None:
+        ref = ref + bias
+    if flags & L.GEMM_GELU:
+        ref = O.gelu(ref)
+    if res is not None:
+        ref = ref + res
+    out_bf16 = bool(flags & L.GEMM_OUT_BF16)
+    pa, pb = device.upload(a), device.upload(b)
+    pbias = device.upload(bias) if bias is not None else None
+    c = device.upload(res) if (res is not None and not out_bf16) else device.alloc(M * N * (2 if out_bf16 else 4))
+    pres = c if (res is not None and not out_bf16) else (device.upload(res) if res is not None else None)
+    dp = lambda bid: device.dptr(bid) if bid is not None else None
+    for _ in range(2):   # twice: the second call must not depend on the first (the in-place residual aside)
+        if pres is not None and pres == c:
+            device.write(c, res)
+        L.check(device.lib.sm100_gemm_bf16_ep(dp(pa), dp(pb), dp(c), M, N, K, dp(pbias), dp(pres), flags,
+                                              device.stream), "gemm_bf16_ep")
+        device.sync()
+        assert device.lib.sm100_gemm_status() == 0
+        if out_bf16:
+            got = O.bf16_to_f32(device.read(c, np.uint16, (M, N)))
+            step = np.abs(ref) * 2.0 ** -8
+            excess = np.abs(got - ref) - (step + 1e-4 * (np.sqrt(np.mean(ref * ref)) + np.abs(ref)))
+            assert excess.max() <= 0, excess.max()
+        else:
+            close(device.read(c, np.float32, (M, N)), ref)
+    for bid in {pa, pb, pbias, c, pres} - {None}:
+        device.free(bid)
+
+
+def test_gemm_ep_rejects_bad_shapes(device):
+    from thvm_b200 import _lib as L
+    lib = device.lib
+    assert lib.sm100_gemm_bf16_ep(None, None, None, 128, 256, 64, None, None, 0, device.stream) == L.ERR_ARG
+    a = device.alloc(1 << 16)
+    p = device.dptr(a)
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 100, 64, None, None, 0, device.stream) == L.ERR_ARG   # N % 8
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 104, 60, None, None, 0, device.stream) == L.ERR_ARG   # K % 8
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 104, 64, None, p, 2, device.stream) == L.ERR_ARG     # bf16 in place
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 104, 64, None, None, 4, device.stream) == L.ERR_ARG  # unknown flag
+    device.free(a)

@@ -45,3 +45,52 @@ def test_xl_decode_matches_oracle():
     # bf16 operand by one rounding step; each side then rounds k, v to bf16
     excess = np.abs(kv - rk) - (2.0 ** -7 * np.abs(rk) + 1e-3 * np.sqrt(np.mean(rk * rk)))
     assert excess.max() <= 0, excess.max()
+
+
+@pytest.mark.parametrize("dim,heads,P", [(256, 4, 8), (320, 5, 13)])
+def test_xl_prefill_then_decode_matches_oracle(dim, heads, P):
+    """The prompt pass (XLModel.prefill: every prompt position of the batch
+    through each layer at once, projections on the tcgen05 GEMM with fused
+    epilogues, causal attention on the tcgen05 prefill kernel), then decode
+    steps, against the oracle fed the prompt one position at a time: the
+    first picked ids and logits after the prompt, the cache rows 0..P-1 of
+    layer 0, and 8 decode steps after it, with the bf16 gates of the decode
+    test.  d 320 with P = 13 makes every product ragged (M = 208, N = 320 /
+    960, K = 320)."""
+    import torch
+    from thvm_b200.gpt2_xl import XLConfig, XLModel, shard_of, xl_weights
+    cfg = XLConfig(n_layers=2, dim=dim, heads=heads, vocab=1000, max_ctx=64, batch=16)
+    w = xl_weights(cfg, seed=3)
+    dev = XLModel(cfg, w, shard_of(cfg, 0, 1))
+    ref = O.XLModel(cfg, w)
+    prompt = np.random.default_rng(5).integers(0, cfg.vocab, (cfg.batch, P)).astype(np.int32)
+    for pos in range(P):
+        lg, nxt = ref.step(prompt[:, pos], pos)
+    dev.prefill(prompt)
+    torch.cuda.synchronize()
+    assert int(dev.pos.item()) == P
+    assert dev.lib.sm100_attn_prefill_status() == 0 and dev.lib.sm100_gemm_status() == 0
+    agree, total, worst = 0, 0, 0.0
+    for step in range(9):
+        if step:
+            dev.tok.copy_(torch.from_numpy(tok))
+            dev.step()
+            torch.cuda.synchronize()
+            lg, nxt = ref.step(tok, P + step - 1)
+            assert int(dev.pos.item()) == P + step
+        dl = dev.logits.cpu().numpy()
+        worst = max(worst, float((np.abs(dl - lg).max(1) / np.abs(lg).max(1)).max()))
+        agree += int((dev.tok.cpu().numpy() == nxt).sum())
+        total += cfg.batch
+        tok = nxt
+    assert worst <= 2e-2, worst
+    assert agree / total >= 0.99, agree / total
+    f32 = lambda b: (b.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    kv = f32(dev.kv[0].cpu().numpy().view(np.uint16)[:, :, :P])
+    rk = f32(ref.kv[0][:, :, :P])
+    # one bf16 step of the value, plus one bf16 step of one LayerNorm output
+    # (the f32 LayerNorm sums differ in order; an output near 4 moves by
+    # 2^-6, times a weight of up to ~0.08: ~1.3e-3, 4e-3 of the rms here).
+    # An f64 recomputation of these rows differs from the oracle's as much.
+    excess = np.abs(kv - rk) - (2.0 ** -7 * np.abs(rk) + 5e-3 * np.sqrt(np.mean(rk * rk)))
+    assert excess.max() <= 0, excess.max()

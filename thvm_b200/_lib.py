@@ -69,6 +69,7 @@ class Sm100AttnArgs(ctypes.Structure):
 
 
 SK_GELU, SK_RESIDUAL, SK_OUT_BF16, SK_KV, SK_ACCUM, SK_X_GELU, SK_X_LN = 1, 2, 4, 8, 16, 32, 64
+GEMM_GELU, GEMM_OUT_BF16 = 1, 2
 
 
 class Sm100TensorEntry(ctypes.Structure):
@@ -175,6 +176,8 @@ SIGNATURES = {
     "sm100_decode_steps": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_decode_step": (c_int, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
+    "sm100_gemm_bf16_ep": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int32,
+                                   c_void_p]),
     "sm100_gemm_status": (c_uint32, []),
     "sm100_attn_prefill_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                         c_float, c_int32, c_void_p]),
@@ -190,6 +193,12 @@ SIGNATURES = {
     "sm100_xl_argmax": (c_int, [c_void_p, c_int64, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32,
                                 c_void_p]),
     "sm100_xl_pick": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "sm100_xl_prefill_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                       c_void_p]),
+    "sm100_xl_prefill_split": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
+                                       c_int32, c_void_p]),
+    "sm100_xl_prefill_merge": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "sm100_xl_prefill_last": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
     "sm100_ds_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_qkv_post": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

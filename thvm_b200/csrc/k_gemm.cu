@@ -121,9 +121,83 @@ __device__ __forceinline__ GmItem gm_item(int item, int tiles_n, int n_full) {
   return r;
 }
 
+// The fused epilogue of sm100_gemm_bf16_ep on one 32-column chunk of one row
+// (columns col0 .. col0 + 31, those below N): bias, GELU, residual, then an
+// f32 or bf16 store; the order of the skinny GEMM's epilogue (k_skinny.cu).
+__device__ __forceinline__ void gm_epilogue32(const uint32_t (&r)[32], void *c, const float *bias, const float *res,
+                                              int flags, int64_t row, int col0, int N) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
+  const bool full = col0 + 32 <= N;
+  if (bias) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] += (full || col0 + j < N) ? bias[col0 + j] : 0.0f;
+  }
+  if (flags & SM100_GEMM_GELU) {
+#pragma unroll
+    for (int j = 0; j < 32; j++) v[j] = gelu_tanh(v[j]);
+  }
+  const int64_t o = row * N + col0;
+  if (res) {
+    if (full) {
+      const float4 *rs = reinterpret_cast<const float4 *>(res + o);
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const float4 t = rs[j];
+        v[4 * j] += t.x;
+        v[4 * j + 1] += t.y;
+        v[4 * j + 2] += t.z;
+        v[4 * j + 3] += t.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (col0 + j < N) v[j] += res[o + j];
+    }
+  }
+  if (flags & SM100_GEMM_OUT_BF16) {
+    __nv_bfloat16 *y = reinterpret_cast<__nv_bfloat16 *>(c) + o;
+    if (full) {
+      uint4 *dst = reinterpret_cast<uint4 *>(y);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        uint32_t w[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const __nv_bfloat162 t = __floats2bfloat162_rn(v[8 * j + 2 * i], v[8 * j + 2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t *>(&t);
+        }
+        dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (col0 + j < N) y[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    float *y = reinterpret_cast<float *>(c) + o;
+    if (full) {
+      float4 *dst = reinterpret_cast<float4 *>(y);
+#pragma unroll
+      for (int j = 0; j < 8; j++) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; j++)
+        if (col0 + j < N) y[j] = v[j];
+    }
+  }
+}
+
+// kEp = false: the plain product (f32 C, N % 256 == 0, K % 64 == 0);
+// kEp = true: any N and K that are multiples of 8 (the tensor maps read zeros
+// past them) and the fused epilogue gm_epilogue32.
+template <bool kEp>
 __global__ void __launch_bounds__(kGmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a_half,
-                     const __grid_constant__ CUtensorMap map_b, float *c, int M, int N, int K, int n_full) {
+                     const __grid_constant__ CUtensorMap map_b, void *c_out, int M, int N, int K, int n_full,
+                     const float *bias, const float *res, int flags) {
+  float *c = reinterpret_cast<float *>(c_out);
   extern __shared__ unsigned char smem_raw[];
   // the 128-byte swizzle atoms want 1024-byte aligned tiles
   unsigned char *smem = reinterpret_cast<unsigned char *>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -134,7 +208,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
   uint64_t *mma_done = acc_empty + 2;                                                 // all MMAs retired
   uint32_t *tmem_base_s = reinterpret_cast<uint32_t *>(mma_done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tiles_m = (M + kGmTM - 1) / kGmTM, tiles_n = N / kGmBN, kb_n = K / kGmBK;
+  const int tiles_m = (M + kGmTM - 1) / kGmTM, tiles_n = (N + kGmBN - 1) / kGmBN, kb_n = (K + kGmBK - 1) / kGmBK;
   const int n_tiles = n_full + 2 * (tiles_m * tiles_n - n_full);   // work items: whole tiles, then halves
   uint32_t *status = &g_gemm_status;
 
@@ -236,7 +310,10 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           uint32_t r[32];
           tmem_ld32(taddr + (uint32_t)cc, r);   // every lane of the warp takes part (rows past M included)
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if (row < M) {
+          if constexpr (kEp) {
+            if (row < M && w.tn * kGmBN + cc < N)
+              gm_epilogue32(r, c_out, bias, res, flags, row, w.tn * kGmBN + cc, N);
+          } else if (row < M) {
             float4 *dst = reinterpret_cast<float4 *>(crow + cc);
 #pragma unroll
             for (int j = 0; j < 8; j++)
@@ -292,6 +369,32 @@ static bool make_map(CUtensorMap *m, const void *base, int64_t rows, int64_t col
 
 using namespace sm100;
 
+// Grid and tile split of one launch (tiles of 256 x 256, whole or halved).
+static int gemm_launch(bool ep, const CUtensorMap &ma, const CUtensorMap &mah, const CUtensorMap &mb, void *c,
+                       int64_t M, int64_t N, int64_t K, const float *bias, const float *res, int flags,
+                       void *stream, const char *name) {
+  static int num_sms[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "%s: device %d", name, dev);
+  if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = ((M + kGmTM - 1) / kGmTM) * ((N + kGmBN - 1) / kGmBN);
+  const int grid = (int)(tiles < num_sms[dev] ? tiles : num_sms[dev]);
+  // the last round in 128-row halves when its halves fit one round
+  const int64_t full_rounds = tiles / grid, tail = tiles - full_rounds * grid;
+  const int n_full = (int)(tail > 0 && 2 * tail <= grid ? full_rounds * grid : tiles);
+  const void *fn = ep ? (const void *)gemm_bf16_kernel<true> : (const void *)gemm_bf16_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
+  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
+  if (ep)
+    gemm_bf16_kernel<true><<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N, (int)K,
+                                                                              n_full, bias, res, flags);
+  else
+    gemm_bf16_kernel<false><<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N,
+                                                                               (int)K, n_full, nullptr, nullptr, 0);
+  return launch_status(name);
+}
+
 extern "C" int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M, int64_t N, int64_t K,
                                void *stream) {
   if (!a || !b || !c || M <= 0 || N <= 0 || K <= 0 || M % kGmBM || N % kGmBN || K % kGmBK || M > (1 << 30) ||
@@ -302,21 +405,24 @@ extern "C" int sm100_gemm_bf16(const void *a, const void *b, float *c, int64_t M
   CUtensorMap ma, mah, mb;
   if (!make_map(&ma, a, M, K, kGmTM) || !make_map(&mah, a, M, K, kGmBM) || !make_map(&mb, b, N, K, kGmBN))
     return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: tensor map encoding failed");
-  static int num_sms[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return sm100_set_error(SM100_ERR_ARG, "gemm_bf16: device %d", dev);
-  if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
-  const int64_t tiles = ((M + kGmTM - 1) / kGmTM) * (N / kGmBN);
-  const int grid = (int)(tiles < num_sms[dev] ? tiles : num_sms[dev]);
-  // the last round in 128-row halves when its halves fit one round
-  const int64_t full_rounds = tiles / grid, tail = tiles - full_rounds * grid;
-  const int n_full = (int)(tail > 0 && 2 * tail <= grid ? full_rounds * grid : tiles);
-  cudaError_t e = cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
-  if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16: smem attribute: %s", cudaGetErrorString(e));
-  gemm_bf16_kernel<<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N, (int)K,
-                                                                        n_full);
-  return launch_status("gemm_bf16");
+  return gemm_launch(false, ma, mah, mb, c, M, N, K, nullptr, nullptr, 0, stream, "gemm_bf16");
+}
+
+extern "C" int sm100_gemm_bf16_ep(const void *a, const void *b, void *c, int64_t M, int64_t N, int64_t K,
+                                  const float *bias, const float *residual, int32_t flags, void *stream) {
+  const bool bad_ptr = ((uintptr_t)a & 15) || ((uintptr_t)b & 15) || ((uintptr_t)c & 15) ||
+                       ((uintptr_t)bias & 15) || ((uintptr_t)residual & 15);
+  if (!a || !b || !c || M <= 0 || N <= 0 || K <= 0 || N % 8 || K % 8 || M > (1 << 30) || N > (1 << 30) ||
+      K > (1 << 30) || bad_ptr || (flags & ~(SM100_GEMM_GELU | SM100_GEMM_OUT_BF16)) ||
+      (residual && residual == c && (flags & SM100_GEMM_OUT_BF16)))
+    return sm100_set_error(SM100_ERR_ARG,
+                           "gemm_bf16_ep: shape %lld x %lld x %lld flags %d (N %% 8, K %% 8 must be 0; 16-byte aligned; "
+                           "an in-place residual needs f32 output)",
+                           (long long)M, (long long)N, (long long)K, (int)flags);
+  CUtensorMap ma, mah, mb;
+  if (!make_map(&ma, a, M, K, kGmTM) || !make_map(&mah, a, M, K, kGmBM) || !make_map(&mb, b, N, K, kGmBN))
+    return sm100_set_error(SM100_ERR_CUDA, "gemm_bf16_ep: tensor map encoding failed");
+  return gemm_launch(true, ma, mah, mb, c, M, N, K, bias, residual, flags, stream, "gemm_bf16_ep");
 }
 
 // Status of the GEMM launches since the last call (non-zero: a bounded wait

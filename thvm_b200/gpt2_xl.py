@@ -263,6 +263,14 @@ class XLModel:
             self._skinny(self.g, w[p + "p2.w"], self.h, Fl, D, bias=w[p + "p2.b"] if first else None,
                          residual=self.h if first else None, flags=res)
             self._all_reduce(self.h)
+        self._head()
+        L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, self._stream()), "pos_add")
+        self.launches += 1
+
+    def _head(self):
+        """ln_f, lm_head and the token pick of the B rows in self.h -> self.tok."""
+        cfg, sh, w, lib = self.cfg, self.sh, self.w, self.lib
+        B, D = cfg.batch, cfg.dim
         self._ln(w["ln_f.w"], w["ln_f.b"])
         Vl = sh.v1 - sh.v0
         self._skinny(self.xa, w["lm_head"], self.logits, D, Vl)
@@ -274,5 +282,84 @@ class XLModel:
         else:
             L.check(lib.sm100_xl_pick(self.vals.data_ptr(), self.idxs.data_ptr(), 1, B, self.tok.data_ptr(),
                                       self._stream()), "xl_pick")
-        L.check(lib.sm100_pos_add(self.pos.data_ptr(), 1, self._stream()), "pos_add")
-        self.launches += 2
+        self.launches += 1
+
+    # -- the prompt pass ----------------------------------------------------------
+    def _gemm(self, a, wt, c, M, N, K, bias=None, residual=None, flags=0):
+        L.check(self.lib.sm100_gemm_bf16_ep(a.data_ptr(), wt.data_ptr(), c.data_ptr(), M, N, K,
+                                            bias.data_ptr() if bias is not None else None,
+                                            residual.data_ptr() if residual is not None else None, flags,
+                                            self._stream()), "gemm_bf16_ep")
+        self.launches += 1
+
+    def _prefill_bufs(self, P: int) -> dict:
+        if getattr(self, "_pf", None) is not None and self._pf["P"] == P:
+            return self._pf
+        torch, cfg, sh = self.torch, self.cfg, self.sh
+        B, D, C, Fl, H, M = cfg.batch, cfg.dim, sh.cols, sh.f1 - sh.f0, sh.h1 - sh.h0, cfg.batch * P
+        z = lambda *s, dt=torch.int16: torch.zeros(*s, dtype=dt, device=self.dev)
+        self._pf = dict(P=P, tok=z(M, dt=torch.int32), h=z(M, D, dt=torch.float32), x=z(M, D), qkv=z(M, 3 * C),
+                        q=z(B, H, P, 128), k=z(B, H, P, 128), v=z(B, H, P, 128),   # columns 64.. stay zero
+                        o=z(B, H, P, 128, dt=torch.float32), att=z(M, C), g=z(M, Fl))
+        return self._pf
+
+    def prefill(self, prompts: np.ndarray):
+        """The prompt pass (thvm_gpt2.py:98-128 with start_pos 0): prompts
+        [B, P] ids, all P positions of every sequence through each layer at
+        once (the projections on the tcgen05 GEMM with fused epilogues, the
+        causal attention on the tcgen05 prefill kernel).  Afterwards the cache
+        holds rows 0..P-1, self.tok the ids picked from each sequence's last
+        position and pos = P: the state P decode steps fed the prompt leave.
+        Same numerics as step() up to f32 summation order, except that q is
+        rounded to bf16 for the attention product."""
+        torch, cfg, sh, w, lib = self.torch, self.cfg, self.sh, self.w, self.lib
+        prompts = np.ascontiguousarray(prompts, np.int32)
+        B, D, C, Fl, H = cfg.batch, cfg.dim, sh.cols, sh.f1 - sh.f0, sh.h1 - sh.h0
+        if prompts.ndim != 2 or prompts.shape[0] != B or not 1 <= prompts.shape[1] < cfg.max_ctx:
+            raise ValueError(f"prompts of shape {prompts.shape}: want [{B}, P] with 1 <= P < {cfg.max_ctx}")
+        P = prompts.shape[1]
+        M = B * P
+        f = self._prefill_bufs(P)
+        f["tok"].copy_(torch.from_numpy(prompts.reshape(-1)))
+        first = sh.rank == 0
+        st = self._stream
+        L.check(lib.sm100_xl_prefill_embed(w["wte"].data_ptr(), w["wpe"].data_ptr(), f["tok"].data_ptr(),
+                                           f["h"].data_ptr(), B, P, cfg.vocab, D, st()), "xl_prefill_embed")
+        self.launches += 1
+        h, x = f["h"], f["x"]
+
+        def ln(g, b):
+            L.check(lib.sm100_xl_layernorm(h.data_ptr(), g.data_ptr(), b.data_ptr(), x.data_ptr(), M, D, cfg.norm_eps,
+                                           0, None, 0, st()), "xl_layernorm")
+            self.launches += 1
+
+        def reduce_rows():   # row-split partial sums -> the full sums on every rank
+            if sh.world > 1:
+                torch.distributed.all_reduce(h, group=self.group)
+
+        for i in range(cfg.n_layers):
+            p = f"h.{i}."
+            ln(w[p + "ln_1.w"], w[p + "ln_1.b"])
+            self._gemm(x, w[p + "attn.w"], f["qkv"], M, 3 * C, D, bias=w[p + "attn.b"], flags=L.GEMM_OUT_BF16)
+            L.check(lib.sm100_xl_prefill_split(f["qkv"].data_ptr(), f["q"].data_ptr(), f["k"].data_ptr(),
+                                               f["v"].data_ptr(), self.kv[i].data_ptr(), B, P, H, cfg.max_ctx, st()),
+                    "xl_prefill_split")
+            L.check(lib.sm100_attn_prefill_bf16(f["q"].data_ptr(), f["k"].data_ptr(), f["v"].data_ptr(),
+                                                f["o"].data_ptr(), B, H, P, 128, 1.0 / np.sqrt(HEAD_DIM), 1, st()),
+                    "attn_prefill")
+            L.check(lib.sm100_xl_prefill_merge(f["o"].data_ptr(), f["att"].data_ptr(), B, P, H, st()),
+                    "xl_prefill_merge")
+            self.launches += 3
+            # row-split: rank 0 adds bias + residual, the others leave their partial in h
+            self._gemm(f["att"], w[p + "proj.w"], h, M, D, C, bias=w[p + "proj.b"] if first else None,
+                       residual=h if first else None)
+            reduce_rows()
+            ln(w[p + "ln_2.w"], w[p + "ln_2.b"])
+            self._gemm(x, w[p + "fc.w"], f["g"], M, Fl, D, bias=w[p + "fc.b"], flags=L.GEMM_GELU | L.GEMM_OUT_BF16)
+            self._gemm(f["g"], w[p + "p2.w"], h, M, D, Fl, bias=w[p + "p2.b"] if first else None,
+                       residual=h if first else None)
+            reduce_rows()
+        L.check(lib.sm100_xl_prefill_last(h.data_ptr(), self.h.data_ptr(), self.pos.data_ptr(), B, P, D, st()),
+                "xl_prefill_last")
+        self.launches += 1
+        self._head()
