@@ -441,7 +441,8 @@ uint32_t sm100_gemm_status(void);
 
 /* The same product with its epilogue fused, for the prompt (prefill) pass of
  * the batched decoders: C = epilogue(A . B^T) with, in this order, + bias[n]
- * (f32 [N], or NULL), GELU (SM100_GEMM_GELU; the tanh form of src/nn/gelu.c),
+ * (f32 [N], or NULL), GELU (SM100_GEMM_GELU; the tanh form of src/nn/gelu.c,
+ * evaluated as x sigmoid(2 u) on the fast exponential, ~1e-6 relative),
  * + residual (f32 [M, N], or NULL; may be C itself when C is f32), and the
  * store as f32 or, with SM100_GEMM_OUT_BF16, bf16 (round to nearest even):
  * nn_linear's matmul + bias (src/nn/linear.c:1-6) with the elementwise ops

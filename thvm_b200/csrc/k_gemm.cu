@@ -121,6 +121,17 @@ __device__ __forceinline__ GmItem gm_item(int item, int tiles_n, int n_full) {
   return r;
 }
 
+// GELU, tanh form, as x sigmoid(2 u) = x / (1 + e^(-2 u)) with u = sqrt(2/pi)
+// (x + 0.044715 x^3) (the same function: 0.5 (1 + tanh u) = sigmoid(2 u)),
+// on the fast exponential: ~1e-6 relative, far below the bf16 rounding of
+// the products it feeds, and a few instructions where the bit-exact form of
+// the fp32 decode path (common.cuh gelu_tanh) takes dozens, which would leave
+// the tensor cores idle behind the epilogue.
+__device__ __forceinline__ float gm_gelu(float x) {
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  return __fdividef(x, 1.0f + __expf(-2.0f * fmaxf(u, -40.0f)));
+}
+
 // The fused epilogue of sm100_gemm_bf16_ep on one 32-column chunk of one row
 // (columns col0 .. col0 + 31, those below N): bias, GELU, residual, then an
 // f32 or bf16 store; the order of the skinny GEMM's epilogue (k_skinny.cu).
@@ -136,7 +147,7 @@ __device__ __forceinline__ void gm_epilogue32(const uint32_t (&r)[32], void *c, 
   }
   if (flags & SM100_GEMM_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = gelu_tanh(v[j]);
+    for (int j = 0; j < 32; j++) v[j] = gm_gelu(v[j]);
   }
   const int64_t o = row * N + col0;
   if (res) {
@@ -240,6 +251,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
         const GmItem w = gm_item(tile, tiles_n, n_full);
+        if (w.r0 >= M) continue;   // a half wholly past M: no work (every role skips it)
         for (int kb = 0; kb < kb_n; kb++, it++) {
           const int s = it % kGmStages;
           if (it >= kGmStages && !mbar_wait(&empty[s], (uint32_t)(((it / kGmStages) - 1) & 1), status)) {
@@ -261,7 +273,8 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     if (lane == 0) {
       int it = 0, t_local = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, t_local++) {
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        if (gm_item(tile, tiles_n, n_full).r0 >= M) continue;
         // the epilogue has drained TMEM (the previous tile)
         if (t_local >= 1 && !mbar_wait(&acc_empty[0], (uint32_t)((t_local - 1) & 1), status)) break;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -286,6 +299,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
           umma_commit(&empty[s]);   // the stage is free once these MMAs have read it
         }
         umma_commit(&acc_full[0]);  // the accumulators are complete
+        t_local++;
       }
       // every MMA issued has retired before TMEM is released (also after a timeout)
       umma_commit(mma_done);
@@ -296,8 +310,9 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     // (warp - 2) / 4 ----------------------------------------------------------
     const int q = warp & 3, c0 = ((warp - 2) >> 2) * (kGmBN / 2);
     int t_local = 0;
-    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, t_local++) {
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
       const GmItem w = gm_item(tile, tiles_n, n_full);
+      if (w.r0 >= M) continue;
       if (!mbar_wait(&acc_full[0], (uint32_t)(t_local & 1), status)) break;
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
@@ -325,6 +340,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[0]);
+      t_local++;
     }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -380,17 +396,20 @@ static int gemm_launch(bool ep, const CUtensorMap &ma, const CUtensorMap &mah, c
   if (!num_sms[dev]) cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev);
   const int64_t tiles = ((M + kGmTM - 1) / kGmTM) * ((N + kGmBN - 1) / kGmBN);
   const int grid = (int)(tiles < num_sms[dev] ? tiles : num_sms[dev]);
-  // the last round in 128-row halves when its halves fit one round
+  // the last round in 128-row halves when its halves fit one round (every
+  // tile, when all the halves fit one round of the SMs)
   const int64_t full_rounds = tiles / grid, tail = tiles - full_rounds * grid;
-  const int n_full = (int)(tail > 0 && 2 * tail <= grid ? full_rounds * grid : tiles);
+  int n_full = (int)(tail > 0 && 2 * tail <= grid ? full_rounds * grid : tiles);
+  if (2 * tiles <= num_sms[dev]) n_full = 0;
+  const int grid_items = n_full == 0 ? (int)(2 * tiles) : grid;
   const void *fn = ep ? (const void *)gemm_bf16_kernel<true> : (const void *)gemm_bf16_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGmSmem);
   if (e != cudaSuccess) return sm100_set_error(SM100_ERR_CUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
   if (ep)
-    gemm_bf16_kernel<true><<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N, (int)K,
+    gemm_bf16_kernel<true><<<grid_items, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N, (int)K,
                                                                               n_full, bias, res, flags);
   else
-    gemm_bf16_kernel<false><<<grid, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N,
+    gemm_bf16_kernel<false><<<grid_items, kGmThreads, kGmSmem, (cudaStream_t)stream>>>(ma, mah, mb, c, (int)M, (int)N,
                                                                                (int)K, n_full, nullptr, nullptr, 0);
   return launch_status(name);
 }

@@ -187,6 +187,7 @@ class XLModel:
             from .comm import PeerComm
             self.comm = PeerComm(shard.rank, shard.world, D, group)
         self._pending = False   # h holds this rank's partial sums until the next LayerNorm's all-reduce
+        self._pf = None         # the prompt pass's buffers (for one prompt length)
 
     # -- one launcher per kernel ------------------------------------------------
     def _stream(self):
@@ -293,7 +294,7 @@ class XLModel:
         self.launches += 1
 
     def _prefill_bufs(self, P: int) -> dict:
-        if getattr(self, "_pf", None) is not None and self._pf["P"] == P:
+        if self._pf is not None and self._pf["P"] == P:
             return self._pf
         torch, cfg, sh = self.torch, self.cfg, self.sh
         B, D, C, Fl, H, M = cfg.batch, cfg.dim, sh.cols, sh.f1 - sh.f0, sh.h1 - sh.h0, cfg.batch * P
@@ -312,15 +313,26 @@ class XLModel:
         position and pos = P: the state P decode steps fed the prompt leave.
         Same numerics as step() up to f32 summation order, except that q is
         rounded to bf16 for the attention product."""
-        torch, cfg, sh, w, lib = self.torch, self.cfg, self.sh, self.w, self.lib
+        self.prefill_ids(prompts)
+        self.prefill_run(prompts.shape[1])
+
+    def prefill_ids(self, prompts: np.ndarray):
+        """Copies prompts [B, P] into the prompt pass's id buffer."""
+        cfg = self.cfg
         prompts = np.ascontiguousarray(prompts, np.int32)
+        if prompts.ndim != 2 or prompts.shape[0] != cfg.batch or not 1 <= prompts.shape[1] < cfg.max_ctx:
+            raise ValueError(f"prompts of shape {prompts.shape}: want [{cfg.batch}, P] with 1 <= P < {cfg.max_ctx}")
+        self._prefill_bufs(prompts.shape[1])["tok"].copy_(self.torch.from_numpy(prompts.reshape(-1)))
+
+    def prefill_run(self, P: int):
+        """The launches of the prompt pass over the ids prefill_ids() copied
+        (device work only: a CUDA graph can capture it)."""
+        torch, cfg, sh, w, lib = self.torch, self.cfg, self.sh, self.w, self.lib
         B, D, C, Fl, H = cfg.batch, cfg.dim, sh.cols, sh.f1 - sh.f0, sh.h1 - sh.h0
-        if prompts.ndim != 2 or prompts.shape[0] != B or not 1 <= prompts.shape[1] < cfg.max_ctx:
-            raise ValueError(f"prompts of shape {prompts.shape}: want [{B}, P] with 1 <= P < {cfg.max_ctx}")
-        P = prompts.shape[1]
         M = B * P
-        f = self._prefill_bufs(P)
-        f["tok"].copy_(torch.from_numpy(prompts.reshape(-1)))
+        f = self._pf
+        if f is None or f["P"] != P:
+            raise ValueError(f"prefill_run({P}) without prefill_ids of P = {P} ids")
         first = sh.rank == 0
         st = self._stream
         L.check(lib.sm100_xl_prefill_embed(w["wte"].data_ptr(), w["wpe"].data_ptr(), f["tok"].data_ptr(),
