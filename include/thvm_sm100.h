@@ -532,6 +532,10 @@ int sm100_xl_prefill_embed(const void *wte, const void *wpe, const int32_t *tok,
  * and k, v into kv_cache [2, B, ctx, C] rows 0..P-1 */
 int sm100_xl_prefill_split(const void *qkv, void *q, void *k, void *v, void *kv_cache, int32_t B, int32_t P,
                            int32_t H, int32_t ctx, void *stream);
+/* y (bf16) = LayerNorm(x) * g + b over M rows of D (D % 4 == 0, D <= 2048):
+ * sm100_xl_layernorm's function, one warp per row */
+int sm100_xl_prefill_layernorm(const float *x, const float *g, const float *b, void *y, int32_t M, int32_t D,
+                               float eps, void *stream);
 /* att bf16 [B P, C] = columns 0..63 of o f32 [B, H, P, 128] */
 int sm100_xl_prefill_merge(const float *o, void *att, int32_t B, int32_t P, int32_t H, void *stream);
 /* h_last [B, D] = h [B P, D] rows b P + P - 1; *pos = P */

@@ -3,7 +3,7 @@
 the peer-memory collectives alone, config 5 split over heads, dense units,
 experts and vocabulary rows (its all-reduces fused into RMSNorm kernels over
 peer memory), its speculative decode and serve loop, and config 3 split
-Megatron-style.  Skipped when fewer than two GPUs are visible."""
+Megatron-style (decode steps, and the prompt pass followed by decode steps).  Skipped when fewer than two GPUs are visible."""
 import os
 import subprocess
 import sys

@@ -172,6 +172,39 @@ def run_xl(rank, world, dist):
         print(f"xl world {world}: worst logit error {worst:.3e}, top-1 agreement {agree}/{total}")
         assert worst <= 2e-2, worst
         assert agree / total >= 0.99, agree / total
+    # the prompt pass over the split model (row-split partial sums summed by an
+    # NCCL all-reduce per block), then decode steps after it
+    P = prompt.shape[1]
+    dev2 = XLModel(cfg, shard_weights(w, cfg, sh), sh, dist.group.WORLD)
+    ref2 = O.XLModel(cfg, w) if rank == 0 else None
+    nxt = np.zeros(cfg.batch, np.int32)
+    if rank == 0:
+        for pos in range(P):
+            lg, nxt = ref2.step(prompt[:, pos], pos)
+    dev2.prefill(prompt)
+    torch.cuda.synchronize()
+    agree, total, worst = 0, 0, 0.0
+    for step in range(7):
+        if step:
+            dev2.tok.copy_(torch.from_numpy(tok))
+            dev2.step()
+            torch.cuda.synchronize()
+            if rank == 0:
+                lg, nxt = ref2.step(tok, P + step - 1)
+        lg_all = gathered_logits(dev2, dist, world)
+        if rank == 0:
+            worst = max(worst, float((np.abs(lg_all - lg).max(1) / np.abs(lg).max(1)).max()))
+            agree += int((dev2.tok.cpu().numpy() == nxt).sum())
+            total += cfg.batch
+        t = torch.from_numpy(np.ascontiguousarray(nxt, np.int32)).cuda()
+        dist.broadcast(t, 0)
+        tok = t.cpu().numpy()
+    if rank == 0:
+        print(f"xl prefill world {world}: worst logit error {worst:.3e}, top-1 agreement {agree}/{total}")
+        assert worst <= 2e-2, worst
+        assert agree / total >= 0.99, agree / total
+    dev.close()
+    dev2.close()
 
 
 def run_comm(rank, world, dist):

@@ -198,6 +198,8 @@ SIGNATURES = {
     "sm100_xl_prefill_split": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32,
                                        c_int32, c_void_p]),
     "sm100_xl_prefill_merge": (c_int, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
+    "sm100_xl_prefill_layernorm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float,
+                                           c_void_p]),
     "sm100_xl_prefill_last": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),
     "sm100_ds_rmsnorm": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_float, c_void_p]),
     "sm100_ds_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_void_p]),

@@ -18,6 +18,8 @@
 //                     0..P-1 ([2, B, ctx, C], as the decode step keeps it);
 //   xl_prefill_merge  the attention output's first 64 columns per head ->
 //                     bf16 [B P, C] rows (the next product's operand);
+//   xl_prefill_ln     LayerNorm of the B P rows to the bf16 operand, a warp
+//                     per row;
 //   xl_prefill_last   h of each sequence's last position -> the decode
 //                     step's [B, D] rows, and the cache position = P.
 #include "common.cuh"
@@ -66,6 +68,57 @@ __global__ void xl_prefill_merge_kernel(const float *o, __nv_bfloat16 *att, int 
   }
 }
 
+// y = bf16(LayerNorm(x) * g + b) over the B P rows, one warp per row with
+// the row in registers (one read of x; xl_ln_kernel's one-CTA-per-row form
+// reads it three times and leaves the SMs mostly idle at these row counts).
+// Mean and biased variance as sum * (1/D), 1/sqrt (src/nn/layernorm.c:1-7).
+constexpr int kXpLnVec = 16;   // float4 per lane: D <= 16 * 128 = 2048
+
+__global__ void __launch_bounds__(256) xl_prefill_ln_kernel(const float *x, const float *g, const float *bt,
+                                                             __nv_bfloat16 *y, int M, int D, float eps) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)row * D);
+  const int n4 = D / 4;
+  float4 v[kXpLnVec];
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kXpLnVec; j++) {
+    const int i = lane + 32 * j;
+    v[j] = i < n4 ? xr[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+  }
+  s = warp_sum(s);
+  const float inv_n = 1.0f / (float)D, mean = s * inv_n;
+  float q = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kXpLnVec; j++) {
+    if (lane + 32 * j < n4) {
+      const float a = v[j].x - mean, b = v[j].y - mean, c = v[j].z - mean, d = v[j].w - mean;
+      q += (a * a + b * b) + (c * c + d * d);
+    }
+  }
+  q = warp_sum(q);
+  const float r = 1.0f / sqrtf(q * inv_n + eps);
+  const float4 *g4 = reinterpret_cast<const float4 *>(g), *b4 = reinterpret_cast<const float4 *>(bt);
+  uint2 *yr = reinterpret_cast<uint2 *>(y + (int64_t)row * D);
+#pragma unroll
+  for (int j = 0; j < kXpLnVec; j++) {
+    const int i = lane + 32 * j;
+    if (i < n4) {
+      const float4 gg = g4[i], bb = b4[i];
+      const __nv_bfloat162 lo = __floats2bfloat162_rn((v[j].x - mean) * r * gg.x + bb.x,
+                                                      (v[j].y - mean) * r * gg.y + bb.y);
+      const __nv_bfloat162 hi = __floats2bfloat162_rn((v[j].z - mean) * r * gg.z + bb.z,
+                                                      (v[j].w - mean) * r * gg.w + bb.w);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t *>(&lo);
+      w.y = *reinterpret_cast<const uint32_t *>(&hi);
+      yr[i] = w;
+    }
+  }
+}
+
 __global__ void xl_prefill_last_kernel(const float *h, float *hl, int32_t *pos, int P, int D) {
   const int b = blockIdx.x;
   const float *src = h + ((int64_t)b * P + P - 1) * D;
@@ -103,6 +156,16 @@ extern "C" int sm100_xl_prefill_merge(const float *o, void *att, int32_t B, int3
     return sm100_set_error(SM100_ERR_ARG, "xl_prefill_merge: bad arguments");
   xl_prefill_merge_kernel<<<B * P, 256, 0, (cudaStream_t)stream>>>(o, (__nv_bfloat16 *)att, P, H);
   return launch_status("xl_prefill_merge");
+}
+
+extern "C" int sm100_xl_prefill_layernorm(const float *x, const float *g, const float *b, void *y, int32_t M,
+                                          int32_t D, float eps, void *stream) {
+  if (!x || !g || !b || !y || M < 1 || D < 4 || D % 4 || D > kXpLnVec * 128 ||
+      (((uintptr_t)x | (uintptr_t)g | (uintptr_t)b | (uintptr_t)y) & 15))
+    return sm100_set_error(SM100_ERR_ARG, "xl_prefill_layernorm: %d x %d (D %% 4, D <= %d, 16-byte aligned)", M, D,
+                           kXpLnVec * 128);
+  xl_prefill_ln_kernel<<<(M + 7) / 8, 256, 0, (cudaStream_t)stream>>>(x, g, b, (__nv_bfloat16 *)y, M, D, eps);
+  return launch_status("xl_prefill_layernorm");
 }
 
 extern "C" int sm100_xl_prefill_last(const float *h, float *h_last, int32_t *pos, int32_t B, int32_t P, int32_t D,

@@ -341,8 +341,8 @@ class XLModel:
         h, x = f["h"], f["x"]
 
         def ln(g, b):
-            L.check(lib.sm100_xl_layernorm(h.data_ptr(), g.data_ptr(), b.data_ptr(), x.data_ptr(), M, D, cfg.norm_eps,
-                                           0, None, 0, st()), "xl_layernorm")
+            L.check(lib.sm100_xl_prefill_layernorm(h.data_ptr(), g.data_ptr(), b.data_ptr(), x.data_ptr(), M, D,
+                                                   cfg.norm_eps, st()), "xl_prefill_layernorm")
             self.launches += 1
 
         def reduce_rows():   # row-split partial sums -> the full sums on every rank
