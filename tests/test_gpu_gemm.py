@@ -117,3 +117,40 @@ def test_gemm_ep_rejects_bad_shapes(device):
     assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 104, 64, None, p, 2, device.stream) == L.ERR_ARG     # bf16 in place
     assert lib.sm100_gemm_bf16_ep(p, p, p, 16, 104, 64, None, None, 4, device.stream) == L.ERR_ARG  # unknown flag
     device.free(a)
+
+
+@pytest.mark.parametrize("M,N,K,ep", [(2048, 4864, 512, False), (2000, 4856, 520, True), (4096, 4096, 1024, False)])
+def test_gemm_partial_rounds_match_oracle(device, M, N, K, ep):
+    """Shapes whose 256 x 256 tiles do not fill whole rounds of the 148 SMs
+    (152, 152 and 256 tiles: a last round of 128-row halves, or of whole
+    tiles), twice in a row, 96 seeded rows against the oracle; the second
+    case ragged in M, N and K with the fused epilogue (bias, GELU, bf16
+    out)."""
+    from thvm_b200 import _lib as L
+    a, b = operands(M, N, K, 11 + M + N + K)
+    rows = np.sort(np.random.default_rng(3).choice(M, 96, replace=False))
+    ref = O.gemm_bf16(a[rows], b)
+    bias = np.random.default_rng(8).standard_normal(N).astype(np.float32) if ep else None
+    if ep:
+        ref = O.gelu(ref + bias)
+    pa, pb = device.upload(a), device.upload(b)
+    pbias = device.upload(bias) if ep else None
+    c = device.alloc(M * N * (2 if ep else 4))
+    for _ in range(2):
+        if ep:
+            L.check(device.lib.sm100_gemm_bf16_ep(device.dptr(pa), device.dptr(pb), device.dptr(c), M, N, K,
+                                                  device.dptr(pbias), None, L.GEMM_GELU | L.GEMM_OUT_BF16,
+                                                  device.stream), "gemm_bf16_ep")
+        else:
+            L.check(device.lib.sm100_gemm_bf16(device.dptr(pa), device.dptr(pb), device.dptr(c), M, N, K,
+                                               device.stream), "gemm_bf16")
+        device.sync()
+        assert device.lib.sm100_gemm_status() == 0
+        if ep:
+            got = O.bf16_to_f32(device.read(c, np.uint16, (M, N)))[rows]
+            excess = np.abs(got - ref) - (np.abs(ref) * 2.0 ** -8 + 1e-4 * (np.sqrt(np.mean(ref * ref)) + np.abs(ref)))
+            assert excess.max() <= 0, excess.max()
+        else:
+            close(device.read(c, np.float32, (M, N))[rows], ref)
+    for bid in (pa, pb, c) + ((pbias,) if ep else ()):
+        device.free(bid)

@@ -15,8 +15,10 @@
 //           then tcgen05.commit frees the stage; the tile's last commit
 //           signals the epilogue;
 //   warps 2-9 epilogue: tcgen05.ld both accumulators (a warp its 32-lane
-//           quarter = 32 rows of each half, and half of the columns), store
-//           f32 rows to global memory.
+//           quarter = 32 rows of each half, and half of the columns), each
+//           32 x 32 block through the warp's 4 KB of shared memory (a lane
+//           writes its row, then reads four columns of eight rows), so the
+//           global stores are whole 128-byte rows (f32; 64 bytes bf16).
 // A 256 x 256 tile reads 64 KB of operands per k-block for 8.4 MFLOP, a
 // third less per FLOP than a 128 x 256 tile, which is what bounds the
 // product at these sizes (L2 -> shared-memory traffic).  The two halves fill
@@ -46,7 +48,9 @@ constexpr int kGmStageBytes = kGmABytes + kGmBBytes;
 constexpr int kGmEpiWarps = 8;
 constexpr int kGmThreads = (2 + kGmEpiWarps) * 32;
 constexpr int kGmTmemCols = 2 * kGmBN;                 // the two halves' accumulators
-constexpr int kGmSmem = kGmStages * kGmStageBytes + 1024 /* alignment */ + 256 /* barriers */;
+constexpr int kGmStageF = 32 * 32;                     // one epilogue warp's staging block: 32 rows x 32 f32
+constexpr int kGmSmem = kGmStages * kGmStageBytes + 1024 /* alignment */ + 256 /* barriers */ +
+                        kGmEpiWarps * kGmStageF * 4 /* epilogue staging */;
 
 __device__ uint32_t g_gemm_status;   // set when a bounded wait gave up
 
@@ -132,77 +136,68 @@ __device__ __forceinline__ float gm_gelu(float x) {
   return __fdividef(x, 1.0f + __expf(-2.0f * fmaxf(u, -40.0f)));
 }
 
-// The fused epilogue of sm100_gemm_bf16_ep on one 32-column chunk of one row
-// (columns col0 .. col0 + 31, those below N): bias, GELU, residual, then an
-// f32 or bf16 store; the order of the skinny GEMM's epilogue (k_skinny.cu).
-__device__ __forceinline__ void gm_epilogue32(const uint32_t (&r)[32], void *c, const float *bias, const float *res,
-                                              int flags, int64_t row, int col0, int N) {
-  float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; j++) v[j] = __uint_as_float(r[j]);
-  const bool full = col0 + 32 <= N;
+// The fused epilogue of sm100_gemm_bf16_ep on columns col .. col + 3 of rows
+// row0 + 4 i, i < 8 (N % 4 == 0, so the four columns are all below N or
+// none): bias, GELU, residual, then an f32 or bf16 store; the order of the
+// skinny GEMM's epilogue (k_skinny.cu).  Every load is issued before the
+// first store (the residual may be the output itself, so the compiler could
+// not move them across the stores).
+__device__ __forceinline__ void gm_epilogue4x8(float4 (&v)[8], void *c, const float *bias, const float *res,
+                                               int flags, int row0, int col, int M, int N) {
+  if (col >= N) return;
   if (bias) {
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + col));
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] += (full || col0 + j < N) ? bias[col0 + j] : 0.0f;
+    for (int i = 0; i < 8; i++) {
+      v[i].x += b.x;
+      v[i].y += b.y;
+      v[i].z += b.z;
+      v[i].w += b.w;
+    }
   }
   if (flags & SM100_GEMM_GELU) {
 #pragma unroll
-    for (int j = 0; j < 32; j++) v[j] = gm_gelu(v[j]);
+    for (int i = 0; i < 8; i++) {
+      v[i].x = gm_gelu(v[i].x);
+      v[i].y = gm_gelu(v[i].y);
+      v[i].z = gm_gelu(v[i].z);
+      v[i].w = gm_gelu(v[i].w);
+    }
   }
-  const int64_t o = row * N + col0;
   if (res) {
-    if (full) {
-      const float4 *rs = reinterpret_cast<const float4 *>(res + o);
+    float4 t[8];
 #pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float4 t = rs[j];
-        v[4 * j] += t.x;
-        v[4 * j + 1] += t.y;
-        v[4 * j + 2] += t.z;
-        v[4 * j + 3] += t.w;
-      }
-    } else {
+    for (int i = 0; i < 8; i++)
+      t[i] = row0 + 4 * i < M ? *reinterpret_cast<const float4 *>(res + (int64_t)(row0 + 4 * i) * N + col)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < 32; j++)
-        if (col0 + j < N) v[j] += res[o + j];
+    for (int i = 0; i < 8; i++) {
+      v[i].x += t[i].x;
+      v[i].y += t[i].y;
+      v[i].z += t[i].z;
+      v[i].w += t[i].w;
     }
   }
-  if (flags & SM100_GEMM_OUT_BF16) {
-    __nv_bfloat16 *y = reinterpret_cast<__nv_bfloat16 *>(c) + o;
-    if (full) {
-      uint4 *dst = reinterpret_cast<uint4 *>(y);
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        uint32_t w[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-          const __nv_bfloat162 t = __floats2bfloat162_rn(v[8 * j + 2 * i], v[8 * j + 2 * i + 1]);
-          w[i] = *reinterpret_cast<const uint32_t *>(&t);
-        }
-        dst[j] = make_uint4(w[0], w[1], w[2], w[3]);
-      }
+  for (int i = 0; i < 8; i++) {
+    const int row = row0 + 4 * i;
+    if (row >= M) continue;
+    const int64_t o = (int64_t)row * N + col;
+    if (flags & SM100_GEMM_OUT_BF16) {
+      const __nv_bfloat162 lo = __floats2bfloat162_rn(v[i].x, v[i].y), hi = __floats2bfloat162_rn(v[i].z, v[i].w);
+      uint2 w;
+      w.x = *reinterpret_cast<const uint32_t *>(&lo);
+      w.y = *reinterpret_cast<const uint32_t *>(&hi);
+      *reinterpret_cast<uint2 *>(reinterpret_cast<__nv_bfloat16 *>(c) + o) = w;
     } else {
-#pragma unroll
-      for (int j = 0; j < 32; j++)
-        if (col0 + j < N) y[j] = __float2bfloat16_rn(v[j]);
-    }
-  } else {
-    float *y = reinterpret_cast<float *>(c) + o;
-    if (full) {
-      float4 *dst = reinterpret_cast<float4 *>(y);
-#pragma unroll
-      for (int j = 0; j < 8; j++) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; j++)
-        if (col0 + j < N) y[j] = v[j];
+      *reinterpret_cast<float4 *>(reinterpret_cast<float *>(c) + o) = v[i];
     }
   }
 }
 
 // kEp = false: the plain product (f32 C, N % 256 == 0, K % 64 == 0);
 // kEp = true: any N and K that are multiples of 8 (the tensor maps read zeros
-// past them) and the fused epilogue gm_epilogue32.
+// past them) and the fused epilogue gm_epilogue4x8.
 template <bool kEp>
 __global__ void __launch_bounds__(kGmThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_a_half,
@@ -309,6 +304,7 @@ __global__ void __launch_bounds__(kGmThreads, 1)
     // ---- epilogue: warps 2..9, TMEM lane quarter = warp % 4, column half
     // (warp - 2) / 4 ----------------------------------------------------------
     const int q = warp & 3, c0 = ((warp - 2) >> 2) * (kGmBN / 2);
+    float *stg = reinterpret_cast<float *>(smem + kGmStages * kGmStageBytes + 256) + (warp - 2) * kGmStageF;
     int t_local = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
       const GmItem w = gm_item(tile, tiles_n, n_full);
@@ -317,23 +313,39 @@ __global__ void __launch_bounds__(kGmThreads, 1)
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 #pragma unroll 1
       for (int h = 0; h < w.rows / kGmBM; h++) {
-        const int row = w.r0 + h * kGmBM + q * 32 + lane;
-        float *crow = c + (size_t)row * N + (size_t)w.tn * kGmBN;
         const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(h * kGmBN);
+        const int row_w = w.r0 + h * kGmBM + q * 32;   // the warp's first row
 #pragma unroll 1
         for (int cc = c0; cc < c0 + kGmBN / 2; cc += 32) {
           uint32_t r[32];
           tmem_ld32(taddr + (uint32_t)cc, r);   // every lane of the warp takes part (rows past M included)
           asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          if constexpr (kEp) {
-            if (row < M && w.tn * kGmBN + cc < N)
-              gm_epilogue32(r, c_out, bias, res, flags, row, w.tn * kGmBN + cc, N);
-          } else if (row < M) {
-            float4 *dst = reinterpret_cast<float4 *>(crow + cc);
+          // through the warp's staging block, so that the global stores are
+          // whole 128-byte rows: lane l writes its row l (float4 j at slot
+          // j ^ (l & 7): no bank conflicts either way), then lane l takes
+          // float4 l & 7 of rows l / 8 + 4 i
+          float4 *mine = reinterpret_cast<float4 *>(stg + lane * 32);
 #pragma unroll
-            for (int j = 0; j < 8; j++)
-              dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          for (int j = 0; j < 8; j++)
+            mine[j ^ (lane & 7)] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+          __syncwarp();
+          const int j = lane & 7, col = w.tn * kGmBN + cc + 4 * j;
+          float4 v[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) {
+            const int rr = (lane >> 3) + 4 * i;
+            v[i] = reinterpret_cast<const float4 *>(stg + rr * 32)[j ^ (rr & 7)];
+          }
+          __syncwarp();   // the block is read before the next chunk overwrites it
+          if constexpr (kEp) {
+            gm_epilogue4x8(v, c_out, bias, res, flags, row_w + (lane >> 3), col, M, N);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+              const int row = row_w + (lane >> 3) + 4 * i;
+              if (row < M) *reinterpret_cast<float4 *>(c + (size_t)row * N + col) = v[i];
+            }
           }
         }
       }
