@@ -47,7 +47,7 @@ def test_xl_decode_matches_oracle():
     assert excess.max() <= 0, excess.max()
 
 
-@pytest.mark.parametrize("dim,heads,P", [(256, 4, 8), (320, 5, 13)])
+@pytest.mark.parametrize("dim,heads,P", [(256, 4, 8), (320, 5, 13), (256, 4, 1)])
 def test_xl_prefill_then_decode_matches_oracle(dim, heads, P):
     """The prompt pass (XLModel.prefill: every prompt position of the batch
     through each layer at once, projections on the tcgen05 GEMM with fused
@@ -56,7 +56,8 @@ def test_xl_prefill_then_decode_matches_oracle(dim, heads, P):
     first picked ids and logits after the prompt, the cache rows 0..P-1 of
     layer 0, and 8 decode steps after it, with the bf16 gates of the decode
     test.  d 320 with P = 13 makes every product ragged (M = 208, N = 320 /
-    960, K = 320)."""
+    960, K = 320); P = 1 is a prompt of one id (16 rows, attention over one
+    key)."""
     import torch
     from thvm_b200.gpt2_xl import XLConfig, XLModel, shard_of, xl_weights
     cfg = XLConfig(n_layers=2, dim=dim, heads=heads, vocab=1000, max_ctx=64, batch=16)
