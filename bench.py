@@ -1066,21 +1066,29 @@ def xl_run(args, ctx):
     # the prompt pass: every prompt position through each layer at once
     # (tcgen05 GEMM with fused epilogues, tcgen05 causal prefill attention);
     # once untimed (buffers, launch attributes), then timed
-    # (a CUDA graph of its launches, captured after one eager pass)
+    # (at N = 1 a CUDA graph of its launches, captured after one eager pass;
+    # split over ranks its per-block NCCL all-reduces run eagerly, uncaptured)
     model.prefill_ids(prompts.cpu().numpy())
     with torch.cuda.stream(s):
         model.prefill_run(n_prompt)
     torch.cuda.current_stream().wait_stream(s)
     torch.cuda.synchronize()
-    pf_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(pf_graph):
+    pf_graph = None
+    if ctx.world == 1:
+        pf_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(pf_graph):
+            model.prefill_run(n_prompt)
+        pf_graph.replay()
+    else:
         model.prefill_run(n_prompt)
-    pf_graph.replay()
     torch.cuda.synchronize()
     ctx.barrier()
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     p0.record()
-    pf_graph.replay()
+    if pf_graph is not None:
+        pf_graph.replay()
+    else:
+        model.prefill_run(n_prompt)
     p1.record()
     p1.synchronize()
     pf_ms = ctx.max(p0.elapsed_time(p1))
@@ -1119,7 +1127,8 @@ def xl_run(args, ctx):
     line["prefill"] = {"ms": round(pf_ms, 3), "prompt_tok_s": round(cfg.batch * n_prompt / (pf_ms / 1e3), 1),
                        "flops": pf_flops, "tflops": round(pf_tflops, 1),
                        "frac": round(pf_tflops / (bf16_peak * ctx.world), 4), "peak_source": kind,
-                       "what": f"XLModel.prefill_run of [{cfg.batch}, {n_prompt}] ids, one CUDA graph replay"}
+                       "what": f"XLModel.prefill_run of [{cfg.batch}, {n_prompt}] ids, "
+                               + ("one CUDA graph replay" if ctx.world == 1 else "eager launches")}
     return line
 
 
