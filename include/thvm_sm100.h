@@ -293,6 +293,37 @@ int sm100_ds_model_reset(Sm100DsModel *m);             /* position 0 (the caches
 uint32_t sm100_ds_model_logits(const Sm100DsModel *m); /* buffer id of the last step's f32 logits [batch][vocab] */
 void sm100_ds_model_close(Sm100DsModel *m);
 
+/* ---- the config-3 model with its host in C -------------------------------- */
+/* The batched GPT-2-XL-shaped model of thvm_b200/gpt2_xl.py on one GPU over
+ * this ABI only (bench/gpt2/thvm_gpt2.py:98-128 with bf16 weights: the prompt
+ * forward, then one token at a time): weights from a .safetensors file in the
+ * device layout (named as thvm_b200.gpt2_xl.xl_weights: bf16 "wte", "wpe",
+ * "lm_head", "h.<l>.attn.w" ...; f32 biases and LayerNorm affines),
+ * activations and bf16 KV caches [2, batch, max_ctx, dim] per layer in
+ * backend buffers.  dim = heads * 64.  Call sm100_init first.
+ * prefill: prompts [batch][len] (host, 1 <= len < max_ctx) through every
+ * layer at once (sm100_gemm_bf16_ep, sm100_attn_prefill_bf16 and the
+ * sm100_xl_prefill_* glue, eager launches): cache rows 0..len-1, the first
+ * ids into tok_out (host; null: none), position = len.  step: tok_in [batch]
+ * (host; null keeps the ids the last call chose) at the model's position,
+ * next ids into tok_out; position + 1; captured into graph slot graph_slot
+ * on its first call and replayed after. */
+typedef struct Sm100XlCfg {
+  int32_t n_layers, dim, heads, vocab, max_ctx, batch;
+  float norm_eps;
+} Sm100XlCfg;
+typedef struct Sm100XlModel Sm100XlModel;
+int sm100_xl_model_open(const Sm100XlCfg *cfg, const char *weights_path, uint32_t graph_slot, Sm100XlModel **out);
+/* the same with the weights already on the device (kept alive and owned by
+ * the caller) */
+int sm100_xl_model_open_ptrs(const Sm100XlCfg *cfg, const char *const *names, void *const *ptrs,
+                             const uint64_t *nbytes, int32_t n, uint32_t graph_slot, Sm100XlModel **out);
+int sm100_xl_model_prefill(Sm100XlModel *m, const int32_t *prompts, int32_t len, int32_t *tok_out);
+int sm100_xl_model_step(Sm100XlModel *m, const int32_t *tok_in, int32_t *tok_out);
+int32_t sm100_xl_model_pos(const Sm100XlModel *m);     /* the next step's position (-1 on error) */
+uint32_t sm100_xl_model_logits(const Sm100XlModel *m); /* buffer id of the last f32 logits [batch][vocab] */
+void sm100_xl_model_close(Sm100XlModel *m);
+
 /* ---- blind speculative decode of the batched MoE step --------------------- */
 /* n_seq sequences of S rows each (row i S + s) verify S tokens per step
  * (bench/dsv2_decode_bench.c:1110-1195 draft_prep / accept_commit).  Device

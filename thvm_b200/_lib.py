@@ -83,6 +83,12 @@ class Sm100Insn(ctypes.Structure):
                 ("b", ctypes.c_uint16), ("c", ctypes.c_uint16), ("imm", c_int32)]
 
 
+class Sm100XlCfg(ctypes.Structure):
+    """include/thvm_sm100.h Sm100XlCfg: the config-3 model of the C host."""
+    _fields_ = [(f, c_int32) for f in ("n_layers", "dim", "heads", "vocab", "max_ctx", "batch")] + \
+        [("norm_eps", c_float)]
+
+
 class Sm100DsCfg(ctypes.Structure):
     """include/thvm_sm100.h Sm100DsCfg: the config-5 model of the C host."""
     _fields_ = [(n, c_int32) for n in ("n_layers", "dim", "heads", "kv_lora", "d_nope", "d_rope", "d_v", "n_exp",
@@ -228,6 +234,13 @@ SIGNATURES = {
     "sm100_ds_model_reset": (c_int, [c_void_p]),
     "sm100_ds_model_logits": (c_uint32, [c_void_p]),
     "sm100_ds_model_close": (None, [c_void_p]),
+    "sm100_xl_model_open": (c_int, [c_void_p, ctypes.c_char_p, c_uint32, c_void_p]),
+    "sm100_xl_model_open_ptrs": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_uint32, c_void_p]),
+    "sm100_xl_model_prefill": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
+    "sm100_xl_model_step": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "sm100_xl_model_pos": (c_int32, [c_void_p]),
+    "sm100_xl_model_logits": (c_uint32, [c_void_p]),
+    "sm100_xl_model_close": (None, [c_void_p]),
     "sm100_serve_advance": (c_int, [c_void_p] * 10 + [c_int32, c_int32, c_void_p]),
     "sm100_ds_router_route": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32,
                                       c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
