@@ -70,3 +70,29 @@ def test_custom_program_compiles_for_sm100a_without_a_gpu():
     assert lib.sm100_custom_program(b"fine", good, g, b, 0) == _lib.ERR_STATE
     assert b"compiled" in lib.sm100_last_error()
     assert lib.sm100_custom_program(b"fine", good, g, (c_uint32 * 3)(2048, 1, 1), 0) == _lib.ERR_ARG
+
+
+def test_prompt_pass_entry_points_reject_bad_arguments_without_a_gpu():
+    """The fused-epilogue GEMM, the prompt-pass glue and the config-3 C host
+    check their arguments before anything touches a device: shapes outside
+    their contracts come back as SM100_ERR_ARG with a message."""
+    from thvm_b200 import _lib
+    lib = _lib.lib()
+    p = ctypes.c_void_p(1 << 20)   # an aligned stand-in address; never dereferenced
+    ERR = _lib.ERR_ARG
+    assert lib.sm100_gemm_bf16_ep(None, p, p, 128, 256, 64, None, None, 0, None) == ERR
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 128, 100, 64, None, None, 0, None) == ERR            # N % 8
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 128, 256, 60, None, None, 0, None) == ERR            # K % 8
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 128, 256, 64, None, p, _lib.GEMM_OUT_BF16, None) == ERR  # bf16 in place
+    assert lib.sm100_gemm_bf16_ep(p, p, p, 128, 256, 64, None, None, 8, None) == ERR            # unknown flag
+    assert lib.sm100_xl_prefill_split(p, p, p, p, p, 16, 65, 4, 64, None) == ERR               # P > ctx
+    assert lib.sm100_xl_prefill_layernorm(p, p, p, p, 16, 4096, 1e-5, None) == ERR             # D > 2048
+    assert lib.sm100_xl_prefill_merge(None, p, 16, 8, 4, None) == ERR
+    assert lib.sm100_xl_prefill_embed(p, p, p, p, 0, 8, 1000, 256, None) == ERR
+    assert lib.sm100_xl_prefill_last(p, p, None, 16, 8, 256, None) == ERR
+    cfg = _lib.Sm100XlCfg(n_layers=2, dim=320, heads=4, vocab=1000, max_ctx=64, batch=16, norm_eps=1e-5)  # dim != 64 heads
+    out = ctypes.c_void_p()
+    assert lib.sm100_xl_model_open(ctypes.byref(cfg), b"missing.safetensors", 0, ctypes.byref(out)) == ERR
+    assert not out.value
+    assert b"configuration" in lib.sm100_last_error()
+    assert ctypes.sizeof(_lib.Sm100XlCfg) == 28
