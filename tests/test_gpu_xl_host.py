@@ -43,3 +43,37 @@ def test_c_host_matches_the_python_host(tmp_path):
     finally:
         cm.close()
         cp.close()
+
+
+def test_pure_c_program_decodes_the_python_hosts_ids(tmp_path):
+    """thvm_b200/examples/xl_decode.c, compiled with gcc against the header
+    and the library and run as its own process (no Python in it): the ids
+    of its prompt pass and of 6 greedy steps equal the Python host's."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    from thvm_b200.gpt2_xl import XLConfig, XLModel, shard_of, xl_weights
+    from thvm_b200.weights import save_safetensors
+    root = Path(__file__).resolve().parents[1]
+    cfg = XLConfig(n_layers=2, dim=256, heads=4, vocab=1000, max_ctx=64, batch=4)
+    w = xl_weights(cfg, seed=4)
+    path = tmp_path / "xl.safetensors"
+    save_safetensors(path, w)
+    exe = tmp_path / "xl_decode"
+    subprocess.run([shutil.which("gcc") or "gcc", "-std=c11", "-O2", f"-I{root / 'include'}",
+                    str(root / "thvm_b200/examples/xl_decode.c"), f"-L{root / 'thvm_b200'}", "-lthvm_sm100",
+                    f"-Wl,-rpath,{root / 'thvm_b200'}", "-o", str(exe)], check=True)
+    np_, steps = 9, 6
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab, (cfg.batch, np_)).astype(np.int32)
+    args = [str(exe), str(path)] + [str(v) for v in (cfg.n_layers, cfg.dim, cfg.heads, cfg.vocab, cfg.max_ctx,
+                                                     cfg.batch)]
+    args += [repr(cfg.norm_eps), str(np_), str(steps)] + [str(v) for v in prompt.reshape(-1)]
+    r = subprocess.run(args, capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    got = np.array([[int(v) for v in line.split()] for line in r.stdout.strip().splitlines()], np.int32)
+    ref = XLModel(cfg, w, shard_of(cfg, 0, 1))
+    ref.prefill(prompt)
+    for t in range(steps + 1):
+        if t:
+            ref.step()
+        np.testing.assert_array_equal(got[t], ref.tok.cpu().numpy(), err_msg=f"step {t}")
