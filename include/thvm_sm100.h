@@ -732,6 +732,15 @@ typedef struct {
 } Sm100TensorEntry;
 int sm100_safetensors_load(const char *path, Sm100TensorEntry *entries, int32_t max_entries, int32_t *n_out);
 int sm100_dsv2pack_load(const char *path, Sm100TensorEntry *entries, int32_t max_entries, int32_t *n_out);
+/* A torch.save checkpoint (py/thvm/nn_state.py torch_load, :123-230): the zip
+ * format (<archive>/data.pkl and the storages at <archive>/data/<key>, stored
+ * uncompressed; zip64 included) or the legacy pickle stream.  Every
+ * top-level tensor or parameter of the state dict, elements row-major in
+ * the file's type: dtype "F32", "F64", "F16", "BF16", "I64", "I32", "I16",
+ * "I8", "U8" or "BOOL" (the reference widens BF16 and F64 to f32 on read);
+ * a permuted tensor (strides a permutation of a row-major layout) is made
+ * row-major through a host gather, other strides are refused as there. */
+int sm100_torch_load(const char *path, Sm100TensorEntry *entries, int32_t max_entries, int32_t *n_out);
 
 /* ---- custom-kernel ABI: raw CUDA-C programs -------------------------------
  * Replaces cuda_custom_dispatch (src/backend/cuda/jit.c:802-893) for the

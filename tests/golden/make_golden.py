@@ -22,6 +22,10 @@ package finds its library beside itself) and the reference's GPT-2 model code
                code decoded.
   state.safetensors  a few seeded tensors of several dtypes written by the
                reference's own safe_save (the weight-file loader's fixture).
+  state.pt, state_legacy.pt, torch_state.npz  a seeded state dict saved by
+               torch.save in its zip and legacy formats, and what the
+               reference's own torch_load reads from each (the checkpoint
+               loader's fixture).
   gpt2.npz     GPT-2 small (12 layers, fp32, MAX_CONTEXT=1024) greedy decode:
                the 16 prompt ids, the 64 generated ids, per-step top-1 / top-2
                logits, and the full logits of the prompt step and the first
@@ -283,11 +287,56 @@ def make_state() -> None:
     print("wrote", OUT / "state.safetensors")
 
 
+def torch_state():
+    """The state dict of state.pt / state_legacy.pt: seeded tensors of several
+    dtypes and ranks, a transposed one and a permuted one (strides a
+    permutation of row-major), a slice at a storage offset that shares its
+    storage with another entry, a parameter, a 0-d and an empty tensor."""
+    import torch
+    rng = np.random.default_rng(78)
+    base = torch.from_numpy(rng.standard_normal((6, 10)).astype(np.float32))
+    return {
+        "wte.weight": torch.from_numpy(rng.standard_normal((7, 5)).astype(np.float32)),
+        "h.0.ln_1.weight": torch.from_numpy((rng.standard_normal(9) * 0.5).astype(np.float16)),
+        "h.0.mlp.bf16": torch.from_numpy(rng.standard_normal((3, 4)).astype(np.float32)).bfloat16(),
+        "double": torch.from_numpy(rng.standard_normal(4)),
+        "positions": torch.from_numpy(rng.integers(-1000, 1000, (2, 3))),
+        "ids32": torch.from_numpy(rng.integers(0, 50000, 6).astype(np.int32)),
+        "codes": torch.from_numpy(rng.integers(0, 255, (3, 2)).astype(np.uint8)),
+        "mask": torch.from_numpy(rng.integers(0, 2, 5).astype(bool)),
+        "base": base,
+        "base.rows": base[2:4],
+        "lm_head.t": base.t(),
+        "perm": torch.from_numpy(rng.standard_normal((2, 3, 4)).astype(np.float32)).permute(2, 0, 1),
+        "param": torch.nn.Parameter(torch.from_numpy(rng.standard_normal((2, 2)).astype(np.float32))),
+        "scalar": torch.tensor(3.5),
+        "empty": torch.zeros(0, 4),
+    }
+
+
+def make_torch() -> None:
+    """state.pt (torch.save's zip format) and state_legacy.pt (its legacy
+    pickle format) of torch_state(), and torch_state.npz: what the
+    reference's own torch_load (py/thvm/nn_state.py:123-230) reads from each,
+    as numpy arrays under "zip/<name>" and "legacy/<name>"."""
+    import torch
+    from thvm.nn_state import torch_load
+    sd = torch_state()
+    torch.save(sd, OUT / "state.pt")
+    torch.save(sd, OUT / "state_legacy.pt", _use_new_zipfile_serialization=False)
+    out = {}
+    for tag, fn in (("zip", "state.pt"), ("legacy", "state_legacy.pt")):
+        for k, t in torch_load(OUT / fn).items():
+            out[f"{tag}/{k}"] = t.numpy()
+    np.savez(OUT / "torch_state.npz", **out)
+    print("wrote", OUT / "state.pt", OUT / "state_legacy.pt", OUT / "torch_state.npz")
+
+
 if __name__ == "__main__":
-    which = sys.argv[1:] or ["ops", "gpt2", "gpt2_l2", "dtypes", "state"]
+    which = sys.argv[1:] or ["ops", "gpt2", "gpt2_l2", "dtypes", "state", "torch"]
     if "dtypes" in which:
         make_dtypes()
-    if "ops" in which or "gpt2" in which or "gpt2_l2" in which or "state" in which:
+    if "ops" in which or "gpt2" in which or "gpt2_l2" in which or "state" in which or "torch" in which:
         _setup()
     if "ops" in which:
         make_ops()
@@ -297,3 +346,5 @@ if __name__ == "__main__":
         make_gpt2_l2()
     if "state" in which:
         make_state()
+    if "torch" in which:
+        make_torch()

@@ -102,3 +102,75 @@ def test_save_safetensors_round_trips_through_the_loader():
         assert g.dtype == {"a": "F32", "b.bf16": "BF16", "c.fp8": "F8_E4M3", "d": "I32"}[k] and g.shape == a.shape
         assert np.array_equal(W.read(d, g), a)
     """)
+
+
+def test_torch_checkpoints_load_as_the_reference_reads_them():
+    """torch.save files (tests/golden/state.pt in the zip format,
+    state_legacy.pt in the legacy pickle format) through sm100_torch_load:
+    every tensor's elements equal what the reference's own torch_load read
+    from the same file (tests/golden/torch_state.npz; it widens bf16 and f64
+    to f32 and makes the 0-d tensor (1,)), and byte for byte what torch.load
+    gives, shared storages, storage offsets, transposed and permuted strides
+    included; the dtype tags are the storages' own; every buffer is freed."""
+    run("""
+    import torch
+    gold = np.load("tests/golden/torch_state.npz")
+    tags = {torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16", torch.float64: "F64",
+            torch.int64: "I64", torch.int32: "I32", torch.uint8: "U8", torch.bool: "BOOL"}
+    for fmt, fn in (("zip", "tests/golden/state.pt"), ("legacy", "tests/golden/state_legacy.pt")):
+        got = W.load_torch(fn)
+        want = torch.load(fn, weights_only=True)
+        assert sorted(got) == sorted(want) == sorted(k.split("/", 1)[1] for k in gold.files if k.startswith(fmt))
+        for k, t in want.items():
+            t = t.detach().contiguous()
+            e = got[k]
+            assert e.dtype == tags[t.dtype] and e.shape == tuple(t.shape), (fmt, k, e)
+            raw = t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+            assert e.nbytes == raw.nbytes, (fmt, k)
+            if not raw.size:
+                continue
+            back = W.read(d, e).reshape(-1)
+            assert np.array_equal(back.view(np.uint8), raw.reshape(-1).view(np.uint8)), (fmt, k)
+            ref = gold[f"{fmt}/{k}"].reshape(-1)
+            mine = back
+            if e.dtype == "BF16":
+                mine = (back.astype(np.uint32) << 16).view(np.float32)
+            elif e.dtype == "F64":
+                mine = back.astype(np.float32)
+            assert mine.dtype == ref.dtype and np.array_equal(mine, ref), (fmt, k)
+        before = lib.sm100_buf_live_count()
+        for t in got.values():
+            lib.sm100_buf_free(t.buf_id)
+        assert lib.sm100_buf_live_count() == before - len(got)
+    """)
+
+
+def test_bad_torch_checkpoints_are_refused_and_leave_nothing():
+    """A truncated zip, a file that is neither format, a pickle whose
+    storage is missing from the archive: refused with a message, no buffer
+    left behind."""
+    run("""
+    import os, tempfile, zipfile
+    raw = open("tests/golden/state.pt", "rb").read()
+    with tempfile.TemporaryDirectory() as td:
+        cases = {"trunc.pt": raw[: len(raw) // 2], "junk.pt": b"not a checkpoint" * 4}
+        # the same archive without the first storage member
+        with zipfile.ZipFile("tests/golden/state.pt") as zin, zipfile.ZipFile(os.path.join(td, "nostore.pt"), "w",
+                                                                              zipfile.ZIP_STORED) as zout:
+            for i in zin.infolist():
+                if not i.filename.endswith("/data/0"):
+                    zout.writestr(i, zin.read(i.filename))
+        for name, b in cases.items():
+            with open(os.path.join(td, name), "wb") as f:
+                f.write(b)
+        before = lib.sm100_buf_live_count()
+        for name in list(cases) + ["nostore.pt"]:
+            try:
+                W.load_torch(os.path.join(td, name))
+            except L.Sm100Error:
+                pass
+            else:
+                raise AssertionError(name + " loaded")
+            assert lib.sm100_last_error(), name
+            assert lib.sm100_buf_live_count() == before, name
+    """)

@@ -263,6 +263,7 @@ SIGNATURES = {
     "sm100_comm_status": (c_uint32, []),
     "sm100_safetensors_load": (c_int, [ctypes.c_char_p, POINTER(Sm100TensorEntry), c_int32, POINTER(c_int32)]),
     "sm100_dsv2pack_load": (c_int, [ctypes.c_char_p, POINTER(Sm100TensorEntry), c_int32, POINTER(c_int32)]),
+    "sm100_torch_load": (c_int, [ctypes.c_char_p, POINTER(Sm100TensorEntry), c_int32, POINTER(c_int32)]),
     "sm100_custom_program": (c_int32, [ctypes.c_char_p, ctypes.c_char_p, POINTER(c_uint32), POINTER(c_uint32),
                                        c_uint32]),
     "sm100_custom_dispatch": (c_int, [c_int32, POINTER(c_uint32), c_uint32, c_uint32, c_uint32]),

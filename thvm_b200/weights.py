@@ -1,8 +1,9 @@
 """Weight files into device buffers (include/thvm_sm100.h sm100_safetensors_load,
-sm100_dsv2pack_load): the .safetensors files py/thvm's safe_load / safe_save
-use (py/thvm/nn_state.py:44-85) and the reference DeepSeek-V2 bench's
-DSV2PK01 pack (bench/dsv2_decode_bench.c:229-262), mapped from disk and
-copied once into backend buffers."""
+sm100_dsv2pack_load, sm100_torch_load): the .safetensors files py/thvm's
+safe_load / safe_save use (py/thvm/nn_state.py:44-85), the reference
+DeepSeek-V2 bench's DSV2PK01 pack (bench/dsv2_decode_bench.c:229-262) and
+torch.save checkpoints (torch_load, :123-230), mapped from disk and copied
+once into backend buffers."""
 from __future__ import annotations
 
 import ctypes
@@ -46,6 +47,12 @@ def load_safetensors(path, max_tensors: int = 4096) -> dict[str, DeviceTensor]:
 
 def load_dsv2_pack(path, max_tensors: int = 4096) -> dict[str, DeviceTensor]:
     return _load(L.lib().sm100_dsv2pack_load, path, max_tensors)
+
+
+def load_torch(path, max_tensors: int = 4096) -> dict[str, DeviceTensor]:
+    """The tensors of a torch.save state dict (zip or legacy format; py/thvm's
+    torch_load, py/thvm/nn_state.py:123-230), in their file types."""
+    return _load(L.lib().sm100_torch_load, path, max_tensors)
 
 
 def read(device, t: DeviceTensor) -> np.ndarray:
