@@ -145,6 +145,28 @@ def test_torch_checkpoints_load_as_the_reference_reads_them():
     """)
 
 
+def test_torch_checkpoint_with_zip64_records_loads_the_same():
+    """The members of state.pt rewritten with zip64 size fields (the records
+    torch.save writes for large checkpoints) load to the same bytes."""
+    run("""
+    import os, tempfile, zipfile
+    with tempfile.TemporaryDirectory() as td:
+        p64 = os.path.join(td, "z64.pt")
+        with zipfile.ZipFile("tests/golden/state.pt") as zin, zipfile.ZipFile(p64, "w", zipfile.ZIP_STORED) as zout:
+            for i in zin.infolist():
+                with zout.open(i.filename, "w", force_zip64=True) as f:
+                    f.write(zin.read(i.filename))
+        with open(p64, "rb") as f:
+            assert bytes([1, 0, 16, 0]) in f.read()   # a zip64 extra field (id 1, 16 bytes)
+        a, b = W.load_torch("tests/golden/state.pt"), W.load_torch(p64)
+        assert sorted(a) == sorted(b)
+        for k in a:
+            assert a[k].shape == b[k].shape and a[k].dtype == b[k].dtype
+            if a[k].nbytes:
+                assert np.array_equal(W.read(d, a[k]).reshape(-1).view(np.uint8), W.read(d, b[k]).reshape(-1).view(np.uint8)), k
+    """)
+
+
 def test_bad_torch_checkpoints_are_refused_and_leave_nothing():
     """A truncated zip, a file that is neither format, a pickle whose
     storage is missing from the archive: refused with a message, no buffer
