@@ -822,19 +822,29 @@ static int torch_tensor(const Pv *t, const unsigned char *sdata, uint64_t slen, 
   const int isz = torch_type(t->storage, &tag);
   snprintf(e->dtype, sizeof e->dtype, "%s", tag);
   e->ndim = t->ndim;
+  /* sizes, strides and the offset bounded so that no product below overflows;
+     a contiguous or permuted tensor has no more elements than its storage */
+  const int64_t kLim = (int64_t)1 << 40;
   int64_t numel = 1, maxoff = t->offset;
   for (int32_t d = 0; d < t->ndim; d++) {
-    if (t->size[d] < 0) return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: negative size", e->name);
+    if (t->size[d] < 0 || t->size[d] > kLim || t->stride[d] < 0 || t->stride[d] > kLim)
+      return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: size or stride out of range", e->name);
     e->shape[d] = t->size[d];
-    numel *= t->size[d];
+    if (t->size[d] == 0) numel = 0;
+    else if (numel > kLim / t->size[d]) numel = kLim + 1;   /* saturated: refused below */
+    else numel *= t->size[d];
   }
+  const int64_t cap = (int64_t)(slen / (uint64_t)isz);   /* the storage's elements */
+  if (t->offset < 0 || t->offset > kLim || numel > cap)
+    return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: elements past its storage", e->name);
   for (int32_t d = 0; d < t->ndim && numel; d++) {
-    if (t->stride[d] < 0) return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: negative stride", e->name);
+    if (t->size[d] > 1 && t->stride[d] > (cap - maxoff) / (t->size[d] - 1))
+      return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: elements past its storage", e->name);
     maxoff += (t->size[d] - 1) * t->stride[d];
   }
   e->nbytes = (uint64_t)numel * (uint64_t)isz;
   if (numel == 0) return upload(e, NULL);
-  if (t->offset < 0 || (uint64_t)(maxoff + 1) * (uint64_t)isz > slen)
+  if (maxoff >= cap)
     return sm100_set_error(SM100_ERR_ARG, "torch_load: %s: elements past its storage", e->name);
   /* contiguous: the strides of a row-major layout (dimensions of size 1 aside) */
   int contiguous = 1;
