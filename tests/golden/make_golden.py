@@ -1,7 +1,7 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE itself.
 
-This is test infrastructure, run in a container that holds the reference
-checkout (default /root/reference, or $THVM_REF):
+This is test infrastructure, run where the reference checkout is present
+(its location in $THVM_REF, else the build container's default):
 
     make -C oracle ref                  # builds oracle/_ref/libthvm_py.so
     python tests/golden/make_golden.py  # [ops] [gpt2]
