@@ -30,9 +30,11 @@ a bounded sample), `clocks` (nvidia-smi during the timed region),
 
 `--impl reference` times the reference's own CPU path of the workload: for
 config 5 its DeepSeek-V2 decode bench (oracle/_ref/dsv2_decode_bench, built
-from the reference's sources) at full width on a bounded sample.
+from the reference's sources) at full width on a bounded sample; for `xl` and
+`gpt2` the oracle port of the reference's CPU forward on the host cores.
 The other workloads: `gpt2` (config 1 alone; N > 1 runs N replicas), `xl`
-(config 3, tensor-parallel), `prefill` (config 4, the (batch, head) pairs
+(config 3, tensor-parallel: decode steps and the prompt pass), `prefill`
+(config 4, the (batch, head) pairs
 split over the ranks), `kernels` (config 2 / 4 kernel cases, one line each).
 """
 from __future__ import annotations
@@ -1025,6 +1027,61 @@ def xl_step_bytes(cfg, pos: int) -> int:
     return weights + kv
 
 
+_XL_CPU_WEIGHTS: dict = {}
+
+
+def xl_cpu_sample(batch: int = 16, seed: int = 0):
+    """The oracle port (oracle.c orc_xl_step: the reference's CPU GPT-2 forward
+    with bf16 weights, pthreads over the host cores) on a bounded sample of
+    config 3: one batch-16 decode step of the full-width model (d 1600, 25
+    heads, vocab 50257) with 1 and with 2 layers after one warm step each;
+    the 48-layer step time is t1 + 47 (t2 - t1).  -> (tok/s, sample text, s)."""
+    import oracle as O
+    from thvm_b200.gpt2_xl import GPT2_XL, XLConfig, xl_weights
+    key = (batch, seed)
+    if key not in _XL_CPU_WEIGHTS:   # generated once per process
+        _XL_CPU_WEIGHTS[key] = xl_weights(XLConfig(n_layers=2, max_ctx=64, batch=batch), seed=seed)
+    w = _XL_CPU_WEIGHTS[key]
+    tok = np.random.default_rng(1).integers(0, GPT2_XL.vocab, batch).astype(np.int32)
+    times = []
+    for n in (1, 2):
+        cfg = XLConfig(n_layers=n, max_ctx=64, batch=batch)
+        m = O.XLModel(cfg, {k: v for k, v in w.items() if not k.startswith("h.") or int(k.split(".")[1]) < n})
+        m.step(tok, 0)
+        t0 = time.perf_counter()
+        m.step(tok, 1)
+        times.append(time.perf_counter() - t0)
+    t48 = times[0] + (GPT2_XL.n_layers - 1) * (times[1] - times[0])
+    return (batch / t48, f"one batch-{batch} decode step of the full-width model with 1 and 2 layers "
+                         f"({times[0]:.2f} s, {times[1]:.2f} s); 48-layer step = t1 + 47 (t2 - t1) = {t48:.2f} s", t48)
+
+
+def xl_reference(args, ctx):
+    """The CPU path of config 3 on the host cores: the oracle port of the
+    reference's GPT-2 forward with bf16 weights (xl_cpu_sample), args.steps
+    samples after args.warmup untimed ones (each sample a 1- and 2-layer
+    step pair: the whole run stays within minutes)."""
+    import oracle as O
+    for _ in range(max(args.warmup, 0)):
+        xl_cpu_sample()
+    vals, ts, text = [], [], ""
+    for _ in range(max(args.steps, 1)):
+        v, text, t48 = xl_cpu_sample()
+        vals.append(v)
+        ts.append(t48)
+    v = float(np.mean(vals))
+    print(json.dumps({"metric": "decode tok/s (GPT-2 XL bf16 b16, tensor-parallel)", "value": round(v, 3),
+                      "unit": "tok/s", "n_gpus": ctx.world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(float(np.mean(ts)) * 1e3, 1), "higher_is_better": True,
+                      "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                      "impl": "reference",
+                      "config": {"workload": "config 3: GPT-2 XL-shaped bf16 decode, batch 16", "sample": text},
+                      "cpu_baseline": {"value": round(v, 3), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+                                       "sample": text},
+                      "e2e": {"value": round(v, 3), "unit": "tok/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def xl_prefill_flops(cfg, P: int) -> int:
     """Algorithmic FLOPs of the prompt pass over the whole job: the four
     projections of every layer on all B P rows, the causal q k^T and p v
@@ -1209,7 +1266,7 @@ def main():
     if args.impl == "reference":
         if ctx.rank != 0:
             return
-        return (moe_reference if args.workload == "moe" else gpt2_reference)(args, ctx)
+        return {"moe": moe_reference, "xl": xl_reference}.get(args.workload, gpt2_reference)(args, ctx)
     args.warmup = max(args.warmup, 3)
     cpu = not args.no_cpu_baseline and ctx.rank == 0 and ctx.world == 1
     try:
@@ -1226,6 +1283,11 @@ def main():
             line = gpt2_run(args, ctx, cpu)
         elif args.workload == "xl":
             line = xl_run(args, ctx)
+            if cpu:
+                import oracle as O
+                v, text, _ = xl_cpu_sample()
+                line["cpu_baseline"] = {"value": round(v, 3), "unit": "tok/s", "cores": O.num_threads(), "kind": "port",
+                                        "sample": text}
         elif args.workload == "prefill":
             line = prefill_run(args, ctx)
         else:
