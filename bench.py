@@ -31,7 +31,8 @@ a bounded sample), `clocks` (nvidia-smi during the timed region),
 `--impl reference` times the reference's own CPU path of the workload: for
 config 5 its DeepSeek-V2 decode bench (oracle/_ref/dsv2_decode_bench, built
 from the reference's sources) at full width on a bounded sample; for `xl` and
-`gpt2` the oracle port of the reference's CPU forward on the host cores.
+`gpt2` the oracle port of the reference's CPU forward on the host cores, for
+`prefill` the oracle port of its causal attention.
 The other workloads: `gpt2` (config 1 alone; N > 1 runs N replicas), `xl`
 (config 3, tensor-parallel: decode steps and the prompt pass), `prefill`
 (config 4, the (batch, head) pairs
@@ -1082,6 +1083,36 @@ def xl_reference(args, ctx):
                               "d2h_bytes_per_step": 0}}), flush=True)
 
 
+def prefill_reference(args, ctx):
+    """The CPU path of config 4 on the host cores: the oracle port of the
+    reference's scaled_dot_product_attention with the causal mask
+    (oracle.c orc_sdpa_f32, f32 on the bf16-valued inputs) over a bounded
+    sample, 2 of the 64 (batch, head) pairs at S = 2048, D = 128 per step;
+    TFLOP/s = the pairs' algorithmic FLOPs (2 S^2 D each, the config's count)
+    / time."""
+    import oracle as O
+    S, D, pairs = 2048, 128, 2
+    rng = np.random.default_rng(4)
+    q, k, v = (O.bf16_to_f32(bf16_bits(rng.standard_normal((pairs, S, D)).astype(np.float32))) for _ in range(3))
+    for _ in range(max(args.warmup, 0)):
+        O.sdpa(q, k, v, causal=True)
+    t0 = time.perf_counter()
+    for _ in range(max(args.steps, 1)):
+        O.sdpa(q, k, v, causal=True)
+    dt = (time.perf_counter() - t0) / max(args.steps, 1)
+    tf = pairs * 2.0 * S * S * D / dt / 1e12
+    sample = f"{pairs} of the 64 (batch, head) pairs per step, S {S}, D {D}, causal, f32 on bf16 values"
+    print(json.dumps({"metric": "causal prefill TFLOP/s (B4 H16 S2048 D128 bf16)", "value": round(tf, 5),
+                      "unit": "TFLOP/s", "n_gpus": ctx.world, "steps": args.steps, "warmup": args.warmup,
+                      "ms_per_step": round(dt * 1e3, 1), "higher_is_better": True, "scaling": "strong",
+                      "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                      "config": {"workload": "config 4: causal attention prefill B4 H16 S2048 D128", "sample": sample},
+                      "cpu_baseline": {"value": round(tf, 5), "unit": "TFLOP/s", "cores": O.num_threads(),
+                                       "kind": "port", "sample": sample},
+                      "e2e": {"value": round(tf, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                              "d2h_bytes_per_step": 0}}), flush=True)
+
+
 def xl_prefill_flops(cfg, P: int) -> int:
     """Algorithmic FLOPs of the prompt pass over the whole job: the four
     projections of every layer on all B P rows, the causal q k^T and p v
@@ -1266,7 +1297,8 @@ def main():
     if args.impl == "reference":
         if ctx.rank != 0:
             return
-        return {"moe": moe_reference, "xl": xl_reference}.get(args.workload, gpt2_reference)(args, ctx)
+        return {"moe": moe_reference, "xl": xl_reference, "prefill": prefill_reference}.get(args.workload,
+                                                                                          gpt2_reference)(args, ctx)
     args.warmup = max(args.warmup, 3)
     cpu = not args.no_cpu_baseline and ctx.rank == 0 and ctx.world == 1
     try:
