@@ -1297,8 +1297,14 @@ def main():
     if args.impl == "reference":
         if ctx.rank != 0:
             return
-        return {"moe": moe_reference, "xl": xl_reference, "prefill": prefill_reference}.get(args.workload,
-                                                                                          gpt2_reference)(args, ctx)
+        arms = {"moe": moe_reference, "xl": xl_reference, "prefill": prefill_reference, "gpt2": gpt2_reference}
+        if args.workload not in arms:
+            why = {"spec": "no reference arm for the speculative workload (the reference's DSV2_SPEC mode is its "
+                           "batch-1 decode bench; the default workload's arm runs that bench)",
+                   "kernels": "the kernel cases are single launches with no reference CPU metric of their own"}
+            print(json.dumps({"impl": "reference", "unavailable": why.get(args.workload, args.workload)}), flush=True)
+            return
+        return arms[args.workload](args, ctx)
     args.warmup = max(args.warmup, 3)
     cpu = not args.no_cpu_baseline and ctx.rank == 0 and ctx.world == 1
     try:
